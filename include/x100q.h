@@ -1,0 +1,102 @@
+/*
+ * x100q.h -- C ABI of the block-quantised decode path (dequant-GEMV and the
+ * top-k SwiGLU mixture-of-experts FFN) served by sm_100a CUDA kernels in
+ * libx100gemm_b200.so.
+ *
+ * The reference keeps this path inside its single-file engines as static
+ * functions called from forward():
+ *   Lin lin_new_{hp,i8,q3k}(...)        qwen_moe_q3k.c:843,872,897 (qwen_moe.c:66)
+ *   pack_act_{hp,i8,q3k}(x, K, Abuf)    qwen_moe_q3k.c:860,887,624
+ *   lin_mm_{hp,i8,q3k}(&lin, Abuf, y)   qwen_moe_q3k.c:1029,1040,1048
+ *   MoE block in forward()              qwen_moe.c:295-311, qwen_moe_q3k.c:1916-1978
+ * This header exposes the same steps as a library: a linear is created once
+ * from GGUF-native quantised blocks (weights live in HBM afterwards), then
+ * applied to fp32 activations; the MoE call does router -> softmax -> top-k
+ * -> renormalise -> SwiGLU experts -> weighted combine in one call.
+ *
+ * Activations stay fp32 end to end (no int8 activation packing): the parity
+ * target is the reference's scalar fp32 path.  Calls with host pointers are
+ * synchronous; *_dev calls take device pointers and a cudaStream_t and are
+ * asynchronous.  Every call returns 0 or an X100_E* code (see x100_gemm.h);
+ * constructors return NULL and set x100_last_error() on failure.
+ * Handles are not thread-safe: one caller thread per handle at a time.
+ */
+#ifndef X100Q_H
+#define X100Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* GGUF / ggml tensor type ids, the values the reference's GGUF reader
+ * switches on (qwen_moe.c:158-177, qwen_moe_q3k.c:531).                     */
+enum {
+    X100Q_F32  = 0,
+    X100Q_Q4_0 = 2,    /* 18 B / 32 weights: fp16 d, 16 B nibbles (q-8)*d      */
+    X100Q_Q8_0 = 8,    /* 34 B / 32 weights: fp16 d, int8[32]   q*d            */
+    X100Q_Q3_K = 11,   /* 110 B / 256: hmask[32] qs[64] scales[12] fp16 d      */
+    X100Q_Q4_K = 12    /* 144 B / 256: fp16 d, fp16 dmin, scales[12], qs[128]  */
+};
+
+/* Bytes of one GGUF-native row of K weights of type qtype (0 if K is not a
+ * multiple of the type's block size or qtype is unknown).                   */
+size_t x100q_row_bytes(int qtype, int K);
+
+/* ---- quantised linear ---------------------------------------------------- */
+typedef struct x100q_lin x100q_lin;
+
+/* Create an N x K linear from N rows of GGUF-native blocks (host pointer,
+ * row-major, K/blocksize blocks per row).  Replaces lin_new_q3k
+ * (qwen_moe_q3k.c:897-909, which also reads raw GGUF blocks) and lin_new_hp /
+ * lin_new_i8 (:843, :872).  Blocks are uploaded once and re-laid-out on the
+ * device for 16-byte vector loads.                                          */
+x100q_lin *x100q_lin_create(int qtype, int N, int K, const void *blocks);
+void       x100q_lin_destroy(x100q_lin *lin);
+int        x100q_lin_info(const x100q_lin *lin, int *qtype, int *N, int *K,
+                          size_t *device_bytes);
+
+/* y[b*N + n] = sum_k W[n][k] * x[b*K + k] for b < batch (1 <= batch <= 16).
+ * Replaces pack_act_* + lin_mm_* (qwen_moe_q3k.c:1029-1082): one call per
+ * linear per step.  x and y may be host or device pointers.                 */
+int x100q_lin_gemv(const x100q_lin *lin, const float *x, float *y, int batch);
+int x100q_lin_gemv_dev(const x100q_lin *lin, const float *x, float *y, int batch,
+                       void *stream);
+
+/* ---- mixture-of-experts FFN ---------------------------------------------- */
+typedef struct x100q_moe x100q_moe;
+
+/* d: hidden size; n_exp experts, n_act active per token (top-k, k <= 16);
+ * ffn: expert intermediate size; qtype: expert weight type (Q4_0, Q4_K,
+ * Q3_K or Q8_0).  router: fp32 [n_exp][d] (ffn_gate_inp.weight).
+ * gate_exps / up_exps: GGUF-native blocks [n_exp][ffn][d]; down_exps:
+ * [n_exp][d][ffn] -- the reference's blk.N.ffn_{gate,up,down}_exps tensors
+ * (qwen_moe.c:215-222).  Only experts [expert_lo, expert_hi) are uploaded and
+ * evaluated by this handle (expert parallelism: each process holds a slice;
+ * the router is replicated so every process knows the full top-k).          */
+x100q_moe *x100q_moe_create(int d, int n_exp, int n_act, int ffn, int qtype,
+                            const float *router, const void *gate_exps,
+                            const void *up_exps, const void *down_exps,
+                            int expert_lo, int expert_hi);
+void       x100q_moe_destroy(x100q_moe *moe);
+
+/* For each of `batch` tokens (1 <= batch <= 16), hn[b][d] -> eout[b][d]:
+ *   logits = router . hn;  p = softmax(logits);  top-k by p (strict >, lowest
+ *   index wins ties);  w = p_sel / sum(p_sel);
+ *   eout = sum over selected experts held by this handle of
+ *          w_a * down_a( silu(gate_a . hn) * (up_a . hn) )
+ * (qwen_moe.c:295-311).  sel_out [batch][n_act] and w_out [batch][n_act]
+ * receive the routing (may be NULL).  With a partial expert range, eout is
+ * this process's partial sum; summing eout over all processes (NCCL reduce)
+ * gives the full block output.                                              */
+int x100q_moe_ffn(const x100q_moe *moe, const float *hn, float *eout, int batch,
+                  int *sel_out, float *w_out);
+int x100q_moe_ffn_dev(const x100q_moe *moe, const float *hn, float *eout, int batch,
+                      int *sel_out, float *w_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* X100Q_H */

@@ -1,0 +1,498 @@
+/*
+ * oracle_quant.c -- CPU restatement of the reference's block-quantised
+ * formats (GGUF Q4_0 / Q8_0 / Q4_K / Q3_K), its scalar dequant-GEMV and its
+ * scalar MoE block.  TEST INFRASTRUCTURE ONLY (checker for tests/, smoke()
+ * and bench.py's cpu_baseline); never part of the product library.
+ *
+ * Built with -ffp-contract=off and without -ffast-math so every multiply and
+ * add rounds separately, as the reference's scalar C does on x86-64.
+ */
+#include "x100_oracle.h"
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---- fp16 ----------------------------------------------------------------*/
+
+/* qwen_moe.c:115-118 (f16f): sign/exponent/mantissa unpack, subnormals
+ * renormalised, exponent 31 -> inf/nan.                                    */
+float orc_f16_to_f32(uint16_t h)
+{
+    uint32_t s = (h >> 15) & 1u, e = (h >> 10) & 0x1fu, m = h & 0x3ffu, b;
+    if (e == 0) {
+        if (m == 0) b = s << 31;
+        else {
+            int ee = -14;
+            while (!(m & 0x400u)) { m <<= 1; ee--; }
+            m &= 0x3ffu;
+            b = (s << 31) | ((uint32_t)(ee + 127) << 23) | (m << 13);
+        }
+    } else if (e == 0x1f) b = (s << 31) | (0xffu << 23) | (m << 13);
+    else b = (s << 31) | ((e - 15 + 127) << 23) | (m << 13);
+    float f;
+    memcpy(&f, &b, 4);
+    return f;
+}
+
+/* IEEE-754 binary16 conversion with round-to-nearest-even (what ggml's
+ * GGML_FP32_TO_FP16 does); gcc implements the _Float16 cast that way.      */
+uint16_t orc_f32_to_f16_rne(float f)
+{
+    _Float16 h = (_Float16)f;
+    uint16_t u;
+    memcpy(&u, &h, 2);
+    return u;
+}
+
+/* qwen_moe_hp.c:71-79 (f32_to_f16): truncating conversion used by the
+ * reference's own Q4_0 encoder for the stored block scale.                  */
+uint16_t orc_f32_to_f16_trunc(float f)
+{
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    int32_t exp = (int32_t)((x >> 23) & 0xffu) - 127 + 15;
+    uint32_t mant = x & 0x7fffffu;
+    if (exp <= 0) {
+        if (exp < -10) return (uint16_t)sign;
+        mant |= 0x800000u;
+        uint32_t shift = (uint32_t)(14 - exp);
+        return (uint16_t)(sign | (mant >> shift));
+    }
+    if (exp >= 31) return (uint16_t)(sign | 0x7c00u);
+    return (uint16_t)(sign | ((uint32_t)exp << 10) | (mant >> 13));
+}
+
+static inline float rd_f16(const uint8_t *p) { uint16_t h; memcpy(&h, p, 2); return orc_f16_to_f32(h); }
+static inline void  wr_f16(uint8_t *p, float f) { uint16_t h = orc_f32_to_f16_rne(f); memcpy(p, &h, 2); }
+
+/* ---- sizes ----------------------------------------------------------------*/
+int orc_block_elems(int qtype)
+{
+    switch (qtype) {
+    case ORC_F32: return 1;
+    case ORC_Q4_0: case ORC_Q8_0: return 32;
+    case ORC_Q3_K: case ORC_Q4_K: return 256;
+    default: return 0;
+    }
+}
+int orc_block_bytes(int qtype)
+{
+    switch (qtype) {
+    case ORC_F32: return 4;
+    case ORC_Q4_0: return 18;   /* fp16 d + 16 B               (qwen_moe.c:164) */
+    case ORC_Q8_0: return 34;   /* fp16 d + 32 B               (qwen_moe.c:162) */
+    case ORC_Q3_K: return 110;  /* block_q3_K                  (qwen_moe_q3k.c:531) */
+    case ORC_Q4_K: return 144;  /* block_q4_K, ggml QK_K = 256 */
+    default: return 0;
+    }
+}
+size_t orc_row_bytes(int qtype, int K)
+{
+    int be = orc_block_elems(qtype);
+    if (be <= 0 || K % be) return 0;
+    return (size_t)(K / be) * (size_t)orc_block_bytes(qtype);
+}
+
+/* ---- decode ---------------------------------------------------------------*/
+
+/* qwen_moe_q3k.c:534-538 == repack.cpp:222-233 (get_scale_min_k4). */
+void orc_kq_scale_min(int j, const uint8_t *q, uint8_t *sc, uint8_t *m)
+{
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *sc = (uint8_t)((q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4));
+        *m = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+    }
+}
+
+/* qwen_moe.c:164-165: element j < 16 is the low nibble of qs[j], j >= 16 the
+ * high nibble of qs[j-16]; w = (nib - 8) * d.                               */
+static void dq_q4_0(const uint8_t *blk, float *y)
+{
+    float d = rd_f16(blk);
+    const uint8_t *qs = blk + 2;
+    for (int j = 0; j < 32; j++) {
+        int nib = (j < 16) ? (qs[j] & 0xf) : (qs[j - 16] >> 4);
+        y[j] = (float)(nib - 8) * d;
+    }
+}
+
+/* qwen_moe.c:162-163: w = (int8)q * d. */
+static void dq_q8_0(const uint8_t *blk, float *y)
+{
+    float d = rd_f16(blk);
+    for (int j = 0; j < 32; j++) y[j] = (float)(int8_t)blk[2 + j] * d;
+}
+
+/* Q4_K superblock: fp16 d @0, fp16 dmin @2, scales[12] @4, qs[128] @16.
+ * 64-element chunk c uses scale/min pairs 2c (low nibbles of qs[32c..+31])
+ * and 2c+1 (high nibbles) -- the order of repack.cpp:262-283 and of the
+ * reference's K-quant decoder qwen_moe_q3k.c:541-552 (which is Q4_K when the
+ * fifth bit plane qh is zero).  w = d*sc*q - dmin*m.                        */
+static void dq_q4_k(const uint8_t *blk, float *y)
+{
+    float d = rd_f16(blk), dmin = rd_f16(blk + 2);
+    const uint8_t *sc = blk + 4, *qs = blk + 16;
+    for (int c = 0; c < 4; c++) {
+        uint8_t s0, m0, s1, m1;
+        orc_kq_scale_min(2 * c, sc, &s0, &m0);
+        orc_kq_scale_min(2 * c + 1, sc, &s1, &m1);
+        float d1 = d * (float)s0, mm1 = dmin * (float)m0;
+        float d2 = d * (float)s1, mm2 = dmin * (float)m1;
+        const uint8_t *q = qs + 32 * c;
+        for (int l = 0; l < 32; l++) y[64 * c + l] = d1 * (float)(q[l] & 0xF) - mm1;
+        for (int l = 0; l < 32; l++) y[64 * c + 32 + l] = d2 * (float)(q[l] >> 4) - mm2;
+    }
+}
+
+/* The 16 six-bit Q3_K sub-block scales (biased by 32) packed in 12 bytes:
+ * scale i has low nibble in byte i (i < 8, low half) or byte i-8 (high half),
+ * and its top two bits in byte 8 + i%4 at bit 2*(i/4).  This is the unpacking
+ * done with kmask1/kmask2 in qwen_moe_q3k.c:560-564.                        */
+static void q3k_scales(const uint8_t *s12, int *out)
+{
+    for (int i = 0; i < 16; i++) {
+        int lo = (i < 8) ? (s12[i] & 0xF) : (s12[i - 8] >> 4);
+        int hi = (s12[8 + (i & 3)] >> (2 * (i >> 2))) & 3;
+        out[i] = (int)(int8_t)(uint8_t)(lo | (hi << 4));
+    }
+}
+
+/* qwen_moe_q3k.c:557-577: block_q3_K = hmask[32] @0, qs[64] @32,
+ * scales[12] @96, fp16 d @108.  Element 128h + 32j + l (h < 2, j < 4,
+ * l < 32): 2-bit value (qs[32h+l] >> 2j) & 3, minus 4 when bit (4h+j) of
+ * hmask[l] is clear, times d*(scale[8h + 2j + (l >= 16)] - 32).             */
+static void dq_q3_k(const uint8_t *blk, float *y)
+{
+    const uint8_t *hm = blk, *qs = blk + 32;
+    float d_all = rd_f16(blk + 108);
+    int sc[16];
+    q3k_scales(blk + 96, sc);
+    for (int h = 0; h < 2; h++) {
+        const uint8_t *q = qs + 32 * h;
+        for (int j = 0; j < 4; j++) {
+            int shift = 2 * j;
+            uint8_t m = (uint8_t)(1u << (4 * h + j));
+            float dl = d_all * (float)(sc[8 * h + 2 * j] - 32);
+            for (int l = 0; l < 16; l++)
+                y[128 * h + 32 * j + l] = dl * (float)((int)((q[l] >> shift) & 3) - ((hm[l] & m) ? 0 : 4));
+            dl = d_all * (float)(sc[8 * h + 2 * j + 1] - 32);
+            for (int l = 16; l < 32; l++)
+                y[128 * h + 32 * j + l] = dl * (float)((int)((q[l] >> shift) & 3) - ((hm[l] & m) ? 0 : 4));
+        }
+    }
+}
+
+void orc_dequant_row(int qtype, const void *blocks, int K, float *out)
+{
+    const uint8_t *b = (const uint8_t *)blocks;
+    int be = orc_block_elems(qtype), bb = orc_block_bytes(qtype);
+    if (qtype == ORC_F32) { memcpy(out, blocks, (size_t)K * 4); return; }
+    for (int i = 0; i < K / be; i++) {
+        const uint8_t *blk = b + (size_t)i * bb;
+        float *y = out + (size_t)i * be;
+        switch (qtype) {
+        case ORC_Q4_0: dq_q4_0(blk, y); break;
+        case ORC_Q8_0: dq_q8_0(blk, y); break;
+        case ORC_Q4_K: dq_q4_k(blk, y); break;
+        case ORC_Q3_K: dq_q3_k(blk, y); break;
+        }
+    }
+}
+
+/* ---- encode (own encoders, written from the format definitions) ---------*/
+
+static int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+/* Q4_0 with the BASELINE rule: d = max|w|/7 (fp32, floor 1e-6 as in
+ * qwen_moe.c:70-72), q = lrintf(w/d) clamped to +-7, stored nibble q+8 and
+ * fp16(d).                                                                  */
+static void enc_q4_0(const float *w, uint8_t *blk)
+{
+    float amax = 1e-6f;
+    for (int i = 0; i < 32; i++) { float a = fabsf(w[i]); if (a > amax) amax = a; }
+    float s = amax / 7.0f, inv = 1.0f / s;
+    int q[32];
+    for (int i = 0; i < 32; i++) q[i] = clampi((int)lrintf(w[i] * inv), -7, 7) + 8;
+    wr_f16(blk, s);
+    for (int l = 0; l < 16; l++) blk[2 + l] = (uint8_t)((q[l] & 0xF) | ((q[l + 16] & 0xF) << 4));
+}
+
+static void enc_q8_0(const float *w, uint8_t *blk)
+{
+    float amax = 1e-6f;
+    for (int i = 0; i < 32; i++) { float a = fabsf(w[i]); if (a > amax) amax = a; }
+    float s = amax / 127.0f, inv = 1.0f / s;
+    wr_f16(blk, s);
+    for (int i = 0; i < 32; i++) blk[2 + i] = (uint8_t)(int8_t)clampi((int)lrintf(w[i] * inv), -127, 127);
+}
+
+/* Q4_K: per 32-element sub-block an affine (scale, min) pair; the pairs are
+ * quantised to 6 bits against the superblock's fp16 d and dmin.            */
+static void enc_q4_k(const float *w, uint8_t *blk)
+{
+    float scl[8], mns[8], maxs = 0.f, maxm = 0.f;
+    for (int j = 0; j < 8; j++) {
+        float mn = w[32 * j], mx = w[32 * j];
+        for (int l = 1; l < 32; l++) { float v = w[32 * j + l]; if (v < mn) mn = v; if (v > mx) mx = v; }
+        if (mn > 0.f) mn = 0.f;
+        scl[j] = (mx - mn) / 15.0f;
+        mns[j] = -mn;
+        if (scl[j] > maxs) maxs = scl[j];
+        if (mns[j] > maxm) maxm = mns[j];
+    }
+    wr_f16(blk, maxs / 63.0f);
+    wr_f16(blk + 2, maxm / 63.0f);
+    float d = rd_f16(blk), dmin = rd_f16(blk + 2);
+    int sc[8], mq[8];
+    for (int j = 0; j < 8; j++) {
+        sc[j] = d > 0.f ? clampi((int)lrintf(scl[j] / d), 0, 63) : 0;
+        mq[j] = dmin > 0.f ? clampi((int)lrintf(mns[j] / dmin), 0, 63) : 0;
+    }
+    uint8_t *s = blk + 4;
+    for (int j = 0; j < 4; j++) {
+        s[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+        s[j + 4] = (uint8_t)((mq[j] & 63) | ((mq[j + 4] >> 4) << 6));
+        s[j + 8] = (uint8_t)((sc[j + 4] & 0xF) | ((mq[j + 4] & 0xF) << 4));
+    }
+    int q[256];
+    for (int j = 0; j < 8; j++) {
+        float dd = d * (float)sc[j], mm = dmin * (float)mq[j];
+        for (int l = 0; l < 32; l++)
+            q[32 * j + l] = dd > 0.f ? clampi((int)lrintf((w[32 * j + l] + mm) / dd), 0, 15) : 0;
+    }
+    uint8_t *qs = blk + 16;
+    for (int c = 0; c < 4; c++)
+        for (int l = 0; l < 32; l++)
+            qs[32 * c + l] = (uint8_t)(q[64 * c + l] | (q[64 * c + 32 + l] << 4));
+}
+
+/* Q3_K: per 16-element sub-block a signed scale chosen so the largest-|w|
+ * element maps to -4; scales quantised to 6 bits (biased 32) against fp16 d;
+ * values q in [-4, 3] stored as v = q + 4: low two bits in qs, bit 2 in
+ * hmask (set bit = no -4 offset).                                            */
+static void enc_q3_k(const float *w, uint8_t *blk)
+{
+    float s[16], maxs = 0.f;
+    for (int j = 0; j < 16; j++) {
+        float best = 0.f;
+        for (int l = 0; l < 16; l++) { float v = w[16 * j + l]; if (fabsf(v) > fabsf(best)) best = v; }
+        s[j] = -best / 4.0f;
+        if (fabsf(s[j]) > maxs) maxs = fabsf(s[j]);
+    }
+    memset(blk, 0, 110);
+    wr_f16(blk + 108, maxs / 32.0f);
+    float d = rd_f16(blk + 108);
+    int lsc[16];
+    for (int j = 0; j < 16; j++) lsc[j] = d > 0.f ? clampi((int)lrintf(s[j] / d), -32, 31) : 0;
+    uint8_t *s12 = blk + 96;
+    for (int k = 0; k < 8; k++)
+        s12[k] = (uint8_t)(((lsc[k] + 32) & 0xF) | (((lsc[k + 8] + 32) & 0xF) << 4));
+    for (int r = 0; r < 4; r++) {
+        uint8_t v = 0;
+        for (int g = 0; g < 4; g++) v |= (uint8_t)((((lsc[4 * g + r] + 32) >> 4) & 3) << (2 * g));
+        s12[8 + r] = v;
+    }
+    uint8_t *hm = blk, *qs = blk + 32;
+    for (int h = 0; h < 2; h++)
+        for (int j = 0; j < 4; j++)
+            for (int l = 0; l < 32; l++) {
+                int e = 128 * h + 32 * j + l;
+                int is = 8 * h + 2 * j + (l >= 16);
+                float dd = d * (float)lsc[is];
+                int q = dd != 0.f ? clampi((int)lrintf(w[e] / dd), -4, 3) : 0;
+                int v = q + 4;
+                qs[32 * h + l] |= (uint8_t)((v & 3) << (2 * j));
+                if (v & 4) hm[l] |= (uint8_t)(1u << (4 * h + j));
+            }
+}
+
+void orc_quantize(int qtype, int N, int K, const float *w, void *blocks)
+{
+    uint8_t *b = (uint8_t *)blocks;
+    int be = orc_block_elems(qtype), bb = orc_block_bytes(qtype);
+    if (qtype == ORC_F32) { memcpy(blocks, w, (size_t)N * K * 4); return; }
+    size_t nblk = (size_t)N * (K / be);
+    for (size_t i = 0; i < nblk; i++) {
+        const float *src = w + i * be;
+        uint8_t *dst = b + i * bb;
+        switch (qtype) {
+        case ORC_Q4_0: enc_q4_0(src, dst); break;
+        case ORC_Q8_0: enc_q8_0(src, dst); break;
+        case ORC_Q4_K: enc_q4_k(src, dst); break;
+        case ORC_Q3_K: enc_q3_k(src, dst); break;
+        }
+    }
+}
+
+/* ---- dequant-GEMV ----------------------------------------------------------
+ * The reference's scalar fp32 path: dequantise the row, then a k-ordered fp32
+ * dot product with the fp32 activation (the router loop of qwen_moe.c:296 and
+ * the float loops of qwen_moe.c:97-98).                                      */
+typedef struct { int qtype, N, K, batch, r0, r1; const uint8_t *W; const float *x; float *y; } gemv_job;
+
+static void *gemv_worker(void *p)
+{
+    gemv_job *j = (gemv_job *)p;
+    size_t rb = orc_row_bytes(j->qtype, j->K);
+    float *row = (float *)malloc((size_t)j->K * sizeof(float));
+    for (int n = j->r0; n < j->r1; n++) {
+        orc_dequant_row(j->qtype, j->W + (size_t)n * rb, j->K, row);
+        for (int b = 0; b < j->batch; b++) {
+            const float *x = j->x + (size_t)b * j->K;
+            float acc = 0.f;
+            for (int k = 0; k < j->K; k++) acc += row[k] * x[k];
+            j->y[(size_t)b * j->N + n] = acc;
+        }
+    }
+    free(row);
+    return NULL;
+}
+
+void orc_qgemv_mt(int qtype, int N, int K, const void *blocks, const float *x, float *y,
+                  int batch, int nt)
+{
+    if (nt < 1) nt = 1;
+    if (nt > N) nt = N > 0 ? N : 1;
+    pthread_t *th = (pthread_t *)calloc((size_t)nt, sizeof(pthread_t));
+    gemv_job *jb = (gemv_job *)calloc((size_t)nt, sizeof(gemv_job));
+    for (int t = 0; t < nt; t++) {
+        jb[t] = (gemv_job){qtype, N, K, batch, (int)((long)N * t / nt), (int)((long)N * (t + 1) / nt),
+                           (const uint8_t *)blocks, x, y};
+        if (t) pthread_create(&th[t], NULL, gemv_worker, &jb[t]);
+    }
+    gemv_worker(&jb[0]);
+    for (int t = 1; t < nt; t++) pthread_join(th[t], NULL);
+    free(th); free(jb);
+}
+
+void orc_qgemv(int qtype, int N, int K, const void *blocks, const float *x, float *y, int batch)
+{
+    orc_qgemv_mt(qtype, N, K, blocks, x, y, batch, 1);
+}
+
+/* ---- MoE block -------------------------------------------------------------*/
+
+/* qwen_moe.c:189 */
+void orc_softmax(float *x, int n)
+{
+    float m = -1e30f;
+    for (int i = 0; i < n; i++) if (x[i] > m) m = x[i];
+    float s = 0.f;
+    for (int i = 0; i < n; i++) { x[i] = expf(x[i] - m); s += x[i]; }
+    float inv = 1.0f / s;
+    for (int i = 0; i < n; i++) x[i] *= inv;
+}
+
+/* qwen_moe.c:299-301 / qwen_moe_q3k.c:1934-1936: greedy selection, strict >
+ * so the lowest index wins a tie, then renormalise the selected weights.   */
+void orc_topk(const float *p, int n, int k, int *sel, float *w)
+{
+    for (int a = 0; a < k; a++) {
+        int bi = -1;
+        float bv = -1e30f;
+        for (int e = 0; e < n; e++) {
+            int used = 0;
+            for (int b = 0; b < a; b++) if (sel[b] == e) used = 1;
+            if (!used && p[e] > bv) { bv = p[e]; bi = e; }
+        }
+        sel[a] = bi;
+        w[a] = bv;
+    }
+    float ssum = 0.f;
+    for (int a = 0; a < k; a++) ssum += w[a];
+    for (int a = 0; a < k; a++) w[a] /= ssum;
+}
+
+/* qwen_moe.c:309 / qwen_moe_q3k.c:1678-1680 (swiglu_exact) */
+float orc_silu(float x) { return x / (1.0f + expf(-x)); }
+
+/* qwen_moe.c:295-311 with the fp32 router (router mode 0) and exact SiLU
+ * (swiglu mode 0) of qwen_moe_q3k.c:1925-1973.  Expert e's gate/up matrices
+ * start at row e*ffn of gate_exps/up_exps, its down matrix at row e*d of
+ * down_exps.  Only experts in [expert_lo, expert_hi) contribute to eout.    */
+void orc_moe_ffn(int d, int n_exp, int n_act, int ffn, int qtype,
+                 const float *router, const void *gate_exps, const void *up_exps,
+                 const void *down_exps, int expert_lo, int expert_hi,
+                 const float *hn_all, float *eout_all, int batch, int *sel_out, float *w_out,
+                 int nthreads)
+{
+    size_t rb_d = orc_row_bytes(qtype, d), rb_f = orc_row_bytes(qtype, ffn);
+    float *rl = (float *)malloc((size_t)n_exp * sizeof(float));
+    float *g = (float *)malloc((size_t)ffn * sizeof(float));
+    float *u = (float *)malloc((size_t)ffn * sizeof(float));
+    float *tmp = (float *)malloc((size_t)d * sizeof(float));
+    int sel[64];
+    float sw[64];
+    for (int b = 0; b < batch; b++) {
+        const float *hn = hn_all + (size_t)b * d;
+        float *eout = eout_all + (size_t)b * d;
+        for (int e = 0; e < n_exp; e++) {
+            const float *rw = router + (size_t)e * d;
+            float s = 0.f;
+            for (int i = 0; i < d; i++) s += rw[i] * hn[i];
+            rl[e] = s;
+        }
+        orc_softmax(rl, n_exp);
+        orc_topk(rl, n_exp, n_act, sel, sw);
+        if (sel_out) memcpy(sel_out + (size_t)b * n_act, sel, (size_t)n_act * sizeof(int));
+        if (w_out) memcpy(w_out + (size_t)b * n_act, sw, (size_t)n_act * sizeof(float));
+        for (int i = 0; i < d; i++) eout[i] = 0.f;
+        for (int a = 0; a < n_act; a++) {
+            int e = sel[a];
+            if (e < expert_lo || e >= expert_hi) continue;
+            float w = sw[a];
+            orc_qgemv_mt(qtype, ffn, d, (const uint8_t *)gate_exps + (size_t)e * ffn * rb_d, hn, g, 1, nthreads);
+            orc_qgemv_mt(qtype, ffn, d, (const uint8_t *)up_exps + (size_t)e * ffn * rb_d, hn, u, 1, nthreads);
+            for (int i = 0; i < ffn; i++) g[i] = orc_silu(g[i]) * u[i];
+            orc_qgemv_mt(qtype, d, ffn, (const uint8_t *)down_exps + (size_t)e * d * rb_f, g, tmp, 1, nthreads);
+            for (int i = 0; i < d; i++) eout[i] += w * tmp[i];
+        }
+    }
+    free(rl); free(g); free(u); free(tmp);
+}
+
+/* ---- decode-step pieces ----------------------------------------------------*/
+
+/* qwen_moe_q3k.c:1166 */
+void orc_rmsnorm(float *o, const float *x, const float *w, int n, float eps)
+{
+    float s = 0.f;
+    for (int i = 0; i < n; i++) s += x[i] * x[i];
+    s = 1.0f / sqrtf(s / n + eps);
+    for (int i = 0; i < n; i++) o[i] = x[i] * s * w[i];
+}
+
+/* qwen_moe.c:188 / qwen_moe_q3k.c:1170-1175: NEOX rotation of the pair
+ * (i, i + hd/2) by pos * base^(-2i/hd).                                     */
+void orc_rope_neox(float *v, int hd, int pos, float base)
+{
+    for (int i = 0; i < hd / 2; i++) {
+        float fr = powf(base, -2.0f * i / hd), a = pos * fr, c = cosf(a), s = sinf(a);
+        float x = v[i], y = v[i + hd / 2];
+        v[i] = x * c - y * s;
+        v[i + hd / 2] = x * s + y * c;
+    }
+}
+
+/* ---- generators ------------------------------------------------------------*/
+uint64_t orc_rng_seed(uint64_t s) { return s ? s : 0x243F6A8885A308D3ULL; }
+
+/* bench/q3k_probe.c:403-404 (xorshift64, shifts 13/7/17) */
+uint32_t orc_rng_u32(uint64_t *st)
+{
+    uint64_t x = *st;
+    x ^= x << 13; x ^= x >> 7; x ^= x << 17;
+    *st = x;
+    return (uint32_t)x;
+}
+
+void orc_fill_u8(uint64_t seed, uint8_t *dst, size_t n)
+{
+    uint64_t st = orc_rng_seed(seed);
+    for (size_t i = 0; i < n; i++) dst[i] = (uint8_t)orc_rng_u32(&st);
+}

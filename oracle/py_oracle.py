@@ -1,0 +1,191 @@
+"""ctypes view of oracle/liboracle.so and oracle/_ref/libx100ref.so.
+
+TEST INFRASTRUCTURE ONLY.  Imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg as the checker; the product library never calls
+it.  liboracle.so is this repository's C restatement of the reference's
+scalar paths (see x100_oracle.h for the file:line each function follows);
+libx100ref.so is the reference's own src/gemm_ref.c etc. compiled unchanged
+(built by oracle/Makefile when the reference tree is present).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+Q_F32, Q4_0, Q8_0, Q3_K, Q4_K = 0, 2, 8, 11, 12
+BLOCK_ELEMS = {Q_F32: 1, Q4_0: 32, Q8_0: 32, Q3_K: 256, Q4_K: 256}
+BLOCK_BYTES = {Q_F32: 4, Q4_0: 18, Q8_0: 34, Q3_K: 110, Q4_K: 144}
+QNAMES = {Q4_0: "Q4_0", Q8_0: "Q8_0", Q3_K: "Q3_K", Q4_K: "Q4_K", Q_F32: "F32"}
+
+_lib = None
+_ref = None
+
+
+def _ptr(a):
+    return C.c_void_p(a.ctypes.data) if a is not None else C.c_void_p(0)
+
+
+def build():
+    """Build liboracle.so (and _ref/ when the reference tree exists)."""
+    subprocess.check_call(["make", "-s", "-C", HERE, "all"])
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = C.CDLL(path)
+        vp, i, f = C.c_void_p, C.c_int, C.c_float
+        for name, args in {
+            "orc_gemm_i8": [i, i, i, vp, vp, vp],
+            "orc_gemm_f32": [i, i, i, vp, vp, vp],
+            "orc_gemm_i8_mt": [i, i, i, vp, vp, vp, i],
+            "orc_gemm_f32_mt": [i, i, i, vp, vp, vp, i],
+            "orc_ime2_pack_a": [i, i, vp, vp],
+            "orc_ime2_pack_b": [i, i, vp, vp],
+            "orc_dequant_row": [i, vp, i, vp],
+            "orc_quantize": [i, i, i, vp, vp],
+            "orc_qgemv_mt": [i, i, i, vp, vp, vp, i, i],
+            "orc_softmax": [vp, i],
+            "orc_topk": [vp, i, i, vp, vp],
+            "orc_moe_ffn": [i, i, i, i, i, vp, vp, vp, vp, i, i, vp, vp, i, vp, vp, i],
+            "orc_rmsnorm": [vp, vp, vp, i, f],
+            "orc_rope_neox": [vp, i, i, f],
+            "orc_fill_u8": [C.c_uint64, vp, C.c_size_t],
+            "orc_kq_scale_min": [i, vp, vp, vp],
+        }.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = None
+        L.orc_f16_to_f32.argtypes = [C.c_uint16]
+        L.orc_f16_to_f32.restype = C.c_float
+        L.orc_f32_to_f16_rne.argtypes = [C.c_float]
+        L.orc_f32_to_f16_rne.restype = C.c_uint16
+        L.orc_f32_to_f16_trunc.argtypes = [C.c_float]
+        L.orc_f32_to_f16_trunc.restype = C.c_uint16
+        L.orc_silu.argtypes = [C.c_float]
+        L.orc_silu.restype = C.c_float
+        _lib = L
+    return _lib
+
+
+def ref_lib():
+    """The reference's own GEMM sources compiled unchanged, or None."""
+    global _ref
+    if _ref is None:
+        path = os.path.join(HERE, "_ref", "libx100ref.so")
+        if not os.path.exists(path):
+            return None
+        L = C.CDLL(path)
+        for n in ("gemm_ref_i8", "gemm_ref_f32", "gemm_ime_i8", "gemm_rvv_f32"):
+            getattr(L, n).argtypes = [C.c_int] * 3 + [C.c_void_p] * 3
+            getattr(L, n).restype = None
+        _ref = L
+    return _ref
+
+
+# ---- generators ------------------------------------------------------------
+def fill_u8(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.uint8)
+    lib().orc_fill_u8(seed, _ptr(out), n)
+    return out
+
+
+def rand_i8(seed: int, n: int) -> np.ndarray:
+    """Uniform int8 in [-128, 127] from the reference's xorshift64 stream."""
+    return fill_u8(seed, n).view(np.int8)
+
+
+def rand_f32(seed: int, n: int, lo=-1.0, hi=1.0) -> np.ndarray:
+    """Uniform fp32 in [lo, hi) with 24-bit resolution (exactly representable)."""
+    u = fill_u8(seed, 4 * n).view(np.uint32)
+    return (lo + (hi - lo) * ((u >> 8).astype(np.float64) / float(1 << 24))).astype(np.float32)
+
+
+# ---- GEMM -------------------------------------------------------------------
+def gemm_i8(A, B, C, nthreads=1):
+    M, K = A.shape
+    N = B.shape[1]
+    assert A.dtype == np.int8 and B.dtype == np.int8 and C.dtype == np.int32
+    lib().orc_gemm_i8_mt(M, N, K, _ptr(A), _ptr(B), _ptr(C), nthreads)
+    return C
+
+
+def gemm_f32(A, B, C, nthreads=1):
+    M, K = A.shape
+    N = B.shape[1]
+    assert A.dtype == np.float32 and B.dtype == np.float32 and C.dtype == np.float32
+    lib().orc_gemm_f32_mt(M, N, K, _ptr(A), _ptr(B), _ptr(C), nthreads)
+    return C
+
+
+def ime2_pack(A, B):
+    M, K = A.shape
+    N = B.shape[1]
+    pa = np.empty(M * K, np.int8)
+    pb = np.empty(K * N, np.int8)
+    lib().orc_ime2_pack_a(M, K, _ptr(A), _ptr(pa))
+    lib().orc_ime2_pack_b(K, N, _ptr(B), _ptr(pb))
+    return pa, pb
+
+
+# ---- quantised formats --------------------------------------------------------
+def row_bytes(qtype: int, K: int) -> int:
+    be = BLOCK_ELEMS[qtype]
+    assert K % be == 0
+    return K // be * BLOCK_BYTES[qtype]
+
+
+def quantize(qtype: int, w: np.ndarray) -> np.ndarray:
+    w = np.ascontiguousarray(w, np.float32)
+    N, K = w.shape
+    out = np.zeros(N * row_bytes(qtype, K), np.uint8)
+    lib().orc_quantize(qtype, N, K, _ptr(w), _ptr(out))
+    return out
+
+
+def dequant(qtype: int, blocks: np.ndarray, N: int, K: int) -> np.ndarray:
+    out = np.empty((N, K), np.float32)
+    rb = row_bytes(qtype, K)
+    blocks = np.ascontiguousarray(blocks, np.uint8)
+    for n in range(N):
+        lib().orc_dequant_row(qtype, C.c_void_p(blocks.ctypes.data + n * rb), K,
+                              C.c_void_p(out.ctypes.data + n * K * 4))
+    return out
+
+
+def qgemv(qtype: int, blocks: np.ndarray, N: int, K: int, x: np.ndarray, nthreads=1):
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, K)
+    y = np.empty((x.shape[0], N), np.float32)
+    lib().orc_qgemv_mt(qtype, N, K, _ptr(blocks), _ptr(x), _ptr(y), x.shape[0], nthreads)
+    return y
+
+
+def moe_ffn(d, n_exp, n_act, ffn, qtype, router, gate, up, down, hn,
+            expert_lo=0, expert_hi=None, nthreads=1):
+    expert_hi = n_exp if expert_hi is None else expert_hi
+    hn = np.ascontiguousarray(hn, np.float32).reshape(-1, d)
+    B = hn.shape[0]
+    eout = np.empty((B, d), np.float32)
+    sel = np.empty((B, n_act), np.int32)
+    w = np.empty((B, n_act), np.float32)
+    lib().orc_moe_ffn(d, n_exp, n_act, ffn, qtype, _ptr(router), _ptr(gate), _ptr(up), _ptr(down),
+                      expert_lo, expert_hi, _ptr(hn), _ptr(eout), B, _ptr(sel), _ptr(w), nthreads)
+    return eout, sel, w
+
+
+def f16_to_f32(h: int) -> float:
+    return lib().orc_f16_to_f32(h)
+
+
+def rel_l2(y, ref) -> float:
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.linalg.norm(y - ref) / max(np.linalg.norm(ref), 1e-30))

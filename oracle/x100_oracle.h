@@ -1,0 +1,81 @@
+/*
+ * x100_oracle.h -- CPU restatement of the reference's scalar algorithms for
+ * the x100-gemm hot path.  TEST INFRASTRUCTURE ONLY: the parity tests, the
+ * smoke check and bench.py's CPU-baseline leg call it as the checker.  It is
+ * never linked into libx100gemm_b200.so and never used as a product path.
+ *
+ * Every function cites the reference file:line it restates (paths relative
+ * to the docdailey/x100-gemm tree).
+ */
+#ifndef X100_ORACLE_H
+#define X100_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- dense GEMM (C += A*B, row-major, beta = 1) ------------------------- */
+void orc_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, int32_t *C);
+void orc_gemm_f32(int M, int N, int K, const float *A, const float *B, float *C);
+/* row-sliced over `nthreads` POSIX threads (same per-row arithmetic)       */
+void orc_gemm_i8_mt(int M, int N, int K, const int8_t *A, const int8_t *B, int32_t *C, int nthreads);
+void orc_gemm_f32_mt(int M, int N, int K, const float *A, const float *B, float *C, int nthreads);
+/* IME-2 packed layouts of src/gemm_ime2_i8.c:40-56 */
+void orc_ime2_pack_a(int M, int K, const int8_t *A, int8_t *pa);
+void orc_ime2_pack_b(int K, int N, const int8_t *B, int8_t *pb);
+
+/* ---- fp16 ---------------------------------------------------------------- */
+float    orc_f16_to_f32(uint16_t h);          /* qwen_moe.c:115-118          */
+uint16_t orc_f32_to_f16_rne(float f);         /* IEEE round-to-nearest-even  */
+uint16_t orc_f32_to_f16_trunc(float f);       /* qwen_moe_hp.c:71-79         */
+
+/* ---- block formats: sizes ------------------------------------------------ */
+enum { ORC_F32 = 0, ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_Q3_K = 11, ORC_Q4_K = 12 };
+int    orc_block_elems(int qtype);            /* 32 or 256                    */
+int    orc_block_bytes(int qtype);            /* 18, 34, 110, 144             */
+size_t orc_row_bytes(int qtype, int K);
+
+/* ---- block formats: decode (n elements = whole blocks) ------------------ */
+void orc_dequant_row(int qtype, const void *blocks, int K, float *out);
+/* scale/min pair j of a K-quant 12-byte scale array (qwen_moe_q3k.c:534-538,
+ * repack.cpp:222-233)                                                      */
+void orc_kq_scale_min(int j, const uint8_t *q, uint8_t *sc, uint8_t *m);
+
+/* ---- block formats: encode (own encoders; the reference has no Q4_K/Q3_K
+ * encoder).  w has K elements per row, N rows.                             */
+void orc_quantize(int qtype, int N, int K, const float *w, void *blocks);
+
+/* ---- dequant-GEMV (fp32 x, fp32 accumulate in k order) ------------------- */
+/* y[b*N+n] = sum_k dequant(W)[n][k] * x[b*K+k]                             */
+void orc_qgemv(int qtype, int N, int K, const void *blocks, const float *x, float *y, int batch);
+void orc_qgemv_mt(int qtype, int N, int K, const void *blocks, const float *x, float *y,
+                  int batch, int nthreads);
+
+/* ---- MoE block (qwen_moe.c:295-311) -------------------------------------- */
+void orc_softmax(float *x, int n);            /* qwen_moe.c:189              */
+/* greedy top-k over p: strict >, lowest index wins, sentinel -1e30 (or -1
+ * for the qwen_moe.c variant -- identical for softmax probabilities).      */
+void orc_topk(const float *p, int n, int k, int *sel, float *w);
+float orc_silu(float x);                      /* x/(1+expf(-x)), qwen_moe.c:309 */
+void orc_moe_ffn(int d, int n_exp, int n_act, int ffn, int qtype,
+                 const float *router, const void *gate_exps, const void *up_exps,
+                 const void *down_exps, int expert_lo, int expert_hi,
+                 const float *hn, float *eout, int batch, int *sel_out, float *w_out,
+                 int nthreads);
+
+/* ---- decode-step pieces (qwen_moe_q3k.c:1166-1175, qwen_moe.c:186-189) -- */
+void orc_rmsnorm(float *o, const float *x, const float *w, int n, float eps);
+void orc_rope_neox(float *v, int hd, int pos, float base);
+
+/* ---- seeded generators (xorshift64 13/7/17 of bench/q3k_probe.c:403-405) */
+uint64_t orc_rng_seed(uint64_t s);
+uint32_t orc_rng_u32(uint64_t *state);
+void     orc_fill_u8(uint64_t seed, uint8_t *dst, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

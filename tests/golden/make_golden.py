@@ -1,0 +1,241 @@
+"""Generate the golden fixtures in tests/golden/ from the reference itself.
+
+Run in a container where the reference tree is mounted (REF_ROOT, default
+/root/reference); the fixtures it writes are committed so that the tests never
+need the reference at run time.
+
+What it pins, and from which reference code:
+  gemm_golden.npz   gemm_ref_i8 / gemm_ref_f32 of the reference's
+                    src/gemm_ref.c (compiled unchanged by oracle/Makefile into
+                    oracle/_ref/libx100ref.so) on xorshift64 inputs, C != 0
+                    on entry (beta = 1).
+  quant_golden.npz  the reference's own block decoders, compiled in a
+                    temporary directory straight out of its engine sources:
+                      Q4_0 / Q8_0  gguf_dequant_into   qwen_moe.c:156-179
+                      Q3_K         dequantize_q3_K_block qwen_moe_q3k.c:557-577
+                      Q4_K         dequantize_q5_K_block qwen_moe_q3k.c:541-552
+                                   on blocks whose fifth bit plane qh is zero
+                                   (a Q5_K block with qh = 0 decodes exactly
+                                   as the Q4_K block with the same d, dmin,
+                                   scales and qs)
+                    applied to random well-formed blocks (random bytes, fp16
+                    scales in a bounded range, as bench/q3k_probe.c:418-425
+                    builds its test blocks) plus edge blocks.
+  meta.json         struct-size known answers (block_q3_K 110 B,
+                    block_q5_K 176 B, bench/q3k_probe.c:410-413) and the
+                    x100_caps_t layout of the reference header.
+The extracted reference functions are compiled under a temporary directory
+and never written into this repository.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import hashlib
+import json
+import os
+import re
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+import py_oracle as po  # noqa: E402
+
+REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+
+GEMM_SHAPES = [(1, 1, 1), (3, 5, 7), (7, 9, 33), (16, 16, 16), (33, 17, 5),
+               (64, 48, 40), (128, 64, 96), (129, 130, 131)]
+GEMM_HASH_SHAPES = [(256, 256, 256)]
+
+
+def extract_function(src: str, signature_regex: str) -> str:
+    m = re.search(signature_regex, src)
+    if not m:
+        raise RuntimeError("signature not found: " + signature_regex)
+    start = m.start()
+    i = src.index("{", m.end() - 1)
+    depth = 0
+    for j in range(i, len(src)):
+        if src[j] == "{":
+            depth += 1
+        elif src[j] == "}":
+            depth -= 1
+            if depth == 0:
+                return src[start:j + 1]
+    raise RuntimeError("unbalanced braces")
+
+
+def extract_line(src: str, regex: str) -> str:
+    m = re.search(regex, src, re.M)
+    if not m:
+        raise RuntimeError("line not found: " + regex)
+    return m.group(0)
+
+
+def build_ref_decoders(tmp: str) -> C.CDLL:
+    moe = open(os.path.join(REF_ROOT, "qwen_moe.c")).read()
+    q3k = open(os.path.join(REF_ROOT, "qwen_moe_q3k.c")).read()
+    parts = [
+        "#include <stdio.h>\n#include <stdlib.h>\n#include <stdint.h>\n#include <string.h>\n#include <math.h>\n",
+        # qwen_moe.c: f16 decode, GGUF tensor structs, generic dequant
+        extract_function(moe, r"static float f16f\(uint16_t h\)\{"),
+        extract_line(moe, r"^typedef struct \{ uint32_t typ;.*\} TInfo;$"),
+        extract_line(moe, r"^typedef struct \{ unsigned char\*p;[^\n]*\n[^\n]*\} Gguf;$"),
+        extract_function(moe, r"static void gguf_dequant_into\(Gguf\*g,TInfo\*ti,size_t elem0,size_t n,float\*out\)\{"),
+        # qwen_moe_q3k.c: K-quant block types and decoders
+        extract_line(q3k, r"^typedef struct \{ uint8_t hmask\[32\];.*\} block_q3_K;.*$"),
+        extract_line(q3k, r"^typedef struct \{ _Float16 d; _Float16 dmin;.*\} block_q5_K;.*$"),
+        extract_function(q3k, r"static inline void q5k_get_scale_min\(int j,const uint8_t\*q,uint8_t\*d,uint8_t\*m\)\{"),
+        extract_function(q3k, r"static void dequantize_q5_K_block\(const block_q5_K\*x,float\*y\)\{"),
+        extract_function(q3k, r"static void dequantize_q3_K_block\(const block_q3_K\*x,float\*y\)\{"),
+        # thin exported wrappers (written here, not reference code)
+        """
+size_t golden_sizeof_q3k(void){ return sizeof(block_q3_K); }
+size_t golden_sizeof_q5k(void){ return sizeof(block_q5_K); }
+void golden_dq_q3k(const void*b,int nblk,float*out){ for(int i=0;i<nblk;i++) dequantize_q3_K_block((const block_q3_K*)b+i,out+256*i); }
+void golden_dq_q5k(const void*b,int nblk,float*out){ for(int i=0;i<nblk;i++) dequantize_q5_K_block((const block_q5_K*)b+i,out+256*i); }
+void golden_dq_gguf(unsigned typ,const void*data,size_t n,float*out){
+  Gguf g; memset(&g,0,sizeof g); g.p=(unsigned char*)data; g.data_start=0;
+  TInfo t; memset(&t,0,sizeof t); t.typ=typ; t.off=0; gguf_dequant_into(&g,&t,0,n,out); }
+""",
+    ]
+    path = os.path.join(tmp, "refdec.c")
+    with open(path, "w") as f:
+        f.write("\n".join(parts))
+    so = os.path.join(tmp, "librefdec.so")
+    subprocess.check_call(["gcc", "-std=gnu11", "-O2", "-ffp-contract=off", "-fPIC", "-shared",
+                           "-o", so, path, "-lm"])
+    L = C.CDLL(so)
+    L.golden_dq_q3k.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+    L.golden_dq_q5k.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+    L.golden_dq_gguf.argtypes = [C.c_uint, C.c_void_p, C.c_size_t, C.c_void_p]
+    L.golden_sizeof_q3k.restype = C.c_size_t
+    L.golden_sizeof_q5k.restype = C.c_size_t
+    return L
+
+
+def caps_layout(tmp: str) -> dict:
+    prog = os.path.join(tmp, "caps.c")
+    with open(prog, "w") as f:
+        f.write('#include <stdio.h>\n#include <stddef.h>\n#include "x100_gemm.h"\n'
+                'int main(void){printf("%zu %zu %zu %zu\\n", sizeof(x100_caps_t),'
+                ' offsetof(x100_caps_t, has_ime), offsetof(x100_caps_t, mvendorid),'
+                ' offsetof(x100_caps_t, isa)); return 0;}\n')
+    exe = os.path.join(tmp, "caps")
+    subprocess.check_call(["gcc", "-I", os.path.join(REF_ROOT, "include"), "-o", exe, prog])
+    s, hi, mv, isa = map(int, subprocess.check_output([exe]).split())
+    return {"sizeof": s, "has_ime": hi, "mvendorid": mv, "isa": isa}
+
+
+def f16_bytes(vals) -> np.ndarray:
+    return np.asarray(vals, np.float16).view(np.uint8).reshape(-1, 2)
+
+
+def random_blocks(qtype: int, n: int, seed: int) -> np.ndarray:
+    """Random well-formed blocks: random payload bytes, fp16 scales drawn from
+    +-[0.001, 0.08] (plus a few edge blocks appended by the caller)."""
+    rng = np.random.default_rng(seed)
+    bb = po.BLOCK_BYTES[qtype]
+    blk = rng.integers(0, 256, size=(n, bb), dtype=np.uint8)
+    mag = rng.uniform(0.001, 0.08, size=n) * rng.choice([-1.0, 1.0], size=n)
+    if qtype in (po.Q4_0, po.Q8_0):
+        blk[:, 0:2] = f16_bytes(mag)
+    elif qtype == po.Q4_K:
+        blk[:, 0:2] = f16_bytes(np.abs(mag))
+        blk[:, 2:4] = f16_bytes(rng.uniform(0.0, 0.05, size=n))
+    elif qtype == po.Q3_K:
+        blk[:, 108:110] = f16_bytes(mag)
+    return blk
+
+
+def edge_blocks(qtype: int) -> np.ndarray:
+    bb = po.BLOCK_BYTES[qtype]
+    out = []
+    z = np.zeros(bb, np.uint8)
+    out.append(z.copy())                                     # all zero
+    f = np.full(bb, 0xFF, np.uint8)                          # all ones payload
+    dpos = {po.Q4_0: [0], po.Q8_0: [0], po.Q4_K: [0, 2], po.Q3_K: [108]}[qtype]
+    for p in dpos:
+        f[p:p + 2] = f16_bytes([1.0])[0]
+    out.append(f)
+    sub = np.full(bb, 0x5A, np.uint8)                        # subnormal scale
+    for p in dpos:
+        sub[p:p + 2] = np.array([0x01, 0x00], np.uint8)
+    out.append(sub)
+    big = np.full(bb, 0xA5, np.uint8)                        # large scale
+    for p in dpos:
+        big[p:p + 2] = f16_bytes([-1024.0])[0]
+    out.append(big)
+    return np.stack(out)
+
+
+def to_q5k_layout(q4k: np.ndarray) -> np.ndarray:
+    """block_q4_K (d, dmin, scales[12], qs[128]) -> block_q5_K with qh = 0
+    (d, dmin, scales[12], qh[32], qs[128])."""
+    n = q4k.shape[0]
+    out = np.zeros((n, 176), np.uint8)
+    out[:, 0:16] = q4k[:, 0:16]
+    out[:, 48:176] = q4k[:, 16:144]
+    return out
+
+
+def main():
+    po.build()
+    ref = po.ref_lib()
+    if ref is None:
+        raise SystemExit("oracle/_ref/libx100ref.so missing: the reference tree is needed")
+    meta = {"ref_root": REF_ROOT, "gemm_shapes": GEMM_SHAPES, "gemm_hash_shapes": GEMM_HASH_SHAPES}
+    gem = {}
+    for (M, N, K) in GEMM_SHAPES + GEMM_HASH_SHAPES:
+        seed = 1000003 * M + 1009 * N + K
+        A = po.rand_i8(seed, M * K).reshape(M, K)
+        B = po.rand_i8(seed + 1, K * N).reshape(K, N)
+        C0 = po.rand_i8(seed + 2, M * N).astype(np.int32).reshape(M, N) * 1000
+        Ci = C0.copy()
+        ref.gemm_ref_i8(M, N, K, A.ctypes.data, B.ctypes.data, Ci.ctypes.data)
+        Af = po.rand_f32(seed + 3, M * K).reshape(M, K)
+        Bf = po.rand_f32(seed + 4, K * N).reshape(K, N)
+        Cf = po.rand_f32(seed + 5, M * N).reshape(M, N)
+        ref.gemm_ref_f32(M, N, K, Af.ctypes.data, Bf.ctypes.data, Cf.ctypes.data)
+        key = f"{M}x{N}x{K}"
+        if (M, N, K) in GEMM_SHAPES:
+            gem[f"i8_{key}"] = Ci
+            gem[f"f32_{key}"] = Cf
+        else:
+            meta[f"sha256_i8_{key}"] = hashlib.sha256(Ci.tobytes()).hexdigest()
+            meta[f"sha256_f32_{key}"] = hashlib.sha256(Cf.tobytes()).hexdigest()
+    np.savez_compressed(os.path.join(HERE, "gemm_golden.npz"), **gem)
+
+    with tempfile.TemporaryDirectory() as tmp:
+        dec = build_ref_decoders(tmp)
+        meta["sizeof_block_q3_K"] = int(dec.golden_sizeof_q3k())
+        meta["sizeof_block_q5_K"] = int(dec.golden_sizeof_q5k())
+        meta["caps_layout"] = caps_layout(tmp)
+        qg = {}
+        for qtype, name in ((po.Q4_0, "Q4_0"), (po.Q8_0, "Q8_0"), (po.Q3_K, "Q3_K"), (po.Q4_K, "Q4_K")):
+            blk = np.concatenate([random_blocks(qtype, 96, 77 + qtype), edge_blocks(qtype)])
+            blk = np.ascontiguousarray(blk)
+            nb = blk.shape[0]
+            be = po.BLOCK_ELEMS[qtype]
+            out = np.zeros(nb * be, np.float32)
+            if qtype in (po.Q4_0, po.Q8_0):
+                dec.golden_dq_gguf(qtype, blk.ctypes.data, nb * be, out.ctypes.data)
+            elif qtype == po.Q3_K:
+                dec.golden_dq_q3k(blk.ctypes.data, nb, out.ctypes.data)
+            else:
+                q5 = np.ascontiguousarray(to_q5k_layout(blk))
+                dec.golden_dq_q5k(q5.ctypes.data, nb, out.ctypes.data)
+            qg[f"{name}_blocks"] = blk
+            qg[f"{name}_values"] = out
+        np.savez_compressed(os.path.join(HERE, "quant_golden.npz"), **qg)
+    with open(os.path.join(HERE, "meta.json"), "w") as f:
+        json.dump(meta, f, indent=1, sort_keys=True)
+    print("wrote gemm_golden.npz, quant_golden.npz, meta.json")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,163 @@
+"""Pin the CPU oracle against fixtures produced by the reference's own code.
+
+The fixtures (tests/golden/*.npz, meta.json) were written by
+tests/golden/make_golden.py from the reference's src/gemm_ref.c and from its
+block decoders (qwen_moe.c:156-179, qwen_moe_q3k.c:541-577).  Every check
+here is bit-exact.
+"""
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+import py_oracle as po
+
+QT = {"Q4_0": po.Q4_0, "Q8_0": po.Q8_0, "Q3_K": po.Q3_K, "Q4_K": po.Q4_K}
+
+
+@pytest.fixture(scope="module")
+def meta(golden_dir):
+    with open(os.path.join(golden_dir, "meta.json")) as f:
+        return json.load(f)
+
+
+@pytest.fixture(scope="module")
+def gemm_golden(golden_dir):
+    return np.load(os.path.join(golden_dir, "gemm_golden.npz"))
+
+
+@pytest.fixture(scope="module")
+def quant_golden(golden_dir):
+    return np.load(os.path.join(golden_dir, "quant_golden.npz"))
+
+
+def gemm_inputs(M, N, K):
+    seed = 1000003 * M + 1009 * N + K
+    A = po.rand_i8(seed, M * K).reshape(M, K)
+    B = po.rand_i8(seed + 1, K * N).reshape(K, N)
+    C0 = po.rand_i8(seed + 2, M * N).astype(np.int32).reshape(M, N) * 1000
+    Af = po.rand_f32(seed + 3, M * K).reshape(M, K)
+    Bf = po.rand_f32(seed + 4, K * N).reshape(K, N)
+    Cf = po.rand_f32(seed + 5, M * N).reshape(M, N)
+    return A, B, C0, Af, Bf, Cf
+
+
+def test_struct_sizes(meta):
+    # bench/q3k_probe.c:410-413 known answers
+    assert meta["sizeof_block_q3_K"] == 110 == po.BLOCK_BYTES[po.Q3_K]
+    assert meta["sizeof_block_q5_K"] == 176
+    assert po.BLOCK_BYTES[po.Q4_K] == 144 and po.BLOCK_BYTES[po.Q4_0] == 18 and po.BLOCK_BYTES[po.Q8_0] == 34
+
+
+def test_caps_layout_matches_reference_header(meta):
+    import ctypes
+
+    class Caps(ctypes.Structure):
+        _fields_ = [("vlen_bits", ctypes.c_int), ("vlenb", ctypes.c_int), ("has_v", ctypes.c_int),
+                    ("has_zvfh", ctypes.c_int), ("has_zvbb", ctypes.c_int), ("has_ime", ctypes.c_int),
+                    ("mvendorid", ctypes.c_ulong), ("isa", ctypes.c_char * 1024)]
+    lay = meta["caps_layout"]
+    assert ctypes.sizeof(Caps) == lay["sizeof"]
+    assert Caps.has_ime.offset == lay["has_ime"]
+    assert Caps.mvendorid.offset == lay["mvendorid"]
+    assert Caps.isa.offset == lay["isa"]
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (3, 5, 7), (7, 9, 33), (16, 16, 16), (33, 17, 5),
+                                   (64, 48, 40), (128, 64, 96), (129, 130, 131)])
+def test_oracle_gemm_matches_reference(gemm_golden, shape):
+    M, N, K = shape
+    A, B, C0, Af, Bf, Cf = gemm_inputs(M, N, K)
+    Ci = po.gemm_i8(A, B, C0.copy())
+    np.testing.assert_array_equal(Ci, gemm_golden[f"i8_{M}x{N}x{K}"])
+    Co = po.gemm_f32(Af, Bf, Cf.copy())
+    assert Co.tobytes() == gemm_golden[f"f32_{M}x{N}x{K}"].tobytes()
+
+
+def test_oracle_gemm_256_hash(meta):
+    M = N = K = 256
+    A, B, C0, Af, Bf, Cf = gemm_inputs(M, N, K)
+    Ci = po.gemm_i8(A, B, C0.copy(), nthreads=4)
+    assert hashlib.sha256(Ci.tobytes()).hexdigest() == meta["sha256_i8_256x256x256"]
+    Co = po.gemm_f32(Af, Bf, Cf.copy(), nthreads=4)
+    assert hashlib.sha256(Co.tobytes()).hexdigest() == meta["sha256_f32_256x256x256"]
+
+
+@pytest.mark.parametrize("name", ["Q4_0", "Q8_0", "Q3_K", "Q4_K"])
+def test_oracle_decode_matches_reference(quant_golden, name):
+    qt = QT[name]
+    blk = quant_golden[f"{name}_blocks"]
+    ref = quant_golden[f"{name}_values"]
+    be = po.BLOCK_ELEMS[qt]
+    nb = blk.shape[0]
+    got = po.dequant(qt, blk.reshape(-1), 1, nb * be).reshape(-1)
+    # bit-exact, NaN-aware (edge blocks may decode to inf*0 = nan)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)) or \
+        np.array_equal(got, ref, equal_nan=True)
+
+
+def test_f16_conversions():
+    for v in (0.0, 1.0, -2.5, 65504.0, 6.1e-5, 5.96e-8, 0.1):
+        h = po.lib().orc_f32_to_f16_rne(v)
+        assert np.float16(v).view(np.uint16) == h
+        assert po.f16_to_f32(h) == float(np.float16(v))
+    # the reference's truncating encoder (qwen_moe_hp.c:71-79) rounds toward zero
+    t = po.lib().orc_f32_to_f16_trunc(0.1)
+    assert po.f16_to_f32(t) <= 0.1 and po.f16_to_f32(t) > 0.0999
+
+
+@pytest.mark.parametrize("qt", [po.Q4_0, po.Q8_0, po.Q3_K, po.Q4_K])
+def test_encoder_roundtrip(qt):
+    """Own encoders: quantise N(0, 0.02) weights, decode, bounded error."""
+    rng = np.random.default_rng(5)
+    N, K = 8, 512
+    w = rng.normal(0, 0.02, size=(N, K)).astype(np.float32)
+    blk = po.quantize(qt, w)
+    assert blk.size == N * po.row_bytes(qt, K)
+    wd = po.dequant(qt, blk, N, K)
+    err = po.rel_l2(wd, w)
+    bound = {po.Q8_0: 0.01, po.Q4_0: 0.15, po.Q4_K: 0.12, po.Q3_K: 0.30}[qt]
+    assert err < bound, (po.QNAMES[qt], err)
+    # idempotence: re-encoding the decoded weights reproduces the same values
+    wd2 = po.dequant(qt, po.quantize(qt, wd), N, K)
+    assert po.rel_l2(wd2, wd) < bound
+
+
+def test_q4_0_encoder_follows_baseline_rule():
+    """scale = max|w|/7 stored as fp16, q = round(w/scale) in [-7, 7]."""
+    rng = np.random.default_rng(9)
+    w = rng.normal(0, 0.02, size=(1, 32)).astype(np.float32)
+    blk = po.quantize(po.Q4_0, w)
+    d = np.frombuffer(blk[:2].tobytes(), np.float16)[0]
+    assert abs(float(d) - np.abs(w).max() / 7) <= 1e-3 * abs(float(d)) + 1e-7
+    qs = blk[2:18]
+    nibs = np.concatenate([qs & 0xF, qs >> 4]).astype(int) - 8
+    assert nibs.min() >= -7 and nibs.max() <= 7
+
+
+def test_topk_tie_break_and_renorm():
+    p = np.array([0.1, 0.3, 0.3, 0.05, 0.25], np.float32)
+    sel = np.zeros(3, np.int32)
+    w = np.zeros(3, np.float32)
+    po.lib().orc_topk(po._ptr(p), 5, 3, po._ptr(sel), po._ptr(w))
+    assert list(sel) == [1, 2, 4]          # strict >: lower index first on a tie
+    assert abs(w.sum() - 1.0) < 1e-6
+
+
+def test_moe_oracle_partial_experts_sum_to_full():
+    """Expert-parallel property: partial eouts over disjoint expert ranges
+    add up to the full block output (same routing everywhere)."""
+    rng = np.random.default_rng(3)
+    d, E, k, ffn = 256, 16, 4, 256
+    router = rng.normal(0, 0.02, size=(E, d)).astype(np.float32)
+    gate = po.quantize(po.Q4_K, rng.normal(0, 0.02, size=(E * ffn, d)).astype(np.float32))
+    up = po.quantize(po.Q4_K, rng.normal(0, 0.02, size=(E * ffn, d)).astype(np.float32))
+    down = po.quantize(po.Q4_K, rng.normal(0, 0.02, size=(E * d, ffn)).astype(np.float32))
+    hn = rng.normal(0, 1, size=(2, d)).astype(np.float32)
+    full, sel, w = po.moe_ffn(d, E, k, ffn, po.Q4_K, router, gate, up, down, hn)
+    parts = [po.moe_ffn(d, E, k, ffn, po.Q4_K, router, gate, up, down, hn, lo, lo + 4)[0]
+             for lo in range(0, E, 4)]
+    assert po.rel_l2(sum(parts), full) < 1e-6
+    assert np.allclose(w.sum(1), 1.0, atol=1e-6)
