@@ -1,0 +1,434 @@
+#!/usr/bin/env python3
+"""Benchmark of the x100-gemm hot path on B200 (one process per GPU).
+
+Default workload (the BASELINE metric's first item, configs[1]): the exact
+int8 x int8 -> int32 GEMM C += A.B at M = N = K = 8192 through the tcgen05
+kernel of libx100gemm_b200.so.  With --gpus N (under torchrun) B and C are
+split by columns across ranks (8192/N columns each, A replicated): total
+work is fixed, so scaling is "strong"; no collective touches the data path.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload W]
+                  [--impl reference]
+
+Prints ONE JSON line on rank 0.  `value` is whole-job throughput with the
+operands resident in HBM (CUDA events on the launching stream, max over
+ranks); `e2e` is the same metric through the reference-signature host API
+(gemm_ime_i8 with pinned host buffers: H2D of A, B, C and D2H of C inside
+the timed region).  --impl reference times the reference's own CPU code
+(oracle/_ref/libx100ref.so: the reference's src/gemm_ref.c compiled
+unchanged) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "x100-gemm_b200"))
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="x100", choices=["x100", "reference"])
+    ap.add_argument("--workload", default="gemm_i8",
+                    choices=["gemm_i8", "gemm_f16", "gemm_f32", "q4gemv", "moe"])
+    ap.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workloads")
+    ap.add_argument("--batch", type=int, default=1, help="tokens per step for q4gemv / moe")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def load_traffic(key):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary
+    (profiles/roofline_traffic.txt lines: '<key> <bytes>')."""
+    p = os.path.join(REPO, "profiles", "roofline_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == key:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+# ---- clocks --------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.th.join(timeout=2)
+        mhz, maxmhz, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            c = [x.strip() for x in ln.split(",")]
+            if len(c) < 9:
+                continue
+            try:
+                mhz.append(float(c[1]))
+                maxmhz = float(c[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, c[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not mhz:
+            return None
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": maxmhz, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# ---- distributed plumbing ---------------------------------------------------------------
+class Dist:
+    def __init__(self, n):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world != n:
+            raise SystemExit(f"--gpus {n} but WORLD_SIZE={self.world}")
+
+    def init(self):
+        import torch
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+    def physical_gpu(self):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            ids = [x for x in vis.split(",") if x]
+            if self.local < len(ids):
+                return ids[self.local]
+        return str(self.local)
+
+
+# ---- CPU baseline (reference code on the host cores) -----------------------------------------
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def ref_gemm_i8_rows(M, N, K, rows, nthreads):
+    """Run the reference's gemm_ref_i8 (oracle/_ref/libx100ref.so) on a
+    `rows` x N x K slice of the M x N x K problem, row-sliced over
+    `nthreads` host threads; returns (seconds, ops, kind)."""
+    import numpy as np
+    import py_oracle as po
+    ref = po.ref_lib()
+    kind = "reference"
+    if ref is None:
+        kind = "port"
+    A = po.rand_i8(11, rows * K).reshape(rows, K)
+    B = po.rand_i8(12, K * N).reshape(K, N)
+    C = np.zeros((rows, N), np.int32)
+    per = [(rows * t) // nthreads for t in range(nthreads + 1)]
+
+    def work(t):
+        r0, r1 = per[t], per[t + 1]
+        if r1 <= r0:
+            return
+        a = A[r0:r1]
+        c = C[r0:r1]
+        if ref is not None:
+            ref.gemm_ref_i8(r1 - r0, N, K, a.ctypes.data, B.ctypes.data, c.ctypes.data)
+        else:
+            po.lib().orc_gemm_i8(r1 - r0, N, K, po._ptr(a), po._ptr(B), po._ptr(c))
+
+    th = [threading.Thread(target=work, args=(t,)) for t in range(nthreads)]
+    t0 = time.perf_counter()
+    for x in th:
+        x.start()
+    for x in th:
+        x.join()
+    dt = time.perf_counter() - t0
+    return dt, 2.0 * rows * N * K, kind
+
+
+def cpu_baseline_gemm_i8(size, target_s=8.0):
+    nt = cpu_threads()
+    # calibrate on one row per thread, then size the sample for ~target_s
+    dt, ops, kind = ref_gemm_i8_rows(size, size, size, nt, nt)
+    rate = ops / max(dt, 1e-9)
+    rows = int(min(size, max(nt, rate * target_s / (2.0 * size * size))))
+    rows = max(nt, rows // nt * nt)
+    dt, ops, kind = ref_gemm_i8_rows(size, size, size, rows, nt)
+    return {"value": ops / dt / 1e12, "unit": "TOPS", "cores": nt, "kind": kind,
+            "sample": f"gemm_ref_i8 on rows 0..{rows - 1} of the {size}^3 problem ({rows}x{size}x{size}), "
+                      f"row-sliced over {nt} host threads, {dt:.2f} s"}
+
+
+# ---- GEMM workloads -----------------------------------------------------------------------
+def bench_gemm(args, dist, peaks, peak_src):
+    import numpy as np
+    import torch
+    import x100b
+
+    kind = args.workload
+    S = args.size
+    world, rank = dist.world, dist.rank
+    if S % world:
+        raise SystemExit("size must divide by the GPU count")
+    M, K = S, S
+    N = S // world                       # this rank's column slice of B and C
+    es = {"gemm_i8": 1, "gemm_f16": 2, "gemm_f32": 4}[kind]
+    ce = 2 if kind == "gemm_f16" else 4
+    set_bytes = M * K * es + K * N * es + M * N * ce
+    nsets = max(1, -(-2 * L2_BYTES // set_bytes))     # rotate so reuse distance > 2 x L2
+    nsets = min(nsets, 8)
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    sets = []
+    for _ in range(nsets):
+        if kind == "gemm_i8":
+            A = torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+            B = torch.randint(-128, 128, (K, N), dtype=torch.int8, device="cuda", generator=g)
+            C = torch.zeros((M, N), dtype=torch.int32, device="cuda")
+        else:
+            dt_ = torch.float16 if kind == "gemm_f16" else torch.float32
+            A = (torch.rand((M, K), device="cuda", generator=g) * 2 - 1).to(dt_)
+            B = (torch.rand((K, N), device="cuda", generator=g) * 2 - 1).to(dt_)
+            C = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+        sets.append((A, B, C))
+    fn = {"gemm_i8": "gemm_ime_i8_dev", "gemm_f16": "gemm_f16_f32acc_dev", "gemm_f32": "gemm_f32_dev"}[kind]
+    stream = torch.cuda.current_stream()
+    L = x100b.lib()
+    cfn = getattr(L, fn)
+    sptr = stream.cuda_stream
+
+    def step(i):
+        A, B, C = sets[i % nsets]
+        rc = cfn(M, N, K, A.data_ptr(), B.data_ptr(), C.data_ptr(), sptr)
+        if rc:
+            raise x100b.X100Error(rc, fn)
+
+    # parity spot-check before timing (tensor cores vs the exact CUDA-core kernel)
+    if kind == "gemm_i8":
+        A, B, _ = sets[0]
+        Ct = torch.zeros((256, N), dtype=torch.int32, device="cuda")
+        Cr = torch.zeros_like(Ct)
+        x100b.gemm_dev("gemm_ime_i8_dev", A[:256], B, Ct)
+        x100b.gemm_dev("gemm_ref_i8_dev", A[:256], B, Cr)
+        x100b.sync()
+        assert torch.equal(Ct, Cr), "tensor-core GEMM disagrees with the exact kernel"
+
+    for i in range(args.warmup):
+        step(i)
+    x100b.sync()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(dist.physical_gpu())
+    clk.start()
+    time.sleep(0.3)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev[0].record(stream)
+    for i in range(args.steps):
+        step(i)
+        ev[i + 1].record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = clk.stop()
+    st = x100b.lib().x100_sync(sptr)
+    if st:
+        raise x100b.X100Error(st, "device status after timing")
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    total_ms = ev[0].elapsed_time(ev[-1])
+    total_ms = dist.max(total_ms)
+    ops_rank = 2.0 * M * N * K
+    ops_total = 2.0 * S * S * S
+    value = ops_total * args.steps / (total_ms / 1e3) / 1e12
+    kernel_ms = statistics.mean(per)
+    achieved = ops_rank / (kernel_ms / 1e3) / 1e12
+    if kind == "gemm_i8":
+        peak = 2.0 * peaks["bf16_tflops"]
+        peak_note = (f"2 x bf16_tflops ({peak_src} MEASURED_PEAKS.json burst): tcgen05 kind::i8 issues at "
+                     "twice the kind::f16 dense rate (4.5 vs 2.25 POPS nominal)")
+        unit = "TOPS"
+    elif kind == "gemm_f16":
+        peak = peaks["bf16_tflops"]
+        peak_note = f"bf16_tflops ({peak_src} MEASURED_PEAKS.json burst); kind::f16 runs at the bf16 rate"
+        unit = "TFLOP/s"
+    else:
+        peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        peak_note = "nominal CUDA-core fp32 FMA peak: 148 SMs x 128 lanes x 2 x 1.965 GHz"
+        unit = "TFLOP/s"
+    traffic = load_traffic(f"{kind}_{S}_{world}")
+
+    # ---- end to end through the reference-signature host API ----
+    e2e = None
+    if kind in ("gemm_i8", "gemm_f32"):
+        hostfn = {"gemm_i8": L.gemm_ime_i8, "gemm_f32": L.gemm_rvv_f32}[kind]
+        A, B, C = sets[0]
+        Ah = torch.empty(A.shape, dtype=A.dtype, pin_memory=True).copy_(A)
+        Bh = torch.empty(B.shape, dtype=B.dtype, pin_memory=True).copy_(B)
+        Ch = torch.zeros(C.shape, dtype=C.dtype, pin_memory=True)
+        e2e_steps = max(3, min(args.steps, 10))
+        hostfn(M, N, K, Ah.data_ptr(), Bh.data_ptr(), Ch.data_ptr())        # warm-up
+        x100b.check_last("host gemm warm-up")
+        dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            hostfn(M, N, K, Ah.data_ptr(), Bh.data_ptr(), Ch.data_ptr())
+        x100b.check_last("host gemm")
+        dt = dist.max(time.perf_counter() - t0)
+        dist.barrier()
+        e2e = {"value": ops_total * e2e_steps / dt / 1e12, "unit": unit,
+               "h2d_bytes_per_step": int(A.numel() * A.element_size() + B.numel() * B.element_size()
+                                         + C.numel() * C.element_size()),
+               "d2h_bytes_per_step": int(C.numel() * C.element_size()),
+               "steps": e2e_steps,
+               "api": f"{hostfn.__name__}(M,N,K,A,B,C) with pinned host buffers (synchronous call)"}
+
+    cpu = None
+    if kind == "gemm_i8" and world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_gemm_i8(S)
+
+    metric = {"gemm_i8": "int8 GEMM TOPS", "gemm_f16": "fp16 GEMM (fp32 accumulate) TFLOP/s",
+              "gemm_f32": "fp32 GEMM TFLOP/s"}[kind]
+    line = {
+        "metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": {"gemm_i8": "int8", "gemm_f16": "fp16", "gemm_f32": "fp32"}[kind],
+        "data": "synthetic (uniform int8 in [-128,127] / uniform [-1,1]), generated on device",
+        "config": {"workload": f"{kind} C+=A.B M=N=K={S}" + (f", B/C column-sharded 1/{world} per GPU"
+                                                              if world > 1 else ""),
+                   "M": S, "N": S, "K": S, "parallelism": f"n-shard{world}" if world > 1 else "single",
+                   "l2": f"inputs rotate over {nsets} buffer set(s) of {set_bytes / 2**20:.0f} MiB per GPU "
+                         f"(> L2 between reuses)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": unit,
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_note,
+                     "kernel": "x100::tc::gemm_tc_kernel" if kind != "gemm_f32" else "gemm_fast_kernel",
+                     "algorithmic_ops_per_launch": ops_rank,
+                     "kernel_ms_mean": round(kernel_ms, 4)},
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "cpu_baseline": cpu,
+    }
+    return line
+
+
+def bench_reference(args):
+    """--impl reference: the reference's own CPU GEMM on this host's cores."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
+    S = args.size
+    nt = cpu_threads()
+    vals = []
+    for i in range(args.warmup + args.steps):
+        rows = nt * 2
+        dt, ops, kind = ref_gemm_i8_rows(S, S, S, rows, nt)
+        if i >= args.warmup:
+            vals.append(ops / dt / 1e12)
+    v = statistics.mean(vals)
+    return {
+        "impl": "reference", "metric": "int8 GEMM TOPS", "value": v, "unit": "TOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"gemm_i8 C+=A.B M=N=K={S}", "M": S, "N": S, "K": S},
+        "cpu_baseline": {"value": v, "unit": "TOPS", "cores": nt, "kind": kind,
+                         "sample": f"each step: gemm_ref_i8 (reference src/gemm_ref.c) on {2 * nt} rows of "
+                                   f"the {S}^3 problem, row-sliced over {nt} host threads"},
+        "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        line = bench_reference(args)
+        if line:
+            print(json.dumps(line))
+        return
+    dist = Dist(args.gpus)
+    dist.init()
+    peaks, src = load_peaks()
+    try:
+        if args.workload.startswith("gemm"):
+            line = bench_gemm(args, dist, peaks, src)
+        else:
+            import bench_quant
+            line = bench_quant.run(args, dist, peaks, src)
+    finally:
+        dist.close()
+    if dist.rank == 0:
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -30,6 +30,9 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -105,6 +108,15 @@ int gemm_f16_f32acc_dev(int M, int N, int K, const void *A, const void *B, float
 int gemm_f16_dev      (int M, int N, int K, const void *A, const void *B, void *C, void *stream);
 int gemm_f32_dev      (int M, int N, int K, const float *A, const float *B, float *C, void *stream);
 int gemm_ref_f32_dev  (int M, int N, int K, const float *A, const float *B, float *C, void *stream);
+/* int8 GEMM with explicit leading dimensions (elements); tensor cores when
+ * A, B are 16-byte aligned and lda, ldb are multiples of 16, CUDA cores
+ * otherwise.                                                                */
+int gemm_ime_i8_dev_ld(int M, int N, int K, const int8_t *A, long lda, const int8_t *B, long ldb,
+                       int32_t *C, long ldc, void *stream);
+/* Synchronise `stream` and return the status the library's kernels left in
+ * the device status word (0, or X100_E_TIMEOUT when a bounded device-side
+ * wait gave up), clearing it.                                               */
+int x100_sync(void *stream);
 
 /* ---- errors and device selection (new) ---------------------------------- */
 enum {
@@ -128,5 +140,8 @@ int         x100_set_device(int device);
 
 #ifdef __cplusplus
 }
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility pop
 #endif
 #endif /* X100_GEMM_H */

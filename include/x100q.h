@@ -27,6 +27,9 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -98,5 +101,8 @@ int x100q_moe_ffn_dev(const x100q_moe *moe, const float *hn, float *eout, int ba
 
 #ifdef __cplusplus
 }
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility pop
 #endif
 #endif /* X100Q_H */

@@ -1,0 +1,66 @@
+// runtime.h -- host-side runtime of libx100gemm_b200.so: per-device context
+// (stream, status word, grow-only staging buffers, tensor-map encoder),
+// thread-local error reporting, pointer classification and the host-side
+// fault injector.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <mutex>
+
+#include "../../include/x100_gemm.h"
+
+namespace x100 {
+
+// Per-thread status of the last API call.
+void set_error(int code);
+int get_error();
+
+// X100_FAULT=<site>[,<site>...] makes the library fail at that site without
+// touching the GPU: "alloc", "copy", "launch", "device", "comm".  Returns
+// true (and records X100_E_INJECTED) when the site is armed.
+bool fault_injected(const char *site);
+
+// A grow-only device buffer owned by a context.
+struct DevBuf {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+};
+
+struct DevCtx {
+    int device = -1;
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+    size_t smem_optin = 0;
+    cudaStream_t stream = nullptr;   // stream of the synchronous host-pointer API
+    int *d_status = nullptr;         // device status word written by kernels
+    DevBuf stage[4];                 // staging buffers of host-pointer calls
+    std::mutex mu;                   // serialises host-pointer calls on this device
+};
+
+// Context of the calling thread's selected device (created on first use).
+// Returns nullptr and records the error if no usable device exists.
+DevCtx *ctx();
+int current_device();
+
+// Ensure staging buffer `slot` of `c` holds at least `bytes`; returns its
+// device pointer or nullptr (error recorded).
+void *stage_buf(DevCtx *c, int slot, size_t bytes);
+
+// True when `p` is device (or managed) memory usable by kernels directly.
+bool is_device_ptr(const void *p);
+
+// Encode a 2-D row-major tensor map: `inner` elements per row (contiguous),
+// `outer` rows, `row_stride_bytes` between rows, box `box_inner` x
+// `box_outer`, 128-byte swizzle, out-of-bounds elements read as zero.
+bool make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+
+// Map a CUDA error to an X100 status and record it.  Returns the status.
+int check_cuda(cudaError_t e, int code_if_error);
+
+// Read and clear the device status word after synchronising `s`.
+int sync_and_status(DevCtx *c, cudaStream_t s);
+
+}  // namespace x100

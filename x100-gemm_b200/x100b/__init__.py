@@ -1,0 +1,232 @@
+"""Python binding of libx100gemm_b200.so (ctypes over the C ABI).
+
+The library is the product: hand-written sm_100a kernels behind the C ABI
+declared in include/x100_gemm.h and include/x100q.h.  This module only loads
+it, declares the signatures and offers numpy / torch conveniences for the
+tests and bench.py.  There is no fallback: if the shared library is missing
+or a call fails, an exception is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+import numpy as np
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REPO = os.path.dirname(PKG_DIR)
+LIB_PATH = os.path.join(PKG_DIR, "libx100gemm_b200.so")
+HEADERS = [os.path.join(REPO, "include", "x100_gemm.h"), os.path.join(REPO, "include", "x100q.h")]
+
+X100_OK, X100_E_ARG, X100_E_NODEV, X100_E_ARCH, X100_E_ALLOC, X100_E_COPY, X100_E_LAUNCH, \
+    X100_E_TIMEOUT, X100_E_COMM, X100_E_INJECTED, X100_E_UNSUPPORTED = range(11)
+
+Q_F32, Q4_0, Q8_0, Q3_K, Q4_K = 0, 2, 8, 11, 12
+
+
+class X100Error(RuntimeError):
+    def __init__(self, code: int, what: str = ""):
+        self.code = code
+        super().__init__(f"{what}: x100 error {code} ({strerror(code)})")
+
+
+class Caps(C.Structure):
+    _fields_ = [("vlen_bits", C.c_int), ("vlenb", C.c_int), ("has_v", C.c_int), ("has_zvfh", C.c_int),
+                ("has_zvbb", C.c_int), ("has_ime", C.c_int), ("mvendorid", C.c_ulong), ("isa", C.c_char * 1024)]
+
+
+_lib = None
+vp, i32, i64 = C.c_void_p, C.c_int, C.c_long
+
+_SIGS = {
+    # reference signatures (void)
+    "gemm_ref_f32": ([i32, i32, i32, vp, vp, vp], None),
+    "gemm_rvv_f32": ([i32, i32, i32, vp, vp, vp], None),
+    "gemm_rvv_f16": ([i32, i32, i32, vp, vp, vp], None),
+    "gemm_f16_f32acc": ([i32, i32, i32, vp, vp, vp], None),
+    "gemm_ref_i8": ([i32, i32, i32, vp, vp, vp], None),
+    "gemm_ime_i8": ([i32, i32, i32, vp, vp, vp], None),
+    "gemm_ime2_pack_a": ([i32, i32, vp, vp], None),
+    "gemm_ime2_pack_b": ([i32, i32, vp, vp], None),
+    "gemm_ime2_i8_st": ([i32, i32, i32, vp, vp, vp], None),
+    "gemm_ime2_i8_mt": ([i32, i32, i32, vp, vp, vp, i32], None),
+    "x100_detect": ([vp], None),
+    "x100_caps_print": ([vp], None),
+    # device variants
+    "gemm_ime_i8_dev": ([i32, i32, i32, vp, vp, vp, vp], i32),
+    "gemm_ref_i8_dev": ([i32, i32, i32, vp, vp, vp, vp], i32),
+    "gemm_f16_f32acc_dev": ([i32, i32, i32, vp, vp, vp, vp], i32),
+    "gemm_f16_dev": ([i32, i32, i32, vp, vp, vp, vp], i32),
+    "gemm_f32_dev": ([i32, i32, i32, vp, vp, vp, vp], i32),
+    "gemm_ref_f32_dev": ([i32, i32, i32, vp, vp, vp, vp], i32),
+    "gemm_ime_i8_dev_ld": ([i32, i32, i32, vp, i64, vp, i64, vp, i64, vp], i32),
+    "x100_sync": ([vp], i32),
+    "x100_last_error": ([], i32),
+    "x100_strerror": ([i32], C.c_char_p),
+    "x100_set_device": ([i32], i32),
+    # quantised path
+    "x100q_row_bytes": ([i32, i32], C.c_size_t),
+    "x100q_lin_create": ([i32, i32, i32, vp], vp),
+    "x100q_lin_destroy": ([vp], None),
+    "x100q_lin_info": ([vp, vp, vp, vp, vp], i32),
+    "x100q_lin_gemv": ([vp, vp, vp, i32], i32),
+    "x100q_lin_gemv_dev": ([vp, vp, vp, i32, vp], i32),
+    "x100q_moe_create": ([i32, i32, i32, i32, i32, vp, vp, vp, vp, i32, i32], vp),
+    "x100q_moe_destroy": ([vp], None),
+    "x100q_moe_ffn": ([vp, vp, vp, i32, vp, vp], i32),
+    "x100q_moe_ffn_dev": ([vp, vp, vp, i32, vp, vp, vp], i32),
+}
+
+
+def lib():
+    """Load libx100gemm_b200.so; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} missing: run __graft_entry__.build() (make -C x100-gemm_b200)")
+        L = C.CDLL(LIB_PATH)
+        for name, (args, res) in _SIGS.items():
+            fn = getattr(L, name, None)
+            if fn is None:
+                continue
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def header_functions() -> list[str]:
+    """Names of every function declared in include/*.h."""
+    names = []
+    for h in HEADERS:
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^[A-Za-z_][\w \*]*?\b([a-z_][a-z0-9_]*)\s*\(", src, flags=re.M):
+            if m.group(1) not in ("defined",):
+                names.append(m.group(1))
+    return sorted(set(names))
+
+
+def strerror(code: int) -> str:
+    return lib().x100_strerror(code).decode()
+
+
+def last_error() -> int:
+    return lib().x100_last_error()
+
+
+def check(code: int, what: str = "x100") -> None:
+    if code != X100_OK:
+        raise X100Error(code, what)
+
+
+def check_last(what: str) -> None:
+    check(last_error(), what)
+
+
+def detect() -> Caps:
+    caps = Caps()
+    lib().x100_detect(C.byref(caps))
+    return caps
+
+
+def _p(a):
+    """Raw pointer of a numpy array or torch tensor."""
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    return a.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream if isinstance(stream, int) else stream.cuda_stream
+
+
+# ---- host-pointer (reference-signature) calls ------------------------------------
+def gemm_host(fn: str, A, B, Cm) -> None:
+    """Call a void reference-signature GEMM (gemm_ime_i8, gemm_ref_f32, ...)
+    on numpy arrays (or torch tensors); C += A @ B in place."""
+    M, K = A.shape
+    N = B.shape[1]
+    getattr(lib(), fn)(M, N, K, _p(A), _p(B), _p(Cm))
+    check_last(fn)
+
+
+# ---- device-pointer calls (torch tensors) ----------------------------------------------
+def gemm_dev(fn: str, A, B, Cm, stream=None) -> None:
+    M, K = A.shape
+    N = B.shape[1]
+    check(getattr(lib(), fn)(M, N, K, _p(A), _p(B), _p(Cm), _stream(stream)), fn)
+
+
+def sync(stream=None) -> None:
+    check(lib().x100_sync(_stream(stream)), "x100_sync")
+
+
+# ---- quantised linear / MoE -----------------------------------------------------------
+class Lin:
+    """x100q_lin handle: an N x K block-quantised linear resident in HBM."""
+
+    def __init__(self, qtype: int, N: int, K: int, blocks: np.ndarray):
+        blocks = np.ascontiguousarray(blocks, np.uint8)
+        self.qtype, self.N, self.K = qtype, N, K
+        self.h = lib().x100q_lin_create(qtype, N, K, blocks.ctypes.data)
+        if not self.h:
+            check_last("x100q_lin_create")
+
+    def gemv(self, x, y, batch: int) -> None:
+        check(lib().x100q_lin_gemv(self.h, _p(x), _p(y), batch), "x100q_lin_gemv")
+
+    def gemv_dev(self, x, y, batch: int, stream=None) -> None:
+        check(lib().x100q_lin_gemv_dev(self.h, _p(x), _p(y), batch, _stream(stream)), "x100q_lin_gemv_dev")
+
+    def device_bytes(self) -> int:
+        b = C.c_size_t()
+        check(lib().x100q_lin_info(self.h, None, None, None, C.byref(b)), "x100q_lin_info")
+        return b.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().x100q_lin_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+
+class Moe:
+    """x100q_moe handle: router + top-k + SwiGLU experts [lo, hi) in HBM."""
+
+    def __init__(self, d, n_exp, n_act, ffn, qtype, router, gate, up, down, expert_lo=0, expert_hi=None):
+        expert_hi = n_exp if expert_hi is None else expert_hi
+        self.d, self.n_exp, self.n_act, self.ffn = d, n_exp, n_act, ffn
+        router = np.ascontiguousarray(router, np.float32)
+        self.h = lib().x100q_moe_create(d, n_exp, n_act, ffn, qtype, router.ctypes.data, _p(gate), _p(up),
+                                        _p(down), expert_lo, expert_hi)
+        if not self.h:
+            check_last("x100q_moe_create")
+
+    def ffn_host(self, hn: np.ndarray):
+        hn = np.ascontiguousarray(hn, np.float32).reshape(-1, self.d)
+        B = hn.shape[0]
+        eout = np.empty_like(hn)
+        sel = np.empty((B, self.n_act), np.int32)
+        w = np.empty((B, self.n_act), np.float32)
+        check(lib().x100q_moe_ffn(self.h, hn.ctypes.data, eout.ctypes.data, B, sel.ctypes.data, w.ctypes.data),
+              "x100q_moe_ffn")
+        return eout, sel, w
+
+    def ffn_dev(self, hn, eout, batch, sel=None, w=None, stream=None):
+        check(lib().x100q_moe_ffn_dev(self.h, _p(hn), _p(eout), batch, _p(sel), _p(w), _stream(stream)),
+              "x100q_moe_ffn_dev")
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().x100q_moe_destroy(self.h)
+            self.h = None
+
+    __del__ = close
