@@ -39,8 +39,8 @@ L2_BYTES = 126 * 1024 * 1024
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="x100", choices=["x100", "reference"])
     ap.add_argument("--workload", default="gemm_i8",
                     choices=["gemm_i8", "gemm_f16", "gemm_f32", "q4gemv", "moe"])
@@ -77,6 +77,8 @@ def load_traffic(key):
 
 # ---- clocks --------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and throttle reasons sampled while the timed region runs:
+    NVML every 5 ms (reads only; no setting is changed), else nvidia-smi."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -85,8 +87,37 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.nvml = None
+        self.samples = []
+        self.stop_ev = threading.Event()
+
+    def _nvml_loop(self, nv, h):
+        names = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                 "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                 "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        while not self.stop_ev.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((mhz, {k for k, bit in names.items() if rs & bit}))
+            except Exception:  # noqa: BLE001 - sampling is best effort
+                pass
+            self.stop_ev.wait(0.005)
 
     def start(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByUUID(self.gpu) if str(self.gpu).startswith("GPU-") else \
+                nv.nvmlDeviceGetHandleByIndex(int(self.gpu))
+            self.maxmhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.nvml = nv
+            self.th = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            self.th.start()
+            return
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
@@ -101,6 +132,16 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            self.stop_ev.set()
+            self.th.join(timeout=2)
+            if not self.samples:
+                return None
+            reasons = set()
+            for _, r in self.samples:
+                reasons |= r
+            return {"sm_mhz": statistics.median([m for m, _ in self.samples]), "sm_max_mhz": self.maxmhz,
+                    "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml 5 ms"}
         if not self.proc:
             return None
         self.proc.terminate()
@@ -291,7 +332,6 @@ def bench_gemm(args, dist, peaks, peak_src):
     torch.cuda.synchronize()
     clk = ClockSampler(dist.physical_gpu())
     clk.start()
-    time.sleep(0.3)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     dist.barrier()
     torch.cuda.synchronize()

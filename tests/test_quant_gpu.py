@@ -1,0 +1,190 @@
+"""GPU parity of the block-quantised decode path against the CPU oracle.
+
+Dequant-GEMV and MoE outputs must stay within relative L2 error 1e-3 of the
+reference's scalar fp32 path (oracle: dequantise the stored blocks, fp32
+activations, fp32 k-ordered dot products); the MoE's selected experts must
+equal the oracle's.  All calls go through the C ABI (include/x100q.h).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import py_oracle as po
+import x100b
+
+pytestmark = pytest.mark.gpu
+
+REL_Q = 1e-3   # relative L2 bar for dequant-GEMV and MoE outputs (BASELINE)
+QTS = [po.Q4_0, po.Q8_0, po.Q4_K, po.Q3_K]
+
+
+def wellformed_blocks(qtype, nblocks, seed):
+    """Random payload bytes with fp16 scales in a realistic range (the way
+    bench/q3k_probe.c:418-425 builds its test blocks)."""
+    rng = np.random.default_rng(seed)
+    bb = po.BLOCK_BYTES[qtype]
+    blk = rng.integers(0, 256, size=(nblocks, bb), dtype=np.uint8)
+    f16 = lambda v: np.asarray(v, np.float16).view(np.uint8).reshape(-1, 2)  # noqa: E731
+    if qtype in (po.Q4_0, po.Q8_0):
+        blk[:, 0:2] = f16(rng.uniform(0.001, 0.01, nblocks) * rng.choice([-1, 1], nblocks))
+    elif qtype == po.Q4_K:
+        blk[:, 0:2] = f16(rng.uniform(0.0002, 0.002, nblocks))
+        blk[:, 2:4] = f16(rng.uniform(0.0, 0.001, nblocks))
+    else:
+        blk[:, 108:110] = f16(rng.uniform(0.0002, 0.002, nblocks) * rng.choice([-1, 1], nblocks))
+    return np.ascontiguousarray(blk.reshape(-1))
+
+
+def encoded(qtype, N, K, seed, std=0.02):
+    rng = np.random.default_rng(seed)
+    return po.quantize(qtype, rng.normal(0, std, size=(N, K)).astype(np.float32))
+
+
+@pytest.mark.parametrize("batch", [1, 4, 8])
+def test_q4_0_config_6144x2048(batch):
+    """BASELINE config: Q4_0 6144 x 2048, scale max|w|/7, x ~ N(0,1)."""
+    N, K = 6144, 2048
+    W = encoded(po.Q4_0, N, K, 11)
+    x = np.random.default_rng(12).normal(0, 1, size=(batch, K)).astype(np.float32)
+    ref = po.qgemv(po.Q4_0, W, N, K, x, nthreads=8)
+    lin = x100b.Lin(x100b.Q4_0, N, K, W)
+    y = np.empty((batch, N), np.float32)
+    lin.gemv(x, y, batch)
+    assert po.rel_l2(y, ref) <= REL_Q
+    assert lin.device_bytes() == N * K // 32 * 18
+
+
+@pytest.mark.parametrize("qt", QTS)
+@pytest.mark.parametrize("shape", [(37, 256), (768, 2048), (2048, 768), (512, 4096), (1, 512)])
+@pytest.mark.parametrize("batch", [1, 2, 3, 5, 16])
+def test_qgemv_wellformed_blocks(qt, shape, batch):
+    N, K = shape
+    W = wellformed_blocks(qt, N * K // po.BLOCK_ELEMS[qt], 100 + qt + N + batch)
+    x = np.random.default_rng(N + K + batch).normal(0, 1, size=(batch, K)).astype(np.float32)
+    ref = po.qgemv(qt, W, N, K, x, nthreads=8)
+    lin = x100b.Lin(qt, N, K, W)
+    y = np.empty((batch, N), np.float32)
+    lin.gemv(x, y, batch)
+    assert po.rel_l2(y, ref) <= REL_Q, (po.QNAMES[qt], shape, batch, po.rel_l2(y, ref))
+
+
+@pytest.mark.parametrize("qt", QTS)
+def test_qgemv_encoded_weights_and_device_path(qt):
+    import torch
+    N, K = 1024, 2048
+    W = encoded(qt, N, K, 7 + qt)
+    x = np.random.default_rng(8).normal(0, 1, size=(4, K)).astype(np.float32)
+    ref = po.qgemv(qt, W, N, K, x, nthreads=8)
+    lin = x100b.Lin(qt, N, K, W)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty((4, N), device="cuda")
+    lin.gemv_dev(xd, yd, 4)
+    x100b.sync()
+    assert po.rel_l2(yd.cpu().numpy(), ref) <= REL_Q
+
+
+def test_qgemv_edge_activations():
+    """Zero rows, a single huge outlier and tiny values in x."""
+    qt, N, K = po.Q4_K, 256, 1024
+    W = wellformed_blocks(qt, N * K // 256, 5)
+    x = np.zeros((4, K), np.float32)
+    x[1, 7] = 1e4
+    x[2] = np.random.default_rng(1).normal(0, 1e-6, K)
+    x[3] = np.random.default_rng(2).normal(0, 1, K)
+    x[3, 100] = -3e3
+    ref = po.qgemv(qt, W, N, K, x)
+    lin = x100b.Lin(qt, N, K, W)
+    y = np.empty((4, N), np.float32)
+    lin.gemv(x, y, 4)
+    assert np.all(y[0] == 0.0)
+    for b in range(1, 4):
+        assert po.rel_l2(y[b], ref[b]) <= REL_Q
+
+
+def test_lin_rejects_bad_shapes():
+    W = np.zeros(1000, np.uint8)
+    L = x100b.lib()
+    assert not L.x100q_lin_create(x100b.Q4_K, 8, 300, W.ctypes.data)        # K % 256
+    assert x100b.last_error() == x100b.X100_E_ARG
+    assert not L.x100q_lin_create(99, 8, 256, W.ctypes.data)
+    assert x100b.last_error() == x100b.X100_E_UNSUPPORTED
+    lin = x100b.Lin(x100b.Q4_0, 8, 64, np.zeros(8 * 2 * 18, np.uint8))
+    y = np.empty(8, np.float32)
+    assert L.x100q_lin_gemv(lin.h, y.ctypes.data, y.ctypes.data, 17) == x100b.X100_E_ARG
+
+
+# ---- MoE -------------------------------------------------------------------------
+def moe_weights(qt, d, E, ffn, seed):
+    rng = np.random.default_rng(seed)
+    router = rng.normal(0, 0.02, size=(E, d)).astype(np.float32)
+    nb_d, nb_f = d // po.BLOCK_ELEMS[qt], ffn // po.BLOCK_ELEMS[qt]
+    gate = wellformed_blocks(qt, E * ffn * nb_d, seed + 1)
+    up = wellformed_blocks(qt, E * ffn * nb_d, seed + 2)
+    down = wellformed_blocks(qt, E * d * nb_f, seed + 3)
+    return router, gate, up, down
+
+
+@pytest.fixture(scope="module")
+def c4_layer():
+    """BASELINE config 4 shape: d 2048, 128 experts, top-8, ffn 768, Q4_K."""
+    d, E, k, ffn = 2048, 128, 8, 768
+    return (d, E, k, ffn) + moe_weights(po.Q4_K, d, E, ffn, 42)
+
+
+@pytest.mark.parametrize("batch", [1, 4, 16])
+def test_moe_c4_matches_oracle(c4_layer, batch):
+    d, E, k, ffn, router, gate, up, down = c4_layer
+    hn = np.random.default_rng(batch).normal(0, 1, size=(batch, d)).astype(np.float32)
+    ref, rsel, rw = po.moe_ffn(d, E, k, ffn, po.Q4_K, router, gate, up, down, hn, nthreads=8)
+    moe = x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down)
+    eout, sel, w = moe.ffn_host(hn)
+    np.testing.assert_array_equal(sel, rsel)
+    np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-7)
+    for b in range(batch):
+        assert po.rel_l2(eout[b], ref[b]) <= REL_Q
+
+
+@pytest.mark.parametrize("qt", [po.Q3_K, po.Q4_0, po.Q8_0])
+def test_moe_other_formats(qt):
+    d, E, k, ffn = 1024, 32, 4, 512
+    router, gate, up, down = moe_weights(qt, d, E, ffn, 7 + qt)
+    hn = np.random.default_rng(3).normal(0, 1, size=(3, d)).astype(np.float32)
+    ref, rsel, _ = po.moe_ffn(d, E, k, ffn, qt, router, gate, up, down, hn, nthreads=8)
+    moe = x100b.Moe(d, E, k, ffn, qt, router, gate, up, down)
+    eout, sel, _ = moe.ffn_host(hn)
+    np.testing.assert_array_equal(sel, rsel)
+    assert po.rel_l2(eout, ref) <= REL_Q
+
+
+def test_moe_expert_parallel_partials_sum(c4_layer):
+    """Expert-parallel slices (16 experts each, as on 8 GPUs) give partial
+    outputs whose sum is the full layer output."""
+    d, E, k, ffn, router, gate, up, down = c4_layer
+    hn = np.random.default_rng(99).normal(0, 1, size=(2, d)).astype(np.float32)
+    full = x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down).ffn_host(hn)[0]
+    parts = []
+    for lo in range(0, E, 16):
+        m = x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down, lo, lo + 16)
+        parts.append(m.ffn_host(hn)[0])
+        m.close()
+    assert po.rel_l2(sum(parts), full) <= 1e-5
+    ref = po.moe_ffn(d, E, k, ffn, po.Q4_K, router, gate, up, down, hn, nthreads=8)[0]
+    assert po.rel_l2(sum(parts), ref) <= REL_Q
+
+
+def test_moe_device_path_and_repeat(c4_layer):
+    import torch
+    d, E, k, ffn, router, gate, up, down = c4_layer
+    moe = x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down)
+    hn = np.random.default_rng(5).normal(0, 1, size=(2, d)).astype(np.float32)
+    hd = torch.from_numpy(hn).cuda()
+    out = torch.empty_like(hd)
+    sel = torch.empty((2, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((2, k), device="cuda")
+    for _ in range(3):                   # scratch and ticket are reused across calls
+        moe.ffn_dev(hd, out, 2, sel, w)
+    x100b.sync()
+    ref, rsel, _ = po.moe_ffn(d, E, k, ffn, po.Q4_K, router, gate, up, down, hn, nthreads=8)
+    assert np.array_equal(sel.cpu().numpy(), rsel)
+    assert po.rel_l2(out.cpu().numpy(), ref) <= REL_Q

@@ -1,0 +1,430 @@
+// moe.cu -- the top-k SwiGLU mixture-of-experts FFN of the decode step and the
+// x100q_moe_* entry points of include/x100q.h.
+//
+// Replaces the MoE block of the reference's forward() (qwen_moe.c:295-311;
+// qwen_moe_q3k.c:1916-1978 with router mode 0 = fp32 and SwiGLU mode 0 =
+// exact): router GEMV -> softmax -> greedy top-k -> renormalise -> for each
+// selected expert gate/up GEMV, silu(g)*u, down GEMV, weighted sum.
+//
+// Three kernels per call (captured into one CUDA graph by callers that loop):
+//   router_topk   one warp per expert row: fp32 logits for every token; the
+//                 last CTA to finish (atomic ticket, no waiting) does the
+//                 softmax, the greedy top-k (strict >, lowest index wins)
+//                 and the renormalisation, writing sel / w.
+//   gate_up       grid (ffn rows, token x slot): each warp streams gate row i
+//                 and up row i of the selected expert once and writes
+//                 h[token][slot][i] = silu(g) * u (SwiGLU fused).
+//   down_combine  grid (d rows, token): each warp streams row n of the down
+//                 matrix of every selected expert and writes
+//                 eout[token][n] = sum_a w_a * (down_a[n] . h_a), summed in
+//                 slot order a = 0..k-1 like the reference (no atomics).
+// Experts outside [expert_lo, expert_hi) contribute nothing (expert
+// parallelism: the caller sums eout over processes, e.g. NCCL all-reduce).
+#include <cuda_fp16.h>
+
+#include <cstring>
+
+#include "../../include/x100q.h"
+#include "moe.h"
+#include "qgemv.h"
+
+namespace x100 {
+namespace q {
+
+constexpr int kMaxBatch = 16;
+constexpr int kMaxAct = 16;
+constexpr int kMaxExp = 256;
+
+// ---- router + softmax + top-k ------------------------------------------------------
+__global__ void __launch_bounds__(256) router_topk_kernel(const float *__restrict__ router,
+                                                          const float *__restrict__ hn, int d, int n_exp, int n_act,
+                                                          int batch, float *__restrict__ logits, int *__restrict__ sel,
+                                                          float *__restrict__ wsel, unsigned *__restrict__ ticket) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int e = blockIdx.x * nwarps + warp;
+    if (e < n_exp) {
+        const float4 *rw = reinterpret_cast<const float4 *>(router + (long)e * d);
+        for (int b = 0; b < batch; ++b) {
+            const float4 *x = reinterpret_cast<const float4 *>(hn + (long)b * d);
+            float s = 0.f;
+            for (int i = lane; i < d / 4; i += 32) {
+                const float4 r = __ldg(rw + i), v = __ldg(x + i);
+                s = fmaf(r.x, v.x, s);
+                s = fmaf(r.y, v.y, s);
+                s = fmaf(r.z, v.z, s);
+                s = fmaf(r.w, v.w, s);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+            if (lane == 0) logits[b * n_exp + e] = s;
+        }
+    }
+    // last CTA to arrive finishes the routing (threadFenceReduction pattern)
+    __shared__ unsigned s_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int b = warp; b < batch; b += nwarps) {
+        const volatile float *lg = logits + b * n_exp;
+        float p[kMaxExp / 32];
+        float m = -1e30f;
+#pragma unroll
+        for (int i = 0; i < kMaxExp / 32; ++i) {
+            const int ee = lane + 32 * i;
+            p[i] = ee < n_exp ? lg[ee] : -1e30f;
+            m = fmaxf(m, p[i]);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxExp / 32; ++i) {
+            const int ee = lane + 32 * i;
+            p[i] = ee < n_exp ? expf(p[i] - m) : 0.f;
+            s += p[i];
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        const float inv = 1.0f / s;
+#pragma unroll
+        for (int i = 0; i < kMaxExp / 32; ++i) p[i] *= inv;
+        unsigned used = 0;   // bit i: this lane's entry i is taken
+        float sw[kMaxAct];
+        int si[kMaxAct];
+        for (int a = 0; a < n_act; ++a) {
+            float bv = -1e30f;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int i = 0; i < kMaxExp / 32; ++i) {
+                const int ee = lane + 32 * i;
+                if (ee < n_exp && !(used & (1u << i)) && p[i] > bv) {
+                    bv = p[i];
+                    bi = ee;
+                }
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if ((bi & 31) == lane) used |= 1u << (bi >> 5);
+            sw[a] = bv;
+            si[a] = bi;
+        }
+        if (lane == 0) {
+            float ssum = 0.f;
+            for (int a = 0; a < n_act; ++a) ssum += sw[a];
+            for (int a = 0; a < n_act; ++a) {
+                sel[b * n_act + a] = si[a];
+                wsel[b * n_act + a] = sw[a] / ssum;
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *ticket = 0;   // ready for the next call
+}
+
+// ---- gate / up + SwiGLU ------------------------------------------------------------------
+template <int QT>
+__global__ void __launch_bounds__(256) gate_up_kernel(QView G, QView U, int ffn, int d, int n_act, int lo, int hi,
+                                                      const float *__restrict__ hn, const int *__restrict__ sel,
+                                                      float *__restrict__ h) {
+    __shared__ XBlk xq[kMaxDXB];
+    __shared__ XF xf[kMaxDXB];
+    const int pair = blockIdx.y;                 // token * n_act + slot
+    const int tok = pair / n_act;
+    const int e = sel[pair];
+    if (e < lo || e >= hi) return;               // expert held by another process
+    xprep_all(hn + (long)tok * d, d, 1, xq, xf);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int i = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (i >= ffn) return;
+    const int row = (e - lo) * ffn + i;
+    const int units = units_per_row(QT, d);
+    float g = 0.f, u = 0.f;
+    for (int k = lane; k < units; k += 32) {
+        const WUnit<QT> wg = load_unit<QT>(G, row, k);
+        const WUnit<QT> wu = load_unit<QT>(U, row, k);
+        g += dot_unit<QT>(wg, xq, xf, k);
+        u += dot_unit<QT>(wu, xq, xf, k);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        g += __shfl_xor_sync(0xffffffffu, g, off);
+        u += __shfl_xor_sync(0xffffffffu, u, off);
+    }
+    if (lane == 0) h[(long)pair * ffn + i] = (g / (1.0f + expf(-g))) * u;   // silu(g) * u, qwen_moe.c:309
+}
+
+// ---- down projection + weighted combine -------------------------------------------------------
+template <int QT>
+__global__ void __launch_bounds__(256) down_combine_kernel(QView D, int ffn, int d, int n_act, int lo, int hi,
+                                                           const float *__restrict__ h, const int *__restrict__ sel,
+                                                           const float *__restrict__ wsel, float *__restrict__ eout,
+                                                           int lpr) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int nxb = ffn / 32;
+    XBlk *xq = reinterpret_cast<XBlk *>(smem);
+    XF *xf = reinterpret_cast<XF *>(smem + sizeof(XBlk) * n_act * nxb);
+    const int tok = blockIdx.y;
+    // activation planes of every slot's h (slots of remote experts are unused)
+    xprep_all(h + (long)tok * n_act * ffn, ffn, n_act, xq, xf);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (n >= d) return;
+    const int groups = 32 / lpr, grp = lane / lpr, sig = lane % lpr;
+    const int units = units_per_row(QT, ffn);
+    float total = 0.f;
+    for (int a0 = 0; a0 < n_act; a0 += groups) {
+        const int a = a0 + grp;
+        float acc = 0.f;
+        int e = -1;
+        if (a < n_act) {
+            e = sel[tok * n_act + a];
+            if (e >= lo && e < hi) {
+                const int row = (e - lo) * d + n;
+                for (int k = sig; k < units; k += lpr) {
+                    const WUnit<QT> wd = load_unit<QT>(D, row, k);
+                    acc += dot_unit<QT>(wd, xq + a * nxb, xf + a * nxb, k);
+                }
+            }
+        }
+        for (int off = lpr >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        // lane 0 folds the groups' results in slot order
+        for (int gi = 0; gi < groups; ++gi) {
+            const float v = __shfl_sync(0xffffffffu, acc, gi * lpr);
+            const int ag = a0 + gi;
+            if (lane == 0 && ag < n_act) {
+                const int eg = sel[tok * n_act + ag];
+                if (eg >= lo && eg < hi) total += wsel[tok * n_act + ag] * v;
+            }
+        }
+    }
+    if (lane == 0) eout[(long)tok * d + n] = total;
+}
+
+}  // namespace q
+
+using namespace q;
+
+bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype) {
+    const int be = (int)qtype_block_elems(qtype);
+    return be && d > 0 && ffn > 0 && d % be == 0 && ffn % be == 0 && d % 32 == 0 && ffn % 32 == 0 &&
+           d / 32 <= kMaxDXB && n_exp > 0 && n_exp <= kMaxExp && n_act > 0 && n_act <= kMaxAct &&
+           n_act <= n_exp && (size_t)n_act * (ffn / 32) * (sizeof(XBlk) + sizeof(XF)) <= 200 * 1024;
+}
+
+template <int QT>
+static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
+                         cudaStream_t s) {
+    const QView G = qmat_view(L.gate, 0), U = qmat_view(L.up, 0), D = qmat_view(L.down, 0);
+    router_topk_kernel<<<(L.n_exp + 7) / 8, 256, 0, s>>>(L.router, hn, L.d, L.n_exp, L.n_act, batch, S.logits, S.sel,
+                                                        S.w, S.ticket);
+    dim3 g1((L.ffn + 7) / 8, batch * L.n_act);
+    gate_up_kernel<QT><<<g1, 256, 0, s>>>(G, U, L.ffn, L.d, L.n_act, L.lo, L.hi, hn, S.sel, S.h);
+    const int lpr = lanes_per_row(units_per_row(QT, L.ffn));
+    const size_t smem = (size_t)L.n_act * (L.ffn / 32) * (sizeof(XBlk) + sizeof(XF));
+    static bool attr[64];
+    if (smem > 48 * 1024 && !attr[c->device]) {
+        cudaFuncSetAttribute(down_combine_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr[c->device] = true;
+    }
+    dim3 g2((L.d + 7) / 8, batch);
+    down_combine_kernel<QT><<<g2, 256, smem, s>>>(D, L.ffn, L.d, L.n_act, L.lo, L.hi, S.h, S.sel, S.w, eout, lpr);
+    return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+}
+
+int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
+               cudaStream_t s) {
+    if (batch < 1 || batch > kMaxBatch) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    if (fault_injected("launch")) return X100_E_INJECTED;
+    switch (L.qtype) {
+    case Q4_0: return launch_moe_qt<Q4_0>(c, L, S, hn, eout, batch, s);
+    case Q8_0: return launch_moe_qt<Q8_0>(c, L, S, hn, eout, batch, s);
+    case Q4_K: return launch_moe_qt<Q4_K>(c, L, S, hn, eout, batch, s);
+    case Q3_K: return launch_moe_qt<Q3_K>(c, L, S, hn, eout, batch, s);
+    default: set_error(X100_E_UNSUPPORTED); return X100_E_UNSUPPORTED;
+    }
+}
+
+size_t moe_scratch_bytes(int n_exp, int n_act, int ffn) {
+    size_t b = 0;
+    b += (size_t)kMaxBatch * n_exp * 4;           // logits
+    b += (size_t)kMaxBatch * n_act * 4 * 2;       // sel, w
+    b += (size_t)kMaxBatch * n_act * ffn * 4;     // h
+    b += 256 * 5;                                 // alignment + ticket
+    return b;
+}
+
+// Carve the scratch regions out of one buffer of moe_scratch_bytes().
+MoeScratch moe_scratch_carve(void *base, int n_exp, int n_act, int ffn) {
+    MoeScratch S;
+    uintptr_t p = (reinterpret_cast<uintptr_t>(base) + 255) & ~uintptr_t(255);
+    auto take = [&](size_t bytes) {
+        void *r = reinterpret_cast<void *>(p);
+        p = (p + bytes + 255) & ~uintptr_t(255);
+        return r;
+    };
+    S.ticket = static_cast<unsigned *>(take(256));
+    S.logits = static_cast<float *>(take((size_t)kMaxBatch * n_exp * 4));
+    S.sel = static_cast<int *>(take((size_t)kMaxBatch * n_act * 4));
+    S.w = static_cast<float *>(take((size_t)kMaxBatch * n_act * 4));
+    S.h = static_cast<float *>(take((size_t)kMaxBatch * n_act * ffn * 4));
+    return S;
+}
+
+}  // namespace x100
+
+using namespace x100;
+
+struct x100q_moe {
+    int device;
+    MoeLayer L;
+    void *scratch = nullptr;
+    MoeScratch S;
+};
+
+extern "C" {
+
+x100q_moe *x100q_moe_create(int d, int n_exp, int n_act, int ffn, int qtype, const float *router,
+                            const void *gate_exps, const void *up_exps, const void *down_exps, int expert_lo,
+                            int expert_hi) {
+    set_error(X100_OK);
+    if (!moe_shapes_ok(d, n_exp, n_act, ffn, qtype) || !router || !gate_exps || !up_exps || !down_exps ||
+        expert_lo < 0 || expert_hi > n_exp || expert_lo >= expert_hi) {
+        set_error(X100_E_ARG);
+        return nullptr;
+    }
+    DevCtx *c = ctx();
+    if (!c) return nullptr;
+    std::lock_guard<std::mutex> lk(c->mu);
+    x100q_moe *m = new x100q_moe();
+    m->device = c->device;
+    MoeLayer &L = m->L;
+    L.d = d;
+    L.n_exp = n_exp;
+    L.n_act = n_act;
+    L.ffn = ffn;
+    L.qtype = qtype;
+    L.lo = expert_lo;
+    L.hi = expert_hi;
+    const int ne = expert_hi - expert_lo;
+    const size_t rb_d = x100q_row_bytes(qtype, d), rb_f = x100q_row_bytes(qtype, ffn);
+    const uint8_t *g = static_cast<const uint8_t *>(gate_exps) + (size_t)expert_lo * ffn * rb_d;
+    const uint8_t *u = static_cast<const uint8_t *>(up_exps) + (size_t)expert_lo * ffn * rb_d;
+    const uint8_t *dn = static_cast<const uint8_t *>(down_exps) + (size_t)expert_lo * d * rb_f;
+    bool ok = cudaMalloc(&L.router, (size_t)n_exp * d * 4) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        set_error(X100_E_ALLOC);
+    }
+    ok = ok && check_cuda(cudaMemcpy(L.router, router, (size_t)n_exp * d * 4, cudaMemcpyHostToDevice), X100_E_COPY) == 0;
+    ok = ok && qmat_upload(c, qtype, ne * ffn, d, g, L.gate, c->stream);
+    ok = ok && qmat_upload(c, qtype, ne * ffn, d, u, L.up, c->stream);
+    ok = ok && qmat_upload(c, qtype, ne * d, ffn, dn, L.down, c->stream);
+    if (ok) {
+        const size_t sb = moe_scratch_bytes(n_exp, n_act, ffn);
+        if (fault_injected("alloc") || cudaMalloc(&m->scratch, sb) != cudaSuccess) {
+            cudaGetLastError();
+            set_error(X100_E_ALLOC);
+            ok = false;
+        } else {
+            cudaMemset(m->scratch, 0, sb);
+            m->S = moe_scratch_carve(m->scratch, n_exp, n_act, ffn);
+        }
+    }
+    if (!ok) {
+        cudaFree(L.router);
+        cudaFree(L.gate.w);
+        cudaFree(L.up.w);
+        cudaFree(L.down.w);
+        cudaFree(m->scratch);
+        delete m;
+        return nullptr;
+    }
+    return m;
+}
+
+void x100q_moe_destroy(x100q_moe *m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    cudaFree(m->L.router);
+    cudaFree(m->L.gate.w);
+    cudaFree(m->L.up.w);
+    cudaFree(m->L.down.w);
+    cudaFree(m->scratch);
+    delete m;
+}
+
+int x100q_moe_ffn_dev(const x100q_moe *m, const float *hn, float *eout, int batch, int *sel_out, float *w_out,
+                      void *stream) {
+    set_error(X100_OK);
+    if (!m || !hn || !eout || (reinterpret_cast<uintptr_t>(hn) & 15) != 0) {   // 16-byte loads of hn
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    DevCtx *c = ctx();
+    if (!c) return get_error();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int st = launch_moe(c, m->L, m->S, hn, eout, batch, s);
+    const size_t rb = (size_t)batch * m->L.n_act * 4;
+    if (st == X100_OK && sel_out)
+        st = check_cuda(cudaMemcpyAsync(sel_out, m->S.sel, rb, cudaMemcpyDeviceToDevice, s), X100_E_COPY);
+    if (st == X100_OK && w_out)
+        st = check_cuda(cudaMemcpyAsync(w_out, m->S.w, rb, cudaMemcpyDeviceToDevice, s), X100_E_COPY);
+    if (st) set_error(st);
+    return st;
+}
+
+int x100q_moe_ffn(const x100q_moe *m, const float *hn, float *eout, int batch, int *sel_out, float *w_out) {
+    set_error(X100_OK);
+    if (!m || !hn || !eout || batch < 1 || batch > kMaxBatch) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    DevCtx *c = ctx();
+    if (!c) return get_error();
+    std::lock_guard<std::mutex> lk(c->mu);
+    const size_t xb = (size_t)batch * m->L.d * 4;
+    const float *hd = hn;
+    float *ed = eout;
+    const bool hdev = is_device_ptr(hn), edev = is_device_ptr(eout);
+    if (!hdev) {
+        void *b = stage_buf(c, 0, xb);
+        if (!b) return get_error();
+        if (fault_injected("copy") || check_cuda(cudaMemcpyAsync(b, hn, xb, cudaMemcpyHostToDevice, c->stream), X100_E_COPY))
+            return get_error();
+        hd = static_cast<const float *>(b);
+    }
+    if (!edev) {
+        void *b = stage_buf(c, 1, xb);
+        if (!b) return get_error();
+        ed = static_cast<float *>(b);
+    }
+    int st = launch_moe(c, m->L, m->S, hd, ed, batch, c->stream);
+    const size_t rb = (size_t)batch * m->L.n_act * 4;
+    if (st == X100_OK && !edev)
+        st = check_cuda(cudaMemcpyAsync(eout, ed, xb, cudaMemcpyDeviceToHost, c->stream), X100_E_COPY);
+    if (st == X100_OK && sel_out)
+        st = check_cuda(cudaMemcpyAsync(sel_out, m->S.sel, rb, cudaMemcpyDefault, c->stream), X100_E_COPY);
+    if (st == X100_OK && w_out)
+        st = check_cuda(cudaMemcpyAsync(w_out, m->S.w, rb, cudaMemcpyDefault, c->stream), X100_E_COPY);
+    const int st2 = sync_and_status(c, c->stream);
+    if (st == X100_OK) st = st2;
+    if (st) set_error(st);
+    return st;
+}
+
+}  // extern "C"

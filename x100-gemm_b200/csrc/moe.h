@@ -1,0 +1,38 @@
+// moe.h -- resident mixture-of-experts layer and its launcher (moe.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "qgemv.h"
+
+namespace x100 {
+
+namespace q {
+constexpr int kMaxDXB = 256;   // hidden size up to 8192 (256 activation blocks)
+}
+
+// Weights of one MoE layer resident in HBM: fp32 router [n_exp][d] and the
+// local experts [lo, hi): gate/up rows (hi-lo)*ffn x d, down (hi-lo)*d x ffn.
+struct MoeLayer {
+    int d = 0, n_exp = 0, n_act = 0, ffn = 0, qtype = 0, lo = 0, hi = 0;
+    float *router = nullptr;
+    QMat gate, up, down;
+};
+
+// Device scratch of one call (batch <= 16): routing logits, selection,
+// weights, SwiGLU intermediates h[token][slot][ffn] and the ticket counter.
+struct MoeScratch {
+    unsigned *ticket = nullptr;
+    float *logits = nullptr;
+    int *sel = nullptr;
+    float *w = nullptr;
+    float *h = nullptr;
+};
+
+bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype);
+size_t moe_scratch_bytes(int n_exp, int n_act, int ffn);
+MoeScratch moe_scratch_carve(void *base, int n_exp, int n_act, int ffn);
+// eout[b][:] for b < batch; hn, eout device pointers; asynchronous on s.
+int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
+               cudaStream_t s);
+
+}  // namespace x100

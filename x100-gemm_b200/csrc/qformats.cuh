@@ -35,7 +35,9 @@ using XF = float4;
 
 constexpr int kXScale = 32639;   // |256 h + l| <= 32639 keeps h in [-127, 127]
 
-__host__ __device__ constexpr int units_per_row(int qt, int K) { return K / 32; }
+// Units per row: 32 weights per unit, except Q3_K whose unit covers 64
+// weights (one 16-byte qs slice and one 16-byte hmask slice, see load_unit).
+__host__ __device__ constexpr int units_per_row(int qt, int K) { return qt == Q3_K ? K / 64 : K / 32; }
 __host__ __device__ constexpr long row_bytes_dev(int qt, int K) {
     return qt == Q4_0 ? (long)(K / 32) * 16
          : qt == Q8_0 ? (long)(K / 32) * 32
@@ -46,6 +48,7 @@ __host__ __device__ constexpr long row_bytes_dev(int qt, int K) {
 
 // Device view of a resident quantised matrix.
 struct QView {
+    int qt;              // Q4_0 / Q8_0 / Q4_K / Q3_K
     const uint8_t *w;    // weight plane / superblocks
     const __half *d;     // Q4_0 / Q8_0 block scales (nullptr for K-quants)
     long wstride;        // bytes per row in w
@@ -228,10 +231,12 @@ template <> __device__ __forceinline__ float dot_unit<Q3_K>(const WUnit<Q3_K> &w
 }
 
 // ---- activation preparation -----------------------------------------------------
-// Eight consecutive threads (t = threadIdx % 8) convert one 32-element block
-// x[0..31] into (xq, xf).  All 8 lanes of the group must call it together.
-__device__ __forceinline__ void xprep_block(const float *x, XBlk *xq, XF *xf, int t) {
-    const float4 v = *reinterpret_cast<const float4 *>(x + 4 * t);
+// Eight consecutive threads (t = lane % 8) convert one 32-element block
+// x[0..31] into (xq, xf).  Every lane of the warp must call it together (it
+// shuffles across the whole warp); lanes whose group has no block pass
+// active = false and write nothing.
+__device__ __forceinline__ void xprep_block(const float *x, XBlk *xq, XF *xf, int t, bool active) {
+    const float4 v = active ? *reinterpret_cast<const float4 *>(x + 4 * t) : make_float4(0.f, 0.f, 0.f, 0.f);
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     float s16 = (v.x + v.y) + (v.z + v.w);
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
@@ -254,12 +259,31 @@ __device__ __forceinline__ void xprep_block(const float *x, XBlk *xq, XF *xf, in
         hw |= (uint32_t)(h & 0xFF) << (8 * k);
         lw |= (uint32_t)(l & 0xFF) << (8 * k);
     }
+    if (!active) return;
     uint32_t *hwords = reinterpret_cast<uint32_t *>(&xq->h0);
     uint32_t *lwords = reinterpret_cast<uint32_t *>(&xq->l0);
     hwords[t] = hw;
     lwords[t] = lw;
-    if (t == 0) *xf = make_float4(s, s32, t < 4 ? s16 : other16, t < 4 ? other16 : s16);
+    if (t == 0) *xf = make_float4(s, s32, s16, other16);
 }
 
+}  // namespace q
+}  // namespace x100
+
+namespace x100 {
+namespace q {
+// The whole CTA prepares `batch` activation rows x[c*K .. c*K+K) into
+// xq/xf[c*(K/32) + j]; warp-uniform trip counts keep the shuffles legal.
+__device__ __forceinline__ void xprep_all(const float *x, int K, int batch, XBlk *xq, XF *xf) {
+    const int nxb = K / 32;
+    const int total = batch * nxb;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (int b0 = warp * 4; b0 < total; b0 += nwarps * 4) {
+        const int blk = b0 + (lane >> 3);
+        const bool active = blk < total;
+        const int c = active ? blk / nxb : 0, j = active ? blk - c * nxb : 0;
+        xprep_block(x + (long)c * K + j * 32, &xq[c * nxb + j], &xf[c * nxb + j], lane & 7, active);
+    }
+}
 }  // namespace q
 }  // namespace x100
