@@ -99,6 +99,29 @@ int x100q_moe_ffn(const x100q_moe *moe, const float *hn, float *eout, int batch,
 int x100q_moe_ffn_dev(const x100q_moe *moe, const float *hn, float *eout, int batch,
                       int *sel_out, float *w_out, void *stream);
 
+/* No counterpart in the reference.  Router -> softmax -> top-k ->
+ * renormalise for `batch` tokens, the routing step of x100q_moe_ffn, for
+ * callers that may not allocate GPU memory: code whose device memory is owned
+ * by a framework pool or a fixed, pre-committed budget, and hot loops that
+ * cannot afford cudaMalloc/cudaFree (which may synchronise the device).  The
+ * library allocates nothing here, not even its per-device context: the
+ * routing logits and the completion ticket live in a fixed static device
+ * array of 256 + 8192 bytes that every GPU which loads the library holds
+ * until exit.  Limit: batch * n_exp <= 2048 (e.g. 16 tokens x 128 experts),
+ * larger requests return X100_E_TOO_LARGE; also 1 <= batch <= 16,
+ * 1 <= n_exp <= 256, 1 <= n_act <= min(16, n_exp), d % 4 == 0.
+ * router [n_exp][d] and hn [batch][d] (fp32, 16-byte aligned), sel_out
+ * [batch][n_act] and w_out [batch][n_act] are device pointers on the calling
+ * thread's current CUDA device; the work is enqueued on `stream` and the call
+ * returns without synchronising.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  All calls share the one array: calls whose work
+ * overlaps on the GPU (other streams, other threads) race and must be
+ * serialised by the caller.                                                 */
+int x100q_router_topk_noalloc(const float *router, const float *hn, int d, int n_exp,
+                              int n_act, int batch, int *sel_out, float *w_out,
+                              void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -428,3 +428,55 @@ int x100q_moe_ffn(const x100q_moe *m, const float *hn, float *eout, int batch, i
 }
 
 }  // extern "C"
+
+// ---- routing without allocation ----------------------------------------------------------
+// Scratch of x100q_router_topk_noalloc: the completion ticket (first 256
+// bytes) and up to kNoAllocLogits routing logits.  One copy per device,
+// created when the library's module loads, shared by every call.
+namespace {
+constexpr int kNoAllocLogits = 2048;
+static __device__ __align__(256) unsigned char g_router_scratch[256 + kNoAllocLogits * 4];
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[64];   // device address of g_router_scratch, per device
+}  // namespace
+
+extern "C" int x100q_router_topk_noalloc(const float *router, const float *hn, int d, int n_exp, int n_act,
+                                         int batch, int *sel_out, float *w_out, void *stream) {
+    set_error(X100_OK);
+    if (!router || !hn || !sel_out || !w_out || d <= 0 || d % 4 || n_exp < 1 || n_exp > kMaxExp || n_act < 1 ||
+        n_act > kMaxAct || n_act > n_exp || batch < 1 || batch > kMaxBatch ||
+        (reinterpret_cast<uintptr_t>(router) & 15) || (reinterpret_cast<uintptr_t>(hn) & 15)) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    if (batch * n_exp > kNoAllocLogits) {
+        set_error(X100_E_TOO_LARGE);
+        return X100_E_TOO_LARGE;
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        set_error(X100_E_NODEV);
+        return X100_E_NODEV;
+    }
+    void *base;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_addr[dev]) {   // once per device, with that device current
+            void *p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
+            if (e != cudaSuccess || !p) return check_cuda(e != cudaSuccess ? e : cudaErrorUnknown, X100_E_LAUNCH);
+            g_noalloc_addr[dev] = p;
+        }
+        base = g_noalloc_addr[dev];
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned *ticket = static_cast<unsigned *>(base);
+    float *logits = reinterpret_cast<float *>(static_cast<unsigned char *>(base) + 256);
+    // the ticket must start at zero; the logits are fully written before use
+    if (check_cuda(cudaMemsetAsync(ticket, 0, sizeof(unsigned), s), X100_E_LAUNCH)) return get_error();
+    q::router_topk_kernel<<<(n_exp + 7) / 8, 256, 0, s>>>(router, hn, d, n_exp, n_act, batch, logits, sel_out,
+                                                          w_out, ticket);
+    return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+}
+

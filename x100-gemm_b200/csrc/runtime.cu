@@ -183,6 +183,8 @@ const char *x100_strerror(int code) {
     case X100_E_COMM: return "collective / peer exchange failed";
     case X100_E_INJECTED: return "failure injected by X100_FAULT";
     case X100_E_UNSUPPORTED: return "unsupported shape, type or layout";
+    case X100_E_TOO_LARGE:
+        return "request larger than the fixed scratch of a no-allocation entry point";
     default: return "unknown error";
     }
 }

@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libx100gemm_b200.so")
 HEADERS = [os.path.join(REPO, "include", "x100_gemm.h"), os.path.join(REPO, "include", "x100q.h")]
 
 X100_OK, X100_E_ARG, X100_E_NODEV, X100_E_ARCH, X100_E_ALLOC, X100_E_COPY, X100_E_LAUNCH, \
-    X100_E_TIMEOUT, X100_E_COMM, X100_E_INJECTED, X100_E_UNSUPPORTED = range(11)
+    X100_E_TIMEOUT, X100_E_COMM, X100_E_INJECTED, X100_E_UNSUPPORTED, X100_E_TOO_LARGE = range(12)
 
 Q_F32, Q4_0, Q8_0, Q3_K, Q4_K = 0, 2, 8, 11, 12
 
@@ -76,6 +76,7 @@ _SIGS = {
     "x100q_moe_destroy": ([vp], None),
     "x100q_moe_ffn": ([vp, vp, vp, i32, vp, vp], i32),
     "x100q_moe_ffn_dev": ([vp, vp, vp, i32, vp, vp, vp], i32),
+    "x100q_router_topk_noalloc": ([vp, vp, i32, i32, i32, i32, vp, vp, vp], i32),
 }
 
 
