@@ -423,6 +423,285 @@ def bench_gemm(args, dist, peaks, peak_src):
     return line
 
 
+
+# ---- quantised decode workloads ------------------------------------------------------------
+def wellformed_blocks_dev(qtype, nblocks, gen):
+    """Random well-formed GGUF blocks built on the device: random payload
+    bytes, fp16 scales in the range N(0, 0.02) weights give (host copy)."""
+    import numpy as np
+    import torch
+    bb = {2: 18, 8: 34, 11: 110, 12: 144}[qtype]
+    blk = torch.randint(0, 256, (nblocks, bb), dtype=torch.uint8, device="cuda", generator=gen)
+    def f16(lo, hi, sign):
+        v = torch.rand(nblocks, device="cuda", generator=gen) * (hi - lo) + lo
+        if sign:
+            v = v * (torch.randint(0, 2, (nblocks,), device="cuda", generator=gen) * 2 - 1)
+        return v.half().view(torch.uint8).view(nblocks, 2)
+    if qtype in (2, 8):
+        blk[:, 0:2] = f16(0.004, 0.012, True)
+    elif qtype == 12:
+        blk[:, 0:2] = f16(0.0002, 0.002, False)
+        blk[:, 2:4] = f16(0.0, 0.001, False)
+    else:
+        blk[:, 108:110] = f16(0.0002, 0.002, True)
+    return np.ascontiguousarray(blk.cpu().numpy().reshape(-1))
+
+
+def timed_graph(fn, steps, warmup, dist, stream):
+    """Warm up, capture one call of fn() in a CUDA graph, replay it `steps`
+    times between CUDA events; returns (total_ms, clocks)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = ClockSampler(dist.physical_gpu())
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = clk.stop()
+    ms = dist.max(e0.elapsed_time(e1))
+    del g
+    return ms, clocks
+
+
+def bench_q4gemv(args, dist, peaks, peak_src):
+    """Q4_0 6144 x 2048 GEMV at batch B.  64 distinct
+    weight copies (453 MB, > L2) are rotated inside one CUDA graph; a step is
+    one graph replay = 64 GEMV calls."""
+    import numpy as np
+    import torch
+    import x100b
+    N, K, B, COPIES = 6144, 2048, args.batch, 64
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    lins = [x100b.Lin(x100b.Q4_0, N, K, wellformed_blocks_dev(2, N * K // 32, gen)) for _ in range(COPIES)]
+    xs = torch.randn((COPIES, B, K), device="cuda", generator=gen)
+    ys = torch.empty((COPIES, B, N), device="cuda")
+    stream = torch.cuda.Stream()
+    L = x100b.lib()
+
+    def run():
+        s = torch.cuda.current_stream().cuda_stream
+        for c in range(COPIES):
+            rc = L.x100q_lin_gemv_dev(lins[c].h, xs[c].data_ptr(), ys[c].data_ptr(), B, s)
+            if rc:
+                raise x100b.X100Error(rc, "x100q_lin_gemv_dev")
+    with torch.cuda.stream(stream):
+        ms, clocks = timed_graph(run, args.steps, args.warmup, dist, stream)
+    calls = args.steps * COPIES
+    wbytes = N * K // 32 * 18
+    alg = wbytes + B * (4 * K + 4 * N)
+    per_call_s = ms / 1e3 / calls
+    gbs = alg / per_call_s / 1e9
+    # parity spot check of the last outputs against the oracle
+    import py_oracle as po  # checker only
+    blk = wellformed_blocks_dev(2, N * K // 32, torch.Generator(device="cuda").manual_seed(5))
+    chk = x100b.Lin(x100b.Q4_0, N, K, blk)
+    xh = np.random.default_rng(1).normal(0, 1, size=(B, K)).astype(np.float32)
+    yh = np.empty((B, N), np.float32)
+    chk.gemv(xh, yh, B)
+    err = po.rel_l2(yh, po.qgemv(po.Q4_0, blk, N, K, xh, nthreads=cpu_threads()))
+    assert err <= 1e-3, err
+    # e2e: host x in pinned memory -> y on host, through the synchronous API
+    xh_p = torch.empty((B, K), pin_memory=True).copy_(xs[0])
+    yh_p = torch.empty((B, N), pin_memory=True)
+    for _ in range(5):
+        L.x100q_lin_gemv(lins[0].h, xh_p.data_ptr(), yh_p.data_ptr(), B)
+    e2e_steps = 200
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        rc = L.x100q_lin_gemv(lins[i % COPIES].h, xh_p.data_ptr(), yh_p.data_ptr(), B)
+    dt = dist.max(time.perf_counter() - t0)
+    if rc:
+        raise x100b.X100Error(rc, "x100q_lin_gemv")
+    cpu = None
+    if dist.world == 1 and not args.no_cpu_baseline:
+        nt = cpu_threads()
+        reps = 20
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            po.qgemv(po.Q4_0, blk, N, K, xh, nthreads=nt)
+        cdt = (time.perf_counter() - t0) / reps
+        cpu = {"value": round(alg / cdt / 1e9, 3), "unit": "GB/s", "cores": nt, "kind": "port",
+               "sample": f"oracle scalar dequant-GEMV (restates qwen_moe.c:164-165 + fp32 dot) on the full "
+                         f"{N}x{K} Q4_0 matrix, batch {B}, {reps} reps, row-sliced over {nt} threads"}
+    return {
+        "metric": "Q4_0 dequant-GEMV HBM GB/s", "value": round(gbs * dist.world, 2), "unit": "GB/s",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_0 weights, fp32 activations (int32 dp4a on 16-bit split x)",
+        "data": "synthetic random well-formed Q4_0 blocks, x ~ N(0,1)",
+        "config": {"workload": f"Q4_0 GEMV y=W.x W {N}x{K} batch {B}", "N": N, "K": K, "batch": B,
+                   "l2": f"{COPIES} weight copies rotated per step ({COPIES * wbytes / 2**20:.0f} MiB > L2)",
+                   "graph": f"one CUDA graph of {COPIES} GEMV launches per step"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": load_traffic(f"q4gemv_b{B}"),
+                     "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
+                     "kernel": "x100::q::qgemv_kernel<Q4_0>", "algorithmic_bytes_per_launch": alg,
+                     "kernel_us_mean": round(per_call_s * 1e6, 3), "parity_rel_l2": err},
+        "clocks": clocks,
+        "e2e": {"value": round(alg * e2e_steps / dt / 1e9, 3), "unit": "GB/s",
+                "h2d_bytes_per_step": 4 * B * K, "d2h_bytes_per_step": 4 * B * N,
+                "api": "x100q_lin_gemv(lin, x, y, batch) with pinned host x, y (synchronous)"},
+        "gpu_launches": calls,
+        "cpu_baseline": cpu,
+    }
+
+
+def bench_moe(args, dist, peaks, peak_src):
+    """one MoE layer (d 2048, 128 experts, top-8, ffn 768,
+    Q4_K).  Each rank holds 128/N experts (expert parallel) and the full
+    router; per step every rank runs the layer for `batch` tokens and the
+    partial outputs are summed with an NCCL all-reduce."""
+    import numpy as np
+    import torch
+    import x100b
+    d, E, k, ffn, B = 2048, 128, 8, 768, args.batch
+    world, rank = dist.world, dist.rank
+    lo, hi = rank * E // world, (rank + 1) * E // world
+    gen = torch.Generator(device="cuda").manual_seed(99)
+    router = (torch.randn((E, d), device="cuda", generator=gen) * 0.02).cpu().numpy()
+    nb_d = ffn * d // 256
+    layers = []
+    host0 = None
+    LAYERS = 2
+    for li in range(LAYERS):
+        # full-size tensors, only the local slice [lo, hi) is uploaded
+        gate = np.zeros(E * nb_d * 144, np.uint8)
+        up = np.zeros_like(gate)
+        down = np.zeros_like(gate)
+        sl = slice(lo * nb_d * 144, hi * nb_d * 144)
+        gate[sl] = wellformed_blocks_dev(12, (hi - lo) * nb_d, gen)
+        up[sl] = wellformed_blocks_dev(12, (hi - lo) * nb_d, gen)
+        down[sl] = wellformed_blocks_dev(12, (hi - lo) * nb_d, gen)
+        layers.append(x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down, lo, hi))
+        if li == 0:
+            host0 = (gate, up, down)
+    POOL = 64
+    hns = torch.randn((POOL, B, d), device="cuda", generator=gen)
+    out = torch.empty((POOL, B, d), device="cuda")
+    L = x100b.lib()
+    stream = torch.cuda.Stream()
+    state = {"i": 0}
+
+    def one(i):
+        s = torch.cuda.current_stream().cuda_stream
+        rc = L.x100q_moe_ffn_dev(layers[i % LAYERS].h, hns[i % POOL].data_ptr(), out[i % POOL].data_ptr(), B,
+                                 None, None, s)
+        if rc:
+            raise x100b.X100Error(rc, "x100q_moe_ffn_dev")
+        if world > 1:
+            dist.pg.all_reduce(out[i % POOL])
+
+    PER = 16   # MoE calls per captured graph (each a different hn, layer copy)
+
+    def run():
+        for j in range(PER):
+            one(j)
+    with torch.cuda.stream(stream):
+        if world == 1:
+            ms, clocks = timed_graph(run, args.steps, args.warmup, dist, stream)
+            calls = args.steps * PER
+        else:
+            for i in range(args.warmup * PER):
+                one(i)
+            torch.cuda.synchronize()
+            dist.barrier()
+            clk = ClockSampler(dist.physical_gpu())
+            clk.start()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(args.steps * PER):
+                one(i)
+            e1.record()
+            torch.cuda.synchronize()
+            dist.barrier()
+            clocks = clk.stop()
+            ms = dist.max(e0.elapsed_time(e1))
+            calls = args.steps * PER
+    tok_s = calls * B / (ms / 1e3)
+    alg_tok = 8 * 2654208 + 1048576 + 16384        # bytes per token (SURVEY config C4)
+    per_call_us = ms * 1e3 / calls
+    achieved = alg_tok * B / (per_call_us / 1e6) / 1e9 / world   # per-GPU share
+    # parity of one step against the oracle on the same weights (1 GPU only)
+    err = None
+    if world == 1:
+        import py_oracle as po  # checker only
+        hh = hns[0].cpu().numpy()
+        eo, sel, _ = layers[0].ffn_host(hh)
+        ref, rsel, _ = po.moe_ffn(d, E, k, ffn, po.Q4_K, router, *host0, hh, nthreads=cpu_threads())
+        assert np.array_equal(sel, rsel), "expert selection differs from the oracle"
+        err = po.rel_l2(eo, ref)
+        assert err <= 1e-3, err
+    # e2e through the synchronous host API
+    hn_p = torch.empty((B, d), pin_memory=True).copy_(hns[0])
+    eo_p = torch.empty((B, d), pin_memory=True)
+    for _ in range(5):
+        L.x100q_moe_ffn(layers[0].h, hn_p.data_ptr(), eo_p.data_ptr(), B, None, None)
+    e2e_steps = 100
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        rc = L.x100q_moe_ffn(layers[i % LAYERS].h, hn_p.data_ptr(), eo_p.data_ptr(), B, None, None)
+        if world > 1:
+            t = torch.from_numpy(eo_p.numpy()).cuda()
+            dist.pg.all_reduce(t)
+            eo_p.copy_(t)
+    dt = dist.max(time.perf_counter() - t0)
+    if rc:
+        raise x100b.X100Error(rc, "x100q_moe_ffn")
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        import py_oracle as po
+        rng = np.random.default_rng(0)
+        nt = cpu_threads()
+        hh = rng.normal(0, 1, size=(1, d)).astype(np.float32)
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            po.moe_ffn(d, E, k, ffn, po.Q4_K, router, *host0, hh, nthreads=nt)
+        cdt = (time.perf_counter() - t0) / reps
+        cpu = {"value": round(1.0 / cdt, 3), "unit": "tokens/s", "cores": nt, "kind": "port",
+               "sample": f"oracle MoE block (restates qwen_moe.c:295-311, fp32 router, exact SiLU) for one "
+                         f"token through the same {E}-expert Q4_K layer, {reps} reps, GEMV rows over {nt} threads"}
+    return {
+        "metric": "Q4_K MoE layer decode tokens/s", "value": round(tok_s, 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "q4_k weights, fp32 activations",
+        "data": "synthetic: random well-formed Q4_K expert blocks, fp32 router N(0,0.02), hn ~ N(0,1)",
+        "config": {"workload": f"MoE layer d={d} experts={E} top-{k} ffn={ffn} Q4_K, batch {B}",
+                   "batch": B, "expert_parallel": f"{E // world} experts per GPU",
+                   "l2": f"{LAYERS} layer copies x {POOL} hn vectors rotated",
+                   "graph": f"{PER} MoE calls per CUDA graph" if world == 1 else "eager + NCCL all-reduce"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(f"moe_b{B}"),
+                     "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
+                     "kernel": "router_topk + gate_up + down_combine (3 launches per call)",
+                     "algorithmic_bytes_per_token": alg_tok, "call_us_mean": round(per_call_us, 3),
+                     "parity": err},
+        "clocks": clocks,
+        "e2e": {"value": round(e2e_steps * B / dt, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": 4 * B * d, "d2h_bytes_per_step": 4 * B * d,
+                "api": "x100q_moe_ffn(moe, hn, eout, batch) with pinned host hn, eout (synchronous)"},
+        "gpu_launches": calls * 3,
+        "cpu_baseline": cpu,
+    }
+
+
 def bench_reference(args):
     """--impl reference: the reference's own CPU GEMM on this host's cores."""
     if int(os.environ.get("RANK", "0")) != 0:
@@ -461,9 +740,10 @@ def main():
     try:
         if args.workload.startswith("gemm"):
             line = bench_gemm(args, dist, peaks, src)
+        elif args.workload == "q4gemv":
+            line = bench_q4gemv(args, dist, peaks, src)
         else:
-            import bench_quant
-            line = bench_quant.run(args, dist, peaks, src)
+            line = bench_moe(args, dist, peaks, src)
     finally:
         dist.close()
     if dist.rank == 0:

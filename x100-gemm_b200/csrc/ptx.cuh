@@ -107,6 +107,17 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         : "memory");
 }
 
+// 1-D bulk copy global -> this CTA's shared memory (no registers involved);
+// dst, src 16-byte aligned, bytes a multiple of 16; completion is signalled as
+// transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // ---- tcgen05 ---------------------------------------------------------------------
 // Whole-warp collective: allocate `ncols` TMEM columns, address written to smem.
 __device__ __forceinline__ void tmem_alloc(uint32_t *smem_dst, uint32_t ncols) {

@@ -16,6 +16,7 @@
 // CTA itself from the fp32 x (qformats.cuh: xprep_block).
 #include <cuda_fp16.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "../../include/x100q.h"
@@ -24,6 +25,14 @@
 
 namespace x100 {
 namespace q {
+
+bool pdl_enabled_impl() {
+    static const bool on = [] {
+        const char *e = getenv("X100_NO_PDL");
+        return !(e && *e && *e != '0');
+    }();
+    return on;
+}
 
 int lanes_per_row(int units) {
     int l = 32;
@@ -34,10 +43,12 @@ int lanes_per_row(int units) {
 template <int QT, int B, int RR>
 __global__ void __launch_bounds__(256) qgemv_kernel(QView W, const float *__restrict__ x, float *__restrict__ y,
                                                     int batch, int lpr) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem[];
     const int nxb = W.K / 32;
     XBlk *xq = reinterpret_cast<XBlk *>(smem);
     XF *xf = reinterpret_cast<XF *>(smem + sizeof(XBlk) * B * nxb);
+    pdl_launch_dependents();
+    pdl_wait();
     // activation planes for all batch columns
     xprep_all(x, W.K, batch, xq, xf);
     __syncthreads();
@@ -85,6 +96,318 @@ __global__ void __launch_bounds__(256) qgemv_kernel(QView W, const float *__rest
     }
 }
 
+// Slice kernel (K % 256 == 0, K <= 4096): warp w owns the 256-element slice
+// w of 32 consecutive rows (lane = row).  Each lane issues its slice's
+// 16-byte weight loads first, the CTA then prepares the activation planes in
+// shared memory while those loads are in flight, every lane dots its slice
+// against the same (broadcast) activation blocks, and the per-slice partial
+// sums are added in slice order through shared memory.
+template <int QT, int B>
+__global__ void __launch_bounds__(512) qgemv_slice_kernel(QView W, const float *__restrict__ x,
+                                                          float *__restrict__ y, int batch) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int nxb = W.K / 32, ns = W.K / 256;
+    XBlk *xq = reinterpret_cast<XBlk *>(smem);
+    XF *xf = reinterpret_cast<XF *>(smem + sizeof(XBlk) * B * nxb);
+    float *red = reinterpret_cast<float *>(xf + B * nxb);   // [slice][b][lane]
+    const int lane = threadIdx.x & 31, sl = threadIdx.x >> 5;
+    const int row = blockIdx.x * 32 + lane;
+    WSlice<QT> ws;
+    if (row < W.N) load_slice<QT>(W, row, sl, ws);
+    pdl_launch_dependents();
+    pdl_wait();
+    xprep_all(x, W.K, batch, xq, xf);
+    __syncthreads();
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        float a = 0.f;
+        if (b < batch && row < W.N) a = dot_slice<QT>(ws, xq + b * nxb + sl * 8, xf + b * nxb + sl * 8);
+        red[(sl * B + b) * 32 + lane] = a;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < 32 * B; t += blockDim.x) {
+        const int l = t & 31, b = t >> 5;
+        const int r = blockIdx.x * 32 + l;
+        if (b < batch && r < W.N) {
+            float acc = 0.f;
+            for (int k = 0; k < ns; ++k) acc += red[(k * B + b) * 32 + l];
+            y[(long)b * W.N + r] = acc;
+        }
+    }
+}
+
+// Half-slice kernel (K % 256 == 0, K <= 2048): warp w owns half w % 2 of
+// slice w / 2 for 32 consecutive rows (lane = row), so a CTA of K/4 threads
+// covers 32 full rows.  Weight loads are issued before waiting on the
+// previous kernel of the stream (programmatic dependent launch), the
+// activation planes are prepared once per CTA, every lane of a warp reads the
+// same activation blocks (broadcast), and the per-half partial sums are added
+// in K order through shared memory.
+template <int QT, int B>
+__global__ void __launch_bounds__(512) qgemv_half_kernel(QView W, const float *__restrict__ x,
+                                                         float *__restrict__ y, int batch) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int nxb = W.K / 32, nh = W.K / 128;
+    XBlk *xq = reinterpret_cast<XBlk *>(smem);
+    XF *xf = reinterpret_cast<XF *>(smem + sizeof(XBlk) * B * nxb);
+    float *red = reinterpret_cast<float *>(xf + B * nxb);   // [half slice][b][lane]
+    const int lane = threadIdx.x & 31, hs = threadIdx.x >> 5;
+    const int row = blockIdx.x * 32 + lane;
+    WHalf<QT> wh;
+    if (row < W.N) load_half<QT>(W, row, hs >> 1, hs & 1, wh);
+    pdl_launch_dependents();
+    pdl_wait();
+    xprep_all(x, W.K, batch, xq, xf);
+    __syncthreads();
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        float a = 0.f;
+        if (b < batch && row < W.N) a = dot_half<QT>(wh, hs & 1, xq + b * nxb + hs * 4, xf + b * nxb + hs * 4);
+        red[(hs * B + b) * 32 + lane] = a;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < 32 * B; t += blockDim.x) {
+        const int l = t & 31, b = t >> 5;
+        const int r = blockIdx.x * 32 + l;
+        if (b < batch && r < W.N) {
+            float acc = 0.f;
+            for (int k = 0; k < nh; ++k) acc += red[(k * B + b) * 32 + l];
+            y[(long)b * W.N + r] = acc;
+        }
+    }
+}
+
+// Staged kernel (K % 256 == 0): a CTA owns 32 consecutive rows.  All threads
+// copy the 32 rows (and their scale rows) into padded shared memory with
+// 16-byte cp.async requests -- issued before waiting on the previous kernel
+// of the stream, with no registers tied up by loads in flight -- and then
+// prepare the activation planes while the copies land.  Warp w dots slices
+// w, w+nw, ... of every row (lane = row) against the broadcast activation
+// blocks; the per-warp partial sums are added in warp order.
+template <int QT, int B>
+__global__ void __launch_bounds__(256, 2) qgemv_bulk_kernel(QView W, const float *__restrict__ x,
+                                                         float *__restrict__ y, int batch, int *status) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int K = W.K, nxb = K / 32, ns = K / 256;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int row0 = blockIdx.x * 32;
+    const int rows = min(32, W.N - row0);
+    uint8_t *tile = smem;
+    XBlk *xq = reinterpret_cast<XBlk *>(smem + tile_bytes(QT, K, 32));
+    XF *xf = reinterpret_cast<XF *>(xq + B * nxb);
+    float *red = reinterpret_cast<float *>(xf + B * nxb);   // [warp][b][lane]
+    if (rows > 0) tile_cp_async(W, row0, rows, tile, 32);
+    cp_async_commit();
+    pdl_launch_dependents();
+    pdl_wait();
+    xprep_all(x, K, batch, xq, xf);
+    cp_async_wait_all();
+    __syncthreads();
+    const bool ok = true;
+    float acc[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = 0.f;
+    if (ok && lane < rows) {
+        const QView T = tile_view(QT, K, tile, 32);
+        for (int sl = warp; sl < ns; sl += nw) {
+            WSlice<QT> ws;
+            load_slice<QT, false>(T, lane, sl, ws);
+#pragma unroll
+            for (int b = 0; b < B; ++b)
+                if (b < batch) acc[b] += dot_slice<QT>(ws, xq + b * nxb + sl * 8, xf + b * nxb + sl * 8);
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) red[(warp * B + b) * 32 + lane] = acc[b];
+    __syncthreads();
+    for (int t = threadIdx.x; t < 32 * B; t += blockDim.x) {
+        const int l = t & 31, b = t >> 5;
+        if (b < batch && l < rows) {
+            float sum = 0.f;
+            for (int k = 0; k < nw; ++k) sum += red[(k * B + b) * 32 + l];
+            y[(long)b * W.N + row0 + l] = sum;
+        }
+    }
+}
+
+// Warp-independent kernel (K % 256 == 0): a CTA owns 32 consecutive rows
+// and warp w owns K-slices w, w+nw, ...  Each warp stages its own slices of
+// the 32 rows (one 1-D bulk copy per row and slice, issued before waiting on
+// the previous kernel of the stream) behind its own mbarrier, prepares the
+// activation blocks of those slices, and computes as soon as its bytes have
+// landed; the only CTA-wide synchronisation is the final reduction of the
+// per-warp partial sums (added in warp order).
+template <int QT> struct SliceBytes;
+template <> struct SliceBytes<Q4_0> { static constexpr int w = 128, s = 16; };
+template <> struct SliceBytes<Q8_0> { static constexpr int w = 256, s = 16; };
+template <> struct SliceBytes<Q4_K> { static constexpr int w = 144, s = 0; };
+template <> struct SliceBytes<Q3_K> { static constexpr int w = 112, s = 0; };
+template <int QT> __host__ __device__ constexpr int ws_slice_stride() { return bulk_stride(SliceBytes<QT>::w); }
+template <int QT> __host__ __device__ constexpr int ws_scale_stride() { return SliceBytes<QT>::s ? bulk_stride(SliceBytes<QT>::s) : 0; }
+// shared bytes for one staged slice of 32 rows
+template <int QT> __host__ __device__ constexpr int ws_slice_tile() { return 32 * (ws_slice_stride<QT>() + ws_scale_stride<QT>()); }
+
+template <int QT, int B>
+__global__ void __launch_bounds__(256, 2) qgemv_ws_kernel(QView W, const float *__restrict__ x,
+                                                          float *__restrict__ y, int batch, int *status) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ uint64_t bars[8];
+    __shared__ int abort_flag;
+    const int K = W.K, ns = K / 256;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int spw = (ns + nw - 1) / nw;                        // slices per warp (last warps may have fewer)
+    const int row0 = blockIdx.x * 32;
+    const int rows = min(32, W.N - row0);
+    constexpr int TS = ws_slice_tile<QT>();
+    uint8_t *tiles = smem + (size_t)warp * spw * TS;
+    XBlk *xq = reinterpret_cast<XBlk *>(smem + (size_t)nw * spw * TS) + (size_t)warp * spw * 8 * B;
+    XF *xf = reinterpret_cast<XF *>(reinterpret_cast<XBlk *>(smem + (size_t)nw * spw * TS) + (size_t)nw * spw * 8 * B) +
+             (size_t)warp * spw * 8 * B;
+    float *red = reinterpret_cast<float *>(reinterpret_cast<XF *>(reinterpret_cast<XBlk *>(smem + (size_t)nw * spw * TS) +
+                                                                  (size_t)nw * spw * 8 * B) + (size_t)nw * spw * 8 * B);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nw; ++i) mbar_init(&bars[i], 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    int my_slices = 0;
+    for (int k = 0; k < spw; ++k) my_slices += (warp + k * nw < ns);
+    if (lane == 0)
+        mbar_arrive_expect_tx(&bars[warp], (uint32_t)(my_slices * rows * (SliceBytes<QT>::w + SliceBytes<QT>::s)));
+    __syncwarp();
+    if (lane < rows) {
+        const long grow = row0 + lane;
+        for (int k = 0; k < my_slices; ++k) {
+            const int sl = warp + k * nw;
+            uint8_t *t = tiles + k * TS;
+            bulk_load(t + lane * ws_slice_stride<QT>(), W.w + grow * W.wstride + (long)sl * SliceBytes<QT>::w,
+                      SliceBytes<QT>::w, &bars[warp]);
+            if (SliceBytes<QT>::s)
+                bulk_load(t + 32 * ws_slice_stride<QT>() + lane * ws_scale_stride<QT>(),
+                          reinterpret_cast<const uint8_t *>(W.d + grow * W.dstride) + sl * SliceBytes<QT>::s,
+                          SliceBytes<QT>::s, &bars[warp]);
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    // this warp's activation blocks: batch b, slice k -> 8 blocks at xq[(k * B + b) * 8]
+    {
+        const int total = my_slices * batch * 8;
+        for (int b0 = 0; b0 < total; b0 += 4) {
+            const int blk = b0 + (lane >> 3);
+            const bool act = blk < total;
+            const int k = act ? blk / (batch * 8) : 0, rem = act ? blk % (batch * 8) : 0;
+            const int b = rem / 8, j = rem % 8;
+            const int sl = warp + k * nw;
+            xprep_block(x + (long)b * K + sl * 256 + j * 32, &xq[(k * B + b) * 8 + j], &xf[(k * B + b) * 8 + j],
+                        lane & 7, act);
+        }
+    }
+    __syncwarp();
+    const bool ok = mbar_wait(&bars[warp], 0, &abort_flag, status);
+    float acc[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = 0.f;
+    if (ok && lane < rows) {
+        for (int k = 0; k < my_slices; ++k) {
+            QView T;
+            T.qt = QT;
+            T.K = 256;
+            T.N = 32;
+            T.w = tiles + k * TS;
+            T.wstride = ws_slice_stride<QT>();
+            T.d = reinterpret_cast<const __half *>(tiles + k * TS + 32 * ws_slice_stride<QT>());
+            T.dstride = ws_scale_stride<QT>() / 2;
+            WSlice<QT> w;
+            load_slice<QT, false>(T, lane, 0, w);
+#pragma unroll
+            for (int b = 0; b < B; ++b)
+                if (b < batch) acc[b] += dot_slice<QT>(w, xq + (k * B + b) * 8, xf + (k * B + b) * 8);
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) red[(warp * B + b) * 32 + lane] = acc[b];
+    __syncthreads();
+    if (abort_flag) {
+        if (lane == 0) mbar_wait_drain(&bars[warp], 0, 100000000ull);
+        return;
+    }
+    for (int t = threadIdx.x; t < 32 * B; t += blockDim.x) {
+        const int l = t & 31, b = t >> 5;
+        if (b < batch && l < rows) {
+            float sum = 0.f;
+            for (int k = 0; k < nw; ++k) sum += red[(k * B + b) * 32 + l];
+            y[(long)b * W.N + row0 + l] = sum;
+        }
+    }
+}
+
+// TMA kernel (K % 256 == 0): a CTA owns 32 consecutive rows; one thread
+// stages them with 2-D TMA boxes (32 rows x 128 bytes, a handful of requests
+// per CTA) issued before waiting on the previous kernel of the stream; the
+// CTA prepares the activation planes while the boxes land; warp w then dots
+// slices w, w+nw, ... of every row (lane = row) against the broadcast
+// activation blocks; the per-warp partial sums are added in warp order.
+template <int QT, int B>
+__global__ void __launch_bounds__(256, 2) qgemv_tma_kernel(const __grid_constant__ CUtensorMap tmw,
+                                                           const __grid_constant__ CUtensorMap tmd, QView W,
+                                                           const float *__restrict__ x, float *__restrict__ y,
+                                                           int batch, int *status) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    const int K = W.K, nxb = K / 32, ns = K / 256;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int row0 = blockIdx.x * 32;
+    const int rows = min(32, W.N - row0);
+    // TMA 128-byte swizzle needs 1024-byte aligned boxes
+    uint8_t *tile = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
+    XBlk *xq = reinterpret_cast<XBlk *>(tile + tma_tile_bytes(QT, K));
+    XF *xf = reinterpret_cast<XF *>(xq + B * nxb);
+    float *red = reinterpret_cast<float *>(xf + B * nxb);   // [warp][b][lane]
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+        mbar_arrive_expect_tx(&bar, (uint32_t)tma_tile_bytes(QT, K));
+        tma_issue_tile(&tmw, &tmd, QT, K, row0, tile, &bar);
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    xprep_all(x, K, batch, xq, xf);
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0, &abort_flag, status);
+    float acc[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = 0.f;
+    if (ok && lane < rows) {
+        const int nwb = tma_wboxes(QT, K);
+        for (int sl = warp; sl < ns; sl += nw) {
+            WSlice<QT> ws;
+            load_slice_swz<QT>(tile, nwb, lane, sl, ws);
+#pragma unroll
+            for (int b = 0; b < B; ++b)
+                if (b < batch) acc[b] += dot_slice<QT>(ws, xq + b * nxb + sl * 8, xf + b * nxb + sl * 8);
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) red[(warp * B + b) * 32 + lane] = acc[b];
+    __syncthreads();
+    if (abort_flag) {
+        if (threadIdx.x == 0) mbar_wait_drain(&bar, 0, 100000000ull);   // boxes still in flight
+        return;
+    }
+    for (int t = threadIdx.x; t < 32 * B; t += blockDim.x) {
+        const int l = t & 31, b = t >> 5;
+        if (b < batch && l < rows) {
+            float sum = 0.f;
+            for (int k = 0; k < nw; ++k) sum += red[(k * B + b) * 32 + l];
+            y[(long)b * W.N + row0 + l] = sum;
+        }
+    }
+}
+
 // ---- device re-layout of GGUF-native blocks ------------------------------------
 __global__ void repack_kernel(int qt, long nblocks, const uint8_t *__restrict__ src, uint8_t *__restrict__ w,
                               __half *__restrict__ d) {
@@ -112,6 +435,8 @@ __global__ void repack_kernel(int qt, long nblocks, const uint8_t *__restrict__ 
 }
 
 }  // namespace q
+
+bool pdl_enabled() { return q::pdl_enabled_impl(); }
 
 using namespace q;
 
@@ -162,6 +487,15 @@ bool qmat_upload(DevCtx *c, int qt, int N, int K, const void *blocks, QMat &m, c
         if (check_cuda(e == cudaSuccess ? cudaGetLastError() : e, X100_E_LAUNCH)) goto fail;
     }
     if (check_cuda(cudaStreamSynchronize(s), X100_E_COPY)) goto fail;
+    {
+        const int wb = (int)row_bytes_dev(qt, K), sb = qscale_row_bytes(qt, K);
+        m.tma_ok = make_tmap_2d(&m.tmw, m.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)wb, (uint64_t)N, (uint64_t)wb, 128,
+                                32);
+        if (m.tma_ok && sb)
+            m.tma_ok = make_tmap_2d(&m.tmd, m.d, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)sb, (uint64_t)N, (uint64_t)sb,
+                                    128, 32);
+        if (!sb) m.tmd = m.tmw;
+    }
     return true;
 fail:
     cudaFree(m.w);
@@ -182,7 +516,112 @@ QView qmat_view(const QMat &m, long row0) {
 }
 
 template <int QT, int B>
-static int launch_B(DevCtx *c, const QView &v, const float *x, float *y, int batch, cudaStream_t s) {
+static int launch_slice(DevCtx *c, const QView &v, const float *x, float *y, int batch, cudaStream_t s) {
+    const int ns = v.K / 256;
+    const size_t smem = (size_t)B * (v.K / 32) * (sizeof(XBlk) + sizeof(XF)) + (size_t)ns * B * 32 * 4;
+    static bool attr[64];
+    if (!attr[c->device]) {
+        set_qkernel_attrs(qgemv_slice_kernel<QT, B>);
+        attr[c->device] = true;
+    }
+    return launch_pdl(qgemv_slice_kernel<QT, B>, dim3((v.N + 31) / 32), dim3(32 * ns), smem, s, v, x, y, batch);
+}
+
+// The slice kernel serves K % 256 == 0, K <= 4096 while its shared memory
+// fits; other shapes take the unit kernel.
+static bool slice_ok(int K, int B) {
+    if (K % 256 || K > 4096) return false;
+    const size_t smem = (size_t)B * (K / 32) * (sizeof(XBlk) + sizeof(XF)) + (size_t)(K / 256) * B * 32 * 4;
+    return smem <= 200 * 1024;
+}
+
+template <int QT, int B>
+static int launch_half(DevCtx *c, const QView &v, const float *x, float *y, int batch, cudaStream_t s) {
+    const int nh = v.K / 128;
+    const size_t smem = (size_t)B * (v.K / 32) * (sizeof(XBlk) + sizeof(XF)) + (size_t)nh * B * 32 * 4;
+    static bool attr[64];
+    if (!attr[c->device]) {
+        set_qkernel_attrs(qgemv_half_kernel<QT, B>);
+        attr[c->device] = true;
+    }
+    return launch_pdl(qgemv_half_kernel<QT, B>, dim3((v.N + 31) / 32), dim3(32 * nh), smem, s, v, x, y, batch);
+}
+
+static bool half_ok(int K, int B) {
+    if (K % 256 || K > 2048) return false;
+    const size_t smem = (size_t)B * (K / 32) * (sizeof(XBlk) + sizeof(XF)) + (size_t)(K / 128) * B * 32 * 4;
+    return smem <= 200 * 1024;
+}
+
+template <int QT, int B>
+static size_t bulk_smem(int K) {
+    const int nw = std::min(K / 256, 8);
+    return (size_t)tile_bytes(QT, K, 32) + (size_t)B * (K / 32) * (sizeof(XBlk) + sizeof(XF)) + (size_t)nw * B * 32 * 4;
+}
+
+template <int QT, int B>
+static int launch_bulk(DevCtx *c, const QView &v, const float *x, float *y, int batch, cudaStream_t s) {
+    const size_t smem = bulk_smem<QT, B>(v.K);
+    static bool attr[64];
+    if (!attr[c->device]) {
+        set_qkernel_attrs(qgemv_bulk_kernel<QT, B>);
+        attr[c->device] = true;
+    }
+    const int nw = std::min(v.K / 256, 8);
+    return launch_pdl(qgemv_bulk_kernel<QT, B>, dim3((v.N + 31) / 32), dim3(32 * nw), smem, s, v, x, y, batch,
+                      c->d_status);
+}
+
+template <int QT, int B>
+static size_t ws_smem(int K) {
+    const int ns = K / 256, nw = std::min(ns, 8), spw = (ns + nw - 1) / nw;
+    return (size_t)nw * spw * ws_slice_tile<QT>() + (size_t)nw * spw * 8 * B * (sizeof(XBlk) + sizeof(XF)) +
+           (size_t)nw * B * 32 * 4;
+}
+
+template <int QT, int B>
+static int launch_ws(DevCtx *c, const QView &v, const float *x, float *y, int batch, cudaStream_t s) {
+    const size_t smem = ws_smem<QT, B>(v.K);
+    static bool attr[64];
+    if (!attr[c->device]) {
+        set_qkernel_attrs(qgemv_ws_kernel<QT, B>);
+        attr[c->device] = true;
+    }
+    const int nw = std::min(v.K / 256, 8);
+    return launch_pdl(qgemv_ws_kernel<QT, B>, dim3((v.N + 31) / 32), dim3(32 * nw), smem, s, v, x, y, batch,
+                      c->d_status);
+}
+
+template <int QT, int B>
+static size_t tma_smem(int K) {
+    const int nw = std::min(K / 256, 8);
+    return 1024 + (size_t)tma_tile_bytes(QT, K) + (size_t)B * (K / 32) * (sizeof(XBlk) + sizeof(XF)) +
+           (size_t)nw * B * 32 * 4;
+}
+
+template <int QT, int B>
+static int launch_tma(DevCtx *c, const QMat &m, const QView &v, const float *x, float *y, int batch, cudaStream_t s) {
+    const size_t smem = tma_smem<QT, B>(v.K);
+    static bool attr[64];
+    if (!attr[c->device]) {
+        set_qkernel_attrs(qgemv_tma_kernel<QT, B>);
+        attr[c->device] = true;
+    }
+    const int nw = std::min(v.K / 256, 8);
+    return launch_pdl(qgemv_tma_kernel<QT, B>, dim3((v.N + 31) / 32), dim3(32 * nw), smem, s, m.tmw, m.tmd, v, x, y,
+                      batch, c->d_status);
+}
+
+template <int QT, int B>
+static int launch_B(DevCtx *c, const QMat &m, const QView &v, const float *x, float *y, int batch, cudaStream_t s) {
+    static const int mode = [] { const char *e = getenv("X100_GEMV_KERNEL"); return e ? atoi(e) : 0; }();
+    if (mode == 0 && m.tma_ok && v.K % 256 == 0 && tma_smem<QT, B>(v.K) <= 200 * 1024)
+        return launch_tma<QT, B>(c, m, v, x, y, batch, s);
+    if (mode == 3 && v.K % 256 == 0 && ws_smem<QT, B>(v.K) <= 200 * 1024) return launch_ws<QT, B>(c, v, x, y, batch, s);
+    if (mode <= 1 && v.K % 256 == 0 && bulk_smem<QT, B>(v.K) <= 200 * 1024)
+        return launch_bulk<QT, B>(c, v, x, y, batch, s);
+    if (half_ok(v.K, B)) return launch_half<QT, B>(c, v, x, y, batch, s);
+    if (slice_ok(v.K, B)) return launch_slice<QT, B>(c, v, x, y, batch, s);
     constexpr int RR = B <= 2 ? 2 : 1;
     const int lpr = lanes_per_row(units_per_row(QT, v.K));
     const int rows_per_warp = (32 / lpr) * RR;
@@ -193,37 +632,37 @@ static int launch_B(DevCtx *c, const QView &v, const float *x, float *y, int bat
         return X100_E_UNSUPPORTED;
     }
     static bool attr[64][2];
-    if (smem > 48 * 1024 && !attr[c->device][0]) {
-        cudaFuncSetAttribute(qgemv_kernel<QT, B, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (!attr[c->device][0]) {
+        set_qkernel_attrs(qgemv_kernel<QT, B, RR>);
         attr[c->device][0] = true;
     }
     long grid = (passes + 7) / 8;
     const long cap = (long)c->sm_count * 4;
     if (grid > cap) grid = cap;
-    qgemv_kernel<QT, B, RR><<<(int)grid, 256, smem, s>>>(v, x, y, batch, lpr);
-    return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+    return launch_pdl(qgemv_kernel<QT, B, RR>, dim3((unsigned)grid), dim3(256), smem, s, v, x, y, batch, lpr);
 }
 
 template <int QT>
-static int launch_qt(DevCtx *c, const QView &v, const float *x, float *y, int batch, cudaStream_t s) {
-    if (batch <= 1) return launch_B<QT, 1>(c, v, x, y, batch, s);
-    if (batch <= 2) return launch_B<QT, 2>(c, v, x, y, batch, s);
-    if (batch <= 4) return launch_B<QT, 4>(c, v, x, y, batch, s);
-    if (batch <= 8) return launch_B<QT, 8>(c, v, x, y, batch, s);
-    return launch_B<QT, 16>(c, v, x, y, batch, s);
+static int launch_qt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, cudaStream_t s) {
+    const QView v = qmat_view(m, 0);
+    if (batch <= 1) return launch_B<QT, 1>(c, m, v, x, y, batch, s);
+    if (batch <= 2) return launch_B<QT, 2>(c, m, v, x, y, batch, s);
+    if (batch <= 4) return launch_B<QT, 4>(c, m, v, x, y, batch, s);
+    if (batch <= 8) return launch_B<QT, 8>(c, m, v, x, y, batch, s);
+    return launch_B<QT, 16>(c, m, v, x, y, batch, s);
 }
 
-int launch_qgemv(DevCtx *c, const QView &v, const float *x, float *y, int batch, cudaStream_t s) {
+int launch_qgemv(DevCtx *c, const QMat &m, const float *x, float *y, int batch, cudaStream_t s) {
     if (batch < 1 || batch > 16) {
         set_error(X100_E_ARG);
         return X100_E_ARG;
     }
     if (fault_injected("launch")) return X100_E_INJECTED;
-    switch (v.qt) {
-    case Q4_0: return launch_qt<Q4_0>(c, v, x, y, batch, s);
-    case Q8_0: return launch_qt<Q8_0>(c, v, x, y, batch, s);
-    case Q4_K: return launch_qt<Q4_K>(c, v, x, y, batch, s);
-    case Q3_K: return launch_qt<Q3_K>(c, v, x, y, batch, s);
+    switch (m.qtype) {
+    case Q4_0: return launch_qt<Q4_0>(c, m, x, y, batch, s);
+    case Q8_0: return launch_qt<Q8_0>(c, m, x, y, batch, s);
+    case Q4_K: return launch_qt<Q4_K>(c, m, x, y, batch, s);
+    case Q3_K: return launch_qt<Q3_K>(c, m, x, y, batch, s);
     default: set_error(X100_E_UNSUPPORTED); return X100_E_UNSUPPORTED;
     }
 }
@@ -295,7 +734,7 @@ int x100q_lin_gemv_dev(const x100q_lin *l, const float *x, float *y, int batch, 
     }
     DevCtx *c = ctx();
     if (!c) return get_error();
-    int st = launch_qgemv(c, qmat_view(l->m, 0), x, y, batch, static_cast<cudaStream_t>(stream));
+    int st = launch_qgemv(c, l->m, x, y, batch, static_cast<cudaStream_t>(stream));
     if (st) set_error(st);
     return st;
 }
@@ -325,7 +764,7 @@ int x100q_lin_gemv(const x100q_lin *l, const float *x, float *y, int batch) {
         if (!b) return get_error();
         yd = static_cast<float *>(b);
     }
-    int st = launch_qgemv(c, qmat_view(l->m, 0), xd, yd, batch, c->stream);
+    int st = launch_qgemv(c, l->m, xd, yd, batch, c->stream);
     if (st == X100_OK && !ydev)
         st = check_cuda(cudaMemcpyAsync(y, yd, yb, cudaMemcpyDeviceToHost, c->stream), X100_E_COPY);
     int st2 = sync_and_status(c, c->stream);

@@ -15,6 +15,11 @@ struct QMat {
     void *w = nullptr;
     __half *d = nullptr;
     size_t bytes = 0;
+    // 2-D TMA maps over the weight rows and the scale rows (boxes of 32 rows
+    // x 128 bytes, 128-byte swizzle); tma_ok is false when they could not be
+    // encoded (the kernels then stage rows with cp.async).
+    CUtensorMap tmw, tmd;
+    bool tma_ok = false;
 };
 
 size_t qtype_block_elems(int qt);
@@ -25,10 +30,39 @@ bool qmat_upload(DevCtx *c, int qt, int N, int K, const void *blocks, QMat &m, c
 // Device view of rows [row0, N) of m.
 q::QView qmat_view(const QMat &m, long row0);
 // y[b*N + n] = sum_k W[n][k] x[b*K + k], b < batch (<= 16); x, y device.
-int launch_qgemv(DevCtx *c, const q::QView &v, const float *x, float *y, int batch, cudaStream_t s);
+int launch_qgemv(DevCtx *c, const QMat &m, const float *x, float *y, int batch, cudaStream_t s);
 
 namespace q {
 int lanes_per_row(int units);
+}
+
+// Launch `kernel` on `s` with programmatic stream serialization (the kernel
+// may start while the previous kernel of the stream runs; it orders itself
+// with griddepcontrol.wait).  X100_NO_PDL=1 launches without the attribute.
+bool pdl_enabled();
+
+// One-time kernel attributes for the quantised path: allow up to 200 KB of
+// dynamic shared memory and ask for the maximum shared-memory carveout, so
+// consecutive kernels of a decode step share one L1/shared split and the SM
+// need not be reconfigured (drained) between them.
+template <typename F>
+void set_qkernel_attrs(F *kernel) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+}
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return check_cuda(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...), X100_E_LAUNCH);
 }
 
 }  // namespace x100
