@@ -188,3 +188,80 @@ def test_moe_device_path_and_repeat(c4_layer):
     ref, rsel, _ = po.moe_ffn(d, E, k, ffn, po.Q4_K, router, gate, up, down, hn, nthreads=8)
     assert np.array_equal(sel.cpu().numpy(), rsel)
     assert po.rel_l2(out.cpu().numpy(), ref) <= REL_Q
+
+
+# ---- one-token calls (the fused expert kernel) ----------------------------------------
+@pytest.mark.parametrize("qt", [po.Q4_0, po.Q8_0, po.Q3_K, po.Q4_K])
+def test_moe_single_token_calls(qt):
+    """Batch-1 calls, one token at a time, against the oracle (selection exact)."""
+    d, E, k, ffn = 1024, 64, 8, 512
+    router, gate, up, down = moe_weights(qt, d, E, ffn, 21 + qt)
+    hn = np.random.default_rng(qt).normal(0, 1, size=(4, d)).astype(np.float32)
+    ref, rsel, rw = po.moe_ffn(d, E, k, ffn, qt, router, gate, up, down, hn, nthreads=8)
+    moe = x100b.Moe(d, E, k, ffn, qt, router, gate, up, down)
+    for b in range(4):
+        eout, sel, w = moe.ffn_host(hn[b:b + 1])
+        np.testing.assert_array_equal(sel[0], rsel[b])
+        np.testing.assert_allclose(w[0], rw[b], rtol=1e-5, atol=1e-7)
+        assert po.rel_l2(eout[0], ref[b]) <= REL_Q
+
+
+def test_moe_single_token_matches_batched(c4_layer):
+    """A token run alone and the same token inside a batch give the same
+    output up to summation order."""
+    d, E, k, ffn, router, gate, up, down = c4_layer
+    hn = np.random.default_rng(123).normal(0, 1, size=(2, d)).astype(np.float32)
+    moe = x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down)
+    both, sel2, _ = moe.ffn_host(hn)
+    for b in range(2):
+        one, sel1, _ = moe.ffn_host(hn[b:b + 1])
+        np.testing.assert_array_equal(sel1[0], sel2[b])
+        assert po.rel_l2(one[0], both[b]) <= 1e-5
+
+
+def test_moe_single_token_expert_parallel(c4_layer):
+    """Expert slices of 16 experts (8-way expert parallel), one token per
+    call: partial outputs sum to the full output, and a slice holding none of
+    the token's experts returns exact zeros."""
+    d, E, k, ffn, router, gate, up, down = c4_layer
+    hn = np.random.default_rng(7).normal(0, 1, size=(3, d)).astype(np.float32)
+    full = x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down)
+    ref = po.moe_ffn(d, E, k, ffn, po.Q4_K, router, gate, up, down, hn, nthreads=8)[0]
+    slices = [x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down, lo, lo + 16) for lo in range(0, E, 16)]
+    empty_seen = 0
+    for b in range(3):
+        f, sel, _ = full.ffn_host(hn[b:b + 1])
+        parts = []
+        for i, m in enumerate(slices):
+            p, psel, _ = m.ffn_host(hn[b:b + 1])
+            np.testing.assert_array_equal(psel, sel)
+            if not np.any((sel[0] >= 16 * i) & (sel[0] < 16 * i + 16)):
+                assert not np.any(p), "slice without a selected expert must return zeros"
+                empty_seen += 1
+            parts.append(p[0])
+        assert po.rel_l2(sum(parts), f[0]) <= 1e-5
+        assert po.rel_l2(sum(parts), ref[b]) <= REL_Q
+    assert empty_seen > 0
+    for m in slices:
+        m.close()
+
+
+def test_moe_single_token_device_repeat(c4_layer):
+    """Back-to-back device calls reuse the completion counter; every call
+    must see its own token."""
+    import torch
+    d, E, k, ffn, router, gate, up, down = c4_layer
+    moe = x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down)
+    hn = np.random.default_rng(55).normal(0, 1, size=(6, d)).astype(np.float32)
+    hd = torch.from_numpy(hn).cuda()
+    out = torch.empty_like(hd)
+    sel = torch.empty((6, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((6, k), device="cuda")
+    for b in range(6):
+        moe.ffn_dev(hd[b:b + 1], out[b:b + 1], 1, sel[b:b + 1], w[b:b + 1])
+    x100b.sync()
+    ref, rsel, _ = po.moe_ffn(d, E, k, ffn, po.Q4_K, router, gate, up, down, hn, nthreads=8)
+    assert np.array_equal(sel.cpu().numpy(), rsel)
+    o = out.cpu().numpy()
+    for b in range(6):
+        assert po.rel_l2(o[b], ref[b]) <= REL_Q

@@ -6,22 +6,28 @@
 // exact): router GEMV -> softmax -> greedy top-k -> renormalise -> for each
 // selected expert gate/up GEMV, silu(g)*u, down GEMV, weighted sum.
 //
-// Three kernels per call (captured into one CUDA graph by callers that loop):
-//   router_topk   one warp per expert row: fp32 logits for every token; the
-//                 last CTA to finish (atomic ticket, no waiting) does the
-//                 softmax, the greedy top-k (strict >, lowest index wins)
-//                 and the renormalisation, writing sel / w.
-//   gate_up       grid (ffn rows, token x slot): each warp streams gate row i
-//                 and up row i of the selected expert once and writes
-//                 h[token][slot][i] = silu(g) * u (SwiGLU fused).
-//   down_combine  grid (d rows, token): each warp streams row n of the down
-//                 matrix of every selected expert and writes
-//                 eout[token][n] = sum_a w_a * (down_a[n] . h_a), summed in
-//                 slot order a = 0..k-1 like the reference (no atomics).
+// Kernels per call (each launched with programmatic dependent launch, so the
+// next one starts staging weights while the previous one finishes):
+//   router_logits  one warp per expert row (row held in registers before the
+//                  wait): fp32 logits of every token.
+//   batch 1 -- moe_fused: one CTA per SM; each CTA routes the token itself
+//                  (softmax, greedy top-k with strict > and lowest index
+//                  first, renormalisation), stages every gate/up and down
+//                  row it owns at once, writes h = silu(g) * u for its
+//                  gate/up rows, and -- once a grid-wide counter shows all h
+//                  written -- sums the down rows of the selected experts in
+//                  slot order a = 0..k-1 like the reference (no atomics).
+//   batch > 1 -- gate_up (grid: row tile x token x slot) writes
+//                  h[token][slot][rows]; down (grid: row tile x token) stages
+//                  the rows of every selected expert and writes
+//                  eout[token][rows] = sum_a w_a * (down_a . h_a) in slot order.
+// router_topk (router logits + the routing in the last CTA to finish) serves
+// x100q_router_topk_noalloc.
 // Experts outside [expert_lo, expert_hi) contribute nothing (expert
 // parallelism: the caller sums eout over processes, e.g. NCCL all-reduce).
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 
@@ -158,9 +164,13 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float *__restric
 // previous kernel); writes logits[b][e].  The consumers (gate/up and down
 // kernels) each finish the routing themselves with route_cta, so no kernel
 // waits on a last-arriving CTA.
+// When `zero` is set, CTA 0 also clears zero[0 .. nzero) -- the completion
+// counters of the fused expert kernel that follows -- after the previous
+// kernel on the stream has finished with them.
 __global__ void __launch_bounds__(64) router_logits_kernel(const float *__restrict__ router,
                                                            const float *__restrict__ hn, int d, int n_exp,
-                                                           int batch, float *__restrict__ logits) {
+                                                           int batch, float *__restrict__ logits,
+                                                           int *__restrict__ zero, int nzero) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int e = blockIdx.x * nwarps + warp;
     constexpr int RV = 16;
@@ -172,6 +182,8 @@ __global__ void __launch_bounds__(64) router_logits_kernel(const float *__restri
         if (e < n_exp && i < nv) r[i] = __ldg(rw + lane + 32 * i);
     pdl_launch_dependents();
     pdl_wait();
+    if (zero && blockIdx.x == 0)
+        for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
     if (e >= n_exp) return;
     for (int b = 0; b < batch; ++b) {
         const float4 *x = reinterpret_cast<const float4 *>(hn + (long)b * d);
@@ -200,480 +212,233 @@ __global__ void __launch_bounds__(64) router_logits_kernel(const float *__restri
 }
 
 // Softmax over one token's logits, greedy top-k (strict >, lowest index wins)
-// and renormalisation, by a whole CTA: warp 0 forms the probabilities exactly
-// as router_topk_kernel does; every thread then ranks its experts (rank =
-// number of experts with a larger probability, or an equal one at a lower
-// index), which reproduces the greedy selection order.  Results in shared
-// memory: s_sel[a], s_w[a] for a < n_act.  All threads must call it.
-__device__ __forceinline__ void route_cta(const float *lg, int n_exp, int n_act, float *s_p, int *s_sel, float *s_w) {
+// and renormalisation, by a whole CTA (qwen_moe.c:296-301).  Warp 0 forms the
+// probabilities exactly as router_topk_kernel does; the rank of expert e is
+// the number of experts with a larger probability, or an equal one at a lower
+// index, which reproduces the greedy selection order.  Thread t ranks expert
+// t % n_exp against one half of the experts (read four at a time) and the two
+// halves are added.  Results in shared memory: s_sel[a], s_w[a] for a <
+// n_act.  s_p holds kMaxExp + 8 floats, s_rk 2 * kMaxExp ints; s_wr is
+// scratch of kMaxAct floats.  blockDim.x must be >= 64 and >= n_act.
+__device__ __forceinline__ void route_fast(const float *lg, int n_exp, int n_act, float *s_p, int *s_rk, int *s_sel,
+                                           float *s_w, float *s_wr) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int hl = ((n_exp + 7) / 8) * 4;   // experts per half, a multiple of 4
     if (warp == 0) {
         float p[kMaxExp / 32];
         float m = -1e30f;
 #pragma unroll
         for (int i = 0; i < kMaxExp / 32; ++i) {
             const int ee = lane + 32 * i;
-            p[i] = ee < n_exp ? __ldcg(lg + ee) : -1e30f;   // L2: written by an earlier grid
+            p[i] = ee < n_exp ? __ldcg(lg + ee) : -1e30f;
             m = fmaxf(m, p[i]);
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        float s = 0.f;
+        float sum = 0.f;
 #pragma unroll
         for (int i = 0; i < kMaxExp / 32; ++i) {
             const int ee = lane + 32 * i;
             p[i] = ee < n_exp ? expf(p[i] - m) : 0.f;
-            s += p[i];
+            sum += p[i];
         }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        const float inv = 1.0f / s;
+        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        const float inv = 1.0f / sum;
 #pragma unroll
         for (int i = 0; i < kMaxExp / 32; ++i) {
             const int ee = lane + 32 * i;
             if (ee < n_exp) s_p[ee] = p[i] * inv;
+            else if (ee < 2 * hl) s_p[ee] = -1.0f;   // padding never outranks a probability
         }
+        if (lane < 8 && kMaxExp + lane < 2 * hl) s_p[kMaxExp + lane] = -1.0f;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < 2 * n_exp; idx += blockDim.x) {
+        const int e = idx % n_exp, h = idx / n_exp;
+        const float pe = s_p[e];
+        const float4 *q = reinterpret_cast<const float4 *>(s_p + h * hl);
+        int rank = 0;
+#pragma unroll 4
+        for (int i = 0; i < hl / 4; ++i) {
+            const float4 v = q[i];
+            const int f = h * hl + 4 * i;
+            rank += (v.x > pe) || (v.x == pe && f < e);
+            rank += (v.y > pe) || (v.y == pe && f + 1 < e);
+            rank += (v.z > pe) || (v.z == pe && f + 2 < e);
+            rank += (v.w > pe) || (v.w == pe && f + 3 < e);
+        }
+        s_rk[h * kMaxExp + e] = rank;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < n_exp; e += blockDim.x) {
-        const float pe = s_p[e];
-        int rank = 0;
-        for (int f = 0; f < n_exp; ++f) {
-            const float pf = s_p[f];
-            rank += (pf > pe) || (pf == pe && f < e);
-        }
+        const int rank = s_rk[e] + s_rk[kMaxExp + e];
         if (rank < n_act) {
             s_sel[rank] = e;
-            s_w[rank] = pe;
+            s_wr[rank] = s_p[e];
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < n_act) {
         float ssum = 0.f;
-        for (int a = 0; a < n_act; ++a) ssum += s_w[a];
-        for (int a = 0; a < n_act; ++a) s_w[a] = s_w[a] / ssum;
+        for (int a = 0; a < n_act; ++a) ssum += s_wr[a];
+        s_w[threadIdx.x] = s_wr[threadIdx.x] / ssum;
     }
     __syncthreads();
 }
 
-// ---- gate / up + SwiGLU ------------------------------------------------------------------
-template <int QT>
-__global__ void __launch_bounds__(256) gate_up_kernel(QView G, QView U, int ffn, int d, int n_act, int lo, int hi,
-                                                      const float *__restrict__ hn, const int *__restrict__ sel,
-                                                      float *__restrict__ h) {
-    __shared__ XBlk xq[kMaxDXB];
-    __shared__ XF xf[kMaxDXB];
-    const int pair = blockIdx.y;                 // token * n_act + slot
-    const int tok = pair / n_act;
-    const int e = sel[pair];
-    if (e < lo || e >= hi) return;               // expert held by another process
-    xprep_all(hn + (long)tok * d, d, 1, xq, xf);
-    __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int i = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (i >= ffn) return;
-    const int row = (e - lo) * ffn + i;
-    const int units = units_per_row(QT, d);
-    float g = 0.f, u = 0.f;
-    for (int k = lane; k < units; k += 32) {
-        const WUnit<QT> wg = load_unit<QT>(G, row, k);
-        const WUnit<QT> wu = load_unit<QT>(U, row, k);
-        g += dot_unit<QT>(wg, xq, xf, k);
-        u += dot_unit<QT>(wu, xq, xf, k);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        g += __shfl_xor_sync(0xffffffffu, g, off);
-        u += __shfl_xor_sync(0xffffffffu, u, off);
-    }
-    if (lane == 0) h[(long)pair * ffn + i] = (g / (1.0f + expf(-g))) * u;   // silu(g) * u, qwen_moe.c:309
-}
+// ---- expert kernels ---------------------------------------------------------------------
+// Weights are in the slice layout of qformats.cuh: the rows of one expert are
+// contiguous, so a run of rows is one bulk copy into shared memory, and a
+// thread dots half a slice (half p of a staged run is half p % 2 of slice
+// p / 2, which is row (p/2) / ns, slice (p/2) % ns).  red[] holds the sums as
+// [matrix or slot][slice][half][row] with row stride R + 1, so both the
+// writes and the per-row sums avoid bank conflicts.
 
-// ---- down projection + weighted combine -------------------------------------------------------
-template <int QT>
-__global__ void __launch_bounds__(256) down_combine_kernel(QView D, int ffn, int d, int n_act, int lo, int hi,
-                                                           const float *__restrict__ h, const int *__restrict__ sel,
-                                                           const float *__restrict__ wsel, float *__restrict__ eout,
-                                                           int lpr) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    const int nxb = ffn / 32;
-    XBlk *xq = reinterpret_cast<XBlk *>(smem);
-    XF *xf = reinterpret_cast<XF *>(smem + sizeof(XBlk) * n_act * nxb);
-    const int tok = blockIdx.y;
-    // activation planes of every slot's h (slots of remote experts are unused)
-    xprep_all(h + (long)tok * n_act * ffn, ffn, n_act, xq, xf);
-    __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int n = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (n >= d) return;
-    const int groups = 32 / lpr, grp = lane / lpr, sig = lane % lpr;
-    const int units = units_per_row(QT, ffn);
-    float total = 0.f;
-    for (int a0 = 0; a0 < n_act; a0 += groups) {
-        const int a = a0 + grp;
-        float acc = 0.f;
-        int e = -1;
-        if (a < n_act) {
-            e = sel[tok * n_act + a];
-            if (e >= lo && e < hi) {
-                const int row = (e - lo) * d + n;
-                for (int k = sig; k < units; k += lpr) {
-                    const WUnit<QT> wd = load_unit<QT>(D, row, k);
-                    acc += dot_unit<QT>(wd, xq + a * nxb, xf + a * nxb, k);
-                }
-            }
-        }
-        for (int off = lpr >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-        // lane 0 folds the groups' results in slot order
-        for (int gi = 0; gi < groups; ++gi) {
-            const float v = __shfl_sync(0xffffffffu, acc, gi * lpr);
-            const int ag = a0 + gi;
-            if (lane == 0 && ag < n_act) {
-                const int eg = sel[tok * n_act + ag];
-                if (eg >= lo && eg < hi) total += wsel[tok * n_act + ag] * v;
-            }
-        }
-    }
-    if (lane == 0) eout[(long)tok * d + n] = total;
-}
+// silu(g) * u of one row (qwen_moe.c:309)
+__device__ __forceinline__ float swiglu(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
 
-// ---- slice versions (d a multiple of 256 up to 2048, ffn a multiple of 256 up to 4096) ----------
-// gate/up: CTA = 32 consecutive rows of one selected expert for one
-// (token, slot); warp w owns slice w of both the gate and the up row of its
-// lane; partial sums are added in slice order, then h = silu(g) * u.
+// Gate and up rows [0, rows) staged at tg / tu (each R rows of rb bytes) dotted
+// with token 0 of xb; thread t < rows gets h for row t (other threads 0).
 template <int QT>
-__global__ void __launch_bounds__(256) gate_up_slice_kernel(QView G, QView U, int ffn, int d, int n_act, int lo,
-                                                            int hi, const float *__restrict__ hn,
-                                                            const int *__restrict__ sel, float *__restrict__ h) {
-    __shared__ XBlk xq[kMaxDXB];
-    __shared__ XF xf[kMaxDXB];
-    __shared__ float red[2][8][32];
-    const int pair = blockIdx.y;
-    const int tok = pair / n_act;
-    pdl_wait();                                  // sel comes from the router kernel
-    pdl_launch_dependents();
-    const int e = sel[pair];
-    if (e < lo || e >= hi) return;
-    const int lane = threadIdx.x & 31, sl = threadIdx.x >> 5, ns = d / 256;
-    const int i = blockIdx.x * 32 + lane;
-    const int row = (e - lo) * ffn + i;
-    WSlice<QT> wg, wu;
-    if (i < ffn) {
-        load_slice<QT>(G, row, sl, wg);
-        load_slice<QT>(U, row, sl, wu);
-    }
-    xprep_all(hn + (long)tok * d, d, 1, xq, xf);
-    __syncthreads();
-    float g = 0.f, u = 0.f;
-    if (i < ffn) {
-        g = dot_slice<QT>(wg, xq + sl * 8, xf + sl * 8);
-        u = dot_slice<QT>(wu, xq + sl * 8, xf + sl * 8);
-    }
-    red[0][sl][lane] = g;
-    red[1][sl][lane] = u;
-    __syncthreads();
-    if (threadIdx.x < 32 && i < ffn) {
-        float gs = 0.f, us = 0.f;
-        for (int k = 0; k < ns; ++k) {
-            gs += red[0][k][lane];
-            us += red[1][k][lane];
-        }
-        h[(long)pair * ffn + i] = (gs / (1.0f + expf(-gs))) * us;   // silu(g) * u, qwen_moe.c:309
-    }
-}
-
-// down + combine: CTA = 32 consecutive output rows n of one token; warp w
-// owns (slot w / ns, slice w % ns), looping over slots when there are more
-// than fit in 32 warps; the weighted sum over slots runs in slot order.
-template <int QT>
-__global__ void __launch_bounds__(1024) down_slice_kernel(QView D, int ffn, int d, int n_act, int lo, int hi,
-                                                          const float *__restrict__ h, const int *__restrict__ sel,
-                                                          const float *__restrict__ wsel, float *__restrict__ eout) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    const int nxb = ffn / 32, ns = ffn / 256;
-    XBlk *xq = reinterpret_cast<XBlk *>(smem);
-    XF *xf = reinterpret_cast<XF *>(smem + sizeof(XBlk) * n_act * nxb);
-    float *red = reinterpret_cast<float *>(xf + n_act * nxb);      // [slot][slice][lane]
-    const int tok = blockIdx.y;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const int n = blockIdx.x * 32 + lane;
-    const int slots_per_pass = nwarps / ns;
-    // The routing was finished by the kernel before the previous one (the
-    // gate/up kernel lets this grid launch only after it has waited for the
-    // router), so the first pass's weights are loaded before waiting for h.
-    const int sl = warp % ns;
-    const bool active = warp < slots_per_pass * ns;
-    WSlice<QT> w0;
-    bool have0 = false;
-    {
-        const int a = warp / ns;
-        if (active && a < n_act) {
-            const int e = sel[tok * n_act + a];
-            if (e >= lo && e < hi && n < d) {
-                load_slice<QT>(D, (e - lo) * d + n, sl, w0);
-                have0 = true;
-            }
-        }
-    }
-    pdl_launch_dependents();
-    pdl_wait();                                  // h comes from the gate/up kernel
-    xprep_all(h + (long)tok * n_act * ffn, ffn, n_act, xq, xf);
-    __syncthreads();
-    for (int a0 = 0; a0 < n_act; a0 += slots_per_pass) {
-        const int a = a0 + warp / ns;
-        if (active && a < n_act) {
-            float v = 0.f;
-            if (a0 == 0) {
-                if (have0) v = dot_slice<QT>(w0, xq + a * nxb + sl * 8, xf + a * nxb + sl * 8);
-            } else {
-                const int e = sel[tok * n_act + a];
-                if (e >= lo && e < hi && n < d) {
-                    WSlice<QT> w;
-                    load_slice<QT>(D, (e - lo) * d + n, sl, w);
-                    v = dot_slice<QT>(w, xq + a * nxb + sl * 8, xf + a * nxb + sl * 8);
-                }
-            }
-            red[(a * ns + sl) * 32 + lane] = v;
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x < 32 && n < d) {
-        float total = 0.f;
-        for (int a = 0; a < n_act; ++a) {
-            const int e = sel[tok * n_act + a];
-            if (e < lo || e >= hi) continue;
-            float v = 0.f;
-            for (int k = 0; k < ns; ++k) v += red[(a * ns + k) * 32 + lane];
-            total += wsel[tok * n_act + a] * v;
-        }
-        eout[(long)tok * d + n] = total;
-    }
-}
-
-// ---- bulk-copy versions --------------------------------------------------------------------
-// gate/up: CTA = 32 consecutive rows (lane = row) of the gate and the up
-// matrix of one selected expert for one (token, slot); warp 0 stages both
-// 32-row tiles in shared memory with per-row bulk copies while the CTA
-// prepares the activation planes; warp w dots slices w, w+nw, ...
-template <int QT>
-__global__ void __launch_bounds__(256, 2) gate_up_bulk_kernel(QView G, QView U, int ffn, int d, int n_exp, int n_act,
-                                                           int lo, int hi, const float *__restrict__ hn,
-                                                           const float *__restrict__ logits, int *__restrict__ sel_out,
-                                                           float *__restrict__ w_out, float *__restrict__ h,
-                                                           int *status) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ float red[2][8][32];
-    __shared__ float s_p[kMaxExp];
-    __shared__ int s_sel[kMaxAct];
-    __shared__ float s_w[kMaxAct];
-    const int pair = blockIdx.y;
-    const int tok = pair / n_act, slot = pair % n_act;
-    pdl_wait();                                  // logits come from the router kernel
-    pdl_launch_dependents();
-    route_cta(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_sel, s_w);
-    if (blockIdx.x == 0 && slot == 0 && threadIdx.x < n_act) {   // routing result for the API
-        sel_out[tok * n_act + threadIdx.x] = s_sel[threadIdx.x];
-        w_out[tok * n_act + threadIdx.x] = s_w[threadIdx.x];
-    }
-    const int e = s_sel[slot];
-    if (e < lo || e >= hi) return;               // expert held by another process
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, ns = d / 256;
-    const int i0 = blockIdx.x * 32;
-    const int rows = min(32, ffn - i0);
-    const int tb = tile_bytes(QT, d, 32);
-    uint8_t *tg = smem, *tu = smem + tb;
-    XBlk *xq = reinterpret_cast<XBlk *>(smem + 2 * tb);
-    XF *xf = reinterpret_cast<XF *>(xq + d / 32);
-    tile_cp_async(G, (long)(e - lo) * ffn + i0, rows, tg, 32);
-    tile_cp_async(U, (long)(e - lo) * ffn + i0, rows, tu, 32);
-    cp_async_commit();
-    xprep_all(hn + (long)tok * d, d, 1, xq, xf);
-    cp_async_wait_all();
-    __syncthreads();
-    const bool ok = true;
-    float g = 0.f, u = 0.f;
-    if (ok && lane < rows) {
-        const QView TG = tile_view(QT, d, tg, 32), TU = tile_view(QT, d, tu, 32);
-        for (int sl = warp; sl < ns; sl += nw) {
-            WSlice<QT> w;
-            load_slice<QT, false>(TG, lane, sl, w);
-            g += dot_slice<QT>(w, xq + sl * 8, xf + sl * 8);
-            load_slice<QT, false>(TU, lane, sl, w);
-            u += dot_slice<QT>(w, xq + sl * 8, xf + sl * 8);
-        }
-    }
-    red[0][warp][lane] = g;
-    red[1][warp][lane] = u;
-    __syncthreads();
-    if (threadIdx.x < 32 && lane < rows) {
-        float gs = 0.f, us = 0.f;
-        for (int k = 0; k < nw; ++k) {
-            gs += red[0][k][lane];
-            us += red[1][k][lane];
-        }
-        h[(long)pair * ffn + i0 + lane] = (gs / (1.0f + expf(-gs))) * us;   // silu(g) * u, qwen_moe.c:309
-    }
-}
-
-// down + combine: CTA = 32 consecutive output rows n of one token; warp 0
-// stages the 32 rows of the down matrix of every locally held selected expert
-// (per-row bulk copies, issued before waiting for h); warp w handles
-// (slot w / ns, slice w % ns) pairs; the weighted sum runs in slot order.
-template <int QT>
-__global__ void __launch_bounds__(1024) down_bulk_kernel(QView D, int ffn, int d, int n_exp, int n_act, int lo,
-                                                         int hi, const float *__restrict__ h,
-                                                         const float *__restrict__ logits, float *__restrict__ eout,
-                                                         int *status) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ int s_sel[kMaxAct];
-    __shared__ float s_w[kMaxAct];
-    __shared__ float s_p[kMaxExp];
-    const int nxb = ffn / 32, ns = ffn / 256;
-    const int tok = blockIdx.y;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const int n0 = blockIdx.x * 32;
-    const int rows = min(32, d - n0);
-    const int tb = tile_bytes(QT, ffn, 32);
-    XBlk *xq = reinterpret_cast<XBlk *>(smem + n_act * tb);
-    XF *xf = reinterpret_cast<XF *>(xq + n_act * nxb);
-    float *red = reinterpret_cast<float *>(xf + n_act * nxb);   // [slot][slice][lane]
-    // The router kernel finished before the gate/up kernel let this grid
-    // launch, so the logits may be read before waiting for h.
-    route_cta(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_sel, s_w);
-    for (int a = 0; a < n_act; ++a) {
-        const int e = s_sel[a];
-        if (e >= lo && e < hi) tile_cp_async(D, (long)(e - lo) * d + n0, rows, smem + a * tb, 32);
-    }
-    cp_async_commit();
-    pdl_launch_dependents();
-    pdl_wait();                                  // h comes from the gate/up kernel
-    xprep_all(h + (long)tok * n_act * ffn, ffn, n_act, xq, xf);
-    cp_async_wait_all();
-    __syncthreads();
-    const bool ok = true;
-    for (int p = warp; p < n_act * ns; p += nwarps) {
-        const int a = p / ns, sl = p % ns;
-        const int e = s_sel[a];
+__device__ __forceinline__ float gate_up_rows(const uint8_t *tg, const uint8_t *tu, int rows, int R, int ns,
+                                              const XBuf &xb, float *red, bool ok) {
+    constexpr int SB = slice_bytes(QT);
+    const int per = rows * ns * 2;   // halves per matrix
+    for (int p = threadIdx.x; p < 2 * per; p += blockDim.x) {
+        const int mat = p >= per, q = p - mat * per;
+        const int sp = q >> 1, hf = q & 1;
+        const int r = sp / ns, sl = sp - r * ns;
         float v = 0.f;
-        if (ok && e >= lo && e < hi && lane < rows) {
-            const QView T = tile_view(QT, ffn, smem + a * tb, 32);
-            WSlice<QT> w;
-            load_slice<QT, false>(T, lane, sl, w);
-            v = dot_slice<QT>(w, xq + a * nxb + sl * 8, xf + a * nxb + sl * 8);
+        if (ok) {
+            WHalf<QT> w;
+            load_half<QT>((mat ? tu : tg) + (long)sp * SB, hf, w);
+            v = dot_half<QT>(w, hf, xb.half(0, sl, hf));
         }
-        red[p * 32 + lane] = v;
+        red[((mat * ns + sl) * 2 + hf) * (R + 1) + r] = v;
     }
     __syncthreads();
-    if (threadIdx.x < 32 && lane < rows) {
-        float total = 0.f;
-        for (int a = 0; a < n_act; ++a) {
-            const int e = s_sel[a];
-            if (e < lo || e >= hi) continue;
-            float v = 0.f;
-            for (int k = 0; k < ns; ++k) v += red[(a * ns + k) * 32 + lane];
-            total += s_w[a] * v;
+    float h = 0.f;
+    if (threadIdx.x < rows) {
+        float g = 0.f, u = 0.f;
+        for (int sl = 0; sl < ns; ++sl) {
+            g += red[(sl * 2) * (R + 1) + threadIdx.x] + red[(sl * 2 + 1) * (R + 1) + threadIdx.x];
+            u += red[((ns + sl) * 2) * (R + 1) + threadIdx.x] + red[((ns + sl) * 2 + 1) * (R + 1) + threadIdx.x];
         }
-        eout[(long)tok * d + n0 + lane] = total;
+        h = swiglu(g, u);
     }
+    return h;
 }
 
-// ---- TMA-staged versions ---------------------------------------------------------------------
-// Same work split as the bulk kernels; the 32-row tiles arrive as 2-D TMA
-// boxes (32 rows x 128 bytes, 128-byte swizzle) issued by one thread.
+// Down rows [0, rows) of nl local experts staged at dt + li * R * rb, dotted
+// with token li of xb (h of that expert's slot); thread t < rows gets the
+// weighted sum over li in order (slot order), weight s_w[s_loc[li]].
 template <int QT>
-__global__ void __launch_bounds__(256, 2) gate_up_tma_kernel(
-    const __grid_constant__ CUtensorMap tgw, const __grid_constant__ CUtensorMap tgd,
-    const __grid_constant__ CUtensorMap tuw, const __grid_constant__ CUtensorMap tud, int ffn, int d, int n_exp,
-    int n_act, int lo, int hi, const float *__restrict__ hn, const float *__restrict__ logits,
-    int *__restrict__ sel_out, float *__restrict__ w_out, float *__restrict__ h, int *status) {
-    extern __shared__ __align__(1024) uint8_t smem[];
+__device__ __forceinline__ float down_rows(const uint8_t *dt, int nl, int rows, int R, int ns, long rb, const XBuf &xb,
+                                           float *red, bool ok, const int *s_loc, const float *s_w) {
+    constexpr int SB = slice_bytes(QT);
+    const int per = rows * ns * 2;   // halves per expert
+    for (int p = threadIdx.x; p < nl * per; p += blockDim.x) {
+        const int li = p / per, q = p - li * per;
+        const int sp = q >> 1, hf = q & 1;
+        const int r = sp / ns, sl = sp - r * ns;
+        float v = 0.f;
+        if (ok) {
+            WHalf<QT> w;
+            load_half<QT>(dt + li * R * rb + (long)sp * SB, hf, w);
+            v = dot_half<QT>(w, hf, xb.half(li, sl, hf));
+        }
+        red[((li * ns + sl) * 2 + hf) * (R + 1) + r] = v;
+    }
+    __syncthreads();
+    float tot = 0.f;
+    if (threadIdx.x < rows) {
+        for (int li = 0; li < nl; ++li) {
+            float y = 0.f;
+            for (int sl = 0; sl < ns; ++sl)
+                y += red[((li * ns + sl) * 2) * (R + 1) + threadIdx.x] + red[((li * ns + sl) * 2 + 1) * (R + 1) + threadIdx.x];
+            tot += s_w[s_loc[li]] * y;   // eout += w_a * y_a in slot order (qwen_moe.c:310)
+        }
+    }
+    return tot;
+}
+
+// ---- batched path: gate/up kernel + down kernel ------------------------------------------
+// gate_up: grid (row tiles of TRg rows, token x slot).  Each CTA routes its
+// token, stages TRg gate rows and TRg up rows of the selected expert (two bulk
+// copies) and writes h[token][slot][rows] = silu(g) * u.
+constexpr int kMoeThreads = 512;
+
+template <int QT>
+__global__ void __launch_bounds__(kMoeThreads, 1)
+    gate_up_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
+                   int n_act, int lo, int hi, int TRg, const float *__restrict__ hn, const float *__restrict__ logits,
+                   int *__restrict__ sel_out, float *__restrict__ w_out, float *__restrict__ h, int *status) {
+    extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bar;
     __shared__ int abort_flag;
-    __shared__ float red[2][8][32];
-    __shared__ float s_p[kMaxExp];
+    __shared__ __align__(16) float s_p[kMaxExp + 8];
+    __shared__ int s_rk[2 * kMaxExp];
     __shared__ int s_sel[kMaxAct];
-    __shared__ float s_w[kMaxAct];
-    const int pair = blockIdx.y;
-    const int tok = pair / n_act, slot = pair % n_act;
-    pdl_wait();                                  // logits come from the router kernel
-    pdl_launch_dependents();
-    route_cta(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_sel, s_w);
-    if (blockIdx.x == 0 && slot == 0 && threadIdx.x < n_act) {   // routing result for the API
-        sel_out[tok * n_act + threadIdx.x] = s_sel[threadIdx.x];
-        w_out[tok * n_act + threadIdx.x] = s_w[threadIdx.x];
-    }
-    const int e = s_sel[slot];
-    if (e < lo || e >= hi) return;               // expert held by another process
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, ns = d / 256;
-    const int i0 = blockIdx.x * 32;
-    const int rows = min(32, ffn - i0);
-    const int tb = tma_tile_bytes(QT, d);
-    uint8_t *tg = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
-    uint8_t *tu = tg + tb;
-    XBlk *xq = reinterpret_cast<XBlk *>(tu + tb);
-    XF *xf = reinterpret_cast<XF *>(xq + d / 32);
+    __shared__ float s_w[kMaxAct], s_wr[kMaxAct];
+    const int tok = blockIdx.y / n_act, slot = blockIdx.y % n_act;
+    const int ns = slices_per_row(d);
+    const long rb = row_bytes_dev(QT, d);
+    const int i0 = blockIdx.x * TRg, rows = min(TRg, ffn - i0);
+    uint8_t *tg = smem, *tu = smem + TRg * rb;
+    const XBuf xb = xbuf_at(smem + 2 * TRg * rb, ns);
+    float *red = reinterpret_cast<float *>(smem + 2 * TRg * rb + xbuf_bytes(ns, 1));
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         abort_flag = 0;
         fence_barrier_init();
-        mbar_arrive_expect_tx(&bar, 2u * (uint32_t)tb);
-        const int row0 = (e - lo) * ffn + i0;
-        tma_issue_tile(&tgw, &tgd, QT, d, row0, tg, &bar);
-        tma_issue_tile(&tuw, &tud, QT, d, row0, tu, &bar);
     }
-    xprep_all(hn + (long)tok * d, d, 1, xq, xf);
+    pdl_wait();                                  // logits come from the router kernel
+    pdl_launch_dependents();
+    route_fast(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_rk, s_sel, s_w, s_wr);
+    if (blockIdx.x == 0 && slot == 0 && threadIdx.x < n_act) {   // routing result for the API
+        sel_out[tok * n_act + threadIdx.x] = s_sel[threadIdx.x];
+        w_out[tok * n_act + threadIdx.x] = s_w[threadIdx.x];
+    }
+    const int e = s_sel[slot];
+    if (e < lo || e >= hi) return;               // expert held by another process
+    if (threadIdx.x == 0) {
+        const long r0 = (long)(e - lo) * ffn + i0;
+        mbar_arrive_expect_tx(&bar, (uint32_t)(2 * rows * rb));
+        stage_bytes(tg, gw + r0 * rb, (uint32_t)(rows * rb), &bar);
+        stage_bytes(tu, uw + r0 * rb, (uint32_t)(rows * rb), &bar);
+    }
+    xprep_rows([hn, tok, d](int) { return hn + (long)tok * d; }, d, 1, xb);
     __syncthreads();
     const bool ok = mbar_wait(&bar, 0, &abort_flag, status);
-    float g = 0.f, u = 0.f;
-    if (ok && lane < rows) {
-        const int nwb = tma_wboxes(QT, d);
-        for (int sl = warp; sl < ns; sl += nw) {
-            WSlice<QT> w;
-            load_slice_swz<QT>(tg, nwb, lane, sl, w);
-            g += dot_slice<QT>(w, xq + sl * 8, xf + sl * 8);
-            load_slice_swz<QT>(tu, nwb, lane, sl, w);
-            u += dot_slice<QT>(w, xq + sl * 8, xf + sl * 8);
-        }
-    }
-    red[0][warp][lane] = g;
-    red[1][warp][lane] = u;
-    __syncthreads();
-    if (abort_flag) {
-        if (threadIdx.x == 0) mbar_wait_drain(&bar, 0, 100000000ull);
-        return;
-    }
-    if (threadIdx.x < 32 && lane < rows) {
-        float gs = 0.f, us = 0.f;
-        for (int k = 0; k < nw; ++k) {
-            gs += red[0][k][lane];
-            us += red[1][k][lane];
-        }
-        h[(long)pair * ffn + i0 + lane] = (gs / (1.0f + expf(-gs))) * us;   // silu(g) * u, qwen_moe.c:309
-    }
+    const float hv = gate_up_rows<QT>(tg, tu, rows, TRg, ns, xb, red, ok);
+    if (threadIdx.x < rows) h[((long)tok * n_act + slot) * ffn + i0 + threadIdx.x] = hv;
+    if (threadIdx.x == 0 && abort_flag) mbar_wait_drain(&bar, 0, 100000000ull);
 }
 
+// down: grid (row tiles of TRd rows, token).  Each CTA routes its token,
+// stages TRd down rows of every local selected expert (one bulk copy each,
+// issued before waiting for h) and writes eout[token][rows] summed over the
+// slots in order.
 template <int QT>
-__global__ void __launch_bounds__(1024) down_tma_kernel(const __grid_constant__ CUtensorMap tdw,
-                                                        const __grid_constant__ CUtensorMap tdd, int ffn, int d,
-                                                        int n_exp, int n_act, int lo, int hi,
-                                                        const float *__restrict__ h, const float *__restrict__ logits,
-                                                        float *__restrict__ eout, int *status) {
-    extern __shared__ __align__(1024) uint8_t smem[];
+__global__ void __launch_bounds__(kMoeThreads, 1)
+    down_kernel(const uint8_t *__restrict__ dw, int ffn, int d, int n_exp, int n_act, int lo, int hi, int TRd,
+                const float *__restrict__ h, const float *__restrict__ logits, float *__restrict__ eout, int *status) {
+    extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bar;
     __shared__ int abort_flag;
-    __shared__ int s_sel[kMaxAct];
-    __shared__ float s_w[kMaxAct];
-    __shared__ float s_p[kMaxExp];
-    const int nxb = ffn / 32, ns = ffn / 256;
+    __shared__ __align__(16) float s_p[kMaxExp + 8];
+    __shared__ int s_rk[2 * kMaxExp];
+    __shared__ int s_sel[kMaxAct], s_loc[kMaxAct];
+    __shared__ float s_w[kMaxAct], s_wr[kMaxAct];
+    __shared__ int s_nl;
     const int tok = blockIdx.y;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const int n0 = blockIdx.x * 32;
-    const int rows = min(32, d - n0);
-    const int tb = tma_tile_bytes(QT, ffn);
-    uint8_t *tiles = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
-    XBlk *xq = reinterpret_cast<XBlk *>(tiles + n_act * tb);
-    XF *xf = reinterpret_cast<XF *>(xq + n_act * nxb);
-    float *red = reinterpret_cast<float *>(xf + n_act * nxb);   // [slot][slice][lane]
+    const int ns = slices_per_row(ffn);
+    const long rb = row_bytes_dev(QT, ffn);
+    const int n0 = blockIdx.x * TRd, rows = min(TRd, d - n0);
+    uint8_t *dt = smem;
+    const XBuf xb = xbuf_at(smem + n_act * TRd * rb, ns);
+    float *red = reinterpret_cast<float *>(smem + n_act * TRd * rb + xbuf_bytes(ns, n_act));
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         abort_flag = 0;
@@ -681,157 +446,300 @@ __global__ void __launch_bounds__(1024) down_tma_kernel(const __grid_constant__ 
     }
     // The router kernel finished before the gate/up kernel let this grid
     // launch, so the logits may be read before waiting for h.
-    route_cta(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_sel, s_w);
+    route_fast(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_rk, s_sel, s_w, s_wr);
     if (threadIdx.x == 0) {
-        int nloc = 0;
-        for (int a = 0; a < n_act; ++a) nloc += (s_sel[a] >= lo && s_sel[a] < hi);
-        mbar_arrive_expect_tx(&bar, (uint32_t)(nloc * tb));
-        for (int a = 0; a < n_act; ++a) {
-            const int e = s_sel[a];
-            if (e >= lo && e < hi) tma_issue_tile(&tdw, &tdd, QT, ffn, (e - lo) * d + n0, tiles + a * tb, &bar);
-        }
+        int nl = 0;
+        for (int a = 0; a < n_act; ++a)
+            if (s_sel[a] >= lo && s_sel[a] < hi) s_loc[nl++] = a;
+        s_nl = nl;
+        mbar_arrive_expect_tx(&bar, (uint32_t)(nl * rows * rb));
+        for (int li = 0; li < nl; ++li)
+            stage_bytes(dt + li * TRd * rb, dw + ((long)(s_sel[s_loc[li]] - lo) * d + n0) * rb,
+                        (uint32_t)(rows * rb), &bar);
     }
     pdl_launch_dependents();
     pdl_wait();                                  // h comes from the gate/up kernel
-    xprep_all(h + (long)tok * n_act * ffn, ffn, n_act, xq, xf);
     __syncthreads();
-    const bool ok = mbar_wait(&bar, 0, &abort_flag, status);
-    const int nwb = tma_wboxes(QT, ffn);
-    for (int p = warp; p < n_act * ns; p += nwarps) {
-        const int a = p / ns, sl = p % ns;
-        const int e = s_sel[a];
-        float v = 0.f;
-        if (ok && e >= lo && e < hi && lane < rows) {
-            WSlice<QT> w;
-            load_slice_swz<QT>(tiles + a * tb, nwb, lane, sl, w);
-            v = dot_slice<QT>(w, xq + a * nxb + sl * 8, xf + a * nxb + sl * 8);
-        }
-        red[p * 32 + lane] = v;
+    const int nl = s_nl;
+    const int *loc = s_loc;
+    xprep_rows([h, tok, n_act, ffn, loc](int li) { return h + ((long)tok * n_act + loc[li]) * ffn; }, ffn, nl, xb);
+    __syncthreads();
+    const bool ok = nl > 0 && mbar_wait(&bar, 0, &abort_flag, status);
+    const float v = down_rows<QT>(dt, nl, rows, TRd, ns, rb, xb, red, ok, s_loc, s_w);
+    if (threadIdx.x < rows) eout[(long)tok * d + n0 + threadIdx.x] = v;
+    if (threadIdx.x == 0 && abort_flag) mbar_wait_drain(&bar, 0, 100000000ull);
+}
+
+// ---- fused expert kernel (one token) ----------------------------------------------------
+// One CTA per SM.  After routing (route_fast on the router kernel's logits)
+// every CTA stages, at once, all the weight rows it owns: gate/up items (kFR
+// rows of one local expert's gate and up matrices) and down units (kFR output
+// rows: those rows of every local expert's down matrix).  A gate/up item
+// writes h = silu(g) * u for its rows and counts itself on a global counter;
+// a CTA's down units start once the counter shows every item of the token
+// done, and sum their experts in slot order, so the result does not depend on
+// timing.  The grid is the SM count with one CTA per SM, so every CTA is
+// resident while others wait for it; the waits are bounded.
+constexpr int kFusedMaxItems = 12;
+constexpr int kFR = 16;   // rows per item / unit
+
+struct FusedArgs {
+    const uint8_t *gw, *uw, *dw;
+    int ffn, d, n_exp, n_act, lo, hi;
+    int tile_region;   // bytes of shared memory for staged rows
+    const float *hn, *logits;
+    float *h;
+    int *cnt;
+    int *sel_out;
+    float *w_out;
+    float *eout;
+    int *status;
+};
+
+// Work split of the fused kernel, shared by the host planner and the kernel:
+// down unit u goes to CTA u % G; the CTAs left with one unit fewer first take
+// up to kfill gate/up items each, and the remaining items go round-robin over
+// all CTAs.
+struct FusedSplit {
+    int dn_n, rA, fill, gu_a, gu_b;
+    __host__ __device__ FusedSplit(int c, int G, int n_gu, int n_dn, int kfill) {
+        dn_n = n_dn > c ? (n_dn - c + G - 1) / G : 0;
+        rA = n_dn % G;
+        fill = 0;
+        if (rA > 0) fill = n_gu < (G - rA) * kfill ? n_gu : (G - rA) * kfill;
+        gu_a = (rA > 0 && c >= rA && fill > c - rA) ? (fill - (c - rA) + (G - rA) - 1) / (G - rA) : 0;
+        const int rest = n_gu - fill;
+        gu_b = rest > c ? (rest - c + G - 1) / G : 0;
+    }
+    __host__ __device__ int gu_n() const { return gu_a + gu_b; }
+    __host__ __device__ int gu_item(int c, int G, int k) const {
+        return k < gu_a ? (c - rA) + k * (G - rA) : fill + c + (k - gu_a) * G;
+    }
+    __host__ __device__ int dn_unit(int c, int G, int k) const { return c + k * G; }
+};
+// gate/up items that balance one CTA's down unit (bytes, rounded)
+__host__ __device__ inline int fused_kfill(int nl, int unit_tile_bytes, int item_bytes) {
+    return (nl * unit_tile_bytes + item_bytes / 2) / item_bytes;
+}
+
+template <int QT>
+__global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ uint64_t bars[kFusedMaxItems];
+    __shared__ int abort_flag;
+    __shared__ __align__(16) float s_p[kMaxExp + 8];
+    __shared__ int s_rk[2 * kMaxExp];
+    __shared__ int s_sel[kMaxAct], s_loc[kMaxAct];
+    __shared__ float s_w[kMaxAct], s_wr[kMaxAct];
+    __shared__ int s_nl;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int ffn = a.ffn, d = a.d;
+    const int nsg = slices_per_row(d), nsd = slices_per_row(ffn);
+    const long rbg = row_bytes_dev(QT, d), rbd = row_bytes_dev(QT, ffn);
+    const int tbg = kFR * (int)rbg, tbd = kFR * (int)rbd;
+    const int tpg = ffn / kFR;   // gate/up items per expert
+    uint8_t *tiles = smem;
+    uint8_t *xbase = smem + a.tile_region;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kFusedMaxItems; ++i) mbar_init(&bars[i], 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    pdl_launch_dependents();
+    pdl_wait();                                  // logits and the cleared counter come from the router kernel
+    route_fast(a.logits, a.n_exp, a.n_act, s_p, s_rk, s_sel, s_w, s_wr);
+    if (threadIdx.x == 0) {
+        int nl = 0;
+        for (int s2 = 0; s2 < a.n_act; ++s2)
+            if (s_sel[s2] >= a.lo && s_sel[s2] < a.hi) s_loc[nl++] = s2;
+        s_nl = nl;
+    }
+    if (c == 0 && threadIdx.x < a.n_act) {
+        a.sel_out[threadIdx.x] = s_sel[threadIdx.x];
+        a.w_out[threadIdx.x] = s_w[threadIdx.x];
     }
     __syncthreads();
-    if (abort_flag) {
-        if (threadIdx.x == 0) mbar_wait_drain(&bar, 0, 100000000ull);
-        return;
-    }
-    if (threadIdx.x < 32 && lane < rows) {
-        float total = 0.f;
-        for (int a = 0; a < n_act; ++a) {
-            const int e = s_sel[a];
-            if (e < lo || e >= hi) continue;
-            float v = 0.f;
-            for (int k = 0; k < ns; ++k) v += red[(a * ns + k) * 32 + lane];
-            total += s_w[a] * v;
+    const int nl = s_nl;
+    const int n_gu = nl * tpg, n_dn = (d + kFR - 1) / kFR;
+    const FusedSplit sp(c, G, n_gu, n_dn, fused_kfill(nl, tbd, 2 * tbg));
+    const int gu_n = sp.gu_n();
+    const int dn_n = nl > 0 ? sp.dn_n : 0;       // units with no local expert load nothing
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < gu_n; ++k) {
+            const int i = sp.gu_item(c, G, k);
+            const long r0 = (long)(s_sel[s_loc[i / tpg]] - a.lo) * ffn + (i % tpg) * kFR;
+            uint8_t *t = tiles + k * 2 * tbg;
+            mbar_arrive_expect_tx(&bars[k], 2u * (uint32_t)tbg);
+            stage_bytes(t, a.gw + r0 * rbg, (uint32_t)tbg, &bars[k]);
+            stage_bytes(t + tbg, a.uw + r0 * rbg, (uint32_t)tbg, &bars[k]);
         }
-        eout[(long)tok * d + n0 + lane] = total;
+        for (int k = 0; k < dn_n; ++k) {
+            const int u = sp.dn_unit(c, G, k);
+            const int rows = min(kFR, d - u * kFR);
+            uint8_t *t = tiles + gu_n * 2 * tbg + k * nl * tbd;
+            mbar_arrive_expect_tx(&bars[gu_n + k], (uint32_t)(nl * rows * rbd));
+            for (int li = 0; li < nl; ++li)
+                stage_bytes(t + li * tbd, a.dw + ((long)(s_sel[s_loc[li]] - a.lo) * d + u * kFR) * rbd,
+                            (uint32_t)(rows * rbd), &bars[gu_n + k]);
+        }
     }
+    // gate / up items: h[li][rows] = silu(gate . hn) * (up . hn)
+    if (gu_n > 0) {
+        const float *hn = a.hn;
+        xprep_rows([hn](int) { return hn; }, d, 1, xbuf_at(xbase, nsg));
+        __syncthreads();
+    }
+    const XBuf xh = xbuf_at(xbase, nsg);
+    float *red_g = reinterpret_cast<float *>(xbase + xbuf_bytes(nsg, 1));
+    for (int k = 0; k < gu_n; ++k) {
+        const bool ok = mbar_wait(&bars[k], 0, &abort_flag, a.status);
+        const uint8_t *t = tiles + k * 2 * tbg;
+        const float hv = gate_up_rows<QT>(t, t + tbg, kFR, kFR, nsg, xh, red_g, ok);
+        if (threadIdx.x < kFR) {
+            const int i = sp.gu_item(c, G, k);
+            a.h[(i / tpg) * ffn + (i % tpg) * kFR + threadIdx.x] = hv;
+            __threadfence();
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            atomicAdd(a.cnt, 1);
+        }
+    }
+    // down units: eout[rows] = sum over local slots (slot order) of w * (down . h)
+    if (sp.dn_n > 0) {
+        const XBuf xd = xbuf_at(xbase, nsd);
+        float *red_d = reinterpret_cast<float *>(xbase + xbuf_bytes(nsd, a.n_act));
+        if (nl > 0) {
+            if (threadIdx.x == 0) spin_until_geq(a.cnt, n_gu, &abort_flag, a.status);
+            __syncthreads();
+            const float *hs = a.h;
+            xprep_rows([hs, ffn](int li) { return hs + (long)li * ffn; }, ffn, nl, xd);
+            __syncthreads();
+        }
+        for (int k = 0; k < sp.dn_n; ++k) {
+            const int u = sp.dn_unit(c, G, k);
+            const int rows = min(kFR, d - u * kFR);
+            const bool ok = nl > 0 && mbar_wait(&bars[gu_n + k], 0, &abort_flag, a.status);
+            const float v = down_rows<QT>(tiles + gu_n * 2 * tbg + k * nl * tbd, nl, rows, kFR, nsd, rbd, xd, red_d,
+                                          ok, s_loc, s_w);
+            if (threadIdx.x < rows) a.eout[u * kFR + threadIdx.x] = v;
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x == 0 && abort_flag)          // copies still in flight after a timeout
+        for (int k = 0; k < gu_n + dn_n; ++k) mbar_wait_drain(&bars[k], 0, 100000000ull);
 }
 
 }  // namespace q
 
 using namespace q;
 
+// Rows per CTA of the batched kernels: about one slice per thread, with the
+// staged rows held to a size that lets two CTAs share an SM.
+static int gate_up_rows_per_cta(int qt, int d) {
+    const int ns = slices_per_row(d);
+    const long rb = row_bytes_dev(qt, d);
+    return (int)std::max<long>(1, std::min<long>(kMoeThreads / (4 * ns), 36864 / rb));
+}
+static int down_rows_per_cta(int qt, int ffn, int n_act) {
+    const int ns = slices_per_row(ffn);
+    const long rb = row_bytes_dev(qt, ffn);
+    return (int)std::max<long>(1, std::min<long>(kMoeThreads / std::max(1, 2 * n_act * ns), 65536 / (n_act * rb)));
+}
+static size_t gate_up_smem(int qt, int d, int TR) {
+    const int ns = slices_per_row(d);
+    return 2 * (size_t)TR * row_bytes_dev(qt, d) + xbuf_bytes(ns, 1) + (size_t)2 * ns * 2 * (TR + 1) * 4;
+}
+static size_t down_smem(int qt, int ffn, int n_act, int TR) {
+    const int ns = slices_per_row(ffn);
+    return (size_t)n_act * TR * row_bytes_dev(qt, ffn) + xbuf_bytes(ns, n_act) + (size_t)n_act * ns * 2 * (TR + 1) * 4;
+}
+
 bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype) {
     const int be = (int)qtype_block_elems(qtype);
-    return be && d > 0 && ffn > 0 && d % be == 0 && ffn % be == 0 && d % 32 == 0 && ffn % 32 == 0 &&
-           d / 32 <= kMaxDXB && n_exp > 0 && n_exp <= kMaxExp && n_act > 0 && n_act <= kMaxAct &&
-           n_act <= n_exp && (size_t)n_act * (ffn / 32) * (sizeof(XBlk) + sizeof(XF)) + (size_t)n_act * (ffn / 256 + 1) * 128 <= 200 * 1024;
+    if (!be || d <= 0 || ffn <= 0 || d % be || ffn % be || d % 32 || ffn % 32 || d / 32 > kMaxDXB || n_exp <= 0 ||
+        n_exp > kMaxExp || n_act <= 0 || n_act > kMaxAct || n_act > n_exp)
+        return false;
+    return gate_up_smem(qtype, d, gate_up_rows_per_cta(qtype, d)) <= 200 * 1024 &&
+           down_smem(qtype, ffn, n_act, down_rows_per_cta(qtype, ffn, n_act)) <= 200 * 1024;
+}
+
+static void fused_plan_impl(MoeLayer &L, int G) {
+    L.fused_ok = false;
+    if (G <= 0) return;
+    const int qt = L.qtype;
+    const int tbg = kFR * (int)row_bytes_dev(qt, L.d), tbd = kFR * (int)row_bytes_dev(qt, L.ffn);
+    const int n_dn = (L.d + kFR - 1) / kFR;
+    long maxb = 0;
+    int maxi = 0;
+    for (int nl = 0; nl <= L.n_act; ++nl) {
+        const int n_gu = nl * (L.ffn / kFR);
+        const int kf = fused_kfill(nl, tbd, 2 * tbg);
+        for (int c = 0; c < G; ++c) {
+            const FusedSplit sp(c, G, n_gu, n_dn, kf);
+            const int dn = nl > 0 ? sp.dn_n : 0;
+            maxb = std::max(maxb, (long)sp.gu_n() * 2 * tbg + (long)dn * nl * tbd);
+            maxi = std::max(maxi, sp.gu_n() + dn);
+        }
+    }
+    const int nsg = slices_per_row(L.d), nsd = slices_per_row(L.ffn);
+    const size_t xg = (size_t)xbuf_bytes(nsg, 1) + (size_t)2 * nsg * 2 * (kFR + 1) * 4;
+    const size_t xd = (size_t)xbuf_bytes(nsd, L.n_act) + (size_t)L.n_act * nsd * 2 * (kFR + 1) * 4;
+    L.fused_grid = G;
+    L.fused_tiles = (int)((maxb + 127) / 128 * 128);
+    L.fused_smem = (size_t)L.fused_tiles + std::max(xg, xd);
+    L.fused_ok = maxi <= kFusedMaxItems && L.fused_smem <= 220 * 1024 && L.ffn % kFR == 0;
 }
 
 template <int QT>
 static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
                          cudaStream_t s) {
-    const QView G = qmat_view(L.gate, 0), U = qmat_view(L.up, 0), D = qmat_view(L.down, 0);
-    static const bool regs_only = getenv("X100_GEMV_KERNEL") && atoi(getenv("X100_GEMV_KERNEL")) >= 2;
-    const size_t up_smem = 2 * (size_t)tile_bytes(QT, L.d, 32) + (size_t)(L.d / 32) * (sizeof(XBlk) + sizeof(XF));
-    const size_t dn_smem = (size_t)L.n_act * tile_bytes(QT, L.ffn, 32) +
-                           (size_t)L.n_act * (L.ffn / 32) * (sizeof(XBlk) + sizeof(XF)) +
-                           (size_t)L.n_act * (L.ffn / 256) * 32 * 4;
-    static bool attr_r[64];
-    if (!attr_r[c->device]) {
-        set_qkernel_attrs(router_logits_kernel);
-        set_qkernel_attrs(router_topk_kernel);
-        attr_r[c->device] = true;
-    }
-    const bool bulk_path = !regs_only && L.d % 256 == 0 && L.d <= 2048 && L.ffn % 256 == 0 &&
-                           up_smem <= 200 * 1024 && dn_smem <= 200 * 1024;
-    int st = bulk_path ? launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2), dim3(64), 0, s,
-                                    (const float *)L.router, hn, L.d, L.n_exp, batch, S.logits)
-                       : launch_pdl(router_topk_kernel, dim3((L.n_exp + 1) / 2), dim3(64), 0, s,
-                                    (const float *)L.router, hn, L.d, L.n_exp, L.n_act, batch, S.logits, S.sel, S.w,
-                                    S.ticket);
-    if (st) return st;
-    const bool tma_path = bulk_path && L.gate.tma_ok && L.up.tma_ok && L.down.tma_ok && !getenv("X100_MOE_NO_TMA");
-    if (tma_path) {
-        const size_t up_t = 1024 + 2 * (size_t)tma_tile_bytes(QT, L.d) + (size_t)(L.d / 32) * (sizeof(XBlk) + sizeof(XF));
-        const size_t dn_t = 1024 + (size_t)L.n_act * tma_tile_bytes(QT, L.ffn) +
-                            (size_t)L.n_act * (L.ffn / 32) * (sizeof(XBlk) + sizeof(XF)) +
-                            (size_t)L.n_act * (L.ffn / 256) * 32 * 4;
-        if (up_t <= 200 * 1024 && dn_t <= 200 * 1024) {
-            static bool attr4[64];
-            if (!attr4[c->device]) {
-                set_qkernel_attrs(gate_up_tma_kernel<QT>);
-                set_qkernel_attrs(down_tma_kernel<QT>);
-                attr4[c->device] = true;
-            }
-            dim3 g1((L.ffn + 31) / 32, batch * L.n_act);
-            st = launch_pdl(gate_up_tma_kernel<QT>, g1, dim3(32 * std::min(L.d / 256, 8)), up_t, s, L.gate.tmw,
-                            L.gate.tmd, L.up.tmw, L.up.tmd, L.ffn, L.d, L.n_exp, L.n_act, L.lo, L.hi, hn,
-                            (const float *)S.logits, S.sel, S.w, S.h, c->d_status);
-            if (st) return st;
-            const int pairs = L.n_act * (L.ffn / 256);
-            dim3 g2((L.d + 31) / 32, batch);
-            return launch_pdl(down_tma_kernel<QT>, g2, dim3(32 * std::min(pairs, 32)), dn_t, s, L.down.tmw, L.down.tmd,
-                              L.ffn, L.d, L.n_exp, L.n_act, L.lo, L.hi, (const float *)S.h, (const float *)S.logits,
-                              eout, c->d_status);
-        }
-    }
-    if (bulk_path) {
-        static bool attr3[64];
-        if (!attr3[c->device]) {
-            set_qkernel_attrs(gate_up_bulk_kernel<QT>);
-            set_qkernel_attrs(down_bulk_kernel<QT>);
-            attr3[c->device] = true;
-        }
-        dim3 g1((L.ffn + 31) / 32, batch * L.n_act);
-        st = launch_pdl(gate_up_bulk_kernel<QT>, g1, dim3(32 * std::min(L.d / 256, 8)), up_smem, s, G, U, L.ffn,
-                        L.d, L.n_exp, L.n_act, L.lo, L.hi, hn, (const float *)S.logits, S.sel, S.w, S.h,
-                        c->d_status);
-        if (st) return st;
-        const int pairs = L.n_act * (L.ffn / 256);
-        dim3 g2((L.d + 31) / 32, batch);
-        return launch_pdl(down_bulk_kernel<QT>, g2, dim3(32 * std::min(pairs, 32)), dn_smem, s, D, L.ffn, L.d,
-                          L.n_exp, L.n_act, L.lo, L.hi, (const float *)S.h, (const float *)S.logits, eout,
-                          c->d_status);
-    }
-    if (L.d % 256 == 0 && L.d <= 2048 && L.ffn % 256 == 0 && L.ffn <= 4096) {
-        dim3 g1((L.ffn + 31) / 32, batch * L.n_act);
-        st = launch_pdl(gate_up_slice_kernel<QT>, g1, dim3(32 * (L.d / 256)), 0, s, G, U, L.ffn, L.d, L.n_act, L.lo,
-                        L.hi, hn, (const int *)S.sel, S.h);
-        if (st) return st;
-        const int ns = L.ffn / 256;
-        const int warps = std::min(32, L.n_act * ns) / ns * ns;
-        const size_t smem = (size_t)L.n_act * (L.ffn / 32) * (sizeof(XBlk) + sizeof(XF)) + (size_t)L.n_act * ns * 32 * 4;
-        static bool attr2[64];
-        if (!attr2[c->device]) {
-            set_qkernel_attrs(down_slice_kernel<QT>);
-            attr2[c->device] = true;
-        }
-        dim3 g2((L.d + 31) / 32, batch);
-        return launch_pdl(down_slice_kernel<QT>, g2, dim3(32 * warps), smem, s, D, L.ffn, L.d, L.n_act, L.lo, L.hi,
-                          (const float *)S.h, (const int *)S.sel, (const float *)S.w, eout);
-    }
-    dim3 g1((L.ffn + 7) / 8, batch * L.n_act);
-    gate_up_kernel<QT><<<g1, 256, 0, s>>>(G, U, L.ffn, L.d, L.n_act, L.lo, L.hi, hn, S.sel, S.h);
-    const int lpr = lanes_per_row(units_per_row(QT, L.ffn));
-    const size_t smem = (size_t)L.n_act * (L.ffn / 32) * (sizeof(XBlk) + sizeof(XF));
+    static const bool no_fused = getenv("X100_MOE_NO_FUSED") != nullptr;
     static bool attr[64];
     if (!attr[c->device]) {
-        set_qkernel_attrs(down_combine_kernel<QT>);
+        set_qkernel_attrs(router_logits_kernel);
+        set_qkernel_attrs(gate_up_kernel<QT>);
+        set_qkernel_attrs(down_kernel<QT>);
+        set_qkernel_attrs(moe_fused_kernel<QT>, 220 * 1024);
         attr[c->device] = true;
     }
-    dim3 g2((L.d + 7) / 8, batch);
-    down_combine_kernel<QT><<<g2, 256, smem, s>>>(D, L.ffn, L.d, L.n_act, L.lo, L.hi, S.h, S.sel, S.w, eout, lpr);
-    return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+    if (batch == 1 && L.fused_ok && !no_fused) {
+        int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2), dim3(64), 0, s, (const float *)L.router, hn,
+                            L.d, L.n_exp, 1, S.logits, S.cnt, 1);
+        if (st) return st;
+        FusedArgs fa;
+        fa.gw = L.gate.w;
+        fa.uw = L.up.w;
+        fa.dw = L.down.w;
+        fa.ffn = L.ffn;
+        fa.d = L.d;
+        fa.n_exp = L.n_exp;
+        fa.n_act = L.n_act;
+        fa.lo = L.lo;
+        fa.hi = L.hi;
+        fa.tile_region = L.fused_tiles;
+        fa.hn = hn;
+        fa.logits = S.logits;
+        fa.h = S.h;
+        fa.cnt = S.cnt;
+        fa.sel_out = S.sel;
+        fa.w_out = S.w;
+        fa.eout = eout;
+        fa.status = c->d_status;
+        return launch_pdl(moe_fused_kernel<QT>, dim3(L.fused_grid), dim3(kMoeThreads), L.fused_smem, s, fa);
+    }
+    int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2), dim3(64), 0, s, (const float *)L.router, hn,
+                        L.d, L.n_exp, batch, S.logits, (int *)nullptr, 0);
+    if (st) return st;
+    const int TRg = gate_up_rows_per_cta(QT, L.d), TRd = down_rows_per_cta(QT, L.ffn, L.n_act);
+    st = launch_pdl(gate_up_kernel<QT>, dim3((L.ffn + TRg - 1) / TRg, batch * L.n_act), dim3(kMoeThreads),
+                    gate_up_smem(QT, L.d, TRg), s, (const uint8_t *)L.gate.w, (const uint8_t *)L.up.w, L.ffn, L.d,
+                    L.n_exp, L.n_act, L.lo, L.hi, TRg, hn, (const float *)S.logits, S.sel, S.w, S.h, c->d_status);
+    if (st) return st;
+    return launch_pdl(down_kernel<QT>, dim3((L.d + TRd - 1) / TRd, batch), dim3(kMoeThreads),
+                      down_smem(QT, L.ffn, L.n_act, TRd), s, (const uint8_t *)L.down.w, L.ffn, L.d, L.n_exp, L.n_act,
+                      L.lo, L.hi, TRd, (const float *)S.h, (const float *)S.logits, eout, c->d_status);
 }
 
 int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
@@ -850,12 +758,14 @@ int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *h
     }
 }
 
+void moe_fused_plan(MoeLayer &L, int sm_count) { fused_plan_impl(L, sm_count); }
+
 size_t moe_scratch_bytes(int n_exp, int n_act, int ffn) {
     size_t b = 0;
     b += (size_t)kMaxBatch * n_exp * 4;           // logits
     b += (size_t)kMaxBatch * n_act * 4 * 2;       // sel, w
     b += (size_t)kMaxBatch * n_act * ffn * 4;     // h
-    b += 256 * 5;                                 // alignment + ticket
+    b += 256 * 6;                                 // alignment, ticket, counter
     return b;
 }
 
@@ -869,6 +779,7 @@ MoeScratch moe_scratch_carve(void *base, int n_exp, int n_act, int ffn) {
         return r;
     };
     S.ticket = static_cast<unsigned *>(take(256));
+    S.cnt = static_cast<int *>(take(256));
     S.logits = static_cast<float *>(take((size_t)kMaxBatch * n_exp * 4));
     S.sel = static_cast<int *>(take((size_t)kMaxBatch * n_act * 4));
     S.w = static_cast<float *>(take((size_t)kMaxBatch * n_act * 4));
@@ -934,6 +845,7 @@ x100q_moe *x100q_moe_create(int d, int n_exp, int n_act, int ffn, int qtype, con
         } else {
             cudaMemset(m->scratch, 0, sb);
             m->S = moe_scratch_carve(m->scratch, n_exp, n_act, ffn);
+            moe_fused_plan(L, c->sm_count);
         }
     }
     if (!ok) {

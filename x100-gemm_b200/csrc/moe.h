@@ -16,6 +16,12 @@ struct MoeLayer {
     int d = 0, n_exp = 0, n_act = 0, ffn = 0, qtype = 0, lo = 0, hi = 0;
     float *router = nullptr;
     QMat gate, up, down;
+    // plan of the fused one-token expert kernel (moe_fused_plan): grid,
+    // dynamic shared memory and the bytes of it that hold staged rows;
+    // fused_ok false when it does not fit
+    bool fused_ok = false;
+    int fused_grid = 0, fused_tiles = 0;
+    size_t fused_smem = 0;
 };
 
 // Device scratch of one call (batch <= 16): routing logits, selection,
@@ -26,9 +32,12 @@ struct MoeScratch {
     int *sel = nullptr;
     float *w = nullptr;
     float *h = nullptr;
+    int *cnt = nullptr;   // completion counter of the fused expert kernel
 };
 
 bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype);
+// Fill L.fused_* for a device with sm_count SMs (after the weights are uploaded).
+void moe_fused_plan(MoeLayer &L, int sm_count);
 size_t moe_scratch_bytes(int n_exp, int n_act, int ffn);
 MoeScratch moe_scratch_carve(void *base, int n_exp, int n_act, int ffn);
 // eout[b][:] for b < batch; hn, eout device pointers; asynchronous on s.

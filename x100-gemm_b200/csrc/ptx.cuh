@@ -92,6 +92,31 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, 
     return true;
 }
 
+// ---- flags in global memory ------------------------------------------------------
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Spin until *p >= target (another CTA of the same grid raises it).  Bounded
+// like mbar_wait: gives up when *abort_flag is raised or after kWaitLimitNs,
+// recording X100_E_TIMEOUT (7) in *err.  Returns true when the target was met.
+__device__ __forceinline__ bool spin_until_geq(const int *p, int target, volatile int *abort_flag, int *err) {
+    if (ld_acquire_gpu(p) >= target) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (ld_acquire_gpu(p) >= target) return true;
+        if ((it & 15u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                if (err) atomicExch(err, 7);
+                return false;
+            }
+        }
+    }
+}
+
 // ---- TMA ----------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

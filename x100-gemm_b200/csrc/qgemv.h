@@ -8,18 +8,14 @@
 
 namespace x100 {
 
-// A block-quantised N x K matrix resident in HBM in the device layout of
-// qformats.cuh (weights at w, Q4_0/Q8_0 block scales at d).
+// A block-quantised N x K matrix resident in HBM in the slice layout of
+// qformats.cuh: N contiguous rows of ns slices (row_bytes each).
 struct QMat {
-    int qtype = 0, N = 0, K = 0;
-    void *w = nullptr;
-    __half *d = nullptr;
+    int qtype = 0, N = 0, K = 0, ns = 0;
+    long row_bytes = 0;
+    uint8_t *w = nullptr;
     size_t bytes = 0;
-    // 2-D TMA maps over the weight rows and the scale rows (boxes of 32 rows
-    // x 128 bytes, 128-byte swizzle); tma_ok is false when they could not be
-    // encoded (the kernels then stage rows with cp.async).
-    CUtensorMap tmw, tmd;
-    bool tma_ok = false;
+    const uint8_t *row(long r) const { return w + r * row_bytes; }
 };
 
 size_t qtype_block_elems(int qt);
@@ -27,27 +23,21 @@ size_t qtype_block_bytes(int qt);
 // Upload N rows of GGUF-native blocks (host pointer) and re-lay them out on
 // the device; synchronous on `s`.  Returns false with the error recorded.
 bool qmat_upload(DevCtx *c, int qt, int N, int K, const void *blocks, QMat &m, cudaStream_t s);
-// Device view of rows [row0, N) of m.
-q::QView qmat_view(const QMat &m, long row0);
 // y[b*N + n] = sum_k W[n][k] x[b*K + k], b < batch (<= 16); x, y device.
 int launch_qgemv(DevCtx *c, const QMat &m, const float *x, float *y, int batch, cudaStream_t s);
-
-namespace q {
-int lanes_per_row(int units);
-}
 
 // Launch `kernel` on `s` with programmatic stream serialization (the kernel
 // may start while the previous kernel of the stream runs; it orders itself
 // with griddepcontrol.wait).  X100_NO_PDL=1 launches without the attribute.
 bool pdl_enabled();
 
-// One-time kernel attributes for the quantised path: allow up to 200 KB of
-// dynamic shared memory and ask for the maximum shared-memory carveout, so
+// One-time kernel attributes for the quantised path: allow `smem_max` bytes
+// of dynamic shared memory and ask for the maximum shared-memory carveout, so
 // consecutive kernels of a decode step share one L1/shared split and the SM
 // need not be reconfigured (drained) between them.
 template <typename F>
-void set_qkernel_attrs(F *kernel) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+void set_qkernel_attrs(F *kernel, int smem_max = 200 * 1024) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
     cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
 }
 template <typename... KArgs, typename... Args>
