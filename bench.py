@@ -32,6 +32,7 @@ import time
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REPO, "x100-gemm_b200"))
 sys.path.insert(0, os.path.join(REPO, "oracle"))
+from x100b import shard  # noqa: E402  (how the path splits over GPUs; no device code)
 
 L2_BYTES = 126 * 1024 * 1024
 
@@ -284,7 +285,8 @@ def bench_gemm(args, dist, peaks, peak_src):
     if S % world:
         raise SystemExit("size must divide by the GPU count")
     M, K = S, S
-    N = S // world                       # this rank's column slice of B and C
+    n0, n1 = shard.gemm_cols(S, world, rank)
+    N = n1 - n0                          # this rank's column slice of B and C
     es = {"gemm_i8": 1, "gemm_f16": 2, "gemm_f32": 4}[kind]
     ce = 2 if kind == "gemm_f16" else 4
     set_bytes = M * K * es + K * N * es + M * N * ce
@@ -571,7 +573,7 @@ def bench_moe(args, dist, peaks, peak_src):
     import x100b
     d, E, k, ffn, B = 2048, 128, 8, 768, args.batch
     world, rank = dist.world, dist.rank
-    lo, hi = rank * E // world, (rank + 1) * E // world
+    lo, hi = shard.expert_slice(E, world, rank)
     gen = torch.Generator(device="cuda").manual_seed(99)
     router = (torch.randn((E, d), device="cuda", generator=gen) * 0.02).cpu().numpy()
     nb_d = ffn * d // 256

@@ -136,7 +136,8 @@ enum {
 /* Last status recorded on the calling thread (0 when the last call worked). */
 int         x100_last_error(void);
 const char *x100_strerror(int code);
-/* Select the CUDA device used by later calls on this thread (default 0).    */
+/* Select the CUDA device used by later calls on this thread (default: the  */
+/* thread's current CUDA device, so one process per GPU needs no call).      */
 int         x100_set_device(int device);
 
 #ifdef __cplusplus

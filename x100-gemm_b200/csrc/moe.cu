@@ -862,7 +862,7 @@ x100q_moe *x100q_moe_create(int d, int n_exp, int n_act, int ffn, int qtype, con
 
 void x100q_moe_destroy(x100q_moe *m) {
     if (!m) return;
-    cudaSetDevice(m->device);
+    DeviceGuard dg(m->device);
     cudaFree(m->L.router);
     cudaFree(m->L.gate.w);
     cudaFree(m->L.up.w);

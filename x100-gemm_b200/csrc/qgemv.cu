@@ -289,7 +289,7 @@ x100q_lin *x100q_lin_create(int qtype, int N, int K, const void *blocks) {
 
 void x100q_lin_destroy(x100q_lin *l) {
     if (!l) return;
-    cudaSetDevice(l->device);
+    DeviceGuard dg(l->device);
     cudaFree(l->m.w);
     delete l;
 }

@@ -9,7 +9,9 @@
 namespace x100 {
 
 static thread_local int t_error = 0;
-static thread_local int t_device = 0;
+// Device chosen with x100_set_device on this thread, or -1: follow the
+// thread's current CUDA device (one process or thread per GPU).
+static thread_local int t_device = -1;
 
 void set_error(int code) { t_error = code; }
 int get_error() { return t_error; }
@@ -39,11 +41,19 @@ int check_cuda(cudaError_t e, int code_if_error) {
 static std::mutex g_ctx_mu;
 static DevCtx *g_ctx[64];
 
-int current_device() { return t_device; }
+int current_device() {
+    if (t_device >= 0) return t_device;
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) {
+        cudaGetLastError();
+        d = 0;
+    }
+    return d;
+}
 
 DevCtx *ctx() {
     if (fault_injected("device")) return nullptr;
-    int dev = t_device;
+    const int dev = current_device();
     if (dev < 0 || dev >= 64) {
         set_error(X100_E_ARG);
         return nullptr;
@@ -51,7 +61,7 @@ DevCtx *ctx() {
     {
         std::lock_guard<std::mutex> lk(g_ctx_mu);
         if (g_ctx[dev]) {
-            cudaSetDevice(dev);
+            if (t_device >= 0) cudaSetDevice(dev);   // explicit choice; otherwise dev is already current
             return g_ctx[dev];
         }
         int n = 0;

@@ -43,6 +43,22 @@ struct DevCtx {
 // Returns nullptr and records the error if no usable device exists.
 DevCtx *ctx();
 int current_device();
+// Makes `device` current for the guard's lifetime and restores the caller's
+// current device afterwards (used where the library frees memory it owns).
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&prev) != cudaSuccess) {
+            cudaGetLastError();
+            prev = -1;
+        }
+        if (prev != device) cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
 
 // Ensure staging buffer `slot` of `c` holds at least `bytes`; returns its
 // device pointer or nullptr (error recorded).
