@@ -22,6 +22,8 @@
 // and MMAs, frees its TMEM and returns.
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+
 #include "gemm_kernels.h"
 #include "ptx.cuh"
 
@@ -31,14 +33,14 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int STAGES = 4;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;         // two per TMEM lane quadrant, each takes half the columns
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_BYTES = BM * 128;   // one stage of A: 128 rows x 128 bytes of K
 constexpr int B_BYTES = BN * 128;   // one stage of B: 128 bytes of K (rows) x 256 columns
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int EPI_LD = 33;          // padded row (words) of the transpose buffer
+constexpr int EPI_LD = 33;          // padded row (words) of an epilogue warp's transpose buffer
 constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_LD * 4;
-constexpr int BAR_OFF = STAGES * STAGE_BYTES + EPI_BYTES;
+constexpr int BAR_OFF = STAGES * STAGE_BYTES + EPI_BYTES;   // stages, then the transpose buffers
 constexpr int NBARS = 2 * STAGES + 2 + 2 + 1;
 constexpr int SMEM_BYTES = BAR_OFF + NBARS * 8 + 16 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
@@ -70,31 +72,121 @@ __device__ __forceinline__ __half epi_add(__half c, uint32_t v) {
     return __float2half_rn(__half2float(c) + __uint_as_float(v));
 }
 
-// Read-add-write of `rows` (<= 32) rows of one 32-column chunk; lane owns a
-// column, so every row access is one coalesced 32-element segment.  Loads
-// are batched ahead of the stores to keep many requests in flight.
+// ---- epilogue: C += accumulator ------------------------------------------------------
+// Epilogue warp w (w >= 2) may read TMEM lanes 32 * (w % 4) .. +31, i.e. rows
+// 32q .. 32q+31 of the CTA's accumulator (q = w % 4); the two warps of a
+// quadrant split the 32-column chunks.  A chunk arrives from tcgen05.ld with
+// one row per thread; it is transposed through a padded per-warp buffer so
+// that each C access of the warp is one full 128-byte row segment (lane =
+// column; whole sectors, coalesced).  The C rows of a chunk are read ahead:
+// the first chunk before the accumulator is ready, each next chunk while the
+// current one is added and stored.
+// One accumulator (tile) of this warp: rows row_base + 32q .. +31, column
+// chunks [c0, c1) from n0.  Waits for the accumulator (tfull), releases it
+// (arrive on the barrier at release_addr, a shared::cluster address) once
+// read.  Returns false on a timeout.
 template <typename CT>
-__device__ __forceinline__ void epi_rows(CT *cp, long ldc, const uint32_t *buf, int lane, int rows) {
-    if (rows == 32) {
+__device__ __forceinline__ bool epi_tile(uint32_t tmem_acc, int q, int lane, int c0, int c1, CT *__restrict__ C,
+                                         long ldc, int M, int N, int row_base, int n0, uint64_t *tfull,
+                                         uint32_t parity, uint32_t release_addr, uint32_t *buf,
+                                         volatile int *abort_flag, int *status) {
+    const int r0 = row_base + q * 32;
+    const int nrows = max(0, min(32, M - r0));
+    auto load = [&](int c, CT (&v)[32]) {
+        const int col = n0 + c * 32 + lane;
+        if (c < c1 && col < N) {
+            const CT *p = C + static_cast<long>(r0) * ldc + col;
 #pragma unroll
-        for (int i0 = 0; i0 < 32; i0 += 16) {
-            CT v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = cp[static_cast<long>(i0 + j) * ldc];
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                cp[static_cast<long>(i0 + j) * ldc] = epi_add(v[j], buf[(i0 + j) * EPI_LD + lane]);
+            for (int i = 0; i < 32; ++i)
+                if (i < nrows) v[i] = __ldcs(p + static_cast<long>(i) * ldc);
         }
-    } else {
-        for (int i = 0; i < rows; ++i)
-            cp[static_cast<long>(i) * ldc] = epi_add(cp[static_cast<long>(i) * ldc], buf[i * EPI_LD + lane]);
+    };
+    CT cur[32];
+    load(c0, cur);
+    if (!mbar_wait(tfull, parity, abort_flag, status)) return false;
+    tc_fence_after();
+    if (c0 >= c1) {   // nothing of this tile for this warp
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(release_addr);
+        return true;
     }
+    for (int c = c0; c < c1; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_acc + c * 32 + (static_cast<uint32_t>(q * 32) << 16), r);
+        tmem_wait_ld();
+        if (c == c1 - 1) {   // accumulator fully read: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(release_addr);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) buf[lane * EPI_LD + j] = r[j];
+        __syncwarp();
+        CT nxt[32];
+        load(c + 1, nxt);
+        const int col = n0 + c * 32 + lane;
+        if (col < N) {
+            CT *p = C + static_cast<long>(r0) * ldc + col;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (i < nrows) __stcs(p + static_cast<long>(i) * ldc, epi_add(cur[i], buf[i * EPI_LD + lane]));
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) cur[i] = nxt[i];
+    }
+    return true;
 }
 
-template <int KIND>
+// The same for 32-bit C whose tensor map allows TMA: the chunk goes from
+// TMEM through a 4 KB per-warp buffer (128-byte swizzle: row r's 16-byte
+// piece i sits at position i ^ (r % 8), so the 8 lanes of a quarter-warp
+// write 8 distinct bank groups) and is added into C by one TMA reduce-add,
+// so C never passes through the SM (the L2 reads, adds and writes it).
+__device__ __forceinline__ bool epi_tile_tma(uint32_t tmem_acc, int q, int lane, int c0, int c1,
+                                             const CUtensorMap *tmC, int row_base, int n0, uint64_t *tfull,
+                                             uint32_t parity, uint32_t release_addr, uint8_t *buf,
+                                             volatile int *abort_flag, int *status) {
+    if (!mbar_wait(tfull, parity, abort_flag, status)) return false;
+    tc_fence_after();
+    if (c0 >= c1) {   // nothing of this tile for this warp
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(release_addr);
+        return true;
+    }
+    for (int c = c0; c < c1; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_acc + c * 32 + (static_cast<uint32_t>(q * 32) << 16), r);
+        tmem_wait_ld();
+        if (c == c1 - 1) {   // accumulator fully read: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(release_addr);
+        }
+        if (lane == 0) bulk_wait_read_all();   // the previous chunk's reduce has read the buffer
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<uint4 *>(buf + lane * 128 + ((i ^ (lane & 7)) << 4)) =
+                make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_reduce_add_2d(tmC, n0 + c * 32, row_base + q * 32, buf);
+            bulk_commit();
+        }
+    }
+    return true;
+}
+
+// TE: C += accumulator by TMA reduce-add (32-bit C with a TMA-compatible layout)
+template <int KIND, bool TE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   typename Traits<KIND>::CT *__restrict__ C, int M, int N, int K, long ldc, int *status) {
+                   const __grid_constant__ CUtensorMap tmC, typename Traits<KIND>::CT *__restrict__ C, int M, int N,
+                   int K, long ldc, int *status) {
     using CT = typename Traits<KIND>::CT;
     constexpr int ES = Traits<KIND>::ES;
     constexpr int BK = 128 / ES;          // K elements per stage
@@ -109,7 +201,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_BYTES;
-    uint32_t *epi = reinterpret_cast<uint32_t *>(smem + STAGES * STAGE_BYTES);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + BAR_OFF);
     uint64_t *full = bars;
     uint64_t *empty = bars + STAGES;
@@ -241,45 +332,298 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
         // ---------------- epilogue ----------------
         const int q = warp & 3;   // TMEM lane quadrant this warp may access
-        uint32_t *buf = epi + (warp - 2) * 32 * EPI_LD;
+        const int h = (warp - 2) >> 2;
+        uint32_t *buf = reinterpret_cast<uint32_t *>(smem + STAGES * STAGE_BYTES) + (warp - 2) * 32 * EPI_LD;
+        uint8_t *tbuf = smem + STAGES * STAGE_BYTES + (warp - 2) * 4096;   // 1024-aligned (TE)
+        const uint32_t rel[2] = {smem_u32(&tempty[0]), smem_u32(&tempty[1])};
         uint32_t acc = 0, acc_phase = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
             int mt, nt;
             tile_coords(tile, num_m, num_n, mt, nt);
-            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, status)) break;
-            tc_fence_after();
-            const int row0 = mt * BM + q * 32;
             const int n0 = nt * BN;
             const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
-            for (int c = 0; c < nchunks; ++c) {
-                uint32_t r[32];
-                tmem_ld32(tmem_base + acc * BN + c * 32 + (static_cast<uint32_t>(q * 32) << 16), r);
-                tmem_wait_ld();
-                if (c == nchunks - 1) {
-                    // accumulator fully read: hand it back to the MMA warp
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[acc]);
-                }
-#pragma unroll
-                for (int j = 0; j < 32; ++j) buf[lane * EPI_LD + j] = r[j];
-                __syncwarp();
-                const int col = n0 + c * 32 + lane;
-                if (row0 < M && col < N)
-                    epi_rows<CT>(C + static_cast<long>(row0) * ldc + col, ldc, buf, lane, min(32, M - row0));
-                __syncwarp();
-            }
+            const int c0 = min(h * (BN / 64), nchunks), c1 = min((h + 1) * (BN / 64), nchunks);
+            bool ok;
+            if constexpr (TE)
+                ok = epi_tile_tma(tmem_base + acc * BN, q, lane, c0, c1, &tmC, mt * BM, n0, &tfull[acc], acc_phase,
+                                  rel[acc], tbuf, abort_flag, status);
+            else
+                ok = epi_tile<CT>(tmem_base + acc * BN, q, lane, c0, c1, C, ldc, M, N, mt * BM, n0, &tfull[acc],
+                                  acc_phase, rel[acc], buf, abort_flag, status);
+            if (!ok) break;
             acc ^= 1u;
             if (acc == 0) acc_phase ^= 1u;
         }
     }
 
+    if (TE && warp >= 2 && lane == 0) bulk_wait_all();   // this warp's reduce-adds into C are done
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
     }
+}
+
+// ---- 2-SM version: one CTA pair (cluster of 2) per 256 x 256 output tile ----------------
+// Each CTA stages its 128 rows of A and its 128 columns of B (32 KB per
+// 128-byte K slab, six stages); the pair leader (CTA rank 0) issues
+// tcgen05.mma.cta_group::2 with M = N = 256, whose accumulator rows 0-127
+// live in the leader's TMEM and rows 128-255 in the peer's.  Per output
+// element this halves the bytes each SM pulls from L2 compared with the
+// 128 x 256 single-CTA tile.  Both CTAs' copies complete on the leader's
+// `full` barrier (the leader announces both halves); the leader's commits
+// arrive on the `empty` / `tfull` barriers of both CTAs; both epilogues
+// release an accumulator on the leader's `tempty` barrier.
+constexpr int P_STAGES = 6;
+constexpr int P_ROWS = 128;                       // A rows (and C rows) per CTA
+constexpr int P_COLS = 128;                       // B columns per CTA
+constexpr int P_A_BYTES = P_ROWS * 128;
+constexpr int P_B_BYTES = P_COLS * 128;
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_BAR_OFF = P_STAGES * P_STAGE_BYTES + EPI_BYTES;
+constexpr int P_NBARS = 2 * P_STAGES + 2 + 2 + 1;
+constexpr int P_SMEM_BYTES = P_BAR_OFF + P_NBARS * 8 + 16 + 1024;
+
+template <int KIND, bool TE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, typename Traits<KIND>::CT *__restrict__ C, int M, int N,
+                    int K, long ldc, int *status) {
+    using CT = typename Traits<KIND>::CT;
+    constexpr int ES = Traits<KIND>::ES;
+    constexpr int BK = 128 / ES;          // K elements per stage
+    constexpr int UK = 32 / ES;           // K elements per MMA
+    constexpr int KSTEPS = BK / UK;       // MMAs per stage (4)
+    constexpr int ATOM_N = 128 / ES;      // N elements per 128-byte swizzle atom
+    constexpr int NBOX = P_COLS / ATOM_N; // B boxes per stage per CTA
+    constexpr int BOX_B_BYTES = BK * 128;
+    constexpr int TM = 2 * P_ROWS, TN = 2 * P_COLS;   // output tile of the pair
+    constexpr uint32_t IDESC = (KIND == 0) ? idesc_make(2, 1, 1, TM, TN) : idesc_make(1, 0, 1, TM, TN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + P_STAGES * P_A_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_BAR_OFF);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + P_STAGES;
+    uint64_t *tfull = bars + 2 * P_STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + P_NBARS);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * EPI_WARPS);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();                  // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_m = (M + TM - 1) / TM;
+    const int num_n = (N + TN - 1) / TN;
+    const int total = num_m * num_n;
+    const int num_kb = (K + BK - 1) / BK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs) ----------------
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued[P_STAGES];
+            for (int s = 0; s < P_STAGES; ++s) issued[s] = 0;
+            uint32_t full_l[P_STAGES];
+            for (int s = 0; s < P_STAGES; ++s) full_l[s] = mapa_shared(&full[s], 0);
+            bool ok = true;
+            for (int tile = pair; tile < total && ok; tile += npairs) {
+                int mt, nt;
+                tile_coords(tile, num_m, num_n, mt, nt);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+                    tma_load_2d_pair(sA + stage * P_A_BYTES, &tmA, kb * BK, mt * TM + (int)rank * P_ROWS, full_l[stage]);
+#pragma unroll
+                    for (int j = 0; j < NBOX; ++j)
+                        tma_load_2d_pair(sB + stage * P_B_BYTES + j * BOX_B_BYTES, &tmB,
+                                         nt * TN + (int)rank * P_COLS + j * ATOM_N, kb * BK, full_l[stage]);
+                    issued[stage]++;
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (ok) {
+                // wait until the leader's MMAs have released every stage
+                for (int i = 0; i < P_STAGES; ++i) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status)) break;
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            } else if (leader) {
+                // aborting: wait (bounded) for the copies of both CTAs announced so far
+                for (int s = 0; s < P_STAGES; ++s)
+                    if (issued[s]) mbar_wait_drain(&full[s], (issued[s] - 1u) & 1u, kDrainNs);
+            } else {
+                // aborting: this CTA's copies complete on the leader's barrier; give them
+                // time to land before the shared memory is released
+                const unsigned long long t0 = globaltimer_ns();
+                while (globaltimer_ns() - t0 < 1000000ull) {
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer (pair leader) ----------------
+            uint32_t empty_p[P_STAGES], tfull_p[2];
+            for (int s = 0; s < P_STAGES; ++s) empty_p[s] = mapa_shared(&empty[s], 1);
+            for (int b = 0; b < 2; ++b) tfull_p[b] = mapa_shared(&tfull[b], 1);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (int tile = pair; tile < total && ok; tile += npairs) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * TN;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * P_A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * P_B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < KSTEPS; ++k) {
+                        const uint64_t adesc = smem_desc_sw128(a0 + k * 32, 16, 1024);
+                        const uint64_t bdesc = smem_desc_sw128(b0 + k * UK * 128, BOX_B_BYTES, 1024);
+                        if (KIND == 0)
+                            umma_i8_pair(d_tmem, adesc, bdesc, IDESC, (kb | k) ? 1u : 0u);
+                        else
+                            umma_f16_pair(d_tmem, adesc, bdesc, IDESC, (kb | k) ? 1u : 0u);
+                    }
+                    umma_commit_pair(smem_u32(&empty[stage]));
+                    umma_commit_pair(empty_p[stage]);
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair(smem_u32(&tfull[acc]));
+                umma_commit_pair(tfull_p[acc]);
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            // all MMAs issued by this thread complete before TMEM is freed
+            umma_commit_pair(smem_u32(drain));
+            mbar_wait_drain(drain, 0, kDrainNs);
+        }
+    } else {
+        // ---------------- epilogue (both CTAs) ----------------
+        const int q = warp & 3;   // TMEM lane quadrant this warp may access
+        const int h = (warp - 2) >> 2;
+        uint32_t *buf = reinterpret_cast<uint32_t *>(smem + P_STAGES * P_STAGE_BYTES) + (warp - 2) * 32 * EPI_LD;
+        uint8_t *tbuf = smem + P_STAGES * P_STAGE_BYTES + (warp - 2) * 4096;   // 1024-aligned (TE)
+        const uint32_t rel[2] = {mapa_shared(&tempty[0], 0), mapa_shared(&tempty[1], 0)};
+        uint32_t acc = 0, acc_phase = 0;
+        for (int tile = pair; tile < total; tile += npairs) {
+            int mt, nt;
+            tile_coords(tile, num_m, num_n, mt, nt);
+            const int n0 = nt * TN;
+            const int nchunks = min(TN / 32, (N - n0 + 31) / 32);
+            const int c0 = min(h * (TN / 64), nchunks), c1 = min((h + 1) * (TN / 64), nchunks);
+            bool ok;
+            if constexpr (TE)
+                ok = epi_tile_tma(tmem_base + acc * TN, q, lane, c0, c1, &tmC, mt * TM + (int)rank * P_ROWS, n0,
+                                  &tfull[acc], acc_phase, rel[acc], tbuf, abort_flag, status);
+            else
+                ok = epi_tile<CT>(tmem_base + acc * TN, q, lane, c0, c1, C, ldc, M, N, mt * TM + (int)rank * P_ROWS,
+                                  n0, &tfull[acc], acc_phase, rel[acc], buf, abort_flag, status);
+            if (!ok) break;
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+
+    if (TE && warp >= 2 && lane == 0) bulk_wait_all();   // this warp's reduce-adds into C are done
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();                  // no arrival into either CTA is still pending
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    }
+    cluster_sync_all();
+}
+
+template <int KIND, bool TE>
+static int launch_te(DevCtx *c, int M, int N, int K, const CUtensorMap &ta, const CUtensorMap &tb,
+                     const CUtensorMap &tc_, void *C, long ldc, cudaStream_t s) {
+    using CT = typename Traits<KIND>::CT;
+    static const bool one_sm = getenv("X100_GEMM_1SM") != nullptr;
+    static int pairs_fit[64] = {};       // co-resident CTA pairs of the 2-SM kernel
+    static bool attr_set[64] = {};
+    if (!attr_set[c->device]) {
+        if (cudaFuncSetAttribute(gemm_tc_kernel<KIND, TE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(gemm_tc2_kernel<KIND, TE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 P_SMEM_BYTES) != cudaSuccess)
+            return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (c->sm_count / 2));
+        cfg.blockDim = dim3(THREADS);
+        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        int nclusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&nclusters, gemm_tc2_kernel<KIND, TE>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            nclusters = 0;
+        }
+        pairs_fit[c->device] = nclusters;
+        attr_set[c->device] = true;
+    }
+    const int pair_tiles = ((M + 2 * P_ROWS - 1) / (2 * P_ROWS)) * ((N + 2 * P_COLS - 1) / (2 * P_COLS));
+    if (!one_sm && pairs_fit[c->device] > 0) {
+        const int pairs = pair_tiles < pairs_fit[c->device] ? pair_tiles : pairs_fit[c->device];
+        gemm_tc2_kernel<KIND, TE><<<2 * pairs, THREADS, P_SMEM_BYTES, s>>>(ta, tb, tc_, reinterpret_cast<CT *>(C), M,
+                                                                          N, K, ldc, c->d_status);
+        return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+    }
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int grid = tiles < c->sm_count ? tiles : c->sm_count;
+    gemm_tc_kernel<KIND, TE><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, tc_, reinterpret_cast<CT *>(C), M, N, K, ldc,
+                                                              c->d_status);
+    return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
 }
 
 template <int KIND>
@@ -289,24 +633,24 @@ static int launch_kind(DevCtx *c, int M, int N, int K, const void *A, long lda, 
     constexpr int BK = 128 / ES;
     constexpr int ATOM_N = 128 / ES;
     const CUtensorMapDataType dt = (KIND == 0) ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tcm;
+    // boxes: A BK x 128 rows, B ATOM_N columns x BK rows (the 2-SM kernel
+    // loads one 128-column half of B per CTA in 128 / ATOM_N boxes)
     if (!make_tmap_2d(&ta, A, dt, (uint64_t)K, (uint64_t)M, (uint64_t)lda * ES, BK, BM) ||
         !make_tmap_2d(&tb, B, dt, (uint64_t)N, (uint64_t)K, (uint64_t)ldb * ES, ATOM_N, BK)) {
         set_error(X100_E_UNSUPPORTED);
         return X100_E_UNSUPPORTED;
     }
-    static bool attr_set[64] = {};
-    if (!attr_set[c->device]) {
-        if (cudaFuncSetAttribute(gemm_tc_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-            cudaSuccess)
-            return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
-        attr_set[c->device] = true;
+    // 32-bit C: 32 x 32 boxes added by TMA reduce-add when the layout allows
+    bool te = false;
+    if (KIND != 2 && reinterpret_cast<uintptr_t>(C) % 16 == 0 && (ldc * 4) % 16 == 0 && !getenv("X100_GEMM_LSU_EPI"))
+        te = make_tmap_2d(&tcm, C, KIND == 0 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          (uint64_t)N, (uint64_t)M, (uint64_t)ldc * 4, 32, 32);
+    if (!te) tcm = ta;   // unused by the kernel
+    if constexpr (KIND != 2) {
+        if (te) return launch_te<KIND, true>(c, M, N, K, ta, tb, tcm, C, ldc, s);
     }
-    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    const int grid = tiles < c->sm_count ? tiles : c->sm_count;
-    gemm_tc_kernel<KIND><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, reinterpret_cast<typename Traits<KIND>::CT *>(C),
-                                                          M, N, K, ldc, c->d_status);
-    return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+    return launch_te<KIND, false>(c, M, N, K, ta, tb, tcm, C, ldc, s);
 }
 
 }  // namespace tc
