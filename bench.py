@@ -414,7 +414,7 @@ def bench_gemm(args, dist, peaks, peak_src):
                          f"(> L2 between reuses)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": unit,
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_note,
-                     "kernel": "x100::tc::gemm_tc_kernel" if kind != "gemm_f32" else "gemm_fast_kernel",
+                     "kernel": "x100::tc::gemm_tc2_kernel (2-SM, TMA reduce-add epilogue)" if kind != "gemm_f32" else "gemm_fast_kernel",
                      "algorithmic_ops_per_launch": ops_rank,
                      "kernel_ms_mean": round(kernel_ms, 4)},
         "clocks": clocks,
@@ -692,7 +692,7 @@ def bench_moe(args, dist, peaks, peak_src):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(f"moe_b{B}"),
                      "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
-                     "kernel": "router_topk + gate_up + down_combine (3 launches per call)",
+                     "kernel": ("router_logits + moe_fused (2 launches per call)" if B == 1 else "router_logits + gate_up + down (3 launches per call)"),
                      "algorithmic_bytes_per_token": alg_tok, "call_us_mean": round(per_call_us, 3),
                      "parity": err},
         "clocks": clocks,
