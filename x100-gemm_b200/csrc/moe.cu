@@ -43,10 +43,14 @@ constexpr int kMaxAct = 16;
 constexpr int kMaxExp = 256;
 
 // ---- router + softmax + top-k ------------------------------------------------------
+// When `zero` is set, CTA 0 also clears zero[0 .. nzero) (the completion
+// counter of the fused expert kernel that follows) once the previous kernel
+// on the stream is done with it.
 __global__ void __launch_bounds__(256) router_topk_kernel(const float *__restrict__ router,
                                                           const float *__restrict__ hn, int d, int n_exp, int n_act,
                                                           int batch, float *__restrict__ logits, int *__restrict__ sel,
-                                                          float *__restrict__ wsel, unsigned *__restrict__ ticket) {
+                                                          float *__restrict__ wsel, unsigned *__restrict__ ticket,
+                                                          int *__restrict__ zero, int nzero) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int e = blockIdx.x * nwarps + warp;
     // the router row (independent of the previous kernel) is loaded before
@@ -61,6 +65,8 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float *__restric
         if (e < n_exp && i < nv) r[i] = __ldg(rw + lane + 32 * i);
     pdl_launch_dependents();
     pdl_wait();
+    if (zero && blockIdx.x == 0)
+        for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
     if (e < n_exp) {
         for (int b = 0; b < batch; ++b) {
             const float4 *x = reinterpret_cast<const float4 *>(hn + (long)b * d);
@@ -215,22 +221,32 @@ __global__ void __launch_bounds__(64) router_logits_kernel(const float *__restri
 // and renormalisation, by a whole CTA (qwen_moe.c:296-301).  Warp 0 forms the
 // probabilities exactly as router_topk_kernel does; the rank of expert e is
 // the number of experts with a larger probability, or an equal one at a lower
-// index, which reproduces the greedy selection order.  Thread t ranks expert
-// t % n_exp against one half of the experts (read four at a time) and the two
-// halves are added.  Results in shared memory: s_sel[a], s_w[a] for a <
-// n_act.  s_p holds kMaxExp + 8 floats, s_rk 2 * kMaxExp ints; s_wr is
+// index, which reproduces the greedy selection order.  A thread ranks one
+// expert against one quarter of the experts (read four at a time) and the
+// four counts are added.  Results in shared memory: s_sel[a], s_w[a] for
+// a < n_act.  s_p holds kMaxExp + 16 floats, s_rk 4 * kMaxExp ints; s_wr is
 // scratch of kMaxAct floats.  blockDim.x must be >= 64 and >= n_act.
-__device__ __forceinline__ void route_fast(const float *lg, int n_exp, int n_act, float *s_p, int *s_rk, int *s_sel,
-                                           float *s_w, float *s_wr) {
+//
+// Warp 0 (lane l) loads logits l, l+32, ... of one token into pre[].
+__device__ __forceinline__ void route_load(const float *lg, int n_exp, float (&pre)[kMaxExp / 32]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < kMaxExp / 32; ++i) {
+        const int ee = lane + 32 * i;
+        pre[i] = ee < n_exp ? __ldcg(lg + ee) : -1e30f;
+    }
+}
+// Routing from logits already loaded by warp 0 (route_load).
+__device__ __forceinline__ void route_from(const float (&pre)[kMaxExp / 32], int n_exp, int n_act, float *s_p,
+                                           int *s_rk, int *s_sel, float *s_w, float *s_wr) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int hl = ((n_exp + 7) / 8) * 4;   // experts per half, a multiple of 4
+    const int ql = ((n_exp + 15) / 16) * 4;   // experts per quarter, a multiple of 4
     if (warp == 0) {
         float p[kMaxExp / 32];
         float m = -1e30f;
 #pragma unroll
         for (int i = 0; i < kMaxExp / 32; ++i) {
-            const int ee = lane + 32 * i;
-            p[i] = ee < n_exp ? __ldcg(lg + ee) : -1e30f;
+            p[i] = pre[i];
             m = fmaxf(m, p[i]);
         }
 #pragma unroll
@@ -249,30 +265,32 @@ __device__ __forceinline__ void route_fast(const float *lg, int n_exp, int n_act
         for (int i = 0; i < kMaxExp / 32; ++i) {
             const int ee = lane + 32 * i;
             if (ee < n_exp) s_p[ee] = p[i] * inv;
-            else if (ee < 2 * hl) s_p[ee] = -1.0f;   // padding never outranks a probability
+            else if (ee < 4 * ql) s_p[ee] = -1.0f;   // padding never outranks a probability
         }
-        if (lane < 8 && kMaxExp + lane < 2 * hl) s_p[kMaxExp + lane] = -1.0f;
+        if (lane < 16 && kMaxExp + lane < 4 * ql) s_p[kMaxExp + lane] = -1.0f;
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < 2 * n_exp; idx += blockDim.x) {
-        const int e = idx % n_exp, h = idx / n_exp;
+    // rank of expert e = experts with a larger probability, or an equal one at
+    // a lower index; thread task (e, quarter) counts one quarter of the experts
+    for (int idx = threadIdx.x; idx < 4 * n_exp; idx += blockDim.x) {
+        const int qq = idx / n_exp, e = idx - qq * n_exp;
         const float pe = s_p[e];
-        const float4 *q = reinterpret_cast<const float4 *>(s_p + h * hl);
+        const float4 *qv = reinterpret_cast<const float4 *>(s_p + qq * ql);
         int rank = 0;
 #pragma unroll 4
-        for (int i = 0; i < hl / 4; ++i) {
-            const float4 v = q[i];
-            const int f = h * hl + 4 * i;
+        for (int i = 0; i < ql / 4; ++i) {
+            const float4 v = qv[i];
+            const int f = qq * ql + 4 * i;
             rank += (v.x > pe) || (v.x == pe && f < e);
             rank += (v.y > pe) || (v.y == pe && f + 1 < e);
             rank += (v.z > pe) || (v.z == pe && f + 2 < e);
             rank += (v.w > pe) || (v.w == pe && f + 3 < e);
         }
-        s_rk[h * kMaxExp + e] = rank;
+        s_rk[qq * kMaxExp + e] = rank;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < n_exp; e += blockDim.x) {
-        const int rank = s_rk[e] + s_rk[kMaxExp + e];
+        const int rank = s_rk[e] + s_rk[kMaxExp + e] + s_rk[2 * kMaxExp + e] + s_rk[3 * kMaxExp + e];
         if (rank < n_act) {
             s_sel[rank] = e;
             s_wr[rank] = s_p[e];
@@ -287,16 +305,39 @@ __device__ __forceinline__ void route_fast(const float *lg, int n_exp, int n_act
     __syncthreads();
 }
 
+__device__ __forceinline__ void route_fast(const float *lg, int n_exp, int n_act, float *s_p, int *s_rk, int *s_sel,
+                                           float *s_w, float *s_wr) {
+    float pre[kMaxExp / 32];
+    if ((threadIdx.x >> 5) == 0) route_load(lg, n_exp, pre);
+    route_from(pre, n_exp, n_act, s_p, s_rk, s_sel, s_w, s_wr);
+}
+
 // ---- expert kernels ---------------------------------------------------------------------
 // Weights are in the slice layout of qformats.cuh: the rows of one expert are
 // contiguous, so a run of rows is one bulk copy into shared memory, and a
 // thread dots half a slice (half p of a staged run is half p % 2 of slice
-// p / 2, which is row (p/2) / ns, slice (p/2) % ns).  red[] holds the sums as
-// [matrix or slot][slice][half][row] with row stride R + 1, so both the
-// writes and the per-row sums avoid bank conflicts.
+// p / 2, which is row (p/2) / ns, slice (p/2) % ns).  red[] holds the sums
+// row by row, [matrix or expert][row][slice][half] with an odd row stride
+// 2 ns + 1, so the writes (consecutive threads, consecutive words) and the
+// per-row sums (consecutive threads, rows an odd stride apart) are free of
+// bank conflicts.
+__host__ __device__ constexpr int red_stride(int ns) { return 2 * ns + 1; }
+__host__ __device__ constexpr int gu_red_floats(int R, int ns) { return 2 * R * red_stride(ns); }
+__host__ __device__ constexpr int dn_red_floats(int R, int ns, int n_act) { return n_act * R * (red_stride(ns) + 1); }
 
 // silu(g) * u of one row (qwen_moe.c:309)
 __device__ __forceinline__ float swiglu(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
+
+// sum of a row's 2 ns half-slice terms: the first halves, then the second halves
+__device__ __forceinline__ float row_sum(const float *pr, int ns) {
+    float a = 0.f, b = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < ns; ++j) {
+        a += pr[2 * j];
+        b += pr[2 * j + 1];
+    }
+    return a + b;
+}
 
 // Gate and up rows [0, rows) staged at tg / tu (each R rows of rb bytes) dotted
 // with token 0 of xb; thread t < rows gets h for row t (other threads 0).
@@ -304,6 +345,7 @@ template <int QT>
 __device__ __forceinline__ float gate_up_rows(const uint8_t *tg, const uint8_t *tu, int rows, int R, int ns,
                                               const XBuf &xb, float *red, bool ok) {
     constexpr int SB = slice_bytes(QT);
+    const int S = red_stride(ns);
     const int per = rows * ns * 2;   // halves per matrix
     for (int p = threadIdx.x; p < 2 * per; p += blockDim.x) {
         const int mat = p >= per, q = p - mat * per;
@@ -315,29 +357,26 @@ __device__ __forceinline__ float gate_up_rows(const uint8_t *tg, const uint8_t *
             load_half<QT>((mat ? tu : tg) + (long)sp * SB, hf, w);
             v = dot_half<QT>(w, hf, xb.half(0, sl, hf));
         }
-        red[((mat * ns + sl) * 2 + hf) * (R + 1) + r] = v;
+        red[(mat * R + r) * S + 2 * sl + hf] = v;
     }
     __syncthreads();
     float h = 0.f;
-    if (threadIdx.x < rows) {
-        float g = 0.f, u = 0.f;
-        for (int sl = 0; sl < ns; ++sl) {
-            g += red[(sl * 2) * (R + 1) + threadIdx.x] + red[(sl * 2 + 1) * (R + 1) + threadIdx.x];
-            u += red[((ns + sl) * 2) * (R + 1) + threadIdx.x] + red[((ns + sl) * 2 + 1) * (R + 1) + threadIdx.x];
-        }
-        h = swiglu(g, u);
-    }
+    if (threadIdx.x < rows)
+        h = swiglu(row_sum(red + threadIdx.x * S, ns), row_sum(red + (R + threadIdx.x) * S, ns));
     return h;
 }
 
 // Down rows [0, rows) of nl local experts staged at dt + li * R * rb, dotted
 // with token li of xb (h of that expert's slot); thread t < rows gets the
-// weighted sum over li in order (slot order), weight s_w[s_loc[li]].
+// weighted sum over li in order (slot order), weight s_w[s_loc[li]].  The
+// per-expert row sums are formed by nl * rows threads at once.
 template <int QT>
 __device__ __forceinline__ float down_rows(const uint8_t *dt, int nl, int rows, int R, int ns, long rb, const XBuf &xb,
-                                           float *red, bool ok, const int *s_loc, const float *s_w) {
+                                           float *red, int n_act, bool ok, const int *s_loc, const float *s_w) {
     constexpr int SB = slice_bytes(QT);
-    const int per = rows * ns * 2;   // halves per expert
+    const int S = red_stride(ns);
+    float *yv = red + n_act * R * S;   // [expert][row]
+    const int per = rows * ns * 2;     // halves per expert
     for (int p = threadIdx.x; p < nl * per; p += blockDim.x) {
         const int li = p / per, q = p - li * per;
         const int sp = q >> 1, hf = q & 1;
@@ -348,18 +387,17 @@ __device__ __forceinline__ float down_rows(const uint8_t *dt, int nl, int rows, 
             load_half<QT>(dt + li * R * rb + (long)sp * SB, hf, w);
             v = dot_half<QT>(w, hf, xb.half(li, sl, hf));
         }
-        red[((li * ns + sl) * 2 + hf) * (R + 1) + r] = v;
+        red[(li * R + r) * S + 2 * sl + hf] = v;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < nl * rows; t += blockDim.x) {
+        const int li = t / rows, r = t - li * rows;
+        yv[li * R + r] = row_sum(red + (li * R + r) * S, ns);
     }
     __syncthreads();
     float tot = 0.f;
-    if (threadIdx.x < rows) {
-        for (int li = 0; li < nl; ++li) {
-            float y = 0.f;
-            for (int sl = 0; sl < ns; ++sl)
-                y += red[((li * ns + sl) * 2) * (R + 1) + threadIdx.x] + red[((li * ns + sl) * 2 + 1) * (R + 1) + threadIdx.x];
-            tot += s_w[s_loc[li]] * y;   // eout += w_a * y_a in slot order (qwen_moe.c:310)
-        }
-    }
+    if (threadIdx.x < rows)
+        for (int li = 0; li < nl; ++li) tot += s_w[s_loc[li]] * yv[li * R + threadIdx.x];   // eout += w_a * y_a in slot order (qwen_moe.c:310)
     return tot;
 }
 
@@ -377,8 +415,8 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bar;
     __shared__ int abort_flag;
-    __shared__ __align__(16) float s_p[kMaxExp + 8];
-    __shared__ int s_rk[2 * kMaxExp];
+    __shared__ __align__(16) float s_p[kMaxExp + 16];
+    __shared__ int s_rk[4 * kMaxExp];
     __shared__ int s_sel[kMaxAct];
     __shared__ float s_w[kMaxAct], s_wr[kMaxAct];
     const int tok = blockIdx.y / n_act, slot = blockIdx.y % n_act;
@@ -427,8 +465,8 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bar;
     __shared__ int abort_flag;
-    __shared__ __align__(16) float s_p[kMaxExp + 8];
-    __shared__ int s_rk[2 * kMaxExp];
+    __shared__ __align__(16) float s_p[kMaxExp + 16];
+    __shared__ int s_rk[4 * kMaxExp];
     __shared__ int s_sel[kMaxAct], s_loc[kMaxAct];
     __shared__ float s_w[kMaxAct], s_wr[kMaxAct];
     __shared__ int s_nl;
@@ -465,7 +503,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     xprep_rows([h, tok, n_act, ffn, loc](int li) { return h + ((long)tok * n_act + loc[li]) * ffn; }, ffn, nl, xb);
     __syncthreads();
     const bool ok = nl > 0 && mbar_wait(&bar, 0, &abort_flag, status);
-    const float v = down_rows<QT>(dt, nl, rows, TRd, ns, rb, xb, red, ok, s_loc, s_w);
+    const float v = down_rows<QT>(dt, nl, rows, TRd, ns, rb, xb, red, n_act, ok, s_loc, s_w);
     if (threadIdx.x < rows) eout[(long)tok * d + n0 + threadIdx.x] = v;
     if (threadIdx.x == 0 && abort_flag) mbar_wait_drain(&bar, 0, 100000000ull);
 }
@@ -490,7 +528,7 @@ struct FusedArgs {
     const float *hn, *logits;
     float *h;
     int *cnt;
-    int *sel_out;
+    int *sel_out;         // routing result (CTA 0 writes it)
     float *w_out;
     float *eout;
     int *status;
@@ -527,8 +565,8 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bars[kFusedMaxItems];
     __shared__ int abort_flag;
-    __shared__ __align__(16) float s_p[kMaxExp + 8];
-    __shared__ int s_rk[2 * kMaxExp];
+    __shared__ __align__(16) float s_p[kMaxExp + 16];
+    __shared__ int s_rk[4 * kMaxExp];
     __shared__ int s_sel[kMaxAct], s_loc[kMaxAct];
     __shared__ float s_w[kMaxAct], s_wr[kMaxAct];
     __shared__ int s_nl;
@@ -548,15 +586,15 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
     pdl_launch_dependents();
     pdl_wait();                                  // logits and the cleared counter come from the router kernel
     route_fast(a.logits, a.n_exp, a.n_act, s_p, s_rk, s_sel, s_w, s_wr);
+    if (c == 0 && threadIdx.x < a.n_act) {       // routing result for the API
+        a.sel_out[threadIdx.x] = s_sel[threadIdx.x];
+        a.w_out[threadIdx.x] = s_w[threadIdx.x];
+    }
     if (threadIdx.x == 0) {
         int nl = 0;
         for (int s2 = 0; s2 < a.n_act; ++s2)
             if (s_sel[s2] >= a.lo && s_sel[s2] < a.hi) s_loc[nl++] = s2;
         s_nl = nl;
-    }
-    if (c == 0 && threadIdx.x < a.n_act) {
-        a.sel_out[threadIdx.x] = s_sel[threadIdx.x];
-        a.w_out[threadIdx.x] = s_w[threadIdx.x];
     }
     __syncthreads();
     const int nl = s_nl;
@@ -564,8 +602,8 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
     const FusedSplit sp(c, G, n_gu, n_dn, fused_kfill(nl, tbd, 2 * tbg));
     const int gu_n = sp.gu_n();
     const int dn_n = nl > 0 ? sp.dn_n : 0;       // units with no local expert load nothing
-    if (threadIdx.x == 0) {
-        for (int k = 0; k < gu_n; ++k) {
+    if (threadIdx.x < 16) {                      // lanes 0-15 issue the gate/up items
+        for (int k = threadIdx.x; k < gu_n; k += 16) {
             const int i = sp.gu_item(c, G, k);
             const long r0 = (long)(s_sel[s_loc[i / tpg]] - a.lo) * ffn + (i % tpg) * kFR;
             uint8_t *t = tiles + k * 2 * tbg;
@@ -573,7 +611,8 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
             stage_bytes(t, a.gw + r0 * rbg, (uint32_t)tbg, &bars[k]);
             stage_bytes(t + tbg, a.uw + r0 * rbg, (uint32_t)tbg, &bars[k]);
         }
-        for (int k = 0; k < dn_n; ++k) {
+    } else if (threadIdx.x < 32) {               // lanes 16-31 the down units
+        for (int k = threadIdx.x - 16; k < dn_n; k += 16) {
             const int u = sp.dn_unit(c, G, k);
             const int rows = min(kFR, d - u * kFR);
             uint8_t *t = tiles + gu_n * 2 * tbg + k * nl * tbd;
@@ -583,27 +622,46 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
                             (uint32_t)(rows * rbd), &bars[gu_n + k]);
         }
     }
-    // gate / up items: h[li][rows] = silu(gate . hn) * (up . hn)
-    if (gu_n > 0) {
+    // the hidden state is prepared while the copies are in flight
+    {
         const float *hn = a.hn;
         xprep_rows([hn](int) { return hn; }, d, 1, xbuf_at(xbase, nsg));
         __syncthreads();
     }
+    // gate / up items: h[li][rows] = silu(gate . hn) * (up . hn), all items of
+    // this CTA in one pass (their copies were issued together)
     const XBuf xh = xbuf_at(xbase, nsg);
     float *red_g = reinterpret_cast<float *>(xbase + xbuf_bytes(nsg, 1));
-    for (int k = 0; k < gu_n; ++k) {
-        const bool ok = mbar_wait(&bars[k], 0, &abort_flag, a.status);
-        const uint8_t *t = tiles + k * 2 * tbg;
-        const float hv = gate_up_rows<QT>(t, t + tbg, kFR, kFR, nsg, xh, red_g, ok);
-        if (threadIdx.x < kFR) {
+    if (gu_n > 0) {
+        bool ok = true;
+        for (int k = 0; k < gu_n; ++k) ok = mbar_wait(&bars[k], 0, &abort_flag, a.status) && ok;
+        constexpr int SB = slice_bytes(QT);
+        const int S = red_stride(nsg), per = kFR * nsg * 2;   // halves per matrix of an item
+        for (int p = threadIdx.x; p < gu_n * 2 * per; p += blockDim.x) {
+            const int km = p / per, q = p - km * per;          // km = 2 * item + matrix
+            const int sp = q >> 1, hf = q & 1;
+            const int r = sp / nsg, sl = sp - r * nsg;
+            float v = 0.f;
+            if (ok) {
+                WHalf<QT> w;
+                load_half<QT>(tiles + km * tbg + (long)sp * SB, hf, w);
+                v = dot_half<QT>(w, hf, xh.half(0, sl, hf));
+            }
+            red_g[(km * kFR + r) * S + 2 * sl + hf] = v;
+        }
+        __syncthreads();
+        for (int t = threadIdx.x; t < gu_n * kFR; t += blockDim.x) {
+            const int k = t / kFR, r = t - k * kFR;
+            const float hv = swiglu(row_sum(red_g + ((2 * k) * kFR + r) * S, nsg),
+                                    row_sum(red_g + ((2 * k + 1) * kFR + r) * S, nsg));
             const int i = sp.gu_item(c, G, k);
-            a.h[(i / tpg) * ffn + (i % tpg) * kFR + threadIdx.x] = hv;
+            a.h[(i / tpg) * ffn + (i % tpg) * kFR + r] = hv;
             __threadfence();
         }
         __syncthreads();
         if (threadIdx.x == 0) {
             __threadfence();
-            atomicAdd(a.cnt, 1);
+            atomicAdd(a.cnt, gu_n);
         }
     }
     // down units: eout[rows] = sum over local slots (slot order) of w * (down . h)
@@ -622,7 +680,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
             const int rows = min(kFR, d - u * kFR);
             const bool ok = nl > 0 && mbar_wait(&bars[gu_n + k], 0, &abort_flag, a.status);
             const float v = down_rows<QT>(tiles + gu_n * 2 * tbg + k * nl * tbd, nl, rows, kFR, nsd, rbd, xd, red_d,
-                                          ok, s_loc, s_w);
+                                          a.n_act, ok, s_loc, s_w);
             if (threadIdx.x < rows) a.eout[u * kFR + threadIdx.x] = v;
             __syncthreads();
         }
@@ -649,11 +707,11 @@ static int down_rows_per_cta(int qt, int ffn, int n_act) {
 }
 static size_t gate_up_smem(int qt, int d, int TR) {
     const int ns = slices_per_row(d);
-    return 2 * (size_t)TR * row_bytes_dev(qt, d) + xbuf_bytes(ns, 1) + (size_t)2 * ns * 2 * (TR + 1) * 4;
+    return 2 * (size_t)TR * row_bytes_dev(qt, d) + xbuf_bytes(ns, 1) + (size_t)gu_red_floats(TR, ns) * 4;
 }
 static size_t down_smem(int qt, int ffn, int n_act, int TR) {
     const int ns = slices_per_row(ffn);
-    return (size_t)n_act * TR * row_bytes_dev(qt, ffn) + xbuf_bytes(ns, n_act) + (size_t)n_act * ns * 2 * (TR + 1) * 4;
+    return (size_t)n_act * TR * row_bytes_dev(qt, ffn) + xbuf_bytes(ns, n_act) + (size_t)dn_red_floats(TR, ns, n_act) * 4;
 }
 
 bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype) {
@@ -672,7 +730,7 @@ static void fused_plan_impl(MoeLayer &L, int G) {
     const int tbg = kFR * (int)row_bytes_dev(qt, L.d), tbd = kFR * (int)row_bytes_dev(qt, L.ffn);
     const int n_dn = (L.d + kFR - 1) / kFR;
     long maxb = 0;
-    int maxi = 0;
+    int maxi = 0, gu_max = 0;
     for (int nl = 0; nl <= L.n_act; ++nl) {
         const int n_gu = nl * (L.ffn / kFR);
         const int kf = fused_kfill(nl, tbd, 2 * tbg);
@@ -681,11 +739,12 @@ static void fused_plan_impl(MoeLayer &L, int G) {
             const int dn = nl > 0 ? sp.dn_n : 0;
             maxb = std::max(maxb, (long)sp.gu_n() * 2 * tbg + (long)dn * nl * tbd);
             maxi = std::max(maxi, sp.gu_n() + dn);
+            gu_max = std::max(gu_max, sp.gu_n());
         }
     }
     const int nsg = slices_per_row(L.d), nsd = slices_per_row(L.ffn);
-    const size_t xg = (size_t)xbuf_bytes(nsg, 1) + (size_t)2 * nsg * 2 * (kFR + 1) * 4;
-    const size_t xd = (size_t)xbuf_bytes(nsd, L.n_act) + (size_t)L.n_act * nsd * 2 * (kFR + 1) * 4;
+    const size_t xg = (size_t)xbuf_bytes(nsg, 1) + (size_t)std::max(gu_max, 1) * gu_red_floats(kFR, nsg) * 4;
+    const size_t xd = (size_t)xbuf_bytes(nsd, L.n_act) + (size_t)dn_red_floats(kFR, nsd, L.n_act) * 4;
     L.fused_grid = G;
     L.fused_tiles = (int)((maxb + 127) / 128 * 128);
     L.fused_smem = (size_t)L.fused_tiles + std::max(xg, xd);
@@ -699,6 +758,7 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
     static bool attr[64];
     if (!attr[c->device]) {
         set_qkernel_attrs(router_logits_kernel);
+        set_qkernel_attrs(router_topk_kernel);
         set_qkernel_attrs(gate_up_kernel<QT>);
         set_qkernel_attrs(down_kernel<QT>);
         set_qkernel_attrs(moe_fused_kernel<QT>, 220 * 1024);
@@ -979,7 +1039,7 @@ extern "C" int x100q_router_topk_noalloc(const float *router, const float *hn, i
     // the ticket must start at zero; the logits are fully written before use
     if (check_cuda(cudaMemsetAsync(ticket, 0, sizeof(unsigned), s), X100_E_LAUNCH)) return get_error();
     q::router_topk_kernel<<<(n_exp + 7) / 8, 256, 0, s>>>(router, hn, d, n_exp, n_act, batch, logits, sel_out,
-                                                          w_out, ticket);
+                                                          w_out, ticket, (int *)nullptr, 0);
     return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
 }
 

@@ -14,8 +14,8 @@
 // dots half a slice -- half p of the tile is half p % 2 of slice p / 2, which
 // is row (p/2) / ns, slice (p/2) % ns -- against every batch column (exact
 // dp4a int32 sums, one fp32 scale per block), so each weight byte is read
-// from HBM once per call whatever the batch.  Row sums add the halves in
-// order.
+// from HBM once per call whatever the batch.  Row sums add the first halves
+// in slice order, then the second halves.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -53,7 +53,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     const int rows = min(TR, N - row0);
     uint8_t *tile = smem;
     const XBuf xb = xbuf_at(smem + TR * rb, ns);
-    float *red = reinterpret_cast<float *>(smem + TR * rb + xbuf_bytes(ns, B));   // [b][slice][half][row], row stride TR+1
+    float *red = reinterpret_cast<float *>(smem + TR * rb + xbuf_bytes(ns, B));   // [b][row][slice][half], row stride 2ns+1
+    const int S = 2 * ns + 1;
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         abort_flag = 0;
@@ -74,8 +75,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         load_half<QT>(tile + (long)sp * SB, h, w);
 #pragma unroll
         for (int b = 0; b < B; ++b)
-            if (b < batch)
-                red[((b * ns + sl) * 2 + h) * (TR + 1) + r] = ok ? dot_half<QT>(w, h, xb.half(b, sl, h)) : 0.f;
+            if (b < batch) red[(b * TR + r) * S + 2 * sl + h] = ok ? dot_half<QT>(w, h, xb.half(b, sl, h)) : 0.f;
     }
     __syncthreads();
     if (abort_flag) {
@@ -84,10 +84,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     }
     for (int t = threadIdx.x; t < rows * batch; t += blockDim.x) {
         const int b = t / rows, r = t - b * rows;
-        float s = 0.f;
-        for (int sl = 0; sl < ns; ++sl)
-            s += red[((b * ns + sl) * 2) * (TR + 1) + r] + red[((b * ns + sl) * 2 + 1) * (TR + 1) + r];
-        y[(long)b * N + row0 + r] = s;
+        const float *pr = red + (b * TR + r) * S;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll 4
+        for (int sl = 0; sl < ns; ++sl) {
+            s0 += pr[2 * sl];
+            s1 += pr[2 * sl + 1];
+        }
+        y[(long)b * N + row0 + r] = s0 + s1;
     }
 }
 
@@ -137,7 +141,7 @@ static int gemv_rows(int qt, int K) {
 }
 static size_t gemv_smem(int qt, int K, int TR, int B) {
     const int ns = slices_per_row(K);
-    return (size_t)TR * row_bytes_dev(qt, K) + xbuf_bytes(ns, B) + (size_t)B * ns * 2 * (TR + 1) * 4;
+    return (size_t)TR * row_bytes_dev(qt, K) + xbuf_bytes(ns, B) + (size_t)B * TR * (2 * ns + 1) * 4;
 }
 
 template <int QT, int B>
