@@ -339,33 +339,6 @@ __device__ __forceinline__ float row_sum(const float *pr, int ns) {
     return a + b;
 }
 
-// Gate and up rows [0, rows) staged at tg / tu (each R rows of rb bytes) dotted
-// with token 0 of xb; thread t < rows gets h for row t (other threads 0).
-template <int QT>
-__device__ __forceinline__ float gate_up_rows(const uint8_t *tg, const uint8_t *tu, int rows, int R, int ns,
-                                              const XBuf &xb, float *red, bool ok) {
-    constexpr int SB = slice_bytes(QT);
-    const int S = red_stride(ns);
-    const int per = rows * ns * 2;   // halves per matrix
-    for (int p = threadIdx.x; p < 2 * per; p += blockDim.x) {
-        const int mat = p >= per, q = p - mat * per;
-        const int sp = q >> 1, hf = q & 1;
-        const int r = sp / ns, sl = sp - r * ns;
-        float v = 0.f;
-        if (ok) {
-            WHalf<QT> w;
-            load_half<QT>((mat ? tu : tg) + (long)sp * SB, hf, w);
-            v = dot_half<QT>(w, hf, xb.half(0, sl, hf));
-        }
-        red[(mat * R + r) * S + 2 * sl + hf] = v;
-    }
-    __syncthreads();
-    float h = 0.f;
-    if (threadIdx.x < rows)
-        h = swiglu(row_sum(red + threadIdx.x * S, ns), row_sum(red + (R + threadIdx.x) * S, ns));
-    return h;
-}
-
 // Down rows [0, rows) of nl local experts staged at dt + li * R * rb, dotted
 // with token li of xb (h of that expert's slot); thread t < rows gets the
 // weighted sum over li in order (slot order), weight s_w[s_loc[li]].  The
@@ -401,111 +374,182 @@ __device__ __forceinline__ float down_rows(const uint8_t *dt, int nl, int rows, 
     return tot;
 }
 
-// ---- batched path: gate/up kernel + down kernel ------------------------------------------
-// gate_up: grid (row tiles of TRg rows, token x slot).  Each CTA routes its
-// token, stages TRg gate rows and TRg up rows of the selected expert (two bulk
-// copies) and writes h[token][slot][rows] = silu(g) * u.
+// ---- batched path (batch > 1): tokens grouped by expert ---------------------------------
+// Group layout in S.grp: cnt[le] tokens of local expert le (le < n_exp),
+// [n_exp] the number of active experts, [n_exp + 1 + k] the k-th active
+// expert, then pairs[le][16] = token * n_act + slot.  The order of experts
+// and pairs follows the atomics, but every (token, slot) is computed by one
+// CTA and the combine adds the slots in order, so results do not vary.
 constexpr int kMoeThreads = 512;
+__host__ __device__ inline int grp_active(int n_exp) { return n_exp; }
+__host__ __device__ inline int grp_list(int n_exp) { return n_exp + 1; }
+__host__ __device__ inline int grp_pairs(int n_exp, int le) { return 2 * n_exp + 1 + le * kMaxBatch; }
 
-template <int QT>
+// route_group: one CTA per token routes it, appends its local (token, slot)
+// pairs to their experts' lists, and writes its prepared activations to
+// xq (token tok at tok * xbuf_bytes(ns, 1)) once for all experts.
 __global__ void __launch_bounds__(kMoeThreads, 1)
-    gate_up_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
-                   int n_act, int lo, int hi, int TRg, const float *__restrict__ hn, const float *__restrict__ logits,
-                   int *__restrict__ sel_out, float *__restrict__ w_out, float *__restrict__ h, int *status) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ uint64_t bar;
-    __shared__ int abort_flag;
+    route_group_kernel(int d, int n_exp, int n_act, int lo, int hi, const float *__restrict__ hn,
+                       const float *__restrict__ logits, int *__restrict__ sel_out, float *__restrict__ w_out,
+                       int *__restrict__ grp, uint8_t *__restrict__ xq) {
     __shared__ __align__(16) float s_p[kMaxExp + 16];
     __shared__ int s_rk[4 * kMaxExp];
     __shared__ int s_sel[kMaxAct];
     __shared__ float s_w[kMaxAct], s_wr[kMaxAct];
-    const int tok = blockIdx.y / n_act, slot = blockIdx.y % n_act;
+    const int tok = blockIdx.x;
     const int ns = slices_per_row(d);
+    pdl_wait();                                  // logits and the cleared groups come from the router kernel
+    pdl_launch_dependents();
+    route_fast(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_rk, s_sel, s_w, s_wr);
+    if (threadIdx.x < n_act) {
+        const int a = threadIdx.x, e = s_sel[a];
+        sel_out[tok * n_act + a] = e;
+        w_out[tok * n_act + a] = s_w[a];
+        if (e >= lo && e < hi) {
+            const int le = e - lo;
+            const int pos = atomicAdd(&grp[le], 1);
+            grp[grp_pairs(n_exp, le) + pos] = tok * n_act + a;
+            if (pos == 0) grp[grp_list(n_exp) + atomicAdd(&grp[grp_active(n_exp)], 1)] = le;
+        }
+    }
+    xprep_rows([hn, tok, d](int) { return hn + (long)tok * d; }, d, 1,
+               xbuf_at(xq + (size_t)tok * xbuf_bytes(ns, 1), ns));
+}
+
+// gate_up_group: grid (row tiles of TRg rows, active expert k).  Stages the
+// expert's TRg gate rows and TRg up rows once and dots every half-slice with
+// the prepared activations (read through L1) of each token of the expert;
+// writes h[token][slot][rows] = silu(g) * u.
+template <int QT>
+__global__ void __launch_bounds__(kMoeThreads, 1)
+    gate_up_group_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
+                         int n_act, int TRg, const int *__restrict__ grp, const uint8_t *__restrict__ xq,
+                         float *__restrict__ h, int *status) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    __shared__ int s_pair[kMaxBatch];
+    constexpr int SB = slice_bytes(QT);
+    const int k = blockIdx.y;
+    const int ns = slices_per_row(d), xb1 = xbuf_bytes(ns, 1), S = red_stride(ns);
     const long rb = row_bytes_dev(QT, d);
     const int i0 = blockIdx.x * TRg, rows = min(TRg, ffn - i0);
     uint8_t *tg = smem, *tu = smem + TRg * rb;
-    const XBuf xb = xbuf_at(smem + 2 * TRg * rb, ns);
-    float *red = reinterpret_cast<float *>(smem + 2 * TRg * rb + xbuf_bytes(ns, 1));
+    float *red = reinterpret_cast<float *>(smem + 2 * TRg * rb);   // [token][matrix][row][slice][half]
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         abort_flag = 0;
         fence_barrier_init();
     }
-    pdl_wait();                                  // logits come from the router kernel
+    pdl_wait();                                  // groups and activations come from the routing kernel
     pdl_launch_dependents();
-    route_fast(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_rk, s_sel, s_w, s_wr);
-    if (blockIdx.x == 0 && slot == 0 && threadIdx.x < n_act) {   // routing result for the API
-        sel_out[tok * n_act + threadIdx.x] = s_sel[threadIdx.x];
-        w_out[tok * n_act + threadIdx.x] = s_w[threadIdx.x];
-    }
-    const int e = s_sel[slot];
-    if (e < lo || e >= hi) return;               // expert held by another process
+    if (k >= __ldcg(grp + grp_active(n_exp))) return;   // fewer experts are in use
+    const int le = __ldcg(grp + grp_list(n_exp) + k);
+    const int np = __ldcg(grp + le);
+    if (threadIdx.x < np) s_pair[threadIdx.x] = __ldcg(grp + grp_pairs(n_exp, le) + threadIdx.x);
     if (threadIdx.x == 0) {
-        const long r0 = (long)(e - lo) * ffn + i0;
+        const long r0 = (long)le * ffn + i0;
         mbar_arrive_expect_tx(&bar, (uint32_t)(2 * rows * rb));
         stage_bytes(tg, gw + r0 * rb, (uint32_t)(rows * rb), &bar);
         stage_bytes(tu, uw + r0 * rb, (uint32_t)(rows * rb), &bar);
     }
-    xprep_rows([hn, tok, d](int) { return hn + (long)tok * d; }, d, 1, xb);
     __syncthreads();
     const bool ok = mbar_wait(&bar, 0, &abort_flag, status);
-    const float hv = gate_up_rows<QT>(tg, tu, rows, TRg, ns, xb, red, ok);
-    if (threadIdx.x < rows) h[((long)tok * n_act + slot) * ffn + i0 + threadIdx.x] = hv;
+    const int per = rows * ns * 2;   // halves per matrix
+    for (int p = threadIdx.x; p < 2 * per; p += blockDim.x) {
+        const int mat = p >= per, q = p - mat * per;
+        const int sp = q >> 1, hf = q & 1;
+        const int r = sp / ns, sl = sp - r * ns;
+        WHalf<QT> w;
+        if (ok) load_half<QT>((mat ? tu : tg) + (long)sp * SB, hf, w);
+        for (int j = 0; j < np; ++j) {
+            const XBuf xj = xbuf_at(const_cast<uint8_t *>(xq) + (size_t)(s_pair[j] / n_act) * xb1, ns);
+            red[((j * 2 + mat) * TRg + r) * S + 2 * sl + hf] = ok ? dot_half<QT>(w, hf, xj.half(0, sl, hf)) : 0.f;
+        }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < np * rows; t += blockDim.x) {
+        const int j = t / rows, r = t - j * rows;
+        h[(long)s_pair[j] * ffn + i0 + r] =
+            swiglu(row_sum(red + ((2 * j) * TRg + r) * S, ns), row_sum(red + ((2 * j + 1) * TRg + r) * S, ns));
+    }
     if (threadIdx.x == 0 && abort_flag) mbar_wait_drain(&bar, 0, 100000000ull);
 }
 
-// down: grid (row tiles of TRd rows, token).  Each CTA routes its token,
-// stages TRd down rows of every local selected expert (one bulk copy each,
-// issued before waiting for h) and writes eout[token][rows] summed over the
-// slots in order.
+// down_group: grid (row tiles of TRd rows, active expert k).  Stages the
+// expert's TRd down rows once, prepares h of each of its (token, slot) pairs
+// (at most nb, the batch) and writes the unweighted part[token][slot][rows]
+// = down . h.
 template <int QT>
 __global__ void __launch_bounds__(kMoeThreads, 1)
-    down_kernel(const uint8_t *__restrict__ dw, int ffn, int d, int n_exp, int n_act, int lo, int hi, int TRd,
-                const float *__restrict__ h, const float *__restrict__ logits, float *__restrict__ eout, int *status) {
+    down_group_kernel(const uint8_t *__restrict__ dw, int ffn, int d, int n_exp, int TRd, int nb,
+                      const int *__restrict__ grp, const float *__restrict__ h, float *__restrict__ part, int *status) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bar;
     __shared__ int abort_flag;
-    __shared__ __align__(16) float s_p[kMaxExp + 16];
-    __shared__ int s_rk[4 * kMaxExp];
-    __shared__ int s_sel[kMaxAct], s_loc[kMaxAct];
-    __shared__ float s_w[kMaxAct], s_wr[kMaxAct];
-    __shared__ int s_nl;
-    const int tok = blockIdx.y;
-    const int ns = slices_per_row(ffn);
+    __shared__ int s_pair[kMaxBatch];
+    constexpr int SB = slice_bytes(QT);
+    const int k = blockIdx.y;
+    const int ns = slices_per_row(ffn), S = red_stride(ns);
     const long rb = row_bytes_dev(QT, ffn);
     const int n0 = blockIdx.x * TRd, rows = min(TRd, d - n0);
     uint8_t *dt = smem;
-    const XBuf xb = xbuf_at(smem + n_act * TRd * rb, ns);
-    float *red = reinterpret_cast<float *>(smem + n_act * TRd * rb + xbuf_bytes(ns, n_act));
+    const XBuf xb = xbuf_at(smem + TRd * rb, ns);                                     // [pair] prepared h
+    float *red = reinterpret_cast<float *>(smem + TRd * rb + xbuf_bytes(ns, nb));   // [pair][row][slice][half]
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         abort_flag = 0;
         fence_barrier_init();
     }
-    // The router kernel finished before the gate/up kernel let this grid
-    // launch, so the logits may be read before waiting for h.
-    route_fast(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_rk, s_sel, s_w, s_wr);
+    // The routing kernel finished before the gate/up kernel let this grid
+    // launch, so the groups may be read before waiting for h.
+    if (k >= __ldcg(grp + grp_active(n_exp))) return;
+    const int le = __ldcg(grp + grp_list(n_exp) + k);
+    const int np = __ldcg(grp + le);
+    if (threadIdx.x < np) s_pair[threadIdx.x] = __ldcg(grp + grp_pairs(n_exp, le) + threadIdx.x);
     if (threadIdx.x == 0) {
-        int nl = 0;
-        for (int a = 0; a < n_act; ++a)
-            if (s_sel[a] >= lo && s_sel[a] < hi) s_loc[nl++] = a;
-        s_nl = nl;
-        mbar_arrive_expect_tx(&bar, (uint32_t)(nl * rows * rb));
-        for (int li = 0; li < nl; ++li)
-            stage_bytes(dt + li * TRd * rb, dw + ((long)(s_sel[s_loc[li]] - lo) * d + n0) * rb,
-                        (uint32_t)(rows * rb), &bar);
+        mbar_arrive_expect_tx(&bar, (uint32_t)(rows * rb));
+        stage_bytes(dt, dw + ((long)le * d + n0) * rb, (uint32_t)(rows * rb), &bar);
     }
     pdl_launch_dependents();
     pdl_wait();                                  // h comes from the gate/up kernel
     __syncthreads();
-    const int nl = s_nl;
-    const int *loc = s_loc;
-    xprep_rows([h, tok, n_act, ffn, loc](int li) { return h + ((long)tok * n_act + loc[li]) * ffn; }, ffn, nl, xb);
+    const int *pairs = s_pair;
+    xprep_rows([h, pairs, ffn](int j) { return h + (long)pairs[j] * ffn; }, ffn, np, xb);
     __syncthreads();
-    const bool ok = nl > 0 && mbar_wait(&bar, 0, &abort_flag, status);
-    const float v = down_rows<QT>(dt, nl, rows, TRd, ns, rb, xb, red, n_act, ok, s_loc, s_w);
-    if (threadIdx.x < rows) eout[(long)tok * d + n0 + threadIdx.x] = v;
+    const bool ok = mbar_wait(&bar, 0, &abort_flag, status);
+    const int per = rows * ns * 2;
+    for (int p = threadIdx.x; p < per; p += blockDim.x) {
+        const int sp = p >> 1, hf = p & 1;
+        const int r = sp / ns, sl = sp - r * ns;
+        WHalf<QT> w;
+        if (ok) load_half<QT>(dt + (long)sp * SB, hf, w);
+        for (int j = 0; j < np; ++j)
+            red[(j * TRd + r) * S + 2 * sl + hf] = ok ? dot_half<QT>(w, hf, xb.half(j, sl, hf)) : 0.f;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < np * rows; t += blockDim.x) {
+        const int j = t / rows, r = t - j * rows;
+        part[(long)s_pair[j] * d + n0 + r] = row_sum(red + (j * TRd + r) * S, ns);
+    }
     if (threadIdx.x == 0 && abort_flag) mbar_wait_drain(&bar, 0, 100000000ull);
+}
+
+// combine: eout[token][n] = sum over the token's local slots, in slot order,
+// of w * part[token][slot][n] (qwen_moe.c:310); zero if none is local.
+__global__ void __launch_bounds__(256) combine_kernel(int d, int n_act, int lo, int hi, const int *__restrict__ sel,
+                                                      const float *__restrict__ w, const float *__restrict__ part,
+                                                      float *__restrict__ eout) {
+    const int tok = blockIdx.y, n = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_wait();                                  // part comes from the down kernel
+    pdl_launch_dependents();
+    if (n >= d) return;
+    float tot = 0.f;
+    for (int a = 0; a < n_act; ++a) {
+        const int e = __ldcg(sel + tok * n_act + a);
+        if (e >= lo && e < hi) tot += __ldcg(w + tok * n_act + a) * __ldcg(part + ((long)tok * n_act + a) * d + n);
+    }
+    eout[(long)tok * d + n] = tot;
 }
 
 // ---- fused expert kernel (one token) ----------------------------------------------------
@@ -693,25 +737,25 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
 
 using namespace q;
 
-// Rows per CTA of the batched kernels: about one slice per thread, with the
-// staged rows held to a size that lets two CTAs share an SM.
+// Rows per CTA of the batched kernels: about one half-slice per thread, and
+// at most 36 KB of staged rows.
 static int gate_up_rows_per_cta(int qt, int d) {
     const int ns = slices_per_row(d);
     const long rb = row_bytes_dev(qt, d);
     return (int)std::max<long>(1, std::min<long>(kMoeThreads / (4 * ns), 36864 / rb));
 }
-static int down_rows_per_cta(int qt, int ffn, int n_act) {
+static int down_rows_per_cta(int qt, int ffn) {
     const int ns = slices_per_row(ffn);
     const long rb = row_bytes_dev(qt, ffn);
-    return (int)std::max<long>(1, std::min<long>(kMoeThreads / std::max(1, 2 * n_act * ns), 65536 / (n_act * rb)));
+    return (int)std::max<long>(1, std::min<long>(kMoeThreads / (2 * ns), 36864 / rb));
 }
-static size_t gate_up_smem(int qt, int d, int TR) {
+static size_t gate_up_smem(int qt, int d, int TR, int nb) {
     const int ns = slices_per_row(d);
-    return 2 * (size_t)TR * row_bytes_dev(qt, d) + xbuf_bytes(ns, 1) + (size_t)gu_red_floats(TR, ns) * 4;
+    return 2 * (size_t)TR * row_bytes_dev(qt, d) + (size_t)nb * 2 * TR * red_stride(ns) * 4;
 }
-static size_t down_smem(int qt, int ffn, int n_act, int TR) {
+static size_t down_smem(int qt, int ffn, int TR, int nb) {
     const int ns = slices_per_row(ffn);
-    return (size_t)n_act * TR * row_bytes_dev(qt, ffn) + xbuf_bytes(ns, n_act) + (size_t)dn_red_floats(TR, ns, n_act) * 4;
+    return (size_t)TR * row_bytes_dev(qt, ffn) + xbuf_bytes(ns, nb) + (size_t)nb * TR * red_stride(ns) * 4;
 }
 
 bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype) {
@@ -719,8 +763,8 @@ bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype) {
     if (!be || d <= 0 || ffn <= 0 || d % be || ffn % be || d % 32 || ffn % 32 || d / 32 > kMaxDXB || n_exp <= 0 ||
         n_exp > kMaxExp || n_act <= 0 || n_act > kMaxAct || n_act > n_exp)
         return false;
-    return gate_up_smem(qtype, d, gate_up_rows_per_cta(qtype, d)) <= 200 * 1024 &&
-           down_smem(qtype, ffn, n_act, down_rows_per_cta(qtype, ffn, n_act)) <= 200 * 1024;
+    return gate_up_smem(qtype, d, gate_up_rows_per_cta(qtype, d), kMaxBatch) <= 200 * 1024 &&
+           down_smem(qtype, ffn, down_rows_per_cta(qtype, ffn), kMaxBatch) <= 200 * 1024;
 }
 
 static void fused_plan_impl(MoeLayer &L, int G) {
@@ -759,8 +803,10 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
     if (!attr[c->device]) {
         set_qkernel_attrs(router_logits_kernel);
         set_qkernel_attrs(router_topk_kernel);
-        set_qkernel_attrs(gate_up_kernel<QT>);
-        set_qkernel_attrs(down_kernel<QT>);
+        set_qkernel_attrs(route_group_kernel);
+        set_qkernel_attrs(gate_up_group_kernel<QT>);
+        set_qkernel_attrs(down_group_kernel<QT>);
+        set_qkernel_attrs(combine_kernel);
         set_qkernel_attrs(moe_fused_kernel<QT>, 220 * 1024);
         attr[c->device] = true;
     }
@@ -789,17 +835,25 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
         fa.status = c->d_status;
         return launch_pdl(moe_fused_kernel<QT>, dim3(L.fused_grid), dim3(kMoeThreads), L.fused_smem, s, fa);
     }
+    // batch > 1: tokens grouped by expert
     int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2), dim3(64), 0, s, (const float *)L.router, hn,
-                        L.d, L.n_exp, batch, S.logits, (int *)nullptr, 0);
+                        L.d, L.n_exp, batch, S.logits, S.grp, L.n_exp + 1);
     if (st) return st;
-    const int TRg = gate_up_rows_per_cta(QT, L.d), TRd = down_rows_per_cta(QT, L.ffn, L.n_act);
-    st = launch_pdl(gate_up_kernel<QT>, dim3((L.ffn + TRg - 1) / TRg, batch * L.n_act), dim3(kMoeThreads),
-                    gate_up_smem(QT, L.d, TRg), s, (const uint8_t *)L.gate.w, (const uint8_t *)L.up.w, L.ffn, L.d,
-                    L.n_exp, L.n_act, L.lo, L.hi, TRg, hn, (const float *)S.logits, S.sel, S.w, S.h, c->d_status);
+    st = launch_pdl(route_group_kernel, dim3(batch), dim3(kMoeThreads), 0, s, L.d, L.n_exp, L.n_act, L.lo, L.hi, hn,
+                    (const float *)S.logits, S.sel, S.w, S.grp, S.xq);
     if (st) return st;
-    return launch_pdl(down_kernel<QT>, dim3((L.d + TRd - 1) / TRd, batch), dim3(kMoeThreads),
-                      down_smem(QT, L.ffn, L.n_act, TRd), s, (const uint8_t *)L.down.w, L.ffn, L.d, L.n_exp, L.n_act,
-                      L.lo, L.hi, TRd, (const float *)S.h, (const float *)S.logits, eout, c->d_status);
+    const int kmax = std::min(L.hi - L.lo, batch * L.n_act);   // experts that can be in use
+    const int TRg = gate_up_rows_per_cta(QT, L.d), TRd = down_rows_per_cta(QT, L.ffn);
+    st = launch_pdl(gate_up_group_kernel<QT>, dim3((L.ffn + TRg - 1) / TRg, kmax), dim3(kMoeThreads),
+                    gate_up_smem(QT, L.d, TRg, batch), s, (const uint8_t *)L.gate.w, (const uint8_t *)L.up.w, L.ffn,
+                    L.d, L.n_exp, L.n_act, TRg, (const int *)S.grp, (const uint8_t *)S.xq, S.h, c->d_status);
+    if (st) return st;
+    st = launch_pdl(down_group_kernel<QT>, dim3((L.d + TRd - 1) / TRd, kmax), dim3(kMoeThreads),
+                    down_smem(QT, L.ffn, TRd, batch), s, (const uint8_t *)L.down.w, L.ffn, L.d, L.n_exp, TRd, batch,
+                    (const int *)S.grp, (const float *)S.h, S.part, c->d_status);
+    if (st) return st;
+    return launch_pdl(combine_kernel, dim3((L.d + 255) / 256, batch), dim3(256), 0, s, L.d, L.n_act, L.lo, L.hi,
+                      (const int *)S.sel, (const float *)S.w, (const float *)S.part, eout);
 }
 
 int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
@@ -820,17 +874,20 @@ int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *h
 
 void moe_fused_plan(MoeLayer &L, int sm_count) { fused_plan_impl(L, sm_count); }
 
-size_t moe_scratch_bytes(int n_exp, int n_act, int ffn) {
+size_t moe_scratch_bytes(int d, int n_exp, int n_act, int ffn) {
     size_t b = 0;
-    b += (size_t)kMaxBatch * n_exp * 4;           // logits
-    b += (size_t)kMaxBatch * n_act * 4 * 2;       // sel, w
-    b += (size_t)kMaxBatch * n_act * ffn * 4;     // h
-    b += 256 * 6;                                 // alignment, ticket, counter
+    b += (size_t)kMaxBatch * n_exp * 4;                               // logits
+    b += (size_t)kMaxBatch * n_act * 4 * 2;                           // sel, w
+    b += (size_t)kMaxBatch * n_act * ffn * 4;                         // h
+    b += (size_t)(2 * n_exp + 1 + n_exp * kMaxBatch) * 4;             // groups
+    b += (size_t)kMaxBatch * xbuf_bytes(slices_per_row(d), 1);        // prepared activations
+    b += (size_t)kMaxBatch * n_act * d * 4;                           // partial outputs
+    b += 256 * 10;                                                    // alignment, ticket, counter
     return b;
 }
 
 // Carve the scratch regions out of one buffer of moe_scratch_bytes().
-MoeScratch moe_scratch_carve(void *base, int n_exp, int n_act, int ffn) {
+MoeScratch moe_scratch_carve(void *base, int d, int n_exp, int n_act, int ffn) {
     MoeScratch S;
     uintptr_t p = (reinterpret_cast<uintptr_t>(base) + 255) & ~uintptr_t(255);
     auto take = [&](size_t bytes) {
@@ -844,6 +901,9 @@ MoeScratch moe_scratch_carve(void *base, int n_exp, int n_act, int ffn) {
     S.sel = static_cast<int *>(take((size_t)kMaxBatch * n_act * 4));
     S.w = static_cast<float *>(take((size_t)kMaxBatch * n_act * 4));
     S.h = static_cast<float *>(take((size_t)kMaxBatch * n_act * ffn * 4));
+    S.grp = static_cast<int *>(take((size_t)(2 * n_exp + 1 + n_exp * kMaxBatch) * 4));
+    S.xq = static_cast<uint8_t *>(take((size_t)kMaxBatch * xbuf_bytes(slices_per_row(d), 1)));
+    S.part = static_cast<float *>(take((size_t)kMaxBatch * n_act * d * 4));
     return S;
 }
 
@@ -897,14 +957,14 @@ x100q_moe *x100q_moe_create(int d, int n_exp, int n_act, int ffn, int qtype, con
     ok = ok && qmat_upload(c, qtype, ne * ffn, d, u, L.up, c->stream);
     ok = ok && qmat_upload(c, qtype, ne * d, ffn, dn, L.down, c->stream);
     if (ok) {
-        const size_t sb = moe_scratch_bytes(n_exp, n_act, ffn);
+        const size_t sb = moe_scratch_bytes(d, n_exp, n_act, ffn);
         if (fault_injected("alloc") || cudaMalloc(&m->scratch, sb) != cudaSuccess) {
             cudaGetLastError();
             set_error(X100_E_ALLOC);
             ok = false;
         } else {
             cudaMemset(m->scratch, 0, sb);
-            m->S = moe_scratch_carve(m->scratch, n_exp, n_act, ffn);
+            m->S = moe_scratch_carve(m->scratch, d, n_exp, n_act, ffn);
             moe_fused_plan(L, c->sm_count);
         }
     }

@@ -25,7 +25,9 @@ struct MoeLayer {
 };
 
 // Device scratch of one call (batch <= 16): routing logits, selection,
-// weights, SwiGLU intermediates h[token][slot][ffn] and the ticket counter.
+// weights, SwiGLU intermediates h[token][slot][ffn], the counters, and for
+// the batched path the expert groups, the prepared activations of every token
+// and the per-slot partial outputs part[token][slot][d].
 struct MoeScratch {
     unsigned *ticket = nullptr;
     float *logits = nullptr;
@@ -33,13 +35,18 @@ struct MoeScratch {
     float *w = nullptr;
     float *h = nullptr;
     int *cnt = nullptr;   // completion counter of the fused expert kernel
+    // groups: [0, n_exp) tokens per local expert, [n_exp] active experts,
+    // [n_exp + 1, 2 n_exp + 1) active expert list, then pairs[n_exp][16]
+    int *grp = nullptr;
+    uint8_t *xq = nullptr;   // prepared activations, one token after the other
+    float *part = nullptr;
 };
 
 bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype);
 // Fill L.fused_* for a device with sm_count SMs (after the weights are uploaded).
 void moe_fused_plan(MoeLayer &L, int sm_count);
-size_t moe_scratch_bytes(int n_exp, int n_act, int ffn);
-MoeScratch moe_scratch_carve(void *base, int n_exp, int n_act, int ffn);
+size_t moe_scratch_bytes(int d, int n_exp, int n_act, int ffn);
+MoeScratch moe_scratch_carve(void *base, int d, int n_exp, int n_act, int ffn);
 // eout[b][:] for b < batch; hn, eout device pointers; asynchronous on s.
 int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
                cudaStream_t s);
