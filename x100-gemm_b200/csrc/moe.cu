@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
 // the prepared activations (read through L1) of each token of the expert;
 // writes h[token][slot][rows] = silu(g) * u.
 template <int QT>
-__global__ void __launch_bounds__(kMoeThreads, 1)
+__global__ void __launch_bounds__(kMoeThreads, 2)
     gate_up_group_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
                          int n_act, int TRg, const int *__restrict__ grp, const uint8_t *__restrict__ xq,
                          float *__restrict__ h, int *status) {
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
 // (at most nb, the batch) and writes the unweighted part[token][slot][rows]
 // = down . h.
 template <int QT>
-__global__ void __launch_bounds__(kMoeThreads, 1)
+__global__ void __launch_bounds__(kMoeThreads, 2)
     down_group_kernel(const uint8_t *__restrict__ dw, int ffn, int d, int n_exp, int TRd, int nb,
                       const int *__restrict__ grp, const float *__restrict__ h, float *__restrict__ part, int *status) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -738,7 +738,8 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
 using namespace q;
 
 // Rows per CTA of the batched kernels: about one half-slice per thread, and
-// at most 36 KB of staged rows.
+// at most 36 KB (gate/up) or 18 KB (down) of staged rows, so two CTAs share
+// an SM.
 static int gate_up_rows_per_cta(int qt, int d) {
     const int ns = slices_per_row(d);
     const long rb = row_bytes_dev(qt, d);
@@ -747,7 +748,7 @@ static int gate_up_rows_per_cta(int qt, int d) {
 static int down_rows_per_cta(int qt, int ffn) {
     const int ns = slices_per_row(ffn);
     const long rb = row_bytes_dev(qt, ffn);
-    return (int)std::max<long>(1, std::min<long>(kMoeThreads / (2 * ns), 36864 / rb));
+    return (int)std::max<long>(1, std::min<long>(kMoeThreads / (2 * ns), 18432 / rb));
 }
 static size_t gate_up_smem(int qt, int d, int TR, int nb) {
     const int ns = slices_per_row(d);
