@@ -104,7 +104,7 @@ class ClockSampler:
                 self.samples.append((mhz, {k for k, bit in names.items() if rs & bit}))
             except Exception:  # noqa: BLE001 - sampling is best effort
                 pass
-            self.stop_ev.wait(0.005)
+            self.stop_ev.wait(0.001)
 
     def start(self):
         try:
@@ -142,7 +142,7 @@ class ClockSampler:
             for _, r in self.samples:
                 reasons |= r
             return {"sm_mhz": statistics.median([m for m, _ in self.samples]), "sm_max_mhz": self.maxmhz,
-                    "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml 5 ms"}
+                    "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml 1 ms"}
         if not self.proc:
             return None
         self.proc.terminate()
@@ -692,14 +692,15 @@ def bench_moe(args, dist, peaks, peak_src):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(f"moe_b{B}"),
                      "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
-                     "kernel": ("router_logits + moe_fused (2 launches per call)" if B == 1 else "router_logits + gate_up + down (3 launches per call)"),
+                     "kernel": ("router_logits + moe_fused (2 launches per call)" if B == 1 else
+                                "router_logits + route_group + gate_up_group + down_group + combine (5 launches per call)"),
                      "algorithmic_bytes_per_token": alg_tok, "call_us_mean": round(per_call_us, 3),
                      "parity": err},
         "clocks": clocks,
         "e2e": {"value": round(e2e_steps * B / dt, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": 4 * B * d, "d2h_bytes_per_step": 4 * B * d,
                 "api": "x100q_moe_ffn(moe, hn, eout, batch) with pinned host hn, eout (synchronous)"},
-        "gpu_launches": calls * 3,
+        "gpu_launches": calls * (2 if B == 1 else 5),
         "cpu_baseline": cpu,
     }
 

@@ -71,7 +71,7 @@ def test_i8_256_matches_reference_hash(meta):
 
 
 @pytest.mark.parametrize("shape", [(128, 256, 128), (256, 512, 1024), (300, 700, 520), (1, 16, 16),
-                                   (1000, 1000, 1000), (130, 260, 4096), (512, 48, 2048)])
+                                   (1000, 1000, 1000), (130, 260, 4096), (512, 48, 2048), (600, 528, 2912)])
 def test_i8_tc_vs_oracle(shape):
     M, N, K = shape
     A, B, C0, *_ = inputs(M, N, K)
@@ -115,6 +115,25 @@ def test_i8_device_path_large_properties():
     Ah, Bh = A[rows].cpu().numpy(), B.cpu().numpy()
     ref = po.gemm_i8(Ah, Bh, np.zeros((3, N), np.int32), nthreads=8)
     np.testing.assert_array_equal(C2[rows].cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("N", [1024, 2048])
+def test_i8_stream_k_shard_shapes(N):
+    """The column shards of the 8192^3 GEMM on 8 and 4 GPUs leave a partial
+    last wave of output tiles, which the 2-SM kernel splits along K across all
+    CTA pairs (several pieces reduce-added into one C tile).  The result must
+    equal the CUDA-core exact kernel on a non-zero C."""
+    import torch
+    M = K = 8192
+    g = torch.Generator(device="cuda").manual_seed(N)
+    A = torch.randint(-128, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+    B = torch.randint(-128, 128, (K, N), dtype=torch.int8, device="cuda", generator=g)
+    C0 = torch.randint(-2**30, 2**30, (M, N), dtype=torch.int32, device="cuda", generator=g)
+    C1, C2 = C0.clone(), C0.clone()
+    x100b.gemm_dev("gemm_ime_i8_dev", A, B, C1)
+    x100b.gemm_dev("gemm_ref_i8_dev", A, B, C2)
+    x100b.sync()
+    assert torch.equal(C1, C2)
 
 
 def test_i8_device_unaligned_falls_back_exactly():

@@ -62,6 +62,63 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
     nt = r / gm;
 }
 
+// Work list of one CTA pair of the 2-SM kernel.  Whole output tiles come
+// first, tile = pair + j * npairs, for the full waves; with stream-K on, the
+// tiles of the last, partial wave are cut along K instead: their
+// (tile, k-block) units are split into `spairs` contiguous runs of at least
+// kMinSkBlocks k-blocks, one run per pair, so every pair ends at about the
+// same time.  A run can cover the end of one tile and the start of the next;
+// each piece is accumulated in TMEM from zero and added to C by the TMA
+// reduce-add epilogue, whose element-wise integer adds make the result
+// independent of the order in which the pieces land.  Every role of a pair
+// (TMA producer, MMA issuer, epilogue warps) walks the same list.
+constexpr int kMinSkBlocks = 8;
+
+__host__ __device__ inline int sk_pairs(int total, int num_kb, int npairs) {
+    const int rem = total % npairs;
+    const long units = (long)rem * num_kb;
+    const long sp = units / kMinSkBlocks < npairs ? units / kMinSkBlocks : npairs;
+    return (rem > 0 && sp > rem) ? (int)sp : 0;   // no gain unless more pairs than tiles share the tail
+}
+
+struct PairSched {
+    int npairs, pair, num_kb, dp_tiles, j = 0;
+    long it = 0, end = 0;
+    __device__ PairSched(int total, int num_kb_, int npairs_, int pair_, bool sk)
+        : npairs(npairs_), pair(pair_), num_kb(num_kb_), dp_tiles(total) {
+        const int sp = sk ? sk_pairs(total, num_kb, npairs) : 0;
+        if (sp > 0) {
+            const int rem = total % npairs;
+            const long units = (long)rem * num_kb;
+            dp_tiles = total - rem;
+            if (pair < sp) {
+                it = (long)dp_tiles * num_kb + units * pair / sp;
+                end = (long)dp_tiles * num_kb + units * (pair + 1) / sp;
+            }
+        }
+    }
+    // next piece: output tile and its k-blocks [kb0, kb1)
+    __device__ bool next(int &tile, int &kb0, int &kb1) {
+        const int t = pair + j * npairs;
+        if (t < dp_tiles) {
+            ++j;
+            tile = t;
+            kb0 = 0;
+            kb1 = num_kb;
+            return true;
+        }
+        if (it < end) {
+            tile = (int)(it / num_kb);
+            kb0 = (int)(it - (long)tile * num_kb);
+            const long left = end - it;
+            kb1 = left < num_kb - kb0 ? kb0 + (int)left : num_kb;
+            it += kb1 - kb0;
+            return true;
+        }
+        return false;
+    }
+};
+
 // C element update c + acc for each output type (int32 adds wrap modulo 2^32
 // like the CPU reference; fp16 C is widened, added in fp32, rounded once).
 __device__ __forceinline__ int32_t epi_add(int32_t c, uint32_t v) {
@@ -389,7 +446,7 @@ template <int KIND, bool TE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, typename Traits<KIND>::CT *__restrict__ C, int M, int N,
-                    int K, long ldc, int *status) {
+                    int K, long ldc, int sk, int *status) {
     using CT = typename Traits<KIND>::CT;
     constexpr int ES = Traits<KIND>::ES;
     constexpr int BK = 128 / ES;          // K elements per stage
@@ -458,10 +515,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             uint32_t full_l[P_STAGES];
             for (int s = 0; s < P_STAGES; ++s) full_l[s] = mapa_shared(&full[s], 0);
             bool ok = true;
-            for (int tile = pair; tile < total && ok; tile += npairs) {
+            PairSched sched(total, num_kb, npairs, pair, sk != 0);
+            int tile, kb0, kb1;
+            while (ok && sched.next(tile, kb0, kb1)) {
                 int mt, nt;
                 tile_coords(tile, num_m, num_n, mt, nt);
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status)) {
                         ok = false;
                         break;
@@ -508,14 +567,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             for (int b = 0; b < 2; ++b) tfull_p[b] = mapa_shared(&tfull[b], 1);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
-            for (int tile = pair; tile < total && ok; tile += npairs) {
+            PairSched sched(total, num_kb, npairs, pair, sk != 0);
+            int tile, kb0, kb1;
+            while (ok && sched.next(tile, kb0, kb1)) {
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, status)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * TN;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, status)) {
                         ok = false;
                         break;
@@ -527,10 +588,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     for (int k = 0; k < KSTEPS; ++k) {
                         const uint64_t adesc = smem_desc_sw128(a0 + k * 32, 16, 1024);
                         const uint64_t bdesc = smem_desc_sw128(b0 + k * UK * 128, BOX_B_BYTES, 1024);
+                        const uint32_t accum = (kb != kb0 || k) ? 1u : 0u;
                         if (KIND == 0)
-                            umma_i8_pair(d_tmem, adesc, bdesc, IDESC, (kb | k) ? 1u : 0u);
+                            umma_i8_pair(d_tmem, adesc, bdesc, IDESC, accum);
                         else
-                            umma_f16_pair(d_tmem, adesc, bdesc, IDESC, (kb | k) ? 1u : 0u);
+                            umma_f16_pair(d_tmem, adesc, bdesc, IDESC, accum);
                     }
                     umma_commit_pair(smem_u32(&empty[stage]));
                     umma_commit_pair(empty_p[stage]);
@@ -557,7 +619,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         uint8_t *tbuf = smem + P_STAGES * P_STAGE_BYTES + (warp - 2) * 4096;   // 1024-aligned (TE)
         const uint32_t rel[2] = {mapa_shared(&tempty[0], 0), mapa_shared(&tempty[1], 0)};
         uint32_t acc = 0, acc_phase = 0;
-        for (int tile = pair; tile < total; tile += npairs) {
+        PairSched sched(total, num_kb, npairs, pair, sk != 0);
+        int tile, kb0, kb1;
+        while (sched.next(tile, kb0, kb1)) {
             int mt, nt;
             tile_coords(tile, num_m, num_n, mt, nt);
             const int n0 = nt * TN;
@@ -614,9 +678,16 @@ static int launch_te(DevCtx *c, int M, int N, int K, const CUtensorMap &ta, cons
     }
     const int pair_tiles = ((M + 2 * P_ROWS - 1) / (2 * P_ROWS)) * ((N + 2 * P_COLS - 1) / (2 * P_COLS));
     if (!one_sm && pairs_fit[c->device] > 0) {
-        const int pairs = pair_tiles < pairs_fit[c->device] ? pair_tiles : pairs_fit[c->device];
+        // stream-K tail only where the partial sums are exact: int32 C updated
+        // by TMA reduce-add (X100_GEMM_NO_STREAMK=1 keeps whole tiles)
+        static const bool no_sk = getenv("X100_GEMM_NO_STREAMK") != nullptr;
+        const int sk = (KIND == 0 && TE && !no_sk) ? 1 : 0;
+        const int num_kb = (K + 127 / Traits<KIND>::ES) / (128 / Traits<KIND>::ES);
+        const int fit = pairs_fit[c->device];
+        int pairs = pair_tiles < fit ? pair_tiles : fit;
+        if (sk && sk_pairs(pair_tiles, num_kb, fit) > 0) pairs = fit;
         gemm_tc2_kernel<KIND, TE><<<2 * pairs, THREADS, P_SMEM_BYTES, s>>>(ta, tb, tc_, reinterpret_cast<CT *>(C), M,
-                                                                          N, K, ldc, c->d_status);
+                                                                          N, K, ldc, sk, c->d_status);
         return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
     }
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
