@@ -44,10 +44,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="x100", choices=["x100", "reference"])
     ap.add_argument("--workload", default="gemm_i8",
-                    choices=["gemm_i8", "gemm_f16", "gemm_f32", "q4gemv", "moe"])
+                    choices=["gemm_i8", "gemm_f16", "gemm_f32", "q4gemv", "moe", "decode"])
     ap.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workloads")
     ap.add_argument("--batch", type=int, default=1, help="tokens per step for q4gemv / moe")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=48, help="layers of the decode workload")
     return ap.parse_args()
 
 
@@ -427,9 +428,10 @@ def bench_gemm(args, dist, peaks, peak_src):
 
 
 # ---- quantised decode workloads ------------------------------------------------------------
-def wellformed_blocks_dev(qtype, nblocks, gen):
+def wellformed_blocks_dev(qtype, nblocks, gen, on_device=False):
     """Random well-formed GGUF blocks built on the device: random payload
-    bytes, fp16 scales in the range N(0, 0.02) weights give (host copy)."""
+    bytes, fp16 scales in the range N(0, 0.02) weights give (host copy, or
+    the device tensor with on_device)."""
     import numpy as np
     import torch
     bb = {2: 18, 8: 34, 11: 110, 12: 144}[qtype]
@@ -446,6 +448,8 @@ def wellformed_blocks_dev(qtype, nblocks, gen):
         blk[:, 2:4] = f16(0.0, 0.001, False)
     else:
         blk[:, 108:110] = f16(0.0002, 0.002, True)
+    if on_device:
+        return blk.reshape(-1)
     return np.ascontiguousarray(blk.cpu().numpy().reshape(-1))
 
 
@@ -730,6 +734,200 @@ def bench_reference(args):
     }
 
 
+# ---- full decode step ---------------------------------------------------------------------
+DEC = dict(d=2048, n_heads=32, n_kv_heads=4, head_dim=128, vocab=151936, n_exp=128, n_act=8, moe_ffn=768,
+           attn_qtype=8, expert_qtype=11, lm_qtype=8, ctx=4096, rope_base=1e6, eps=1e-6)
+
+
+def bench_decode(args, dist, peaks, peak_src):
+    """a 48-layer Qwen3-30B-A3B-shaped decode step (GQA
+    32/4 heads of 128, RMSNorm, QK-norm, NEOX RoPE 1e6, Q8_0 attention, fp32
+    router, top-8 of 128 Q3_K SwiGLU experts of 768, Q8_0 lm_head over 151936
+    tokens), `batch` sequences each attending over a 4096-position fp16 KV
+    cache (positions 0..4094 random, the step's token at 4095).  All weights
+    random-init on the device.  One step = embed + 48 layers + head for every
+    sequence; expert parallel over N GPUs (each rank holds 128/N experts and
+    sums the experts' outputs with an NCCL all-reduce per layer)."""
+    import numpy as np
+    import torch
+    import x100b
+    B, NL = args.batch, args.layers
+    world, rank = dist.world, dist.rank
+    c = dict(DEC)
+    d, qd, kvd, E, F, V = c["d"], c["n_heads"] * 128, c["n_kv_heads"] * 128, c["n_exp"], c["moe_ffn"], c["vocab"]
+    lo, hi = shard.expert_slice(E, world, rank)
+    m = x100b.Model(n_layers=NL, max_batch=B, expert_lo=lo, expert_hi=hi, **c)
+    gen = torch.Generator(device="cuda").manual_seed(55)
+    blk = lambda qt, n: wellformed_blocks_dev(qt, n, gen, on_device=True)   # noqa: E731
+    nrm = lambda n: (1 + 0.1 * torch.randn(n, device="cuda", generator=gen)).contiguous()   # noqa: E731
+    host_layers = []
+    for li in range(NL):
+        lw = dict(attn_norm=nrm(d), wq=blk(8, qd * d // 32), wk=blk(8, kvd * d // 32), wv=blk(8, kvd * d // 32),
+                  q_norm=nrm(128), k_norm=nrm(128), wo=blk(8, d * qd // 32), ffn_norm=nrm(d),
+                  router=(0.02 * torch.randn((E, d), device="cuda", generator=gen)).contiguous(),
+                  gate=blk(11, E * F * d // 256), up=blk(11, E * F * d // 256), down=blk(11, E * d * F // 256))
+        m.set_layer(li, *(lw[k] for k in ("attn_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo", "ffn_norm",
+                                          "router", "gate", "up", "down")))
+        if li < 2 and world == 1:
+            host_layers.append({k: v.cpu().numpy() for k, v in lw.items()})
+        del lw
+    emb = torch.randn((V, d), device="cuda", generator=gen)
+    out_norm = nrm(d)
+    lm = blk(8, V * d // 32)
+    m.set_output(emb, out_norm, lm)
+    # KV cache: random fp16 for positions 0..4094 of every layer and slot
+    P = c["ctx"] - 1
+    kvk = (torch.randn((c["n_kv_heads"], P, 128), device="cuda", generator=gen)).half()
+    kvv = (torch.randn((c["n_kv_heads"], P, 128), device="cuda", generator=gen)).half()
+    for li in range(NL):
+        for sl in range(B):
+            m.kv_write(li, sl, 0, kvk, kvv)
+    torch.cuda.synchronize()
+    toks = torch.randint(0, V, (B,), dtype=torch.int32, device="cuda", generator=gen)
+    pos = torch.full((B,), P, dtype=torch.int32, device="cuda")
+    h = torch.empty((B, d), device="cuda")
+    logits = torch.empty((B, V), device="cuda")
+    eout = torch.empty((B, d), device="cuda")
+    stream = torch.cuda.Stream()
+    # launches per step: embed, head, and per layer qkv GEMV, attention, Wo GEMV
+    # (two launches above 8 tokens: its 4096-wide activations of 16 tokens
+    # exceed one CTA's shared memory) and the MoE kernels (2 fused, 5 grouped)
+    launches = 2 + NL * (2 + (1 if B <= 8 else 2) + (2 if B == 1 else 5))
+
+    def step():
+        if world == 1:
+            m.forward_dev(toks, h, pos, logits, B)
+            return
+        m.embed_dev(toks, h, B)
+        for li in range(NL):
+            m.layer_dev(li, h, pos, B, eout=eout)
+            dist.pg.all_reduce(eout)
+            h.add_(eout)
+        m.head_dev(h, logits, B)
+
+    # routing of one step (per-layer expert unions for the algorithmic bytes)
+    with torch.cuda.stream(stream):
+        sel = torch.empty((NL, B, c["n_act"]), dtype=torch.int32, device="cuda")
+        m.embed_dev(toks, h, B)
+        for li in range(NL):
+            if world == 1:
+                m.layer_dev(li, h, pos, B, sel=sel[li])
+            else:
+                m.layer_dev(li, h, pos, B, eout=eout, sel=sel[li])
+                dist.pg.all_reduce(eout)
+                h.add_(eout)
+        torch.cuda.synchronize()
+    selh = sel.cpu().numpy()
+    union = [len(set(int(e) for e in selh[li].reshape(-1) if lo <= e < hi)) for li in range(NL)]
+    attn_b = (qd + 2 * kvd) * d // 32 * 34 + d * qd // 32 * 34
+    exp_b = 3 * F * d // 256 * 110
+    kv_b = B * (P + 1) * kvd * 2 * 2
+    norms_b = (2 * d + 2 * 128) * 4
+    step_bytes = sum(attn_b + E * d * 4 + u * exp_b + kv_b + norms_b for u in union) + V * d // 32 * 34 + d * 4 + \
+        B * d * 4
+    with torch.cuda.stream(stream):
+        if world == 1:
+            ms, clocks = timed_graph(step, args.steps, args.warmup, dist, stream)
+        else:
+            for _ in range(args.warmup):
+                step()
+            torch.cuda.synchronize()
+            dist.barrier()
+            clk = ClockSampler(dist.physical_gpu())
+            clk.start()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+            dist.barrier()
+            clocks = clk.stop()
+            ms = dist.max(e0.elapsed_time(e1))
+    step_ms = ms / args.steps
+    tok_s = B / (step_ms / 1e3)
+    gbs = step_bytes / (step_ms / 1e3) / 1e9
+    err = None
+    cpu = None
+    if world == 1:
+        import py_oracle as po   # checker only
+        nt = cpu_threads()
+        kvk_h = kvk.cpu().numpy().view(np.uint16)
+        kvv_h = kvv.cpu().numpy().view(np.uint16)
+        ocfg = dict(c, ctx=c["ctx"])
+
+        def oracle_cache():
+            kc = np.zeros((c["n_kv_heads"], c["ctx"], 128), np.uint16)
+            vc = np.zeros_like(kc)
+            kc[:, :P], vc[:, :P] = kvk_h, kvv_h
+            return kc, vc
+        # parity: layer 0 of slot 0 on the GPU against the oracle
+        with torch.cuda.stream(stream):
+            m.embed_dev(toks, h, B)
+            h0 = h[0].cpu().numpy().copy()
+            m.layer_dev(0, h, pos, B)
+            torch.cuda.synchronize()
+        kc, vc = oracle_cache()
+        href = h0.copy()
+        po.decode_layer(ocfg, host_layers[0], kc, vc, href, P, nthreads=nt)
+        err = po.rel_l2(h[0].cpu().numpy(), href)
+        assert err <= 1e-3, err
+        if not args.no_cpu_baseline:
+            hh = h0.copy()
+            t0 = time.perf_counter()
+            for li in range(2):
+                kc, vc = oracle_cache()
+                po.decode_layer(ocfg, host_layers[li], kc, vc, hh, P, nthreads=nt)
+            t_layers = time.perf_counter() - t0
+            lm_h = lm.cpu().numpy()
+            t0 = time.perf_counter()
+            po.decode_head(dict(c), out_norm.cpu().numpy(), lm_h, hh, nthreads=nt)
+            t_head = time.perf_counter() - t0
+            t_tok = t_layers / 2 * NL + t_head
+            cpu = {"value": round(1.0 / t_tok, 4), "unit": "tokens/s", "cores": nt, "kind": "port",
+                   "sample": f"oracle forward() restatement (qwen_moe_q3k.c:1842-1983) for one token: 2 of the "
+                             f"{NL} layers ({t_layers:.2f} s) + output norm and lm_head ({t_head:.2f} s), "
+                             f"scaled to {NL} layers; GEMV rows over {nt} threads"}
+    # e2e: the synchronous host call (tokens, pos on the host -> logits on the host)
+    e2e = None
+    if world == 1:
+        tok_p = toks.cpu().numpy()
+        pos_p = pos.cpu().numpy()
+        m.forward(tok_p, pos_p)
+        n_e2e = 10
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            m.forward(tok_p, pos_p)
+        dt = time.perf_counter() - t0
+        e2e = {"value": round(n_e2e * B / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8 * B,
+               "d2h_bytes_per_step": 4 * B * V,
+               "api": "x100q_model_forward(model, tokens, pos, logits, batch) with host tokens/pos/logits"}
+    return {
+        "metric": "decode tokens/s (48-layer Qwen3-30B-A3B-shaped step)", "value": round(tok_s, 2),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "q8_0/q3_k weights, fp32 activations, fp16 KV",
+        "data": "synthetic: random well-formed Q8_0 / Q3_K blocks, fp32 router N(0,0.02), norms 1+N(0,0.1), "
+                "embeddings N(0,1), KV cache N(0,1) fp16",
+        "config": {"workload": f"decode step {NL} layers, batch {B}, context 4096, GQA 32/4x128, "
+                               f"Q8_0 attention, 128 Q3_K experts top-8 ffn 768, Q8_0 lm_head 151936",
+                   "batch": B, "layers": NL, "context": P + 1,
+                   "expert_parallel": f"{E // world} experts per GPU",
+                   "l2": f"weights {step_bytes / 2**30:.2f} GiB per step (> L2)",
+                   "graph": "one CUDA graph per step" if world == 1 else "eager + NCCL all-reduce per layer"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
+                     "kernel": "whole step (qgemv, attn_decode, router, moe kernels)",
+                     "algorithmic_bytes_per_step": step_bytes,
+                     "expert_union_mean": round(float(np.mean(union)), 2), "parity_rel_l2_layer0": err},
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": launches * args.steps,
+        "cpu_baseline": cpu,
+    }
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -745,6 +943,8 @@ def main():
             line = bench_gemm(args, dist, peaks, src)
         elif args.workload == "q4gemv":
             line = bench_q4gemv(args, dist, peaks, src)
+        elif args.workload == "decode":
+            line = bench_decode(args, dist, peaks, src)
         else:
             line = bench_moe(args, dist, peaks, src)
     finally:

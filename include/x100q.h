@@ -122,6 +122,86 @@ int x100q_router_topk_noalloc(const float *router, const float *hn, int d, int n
                               int n_act, int batch, int *sel_out, float *w_out,
                               void *stream);
 
+/* ---- decode step of a whole model ----------------------------------------- */
+/* The reference's forward(Model*, tok, pos, Kv*, logits, ...)
+ * (qwen_moe_q3k.c:1842-1983) for a Qwen3-MoE-shaped model: per layer
+ *   hn = rmsnorm(h, attn_norm);  q, k, v = Wq/Wk/Wv . hn;
+ *   q, k per head: rmsnorm(., q_norm / k_norm) then NEOX RoPE (base rope_base);
+ *   k, v stored to the KV cache at pos;  att = softmax(q.K^T / sqrt(hd)) . V
+ *   over positions 0..pos (query head hh uses kv head hh / (n_heads/n_kv_heads));
+ *   h += Wo . att;  h += MoE(rmsnorm(h, ffn_norm))  (the x100q_moe_ffn block);
+ * then logits = Wlm . rmsnorm(h, out_norm).
+ * Differences from the reference, by design: the KV cache is fp16 (the
+ * reference keeps fp32), activations are never int8-packed, and up to
+ * max_batch independent sequences (slots 0..batch-1) advance together.     */
+typedef struct x100q_model x100q_model;
+
+typedef struct {
+    int n_layers, d, n_heads, n_kv_heads, head_dim, vocab;
+    int n_exp, n_act, moe_ffn;
+    int attn_qtype;      /* q/k/v/o weights (Q8_0 in the BASELINE config)       */
+    int expert_qtype;    /* expert gate/up/down (Q3_K)                          */
+    int lm_qtype;        /* lm_head                                             */
+    int ctx;             /* KV positions per sequence                           */
+    int max_batch;       /* sequences stepped together, 1..16                   */
+    int expert_lo, expert_hi;   /* experts held by this process ([0, n_exp): all) */
+    float rope_base, eps;
+} x100q_model_cfg;
+
+/* Allocates the KV caches (2 * n_layers * max_batch * n_kv_heads * ctx *
+ * head_dim fp16, zeroed) and scratch; weights are added with set_layer /
+ * set_output.  head_dim must be 128, n_heads / n_kv_heads <= 8, d and
+ * n_heads * head_dim multiples of 256, ctx <= 131072.                       */
+x100q_model *x100q_model_create(const x100q_model_cfg *cfg);
+void         x100q_model_destroy(x100q_model *m);
+
+/* Weights of one layer (host or device pointers, uploaded once):
+ * attn_norm/ffn_norm fp32 [d]; q_norm/k_norm fp32 [head_dim];
+ * wq [n_heads*head_dim][d], wk/wv [n_kv_heads*head_dim][d],
+ * wo [d][n_heads*head_dim] as GGUF-native attn_qtype blocks;
+ * router fp32 [n_exp][d]; gate/up [n_exp][moe_ffn][d], down [n_exp][d][moe_ffn]
+ * as expert_qtype blocks (only [expert_lo, expert_hi) are kept).            */
+int x100q_model_set_layer(x100q_model *m, int layer, const float *attn_norm,
+                          const void *wq, const void *wk, const void *wv,
+                          const float *q_norm, const float *k_norm, const void *wo,
+                          const float *ffn_norm, const float *router,
+                          const void *gate_exps, const void *up_exps,
+                          const void *down_exps);
+/* tok_embd fp32 [vocab][d] (may be NULL: callers then pass hidden states),
+ * out_norm fp32 [d], lm [vocab][d] lm_qtype blocks (may be NULL: no logits). */
+int x100q_model_set_output(x100q_model *m, const float *tok_embd,
+                           const float *out_norm, const void *lm);
+
+/* Copy positions [pos0, pos0+npos) of sequence slot `slot`, layer `layer`
+ * between the cache and k, v (host or device), each laid out
+ * [n_kv_heads][npos][head_dim] fp16: to_cache = 1 writes the cache (e.g. a
+ * prompt's keys and values), 0 reads it.  Synchronous.                      */
+int x100q_model_kv_copy(x100q_model *m, int layer, int slot, int pos0, int npos,
+                        void *k, void *v, int to_cache);
+
+/* Device-pointer steps, asynchronous on `stream` (calling thread's current
+ * device).  h: [batch][d] residual stream, updated in place; pos: [batch]
+ * positions (each < ctx; a larger one leaves h undefined and makes the next
+ * synchronising call report X100_E_ARG).
+ * layer_dev with eout == NULL adds the MoE output into h (all experts
+ * held); with eout set it writes this process's experts' share to eout
+ * [batch][d] and the caller sums eout over processes and adds it to h.
+ * sel_out / w_out [batch][n_act] (may be NULL) receive the routing.         */
+int x100q_model_embed_dev(x100q_model *m, const int *tokens, float *h, int batch,
+                          void *stream);
+int x100q_model_layer_dev(x100q_model *m, int layer, float *h, const int *pos,
+                          int batch, float *eout, int *sel_out, float *w_out,
+                          void *stream);
+int x100q_model_head_dev(x100q_model *m, const float *h, float *logits, int batch,
+                         void *stream);
+/* embed (when tokens != NULL) + every layer + head (when logits != NULL).   */
+int x100q_model_forward_dev(x100q_model *m, const int *tokens, float *h,
+                            const int *pos, float *logits, int batch, void *stream);
+/* Synchronous host-pointer step: tokens, pos [batch] -> logits [batch][vocab]
+ * (needs tok_embd and lm).                                                  */
+int x100q_model_forward(x100q_model *m, const int *tokens, const int *pos,
+                        float *logits, int batch);
+
 #ifdef __cplusplus
 }
 #endif

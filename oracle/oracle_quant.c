@@ -496,3 +496,89 @@ void orc_fill_u8(uint64_t seed, uint8_t *dst, size_t n)
     uint64_t st = orc_rng_seed(seed);
     for (size_t i = 0; i < n; i++) dst[i] = (uint8_t)orc_rng_u32(&st);
 }
+
+/* ---- one decode step (qwen_moe_q3k.c:1842-1983) ----------------------------
+ * Restates forward()'s per-layer body for one token of one sequence, with
+ * the fp32 router (router mode 0), exact SiLU and a fp16 KV cache: the step's
+ * k and v are rounded to fp16 (round-to-nearest-even) when stored, and the
+ * attention reads every position, the current one included, from the cache.
+ * kc / vc: this layer's cache of this sequence, [nkv][ctx][hd] fp16 bits.
+ * attn_w: the four projections as GGUF-native blocks of attn_qtype:
+ * wq [nh*hd][d], wk / wv [nkv*hd][d], wo [d][nh*hd].  h (d floats) is
+ * updated in place; sel_out / w_out (n_act each, may be NULL) get the
+ * routing.                                                                   */
+void orc_decode_layer(int d, int nh, int nkv, int hd, int ctx, int pos, float rope_base, float eps,
+                      int attn_qtype, const float *attn_norm, const void *wq, const void *wk,
+                      const void *wv, const float *q_norm, const float *k_norm, const void *wo,
+                      const float *ffn_norm, int n_exp, int n_act, int ffn, int expert_qtype,
+                      const float *router, const void *gate_exps, const void *up_exps,
+                      const void *down_exps, uint16_t *kc, uint16_t *vc, float *h,
+                      int *sel_out, float *w_out, int nthreads)
+{
+    const int qd = nh * hd, kvd = nkv * hd, gpr = nh / nkv;
+    float *hn = (float *)malloc((size_t)d * sizeof(float));
+    float *q = (float *)malloc((size_t)qd * sizeof(float));
+    float *k = (float *)malloc((size_t)kvd * sizeof(float));
+    float *v = (float *)malloc((size_t)kvd * sizeof(float));
+    float *att = (float *)malloc((size_t)qd * sizeof(float));
+    float *sc = (float *)malloc((size_t)ctx * sizeof(float));
+    float *tmp = (float *)malloc((size_t)d * sizeof(float));
+    float *kf = (float *)malloc((size_t)hd * sizeof(float));
+    /* :1850-1860 */
+    orc_rmsnorm(hn, h, attn_norm, d, eps);
+    orc_qgemv_mt(attn_qtype, qd, d, wq, hn, q, 1, nthreads);
+    orc_qgemv_mt(attn_qtype, kvd, d, wk, hn, k, 1, nthreads);
+    orc_qgemv_mt(attn_qtype, kvd, d, wv, hn, v, 1, nthreads);
+    /* :1862-1864 */
+    for (int hh = 0; hh < nh; hh++) {
+        orc_rmsnorm(q + hh * hd, q + hh * hd, q_norm, hd, eps);
+        orc_rope_neox(q + hh * hd, hd, pos, rope_base);
+    }
+    for (int hh = 0; hh < nkv; hh++) {
+        orc_rmsnorm(k + hh * hd, k + hh * hd, k_norm, hd, eps);
+        orc_rope_neox(k + hh * hd, hd, pos, rope_base);
+    }
+    /* :1877-1880 head-major cache write */
+    for (int kvh = 0; kvh < nkv; kvh++)
+        for (int t = 0; t < hd; t++) {
+            kc[((size_t)kvh * ctx + pos) * hd + t] = orc_f32_to_f16_rne(k[kvh * hd + t]);
+            vc[((size_t)kvh * ctx + pos) * hd + t] = orc_f32_to_f16_rne(v[kvh * hd + t]);
+        }
+    /* :1890-1899 serial attention */
+    const float scale = 1.0f / sqrtf((float)hd);
+    for (int hh = 0; hh < nh; hh++) {
+        const int kvh = hh / gpr;
+        const float *qh = q + hh * hd;
+        const uint16_t *Kh = kc + (size_t)kvh * ctx * hd, *Vh = vc + (size_t)kvh * ctx * hd;
+        for (int j = 0; j <= pos; j++) {
+            for (int t = 0; t < hd; t++) kf[t] = orc_f16_to_f32(Kh[(size_t)j * hd + t]);
+            float s = 0.f;
+            for (int t = 0; t < hd; t++) s += qh[t] * kf[t];
+            sc[j] = s * scale;
+        }
+        orc_softmax(sc, pos + 1);
+        float *oh = att + hh * hd;
+        for (int t = 0; t < hd; t++) oh[t] = 0.f;
+        for (int j = 0; j <= pos; j++)
+            for (int t = 0; t < hd; t++) oh[t] += sc[j] * orc_f16_to_f32(Vh[(size_t)j * hd + t]);
+    }
+    /* :1912-1915 */
+    orc_qgemv_mt(attn_qtype, d, qd, wo, att, tmp, 1, nthreads);
+    for (int i = 0; i < d; i++) h[i] += tmp[i];
+    /* :1916-1978 */
+    orc_rmsnorm(hn, h, ffn_norm, d, eps);
+    orc_moe_ffn(d, n_exp, n_act, ffn, expert_qtype, router, gate_exps, up_exps, down_exps, 0, n_exp,
+                hn, tmp, 1, sel_out, w_out, nthreads);
+    for (int i = 0; i < d; i++) h[i] += tmp[i];
+    free(hn); free(q); free(k); free(v); free(att); free(sc); free(tmp); free(kf);
+}
+
+/* qwen_moe_q3k.c:1980-1981: logits = lm . rmsnorm(h, out_norm) */
+void orc_decode_head(int d, int vocab, float eps, int lm_qtype, const float *out_norm, const void *lm,
+                     const float *h, float *logits, int nthreads)
+{
+    float *hn = (float *)malloc((size_t)d * sizeof(float));
+    orc_rmsnorm(hn, h, out_norm, d, eps);
+    orc_qgemv_mt(lm_qtype, vocab, d, lm, hn, logits, 1, nthreads);
+    free(hn);
+}

@@ -58,6 +58,9 @@ def lib():
             "orc_moe_ffn": [i, i, i, i, i, vp, vp, vp, vp, i, i, vp, vp, i, vp, vp, i],
             "orc_rmsnorm": [vp, vp, vp, i, f],
             "orc_rope_neox": [vp, i, i, f],
+            "orc_decode_layer": [i, i, i, i, i, i, f, f, i] + [vp] * 8 + [i, i, i, i] + [vp] * 4 +
+                                [vp, vp, vp, vp, vp, i],
+            "orc_decode_head": [i, i, f, i, vp, vp, vp, vp, i],
             "orc_fill_u8": [C.c_uint64, vp, C.c_size_t],
             "orc_kq_scale_min": [i, vp, vp, vp],
         }.items():
@@ -189,3 +192,36 @@ def rel_l2(y, ref) -> float:
     y = np.asarray(y, np.float64)
     ref = np.asarray(ref, np.float64)
     return float(np.linalg.norm(y - ref) / max(np.linalg.norm(ref), 1e-30))
+
+
+# ---- decode step (qwen_moe_q3k.c:1842-1983) ------------------------------------------
+def decode_layer(cfg, lw, kc, vc, h, pos, nthreads=1):
+    """One layer of forward() for one token: cfg is a dict of the model shape
+    (d, n_heads, n_kv_heads, head_dim, ctx, rope_base, eps, attn_qtype, n_exp,
+    n_act, moe_ffn, expert_qtype); lw a dict of the layer's weights (numpy:
+    attn_norm, wq, wk, wv, q_norm, k_norm, wo, ffn_norm, router, gate, up,
+    down); kc / vc uint16 [n_kv_heads][ctx][head_dim] fp16 caches, updated at
+    pos; h [d] float32 updated in place.  Returns (sel, w) of the router."""
+    assert h.dtype == np.float32 and h.flags.c_contiguous
+    assert kc.dtype == np.uint16 and kc.flags.c_contiguous and vc.flags.c_contiguous
+    sel = np.empty(cfg["n_act"], np.int32)
+    w = np.empty(cfg["n_act"], np.float32)
+    c = lambda a: np.ascontiguousarray(a)
+    ws = {k: c(v) for k, v in lw.items()}
+    lib().orc_decode_layer(cfg["d"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], cfg["ctx"], pos,
+                           cfg["rope_base"], cfg["eps"], cfg["attn_qtype"],
+                           *(_ptr(ws[k]) for k in ("attn_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo",
+                                                   "ffn_norm")),
+                           cfg["n_exp"], cfg["n_act"], cfg["moe_ffn"], cfg["expert_qtype"],
+                           *(_ptr(ws[k]) for k in ("router", "gate", "up", "down")),
+                           _ptr(kc), _ptr(vc), _ptr(h), _ptr(sel), _ptr(w), nthreads)
+    return sel, w
+
+
+def decode_head(cfg, out_norm, lm, h, nthreads=1):
+    """logits = lm . rmsnorm(h, out_norm) (qwen_moe_q3k.c:1980-1981)."""
+    logits = np.empty(cfg["vocab"], np.float32)
+    lib().orc_decode_head(cfg["d"], cfg["vocab"], cfg["eps"], cfg["lm_qtype"], _ptr(np.ascontiguousarray(out_norm)),
+                          _ptr(np.ascontiguousarray(lm)), _ptr(np.ascontiguousarray(h, np.float32)),
+                          _ptr(logits), nthreads)
+    return logits

@@ -69,6 +69,18 @@ void orc_moe_ffn(int d, int n_exp, int n_act, int ffn, int qtype,
 /* ---- decode-step pieces (qwen_moe_q3k.c:1166-1175, qwen_moe.c:186-189) -- */
 void orc_rmsnorm(float *o, const float *x, const float *w, int n, float eps);
 void orc_rope_neox(float *v, int hd, int pos, float base);
+/* one layer of forward() for one token (qwen_moe_q3k.c:1849-1978), fp16
+ * KV cache [nkv][ctx][hd] updated at pos; h updated in place              */
+void orc_decode_layer(int d, int nh, int nkv, int hd, int ctx, int pos, float rope_base, float eps,
+                      int attn_qtype, const float *attn_norm, const void *wq, const void *wk,
+                      const void *wv, const float *q_norm, const float *k_norm, const void *wo,
+                      const float *ffn_norm, int n_exp, int n_act, int ffn, int expert_qtype,
+                      const float *router, const void *gate_exps, const void *up_exps,
+                      const void *down_exps, uint16_t *kc, uint16_t *vc, float *h,
+                      int *sel_out, float *w_out, int nthreads);
+/* logits = lm . rmsnorm(h, out_norm)  (qwen_moe_q3k.c:1980-1981)          */
+void orc_decode_head(int d, int vocab, float eps, int lm_qtype, const float *out_norm, const void *lm,
+                     const float *h, float *logits, int nthreads);
 
 /* ---- seeded generators (xorshift64 13/7/17 of bench/q3k_probe.c:403-405) */
 uint64_t orc_rng_seed(uint64_t s);

@@ -166,55 +166,98 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float *__restric
 }
 
 // ---- router logits only + per-CTA routing --------------------------------------------
-// router_logits: one warp per expert row (loaded before waiting on the
-// previous kernel); writes logits[b][e].  The consumers (gate/up and down
-// kernels) each finish the routing themselves with route_cta, so no kernel
-// waits on a last-arriving CTA.
-// When `zero` is set, CTA 0 also clears zero[0 .. nzero) -- the completion
-// counters of the fused expert kernel that follows -- after the previous
+// router_logits: grid (experts / 2, batch); one warp per (expert row, token),
+// the row and (with a norm) the norm weights loaded into registers before
+// waiting on the previous kernel, then the token's 16-byte loads all issued
+// before any arithmetic, so a CTA costs one memory round trip after the
+// wait.  Writes logits[b][e].  The consumers (the expert kernels) finish the
+// routing themselves, so no kernel waits on a last-arriving CTA.
+// When `zero` is set, CTA (0, 0) also clears zero[0 .. nzero) -- the
+// completion counters of the expert kernels that follow -- after the previous
 // kernel on the stream has finished with them.
+// With `nw` set the input is the residual stream: each warp applies the RMS
+// norm of qwen_moe_q3k.c:1166 (x * s * nw, s = 1/sqrt(mean(x^2) + eps)) to
+// its token, and warp 0 of CTA (0, b) writes the normed token b to hn_out for
+// the expert kernels.
 __global__ void __launch_bounds__(64) router_logits_kernel(const float *__restrict__ router,
                                                            const float *__restrict__ hn, int d, int n_exp,
                                                            int batch, float *__restrict__ logits,
-                                                           int *__restrict__ zero, int nzero) {
+                                                           int *__restrict__ zero, int nzero,
+                                                           const float *__restrict__ nw, float eps,
+                                                           float *__restrict__ hn_out) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const int e = blockIdx.x * nwarps + warp;
+    const int e = blockIdx.x * nwarps + warp, b = blockIdx.y;
     constexpr int RV = 16;
-    const int nv = d / 128;
+    const int nv = min(d / 128, RV);
     const float4 *rw = reinterpret_cast<const float4 *>(router + (long)(e < n_exp ? e : 0) * d);
-    float4 r[RV];
+    const float4 *nw4 = reinterpret_cast<const float4 *>(nw);
+    float4 r[RV], w[RV];
 #pragma unroll
-    for (int i = 0; i < RV; ++i)
+    for (int i = 0; i < RV; ++i) {
         if (e < n_exp && i < nv) r[i] = __ldg(rw + lane + 32 * i);
+        if (nw && i < nv) w[i] = __ldg(nw4 + lane + 32 * i);
+    }
     pdl_launch_dependents();
     pdl_wait();
-    if (zero && blockIdx.x == 0)
+    if (zero && blockIdx.x == 0 && blockIdx.y == 0)
         for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
-    if (e >= n_exp) return;
-    for (int b = 0; b < batch; ++b) {
-        const float4 *x = reinterpret_cast<const float4 *>(hn + (long)b * d);
-        float s = 0.f;
+    if (e >= n_exp || b >= batch) return;
+    const float4 *x = reinterpret_cast<const float4 *>(hn + (long)b * d);
+    float4 v[RV];
 #pragma unroll
-        for (int i = 0; i < RV; ++i) {
-            if (i < nv) {
-                const float4 v = __ldg(x + lane + 32 * i);
-                s = fmaf(r[i].x, v.x, s);
-                s = fmaf(r[i].y, v.y, s);
-                s = fmaf(r[i].z, v.z, s);
-                s = fmaf(r[i].w, v.w, s);
-            }
-        }
-        for (int i = lane + 32 * RV; i < d / 4; i += 32) {
-            const float4 rr = __ldg(rw + i), v = __ldg(x + i);
-            s = fmaf(rr.x, v.x, s);
-            s = fmaf(rr.y, v.y, s);
-            s = fmaf(rr.z, v.z, s);
-            s = fmaf(rr.w, v.w, s);
+    for (int i = 0; i < RV; ++i)
+        if (i < nv) v[i] = __ldcg(x + lane + 32 * i);
+    float sc = 1.f;
+    if (nw) {
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < RV; ++i)
+            if (i < nv) q += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+        for (int i = lane + 32 * RV; i < d / 4; i += 32) {   // hidden sizes above 2048
+            const float4 t = __ldcg(x + i);
+            q += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
         }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        if (lane == 0) logits[b * n_exp + e] = s;
+        for (int off = 16; off > 0; off >>= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
+        sc = 1.0f / sqrtf(q / (float)d + eps);
+#pragma unroll
+        for (int i = 0; i < RV; ++i)
+            if (i < nv)
+                v[i] = make_float4(v[i].x * sc * w[i].x, v[i].y * sc * w[i].y, v[i].z * sc * w[i].z,
+                                   v[i].w * sc * w[i].w);
     }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < RV; ++i) {
+        if (i < nv) {
+            s = fmaf(r[i].x, v[i].x, s);
+            s = fmaf(r[i].y, v[i].y, s);
+            s = fmaf(r[i].z, v[i].z, s);
+            s = fmaf(r[i].w, v[i].w, s);
+        }
+    }
+    const bool write_hn = nw && hn_out && blockIdx.x == 0 && warp == 0;
+    for (int i = lane + 32 * RV; i < d / 4; i += 32) {
+        const float4 rr = __ldg(rw + i);
+        float4 t = __ldcg(x + i);
+        if (nw) {
+            const float4 ww = __ldg(nw4 + i);
+            t = make_float4(t.x * sc * ww.x, t.y * sc * ww.y, t.z * sc * ww.z, t.w * sc * ww.w);
+            if (write_hn) reinterpret_cast<float4 *>(hn_out + (long)b * d)[i] = t;
+        }
+        s = fmaf(rr.x, t.x, s);
+        s = fmaf(rr.y, t.y, s);
+        s = fmaf(rr.z, t.z, s);
+        s = fmaf(rr.w, t.w, s);
+    }
+    if (write_hn) {
+#pragma unroll
+        for (int i = 0; i < RV; ++i)
+            if (i < nv) reinterpret_cast<float4 *>(hn_out + (long)b * d)[lane + 32 * i] = v[i];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) logits[b * n_exp + e] = s;
 }
 
 // Softmax over one token's logits, greedy top-k (strict >, lowest index wins)
@@ -539,7 +582,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2)
 // of w * part[token][slot][n] (qwen_moe.c:310); zero if none is local.
 __global__ void __launch_bounds__(256) combine_kernel(int d, int n_act, int lo, int hi, const int *__restrict__ sel,
                                                       const float *__restrict__ w, const float *__restrict__ part,
-                                                      float *__restrict__ eout) {
+                                                      float *__restrict__ eout, int accum) {
     const int tok = blockIdx.y, n = blockIdx.x * blockDim.x + threadIdx.x;
     pdl_wait();                                  // part comes from the down kernel
     pdl_launch_dependents();
@@ -549,7 +592,8 @@ __global__ void __launch_bounds__(256) combine_kernel(int d, int n_act, int lo, 
         const int e = __ldcg(sel + tok * n_act + a);
         if (e >= lo && e < hi) tot += __ldcg(w + tok * n_act + a) * __ldcg(part + ((long)tok * n_act + a) * d + n);
     }
-    eout[(long)tok * d + n] = tot;
+    float *o = eout + (long)tok * d + n;
+    *o = accum ? *o + tot : tot;
 }
 
 // ---- fused expert kernel (one token) ----------------------------------------------------
@@ -575,6 +619,7 @@ struct FusedArgs {
     int *sel_out;         // routing result (CTA 0 writes it)
     float *w_out;
     float *eout;
+    int accum;            // eout += (residual) instead of eout =
     int *status;
 };
 
@@ -725,7 +770,10 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
             const bool ok = nl > 0 && mbar_wait(&bars[gu_n + k], 0, &abort_flag, a.status);
             const float v = down_rows<QT>(tiles + gu_n * 2 * tbg + k * nl * tbd, nl, rows, kFR, nsd, rbd, xd, red_d,
                                           a.n_act, ok, s_loc, s_w);
-            if (threadIdx.x < rows) a.eout[u * kFR + threadIdx.x] = v;
+            if (threadIdx.x < rows) {
+                float *o = a.eout + u * kFR + threadIdx.x;
+                *o = a.accum ? *o + v : v;
+            }
             __syncthreads();
         }
     }
@@ -797,8 +845,11 @@ static void fused_plan_impl(MoeLayer &L, int G) {
 }
 
 template <int QT>
-static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
-                         cudaStream_t s) {
+static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *x, float *eout, int batch,
+                         const MoeOpts &o, cudaStream_t s) {
+    // with a norm the router kernel writes the normed tokens for the experts
+    const float *hn = o.norm_w ? o.hn_out : x;
+    const int accum = o.accum ? 1 : 0;
     static const bool no_fused = getenv("X100_MOE_NO_FUSED") != nullptr;
     static bool attr[64];
     if (!attr[c->device]) {
@@ -812,8 +863,9 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
         attr[c->device] = true;
     }
     if (batch == 1 && L.fused_ok && !no_fused) {
-        int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2), dim3(64), 0, s, (const float *)L.router, hn,
-                            L.d, L.n_exp, 1, S.logits, S.cnt, 1);
+        int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2, 1), dim3(64), 0, s,
+                            (const float *)L.router, x, L.d, L.n_exp, 1, S.logits, S.cnt, 1, o.norm_w, o.eps,
+                            o.hn_out);
         if (st) return st;
         FusedArgs fa;
         fa.gw = L.gate.w;
@@ -833,12 +885,14 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
         fa.sel_out = S.sel;
         fa.w_out = S.w;
         fa.eout = eout;
+        fa.accum = accum;
         fa.status = c->d_status;
         return launch_pdl(moe_fused_kernel<QT>, dim3(L.fused_grid), dim3(kMoeThreads), L.fused_smem, s, fa);
     }
     // batch > 1: tokens grouped by expert
-    int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2), dim3(64), 0, s, (const float *)L.router, hn,
-                        L.d, L.n_exp, batch, S.logits, S.grp, L.n_exp + 1);
+    int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2, batch), dim3(64), 0, s,
+                        (const float *)L.router, x, L.d, L.n_exp, batch, S.logits, S.grp, L.n_exp + 1, o.norm_w,
+                        o.eps, o.hn_out);
     if (st) return st;
     st = launch_pdl(route_group_kernel, dim3(batch), dim3(kMoeThreads), 0, s, L.d, L.n_exp, L.n_act, L.lo, L.hi, hn,
                     (const float *)S.logits, S.sel, S.w, S.grp, S.xq);
@@ -854,26 +908,72 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
                     (const int *)S.grp, (const float *)S.h, S.part, c->d_status);
     if (st) return st;
     return launch_pdl(combine_kernel, dim3((L.d + 255) / 256, batch), dim3(256), 0, s, L.d, L.n_act, L.lo, L.hi,
-                      (const int *)S.sel, (const float *)S.w, (const float *)S.part, eout);
+                      (const int *)S.sel, (const float *)S.w, (const float *)S.part, eout, accum);
 }
 
 int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
                cudaStream_t s) {
-    if (batch < 1 || batch > kMaxBatch) {
+    return launch_moe_ex(c, L, S, hn, eout, batch, MoeOpts(), s);
+}
+
+int launch_moe_ex(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *x, float *eout, int batch,
+                  const MoeOpts &o, cudaStream_t s) {
+    if (batch < 1 || batch > kMaxBatch || (o.norm_w && !o.hn_out)) {
         set_error(X100_E_ARG);
         return X100_E_ARG;
     }
     if (fault_injected("launch")) return X100_E_INJECTED;
     switch (L.qtype) {
-    case Q4_0: return launch_moe_qt<Q4_0>(c, L, S, hn, eout, batch, s);
-    case Q8_0: return launch_moe_qt<Q8_0>(c, L, S, hn, eout, batch, s);
-    case Q4_K: return launch_moe_qt<Q4_K>(c, L, S, hn, eout, batch, s);
-    case Q3_K: return launch_moe_qt<Q3_K>(c, L, S, hn, eout, batch, s);
+    case Q4_0: return launch_moe_qt<Q4_0>(c, L, S, x, eout, batch, o, s);
+    case Q8_0: return launch_moe_qt<Q8_0>(c, L, S, x, eout, batch, o, s);
+    case Q4_K: return launch_moe_qt<Q4_K>(c, L, S, x, eout, batch, o, s);
+    case Q3_K: return launch_moe_qt<Q3_K>(c, L, S, x, eout, batch, o, s);
     default: set_error(X100_E_UNSUPPORTED); return X100_E_UNSUPPORTED;
     }
 }
 
 void moe_fused_plan(MoeLayer &L, int sm_count) { fused_plan_impl(L, sm_count); }
+
+bool moe_layer_upload(DevCtx *c, MoeLayer &L, int d, int n_exp, int n_act, int ffn, int qtype, const float *router,
+                      const void *gate_exps, const void *up_exps, const void *down_exps, int lo, int hi) {
+    L = MoeLayer();
+    L.d = d;
+    L.n_exp = n_exp;
+    L.n_act = n_act;
+    L.ffn = ffn;
+    L.qtype = qtype;
+    L.lo = lo;
+    L.hi = hi;
+    const int ne = hi - lo;
+    const size_t rb_d = x100q_row_bytes(qtype, d), rb_f = x100q_row_bytes(qtype, ffn);
+    const uint8_t *g = static_cast<const uint8_t *>(gate_exps) + (size_t)lo * ffn * rb_d;
+    const uint8_t *u = static_cast<const uint8_t *>(up_exps) + (size_t)lo * ffn * rb_d;
+    const uint8_t *dn = static_cast<const uint8_t *>(down_exps) + (size_t)lo * d * rb_f;
+    bool ok = cudaMalloc(&L.router, (size_t)n_exp * d * 4) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        set_error(X100_E_ALLOC);
+        L.router = nullptr;
+    }
+    ok = ok && check_cuda(cudaMemcpy(L.router, router, (size_t)n_exp * d * 4, cudaMemcpyDefault), X100_E_COPY) == 0;
+    ok = ok && qmat_upload(c, qtype, ne * ffn, d, g, L.gate, c->stream);
+    ok = ok && qmat_upload(c, qtype, ne * ffn, d, u, L.up, c->stream);
+    ok = ok && qmat_upload(c, qtype, ne * d, ffn, dn, L.down, c->stream);
+    if (!ok) {
+        moe_layer_free(L);
+        return false;
+    }
+    moe_fused_plan(L, c->sm_count);
+    return true;
+}
+
+void moe_layer_free(MoeLayer &L) {
+    cudaFree(L.router);
+    cudaFree(L.gate.w);
+    cudaFree(L.up.w);
+    cudaFree(L.down.w);
+    L = MoeLayer();
+}
 
 size_t moe_scratch_bytes(int d, int n_exp, int n_act, int ffn) {
     size_t b = 0;
@@ -935,49 +1035,21 @@ x100q_moe *x100q_moe_create(int d, int n_exp, int n_act, int ffn, int qtype, con
     std::lock_guard<std::mutex> lk(c->mu);
     x100q_moe *m = new x100q_moe();
     m->device = c->device;
-    MoeLayer &L = m->L;
-    L.d = d;
-    L.n_exp = n_exp;
-    L.n_act = n_act;
-    L.ffn = ffn;
-    L.qtype = qtype;
-    L.lo = expert_lo;
-    L.hi = expert_hi;
-    const int ne = expert_hi - expert_lo;
-    const size_t rb_d = x100q_row_bytes(qtype, d), rb_f = x100q_row_bytes(qtype, ffn);
-    const uint8_t *g = static_cast<const uint8_t *>(gate_exps) + (size_t)expert_lo * ffn * rb_d;
-    const uint8_t *u = static_cast<const uint8_t *>(up_exps) + (size_t)expert_lo * ffn * rb_d;
-    const uint8_t *dn = static_cast<const uint8_t *>(down_exps) + (size_t)expert_lo * d * rb_f;
-    bool ok = cudaMalloc(&L.router, (size_t)n_exp * d * 4) == cudaSuccess;
-    if (!ok) {
-        cudaGetLastError();
-        set_error(X100_E_ALLOC);
-    }
-    ok = ok && check_cuda(cudaMemcpy(L.router, router, (size_t)n_exp * d * 4, cudaMemcpyHostToDevice), X100_E_COPY) == 0;
-    ok = ok && qmat_upload(c, qtype, ne * ffn, d, g, L.gate, c->stream);
-    ok = ok && qmat_upload(c, qtype, ne * ffn, d, u, L.up, c->stream);
-    ok = ok && qmat_upload(c, qtype, ne * d, ffn, dn, L.down, c->stream);
-    if (ok) {
-        const size_t sb = moe_scratch_bytes(d, n_exp, n_act, ffn);
-        if (fault_injected("alloc") || cudaMalloc(&m->scratch, sb) != cudaSuccess) {
-            cudaGetLastError();
-            set_error(X100_E_ALLOC);
-            ok = false;
-        } else {
-            cudaMemset(m->scratch, 0, sb);
-            m->S = moe_scratch_carve(m->scratch, d, n_exp, n_act, ffn);
-            moe_fused_plan(L, c->sm_count);
-        }
-    }
-    if (!ok) {
-        cudaFree(L.router);
-        cudaFree(L.gate.w);
-        cudaFree(L.up.w);
-        cudaFree(L.down.w);
-        cudaFree(m->scratch);
+    if (!moe_layer_upload(c, m->L, d, n_exp, n_act, ffn, qtype, router, gate_exps, up_exps, down_exps, expert_lo,
+                          expert_hi)) {
         delete m;
         return nullptr;
     }
+    const size_t sb = moe_scratch_bytes(d, n_exp, n_act, ffn);
+    if (fault_injected("alloc") || cudaMalloc(&m->scratch, sb) != cudaSuccess) {
+        cudaGetLastError();
+        set_error(X100_E_ALLOC);
+        moe_layer_free(m->L);
+        delete m;
+        return nullptr;
+    }
+    cudaMemset(m->scratch, 0, sb);
+    m->S = moe_scratch_carve(m->scratch, d, n_exp, n_act, ffn);
     return m;
 }
 

@@ -50,5 +50,23 @@ MoeScratch moe_scratch_carve(void *base, int d, int n_exp, int n_act, int ffn);
 // eout[b][:] for b < batch; hn, eout device pointers; asynchronous on s.
 int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
                cudaStream_t s);
+// Options of a MoE call inside a decode step: norm_w (d floats) makes the
+// input the residual stream x, RMS-normed by the router kernel into hn_out
+// (batch x d) for the experts; accum adds the block output into eout.
+struct MoeOpts {
+    const float *norm_w = nullptr;
+    float eps = 1e-6f;
+    float *hn_out = nullptr;
+    bool accum = false;
+};
+int launch_moe_ex(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *x, float *eout, int batch,
+                  const MoeOpts &o, cudaStream_t s);
+// Upload router [n_exp][d] and experts [lo, hi) of GGUF-native gate/up/down
+// blocks (host or device pointers, the full [n_exp] tensors) into L and plan
+// the fused kernel; synchronous.  On failure L holds nothing and the error is
+// recorded.
+bool moe_layer_upload(DevCtx *c, MoeLayer &L, int d, int n_exp, int n_act, int ffn, int qtype, const float *router,
+                      const void *gate_exps, const void *up_exps, const void *down_exps, int lo, int hi);
+void moe_layer_free(MoeLayer &L);
 
 }  // namespace x100

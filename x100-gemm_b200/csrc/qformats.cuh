@@ -299,13 +299,24 @@ __device__ __forceinline__ void xprep_vals(const float4 v, XB *o, int t, bool ac
 // costs one memory round trip.  Groups past the end are skipped whole (the
 // test is warp-uniform, which keeps the shuffles legal).  The loads go
 // through L2: the rows may have been written by other CTAs of the grid.
+//
+// RMS-norm folding: with `nw` set, the values prepared are x[k] * nw[k], and
+// each 8-lane group adds the sum of squares of the raw x of its blocks into
+// ss[(warp * 4 + group) * kSsTok + token] (kSsTok tokens per slot; one writer
+// per slot, so no atomics).  The caller sums the slots in a fixed order into
+// s = 1 / sqrt(mean(x^2) + eps) and scales its dot products by s, which gives
+// W . rmsnorm(x) = s * (W . (x * nw)) without a second pass over x.
 constexpr int kXPF = 4;
+constexpr int kSsTok = 16;
 template <class RowPtr>
-__device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const XBuf &xb) {
+__device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const XBuf &xb,
+                                           const float *__restrict__ nw = nullptr, float *ss = nullptr) {
     const int nxb = xb.ns * 8, kb = K / 32;
     const int total = nrows * nxb;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int g = lane >> 3, t = lane & 7;
+    if (nw && t == 0)
+        for (int c = 0; c < nrows; ++c) ss[(warp * 4 + g) * kSsTok + c] = 0.f;
     for (int base = 0; base < total; base += nwarps * 4 * kXPF) {
         float4 v[kXPF];
 #pragma unroll
@@ -324,10 +335,30 @@ __device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const X
                 const int blk = blk0 + g;
                 const bool active = blk < total;
                 const int c = !active || nrows == 1 ? 0 : blk / nxb, j = active ? blk - c * nxb : 0;
-                xprep_vals(v[i], xb.block(c, j), t, active);
+                float4 x = v[i];
+                if (nw) {
+                    float q = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+                    q += __shfl_xor_sync(0xffffffffu, q, 1);
+                    q += __shfl_xor_sync(0xffffffffu, q, 2);
+                    q += __shfl_xor_sync(0xffffffffu, q, 4);
+                    if (active && t == 0) ss[(warp * 4 + g) * kSsTok + c] += q;
+                    if (active && j < kb) {
+                        const float4 w4 = __ldg(reinterpret_cast<const float4 *>(nw + j * 32) + t);
+                        x = make_float4(x.x * w4.x, x.y * w4.y, x.z * w4.z, x.w * w4.w);
+                    }
+                }
+                xprep_vals(x, xb.block(c, j), t, active);
             }
         }
     }
+}
+
+// 1 / sqrt(mean of squares + eps) of token c from the slots xprep_rows filled
+// (nslots = 4 * warps of the CTA), summed in slot order.
+__device__ __forceinline__ float rms_scale(const float *ss, int nslots, int c, int K, float eps) {
+    float s = 0.f;
+    for (int i = 0; i < nslots; ++i) s += ss[i * kSsTok + c];
+    return 1.0f / sqrtf(s / (float)K + eps);
 }
 
 // ---- programmatic dependent launch -------------------------------------------------

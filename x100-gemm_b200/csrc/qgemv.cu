@@ -39,13 +39,19 @@ static bool pdl_enabled_impl() {
 
 constexpr int kGemvThreads = 512;
 
+// With `nw` set the kernel computes y = W . rmsnorm(x; nw, eps) (RMS norm of
+// each token folded into the activation preparation, see xprep_rows); with
+// `accum` set it adds into y (y += W . x: a residual connection).
 template <int QT, int B>
 __global__ void __launch_bounds__(kGemvThreads, 1)
     qgemv_kernel(const uint8_t *__restrict__ W, int N, int K, int TR, const float *__restrict__ x,
-                 float *__restrict__ y, int batch, int *status) {
+                 float *__restrict__ y, int batch, const float *__restrict__ nw, float eps, int accum,
+                 int *status) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bar;
     __shared__ int abort_flag;
+    __shared__ float ss[(kGemvThreads / 32) * 4 * kSsTok];
+    __shared__ float scale[B];
     constexpr int SB = slice_bytes(QT);
     const int ns = slices_per_row(K);
     const int rb = ns * SB;
@@ -64,18 +70,43 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     }
     pdl_launch_dependents();
     pdl_wait();                                   // x may come from the previous kernel
-    xprep_rows([x, K](int c) { return x + (long)c * K; }, K, batch, xb);
+    xprep_rows([x, K](int c) { return x + (long)c * K; }, K, batch, xb, nw, ss);
     __syncthreads();
+    if (threadIdx.x < batch) scale[threadIdx.x] = nw ? rms_scale(ss, blockDim.x / 8, threadIdx.x, K, eps) : 1.0f;
     const bool ok = mbar_wait(&bar, 0, &abort_flag, status);
-    const int nh = rows * ns * 2;
-    for (int p = threadIdx.x; p < nh; p += blockDim.x) {
-        const int sp = p >> 1, h = p & 1;
-        const int r = sp / ns, sl = sp - r * ns;
-        WHalf<QT> w;
-        load_half<QT>(tile + (long)sp * SB, h, w);
+    if constexpr (B == 1) {
+        const int nh = rows * ns * 2;
+        for (int p = threadIdx.x; p < nh; p += blockDim.x) {
+            const int sp = p >> 1, h = p & 1;
+            const int r = sp / ns, sl = sp - r * ns;
+            WHalf<QT> w;
+            load_half<QT>(tile + (long)sp * SB, h, w);
+            red[r * S + 2 * sl + h] = ok ? dot_half<QT>(w, h, xb.half(0, sl, h)) : 0.f;
+        }
+    } else {
+        // two rows per thread: each token's activation half is read from
+        // shared memory once for both rows (the loads are shared by the two
+        // dot products), halving the activation traffic that bounds batches
+        const int hp = ns * 2, rp = (rows + 1) >> 1;
+        for (int p = threadIdx.x; p < rp * hp; p += blockDim.x) {
+            const int rr = p / hp, qh = p - rr * hp;
+            const int sl = qh >> 1, h = qh & 1;
+            const int r0 = 2 * rr, r1 = r0 + 1;
+            const bool two = r1 < rows;
+            WHalf<QT> w0, w1;
+            load_half<QT>(tile + ((long)r0 * ns + sl) * SB, h, w0);
+            load_half<QT>(tile + ((long)(two ? r1 : r0) * ns + sl) * SB, h, w1);
 #pragma unroll
-        for (int b = 0; b < B; ++b)
-            if (b < batch) red[(b * TR + r) * S + 2 * sl + h] = ok ? dot_half<QT>(w, h, xb.half(b, sl, h)) : 0.f;
+            for (int b = 0; b < B; ++b) {
+                if (b < batch) {
+                    const XB *xh = xb.half(b, sl, h);
+                    const float d0 = dot_half<QT>(w0, h, xh);
+                    const float d1 = dot_half<QT>(w1, h, xh);
+                    red[(b * TR + r0) * S + 2 * sl + h] = ok ? d0 : 0.f;
+                    if (two) red[(b * TR + r1) * S + 2 * sl + h] = ok ? d1 : 0.f;
+                }
+            }
+        }
     }
     __syncthreads();
     if (abort_flag) {
@@ -91,7 +122,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
             s0 += pr[2 * sl];
             s1 += pr[2 * sl + 1];
         }
-        y[(long)b * N + row0 + r] = s0 + s1;
+        float *o = y + (long)b * N + row0 + r;
+        const float v = (s0 + s1) * scale[b];
+        *o = accum ? *o + v : v;
     }
 }
 
@@ -131,39 +164,50 @@ __global__ void repack_kernel(int qt, int N, int K, const uint8_t *__restrict__ 
     }
 }
 
-// Rows per CTA: about one half-slice per thread, and at most 40 KB of weights
-// so the next call's CTAs fit beside this call's.
-static int gemv_rows(int qt, int K) {
-    const int ns = slices_per_row(K);
-    const long rb = row_bytes_dev(qt, K);
-    long tr = std::min<long>(kGemvThreads / (2 * ns), 40960 / rb);
-    return (int)std::max<long>(tr, 1);
-}
+constexpr size_t kGemvSmemMax = 220 * 1024;
+
 static size_t gemv_smem(int qt, int K, int TR, int B) {
     const int ns = slices_per_row(K);
     return (size_t)TR * row_bytes_dev(qt, K) + xbuf_bytes(ns, B) + (size_t)B * TR * (2 * ns + 1) * 4;
 }
+// Rows per CTA.  One token: about one half-slice per thread and at most 40 KB
+// of weights, so the next call's CTAs fit beside this call's (the chain of
+// single-token calls overlaps).  Several tokens: every CTA prepares all the
+// tokens' activations, so the rows go to at most one CTA per SM (one wave)
+// when shared memory allows.
+static int gemv_rows(int qt, int N, int K, int B, int sm_count) {
+    const int ns = slices_per_row(K);
+    const long rb = row_bytes_dev(qt, K);
+    long tr = std::max<long>(std::min<long>(kGemvThreads / (2 * ns), 40960 / rb), 1);
+    if (B > 1 && sm_count > 0) {
+        const long wave = (N + sm_count - 1) / sm_count;
+        while (tr < wave && gemv_smem(qt, K, (int)tr + 1, B) <= kGemvSmemMax) ++tr;
+    }
+    return (int)tr;
+}
 
 template <int QT, int B>
-static int launch_B(DevCtx *c, const QMat &m, const float *x, float *y, int batch, cudaStream_t s) {
-    const int TR = gemv_rows(QT, m.K);
+static int launch_B(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
+                    cudaStream_t s) {
+    const int TR = gemv_rows(QT, m.N, m.K, B, c->sm_count);
     const size_t smem = gemv_smem(QT, m.K, TR, B);
     static bool attr[64];
     if (!attr[c->device]) {
-        set_qkernel_attrs(qgemv_kernel<QT, B>);
+        set_qkernel_attrs(qgemv_kernel<QT, B>, (int)kGemvSmemMax);
         attr[c->device] = true;
     }
-    return launch_pdl(qgemv_kernel<QT, B>, dim3((m.N + TR - 1) / TR), dim3(kGemvThreads), smem, s,
-                      (const uint8_t *)m.w, m.N, m.K, TR, x, y, batch, c->d_status);
+    return launch_k(qgemv_kernel<QT, B>, dim3((m.N + TR - 1) / TR), dim3(kGemvThreads), smem, s, o.pdl,
+                    (const uint8_t *)m.w, m.N, m.K, TR, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0,
+                    c->d_status);
 }
 
 template <int QT>
-static int launch_qt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, cudaStream_t s) {
-    const int TR = gemv_rows(QT, m.K);
+static int launch_qt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, GemvOpts o, cudaStream_t s) {
+    const int TR = gemv_rows(QT, m.N, m.K, 1, 0);
     // tokens per launch: the largest template whose shared memory fits
     int bmax = 16;
-    while (bmax > 1 && gemv_smem(QT, m.K, TR, bmax) > 200 * 1024) bmax >>= 1;
-    if (gemv_smem(QT, m.K, TR, bmax) > 200 * 1024) {
+    while (bmax > 1 && gemv_smem(QT, m.K, TR, bmax) > kGemvSmemMax) bmax >>= 1;
+    if (gemv_smem(QT, m.K, TR, bmax) > kGemvSmemMax) {
         set_error(X100_E_UNSUPPORTED);
         return X100_E_UNSUPPORTED;
     }
@@ -172,12 +216,13 @@ static int launch_qt(DevCtx *c, const QMat &m, const float *x, float *y, int bat
         const float *xb = x + (long)b0 * m.K;
         float *yb = y + (long)b0 * m.N;
         int st;
-        if (nb <= 1) st = launch_B<QT, 1>(c, m, xb, yb, nb, s);
-        else if (nb <= 2) st = launch_B<QT, 2>(c, m, xb, yb, nb, s);
-        else if (nb <= 4) st = launch_B<QT, 4>(c, m, xb, yb, nb, s);
-        else if (nb <= 8) st = launch_B<QT, 8>(c, m, xb, yb, nb, s);
-        else st = launch_B<QT, 16>(c, m, xb, yb, nb, s);
+        if (nb <= 1) st = launch_B<QT, 1>(c, m, xb, yb, nb, o, s);
+        else if (nb <= 2) st = launch_B<QT, 2>(c, m, xb, yb, nb, o, s);
+        else if (nb <= 4) st = launch_B<QT, 4>(c, m, xb, yb, nb, o, s);
+        else if (nb <= 8) st = launch_B<QT, 8>(c, m, xb, yb, nb, o, s);
+        else st = launch_B<QT, 16>(c, m, xb, yb, nb, o, s);
         if (st) return st;
+        o.pdl = true;
     }
     return X100_OK;
 }
@@ -216,14 +261,14 @@ bool qmat_upload(DevCtx *c, int qt, int N, int K, const void *blocks, QMat &m, c
         return false;
     }
     if (qt == Q4_K) {   // the native superblocks are already the slices
-        if (check_cuda(cudaMemcpyAsync(m.w, blocks, native, cudaMemcpyHostToDevice, s), X100_E_COPY)) goto fail;
+        if (check_cuda(cudaMemcpyAsync(m.w, blocks, native, cudaMemcpyDefault, s), X100_E_COPY)) goto fail;
     } else {
         if (cudaMalloc(&tmp, native) != cudaSuccess) {
             cudaGetLastError();
             set_error(X100_E_ALLOC);
             goto fail;
         }
-        if (check_cuda(cudaMemcpyAsync(tmp, blocks, native, cudaMemcpyHostToDevice, s), X100_E_COPY)) goto fail;
+        if (check_cuda(cudaMemcpyAsync(tmp, blocks, native, cudaMemcpyDefault, s), X100_E_COPY)) goto fail;
         const long total = (long)N * m.ns;
         repack_kernel<<<(int)std::min<long>((total + 255) / 256, 65535), 256, 0, s>>>(
             qt, N, K, static_cast<const uint8_t *>(tmp), m.w);
@@ -241,16 +286,21 @@ fail:
 }
 
 int launch_qgemv(DevCtx *c, const QMat &m, const float *x, float *y, int batch, cudaStream_t s) {
+    return launch_qgemv_ex(c, m, x, y, batch, GemvOpts(), s);
+}
+
+int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
+                    cudaStream_t s) {
     if (batch < 1 || batch > 16) {
         set_error(X100_E_ARG);
         return X100_E_ARG;
     }
     if (fault_injected("launch")) return X100_E_INJECTED;
     switch (m.qtype) {
-    case Q4_0: return launch_qt<Q4_0>(c, m, x, y, batch, s);
-    case Q8_0: return launch_qt<Q8_0>(c, m, x, y, batch, s);
-    case Q4_K: return launch_qt<Q4_K>(c, m, x, y, batch, s);
-    case Q3_K: return launch_qt<Q3_K>(c, m, x, y, batch, s);
+    case Q4_0: return launch_qt<Q4_0>(c, m, x, y, batch, o, s);
+    case Q8_0: return launch_qt<Q8_0>(c, m, x, y, batch, o, s);
+    case Q4_K: return launch_qt<Q4_K>(c, m, x, y, batch, o, s);
+    case Q3_K: return launch_qt<Q3_K>(c, m, x, y, batch, o, s);
     default: set_error(X100_E_UNSUPPORTED); return X100_E_UNSUPPORTED;
     }
 }

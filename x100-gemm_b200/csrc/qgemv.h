@@ -20,11 +20,22 @@ struct QMat {
 
 size_t qtype_block_elems(int qt);
 size_t qtype_block_bytes(int qt);
-// Upload N rows of GGUF-native blocks (host pointer) and re-lay them out on
-// the device; synchronous on `s`.  Returns false with the error recorded.
+// Upload N rows of GGUF-native blocks (host or device pointer) and re-lay
+// them out on the device; synchronous on `s`.  Returns false with the error
+// recorded.
 bool qmat_upload(DevCtx *c, int qt, int N, int K, const void *blocks, QMat &m, cudaStream_t s);
 // y[b*N + n] = sum_k W[n][k] x[b*K + k], b < batch (<= 16); x, y device.
 int launch_qgemv(DevCtx *c, const QMat &m, const float *x, float *y, int batch, cudaStream_t s);
+// Options of one GEMV launch: norm_w (device, K floats) applies the RMS norm
+// x * nw / sqrt(mean(x^2) + eps) to every token first; accum adds into y.
+struct GemvOpts {
+    const float *norm_w = nullptr;
+    float eps = 1e-6f;
+    bool accum = false;
+    bool pdl = true;   // false: launch behind a full barrier (see launch_k)
+};
+int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
+                    cudaStream_t s);
 
 // Launch `kernel` on `s` with programmatic stream serialization (the kernel
 // may start while the previous kernel of the stream runs; it orders itself
@@ -40,8 +51,11 @@ void set_qkernel_attrs(F *kernel, int smem_max = 200 * 1024) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
     cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
 }
+// launch_k with pdl = false is an ordinary launch: the kernel starts only
+// after all earlier work of the stream has completed (a full barrier).
 template <typename... KArgs, typename... Args>
-int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+int launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+             Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -51,8 +65,12 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
     return check_cuda(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...), X100_E_LAUNCH);
+}
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    return launch_k(kernel, grid, block, smem, s, true, args...);
 }
 
 }  // namespace x100

@@ -77,7 +77,26 @@ _SIGS = {
     "x100q_moe_ffn": ([vp, vp, vp, i32, vp, vp], i32),
     "x100q_moe_ffn_dev": ([vp, vp, vp, i32, vp, vp, vp], i32),
     "x100q_router_topk_noalloc": ([vp, vp, i32, i32, i32, i32, vp, vp, vp], i32),
+    # decode step
+    "x100q_model_create": ([vp], vp),
+    "x100q_model_destroy": ([vp], None),
+    "x100q_model_set_layer": ([vp, i32] + [vp] * 12, i32),
+    "x100q_model_set_output": ([vp, vp, vp, vp], i32),
+    "x100q_model_kv_copy": ([vp, i32, i32, i32, i32, vp, vp, i32], i32),
+    "x100q_model_embed_dev": ([vp, vp, vp, i32, vp], i32),
+    "x100q_model_layer_dev": ([vp, i32, vp, vp, i32, vp, vp, vp, vp], i32),
+    "x100q_model_head_dev": ([vp, vp, vp, i32, vp], i32),
+    "x100q_model_forward_dev": ([vp, vp, vp, vp, vp, i32, vp], i32),
+    "x100q_model_forward": ([vp, vp, vp, vp, i32], i32),
 }
+
+
+class ModelCfg(C.Structure):
+    """x100q_model_cfg (include/x100q.h)."""
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "d", "n_heads", "n_kv_heads", "head_dim", "vocab", "n_exp",
+                                       "n_act", "moe_ffn", "attn_qtype", "expert_qtype", "lm_qtype", "ctx",
+                                       "max_batch", "expert_lo", "expert_hi")] + \
+               [("rope_base", C.c_float), ("eps", C.c_float)]
 
 
 def lib():
@@ -228,6 +247,66 @@ class Moe:
     def close(self):
         if getattr(self, "h", None):
             lib().x100q_moe_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+
+class Model:
+    """x100q_model handle: a Qwen3-MoE-shaped decode model (weights, fp16 KV
+    cache, scratch) resident on the current device."""
+
+    def __init__(self, **cfg):
+        self.cfg = ModelCfg(**cfg)
+        self.h = lib().x100q_model_create(C.byref(self.cfg))
+        if not self.h:
+            check_last("x100q_model_create")
+
+    def set_layer(self, layer, attn_norm, wq, wk, wv, q_norm, k_norm, wo, ffn_norm, router, gate, up, down):
+        check(lib().x100q_model_set_layer(self.h, layer, *(_p(a) for a in (attn_norm, wq, wk, wv, q_norm, k_norm,
+                                                                            wo, ffn_norm, router, gate, up, down))),
+              "x100q_model_set_layer")
+
+    def set_output(self, tok_embd, out_norm, lm):
+        check(lib().x100q_model_set_output(self.h, _p(tok_embd), _p(out_norm), _p(lm)), "x100q_model_set_output")
+
+    def kv_write(self, layer, slot, pos0, k, v):
+        npos = k.shape[1]
+        check(lib().x100q_model_kv_copy(self.h, layer, slot, pos0, npos, _p(k), _p(v), 1), "x100q_model_kv_copy")
+
+    def kv_read(self, layer, slot, pos0, npos):
+        c = self.cfg
+        k = np.empty((c.n_kv_heads, npos, c.head_dim), np.uint16)
+        v = np.empty_like(k)
+        check(lib().x100q_model_kv_copy(self.h, layer, slot, pos0, npos, _p(k), _p(v), 0), "x100q_model_kv_copy")
+        return k, v
+
+    def layer_dev(self, layer, h, pos, batch, eout=None, sel=None, w=None, stream=None):
+        check(lib().x100q_model_layer_dev(self.h, layer, _p(h), _p(pos), batch, _p(eout), _p(sel), _p(w),
+                                          _stream(stream)), "x100q_model_layer_dev")
+
+    def head_dev(self, h, logits, batch, stream=None):
+        check(lib().x100q_model_head_dev(self.h, _p(h), _p(logits), batch, _stream(stream)), "x100q_model_head_dev")
+
+    def embed_dev(self, tokens, h, batch, stream=None):
+        check(lib().x100q_model_embed_dev(self.h, _p(tokens), _p(h), batch, _stream(stream)),
+              "x100q_model_embed_dev")
+
+    def forward_dev(self, tokens, h, pos, logits, batch, stream=None):
+        check(lib().x100q_model_forward_dev(self.h, _p(tokens), _p(h), _p(pos), _p(logits), batch,
+                                            _stream(stream)), "x100q_model_forward_dev")
+
+    def forward(self, tokens, pos):
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        B = tokens.shape[0]
+        logits = np.empty((B, self.cfg.vocab), np.float32)
+        check(lib().x100q_model_forward(self.h, _p(tokens), _p(pos), _p(logits), B), "x100q_model_forward")
+        return logits
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().x100q_model_destroy(self.h)
             self.h = None
 
     __del__ = close
