@@ -434,7 +434,7 @@ __host__ __device__ inline int grp_pairs(int n_exp, int le) { return 2 * n_exp +
 __global__ void __launch_bounds__(kMoeThreads, 1)
     route_group_kernel(int d, int n_exp, int n_act, int lo, int hi, const float *__restrict__ hn,
                        const float *__restrict__ logits, int *__restrict__ sel_out, float *__restrict__ w_out,
-                       int *__restrict__ grp, uint8_t *__restrict__ xq) {
+                       int *__restrict__ grp, uint8_t *__restrict__ xq, int *__restrict__ work) {
     __shared__ __align__(16) float s_p[kMaxExp + 16];
     __shared__ int s_rk[4 * kMaxExp];
     __shared__ int s_sel[kMaxAct];
@@ -443,6 +443,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     const int ns = slices_per_row(d);
     pdl_wait();                                  // logits and the cleared groups come from the router kernel
     pdl_launch_dependents();
+    if (tok == 0 && threadIdx.x < 2) work[threadIdx.x] = 0;   // work counters of the expert kernels
     route_fast(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_rk, s_sel, s_w, s_wr);
     if (threadIdx.x < n_act) {
         const int a = threadIdx.x, e = s_sel[a];
@@ -459,123 +460,221 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
                xbuf_at(xq + (size_t)tok * xbuf_bytes(ns, 1), ns));
 }
 
-// gate_up_group: grid (row tiles of TRg rows, active expert k).  Stages the
-// expert's TRg gate rows and TRg up rows once and dots every half-slice with
-// the prepared activations (read through L1) of each token of the expert;
-// writes h[token][slot][rows] = silu(g) * u.
+// ---- persistent pipelined expert kernels (batch > 1) ------------------------------
+// The work is a list of items (active expert k, row tile t), expert-major.
+// Thread 0 of each CTA claims chunks of kGrab consecutive items from a
+// per-call counter (so CTAs stay balanced whatever the tokens per expert,
+// and an item's neighbours mostly share its expert), and keeps kStages
+// claimed items in flight as bulk copies (one mbarrier per stage, use u of a
+// stage waits parity u & 1) while the CTA computes the oldest.  A stage is
+// refilled only after the barrier that ends the item last held in it.  The
+// routing metadata (active list, counts, pairs) is read into shared memory
+// once per CTA.
+constexpr int kStages = 4;
+constexpr int kGrab = 4;
+
+struct PipeMeta {            // shared-memory copy of the groups
+    int n_active;
+    int list[kMaxExp];       // active local experts
+    int cnt[kMaxExp];        // pairs per active expert (by list index)
+    int pairs[kMaxExp][kMaxBatch];
+};
+
+__device__ __forceinline__ void load_meta(const int *__restrict__ grp, int n_exp, PipeMeta &M) {
+    if (threadIdx.x == 0) M.n_active = __ldcg(grp + grp_active(n_exp));
+    __syncthreads();
+    const int na = M.n_active;
+    for (int k = threadIdx.x; k < na; k += blockDim.x) {
+        const int le = __ldcg(grp + grp_list(n_exp) + k);
+        M.list[k] = le;
+        M.cnt[k] = __ldcg(grp + le);
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < na * kMaxBatch; t += blockDim.x) {
+        const int k = t / kMaxBatch, j = t - k * kMaxBatch;
+        if (j < M.cnt[k]) M.pairs[k][j] = __ldcg(grp + grp_pairs(n_exp, M.list[k]) + j);
+    }
+    __syncthreads();
+}
+
+// gate_up_pipe: items (k, t) with t over ffn / TRg tiles; an item stages TRg
+// gate rows and TRg up rows of expert list[k], dots every half-slice with
+// each of the expert's tokens (prepared activations xq, read through L2) and
+// writes h[pair][rows] = silu(g) * u.
 template <int QT>
-__global__ void __launch_bounds__(kMoeThreads, 2)
-    gate_up_group_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
-                         int n_act, int TRg, const int *__restrict__ grp, const uint8_t *__restrict__ xq,
-                         float *__restrict__ h, int *status) {
+__global__ void __launch_bounds__(kMoeThreads, 1)
+    gate_up_pipe_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
+                        int n_act, int TRg, const int *__restrict__ grp, const uint8_t *__restrict__ xq,
+                        float *__restrict__ h, int *__restrict__ work, int *status) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ uint64_t bar;
+    __shared__ uint64_t full[kStages];
     __shared__ int abort_flag;
-    __shared__ int s_pair[kMaxBatch];
+    __shared__ int s_item[kStages];
+    __shared__ PipeMeta M;
     constexpr int SB = slice_bytes(QT);
-    const int k = blockIdx.y;
     const int ns = slices_per_row(d), xb1 = xbuf_bytes(ns, 1), S = red_stride(ns);
     const long rb = row_bytes_dev(QT, d);
-    const int i0 = blockIdx.x * TRg, rows = min(TRg, ffn - i0);
-    uint8_t *tg = smem, *tu = smem + TRg * rb;
-    float *red = reinterpret_cast<float *>(smem + 2 * TRg * rb);   // [token][matrix][row][slice][half]
+    const int stage_bytes_ = (int)(2 * TRg * rb);
+    float *red = reinterpret_cast<float *>(smem + kStages * stage_bytes_);   // [pair][matrix][row][slice][half]
     if (threadIdx.x == 0) {
-        mbar_init(&bar, 1);
+        for (int st = 0; st < kStages; ++st) mbar_init(&full[st], 1);
         abort_flag = 0;
         fence_barrier_init();
     }
     pdl_wait();                                  // groups and activations come from the routing kernel
     pdl_launch_dependents();
-    if (k >= __ldcg(grp + grp_active(n_exp))) return;   // fewer experts are in use
-    const int le = __ldcg(grp + grp_list(n_exp) + k);
-    const int np = __ldcg(grp + le);
-    if (threadIdx.x < np) s_pair[threadIdx.x] = __ldcg(grp + grp_pairs(n_exp, le) + threadIdx.x);
-    if (threadIdx.x == 0) {
-        const long r0 = (long)le * ffn + i0;
-        mbar_arrive_expect_tx(&bar, (uint32_t)(2 * rows * rb));
-        stage_bytes(tg, gw + r0 * rb, (uint32_t)(rows * rb), &bar);
-        stage_bytes(tu, uw + r0 * rb, (uint32_t)(rows * rb), &bar);
-    }
-    __syncthreads();
-    const bool ok = mbar_wait(&bar, 0, &abort_flag, status);
-    const int per = rows * ns * 2;   // halves per matrix
-    for (int p = threadIdx.x; p < 2 * per; p += blockDim.x) {
-        const int mat = p >= per, q = p - mat * per;
-        const int sp = q >> 1, hf = q & 1;
-        const int r = sp / ns, sl = sp - r * ns;
-        WHalf<QT> w;
-        if (ok) load_half<QT>((mat ? tu : tg) + (long)sp * SB, hf, w);
-        for (int j = 0; j < np; ++j) {
-            const XBuf xj = xbuf_at(const_cast<uint8_t *>(xq) + (size_t)(s_pair[j] / n_act) * xb1, ns);
-            red[((j * 2 + mat) * TRg + r) * S + 2 * sl + hf] = ok ? dot_half<QT>(w, hf, xj.half(0, sl, hf)) : 0.f;
+    load_meta(grp, n_exp, M);
+    const int tiles = (ffn + TRg - 1) / TRg;
+    const int W = M.n_active * tiles;
+    int g_next = 0, g_end = 0;                   // thread 0: the claimed chunk not yet issued
+    auto issue = [&](int i) {                    // thread 0: the next claimed item into stage i % kStages
+        if (g_next == g_end) {
+            g_next = atomicAdd(work, kGrab);
+            g_end = min(g_next + kGrab, W);
         }
-    }
+        const int it = g_next < W ? g_next++ : -1;
+        s_item[i % kStages] = it;
+        if (it < 0) return;
+        const int k = it / tiles, t = it - k * tiles;
+        const int rows = min(TRg, ffn - t * TRg);
+        uint8_t *dst = smem + (i % kStages) * stage_bytes_;
+        const long r0 = (long)M.list[k] * ffn + (long)t * TRg;
+        mbar_arrive_expect_tx(&full[i % kStages], (uint32_t)(2 * rows * rb));
+        stage_bytes(dst, gw + r0 * rb, (uint32_t)(rows * rb), &full[i % kStages]);
+        stage_bytes(dst + TRg * rb, uw + r0 * rb, (uint32_t)(rows * rb), &full[i % kStages]);
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < kStages - 1; ++i) issue(i);
     __syncthreads();
-    for (int t = threadIdx.x; t < np * rows; t += blockDim.x) {
-        const int j = t / rows, r = t - j * rows;
-        h[(long)s_pair[j] * ffn + i0 + r] =
-            swiglu(row_sum(red + ((2 * j) * TRg + r) * S, ns), row_sum(red + ((2 * j + 1) * TRg + r) * S, ns));
+    int done = 0;
+    for (int i = 0;; ++i) {
+        const int it = s_item[i % kStages];      // claimed items form a prefix: -1 ends the loop
+        if (it < 0) break;
+        __syncthreads();                         // everyone has read the slot before it is refilled
+        if (threadIdx.x == 0) issue(i + kStages - 1);
+        const int k = it / tiles, t = it - k * tiles;
+        const int rows = min(TRg, ffn - t * TRg), np = M.cnt[k];
+        const uint8_t *tg = smem + (i % kStages) * stage_bytes_, *tu = tg + TRg * rb;
+        const bool ok = mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1), &abort_flag, status);
+        done = i + 1;
+        const int per = rows * ns * 2;   // halves per matrix
+        for (int p = threadIdx.x; p < 2 * per; p += blockDim.x) {
+            const int mat = p >= per, q = p - mat * per;
+            const int sp = q >> 1, hf = q & 1;
+            const int r = sp / ns, sl = sp - r * ns;
+            WHalf<QT> w;
+            if (ok) load_half<QT>((mat ? tu : tg) + (long)sp * SB, hf, w);
+            for (int j = 0; j < np; ++j) {
+                const XBuf xj = xbuf_at(const_cast<uint8_t *>(xq) + (size_t)(M.pairs[k][j] / n_act) * xb1, ns);
+                red[((j * 2 + mat) * TRg + r) * S + 2 * sl + hf] = ok ? dot_half<QT>(w, hf, xj.half(0, sl, hf)) : 0.f;
+            }
+        }
+        __syncthreads();
+        for (int u = threadIdx.x; u < np * rows; u += blockDim.x) {
+            const int j = u / rows, r = u - j * rows;
+            h[(long)M.pairs[k][j] * ffn + t * TRg + r] =
+                swiglu(row_sum(red + ((2 * j) * TRg + r) * S, ns), row_sum(red + ((2 * j + 1) * TRg + r) * S, ns));
+        }
+        if (__syncthreads_or(abort_flag)) break;   // the same decision in every thread
     }
-    if (threadIdx.x == 0 && abort_flag) mbar_wait_drain(&bar, 0, 100000000ull);
+    if (threadIdx.x == 0 && abort_flag) {        // copies still in flight after a timeout
+        for (int i = done; i < done + kStages - 1; ++i)
+            if (s_item[i % kStages] >= 0)
+                mbar_wait_drain(&full[i % kStages], (uint32_t)((i / kStages) & 1), 100000000ull);
+        if (done > 0) mbar_wait_drain(&full[(done - 1) % kStages], (uint32_t)(((done - 1) / kStages) & 1), 100000000ull);
+    }
 }
 
-// down_group: grid (row tiles of TRd rows, active expert k).  Stages the
-// expert's TRd down rows once, prepares h of each of its (token, slot) pairs
-// (at most nb, the batch) and writes the unweighted part[token][slot][rows]
-// = down . h.
+// down_pipe: items (k, t) with t over d / TRd tiles; an item stages TRd down
+// rows of expert list[k] and writes the unweighted part[pair][rows] =
+// down . h[pair] for each of the expert's pairs.  The expert's h rows are
+// prepared (xprep_rows) once per run of items of the same expert.
 template <int QT>
-__global__ void __launch_bounds__(kMoeThreads, 2)
-    down_group_kernel(const uint8_t *__restrict__ dw, int ffn, int d, int n_exp, int TRd, int nb,
-                      const int *__restrict__ grp, const float *__restrict__ h, float *__restrict__ part, int *status) {
+__global__ void __launch_bounds__(kMoeThreads, 1)
+    down_pipe_kernel(const uint8_t *__restrict__ dw, int ffn, int d, int n_exp, int TRd, int nb,
+                     const int *__restrict__ grp, const float *__restrict__ h, float *__restrict__ part,
+                     int *__restrict__ work, int *status) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ uint64_t bar;
+    __shared__ uint64_t full[kStages];
     __shared__ int abort_flag;
-    __shared__ int s_pair[kMaxBatch];
+    __shared__ int s_item[kStages];
+    __shared__ PipeMeta M;
     constexpr int SB = slice_bytes(QT);
-    const int k = blockIdx.y;
     const int ns = slices_per_row(ffn), S = red_stride(ns);
     const long rb = row_bytes_dev(QT, ffn);
-    const int n0 = blockIdx.x * TRd, rows = min(TRd, d - n0);
-    uint8_t *dt = smem;
-    const XBuf xb = xbuf_at(smem + TRd * rb, ns);                                     // [pair] prepared h
-    float *red = reinterpret_cast<float *>(smem + TRd * rb + xbuf_bytes(ns, nb));   // [pair][row][slice][half]
+    const int stage_bytes_ = (int)(TRd * rb);
+    const XBuf xb = xbuf_at(smem + kStages * stage_bytes_, ns);   // [pair] prepared h of the current expert
+    float *red = reinterpret_cast<float *>(smem + kStages * stage_bytes_ + xbuf_bytes(ns, nb));
     if (threadIdx.x == 0) {
-        mbar_init(&bar, 1);
+        for (int st = 0; st < kStages; ++st) mbar_init(&full[st], 1);
         abort_flag = 0;
         fence_barrier_init();
     }
     // The routing kernel finished before the gate/up kernel let this grid
-    // launch, so the groups may be read before waiting for h.
-    if (k >= __ldcg(grp + grp_active(n_exp))) return;
-    const int le = __ldcg(grp + grp_list(n_exp) + k);
-    const int np = __ldcg(grp + le);
-    if (threadIdx.x < np) s_pair[threadIdx.x] = __ldcg(grp + grp_pairs(n_exp, le) + threadIdx.x);
-    if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(&bar, (uint32_t)(rows * rb));
-        stage_bytes(dt, dw + ((long)le * d + n0) * rb, (uint32_t)(rows * rb), &bar);
-    }
+    // launch, so the groups may be read, and weights staged, before waiting
+    // for h.
+    load_meta(grp, n_exp, M);
+    const int tiles = (d + TRd - 1) / TRd;
+    const int W = M.n_active * tiles;
+    int g_next = 0, g_end = 0;
+    auto issue = [&](int i) {
+        if (g_next == g_end) {
+            g_next = atomicAdd(work, kGrab);
+            g_end = min(g_next + kGrab, W);
+        }
+        const int it = g_next < W ? g_next++ : -1;
+        s_item[i % kStages] = it;
+        if (it < 0) return;
+        const int k = it / tiles, t = it - k * tiles;
+        const int rows = min(TRd, d - t * TRd);
+        mbar_arrive_expect_tx(&full[i % kStages], (uint32_t)(rows * rb));
+        stage_bytes(smem + (i % kStages) * stage_bytes_, dw + ((long)M.list[k] * d + (long)t * TRd) * rb,
+                    (uint32_t)(rows * rb), &full[i % kStages]);
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < kStages - 1; ++i) issue(i);
     pdl_launch_dependents();
     pdl_wait();                                  // h comes from the gate/up kernel
     __syncthreads();
-    const int *pairs = s_pair;
-    xprep_rows([h, pairs, ffn](int j) { return h + (long)pairs[j] * ffn; }, ffn, np, xb);
-    __syncthreads();
-    const bool ok = mbar_wait(&bar, 0, &abort_flag, status);
-    const int per = rows * ns * 2;
-    for (int p = threadIdx.x; p < per; p += blockDim.x) {
-        const int sp = p >> 1, hf = p & 1;
-        const int r = sp / ns, sl = sp - r * ns;
-        WHalf<QT> w;
-        if (ok) load_half<QT>(dt + (long)sp * SB, hf, w);
-        for (int j = 0; j < np; ++j)
-            red[(j * TRd + r) * S + 2 * sl + hf] = ok ? dot_half<QT>(w, hf, xb.half(j, sl, hf)) : 0.f;
+    int done = 0, kprep = -1;
+    for (int i = 0;; ++i) {
+        const int it = s_item[i % kStages];
+        if (it < 0) break;
+        __syncthreads();
+        if (threadIdx.x == 0) issue(i + kStages - 1);
+        const int k = it / tiles, t = it - k * tiles;
+        const int rows = min(TRd, d - t * TRd), np = M.cnt[k];
+        if (k != kprep) {                        // uniform: every thread sees the same item
+            const int *pr = M.pairs[k];
+            xprep_rows([h, pr, ffn](int j) { return h + (long)pr[j] * ffn; }, ffn, np, xb);
+            __syncthreads();
+            kprep = k;
+        }
+        const uint8_t *dt = smem + (i % kStages) * stage_bytes_;
+        const bool ok = mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1), &abort_flag, status);
+        done = i + 1;
+        const int per = rows * ns * 2;
+        for (int p = threadIdx.x; p < per; p += blockDim.x) {
+            const int sp = p >> 1, hf = p & 1;
+            const int r = sp / ns, sl = sp - r * ns;
+            WHalf<QT> w;
+            if (ok) load_half<QT>(dt + (long)sp * SB, hf, w);
+            for (int j = 0; j < np; ++j)
+                red[(j * TRd + r) * S + 2 * sl + hf] = ok ? dot_half<QT>(w, hf, xb.half(j, sl, hf)) : 0.f;
+        }
+        __syncthreads();
+        for (int u = threadIdx.x; u < np * rows; u += blockDim.x) {
+            const int j = u / rows, r = u - j * rows;
+            part[(long)M.pairs[k][j] * d + t * TRd + r] = row_sum(red + (j * TRd + r) * S, ns);
+        }
+        if (__syncthreads_or(abort_flag)) break;   // the same decision in every thread
     }
-    __syncthreads();
-    for (int t = threadIdx.x; t < np * rows; t += blockDim.x) {
-        const int j = t / rows, r = t - j * rows;
-        part[(long)s_pair[j] * d + n0 + r] = row_sum(red + (j * TRd + r) * S, ns);
+    if (threadIdx.x == 0 && abort_flag) {        // copies still in flight after a timeout
+        for (int i = done; i < done + kStages - 1; ++i)
+            if (s_item[i % kStages] >= 0)
+                mbar_wait_drain(&full[i % kStages], (uint32_t)((i / kStages) & 1), 100000000ull);
+        if (done > 0) mbar_wait_drain(&full[(done - 1) % kStages], (uint32_t)(((done - 1) / kStages) & 1), 100000000ull);
     }
-    if (threadIdx.x == 0 && abort_flag) mbar_wait_drain(&bar, 0, 100000000ull);
 }
 
 // combine: eout[token][n] = sum over the token's local slots, in slot order,
@@ -785,26 +884,28 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_fused_kernel(const FusedAr
 
 using namespace q;
 
-// Rows per CTA of the batched kernels: about one half-slice per thread, and
-// at most 36 KB (gate/up) or 18 KB (down) of staged rows, so two CTAs share
-// an SM.
-static int gate_up_rows_per_cta(int qt, int d) {
-    const int ns = slices_per_row(d);
-    const long rb = row_bytes_dev(qt, d);
-    return (int)std::max<long>(1, std::min<long>(kMoeThreads / (4 * ns), 36864 / rb));
-}
-static int down_rows_per_cta(int qt, int ffn) {
-    const int ns = slices_per_row(ffn);
-    const long rb = row_bytes_dev(qt, ffn);
-    return (int)std::max<long>(1, std::min<long>(kMoeThreads / (2 * ns), 18432 / rb));
-}
+// Rows per item of the pipelined batched kernels: about one half-slice per
+// thread (gate and up together for gate/up), with kStages stages, the
+// reduction buffer and (down) the prepared activations within kPipeSmem
+// bytes of dynamic shared memory.
+constexpr size_t kPipeSmem = 180 * 1024;
 static size_t gate_up_smem(int qt, int d, int TR, int nb) {
     const int ns = slices_per_row(d);
-    return 2 * (size_t)TR * row_bytes_dev(qt, d) + (size_t)nb * 2 * TR * red_stride(ns) * 4;
+    return (size_t)kStages * 2 * TR * row_bytes_dev(qt, d) + (size_t)nb * 2 * TR * red_stride(ns) * 4;
 }
 static size_t down_smem(int qt, int ffn, int TR, int nb) {
     const int ns = slices_per_row(ffn);
-    return (size_t)TR * row_bytes_dev(qt, ffn) + xbuf_bytes(ns, nb) + (size_t)nb * TR * red_stride(ns) * 4;
+    return (size_t)kStages * TR * row_bytes_dev(qt, ffn) + xbuf_bytes(ns, nb) + (size_t)nb * TR * red_stride(ns) * 4;
+}
+static int gate_up_rows_per_cta(int qt, int d) {
+    int tr = std::max(1, kMoeThreads / (4 * slices_per_row(d)));
+    while (tr > 1 && gate_up_smem(qt, d, tr, kMaxBatch) > kPipeSmem) --tr;
+    return tr;
+}
+static int down_rows_per_cta(int qt, int ffn) {
+    int tr = std::max(1, kMoeThreads / (2 * slices_per_row(ffn)));
+    while (tr > 1 && down_smem(qt, ffn, tr, kMaxBatch) > kPipeSmem) --tr;
+    return tr;
 }
 
 bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype) {
@@ -812,8 +913,8 @@ bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype) {
     if (!be || d <= 0 || ffn <= 0 || d % be || ffn % be || d % 32 || ffn % 32 || d / 32 > kMaxDXB || n_exp <= 0 ||
         n_exp > kMaxExp || n_act <= 0 || n_act > kMaxAct || n_act > n_exp)
         return false;
-    return gate_up_smem(qtype, d, gate_up_rows_per_cta(qtype, d), kMaxBatch) <= 200 * 1024 &&
-           down_smem(qtype, ffn, down_rows_per_cta(qtype, ffn), kMaxBatch) <= 200 * 1024;
+    return gate_up_smem(qtype, d, gate_up_rows_per_cta(qtype, d), kMaxBatch) <= kPipeSmem &&
+           down_smem(qtype, ffn, down_rows_per_cta(qtype, ffn), kMaxBatch) <= kPipeSmem;
 }
 
 static void fused_plan_impl(MoeLayer &L, int G) {
@@ -856,8 +957,8 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
         set_qkernel_attrs(router_logits_kernel);
         set_qkernel_attrs(router_topk_kernel);
         set_qkernel_attrs(route_group_kernel);
-        set_qkernel_attrs(gate_up_group_kernel<QT>);
-        set_qkernel_attrs(down_group_kernel<QT>);
+        set_qkernel_attrs(gate_up_pipe_kernel<QT>, (int)kPipeSmem);
+        set_qkernel_attrs(down_pipe_kernel<QT>, (int)kPipeSmem);
         set_qkernel_attrs(combine_kernel);
         set_qkernel_attrs(moe_fused_kernel<QT>, 220 * 1024);
         attr[c->device] = true;
@@ -895,17 +996,17 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
                         o.eps, o.hn_out);
     if (st) return st;
     st = launch_pdl(route_group_kernel, dim3(batch), dim3(kMoeThreads), 0, s, L.d, L.n_exp, L.n_act, L.lo, L.hi, hn,
-                    (const float *)S.logits, S.sel, S.w, S.grp, S.xq);
+                    (const float *)S.logits, S.sel, S.w, S.grp, S.xq, S.cnt + 1);
     if (st) return st;
-    const int kmax = std::min(L.hi - L.lo, batch * L.n_act);   // experts that can be in use
     const int TRg = gate_up_rows_per_cta(QT, L.d), TRd = down_rows_per_cta(QT, L.ffn);
-    st = launch_pdl(gate_up_group_kernel<QT>, dim3((L.ffn + TRg - 1) / TRg, kmax), dim3(kMoeThreads),
-                    gate_up_smem(QT, L.d, TRg, batch), s, (const uint8_t *)L.gate.w, (const uint8_t *)L.up.w, L.ffn,
-                    L.d, L.n_exp, L.n_act, TRg, (const int *)S.grp, (const uint8_t *)S.xq, S.h, c->d_status);
+    const int G = c->sm_count;   // persistent: one CTA per SM
+    st = launch_pdl(gate_up_pipe_kernel<QT>, dim3(G), dim3(kMoeThreads), gate_up_smem(QT, L.d, TRg, batch), s,
+                    (const uint8_t *)L.gate.w, (const uint8_t *)L.up.w, L.ffn, L.d, L.n_exp, L.n_act, TRg,
+                    (const int *)S.grp, (const uint8_t *)S.xq, S.h, S.cnt + 1, c->d_status);
     if (st) return st;
-    st = launch_pdl(down_group_kernel<QT>, dim3((L.d + TRd - 1) / TRd, kmax), dim3(kMoeThreads),
-                    down_smem(QT, L.ffn, TRd, batch), s, (const uint8_t *)L.down.w, L.ffn, L.d, L.n_exp, TRd, batch,
-                    (const int *)S.grp, (const float *)S.h, S.part, c->d_status);
+    st = launch_pdl(down_pipe_kernel<QT>, dim3(G), dim3(kMoeThreads), down_smem(QT, L.ffn, TRd, batch), s,
+                    (const uint8_t *)L.down.w, L.ffn, L.d, L.n_exp, TRd, batch, (const int *)S.grp,
+                    (const float *)S.h, S.part, S.cnt + 2, c->d_status);
     if (st) return st;
     return launch_pdl(combine_kernel, dim3((L.d + 255) / 256, batch), dim3(256), 0, s, L.d, L.n_act, L.lo, L.hi,
                       (const int *)S.sel, (const float *)S.w, (const float *)S.part, eout, accum);
