@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=1, help="tokens per step for q4gemv / moe")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=48, help="layers of the decode workload")
+    ap.add_argument("--combine", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1 expert-parallel sum: the library's peer-memory kernel or an NCCL all-reduce")
     return ap.parse_args()
 
 
@@ -207,6 +209,16 @@ class Dist:
     def close(self):
         if self.pg:
             self.pg.destroy_process_group()
+
+    def ep_group(self, max_floats):
+        """The library's peer-memory combine for this process group."""
+        import x100b
+
+        def exchange(h):
+            out = [None] * self.world
+            self.pg.all_gather_object(out, h)
+            return out
+        return x100b.EpGroup(self.world, self.rank, max_floats, exchange)
 
     def physical_gpu(self):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -603,13 +615,17 @@ def bench_moe(args, dist, peaks, peak_src):
     stream = torch.cuda.Stream()
     state = {"i": 0}
 
+    ep = dist.ep_group(B * d) if world > 1 and args.combine == "p2p" else None
+
     def one(i):
         s = torch.cuda.current_stream().cuda_stream
         rc = L.x100q_moe_ffn_dev(layers[i % LAYERS].h, hns[i % POOL].data_ptr(), out[i % POOL].data_ptr(), B,
                                  None, None, s)
         if rc:
             raise x100b.X100Error(rc, "x100q_moe_ffn_dev")
-        if world > 1:
+        if ep is not None:
+            ep.allreduce_dev(out[i % POOL], out[i % POOL], B * d)
+        elif world > 1:
             dist.pg.all_reduce(out[i % POOL])
 
     PER = 16   # MoE calls per captured graph (each a different hn, layer copy)
@@ -618,26 +634,10 @@ def bench_moe(args, dist, peaks, peak_src):
         for j in range(PER):
             one(j)
     with torch.cuda.stream(stream):
-        if world == 1:
-            ms, clocks = timed_graph(run, args.steps, args.warmup, dist, stream)
-            calls = args.steps * PER
-        else:
-            for i in range(args.warmup * PER):
-                one(i)
-            torch.cuda.synchronize()
-            dist.barrier()
-            clk = ClockSampler(dist.physical_gpu())
-            clk.start()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for i in range(args.steps * PER):
-                one(i)
-            e1.record()
-            torch.cuda.synchronize()
-            dist.barrier()
-            clocks = clk.stop()
-            ms = dist.max(e0.elapsed_time(e1))
-            calls = args.steps * PER
+        # N > 1: the NCCL all-reduces are captured in the same CUDA graph
+        # (the warm-up calls initialise the communicator first)
+        ms, clocks = timed_graph(run, args.steps, args.warmup, dist, stream)
+        calls = args.steps * PER
     tok_s = calls * B / (ms / 1e3)
     alg_tok = 8 * 2654208 + 1048576 + 16384        # bytes per token (SURVEY config C4)
     per_call_us = ms * 1e3 / calls
@@ -692,7 +692,8 @@ def bench_moe(args, dist, peaks, peak_src):
         "config": {"workload": f"MoE layer d={d} experts={E} top-{k} ffn={ffn} Q4_K, batch {B}",
                    "batch": B, "expert_parallel": f"{E // world} experts per GPU",
                    "l2": f"{LAYERS} layer copies x {POOL} hn vectors rotated",
-                   "graph": f"{PER} MoE calls per CUDA graph" if world == 1 else "eager + NCCL all-reduce"},
+                   "graph": f"{PER} MoE calls per CUDA graph" + ("" if world == 1 else
+                                                                  f", each followed by the {args.combine} sum of eout")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(f"moe_b{B}"),
                      "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
@@ -704,7 +705,7 @@ def bench_moe(args, dist, peaks, peak_src):
         "e2e": {"value": round(e2e_steps * B / dt, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": 4 * B * d, "d2h_bytes_per_step": 4 * B * d,
                 "api": "x100q_moe_ffn(moe, hn, eout, batch) with pinned host hn, eout (synchronous)"},
-        "gpu_launches": calls * (2 if B == 1 else 5),
+        "gpu_launches": calls * ((2 if B == 1 else 5) + (1 if ep is not None else 0)),
         "cpu_baseline": cpu,
     }
 
@@ -789,10 +790,11 @@ def bench_decode(args, dist, peaks, peak_src):
     logits = torch.empty((B, V), device="cuda")
     eout = torch.empty((B, d), device="cuda")
     stream = torch.cuda.Stream()
+    ep = dist.ep_group(B * d) if world > 1 and args.combine == "p2p" else None
     # launches per step: embed, head, and per layer qkv GEMV, attention, Wo GEMV
     # (two launches above 8 tokens: its 4096-wide activations of 16 tokens
     # exceed one CTA's shared memory) and the MoE kernels (2 fused, 5 grouped)
-    launches = 2 + NL * (2 + (1 if B <= 8 else 2) + (2 if B == 1 else 5))
+    launches = 2 + NL * (3 + (1 if B <= 8 else 2) + (2 if B == 1 else 5) + (1 if ep is not None else 0))
 
     def step():
         if world == 1:
@@ -801,8 +803,11 @@ def bench_decode(args, dist, peaks, peak_src):
         m.embed_dev(toks, h, B)
         for li in range(NL):
             m.layer_dev(li, h, pos, B, eout=eout)
-            dist.pg.all_reduce(eout)
-            h.add_(eout)
+            if ep is not None:
+                ep.allreduce_dev(eout, h, B * d, accum=True)   # h += sum of the experts' shares
+            else:
+                dist.pg.all_reduce(eout)
+                h.add_(eout)
         m.head_dev(h, logits, B)
 
     # routing of one step (per-layer expert unions for the algorithmic bytes)
@@ -814,8 +819,11 @@ def bench_decode(args, dist, peaks, peak_src):
                 m.layer_dev(li, h, pos, B, sel=sel[li])
             else:
                 m.layer_dev(li, h, pos, B, eout=eout, sel=sel[li])
-                dist.pg.all_reduce(eout)
-                h.add_(eout)
+                if ep is not None:
+                    ep.allreduce_dev(eout, h, B * d, accum=True)
+                else:
+                    dist.pg.all_reduce(eout)
+                    h.add_(eout)
         torch.cuda.synchronize()
     selh = sel.cpu().numpy()
     union = [len(set(int(e) for e in selh[li].reshape(-1) if lo <= e < hi)) for li in range(NL)]
@@ -826,24 +834,7 @@ def bench_decode(args, dist, peaks, peak_src):
     step_bytes = sum(attn_b + E * d * 4 + u * exp_b + kv_b + norms_b for u in union) + V * d // 32 * 34 + d * 4 + \
         B * d * 4
     with torch.cuda.stream(stream):
-        if world == 1:
-            ms, clocks = timed_graph(step, args.steps, args.warmup, dist, stream)
-        else:
-            for _ in range(args.warmup):
-                step()
-            torch.cuda.synchronize()
-            dist.barrier()
-            clk = ClockSampler(dist.physical_gpu())
-            clk.start()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(args.steps):
-                step()
-            e1.record()
-            torch.cuda.synchronize()
-            dist.barrier()
-            clocks = clk.stop()
-            ms = dist.max(e0.elapsed_time(e1))
+        ms, clocks = timed_graph(step, args.steps, args.warmup, dist, stream)
     step_ms = ms / args.steps
     tok_s = B / (step_ms / 1e3)
     gbs = step_bytes / (step_ms / 1e3) / 1e9
@@ -914,7 +905,8 @@ def bench_decode(args, dist, peaks, peak_src):
                    "batch": B, "layers": NL, "context": P + 1,
                    "expert_parallel": f"{E // world} experts per GPU",
                    "l2": f"weights {step_bytes / 2**30:.2f} GiB per step (> L2)",
-                   "graph": "one CUDA graph per step" if world == 1 else "eager + NCCL all-reduce per layer"},
+                   "graph": "one CUDA graph per step" + ("" if world == 1 else
+                                                          f" ({args.combine} sum of the experts' output per layer inside)")},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
                      "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",

@@ -202,6 +202,34 @@ int x100q_model_forward_dev(x100q_model *m, const int *tokens, float *h,
 int x100q_model_forward(x100q_model *m, const int *tokens, const int *pos,
                         float *logits, int batch);
 
+/* ---- expert-parallel combine over peer memory ------------------------------ */
+/* With experts split over `world` processes (one per GPU, x100q_moe_create
+ * with [expert_lo, expert_hi) or a model with a partial expert range), each
+ * process's eout is a partial sum; the reference's single-process block
+ * (qwen_moe.c:305-310) is their sum.  x100q_ep_* sums them with one kernel
+ * over NVLink peer memory instead of a library all-reduce: each process
+ * writes its partial into every process's receive buffer, raises a flag, and
+ * adds the world partials in process order once all flags are up, so every
+ * process ends with the same bits.  Setup: create on every process (same
+ * world, max_floats), exchange the X100Q_EP_HANDLE_BYTES handles (e.g. an
+ * all-gather over the host), then open with all handles in rank order.  The
+ * waits are bounded (1 s): a missing process makes the next synchronising
+ * call report X100_E_TIMEOUT instead of hanging.  Every process must make the
+ * same sequence of calls with the same n.                                   */
+#define X100Q_EP_HANDLE_BYTES 64
+typedef struct x100q_ep x100q_ep;
+
+/* world <= 8; max_floats (a multiple of 4) bounds n of every call.          */
+x100q_ep *x100q_ep_create(int world, int rank, int max_floats);
+int       x100q_ep_handle(const x100q_ep *ep, void *handle_out);
+int       x100q_ep_open(x100q_ep *ep, const void *all_handles);
+/* dst[i] = (accum ? dst[i] : 0) + sum over processes of their src[i], i < n
+ * (n a multiple of 4, src/dst 16-byte aligned device pointers; dst may be
+ * src when accum = 0).  Asynchronous on `stream`.                           */
+int       x100q_ep_allreduce_dev(x100q_ep *ep, const float *src, float *dst, int n,
+                                 int accum, void *stream);
+void      x100q_ep_destroy(x100q_ep *ep);
+
 #ifdef __cplusplus
 }
 #endif

@@ -88,6 +88,12 @@ _SIGS = {
     "x100q_model_head_dev": ([vp, vp, vp, i32, vp], i32),
     "x100q_model_forward_dev": ([vp, vp, vp, vp, vp, i32, vp], i32),
     "x100q_model_forward": ([vp, vp, vp, vp, i32], i32),
+    # expert-parallel combine
+    "x100q_ep_create": ([i32, i32, i32], vp),
+    "x100q_ep_handle": ([vp, vp], i32),
+    "x100q_ep_open": ([vp, vp], i32),
+    "x100q_ep_allreduce_dev": ([vp, vp, vp, i32, i32, vp], i32),
+    "x100q_ep_destroy": ([vp], None),
 }
 
 
@@ -211,8 +217,8 @@ class Lin:
         return b.value
 
     def close(self):
-        if getattr(self, "h", None):
-            lib().x100q_lin_destroy(self.h)
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.x100q_lin_destroy(self.h)
             self.h = None
 
     __del__ = close
@@ -245,8 +251,8 @@ class Moe:
               "x100q_moe_ffn_dev")
 
     def close(self):
-        if getattr(self, "h", None):
-            lib().x100q_moe_destroy(self.h)
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.x100q_moe_destroy(self.h)
             self.h = None
 
     __del__ = close
@@ -305,8 +311,39 @@ class Model:
         return logits
 
     def close(self):
-        if getattr(self, "h", None):
-            lib().x100q_model_destroy(self.h)
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.x100q_model_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+
+EP_HANDLE_BYTES = 64
+
+
+class EpGroup:
+    """x100q_ep handle: the peer-memory combine of expert-parallel partials.
+    `exchange(bytes) -> list[bytes]` must return every process's handle in
+    rank order (e.g. torch.distributed.all_gather_object)."""
+
+    def __init__(self, world: int, rank: int, max_floats: int, exchange):
+        self.h = lib().x100q_ep_create(world, rank, max_floats)
+        if not self.h:
+            check_last("x100q_ep_create")
+        mine = C.create_string_buffer(EP_HANDLE_BYTES)
+        check(lib().x100q_ep_handle(self.h, mine), "x100q_ep_handle")
+        allh = b"".join(exchange(mine.raw))
+        assert len(allh) == world * EP_HANDLE_BYTES
+        buf = C.create_string_buffer(allh, len(allh))
+        check(lib().x100q_ep_open(self.h, buf), "x100q_ep_open")
+
+    def allreduce_dev(self, src, dst, n: int, accum: bool = False, stream=None):
+        check(lib().x100q_ep_allreduce_dev(self.h, _p(src), _p(dst), n, 1 if accum else 0, _stream(stream)),
+              "x100q_ep_allreduce_dev")
+
+    def close(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.x100q_ep_destroy(self.h)
             self.h = None
 
     __del__ = close
