@@ -499,7 +499,10 @@ def timed_graph(fn, steps, warmup, dist, stream):
 def bench_q4gemv(args, dist, peaks, peak_src):
     """Q4_0 6144 x 2048 GEMV at batch B.  64 distinct
     weight copies (453 MB, > L2) are rotated inside one CUDA graph; a step is
-    one graph replay = 64 GEMV calls."""
+    one graph replay = 64 GEMV calls.  The value times independent calls
+    (X100Q_GEMV_INDEPENDENT), the way the reference's bench/q4_gemv.c times
+    repeated GEMVs; the chain of dependent calls (each waiting for the
+    previous kernel, as inside a decode step) is reported beside it."""
     import numpy as np
     import torch
     import x100b
@@ -511,19 +514,23 @@ def bench_q4gemv(args, dist, peaks, peak_src):
     stream = torch.cuda.Stream()
     L = x100b.lib()
 
-    def run():
-        s = torch.cuda.current_stream().cuda_stream
-        for c in range(COPIES):
-            rc = L.x100q_lin_gemv_dev(lins[c].h, xs[c].data_ptr(), ys[c].data_ptr(), B, s)
-            if rc:
-                raise x100b.X100Error(rc, "x100q_lin_gemv_dev")
+    def make_run(flags):
+        def run():
+            s = torch.cuda.current_stream().cuda_stream
+            for c in range(COPIES):
+                rc = L.x100q_lin_gemv_dev_flags(lins[c].h, xs[c].data_ptr(), ys[c].data_ptr(), B, flags, s)
+                if rc:
+                    raise x100b.X100Error(rc, "x100q_lin_gemv_dev_flags")
+        return run
     with torch.cuda.stream(stream):
-        ms, clocks = timed_graph(run, args.steps, args.warmup, dist, stream)
+        ms_chain, _ = timed_graph(make_run(0), args.steps, args.warmup, dist, stream)
+        ms, clocks = timed_graph(make_run(1), args.steps, args.warmup, dist, stream)
     calls = args.steps * COPIES
     wbytes = N * K // 32 * 18
     alg = wbytes + B * (4 * K + 4 * N)
     per_call_s = ms / 1e3 / calls
     gbs = alg / per_call_s / 1e9
+    chain_gbs = alg / (ms_chain / 1e3 / calls) / 1e9
     # parity spot check of the last outputs against the oracle
     import py_oracle as po  # checker only
     blk = wellformed_blocks_dev(2, N * K // 32, torch.Generator(device="cuda").manual_seed(5))
@@ -564,12 +571,18 @@ def bench_q4gemv(args, dist, peaks, peak_src):
         "data": "synthetic random well-formed Q4_0 blocks, x ~ N(0,1)",
         "config": {"workload": f"Q4_0 GEMV y=W.x W {N}x{K} batch {B}", "N": N, "K": K, "batch": B,
                    "l2": f"{COPIES} weight copies rotated per step ({COPIES * wbytes / 2**20:.0f} MiB > L2)",
-                   "graph": f"one CUDA graph of {COPIES} GEMV launches per step"},
+                   "graph": f"one CUDA graph of {COPIES} GEMV launches per step",
+                   "calls": "independent (X100Q_GEMV_INDEPENDENT), as the reference's bench/q4_gemv.c repeats "
+                            "its GEMV; the dependent chain is roofline.dependent_chain"},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": load_traffic(f"q4gemv_b{B}"),
                      "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
                      "kernel": "x100::q::qgemv_kernel<Q4_0>", "algorithmic_bytes_per_launch": alg,
-                     "kernel_us_mean": round(per_call_s * 1e6, 3), "parity_rel_l2": err},
+                     "kernel_us_mean": round(per_call_s * 1e6, 3), "parity_rel_l2": err,
+                     "dependent_chain": {"achieved": round(chain_gbs, 1),
+                                         "frac": round(chain_gbs / peaks["hbm_gbs"], 4),
+                                         "kernel_us_mean": round(ms_chain * 1e3 / calls, 3),
+                                         "note": "each call waits for the previous kernel (decode-step order)"}},
         "clocks": clocks,
         "e2e": {"value": round(alg * e2e_steps / dt / 1e9, 3), "unit": "GB/s",
                 "h2d_bytes_per_step": 4 * B * K, "d2h_bytes_per_step": 4 * B * N,

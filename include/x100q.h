@@ -67,6 +67,16 @@ int        x100q_lin_info(const x100q_lin *lin, int *qtype, int *N, int *K,
 int x100q_lin_gemv(const x100q_lin *lin, const float *x, float *y, int batch);
 int x100q_lin_gemv_dev(const x100q_lin *lin, const float *x, float *y, int batch,
                        void *stream);
+/* As x100q_lin_gemv_dev, with flags.  X100Q_GEMV_INDEPENDENT: the caller
+ * guarantees that x and y are neither written nor read by work still running
+ * on `stream` (e.g. the q, k and v projections of one activation, or repeated
+ * calls as the reference's bench/q4_gemv.c times them); the call then reads x
+ * without waiting for the previous kernel, so consecutive independent calls
+ * overlap and stream their weights back to back.  Calls still complete in
+ * stream order.                                                             */
+#define X100Q_GEMV_INDEPENDENT 1
+int x100q_lin_gemv_dev_flags(const x100q_lin *lin, const float *x, float *y, int batch,
+                             int flags, void *stream);
 
 /* ---- mixture-of-experts FFN ---------------------------------------------- */
 typedef struct x100q_moe x100q_moe;

@@ -84,6 +84,40 @@ def test_qgemv_encoded_weights_and_device_path(qt):
     assert po.rel_l2(yd.cpu().numpy(), ref) <= REL_Q
 
 
+@pytest.mark.parametrize("batch", [1, 4])
+def test_qgemv_independent_calls(batch):
+    """X100Q_GEMV_INDEPENDENT: a run of calls whose inputs and outputs are
+    independent (captured in one CUDA graph, each kernel starting before the
+    previous one ends) gives bit-identical results to ordinary calls, and an
+    ordinary call after the run is ordered after all of them."""
+    import torch
+    N, K, R = 3072, 2048, 8
+    lins = [x100b.Lin(po.Q8_0, N, K, wellformed_blocks(po.Q8_0, N * K // 32, 40 + i)) for i in range(R)]
+    xs = torch.randn((R, batch, K), device="cuda", generator=torch.Generator(device="cuda").manual_seed(3))
+    ref = torch.empty((R, batch, N), device="cuda")
+    got = torch.empty_like(ref)
+    for i in range(R):
+        lins[i].gemv_dev(xs[i], ref[i], batch)
+    x100b.sync()
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for i in range(R):
+                lins[i].gemv_dev(xs[i], got[i], batch, independent=True)
+            # an ordinary (dependent) call after the run, overwriting call 0's output
+            lins[0].gemv_dev(xs[0], got[0], batch)
+        for _ in range(3):
+            g.replay()
+    torch.cuda.synchronize()
+    x100b.sync()
+    assert torch.equal(got[1:], ref[1:])
+    assert torch.equal(got[0], ref[0])
+    with pytest.raises(x100b.X100Error):
+        x100b.check(x100b.lib().x100q_lin_gemv_dev_flags(lins[0].h, xs[0].data_ptr(), got[0].data_ptr(), batch,
+                                                         2, torch.cuda.current_stream().cuda_stream))
+
+
 def test_qgemv_edge_activations():
     """Zero rows, a single huge outlier and tiny values in x."""
     qt, N, K = po.Q4_K, 256, 1024

@@ -41,12 +41,16 @@ constexpr int kGemvThreads = 512;
 
 // With `nw` set the kernel computes y = W . rmsnorm(x; nw, eps) (RMS norm of
 // each token folded into the activation preparation, see xprep_rows); with
-// `accum` set it adds into y (y += W . x: a residual connection).
+// `accum` set it adds into y (y += W . x: a residual connection).  With
+// `indep` the caller guarantees that no kernel still running touches x or y:
+// the CTA prepares x without waiting on the previous kernel and waits only
+// before it exits (so grids still complete in stream order), which lets a run
+// of independent calls stream weights back to back.
 template <int QT, int B>
 __global__ void __launch_bounds__(kGemvThreads, 1)
     qgemv_kernel(const uint8_t *__restrict__ W, int N, int K, int TR, const float *__restrict__ x,
                  float *__restrict__ y, int batch, const float *__restrict__ nw, float eps, int accum,
-                 int *status) {
+                 int indep, int *status) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bar;
     __shared__ int abort_flag;
@@ -69,7 +73,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         stage_bytes(tile, W + (long)row0 * rb, (uint32_t)(rows * rb), &bar);
     }
     pdl_launch_dependents();
-    pdl_wait();                                   // x may come from the previous kernel
+    if (!indep) pdl_wait();                       // x may come from the previous kernel
     xprep_rows([x, K](int c) { return x + (long)c * K; }, K, batch, xb, nw, ss);
     __syncthreads();
     if (threadIdx.x < batch) scale[threadIdx.x] = nw ? rms_scale(ss, blockDim.x / 8, threadIdx.x, K, eps) : 1.0f;
@@ -110,7 +114,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     }
     __syncthreads();
     if (abort_flag) {
-        if (threadIdx.x == 0) mbar_wait_drain(&bar, 0, 100000000ull);   // the copy may still be in flight
+        if (threadIdx.x == 0) {
+            mbar_wait_drain(&bar, 0, 100000000ull);   // the copy may still be in flight
+            if (indep) pdl_wait();
+        }
         return;
     }
     for (int t = threadIdx.x; t < rows * batch; t += blockDim.x) {
@@ -126,6 +133,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         const float v = (s0 + s1) * scale[b];
         *o = accum ? *o + v : v;
     }
+    if (indep && threadIdx.x == 0) pdl_wait();   // complete only after the previous grid
 }
 
 // ---- device re-layout of GGUF-native blocks ------------------------------------
@@ -189,16 +197,21 @@ static int gemv_rows(int qt, int N, int K, int B, int sm_count) {
 template <int QT, int B>
 static int launch_B(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
                     cudaStream_t s) {
-    const int TR = gemv_rows(QT, m.N, m.K, B, c->sm_count);
+    // independent calls overlap, so they keep the small single-token tiles
+    // (several CTAs per SM) instead of one wave of large ones
+    const int TR = o.indep ? gemv_rows(QT, m.N, m.K, 1, 0) : gemv_rows(QT, m.N, m.K, B, c->sm_count);
     const size_t smem = gemv_smem(QT, m.K, TR, B);
     static bool attr[64];
     if (!attr[c->device]) {
         set_qkernel_attrs(qgemv_kernel<QT, B>, (int)kGemvSmemMax);
         attr[c->device] = true;
     }
-    return launch_k(qgemv_kernel<QT, B>, dim3((m.N + TR - 1) / TR), dim3(kGemvThreads), smem, s, o.pdl,
+    // independent calls: half-size CTAs, so more of them fit an SM and more
+    // weight bytes are in flight while the calls overlap
+    const int threads = o.indep ? kGemvThreads / 2 : kGemvThreads;
+    return launch_k(qgemv_kernel<QT, B>, dim3((m.N + TR - 1) / TR), dim3(threads), smem, s, o.pdl,
                     (const uint8_t *)m.w, m.N, m.K, TR, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0,
-                    c->d_status);
+                    o.indep ? 1 : 0, c->d_status);
 }
 
 template <int QT>
@@ -361,7 +374,15 @@ int x100q_lin_info(const x100q_lin *l, int *qtype, int *N, int *K, size_t *devic
 }
 
 int x100q_lin_gemv_dev(const x100q_lin *l, const float *x, float *y, int batch, void *stream) {
+    return x100q_lin_gemv_dev_flags(l, x, y, batch, 0, stream);
+}
+
+int x100q_lin_gemv_dev_flags(const x100q_lin *l, const float *x, float *y, int batch, int flags, void *stream) {
     set_error(X100_OK);
+    if (flags & ~X100Q_GEMV_INDEPENDENT) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
     if (!l || !x || !y) {
         set_error(X100_E_ARG);
         return X100_E_ARG;
@@ -372,7 +393,9 @@ int x100q_lin_gemv_dev(const x100q_lin *l, const float *x, float *y, int batch, 
     }
     DevCtx *c = ctx();
     if (!c) return get_error();
-    int st = launch_qgemv(c, l->m, x, y, batch, static_cast<cudaStream_t>(stream));
+    GemvOpts o;
+    o.indep = (flags & X100Q_GEMV_INDEPENDENT) != 0;
+    int st = launch_qgemv_ex(c, l->m, x, y, batch, o, static_cast<cudaStream_t>(stream));
     if (st) set_error(st);
     return st;
 }

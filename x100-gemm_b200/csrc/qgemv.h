@@ -33,6 +33,7 @@ struct GemvOpts {
     float eps = 1e-6f;
     bool accum = false;
     bool pdl = true;   // false: launch behind a full barrier (see launch_k)
+    bool indep = false;   // x, y untouched by running kernels: prepare x before the dependency wait
 };
 int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
                     cudaStream_t s);

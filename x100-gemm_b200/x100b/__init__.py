@@ -72,6 +72,7 @@ _SIGS = {
     "x100q_lin_info": ([vp, vp, vp, vp, vp], i32),
     "x100q_lin_gemv": ([vp, vp, vp, i32], i32),
     "x100q_lin_gemv_dev": ([vp, vp, vp, i32, vp], i32),
+    "x100q_lin_gemv_dev_flags": ([vp, vp, vp, i32, i32, vp], i32),
     "x100q_moe_create": ([i32, i32, i32, i32, i32, vp, vp, vp, vp, i32, i32], vp),
     "x100q_moe_destroy": ([vp], None),
     "x100q_moe_ffn": ([vp, vp, vp, i32, vp, vp], i32),
@@ -208,8 +209,9 @@ class Lin:
     def gemv(self, x, y, batch: int) -> None:
         check(lib().x100q_lin_gemv(self.h, _p(x), _p(y), batch), "x100q_lin_gemv")
 
-    def gemv_dev(self, x, y, batch: int, stream=None) -> None:
-        check(lib().x100q_lin_gemv_dev(self.h, _p(x), _p(y), batch, _stream(stream)), "x100q_lin_gemv_dev")
+    def gemv_dev(self, x, y, batch: int, stream=None, independent: bool = False) -> None:
+        check(lib().x100q_lin_gemv_dev_flags(self.h, _p(x), _p(y), batch, 1 if independent else 0,
+                                             _stream(stream)), "x100q_lin_gemv_dev_flags")
 
     def device_bytes(self) -> int:
         b = C.c_size_t()
