@@ -378,8 +378,11 @@ def bench_gemm(args, dist, peaks, peak_src):
         peak_note = f"bf16_tflops ({peak_src} MEASURED_PEAKS.json burst); kind::f16 runs at the bf16 rate"
         unit = "TFLOP/s"
     else:
-        peak = 148 * 128 * 2 * 1.965e9 / 1e12
-        peak_note = "nominal CUDA-core fp32 FMA peak: 148 SMs x 128 lanes x 2 x 1.965 GHz"
+        # three tf32 products per fp32 product, tf32 issuing at half the
+        # kind::f16 rate: the fp32-equivalent ceiling is bf16 / 2 / 3
+        peak = peaks["bf16_tflops"] / 6.0
+        peak_note = (f"bf16_tflops / 6 ({peak_src} MEASURED_PEAKS.json burst): each fp32 product is three "
+                     "kind::tf32 products (hi.hi + hi.lo + lo.hi) and tf32 issues at half the kind::f16 rate")
         unit = "TFLOP/s"
     traffic = load_traffic(f"{kind}_{S}_{world}")
 
@@ -427,7 +430,8 @@ def bench_gemm(args, dist, peaks, peak_src):
                          f"(> L2 between reuses)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": unit,
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_note,
-                     "kernel": "x100::tc::gemm_tc2_kernel (2-SM, TMA reduce-add epilogue)" if kind != "gemm_f32" else "gemm_fast_kernel",
+                     "kernel": "x100::tc::gemm_tc2_kernel (2-SM, TMA reduce-add epilogue)" if kind != "gemm_f32" else
+                               "x100::tc::gemm_tc2_kernel<3> (three kind::tf32 products, 512-k accumulator pieces)",
                      "algorithmic_ops_per_launch": ops_rank,
                      "kernel_ms_mean": round(kernel_ms, 4)},
         "clocks": clocks,

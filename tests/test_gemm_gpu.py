@@ -208,6 +208,28 @@ def test_f16_f32acc_within_1e5(shape):
     assert frob(C, ref) <= REL_F32
 
 
+@pytest.mark.parametrize("shape", [(2048, 2048, 4096), (640, 1536, 8192), (1000, 512, 1000), (256, 260, 2048)])
+def test_rvv_f32_tensor_core_path(shape):
+    """gemm_rvv_f32 on TMA-addressable operands runs as three tf32
+    tensor-core products; the result must stay within relative Frobenius
+    1e-5 of an fp64 product (C += A.B with non-zero C).  (1000, 512, 1000):
+    ragged tiles in every dimension; (256, 260, 2048): C's rows are not
+    16-byte aligned, so the K-pieces of a tile are added through the
+    non-TMA epilogue in order."""
+    import torch
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.rand((M, K), device="cuda", generator=g) * 2 - 1
+    B = torch.rand((K, N), device="cuda", generator=g) * 2 - 1
+    C0 = torch.rand((M, N), device="cuda", generator=g) * 2 - 1
+    C = C0.clone()
+    x100b.gemm_dev("gemm_f32_dev", A, B, C)
+    x100b.sync()
+    ref = C0.double() + A.double() @ B.double()
+    err = (torch.linalg.norm(C.double() - ref) / torch.linalg.norm(ref)).item()
+    assert err <= REL_F32, err
+
+
 def test_rvv_f16_fp16_c():
     M, N, K = 256, 256, 512
     *_, Af, Bf, Cf = inputs(M, N, K)

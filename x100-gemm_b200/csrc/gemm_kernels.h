@@ -11,7 +11,8 @@ namespace x100 {
 // tcgen05 tensor-core GEMM (gemm_tc.cu).  lda/ldb in elements; requirements:
 // A, B 16-byte aligned, lda*es and ldb*es multiples of 16 bytes, device is
 // sm_100.  kind 0: int8 x int8 -> int32 C; kind 1: fp16 -> fp32 C;
-// kind 2: fp16 -> fp16 C (fp32 accumulate).
+// kind 2: fp16 -> fp16 C (fp32 accumulate); kind 3: fp32 -> fp32 C as three
+// tf32 products (returns X100_E_UNSUPPORTED where CTA pairs cannot run).
 int launch_gemm_tc(DevCtx *c, int kind, int M, int N, int K, const void *A, long lda, const void *B, long ldb,
                    void *C, long ldc, cudaStream_t s);
 // True when (A, lda, B, ldb) satisfy the tensor-map alignment rules above.

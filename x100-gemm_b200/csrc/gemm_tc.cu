@@ -51,6 +51,11 @@ template <int KIND> struct Traits;
 template <> struct Traits<0> { static constexpr int ES = 1; using CT = int32_t; };
 template <> struct Traits<1> { static constexpr int ES = 2; using CT = float; };
 template <> struct Traits<2> { static constexpr int ES = 2; using CT = __half; };
+// kind 3: fp32 x fp32 -> fp32 as three kind::tf32 products (A_hi.B_hi +
+// A_hi.B_lo + A_lo.B_hi, X_hi = X rounded to tf32, X_lo = X - X_hi), 2-SM
+// kernel only.  B and B_lo come transposed (N x K, both
+// operands K-major): kind::tf32 with an N-major B produced zeros here.
+template <> struct Traits<3> { static constexpr int ES = 4; using CT = float; };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int &mt, int &nt) {
     const int group = GROUP_M * num_n;
@@ -81,11 +86,16 @@ __host__ __device__ inline int sk_pairs(int total, int num_kb, int npairs) {
     return (rem > 0 && sp > rem) ? (int)sp : 0;   // no gain unless more pairs than tiles share the tail
 }
 
+// kp < num_kb (fp32 kind only): every whole tile is further cut into
+// consecutive K-pieces of kp k-blocks, taken in order by the same pair, each
+// accumulated from zero and added into C -- so no accumulator sums more than
+// kp k-blocks (the tensor core's fp32 accumulation loses low bits at every
+// step, an error that grows with the steps of one accumulator).
 struct PairSched {
-    int npairs, pair, num_kb, dp_tiles, j = 0;
+    int npairs, pair, num_kb, dp_tiles, j = 0, kp, piece = 0;
     long it = 0, end = 0;
-    __device__ PairSched(int total, int num_kb_, int npairs_, int pair_, bool sk)
-        : npairs(npairs_), pair(pair_), num_kb(num_kb_), dp_tiles(total) {
+    __device__ PairSched(int total, int num_kb_, int npairs_, int pair_, bool sk, int kp_ = 1 << 30)
+        : npairs(npairs_), pair(pair_), num_kb(num_kb_), dp_tiles(total), kp(kp_ < num_kb_ ? kp_ : num_kb_) {
         const int sp = sk ? sk_pairs(total, num_kb, npairs) : 0;
         if (sp > 0) {
             const int rem = total % npairs;
@@ -101,10 +111,15 @@ struct PairSched {
     __device__ bool next(int &tile, int &kb0, int &kb1) {
         const int t = pair + j * npairs;
         if (t < dp_tiles) {
-            ++j;
             tile = t;
-            kb0 = 0;
-            kb1 = num_kb;
+            kb0 = piece * kp;
+            kb1 = kb0 + kp < num_kb ? kb0 + kp : num_kb;
+            if (kb1 >= num_kb) {
+                ++j;
+                piece = 0;
+            } else {
+                ++piece;
+            }
             return true;
         }
         if (it < end) {
@@ -445,8 +460,9 @@ constexpr int P_SMEM_BYTES = P_BAR_OFF + P_NBARS * 8 + 16 + 1024;
 template <int KIND, bool TE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, typename Traits<KIND>::CT *__restrict__ C, int M, int N,
-                    int K, long ldc, int sk, int *status) {
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmA2,
+                    const __grid_constant__ CUtensorMap tmB2, typename Traits<KIND>::CT *__restrict__ C, int M,
+                    int N, int K, long ldc, int sk, int kp, int *status) {
     using CT = typename Traits<KIND>::CT;
     constexpr int ES = Traits<KIND>::ES;
     constexpr int BK = 128 / ES;          // K elements per stage
@@ -456,12 +472,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     constexpr int NBOX = P_COLS / ATOM_N; // B boxes per stage per CTA
     constexpr int BOX_B_BYTES = BK * 128;
     constexpr int TM = 2 * P_ROWS, TN = 2 * P_COLS;   // output tile of the pair
-    constexpr uint32_t IDESC = (KIND == 0) ? idesc_make(2, 1, 1, TM, TN) : idesc_make(1, 0, 1, TM, TN);
+    constexpr uint32_t IDESC = (KIND == 0)   ? idesc_make(2, 1, 1, TM, TN)
+                               : (KIND == 3) ? idesc_make(1, 2, 0, TM, TN)
+                                             : idesc_make(1, 0, 1, TM, TN);
+    // kind 3 stages hold the low parts too: [A | A_lo] and [B | B_lo], in
+    // half as many stages of the same total size
+    constexpr int NOPS = (KIND == 3) ? 2 : 1;
+    constexpr int PA = NOPS * P_A_BYTES, PB = NOPS * P_B_BYTES, PSTAGES = P_STAGES / NOPS;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
-    uint8_t *sB = smem + P_STAGES * P_A_BYTES;
+    uint8_t *sB = smem + PSTAGES * PA;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_BAR_OFF);
     uint64_t *full = bars;
     uint64_t *empty = bars + P_STAGES;
@@ -515,7 +537,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             uint32_t full_l[P_STAGES];
             for (int s = 0; s < P_STAGES; ++s) full_l[s] = mapa_shared(&full[s], 0);
             bool ok = true;
-            PairSched sched(total, num_kb, npairs, pair, sk != 0);
+            PairSched sched(total, num_kb, npairs, pair, sk != 0, kp);
             int tile, kb0, kb1;
             while (ok && sched.next(tile, kb0, kb1)) {
                 int mt, nt;
@@ -525,14 +547,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
-                    tma_load_2d_pair(sA + stage * P_A_BYTES, &tmA, kb * BK, mt * TM + (int)rank * P_ROWS, full_l[stage]);
+                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (PA + PB));
+                    tma_load_2d_pair(sA + stage * PA, &tmA, kb * BK, mt * TM + (int)rank * P_ROWS, full_l[stage]);
+                    if constexpr (KIND == 3)
+                        tma_load_2d_pair(sA + stage * PA + P_A_BYTES, &tmA2, kb * BK, mt * TM + (int)rank * P_ROWS,
+                                         full_l[stage]);
+                    if constexpr (KIND == 3) {   // B^T and B_lo^T: K-major, one box each
+                        tma_load_2d_pair(sB + stage * PB, &tmB, kb * BK, nt * TN + (int)rank * P_COLS, full_l[stage]);
+                        tma_load_2d_pair(sB + stage * PB + P_B_BYTES, &tmB2, kb * BK, nt * TN + (int)rank * P_COLS,
+                                         full_l[stage]);
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < NBOX; ++j)
-                        tma_load_2d_pair(sB + stage * P_B_BYTES + j * BOX_B_BYTES, &tmB,
-                                         nt * TN + (int)rank * P_COLS + j * ATOM_N, kb * BK, full_l[stage]);
+                        for (int j = 0; j < NBOX; ++j)
+                            tma_load_2d_pair(sB + stage * PB + j * BOX_B_BYTES, &tmB,
+                                             nt * TN + (int)rank * P_COLS + j * ATOM_N, kb * BK, full_l[stage]);
+                    }
                     issued[stage]++;
-                    if (++stage == P_STAGES) {
+                    if (++stage == PSTAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -540,16 +571,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             }
             if (ok) {
                 // wait until the leader's MMAs have released every stage
-                for (int i = 0; i < P_STAGES; ++i) {
+                for (int i = 0; i < PSTAGES; ++i) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, status)) break;
-                    if (++stage == P_STAGES) {
+                    if (++stage == PSTAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
             } else if (leader) {
                 // aborting: wait (bounded) for the copies of both CTAs announced so far
-                for (int s = 0; s < P_STAGES; ++s)
+                for (int s = 0; s < PSTAGES; ++s)
                     if (issued[s]) mbar_wait_drain(&full[s], (issued[s] - 1u) & 1u, kDrainNs);
             } else {
                 // aborting: this CTA's copies complete on the leader's barrier; give them
@@ -567,7 +598,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             for (int b = 0; b < 2; ++b) tfull_p[b] = mapa_shared(&tfull[b], 1);
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
-            PairSched sched(total, num_kb, npairs, pair, sk != 0);
+            PairSched sched(total, num_kb, npairs, pair, sk != 0, kp);
             int tile, kb0, kb1;
             while (ok && sched.next(tile, kb0, kb1)) {
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, status)) {
@@ -582,21 +613,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + stage * P_A_BYTES);
-                    const uint32_t b0 = smem_u32(sB + stage * P_B_BYTES);
+                    const uint32_t a0 = smem_u32(sA + stage * PA);
+                    const uint32_t b0 = smem_u32(sB + stage * PB);
 #pragma unroll
                     for (int k = 0; k < KSTEPS; ++k) {
                         const uint64_t adesc = smem_desc_sw128(a0 + k * 32, 16, 1024);
                         const uint64_t bdesc = smem_desc_sw128(b0 + k * UK * 128, BOX_B_BYTES, 1024);
                         const uint32_t accum = (kb != kb0 || k) ? 1u : 0u;
-                        if (KIND == 0)
+                        if constexpr (KIND == 0) {
                             umma_i8_pair(d_tmem, adesc, bdesc, IDESC, accum);
-                        else
+                        } else if constexpr (KIND == 3) {   // all four operands K-major
+                            const uint64_t a2desc = smem_desc_sw128(a0 + P_A_BYTES + k * 32, 16, 1024);
+                            const uint64_t bkdesc = smem_desc_sw128(b0 + k * 32, 16, 1024);
+                            const uint64_t b2desc = smem_desc_sw128(b0 + P_B_BYTES + k * 32, 16, 1024);
+                            umma_tf32_pair(d_tmem, adesc, bkdesc, IDESC, accum);
+                            umma_tf32_pair(d_tmem, adesc, b2desc, IDESC, 1u);
+                            umma_tf32_pair(d_tmem, a2desc, bkdesc, IDESC, 1u);
+                        } else {
                             umma_f16_pair(d_tmem, adesc, bdesc, IDESC, accum);
+                        }
                     }
                     umma_commit_pair(smem_u32(&empty[stage]));
                     umma_commit_pair(empty_p[stage]);
-                    if (++stage == P_STAGES) {
+                    if (++stage == PSTAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -615,11 +654,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         // ---------------- epilogue (both CTAs) ----------------
         const int q = warp & 3;   // TMEM lane quadrant this warp may access
         const int h = (warp - 2) >> 2;
-        uint32_t *buf = reinterpret_cast<uint32_t *>(smem + P_STAGES * P_STAGE_BYTES) + (warp - 2) * 32 * EPI_LD;
-        uint8_t *tbuf = smem + P_STAGES * P_STAGE_BYTES + (warp - 2) * 4096;   // 1024-aligned (TE)
+        uint32_t *buf = reinterpret_cast<uint32_t *>(smem + PSTAGES * (PA + PB)) + (warp - 2) * 32 * EPI_LD;
+        uint8_t *tbuf = smem + PSTAGES * (PA + PB) + (warp - 2) * 4096;   // 1024-aligned (TE)
         const uint32_t rel[2] = {mapa_shared(&tempty[0], 0), mapa_shared(&tempty[1], 0)};
         uint32_t acc = 0, acc_phase = 0;
-        PairSched sched(total, num_kb, npairs, pair, sk != 0);
+        PairSched sched(total, num_kb, npairs, pair, sk != 0, kp);
         int tile, kb0, kb1;
         while (sched.next(tile, kb0, kb1)) {
             int mt, nt;
@@ -653,14 +692,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
 template <int KIND, bool TE>
 static int launch_te(DevCtx *c, int M, int N, int K, const CUtensorMap &ta, const CUtensorMap &tb,
-                     const CUtensorMap &tc_, void *C, long ldc, cudaStream_t s) {
+                     const CUtensorMap &tc_, const CUtensorMap &ta2, const CUtensorMap &tb2, void *C, long ldc,
+                     cudaStream_t s) {
     using CT = typename Traits<KIND>::CT;
     static const bool one_sm = getenv("X100_GEMM_1SM") != nullptr;
     static int pairs_fit[64] = {};       // co-resident CTA pairs of the 2-SM kernel
     static bool attr_set[64] = {};
     if (!attr_set[c->device]) {
-        if (cudaFuncSetAttribute(gemm_tc_kernel<KIND, TE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-                cudaSuccess ||
+        if ((KIND != 3 && cudaFuncSetAttribute(gemm_tc_kernel<(KIND == 3 ? 1 : KIND), TE>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) ||
             cudaFuncSetAttribute(gemm_tc2_kernel<KIND, TE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  P_SMEM_BYTES) != cudaSuccess)
             return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
@@ -686,31 +726,59 @@ static int launch_te(DevCtx *c, int M, int N, int K, const CUtensorMap &ta, cons
         const int fit = pairs_fit[c->device];
         int pairs = pair_tiles < fit ? pair_tiles : fit;
         if (sk && sk_pairs(pair_tiles, num_kb, fit) > 0) pairs = fit;
-        gemm_tc2_kernel<KIND, TE><<<2 * pairs, THREADS, P_SMEM_BYTES, s>>>(ta, tb, tc_, reinterpret_cast<CT *>(C), M,
-                                                                          N, K, ldc, sk, c->d_status);
+        // fp32 kind: K-pieces of at most X100_GEMM_F32_KPIECE k (default 512:
+        // relative error 3.7e-6 whatever K, measured against fp64 at 8192;
+        // one accumulator over K = 8192 gave 5.7e-5; the pieces cost ~4 %)
+        static const int kpiece = [] {
+            const char *e = getenv("X100_GEMM_F32_KPIECE");
+            const int v = e ? atoi(e) : 512;
+            return v >= 32 ? v : 512;
+        }();
+        const int kp = KIND == 3 ? kpiece / (128 / Traits<KIND>::ES) : (1 << 30);
+        gemm_tc2_kernel<KIND, TE><<<2 * pairs, THREADS, P_SMEM_BYTES, s>>>(
+            ta, tb, tc_, ta2, tb2, reinterpret_cast<CT *>(C), M, N, K, ldc, sk, kp, c->d_status);
         return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+    }
+    if constexpr (KIND == 3) {   // the 3-product form exists only as a 2-SM kernel
+        set_error(X100_E_UNSUPPORTED);
+        return X100_E_UNSUPPORTED;
     }
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = tiles < c->sm_count ? tiles : c->sm_count;
-    gemm_tc_kernel<KIND, TE><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, tc_, reinterpret_cast<CT *>(C), M, N, K, ldc,
-                                                              c->d_status);
+    constexpr int K1 = KIND == 3 ? 1 : KIND;   // not reached for kind 3
+    gemm_tc_kernel<K1, TE><<<grid, THREADS, SMEM_BYTES, s>>>(ta, tb, tc_, reinterpret_cast<typename Traits<K1>::CT *>(C),
+                                                            M, N, K, ldc, c->d_status);
     return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
 }
 
 template <int KIND>
 static int launch_kind(DevCtx *c, int M, int N, int K, const void *A, long lda, const void *B, long ldb, void *C,
-                       long ldc, cudaStream_t s) {
+                       long ldc, cudaStream_t s, const void *A2 = nullptr, const void *B2 = nullptr) {
     constexpr int ES = Traits<KIND>::ES;
     constexpr int BK = 128 / ES;
     constexpr int ATOM_N = 128 / ES;
-    const CUtensorMapDataType dt = (KIND == 0) ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUtensorMap ta, tb, tcm;
+    const CUtensorMapDataType dt = (KIND == 0)   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : (KIND == 3) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap ta, tb, tcm, ta2, tb2;
     // boxes: A BK x 128 rows, B ATOM_N columns x BK rows (the 2-SM kernel
-    // loads one 128-column half of B per CTA in 128 / ATOM_N boxes)
+    // loads one 128-column half of B per CTA in 128 / ATOM_N boxes); kind 3:
+    // B is given transposed (N x K, row stride ldb) and boxed like A
     if (!make_tmap_2d(&ta, A, dt, (uint64_t)K, (uint64_t)M, (uint64_t)lda * ES, BK, BM) ||
-        !make_tmap_2d(&tb, B, dt, (uint64_t)N, (uint64_t)K, (uint64_t)ldb * ES, ATOM_N, BK)) {
+        !(KIND == 3 ? make_tmap_2d(&tb, B, dt, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * ES, BK, P_COLS)
+                    : make_tmap_2d(&tb, B, dt, (uint64_t)N, (uint64_t)K, (uint64_t)ldb * ES, ATOM_N, BK))) {
         set_error(X100_E_UNSUPPORTED);
         return X100_E_UNSUPPORTED;
+    }
+    if constexpr (KIND == 3) {   // the low parts, same layouts
+        if (!make_tmap_2d(&ta2, A2, dt, (uint64_t)K, (uint64_t)M, (uint64_t)lda * ES, BK, BM) ||
+            !make_tmap_2d(&tb2, B2, dt, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * ES, BK, P_COLS)) {
+            set_error(X100_E_UNSUPPORTED);
+            return X100_E_UNSUPPORTED;
+        }
+    } else {
+        ta2 = ta;   // unused by the kernel
+        tb2 = tb;
     }
     // 32-bit C: 32 x 32 boxes added by TMA reduce-add when the layout allows
     bool te = false;
@@ -719,15 +787,55 @@ static int launch_kind(DevCtx *c, int M, int N, int K, const void *A, long lda, 
                           (uint64_t)N, (uint64_t)M, (uint64_t)ldc * 4, 32, 32);
     if (!te) tcm = ta;   // unused by the kernel
     if constexpr (KIND != 2) {
-        if (te) return launch_te<KIND, true>(c, M, N, K, ta, tb, tcm, C, ldc, s);
+        if (te) return launch_te<KIND, true>(c, M, N, K, ta, tb, tcm, ta2, tb2, C, ldc, s);
     }
-    return launch_te<KIND, false>(c, M, N, K, ta, tb, tcm, C, ldc, s);
+    return launch_te<KIND, false>(c, M, N, K, ta, tb, tcm, ta2, tb2, C, ldc, s);
+}
+
+// X = X_hi + X_lo with X_hi = X rounded to tf32 (10 mantissa bits, nearest,
+// ties away from zero) and X_lo = X - X_hi, exact in fp32.  X_hi is stored
+// explicitly, so the products do not depend on how the tensor core reduces
+// an fp32 operand to tf32 (X_hi is already a tf32 value; X_lo only loses
+// bits 2^-11 below its own size).
+__device__ __forceinline__ float tf32_hi(float v) {
+    const uint32_t u = __float_as_uint(v);
+    if ((u & 0x7F800000u) == 0x7F800000u) return v;   // inf, nan
+    return __uint_as_float((u + 0x1000u) & 0xFFFFE000u);
+}
+__global__ void split_tf32_kernel(const float *__restrict__ x, float *__restrict__ hi, float *__restrict__ lo,
+                                  long n) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const float v = x[i], h = tf32_hi(v);
+        hi[i] = h;
+        lo[i] = v - h;
+    }
+}
+// bt[n][k] = hi(b[k][n]) and btlo[n][k] = lo(b[k][n]) for k < K, n < N
+// (row strides ldb and ldt); 32 x 32 tiles through shared memory, grid
+// (ceil(N/32), ceil(K/32)), block 32 x 8.
+__global__ void transpose_split_kernel(const float *__restrict__ b, long ldb, int K, int N, float *__restrict__ bt,
+                                       float *__restrict__ btlo, long ldt) {
+    __shared__ float t[32][33];
+    const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+    for (int r = threadIdx.y; r < 32; r += 8) {
+        const int k = k0 + r, n = n0 + threadIdx.x;
+        t[r][threadIdx.x] = (k < K && n < N) ? b[(long)k * ldb + n] : 0.f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += 8) {
+        const int n = n0 + r, k = k0 + threadIdx.x;
+        if (n < N && k < K) {
+            const float v = t[threadIdx.x][r], h = tf32_hi(v);
+            bt[(long)n * ldt + k] = h;
+            btlo[(long)n * ldt + k] = v - h;
+        }
+    }
 }
 
 }  // namespace tc
 
 bool tc_operands_ok(int kind, const void *A, long lda, const void *B, long ldb) {
-    const int es = kind == 0 ? 1 : 2;
+    const int es = kind == 0 ? 1 : (kind == 3 ? 4 : 2);
     return (reinterpret_cast<uintptr_t>(A) % 16 == 0) && (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
            ((lda * es) % 16 == 0) && ((ldb * es) % 16 == 0);
 }
@@ -744,6 +852,25 @@ int launch_gemm_tc(DevCtx *c, int kind, int M, int N, int K, const void *A, long
     case 0: return tc::launch_kind<0>(c, M, N, K, A, lda, B, ldb, C, ldc, s);
     case 1: return tc::launch_kind<1>(c, M, N, K, A, lda, B, ldb, C, ldc, s);
     case 2: return tc::launch_kind<2>(c, M, N, K, A, lda, B, ldb, C, ldc, s);
+    case 3: {
+        // A_hi, A_lo, B^T_hi and B^T_lo in stream-ordered scratch (freed once
+        // the GEMM has run): every operand of the three products is K-major
+        const long na = (long)(M - 1) * lda + K, nap = (na + 3) & ~3L;
+        const long ldt = (K + 3) & ~3L;   // 16-byte rows
+        const long nt = (long)N * ldt;
+        float *scr = nullptr;
+        if (check_cuda(cudaMallocAsync(reinterpret_cast<void **>(&scr), (size_t)(2 * nap + 2 * nt) * 4, s),
+                       X100_E_ALLOC))
+            return X100_E_ALLOC;
+        float *ahi = scr, *alo = scr + nap, *bt = scr + 2 * nap, *bt2 = bt + nt;
+        tc::split_tf32_kernel<<<c->sm_count * 4, 256, 0, s>>>(static_cast<const float *>(A), ahi, alo, na);
+        tc::transpose_split_kernel<<<dim3((N + 31) / 32, (K + 31) / 32), dim3(32, 8), 0, s>>>(
+            static_cast<const float *>(B), ldb, K, N, bt, bt2, ldt);
+        int st = check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+        if (!st) st = tc::launch_kind<3>(c, M, N, K, ahi, lda, bt, ldt, C, ldc, s, alo, bt2);
+        cudaFreeAsync(scr, s);
+        return st;
+    }
     default: set_error(X100_E_ARG); return X100_E_ARG;
     }
 }

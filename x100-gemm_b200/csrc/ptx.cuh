@@ -279,6 +279,14 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, u
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
 }
+__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
 // Arrive once on the mbarrier at `bar_cluster_addr` (this CTA's or the
 // peer's) when the 2-SM MMAs issued so far by this thread have completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
@@ -300,10 +308,10 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
-// Instruction descriptor for tcgen05.mma kind::i8 / kind::f16 (dense):
-// bits 4-5 D format (1 F32, 2 S32), 7-9 A format, 10-12 B format (i8: 1 =
-// signed; f16: 0 = F16), bit 15 A major (0 = K), bit 16 B major (1 = MN),
-// bits 17-22 N>>3, bits 24-28 M>>4.
+// Instruction descriptor for tcgen05.mma kind::i8 / kind::f16 / kind::tf32
+// (dense): bits 4-5 D format (1 F32, 2 S32), 7-9 A format, 10-12 B format
+// (i8: 1 = signed; f16 / tf32: 0 = F16, 2 = TF32), bit 15 A major (0 = K),
+// bit 16 B major (1 = MN), bits 17-22 N>>3, bits 24-28 M>>4.
 __host__ __device__ constexpr uint32_t idesc_make(uint32_t dfmt, uint32_t abfmt, uint32_t b_mn_major, uint32_t M,
                                                   uint32_t N) {
     return (dfmt << 4) | (abfmt << 7) | (abfmt << 10) | (b_mn_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);

@@ -99,6 +99,21 @@ bool dims_ok(int M, int N, int K, const void *A, const void *B, const void *C) {
 
 enum Route { ROUTE_TC_I8, ROUTE_SIMT_I8, ROUTE_F32_FAST, ROUTE_F32_REF, ROUTE_F16_F32C, ROUTE_F16_F16C };
 
+// The fast fp32 GEMM: three tf32 tensor-core products (A_hi.B_hi + A_hi.B_lo +
+// A_lo.B_hi, relative error about 1e-6, inside the 1e-5 bar) when TMA can
+// address the operands and CTA pairs can be scheduled, else the FFMA kernel.
+// X100_GEMM_F32_FFMA=1 keeps the FFMA kernel.
+int f32_fast(DevCtx *c, int M, int N, int K, const float *A, long lda, const float *B, long ldb, float *C, long ldc,
+             cudaStream_t s) {
+    static const bool ffma = getenv("X100_GEMM_F32_FFMA") != nullptr;
+    if (!ffma && tc_operands_ok(3, A, lda, B, ldb)) {
+        const int st = launch_gemm_tc(c, 3, M, N, K, A, lda, B, ldb, C, ldc, s);
+        if (st != X100_E_UNSUPPORTED) return st;
+        set_error(X100_OK);
+    }
+    return launch_gemm_f32_fast(c, M, N, K, A, lda, B, ldb, C, ldc, s);
+}
+
 // One synchronous host-API GEMM call.
 void host_gemm(Route route, int M, int N, int K, const void *A, const void *B, void *C) {
     set_error(X100_OK);
@@ -110,7 +125,7 @@ void host_gemm(Route route, int M, int N, int K, const void *A, const void *B, v
     const bool is_i8 = route == ROUTE_TC_I8 || route == ROUTE_SIMT_I8;
     const bool is_f16 = route == ROUTE_F16_F32C || route == ROUTE_F16_F16C;
     const int es = is_i8 ? 1 : (is_f16 ? 2 : 4);
-    const bool need_align = route == ROUTE_TC_I8 || is_f16;
+    const bool need_align = route == ROUTE_TC_I8 || route == ROUTE_F32_FAST || is_f16;
     const long pad = 16 / es;
     const size_t c_es = (route == ROUTE_F16_F16C) ? 2 : 4;
     Operand a, b;
@@ -128,8 +143,8 @@ void host_gemm(Route route, int M, int N, int K, const void *A, const void *B, v
                                  (int32_t *)co.dev, N, c->stream);
         break;
     case ROUTE_F32_FAST:
-        st = launch_gemm_f32_fast(c, M, N, K, (const float *)a.dev, a.ld, (const float *)b.dev, b.ld,
-                                  (float *)co.dev, N, c->stream);
+        st = f32_fast(c, M, N, K, (const float *)a.dev, a.ld, (const float *)b.dev, b.ld, (float *)co.dev, N,
+                      c->stream);
         break;
     case ROUTE_F32_REF:
         st = launch_gemm_f32_ref(c, M, N, K, (const float *)a.dev, a.ld, (const float *)b.dev, b.ld,
@@ -173,7 +188,7 @@ int dev_gemm(Route route, int M, int N, int K, const void *A, long lda, const vo
         st = launch_gemm_i8_simt(c, M, N, K, (const int8_t *)A, lda, (const int8_t *)B, ldb, (int32_t *)C, ldc, s);
         break;
     case ROUTE_F32_FAST:
-        st = launch_gemm_f32_fast(c, M, N, K, (const float *)A, lda, (const float *)B, ldb, (float *)C, ldc, s);
+        st = f32_fast(c, M, N, K, (const float *)A, lda, (const float *)B, ldb, (float *)C, ldc, s);
         break;
     case ROUTE_F32_REF:
         st = launch_gemm_f32_ref(c, M, N, K, (const float *)A, lda, (const float *)B, ldb, (float *)C, ldc, s);
