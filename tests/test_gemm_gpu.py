@@ -230,6 +230,22 @@ def test_rvv_f32_tensor_core_path(shape):
     assert err <= REL_F32, err
 
 
+def test_f16_f32acc_long_k():
+    """fp16 operands, fp32 C at K = 12288 (three 4096-k accumulator pieces):
+    relative Frobenius error vs the fp64 product of the fp16 values <= 1e-5."""
+    import torch
+    M, N, K = 1024, 1024, 12288
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = (torch.rand((M, K), device="cuda", generator=g) * 2 - 1).half()
+    B = (torch.rand((K, N), device="cuda", generator=g) * 2 - 1).half()
+    C = torch.zeros((M, N), device="cuda")
+    x100b.gemm_dev("gemm_f16_f32acc_dev", A, B, C)
+    x100b.sync()
+    ref = A.double() @ B.double()
+    err = (torch.linalg.norm(C.double() - ref) / torch.linalg.norm(ref)).item()
+    assert err <= REL_F32, err
+
+
 def test_rvv_f16_fp16_c():
     M, N, K = 256, 256, 512
     *_, Af, Bf, Cf = inputs(M, N, K)

@@ -86,7 +86,7 @@ __host__ __device__ inline int sk_pairs(int total, int num_kb, int npairs) {
     return (rem > 0 && sp > rem) ? (int)sp : 0;   // no gain unless more pairs than tiles share the tail
 }
 
-// kp < num_kb (fp32 kind only): every whole tile is further cut into
+// kp < num_kb (fp32 and fp16 -> fp32 kinds): every whole tile is further cut into
 // consecutive K-pieces of kp k-blocks, taken in order by the same pair, each
 // accumulated from zero and added into C -- so no accumulator sums more than
 // kp k-blocks (the tensor core's fp32 accumulation loses low bits at every
@@ -726,15 +726,19 @@ static int launch_te(DevCtx *c, int M, int N, int K, const CUtensorMap &ta, cons
         const int fit = pairs_fit[c->device];
         int pairs = pair_tiles < fit ? pair_tiles : fit;
         if (sk && sk_pairs(pair_tiles, num_kb, fit) > 0) pairs = fit;
-        // fp32 kind: K-pieces of at most X100_GEMM_F32_KPIECE k (default 512:
-        // relative error 3.7e-6 whatever K, measured against fp64 at 8192;
-        // one accumulator over K = 8192 gave 5.7e-5; the pieces cost ~4 %)
+        // fp32 kind: K-pieces of at most X100_GEMM_F32_KPIECE k (default 1024:
+        // relative error vs fp64 7.2e-6 whatever K (512: 3.7e-6; one
+        // accumulator over K = 8192: 5.7e-5); at 8192^3 512-k pieces halve the
+        // speed -- every piece adds its 256 x 256 accumulator into C)
         static const int kpiece = [] {
             const char *e = getenv("X100_GEMM_F32_KPIECE");
-            const int v = e ? atoi(e) : 512;
-            return v >= 32 ? v : 512;
+            const int v = e ? atoi(e) : 1024;
+            return v >= 32 ? v : 1024;
         }();
-        const int kp = KIND == 3 ? kpiece / (128 / Traits<KIND>::ES) : (1 << 30);
+        // fp16 -> fp32: pieces of 4096 k (relative error vs fp64 measured 4.9e-6 at
+        // K = 4096 and 9.7e-6 at K = 8192 in one piece); int8 is exact and
+        // fp16 C is rounded to fp16 anyway: one piece
+        const int kp = KIND == 3 ? kpiece / (128 / Traits<KIND>::ES) : KIND == 1 ? 4096 / 64 : (1 << 30);
         gemm_tc2_kernel<KIND, TE><<<2 * pairs, THREADS, P_SMEM_BYTES, s>>>(
             ta, tb, tc_, ta2, tb2, reinterpret_cast<CT *>(C), M, N, K, ldc, sk, kp, c->d_status);
         return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
