@@ -270,3 +270,48 @@ def test_f16_device_tc_vs_fp64():
     x100b.sync()
     ref = A.double() @ B.double()
     assert (torch.linalg.norm(C1.double() - ref) / torch.linalg.norm(ref)).item() < REL_F32
+
+
+def test_i8_host_call_in_panels_equals_device_call():
+    """A host call moving more than 32 MiB runs as row panels (copies of A and
+    C, the kernel and the copy back of C overlap on three streams).  Ragged
+    last panel, N whose rows are not 16-byte aligned: the result must equal
+    the device-pointer call bit for bit, and spot rows of every panel the
+    CPU oracle."""
+    import torch
+    M, N, K = 2300, 3001, 4096
+    A = po.rand_i8(11, M * K).reshape(M, K)
+    B = po.rand_i8(12, K * N).reshape(K, N)
+    C0 = po.rand_i8(13, M * N).astype(np.int32).reshape(M, N) * 1000
+    C = C0.copy()
+    x100b.gemm_host("gemm_ime_i8", A, B, C)
+    Cd = torch.from_numpy(C0.copy()).cuda()
+    x100b.gemm_dev("gemm_ime_i8_dev", torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), Cd)
+    x100b.sync()
+    np.testing.assert_array_equal(C, Cd.cpu().numpy())
+    rows = [0, 511, 512, 1023, 1024, 1535, 1536, 2047, 2048, 2299]   # both sides of each 512-row panel edge
+    ref = po.gemm_i8(A[rows], B, C0[rows].copy(), nthreads=8)
+    np.testing.assert_array_equal(C[rows], ref)
+
+
+def test_f32_and_f16_host_calls_in_panels():
+    """Panelled host calls of the fp32 and fp16 routes stay within their
+    bars: fp32 within relative Frobenius 1e-5 of the fp64 product; fp16 with
+    fp16 C within one fp16 rounding of the fp32 result."""
+    M, N, K = 1500, 4096, 2048
+    rng = np.random.default_rng(3)
+    Af = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    Bf = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    Cf = rng.uniform(-1, 1, (M, N)).astype(np.float32)
+    C = Cf.copy()
+    x100b.gemm_host("gemm_rvv_f32", Af, Bf, C)
+    ref = Cf.astype(np.float64) + Af.astype(np.float64) @ Bf.astype(np.float64)
+    assert frob(C, ref) <= REL_F32
+    M, N, K = 2000, 8192, 2048
+    A16 = rng.uniform(-1, 1, (M, K)).astype(np.float16)
+    B16 = rng.uniform(-1, 1, (K, N)).astype(np.float16)
+    C16 = rng.uniform(-1, 1, (M, N)).astype(np.float16)
+    C = C16.copy()
+    x100b.gemm_host("gemm_rvv_f16", A16, B16, C)
+    ref = C16.astype(np.float32) + A16.astype(np.float32) @ B16.astype(np.float32)
+    np.testing.assert_allclose(C.astype(np.float32), ref, rtol=2 ** -10, atol=2e-2)

@@ -83,8 +83,12 @@ DevCtx *ctx() {
         int optin = 0;
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         c->smem_optin = (size_t)optin;
-        if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-            cudaMalloc(&c->d_status, 64) != cudaSuccess || cudaMemset(c->d_status, 0, 64) != cudaSuccess) {
+        bool ok = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&c->up, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&c->down, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaMalloc(&c->d_status, 64) == cudaSuccess && cudaMemset(c->d_status, 0, 64) == cudaSuccess;
+        for (cudaEvent_t &e : c->ev) ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
             cudaGetLastError();
             delete c;
             set_error(X100_E_ALLOC);

@@ -37,6 +37,12 @@ struct DevCtx {
     int *d_status = nullptr;         // device status word written by kernels
     DevBuf stage[4];                 // staging buffers of host-pointer calls
     std::mutex mu;                   // serialises host-pointer calls on this device
+    // Panelled host-pointer calls: host->device copies on `up`, device->host
+    // copies on `down`, the kernels on `stream`; ev[p] marks panel p's inputs
+    // staged, ev[kMaxPanels + p] panel p computed.
+    static constexpr int kMaxPanels = 8;
+    cudaStream_t up = nullptr, down = nullptr;
+    cudaEvent_t ev[2 * kMaxPanels] = {};
 };
 
 // Context of the calling thread's selected device (created on first use).

@@ -3,8 +3,9 @@
 // Host-pointer calls (the reference's own signatures) stage operands into
 // grow-only device buffers (padding leading dimensions to 16 bytes so the
 // tensor-core path's TMA maps are legal), run the kernel on the context's
-// stream and copy C back before returning.  Device pointers are detected and
-// used in place.  Every failure is recorded for x100_last_error(); nothing
+// stream and copy C back before returning; calls that move 32 MiB or more of
+// host A and C run as row panels whose copies in, kernels and copies out
+// overlap.  Device pointers are detected and used in place.  Every failure is recorded for x100_last_error(); nothing
 // aborts.
 #include <cuda_fp16.h>
 
@@ -29,7 +30,7 @@ struct Operand {
 // staging slot `slot` with its leading dimension padded to `pad_elems`,
 // unless it is device memory that already satisfies the alignment.
 bool stage_in(DevCtx *c, int slot, const void *p, long rows, long cols, int es, long pad_elems, bool need_align,
-              Operand &out) {
+              Operand &out, cudaStream_t s) {
     const bool dev = is_device_ptr(p);
     const bool aligned = (reinterpret_cast<uintptr_t>(p) % 16 == 0) && ((cols * es) % 16 == 0);
     if (dev && (!need_align || aligned)) {
@@ -42,7 +43,7 @@ bool stage_in(DevCtx *c, int slot, const void *p, long rows, long cols, int es, 
     if (!d) return false;
     if (fault_injected("copy")) return false;
     cudaError_t e = cudaMemcpy2DAsync(d, ld * es, p, cols * es, cols * es, rows,
-                                      dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream);
+                                      dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) {
         check_cuda(e, X100_E_COPY);
         return false;
@@ -114,6 +115,83 @@ int f32_fast(DevCtx *c, int M, int N, int K, const float *A, long lda, const flo
     return launch_gemm_f32_fast(c, M, N, K, A, lda, B, ldb, C, ldc, s);
 }
 
+// Launch `route`'s kernel for C (M x N, ld ldc) += A (M x K) . B (K x N) on s.
+int launch_route(DevCtx *c, Route route, int M, int N, int K, const void *A, long lda, const void *B, long ldb,
+                 void *C, long ldc, cudaStream_t s) {
+    switch (route) {
+    case ROUTE_TC_I8: return launch_gemm_tc(c, 0, M, N, K, A, lda, B, ldb, C, ldc, s);
+    case ROUTE_SIMT_I8:
+        return launch_gemm_i8_simt(c, M, N, K, (const int8_t *)A, lda, (const int8_t *)B, ldb, (int32_t *)C, ldc, s);
+    case ROUTE_F32_FAST:
+        return f32_fast(c, M, N, K, (const float *)A, lda, (const float *)B, ldb, (float *)C, ldc, s);
+    case ROUTE_F32_REF:
+        return launch_gemm_f32_ref(c, M, N, K, (const float *)A, lda, (const float *)B, ldb, (float *)C, ldc, s);
+    case ROUTE_F16_F32C: return launch_gemm_tc(c, 1, M, N, K, A, lda, B, ldb, C, ldc, s);
+    case ROUTE_F16_F16C: return launch_gemm_tc(c, 2, M, N, K, A, lda, B, ldb, C, ldc, s);
+    }
+    return X100_E_ARG;
+}
+
+// Rows of C per panel of a panelled host call: a multiple of the 256-row
+// tile, at most DevCtx::kMaxPanels panels.
+constexpr long kPanelAlign = 256;
+// Host calls moving fewer bytes than this run as one copy-in, kernel, copy-out.
+constexpr size_t kPanelMinBytes = 32u << 20;
+
+// Host A and host C: the call runs as row panels so that the three engines
+// overlap.  On `up`: B (whole), then per panel its rows of A and of C; on
+// `stream`: panel p's kernel once ev[p] says its rows arrived; on `down`:
+// panel p's rows of C back once ev[kMaxPanels + p] says they are final.
+// Each row of C depends only on its row of A and on B, so the panels are the
+// whole product; the host->device and device->host copies run at the same
+// time (PCIe is full duplex) and the kernels hide behind them.
+int host_gemm_panels(DevCtx *c, Route route, int M, int N, int K, const void *A, const void *B, void *C, int es,
+                     size_t c_es, bool need_align, long pad) {
+    const long lda = need_align ? round_up(K, pad) : K;
+    const long rows = round_up((M + DevCtx::kMaxPanels - 1) / DevCtx::kMaxPanels, kPanelAlign);
+    const int P = (int)((M + rows - 1) / rows);
+    uint8_t *da = static_cast<uint8_t *>(stage_buf(c, 0, (size_t)lda * M * es));
+    uint8_t *dc = static_cast<uint8_t *>(stage_buf(c, 2, (size_t)M * N * c_es));
+    if (!da || !dc) return get_error();
+    if (fault_injected("copy")) return X100_E_INJECTED;
+    Operand b;
+    if (!stage_in(c, 1, B, K, N, es, pad, need_align, b, c->up)) {
+        cudaStreamSynchronize(c->up);
+        return get_error();
+    }
+    const uint8_t *ha = static_cast<const uint8_t *>(A);
+    uint8_t *hc = static_cast<uint8_t *>(C);
+    int st = X100_OK;
+    for (int p = 0; p < P && st == X100_OK; ++p) {
+        const long m0 = p * rows, mr = (M - m0 < rows) ? M - m0 : rows;
+        const size_t c_off = (size_t)m0 * N * c_es, c_bytes = (size_t)mr * N * c_es;
+        cudaError_t e = cudaMemcpy2DAsync(da + (size_t)m0 * lda * es, lda * es, ha + (size_t)m0 * K * es, (size_t)K * es,
+                                          (size_t)K * es, mr, cudaMemcpyHostToDevice, c->up);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dc + c_off, hc + c_off, c_bytes, cudaMemcpyHostToDevice, c->up);
+        if (e == cudaSuccess) e = cudaEventRecord(c->ev[p], c->up);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(c->stream, c->ev[p], 0);
+        if (e != cudaSuccess) {
+            st = check_cuda(e, X100_E_COPY);
+            break;
+        }
+        st = launch_route(c, route, (int)mr, N, K, da + (size_t)m0 * lda * es, lda, b.dev, b.ld, dc + c_off, N,
+                          c->stream);
+        if (st != X100_OK) break;
+        e = cudaEventRecord(c->ev[DevCtx::kMaxPanels + p], c->stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(c->down, c->ev[DevCtx::kMaxPanels + p], 0);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(hc + c_off, dc + c_off, c_bytes, cudaMemcpyDeviceToHost, c->down);
+        if (e != cudaSuccess) st = check_cuda(e, X100_E_COPY);
+    }
+    // every stream drains before the staging buffers can be reused
+    const cudaError_t eu = cudaStreamSynchronize(c->up);
+    const int sk = sync_and_status(c, c->stream);
+    const cudaError_t ed = cudaStreamSynchronize(c->down);
+    if (st == X100_OK && eu != cudaSuccess) st = check_cuda(eu, X100_E_COPY);
+    if (st == X100_OK) st = sk;
+    if (st == X100_OK && ed != cudaSuccess) st = check_cuda(ed, X100_E_COPY);
+    return st;
+}
+
 // One synchronous host-API GEMM call.
 void host_gemm(Route route, int M, int N, int K, const void *A, const void *B, void *C) {
     set_error(X100_OK);
@@ -128,35 +206,18 @@ void host_gemm(Route route, int M, int N, int K, const void *A, const void *B, v
     const bool need_align = route == ROUTE_TC_I8 || route == ROUTE_F32_FAST || is_f16;
     const long pad = 16 / es;
     const size_t c_es = (route == ROUTE_F16_F16C) ? 2 : 4;
+    const size_t moved = (size_t)M * K * es + (size_t)M * N * c_es;
+    if (M >= 2 * kPanelAlign && moved >= kPanelMinBytes && !is_device_ptr(A) && !is_device_ptr(C)) {
+        const int st = host_gemm_panels(c, route, M, N, K, A, B, C, es, c_es, need_align, pad);
+        if (st != X100_OK) set_error(st);
+        return;
+    }
     Operand a, b;
     COperand co;
-    if (!stage_in(c, 0, A, M, K, es, pad, need_align, a) || !stage_in(c, 1, B, K, N, es, pad, need_align, b) ||
-        !stage_c(c, 2, C, (size_t)M * N * c_es, true, co))
+    if (!stage_in(c, 0, A, M, K, es, pad, need_align, a, c->stream) ||
+        !stage_in(c, 1, B, K, N, es, pad, need_align, b, c->stream) || !stage_c(c, 2, C, (size_t)M * N * c_es, true, co))
         return;
-    int st = X100_OK;
-    switch (route) {
-    case ROUTE_TC_I8:
-        st = launch_gemm_tc(c, 0, M, N, K, a.dev, a.ld, b.dev, b.ld, co.dev, N, c->stream);
-        break;
-    case ROUTE_SIMT_I8:
-        st = launch_gemm_i8_simt(c, M, N, K, (const int8_t *)a.dev, a.ld, (const int8_t *)b.dev, b.ld,
-                                 (int32_t *)co.dev, N, c->stream);
-        break;
-    case ROUTE_F32_FAST:
-        st = f32_fast(c, M, N, K, (const float *)a.dev, a.ld, (const float *)b.dev, b.ld, (float *)co.dev, N,
-                      c->stream);
-        break;
-    case ROUTE_F32_REF:
-        st = launch_gemm_f32_ref(c, M, N, K, (const float *)a.dev, a.ld, (const float *)b.dev, b.ld,
-                                 (float *)co.dev, N, c->stream);
-        break;
-    case ROUTE_F16_F32C:
-        st = launch_gemm_tc(c, 1, M, N, K, a.dev, a.ld, b.dev, b.ld, co.dev, N, c->stream);
-        break;
-    case ROUTE_F16_F16C:
-        st = launch_gemm_tc(c, 2, M, N, K, a.dev, a.ld, b.dev, b.ld, co.dev, N, c->stream);
-        break;
-    }
+    int st = launch_route(c, route, M, N, K, a.dev, a.ld, b.dev, b.ld, co.dev, N, c->stream);
     if (st != X100_OK) {
         cudaStreamSynchronize(c->stream);
         set_error(st);
@@ -316,7 +377,8 @@ void gemm_ime2_i8_mt(int Mt, int Nt, int Kt, const int8_t *pa, const int8_t *pb,
     Operand a, b;
     COperand co;
     // packed operands (slots 0, 1), row-major operands (slot 3 holds both), C (slot 2)
-    if (!stage_in(c, 0, pa, 1, (long)na, 1, 16, false, a) || !stage_in(c, 1, pb, 1, (long)nb, 1, 16, false, b) ||
+    if (!stage_in(c, 0, pa, 1, (long)na, 1, 16, false, a, c->stream) ||
+        !stage_in(c, 1, pb, 1, (long)nb, 1, 16, false, b, c->stream) ||
         !stage_c(c, 2, C, nc, false, co))
         return;
     int8_t *rm = static_cast<int8_t *>(stage_buf(c, 3, na + nb));
