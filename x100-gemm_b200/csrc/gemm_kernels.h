@@ -17,6 +17,18 @@ int launch_gemm_tc(DevCtx *c, int kind, int M, int N, int K, const void *A, long
                    void *C, long ldc, cudaStream_t s);
 // True when (A, lda, B, ldb) satisfy the tensor-map alignment rules above.
 bool tc_operands_ok(int kind, const void *A, long lda, const void *B, long ldb);
+// The pieces of kind 3, for callers that prepare an operand once for several
+// products (row panels of one call):
+// hi[i] = x[i] rounded to tf32, lo[i] = x[i] - hi[i], i < n;
+int tf32_split(DevCtx *c, const float *x, long n, float *hi, float *lo, cudaStream_t s);
+// bt[n][k] = hi(B[k][n]), btlo[n][k] = lo(B[k][n]) (row stride ldt >= K,
+// ldt * 4 a multiple of 16 bytes);
+int tf32_split_transpose(DevCtx *c, const float *B, long ldb, int K, int N, float *bt, float *btlo, long ldt,
+                         cudaStream_t s);
+// C += A_hi.B_hi + A_hi.B_lo + A_lo.B_hi from split operands (A parts row
+// stride lda, B parts transposed with row stride ldt).
+int launch_gemm_tf32x3(DevCtx *c, int M, int N, int K, const float *ahi, const float *alo, long lda, const float *bt,
+                       const float *btlo, long ldt, float *C, long ldc, cudaStream_t s);
 
 // CUDA-core kernels (gemm_simt.cu).
 int launch_gemm_i8_simt(DevCtx *c, int M, int N, int K, const int8_t *A, long lda, const int8_t *B, long ldb,

@@ -863,20 +863,43 @@ int launch_gemm_tc(DevCtx *c, int kind, int M, int N, int K, const void *A, long
         const long ldt = (K + 3) & ~3L;   // 16-byte rows
         const long nt = (long)N * ldt;
         float *scr = nullptr;
-        if (check_cuda(cudaMallocAsync(reinterpret_cast<void **>(&scr), (size_t)(2 * nap + 2 * nt) * 4, s),
+        if (check_cuda(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&scr), (size_t)(2 * nap + 2 * nt) * 4,
+                                               c->pool, s),
                        X100_E_ALLOC))
             return X100_E_ALLOC;
         float *ahi = scr, *alo = scr + nap, *bt = scr + 2 * nap, *bt2 = bt + nt;
-        tc::split_tf32_kernel<<<c->sm_count * 4, 256, 0, s>>>(static_cast<const float *>(A), ahi, alo, na);
-        tc::transpose_split_kernel<<<dim3((N + 31) / 32, (K + 31) / 32), dim3(32, 8), 0, s>>>(
-            static_cast<const float *>(B), ldb, K, N, bt, bt2, ldt);
-        int st = check_cuda(cudaGetLastError(), X100_E_LAUNCH);
-        if (!st) st = tc::launch_kind<3>(c, M, N, K, ahi, lda, bt, ldt, C, ldc, s, alo, bt2);
+        int st = tf32_split(c, static_cast<const float *>(A), na, ahi, alo, s);
+        if (!st) st = tf32_split_transpose(c, static_cast<const float *>(B), ldb, K, N, bt, bt2, ldt, s);
+        if (!st) st = launch_gemm_tf32x3(c, M, N, K, ahi, alo, lda, bt, bt2, ldt, static_cast<float *>(C), ldc, s);
         cudaFreeAsync(scr, s);
         return st;
     }
     default: set_error(X100_E_ARG); return X100_E_ARG;
     }
+}
+
+int tf32_split(DevCtx *c, const float *x, long n, float *hi, float *lo, cudaStream_t s) {
+    tc::split_tf32_kernel<<<c->sm_count * 4, 256, 0, s>>>(x, hi, lo, n);
+    return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+}
+
+int tf32_split_transpose(DevCtx *c, const float *B, long ldb, int K, int N, float *bt, float *btlo, long ldt,
+                         cudaStream_t s) {
+    (void)c;
+    tc::transpose_split_kernel<<<dim3((N + 31) / 32, (K + 31) / 32), dim3(32, 8), 0, s>>>(B, ldb, K, N, bt, btlo,
+                                                                                       ldt);
+    return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+}
+
+int launch_gemm_tf32x3(DevCtx *c, int M, int N, int K, const float *ahi, const float *alo, long lda, const float *bt,
+                       const float *btlo, long ldt, float *C, long ldc, cudaStream_t s) {
+    if (c->cc_major != 10) {
+        set_error(X100_E_ARCH);
+        return X100_E_ARCH;
+    }
+    if (M <= 0 || N <= 0 || K <= 0) return X100_OK;
+    if (fault_injected("launch")) return X100_E_INJECTED;
+    return tc::launch_kind<3>(c, M, N, K, ahi, lda, bt, ldt, C, ldc, s, alo, btlo);
 }
 
 }  // namespace x100

@@ -88,6 +88,15 @@ DevCtx *ctx() {
                   cudaStreamCreateWithFlags(&c->down, cudaStreamNonBlocking) == cudaSuccess &&
                   cudaMalloc(&c->d_status, 64) == cudaSuccess && cudaMemset(c->d_status, 0, 64) == cudaSuccess;
         for (cudaEvent_t &e : c->ev) ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+        if (ok) {
+            cudaMemPoolProps pp = {};
+            pp.allocType = cudaMemAllocationTypePinned;
+            pp.location.type = cudaMemLocationTypeDevice;
+            pp.location.id = dev;
+            uint64_t keep = DevCtx::kPoolKeepBytes;
+            ok = cudaMemPoolCreate(&c->pool, &pp) == cudaSuccess &&
+                 cudaMemPoolSetAttribute(c->pool, cudaMemPoolAttrReleaseThreshold, &keep) == cudaSuccess;
+        }
         if (!ok) {
             cudaGetLastError();
             delete c;

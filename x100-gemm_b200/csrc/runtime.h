@@ -35,14 +35,21 @@ struct DevCtx {
     size_t smem_optin = 0;
     cudaStream_t stream = nullptr;   // stream of the synchronous host-pointer API
     int *d_status = nullptr;         // device status word written by kernels
-    DevBuf stage[4];                 // staging buffers of host-pointer calls
+    DevBuf stage[6];                 // staging buffers of host-pointer calls
     std::mutex mu;                   // serialises host-pointer calls on this device
     // Panelled host-pointer calls: host->device copies on `up`, device->host
     // copies on `down`, the kernels on `stream`; ev[p] marks panel p's inputs
     // staged, ev[kMaxPanels + p] panel p computed.
+    // ev[2 * kMaxPanels] marks B staged.
     static constexpr int kMaxPanels = 8;
     cudaStream_t up = nullptr, down = nullptr;
-    cudaEvent_t ev[2 * kMaxPanels] = {};
+    cudaEvent_t ev[2 * kMaxPanels + 1] = {};
+    // Stream-ordered scratch of kernels that need temporaries (the tf32
+    // split operands): a pool of the library's own that keeps up to
+    // kPoolKeepBytes mapped across synchronisations, so a call after a sync
+    // does not map its scratch again.
+    static constexpr uint64_t kPoolKeepBytes = 4ull << 30;
+    cudaMemPool_t pool = nullptr;
 };
 
 // Context of the calling thread's selected device (created on first use).

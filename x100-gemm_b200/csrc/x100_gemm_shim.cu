@@ -162,6 +162,25 @@ int host_gemm_panels(DevCtx *c, Route route, int M, int N, int K, const void *A,
     const uint8_t *ha = static_cast<const uint8_t *>(A);
     uint8_t *hc = static_cast<uint8_t *>(C);
     int st = X100_OK;
+    // fp32 on the tensor cores: B is split into its transposed tf32 high and
+    // low parts once for all panels (slot 4), each panel's rows of A into
+    // theirs (slot 5) as they arrive
+    static const bool ffma = getenv("X100_GEMM_F32_FFMA") != nullptr;
+    bool tf32 = route == ROUTE_F32_FAST && !ffma && tc_operands_ok(3, da, lda, b.dev, b.ld);
+    const long ldt = (K + 3) & ~3L;
+    float *bt = nullptr, *as = nullptr;
+    if (tf32) {
+        bt = static_cast<float *>(stage_buf(c, 4, (size_t)2 * N * ldt * 4));
+        as = static_cast<float *>(stage_buf(c, 5, (size_t)2 * M * lda * 4));
+        if (!bt || !as) st = get_error();
+        cudaError_t e = cudaSuccess;
+        if (!st) e = cudaEventRecord(c->ev[2 * DevCtx::kMaxPanels], c->up);
+        if (!st && e == cudaSuccess) e = cudaStreamWaitEvent(c->stream, c->ev[2 * DevCtx::kMaxPanels], 0);
+        if (!st && e != cudaSuccess) st = check_cuda(e, X100_E_COPY);
+        if (!st)
+            st = tf32_split_transpose(c, static_cast<const float *>(b.dev), b.ld, K, N, bt, bt + (size_t)N * ldt, ldt,
+                                      c->stream);
+    }
     for (int p = 0; p < P && st == X100_OK; ++p) {
         const long m0 = p * rows, mr = (M - m0 < rows) ? M - m0 : rows;
         const size_t c_off = (size_t)m0 * N * c_es, c_bytes = (size_t)mr * N * c_es;
@@ -174,8 +193,22 @@ int host_gemm_panels(DevCtx *c, Route route, int M, int N, int K, const void *A,
             st = check_cuda(e, X100_E_COPY);
             break;
         }
-        st = launch_route(c, route, (int)mr, N, K, da + (size_t)m0 * lda * es, lda, b.dev, b.ld, dc + c_off, N,
-                          c->stream);
+        if (tf32) {
+            float *ahi = as + (size_t)m0 * lda, *alo = as + (size_t)M * lda + (size_t)m0 * lda;
+            st = tf32_split(c, reinterpret_cast<const float *>(da + (size_t)m0 * lda * es), (long)mr * lda, ahi, alo,
+                            c->stream);
+            if (!st)
+                st = launch_gemm_tf32x3(c, (int)mr, N, K, ahi, alo, lda, bt, bt + (size_t)N * ldt, ldt,
+                                        reinterpret_cast<float *>(dc + c_off), N, c->stream);
+            if (st == X100_E_UNSUPPORTED) {   // CTA pairs cannot run: the FFMA kernel from here on
+                set_error(X100_OK);
+                tf32 = false;
+                st = X100_OK;
+            }
+        }
+        if (!tf32 && !st)
+            st = launch_route(c, route, (int)mr, N, K, da + (size_t)m0 * lda * es, lda, b.dev, b.ld, dc + c_off, N,
+                              c->stream);
         if (st != X100_OK) break;
         e = cudaEventRecord(c->ev[DevCtx::kMaxPanels + p], c->stream);
         if (e == cudaSuccess) e = cudaStreamWaitEvent(c->down, c->ev[DevCtx::kMaxPanels + p], 0);
