@@ -131,7 +131,8 @@ enum {
     X100_E_COMM     = 8,   /* collective / peer exchange failed              */
     X100_E_INJECTED = 9,   /* failure injected by X100_FAULT                 */
     X100_E_UNSUPPORTED = 10,
-    X100_E_TOO_LARGE = 11  /* request exceeds a fixed-size scratch area      */
+    X100_E_TOO_LARGE = 11, /* request exceeds a fixed-size scratch area      */
+    X100_E_FORMAT   = 12   /* malformed file, or a tensor missing / of a type that cannot be used */
 };
 /* Last status recorded on the calling thread (0 when the last call worked). */
 int         x100_last_error(void);

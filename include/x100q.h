@@ -240,6 +240,88 @@ int       x100q_ep_allreduce_dev(x100q_ep *ep, const float *src, float *dst, int
                                  int accum, void *stream);
 void      x100q_ep_destroy(x100q_ep *ep);
 
+/* ---- GGUF ingest ----------------------------------------------------------
+ * Replaces the reference's GGUF reader and model loader (gguf_open /
+ * gguf_find / gguf_dequant_into / model_load, qwen_moe_q3k.c:1086-1159 and
+ * :1742-1787; qwen_moe.c:110-181).  The file is mapped read-only; every
+ * offset and length read from it is checked against the file size, and a
+ * malformed file, a missing tensor or an unusable type is reported as
+ * X100_E_FORMAT (the reference prints and exits).  Tensor data is decoded or
+ * re-quantised on the device when loaded.                                   */
+
+/* The further ggml tensor types the loader decodes (with those above).      */
+enum {
+    X100Q_F16  = 1,
+    X100Q_Q4_1 = 3,    /* 20 B / 32: fp16 d, fp16 m, 16 B nibbles  nib*d + m   */
+    X100Q_Q5_K = 13,   /* 176 B / 256: d, dmin, scales[12], qh[32], qs[128]    */
+    X100Q_Q6_K = 14    /* 210 B / 256: ql[128], qh[64], int8 scales[16], d     */
+};
+
+typedef struct x100q_gguf x100q_gguf;
+
+typedef struct {
+    const char *name;     /* NUL-terminated, owned by the handle              */
+    int type;             /* ggml type id                                     */
+    int n_dims;           /* 1..4                                             */
+    uint64_t dims[4];     /* dims[0] is the contiguous row length             */
+    uint64_t n_elems;
+    uint64_t bytes;       /* size of the data; 0 for a type without a known size */
+    const void *data;     /* inside the mapped file (host memory)            */
+} x100q_gguf_tensor;
+
+/* Map and parse a GGUF file (versions 2 and 3).  NULL + x100_last_error()
+ * on failure (X100_E_FORMAT for a malformed file, X100_E_ARG for a path that
+ * cannot be opened).  No GPU is needed until a model is loaded.             */
+x100q_gguf *x100q_gguf_open(const char *path);
+void        x100q_gguf_close(x100q_gguf *g);
+int         x100q_gguf_n_tensors(const x100q_gguf *g);
+/* Tensor i in file order, or the tensor called `name`: 0, X100_E_ARG (index
+ * out of range), X100_E_FORMAT (no such tensor).                           */
+int         x100q_gguf_tensor_at(const x100q_gguf *g, int i, x100q_gguf_tensor *out);
+int         x100q_gguf_find(const x100q_gguf *g, const char *name, x100q_gguf_tensor *out);
+/* Byte offset of the tensor data section in the file.                      */
+uint64_t    x100q_gguf_data_offset(const x100q_gguf *g);
+/* tokenizer.ggml.tokens: count, and token `id` (NULL when out of range).   */
+int         x100q_gguf_n_tokens(const x100q_gguf *g);
+const char *x100q_gguf_token(const x100q_gguf *g, int id);
+/* Metadata by key: 0, X100_E_FORMAT (absent or not convertible).  get_int
+ * reads any integer or bool type; get_f32 reads F32 or F64; get_str returns
+ * a NUL-terminated copy owned by the handle.                               */
+int         x100q_gguf_get_int(const x100q_gguf *g, const char *key, int64_t *out);
+int         x100q_gguf_get_f32(const x100q_gguf *g, const char *key, float *out);
+int         x100q_gguf_get_str(const x100q_gguf *g, const char *key, const char **out);
+
+/* Model configuration of a qwen3moe file, read as the reference reads it
+ * (qwen_moe_q3k.c:1098-1126, :1742-1744): qwen3moe.{block_count,
+ * embedding_length, attention.head_count, attention.head_count_kv,
+ * attention.key_length, expert_count (default 128), expert_used_count (8),
+ * expert_feed_forward_length (768), rope.freq_base (1e6)}; eps 1e-6; vocab =
+ * dims[1] of token_embd.weight.  Weight types: attn_qtype is the type every
+ * layer's attn_q/k/v/output share when the decode GEMV takes it, else Q8_0;
+ * expert_qtype likewise for the expert tensors; lm_qtype is output.weight's
+ * type when the GEMV takes it, else Q8_0 (also for a tied lm_head).  ctx =
+ * 4096, max_batch = 1, all experts: edit these before loading.             */
+int x100q_gguf_model_cfg(const x100q_gguf *g, x100q_model_cfg *cfg);
+
+/* Create a model with `cfg` (dimensions as x100q_gguf_model_cfg reads them)
+ * and upload every layer's weights from the file: a tensor whose type is the
+ * slot's is uploaded as it is; any other decodable type is decoded to fp32
+ * on the device and, for a weight slot, re-quantised to Q8_0 as the
+ * reference's lin_new_i8 does (quantize_q8_0_native, qwen_moe_q3k.c:409-414),
+ * so a slot of another type takes only its own type.  fp32 slots (norms,
+ * router, token embeddings) take any decodable type.  A missing
+ * output.weight ties the lm_head to the token embeddings (Q8_0 of them,
+ * qwen_moe_q3k.c:1747-1750).  NULL + x100_last_error() on failure.         */
+x100q_model *x100q_model_load_gguf(const x100q_gguf *g, const x100q_model_cfg *cfg);
+
+/* Device decoders used by the loader, asynchronous on `stream`:
+ * n elements of GGUF `type` data (device pointer, n a whole number of
+ * blocks) to fp32, bit-identical to the reference's gguf_dequant_into
+ * (qwen_moe_q3k.c:1129-1158; Q4_K as its Q5_K decoder with a zero fifth bit);
+ * and n fp32 values (n % 32 == 0) to Q8_0 blocks as quantize_q8_0_native.  */
+int x100q_gguf_dequant_dev(int type, const void *data, long n, float *out, void *stream);
+int x100q_quantize_q8_0_dev(const float *x, long n, void *blocks, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -204,6 +204,141 @@ void orc_dequant_row(int qtype, const void *blocks, int K, float *out)
     }
 }
 
+/* ---- the other GGUF tensor types (decode only; loader conversions) -------*/
+
+/* qwen_moe.c:115-118 bit-for-bit; F16 tensors hold plain IEEE halves. */
+static void dq_f16(const uint8_t *p, float *y) { *y = rd_f16(p); }
+
+/* qwen_moe_q3k.c:1138 (typ 3): 20 B per 32: fp16 d, fp16 m, 16 B nibbles
+ * laid out as Q4_0; w = nib * d + m (two roundings, no fused multiply-add). */
+static void dq_q4_1(const uint8_t *blk, float *y)
+{
+    float d = rd_f16(blk), m = rd_f16(blk + 2);
+    const uint8_t *qs = blk + 4;
+    for (int j = 0; j < 32; j++) {
+        int nib = (j < 16) ? (qs[j] & 0xf) : (qs[j - 16] >> 4);
+        float t = (float)nib * d;
+        y[j] = t + m;
+    }
+}
+
+/* qwen_moe_q3k.c:540-551 (dequantize_q5_K_block): block_q5_K = fp16 d @0,
+ * fp16 dmin @2, scales[12] @4, qh[32] @16, qs[128] @48.  Chunk c of 64
+ * elements: scale/min pairs 2c (low nibbles of qs[32c..+31]) and 2c+1 (high
+ * nibbles); the fifth bit of element l of the low half is bit 2c of qh[l], of
+ * the high half bit 2c+1.  w = (d*sc)*q - dmin*m.                           */
+static void dq_q5_k(const uint8_t *blk, float *y)
+{
+    float d = rd_f16(blk), dmin = rd_f16(blk + 2);
+    const uint8_t *sc = blk + 4, *qh = blk + 16, *qs = blk + 48;
+    for (int c = 0; c < 4; c++) {
+        uint8_t s0, m0, s1, m1;
+        orc_kq_scale_min(2 * c, sc, &s0, &m0);
+        orc_kq_scale_min(2 * c + 1, sc, &s1, &m1);
+        float d1 = d * (float)s0, mm1 = dmin * (float)m0;
+        float d2 = d * (float)s1, mm2 = dmin * (float)m1;
+        const uint8_t *q = qs + 32 * c;
+        for (int l = 0; l < 32; l++) {
+            int v = (q[l] & 0xF) + ((qh[l] >> (2 * c)) & 1) * 16;
+            y[64 * c + l] = d1 * (float)v - mm1;
+        }
+        for (int l = 0; l < 32; l++) {
+            int v = (q[l] >> 4) + ((qh[l] >> (2 * c + 1)) & 1) * 16;
+            y[64 * c + 32 + l] = d2 * (float)v - mm2;
+        }
+    }
+}
+
+/* qwen_moe_q3k.c:1148-1157 (typ 14): block_q6_K = ql[128] @0, qh[64] @128,
+ * int8 scales[16] @192, fp16 d @208.  Half h (128 elements) uses ql[64h..],
+ * qh[32h..], scales[8h..]; its quarter t (32 elements, l < 32) takes the low
+ * (t = 0, 1) or high (t = 2, 3) nibble of ql[64h + l + 32*(t & 1)], bits
+ * 2t..2t+1 of qh[32h + l] as bits 4-5, minus 32, times d * scale[8h + 2t +
+ * l/16].                                                                    */
+static void dq_q6_k(const uint8_t *blk, float *y)
+{
+    const uint8_t *ql = blk, *qh = blk + 128;
+    const int8_t *sc = (const int8_t *)(blk + 192);
+    float d = rd_f16(blk + 208);
+    for (int h = 0; h < 2; h++)
+        for (int t = 0; t < 4; t++)
+            for (int l = 0; l < 32; l++) {
+                int lo = ql[64 * h + l + 32 * (t & 1)];
+                lo = (t < 2) ? (lo & 0xF) : (lo >> 4);
+                int q = (lo | (((qh[32 * h + l] >> (2 * t)) & 3) << 4)) - 32;
+                float ds = d * (float)sc[8 * h + 2 * t + l / 16];
+                y[128 * h + 32 * t + l] = ds * (float)q;
+            }
+}
+
+static int gguf_block(int type, int *elems, int *bytes)
+{
+    switch (type) {
+    case ORC_F32: *elems = 1; *bytes = 4; return 0;
+    case ORC_F16: *elems = 1; *bytes = 2; return 0;
+    case ORC_Q4_0: *elems = 32; *bytes = 18; return 0;
+    case ORC_Q4_1: *elems = 32; *bytes = 20; return 0;
+    case ORC_Q8_0: *elems = 32; *bytes = 34; return 0;
+    case ORC_Q3_K: *elems = 256; *bytes = 110; return 0;
+    case ORC_Q4_K: *elems = 256; *bytes = 144; return 0;
+    case ORC_Q5_K: *elems = 256; *bytes = 176; return 0;
+    case ORC_Q6_K: *elems = 256; *bytes = 210; return 0;
+    default: return -1;
+    }
+}
+
+size_t orc_gguf_bytes(int type, size_t n)
+{
+    int be, bb;
+    if (gguf_block(type, &be, &bb) || n % (size_t)be) return 0;
+    return n / (size_t)be * (size_t)bb;
+}
+
+int orc_dequant_gguf(int type, const void *data, size_t n, float *out)
+{
+    int be, bb;
+    if (gguf_block(type, &be, &bb) || n % (size_t)be) return -1;
+    const uint8_t *b = (const uint8_t *)data;
+    for (size_t i = 0; i < n / (size_t)be; i++) {
+        const uint8_t *blk = b + i * (size_t)bb;
+        float *y = out + i * (size_t)be;
+        switch (type) {
+        case ORC_F32: memcpy(y, blk, 4); break;
+        case ORC_F16: dq_f16(blk, y); break;
+        case ORC_Q4_0: dq_q4_0(blk, y); break;
+        case ORC_Q4_1: dq_q4_1(blk, y); break;
+        case ORC_Q8_0: dq_q8_0(blk, y); break;
+        case ORC_Q3_K: dq_q3_k(blk, y); break;
+        case ORC_Q4_K: dq_q4_k(blk, y); break;
+        case ORC_Q5_K: dq_q5_k(blk, y); break;
+        case ORC_Q6_K: dq_q6_k(blk, y); break;
+        }
+    }
+    return 0;
+}
+
+void orc_quantize_q8_0_ref(const float *x, size_t n, void *blocks)
+{
+    uint8_t *out = (uint8_t *)blocks;
+    for (size_t b = 0; b < n / 32; b++) {
+        const float *w = x + 32 * b;
+        uint8_t *blk = out + 34 * b;
+        float amax = 1e-6f;
+        for (int i = 0; i < 32; i++) {
+            float v = fabsf(w[i]);
+            if (v > amax) amax = v;
+        }
+        float d = amax / 127.0f;
+        float inv = d != 0.0f ? 1.0f / d : 0.0f;
+        uint16_t h = orc_f32_to_f16_trunc(d);
+        memcpy(blk, &h, 2);
+        for (int i = 0; i < 32; i++) {
+            long q = lrintf(w[i] * inv);
+            blk[2 + i] = (uint8_t)(int8_t)(q > 127 ? 127 : (q < -128 ? -128 : q));
+        }
+    }
+}
+
 /* ---- encode (own encoders, written from the format definitions) ---------*/
 
 static int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }

@@ -21,6 +21,10 @@ Q_F32, Q4_0, Q8_0, Q3_K, Q4_K = 0, 2, 8, 11, 12
 BLOCK_ELEMS = {Q_F32: 1, Q4_0: 32, Q8_0: 32, Q3_K: 256, Q4_K: 256}
 BLOCK_BYTES = {Q_F32: 4, Q4_0: 18, Q8_0: 34, Q3_K: 110, Q4_K: 144}
 QNAMES = {Q4_0: "Q4_0", Q8_0: "Q8_0", Q3_K: "Q3_K", Q4_K: "Q4_K", Q_F32: "F32"}
+# further GGUF tensor types (decode only): id -> (elements, bytes) per block
+F16, Q4_1, Q5_K, Q6_K = 1, 3, 13, 14
+GGUF_BLOCK = {Q_F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q4_1: (32, 20), Q8_0: (32, 34), Q3_K: (256, 110),
+              Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
 
 _lib = None
 _ref = None
@@ -73,6 +77,12 @@ def lib():
         L.orc_f32_to_f16_rne.restype = C.c_uint16
         L.orc_f32_to_f16_trunc.argtypes = [C.c_float]
         L.orc_f32_to_f16_trunc.restype = C.c_uint16
+        L.orc_dequant_gguf.argtypes = [i, vp, C.c_size_t, vp]
+        L.orc_dequant_gguf.restype = C.c_int
+        L.orc_gguf_bytes.argtypes = [i, C.c_size_t]
+        L.orc_gguf_bytes.restype = C.c_size_t
+        L.orc_quantize_q8_0_ref.argtypes = [vp, C.c_size_t, vp]
+        L.orc_quantize_q8_0_ref.restype = None
         L.orc_silu.argtypes = [C.c_float]
         L.orc_silu.restype = C.c_float
         _lib = L
@@ -110,6 +120,29 @@ def rand_f32(seed: int, n: int, lo=-1.0, hi=1.0) -> np.ndarray:
     """Uniform fp32 in [lo, hi) with 24-bit resolution (exactly representable)."""
     u = fill_u8(seed, 4 * n).view(np.uint32)
     return (lo + (hi - lo) * ((u >> 8).astype(np.float64) / float(1 << 24))).astype(np.float32)
+
+
+# ---- GGUF tensor types ---------------------------------------------------------
+def gguf_bytes(gtype: int, n: int) -> int:
+    return int(lib().orc_gguf_bytes(gtype, n))
+
+
+def dequant_gguf(gtype: int, data: np.ndarray, n: int) -> np.ndarray:
+    """n elements of a GGUF tensor of any decodable type, as fp32."""
+    data = np.ascontiguousarray(data).view(np.uint8)
+    assert data.nbytes >= gguf_bytes(gtype, n) > 0
+    out = np.empty(n, np.float32)
+    assert lib().orc_dequant_gguf(gtype, _ptr(data), n, _ptr(out)) == 0
+    return out
+
+
+def quantize_q8_0_ref(x: np.ndarray) -> np.ndarray:
+    """The reference's Q8_0 requantisation of fp32 values (n % 32 == 0)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    assert x.size % 32 == 0
+    out = np.empty(x.size // 32 * 34, np.uint8)
+    lib().orc_quantize_q8_0_ref(_ptr(x), x.size, _ptr(out))
+    return out
 
 
 # ---- GEMM -------------------------------------------------------------------

@@ -34,12 +34,25 @@ uint16_t orc_f32_to_f16_trunc(float f);       /* qwen_moe_hp.c:71-79         */
 
 /* ---- block formats: sizes ------------------------------------------------ */
 enum { ORC_F32 = 0, ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_Q3_K = 11, ORC_Q4_K = 12 };
+/* further ggml types a GGUF file may hold (decode only) */
+enum { ORC_F16 = 1, ORC_Q4_1 = 3, ORC_Q5_K = 13, ORC_Q6_K = 14 };
 int    orc_block_elems(int qtype);            /* 32 or 256                    */
 int    orc_block_bytes(int qtype);            /* 18, 34, 110, 144             */
 size_t orc_row_bytes(int qtype, int K);
 
 /* ---- block formats: decode (n elements = whole blocks) ------------------ */
 void orc_dequant_row(int qtype, const void *blocks, int K, float *out);
+/* n elements (a whole number of blocks) of a GGUF tensor of any type
+ * gguf_dequant_into decodes (qwen_moe_q3k.c:1129-1158): F32, F16, Q4_0,
+ * Q4_1, Q8_0, Q3_K, Q4_K, Q5_K, Q6_K.  Returns 0, or -1 for another type.  */
+int orc_dequant_gguf(int type, const void *data, size_t n, float *out);
+/* Bytes of n elements of a GGUF tensor of `type` (0: unknown type or n not a
+ * whole number of blocks). */
+size_t orc_gguf_bytes(int type, size_t n);
+/* quantize_q8_0_native (qwen_moe_q3k.c:409-414) over n floats (n % 32 == 0):
+ * amax from 1e-6, d = amax/127, q = lrint(w/d) clamped to [-128, 127], d
+ * stored as the truncating fp16 of qwen_moe_q3k.c:71-79.                    */
+void orc_quantize_q8_0_ref(const float *x, size_t n, void *blocks);
 /* scale/min pair j of a K-quant 12-byte scale array (qwen_moe_q3k.c:534-538,
  * repack.cpp:222-233)                                                      */
 void orc_kq_scale_min(int j, const uint8_t *q, uint8_t *sc, uint8_t *m);

@@ -21,6 +21,16 @@ What it pins, and from which reference code:
                     applied to random well-formed blocks (random bytes, fp16
                     scales in a bounded range, as bench/q3k_probe.c:418-425
                     builds its test blocks) plus edge blocks.
+  gguf_golden.npz   the GGUF tensor decoders of the reference's Q3_K engine
+                    (gguf_dequant_into, qwen_moe_q3k.c:1129-1158: F32, F16,
+                    Q4_0, Q4_1, Q8_0, Q3_K, Q5_K, Q6_K) on random well-formed
+                    blocks plus edge blocks, and its Q8_0 requantiser
+                    (quantize_q8_0_native, qwen_moe_q3k.c:409-414, with the
+                    truncating f32_to_f16 of :71-79) on fp32 rows.
+  gguf_parse.json   what the reference's GGUF reader (gguf_open,
+                    qwen_moe_q3k.c:1098-1126) reads from a synthetic file made
+                    by tests/gguf_writer.py (make_parse_file below): model
+                    dimensions, defaults, tokens, tensor infos, data start.
   meta.json         struct-size known answers (block_q3_K 110 B,
                     block_q5_K 176 B, bench/q3k_probe.c:410-413) and the
                     x100_caps_t layout of the reference header.
@@ -118,6 +128,63 @@ void golden_dq_gguf(unsigned typ,const void*data,size_t n,float*out){
     return L
 
 
+def build_ref_gguf(tmp: str) -> C.CDLL:
+    """The Q3_K engine's GGUF reader, tensor decoders and Q8_0 requantiser,
+    extracted unchanged from qwen_moe_q3k.c and compiled under tmp."""
+    q3k = open(os.path.join(REF_ROOT, "qwen_moe_q3k.c")).read()
+    parts = [
+        "#include <stdio.h>\n#include <stdlib.h>\n#include <stdint.h>\n#include <string.h>\n#include <math.h>\n"
+        "#include <fcntl.h>\n#include <sys/mman.h>\n#include <sys/stat.h>\n#include <unistd.h>\n",
+        extract_function(q3k, r"static uint16_t f32_to_f16\(float f\)\{"),
+        extract_line(q3k, r"^typedef struct \{ uint16_t d; int8_t qs\[32\]; \} q8_0_native;$"),
+        extract_function(q3k, r"static void quantize_q8_0_native\(const float\*w /\*32 elems\*/, q8_0_native\*out\)\{"),
+        extract_line(q3k, r"^typedef struct \{ uint8_t hmask\[32\];.*\} block_q3_K;.*$"),
+        extract_line(q3k, r"^typedef struct \{ _Float16 d; _Float16 dmin;.*\} block_q5_K;.*$"),
+        extract_function(q3k, r"static inline void q5k_get_scale_min\(int j,const uint8_t\*q,uint8_t\*d,uint8_t\*m\)\{"),
+        extract_function(q3k, r"static void dequantize_q5_K_block\(const block_q5_K\*x,float\*y\)\{"),
+        extract_function(q3k, r"static void dequantize_q3_K_block\(const block_q3_K\*x,float\*y\)\{"),
+        extract_line(q3k, r"^typedef struct \{ uint32_t typ;.*\} TInfo;$"),
+        extract_line(q3k, r"^typedef struct \{ unsigned char\*p;[^\n]*\n[^\n]*\} Gguf;$"),
+        extract_function(q3k, r"static uint64_t U64\(unsigned char\*b\)\{"),
+        extract_function(q3k, r"static uint32_t U32\(unsigned char\*b\)\{"),
+        extract_function(q3k, r"static float f16f\(uint16_t h\)\{"),
+        extract_function(q3k, r"static size_t skipval\(unsigned char\*p,uint32_t t\)\{"),
+        extract_function(q3k, r"static void gguf_open\(Gguf\*g,const char\*path\)\{"),
+        extract_function(q3k, r"static void gguf_dequant_into\(Gguf\*g,TInfo\*ti,size_t elem0,size_t n,float\*out\)\{"),
+        # thin exported wrappers (written here, not reference code)
+        """
+void golden_dq(unsigned typ,const void*data,size_t n,float*out){
+  Gguf g; memset(&g,0,sizeof g); g.p=(unsigned char*)data; g.data_start=0;
+  TInfo t; memset(&t,0,sizeof t); t.typ=typ; t.off=0; gguf_dequant_into(&g,&t,0,n,out); }
+void golden_q8(const float*w,size_t n,void*out){ for(size_t b=0;b<n/32;b++) quantize_q8_0_native(w+32*b,(q8_0_native*)out+b); }
+size_t golden_sizeof_q8(void){ return sizeof(q8_0_native); }
+static Gguf G;
+void golden_open(const char*path,long*ints,float*rope){ memset(&G,0,sizeof G); gguf_open(&G,path);
+  ints[0]=G.block_count; ints[1]=G.embd; ints[2]=G.ffn; ints[3]=G.nh; ints[4]=G.nkv; ints[5]=G.hd;
+  ints[6]=G.vocab; ints[7]=G.n_exp; ints[8]=G.n_act; ints[9]=G.moe_ffn; ints[10]=G.nt; ints[11]=(long)G.data_start;
+  ints[12]=G.ntok; *rope=G.rope_base; }
+const char*golden_token(int i){ return G.tok[i]; }
+void golden_tensor(int i,char*name,long*v){ TInfo*t=&G.t[i]; strcpy(name,t->name); v[0]=t->typ; v[1]=t->nd;
+  for(int d=0;d<4;d++) v[2+d]=(long)t->dims[d]; v[6]=(long)t->off; }
+""",
+    ]
+    path = os.path.join(tmp, "refgguf.c")
+    with open(path, "w") as f:
+        f.write("\n".join(parts))
+    so = os.path.join(tmp, "librefgguf.so")
+    subprocess.check_call(["gcc", "-std=gnu11", "-O2", "-ffp-contract=off", "-fPIC", "-shared",
+                           "-o", so, path, "-lm"])
+    L = C.CDLL(so)
+    L.golden_dq.argtypes = [C.c_uint, C.c_void_p, C.c_size_t, C.c_void_p]
+    L.golden_q8.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p]
+    L.golden_sizeof_q8.restype = C.c_size_t
+    L.golden_open.argtypes = [C.c_char_p, C.c_void_p, C.c_void_p]
+    L.golden_token.argtypes = [C.c_int]
+    L.golden_token.restype = C.c_char_p
+    L.golden_tensor.argtypes = [C.c_int, C.c_char_p, C.c_void_p]
+    return L
+
+
 def caps_layout(tmp: str) -> dict:
     prog = os.path.join(tmp, "caps.c")
     with open(prog, "w") as f:
@@ -183,7 +250,120 @@ def to_q5k_layout(q4k: np.ndarray) -> np.ndarray:
     return out
 
 
+GGUF_TYPES = ((po.Q_F32, "F32"), (po.F16, "F16"), (po.Q4_0, "Q4_0"), (po.Q4_1, "Q4_1"), (po.Q8_0, "Q8_0"),
+              (po.Q3_K, "Q3_K"), (po.Q5_K, "Q5_K"), (po.Q6_K, "Q6_K"))
+
+
+def gguf_edge_blocks(gtype: int) -> np.ndarray:
+    """Zero, all-ones payload with unit scales, subnormal and large scales."""
+    be, bb = po.GGUF_BLOCK[gtype]
+    if gtype == po.Q_F32:
+        return np.array([0.0, -0.0, 1e-40, -3.4e38, 1.0], np.float32).view(np.uint8).reshape(-1, 4)
+    if gtype == po.F16:
+        return np.array([0x0000, 0x8000, 0x0001, 0x03FF, 0x7BFF, 0xFBFF, 0x3C00], np.uint16).view(np.uint8).reshape(-1, 2)
+    dpos = {po.Q4_0: [0], po.Q8_0: [0], po.Q4_1: [0, 2], po.Q5_K: [0, 2], po.Q3_K: [108], po.Q6_K: [208]}[gtype]
+    out = [np.zeros(bb, np.uint8)]
+    for fill, val in ((0xFF, [1.0]), (0x5A, None), (0xA5, [-1024.0])):
+        b = np.full(bb, fill, np.uint8)
+        for p in dpos:
+            b[p:p + 2] = f16_bytes(val)[0] if val else np.array([0x01, 0x00], np.uint8)
+        out.append(b)
+    return np.stack(out)
+
+
+def make_parse_file(path: str) -> None:
+    """A synthetic qwen3moe GGUF: every metadata value type (scalars, strings,
+    arrays of scalars, of strings and of arrays), the keys the reader takes,
+    a token list, and tensors of several types and ranks."""
+    import gguf_writer as gw
+    rng = np.random.default_rng(2025)
+    toks = [f"tok{i}" for i in range(40)] + ["", "\u00e9t\u00e9", " Tokyo"]
+    kv = [("general.architecture", gw.STR, "qwen3moe"), ("general.alignment", gw.U32, 32),
+          ("general.flag", gw.BOOL, True), ("general.u8", gw.U8, 7), ("general.i8", gw.I8, -7),
+          ("general.u16", gw.U16, 700), ("general.i16", gw.I16, -700), ("general.u64", gw.U64, 1 << 40),
+          ("general.i64", gw.I64, -(1 << 40)), ("general.f64", gw.F64, 0.25),
+          ("qwen3moe.block_count", gw.U32, 2), ("qwen3moe.embedding_length", gw.U32, 256),
+          ("qwen3moe.feed_forward_length", gw.U32, 512), ("qwen3moe.attention.head_count", gw.U32, 4),
+          ("qwen3moe.attention.head_count_kv", gw.I32, 2), ("qwen3moe.attention.key_length", gw.U32, 128),
+          ("qwen3moe.expert_count", gw.U32, 4), ("qwen3moe.expert_used_count", gw.U32, 2),
+          ("qwen3moe.expert_feed_forward_length", gw.U32, 256), ("qwen3moe.rope.freq_base", gw.F32, 5e5),
+          ("qwen3moe.attention.layer_norm_rms_epsilon", gw.F32, 1e-6),
+          ("tokenizer.ggml.scores", gw.ARR, (gw.F32, [float(i) for i in range(len(toks))])),
+          ("tokenizer.ggml.tokens", gw.ARR, (gw.STR, toks)),
+          ("tokenizer.ggml.merges", gw.ARR, (gw.ARR, [(gw.U16, [1, 2, 3]), (gw.U16, [])])),
+          ("tokenizer.ggml.token_type", gw.ARR, (gw.I32, [1] * len(toks)))]
+    specs = [("token_embd.weight", po.Q8_0, [256, 43]), ("output_norm.weight", po.Q_F32, [256]),
+             ("blk.0.attn_q.weight", po.Q3_K, [256, 512]), ("blk.0.attn_k.weight", po.Q8_0, [256, 256]),
+             ("blk.0.attn_output.weight", po.Q5_K, [512, 256]), ("blk.1.ffn_gate_exps.weight", po.Q4_0, [256, 256, 4]),
+             ("output.weight", po.Q6_K, [256, 43]), ("blk.0.attn_norm.weight", po.F16, [256])]
+    tensors = []
+    for name, gt, dims in specs:
+        n = int(np.prod(dims))
+        be, _ = po.GGUF_BLOCK[gt]
+        tensors.append((name, gt, dims, gw.random_blocks(gt, n // be, rng).tobytes()))
+    gw.write_gguf(path, kv, tensors)
+
+
+def make_gguf_golden() -> None:
+    sys.path.insert(0, os.path.dirname(HERE))
+    with tempfile.TemporaryDirectory() as tmp:
+        ref = build_ref_gguf(tmp)
+        import gguf_writer as gw
+        out = {}
+        for gt, name in GGUF_TYPES:
+            be, _ = po.GGUF_BLOCK[gt]
+            blk = np.concatenate([gw.random_blocks(gt, 64 if be > 1 else 512, np.random.default_rng(500 + gt)),
+                                  gguf_edge_blocks(gt)])
+            blk = np.ascontiguousarray(blk)
+            n = blk.shape[0] * be
+            vals = np.zeros(n, np.float32)
+            ref.golden_dq(gt, blk.ctypes.data, n, vals.ctypes.data)
+            out[f"{name}_blocks"] = blk.reshape(-1)
+            out[f"{name}_values"] = vals
+        rng = np.random.default_rng(77)
+        rows = [rng.standard_normal(32 * 64).astype(np.float32),
+                (rng.standard_normal(32 * 16) * 1e-3).astype(np.float32),
+                np.zeros(32, np.float32),                                     # amax stays 1e-6
+                np.tile(np.array([127.0, -127.0, 63.5, -63.5, 0.5, -0.5, 1.5, 2.5], np.float32), 4),  # ties
+                np.full(32, 7e-7, np.float32),                                # below the amax floor
+                (rng.standard_normal(32 * 8) * 3e4).astype(np.float32)]
+        x = np.concatenate(rows)
+        assert ref.golden_sizeof_q8() == 34
+        q = np.zeros(x.size // 32 * 34, np.uint8)
+        ref.golden_q8(x.ctypes.data, x.size, q.ctypes.data)
+        out["Q8REQ_input"] = x
+        out["Q8REQ_blocks"] = q
+        np.savez_compressed(os.path.join(HERE, "gguf_golden.npz"), **out)
+
+        path = os.path.join(tmp, "parse.gguf")
+        make_parse_file(path)
+        ints = np.zeros(13, np.int64)
+        rope = np.zeros(1, np.float32)
+        ref.golden_open(path.encode(), ints.ctypes.data, rope.ctypes.data)
+        names = ["block_count", "embd", "ffn", "nh", "nkv", "hd", "vocab", "n_exp", "n_act", "moe_ffn",
+                 "n_tensors", "data_start", "n_tokens"]
+        parse = {k: int(v) for k, v in zip(names, ints)}
+        parse["rope_base"] = float(rope[0])
+        parse["tokens"] = [ref.golden_token(i).decode() for i in range(parse["n_tokens"])]
+        tens = []
+        for i in range(parse["n_tensors"]):
+            nm = C.create_string_buffer(64)
+            v = np.zeros(7, np.int64)
+            ref.golden_tensor(i, nm, v.ctypes.data)
+            tens.append({"name": nm.value.decode(), "type": int(v[0]), "n_dims": int(v[1]),
+                         "dims": [int(d) for d in v[2:2 + int(v[1])]], "offset": int(v[6])})
+        parse["tensors"] = tens
+        parse["file_sha256"] = hashlib.sha256(open(path, "rb").read()).hexdigest()
+        with open(os.path.join(HERE, "gguf_parse.json"), "w") as f:
+            json.dump(parse, f, indent=1, sort_keys=True)
+    print("wrote gguf_golden.npz, gguf_parse.json")
+
+
 def main():
+    if "--only-gguf" in sys.argv:
+        po.build()
+        make_gguf_golden()
+        return
     po.build()
     ref = po.ref_lib()
     if ref is None:
@@ -235,6 +415,7 @@ def main():
     with open(os.path.join(HERE, "meta.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print("wrote gemm_golden.npz, quant_golden.npz, meta.json")
+    make_gguf_golden()
 
 
 if __name__ == "__main__":

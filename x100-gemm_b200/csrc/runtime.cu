@@ -208,6 +208,7 @@ const char *x100_strerror(int code) {
     case X100_E_UNSUPPORTED: return "unsupported shape, type or layout";
     case X100_E_TOO_LARGE:
         return "request larger than the fixed scratch of a no-allocation entry point";
+    case X100_E_FORMAT: return "malformed file, or a tensor missing or of a type that cannot be used";
     default: return "unknown error";
     }
 }

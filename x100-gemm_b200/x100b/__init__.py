@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libx100gemm_b200.so")
 HEADERS = [os.path.join(REPO, "include", "x100_gemm.h"), os.path.join(REPO, "include", "x100q.h")]
 
 X100_OK, X100_E_ARG, X100_E_NODEV, X100_E_ARCH, X100_E_ALLOC, X100_E_COPY, X100_E_LAUNCH, \
-    X100_E_TIMEOUT, X100_E_COMM, X100_E_INJECTED, X100_E_UNSUPPORTED, X100_E_TOO_LARGE = range(12)
+    X100_E_TIMEOUT, X100_E_COMM, X100_E_INJECTED, X100_E_UNSUPPORTED, X100_E_TOO_LARGE, X100_E_FORMAT = range(13)
 
 Q_F32, Q4_0, Q8_0, Q3_K, Q4_K = 0, 2, 8, 11, 12
 
@@ -95,7 +95,29 @@ _SIGS = {
     "x100q_ep_open": ([vp, vp], i32),
     "x100q_ep_allreduce_dev": ([vp, vp, vp, i32, i32, vp], i32),
     "x100q_ep_destroy": ([vp], None),
+    # GGUF ingest
+    "x100q_gguf_open": ([C.c_char_p], vp),
+    "x100q_gguf_close": ([vp], None),
+    "x100q_gguf_n_tensors": ([vp], i32),
+    "x100q_gguf_tensor_at": ([vp, i32, vp], i32),
+    "x100q_gguf_find": ([vp, C.c_char_p, vp], i32),
+    "x100q_gguf_data_offset": ([vp], C.c_uint64),
+    "x100q_gguf_n_tokens": ([vp], i32),
+    "x100q_gguf_token": ([vp, i32], C.c_char_p),
+    "x100q_gguf_get_int": ([vp, C.c_char_p, vp], i32),
+    "x100q_gguf_get_f32": ([vp, C.c_char_p, vp], i32),
+    "x100q_gguf_get_str": ([vp, C.c_char_p, vp], i32),
+    "x100q_gguf_model_cfg": ([vp, vp], i32),
+    "x100q_model_load_gguf": ([vp, vp], vp),
+    "x100q_gguf_dequant_dev": ([i32, vp, C.c_long, vp, vp], i32),
+    "x100q_quantize_q8_0_dev": ([vp, C.c_long, vp, vp], i32),
 }
+
+
+class GgufTensor(C.Structure):
+    """x100q_gguf_tensor (include/x100q.h)."""
+    _fields_ = [("name", C.c_char_p), ("type", C.c_int), ("n_dims", C.c_int), ("dims", C.c_uint64 * 4),
+                ("n_elems", C.c_uint64), ("bytes", C.c_uint64), ("data", C.c_void_p)]
 
 
 class ModelCfg(C.Structure):
@@ -318,6 +340,91 @@ class Model:
             self.h = None
 
     __del__ = close
+
+
+class Gguf:
+    """x100q_gguf handle: a GGUF file mapped and parsed (no GPU needed)."""
+
+    def __init__(self, path: str):
+        self.h = lib().x100q_gguf_open(os.fsencode(path))
+        if not self.h:
+            check_last("x100q_gguf_open")
+
+    def _info(self, t: GgufTensor) -> dict:
+        return {"name": t.name.decode(), "type": t.type, "n_dims": t.n_dims, "dims": list(t.dims[: t.n_dims]),
+                "n_elems": t.n_elems, "bytes": t.bytes, "data": t.data}
+
+    def tensors(self) -> list[dict]:
+        out = []
+        for i in range(lib().x100q_gguf_n_tensors(self.h)):
+            t = GgufTensor()
+            check(lib().x100q_gguf_tensor_at(self.h, i, C.byref(t)), "x100q_gguf_tensor_at")
+            out.append(self._info(t))
+        return out
+
+    def find(self, name: str) -> dict:
+        t = GgufTensor()
+        check(lib().x100q_gguf_find(self.h, name.encode(), C.byref(t)), "x100q_gguf_find")
+        return self._info(t)
+
+    def tensor_bytes(self, name: str) -> np.ndarray:
+        """The tensor's raw data (a copy out of the mapping)."""
+        t = self.find(name)
+        return np.ctypeslib.as_array((C.c_uint8 * t["bytes"]).from_address(t["data"])).copy()
+
+    @property
+    def data_offset(self) -> int:
+        return int(lib().x100q_gguf_data_offset(self.h))
+
+    def tokens(self) -> list[str]:
+        L = lib()
+        return [L.x100q_gguf_token(self.h, i).decode() for i in range(L.x100q_gguf_n_tokens(self.h))]
+
+    def get_int(self, key: str) -> int:
+        v = C.c_int64()
+        check(lib().x100q_gguf_get_int(self.h, key.encode(), C.byref(v)), key)
+        return v.value
+
+    def get_f32(self, key: str) -> float:
+        v = C.c_float()
+        check(lib().x100q_gguf_get_f32(self.h, key.encode(), C.byref(v)), key)
+        return v.value
+
+    def get_str(self, key: str) -> str:
+        v = C.c_char_p()
+        check(lib().x100q_gguf_get_str(self.h, key.encode(), C.byref(v)), key)
+        return v.value.decode()
+
+    def model_cfg(self) -> dict:
+        c = ModelCfg()
+        check(lib().x100q_gguf_model_cfg(self.h, C.byref(c)), "x100q_gguf_model_cfg")
+        return {n: getattr(c, n) for n, _ in ModelCfg._fields_}
+
+    def load_model(self, **overrides) -> "Model":
+        """x100q_model_load_gguf with the file's configuration, fields such as
+        ctx, max_batch or expert_lo / expert_hi replaced by `overrides`."""
+        cfg = dict(self.model_cfg(), **overrides)
+        m = Model.__new__(Model)
+        m.cfg = ModelCfg(**cfg)
+        m.h = lib().x100q_model_load_gguf(self.h, C.byref(m.cfg))
+        if not m.h:
+            check_last("x100q_model_load_gguf")
+        return m
+
+    def close(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.x100q_gguf_close(self.h)
+            self.h = None
+
+    __del__ = close
+
+
+def gguf_dequant_dev(gtype: int, data, n: int, out, stream=None) -> None:
+    check(lib().x100q_gguf_dequant_dev(gtype, _p(data), n, _p(out), _stream(stream)), "x100q_gguf_dequant_dev")
+
+
+def quantize_q8_0_dev(x, n: int, blocks, stream=None) -> None:
+    check(lib().x100q_quantize_q8_0_dev(_p(x), n, _p(blocks), _stream(stream)), "x100q_quantize_q8_0_dev")
 
 
 EP_HANDLE_BYTES = 64
