@@ -71,6 +71,17 @@ __device__ __forceinline__ XBuf xbuf_at(uint8_t *base, int ns) {
     x.ns = ns;
     return x;
 }
+// Block-major prepared activations for the tensor-core GEMV: block j of
+// token t at (j * ntok + t) * 80 bytes, so the 8 tokens of an MMA column tile
+// sit 80 bytes apart (8 distinct 16-byte bank groups for ldmatrix).
+struct XBufBM {
+    uint8_t *base;
+    int ns;     // slices per token
+    int ntok;   // tokens per block row (a multiple of 8)
+    __device__ __forceinline__ XB *block(int t, int j) const {
+        return reinterpret_cast<XB *>(base + ((long)j * ntok + t) * 80);
+    }
+};
 
 // ---- integer dot products ----------------------------------------------------------
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
@@ -294,9 +305,9 @@ __device__ __forceinline__ void xprep_vals(const float4 v, XB *o, int t, bool ac
 
 // The whole CTA prepares `nrows` activation rows row(c)[0 .. K) into xb as
 // tokens 0 .. nrows-1 (blocks past K, up to the slice boundary, are zero).
-// A warp converts 4 blocks at a time; each pass first issues up to kXPF such
-// groups of 16-byte loads per warp and only then converts them, so a pass
-// costs one memory round trip.  Groups past the end are skipped whole (the
+// A warp converts 4 blocks at a time; each pass first issues up to PF (kXPF
+// by default) such groups of 16-byte loads per warp and only then converts
+// them, so a pass costs one memory round trip.  Groups past the end are skipped whole (the
 // test is warp-uniform, which keeps the shuffles legal).  The loads go
 // through L2: the rows may have been written by other CTAs of the grid.
 //
@@ -308,8 +319,8 @@ __device__ __forceinline__ void xprep_vals(const float4 v, XB *o, int t, bool ac
 // W . rmsnorm(x) = s * (W . (x * nw)) without a second pass over x.
 constexpr int kXPF = 4;
 constexpr int kSsTok = 16;
-template <class RowPtr>
-__device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const XBuf &xb,
+template <int PF = kXPF, class RowPtr, class XBT>
+__device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const XBT &xb,
                                            const float *__restrict__ nw = nullptr, float *ss = nullptr) {
     const int nxb = xb.ns * 8, kb = K / 32;
     const int total = nrows * nxb;
@@ -317,10 +328,10 @@ __device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const X
     const int g = lane >> 3, t = lane & 7;
     if (nw && t == 0)
         for (int c = 0; c < nrows; ++c) ss[(warp * 4 + g) * kSsTok + c] = 0.f;
-    for (int base = 0; base < total; base += nwarps * 4 * kXPF) {
-        float4 v[kXPF];
+    for (int base = 0; base < total; base += nwarps * 4 * PF) {
+        float4 v[PF];
 #pragma unroll
-        for (int i = 0; i < kXPF; ++i) {
+        for (int i = 0; i < PF; ++i) {
             const int blk = base + (i * nwarps + warp) * 4 + g;
             v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (blk < total) {
@@ -329,7 +340,7 @@ __device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const X
             }
         }
 #pragma unroll
-        for (int i = 0; i < kXPF; ++i) {
+        for (int i = 0; i < PF; ++i) {
             const int blk0 = base + (i * nwarps + warp) * 4;
             if (blk0 < total) {
                 const int blk = blk0 + g;

@@ -309,6 +309,19 @@ int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batc
         return X100_E_ARG;
     }
     if (fault_injected("launch")) return X100_E_INJECTED;
+    static const bool dp4a_only = [] {
+        const char *e = getenv("X100_GEMV_DP4A");
+        return e && *e && *e != '0';
+    }();
+    // Independent calls of up to 4 tokens stay on the dp4a kernel: its small
+    // CTAs let consecutive calls overlap, which the persistent tensor-core
+    // kernel (one CTA per SM) cannot (Q4_0 6144 x 2048, 4 tokens: 1187 vs
+    // 900 GB/s measured; from 8 tokens the tensor-core kernel is ahead).
+    if (batch > 1 && !dp4a_only && !(o.indep && batch <= 4) && qgemv_mma_ok(m.qtype, m.K)) {
+        const int st = launch_qgemv_mma(c, m, x, y, batch, o, s);
+        if (st) set_error(st);
+        return st;
+    }
     switch (m.qtype) {
     case Q4_0: return launch_qt<Q4_0>(c, m, x, y, batch, o, s);
     case Q8_0: return launch_qt<Q8_0>(c, m, x, y, batch, o, s);

@@ -18,6 +18,7 @@ struct QMat {
     const uint8_t *row(long r) const { return w + r * row_bytes; }
 };
 
+
 size_t qtype_block_elems(int qt);
 size_t qtype_block_bytes(int qt);
 // Upload N rows of GGUF-native blocks (host or device pointer) and re-lay
@@ -37,6 +38,14 @@ struct GemvOpts {
 };
 int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
                     cudaStream_t s);
+// Several tokens of a Q4_0 / Q8_0 matrix on the tensor cores (qgemv_mma.cu):
+// the same integer block dots and summation order as the dp4a kernel.
+// launch_qgemv_ex uses it for batch > 1 when qgemv_mma_ok, except for
+// independent calls of up to 4 tokens (X100_GEMV_DP4A=1 keeps the dp4a
+// kernel everywhere).
+bool qgemv_mma_ok(int qt, int K);
+int launch_qgemv_mma(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
+                     cudaStream_t s);
 
 // Launch `kernel` on `s` with programmatic stream serialization (the kernel
 // may start while the previous kernel of the stream runs; it orders itself

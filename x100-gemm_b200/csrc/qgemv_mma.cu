@@ -1,0 +1,307 @@
+// qgemv_mma.cu -- dequant-GEMV of several tokens (2..16) on the tensor cores,
+// for the Q4_0 and Q8_0 slice layouts.
+//
+// The single-token kernel (qgemv.cu) forms each block's integer dot with
+// dp4a; with several tokens that work grows with the batch and bounds the
+// call long before HBM does.  Here one m16n8k32 integer MMA computes a whole
+// block (32 weights) for 16 rows x 8 tokens: A = the 16 rows' int8 weights
+// (Q4_0: unsigned nibbles, the -8 folded in as -8 * sum(x) as the dp4a path
+// does; Q8_0: signed bytes), B = the tokens' h or l activation plane
+// (qformats.cuh: x ~= s (256 h + l)), so 256 * MMA(h) + MMA(l) is exactly the
+// integer block dot of the dp4a path, and each half-slice (4 blocks) is
+// scaled and summed in the same order.
+//
+// Persistent kernel, one CTA per SM, in three steps:
+//  1. before the dependency wait, every thread starts 16-byte asynchronous
+//     copies (cp.async) of the first weight items into a ring of shared-
+//     memory stages; an item is a K-chunk of CK slices of a 16-row tile
+//     (tile = blockIdx.x + i * gridDim.x), rows an odd multiple of 16 bytes
+//     apart so the 8 rows of a fragment load hit distinct banks;
+//  2. the CTA prepares every token's activations (block-major, see XBufBM)
+//     with xprep_rows (a grid-wide preparation into device scratch behind a
+//     grid barrier, and a deeper load prefetch, both measured slower);
+//  3. the CTA walks its items through the ring: a warp takes one half-slice
+//     of the chunk at a time; after a tile's last chunk its partials are
+//     summed per row in slice order (first halves, then second halves) as in
+//     the single-token kernel, so results do not depend on the chunking.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "qgemv.h"
+#include "runtime.h"
+
+namespace x100 {
+namespace q {
+
+constexpr int kMmaThreads = 512;
+constexpr int kMmaRows = 16;       // rows per tile (the MMA's M)
+constexpr int kMmaMaxStages = 4;
+constexpr size_t kMmaSmemMax = 220 * 1024;
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most n (0..3) of this thread's committed groups are pending.
+__device__ __forceinline__ void cp_async_wait(int n) {
+    switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    }
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+// D = A (16 x 32, row) . B (32 x 8, col) over int8, int32 accumulate from 0.
+template <bool AU>
+__device__ __forceinline__ void mma_i8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    if constexpr (AU)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+            "{%10, %10, %10, %10};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+            "{%10, %10, %10, %10};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Row stride of a stage holding ck slices per row: an odd multiple of 16.
+__host__ __device__ constexpr int mma_row_stride(int qt, int ck) {
+    return ck * slice_bytes(qt) + (((ck * slice_bytes(qt)) / 16) % 2 ? 32 : 16);
+}
+
+struct MmaPlan {
+    int nt = 0, ck = 0, stages = 0;
+    size_t smem = 0;
+};
+// Shared memory: the block-major activations of 8 nt tokens, the
+// per-half-slice partials [8 nt][16 rows][2 ns], and stages x 16 rows x ck
+// slices.  Prefer 16 tokens per launch when at least 64 KB of weights can be
+// in flight per SM; otherwise 8 tokens with the most bytes in flight.
+static size_t mma_fixed(int K, int nt) {
+    const int ns = slices_per_row(K);
+    return (size_t)ns * 8 * 8 * nt * 80 + ((size_t)8 * nt * (kMmaRows * (2 * ns + 1) + 4) * 4 + 15) / 16 * 16;
+}
+static MmaPlan mma_plan(int qt, int K, int batch) {
+    const int ns = slices_per_row(K);
+    MmaPlan best;
+    for (int nt = batch > 8 ? 2 : 1; nt >= 1; --nt) {
+        const size_t fixed = mma_fixed(K, nt);
+        if (fixed >= kMmaSmemMax) continue;
+        MmaPlan p;
+        size_t inflight = 0;
+        for (int ck = ns; ck >= 1; --ck) {
+            const size_t stage = (size_t)kMmaRows * mma_row_stride(qt, ck);
+            const int st = (int)std::min<size_t>(kMmaMaxStages, (kMmaSmemMax - fixed) / stage);
+            if (st >= 2 && st * stage > inflight) {
+                inflight = st * stage;
+                p.nt = nt;
+                p.ck = ck;
+                p.stages = st;
+                p.smem = fixed + st * stage;
+            }
+        }
+        if (p.stages && (nt == 1 || inflight >= 64 * 1024)) return p;
+        if (p.stages && !best.stages) best = p;
+    }
+    return best;
+}
+
+template <int QT, int NT>
+__global__ void __launch_bounds__(kMmaThreads, 1)
+    qgemv_mma_kernel(const uint8_t *__restrict__ W, int N, int K, int ck, int stages, const float *__restrict__ x,
+                     float *__restrict__ y, int batch, const float *__restrict__ nw, float eps, int accum,
+                     int *status) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float ssq[(kMmaThreads / 32) * 4][kSsTok];   // RMS-norm sums of squares per 8-lane group
+    __shared__ float scale[16];
+    constexpr int SB = slice_bytes(QT);
+    constexpr int NTOK = 8 * NT;
+    const int ns = slices_per_row(K), nb = ns * 8;
+    const long rb = (long)ns * SB;
+    const int rsp = mma_row_stride(QT, ck);
+    // partials [tok][row][half-slice]: row stride RS odd and token stride TS =
+    // 8 mod 32 words per two tokens, so the 32 lanes' writes hit distinct banks
+    const int RS = 2 * ns + 1, TS = kMmaRows * RS + 4;
+    const int ntiles = (N + kMmaRows - 1) / kMmaRows;
+    const int nchunks = (ns + ck - 1) / ck;
+    const int mytiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int nitems = mytiles * nchunks;
+    uint8_t *xbase = smem;
+    float *red = reinterpret_cast<float *>(xbase + (size_t)nb * NTOK * 80);
+    uint8_t *stage_base = xbase + (size_t)nb * NTOK * 80 + ((size_t)NTOK * TS * 4 + 15) / 16 * 16;
+    const XBufBM xb{xbase, ns, NTOK};
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+
+    // every thread copies its 16-byte chunks of item it into stage it % stages
+    // and commits one group (empty past the last item, so counting stays uniform)
+    auto issue = [&](int it) {
+        if (it < nitems) {
+            const int tile = blockIdx.x + (it / nchunks) * gridDim.x, chunk = it % nchunks;
+            const int r0 = tile * kMmaRows, rows = min(kMmaRows, N - r0);
+            const int c0 = chunk * ck, cb = min(ck, ns - c0) * SB / 16;
+            uint8_t *dst = stage_base + (size_t)(it % stages) * kMmaRows * rsp;
+            const uint8_t *src = W + (long)r0 * rb + (long)c0 * SB;
+            for (int k = threadIdx.x; k < rows * cb; k += blockDim.x) {
+                const int r = k / cb, c = k - r * cb;
+                cp_async16(dst + (size_t)r * rsp + 16 * c, src + (long)r * rb + 16 * c);
+            }
+        }
+        cp_async_commit();
+    };
+    for (int s = 0; s < stages - 1; ++s) issue(s);
+    pdl_launch_dependents();
+    pdl_wait();   // x may come from the previous kernel; the previous call on this matrix is complete
+
+    // ---- 2. activations ----
+    xprep_rows([x, K](int c) { return x + (long)c * K; }, K, batch, xb, nw, &ssq[0][0]);
+    __syncthreads();
+    if (threadIdx.x < batch) scale[threadIdx.x] = nw ? rms_scale(&ssq[0][0], blockDim.x / 8, threadIdx.x, K, eps) : 1.0f;
+    __syncthreads();
+    const uint32_t xs_addr = smem_u32(xbase);
+
+    // ---- 3. the items ----
+    for (int it = 0; it < nitems; ++it) {
+        issue(it + stages - 1);   // into the stage item it - 1 used
+        cp_async_wait(stages - 1);
+        __syncthreads();
+        const int st = it % stages;
+        const int tile = blockIdx.x + (it / nchunks) * gridDim.x, chunk = it % nchunks;
+        const int r0 = tile * kMmaRows, rows = min(kMmaRows, N - r0);
+        const int c0 = chunk * ck, cs = min(ck, ns - c0);
+        const uint8_t *tw = stage_base + (size_t)st * kMmaRows * rsp;
+        for (int u = warp; u < 2 * cs; u += nwarps) {
+            const int sll = u >> 1, h = u & 1, sl = c0 + sll;
+            float acc[NT][4];
+#pragma unroll
+            for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+            const uint8_t *pg = tw + (size_t)g * rsp + (size_t)sll * SB, *pg8 = pg + (size_t)8 * rsp;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int bb = 4 * h + b, j = sl * 8 + bb;
+                uint32_t a0, a1, a2, a3;
+                if constexpr (QT == Q4_0) {
+                    const uint32_t w0 = *reinterpret_cast<const uint32_t *>(pg + 16 + 16 * bb + 4 * t);
+                    const uint32_t w1 = *reinterpret_cast<const uint32_t *>(pg8 + 16 + 16 * bb + 4 * t);
+                    a0 = w0 & 0x0F0F0F0Fu;
+                    a2 = (w0 >> 4) & 0x0F0F0F0Fu;
+                    a1 = w1 & 0x0F0F0F0Fu;
+                    a3 = (w1 >> 4) & 0x0F0F0F0Fu;
+                } else {
+                    a0 = *reinterpret_cast<const uint32_t *>(pg + 16 + 32 * bb + 4 * t);
+                    a2 = *reinterpret_cast<const uint32_t *>(pg + 16 + 32 * bb + 16 + 4 * t);
+                    a1 = *reinterpret_cast<const uint32_t *>(pg8 + 16 + 32 * bb + 4 * t);
+                    a3 = *reinterpret_cast<const uint32_t *>(pg8 + 16 + 32 * bb + 16 + 4 * t);
+                }
+                const float d0 = __half2float(*reinterpret_cast<const __half *>(pg + 2 * bb));
+                const float d1 = __half2float(*reinterpret_cast<const __half *>(pg8 + 2 * bb));
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    // lanes 8m .. 8m+7 address matrix m (h0, h1, l0, l1) of tokens 8n .. 8n+7
+                    uint32_t h0, h1, l0, l1;
+                    ldsm_x4(xs_addr + (uint32_t)(((long)j * NTOK + 8 * n + (lane & 7)) * 80 + (lane >> 3) * 16), h0,
+                            h1, l0, l1);
+                    int ch[4], cl[4];
+                    mma_i8<QT == Q4_0>(ch, a0, a1, a2, a3, h0, h1);
+                    mma_i8<QT == Q4_0>(cl, a0, a1, a2, a3, l0, l1);
+                    const XB *x0 = xb.block(8 * n + 2 * t, j), *x1 = xb.block(8 * n + 2 * t + 1, j);
+                    const float2 f0 = *reinterpret_cast<const float2 *>(&x0->f);
+                    const float2 f1 = *reinterpret_cast<const float2 *>(&x1->f);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 f = (i & 1) ? f1 : f0;
+                        const float d = i < 2 ? d0 : d1;
+                        const int dot = ch[i] * 256 + cl[i];
+                        if constexpr (QT == Q4_0)
+                            acc[n][i] += d * (f.x * (float)dot - 8.0f * f.y);   // (nib - 8) * d
+                        else
+                            acc[n][i] += d * (f.x * (float)dot);                // q * d
+                    }
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int tok = 8 * n + 2 * t + (i & 1), row = g + (i < 2 ? 0 : 8);
+                    red[(size_t)tok * TS + row * RS + 2 * sl + h] = acc[n][i];
+                }
+        }
+        __syncthreads();   // the stage is consumed, this chunk's partials written
+        if (chunk == nchunks - 1) {   // the next item's partials are written after the next barrier
+            for (int p = threadIdx.x; p < rows * batch; p += blockDim.x) {
+                const int b = p / rows, r = p - b * rows;
+                const float *pr = red + (size_t)b * TS + r * RS;
+                float s0 = 0.f, s1 = 0.f;
+#pragma unroll 4
+                for (int sl = 0; sl < ns; ++sl) {
+                    s0 += pr[2 * sl];
+                    s1 += pr[2 * sl + 1];
+                }
+                float *o = y + (long)b * N + r0 + r;
+                const float v = (s0 + s1) * scale[b];
+                *o = accum ? *o + v : v;
+            }
+        }
+    }
+    cp_async_wait(0);   // no copy outlives the CTA
+}
+
+template <int QT, int NT>
+static int launch_mma_nt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const MmaPlan &p,
+                         const GemvOpts &o, cudaStream_t s) {
+    static bool attr[64];
+    if (!attr[c->device]) {
+        set_qkernel_attrs(qgemv_mma_kernel<QT, NT>, (int)kMmaSmemMax);
+        attr[c->device] = true;
+    }
+    const int ntiles = (m.N + kMmaRows - 1) / kMmaRows;
+    const int grid = std::min(ntiles, c->sm_count);
+    return launch_k(qgemv_mma_kernel<QT, NT>, dim3(grid), dim3(kMmaThreads), p.smem, s, o.pdl, (const uint8_t *)m.w,
+                    m.N, m.K, p.ck, p.stages, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0, c->d_status);
+}
+
+// Launches of 8 nt tokens each (nt from the plan).
+template <int QT>
+static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, GemvOpts o,
+                         cudaStream_t s) {
+    const MmaPlan p = mma_plan(QT, m.K, batch);
+    if (!p.stages) return X100_E_UNSUPPORTED;
+    const int per = 8 * p.nt;
+    for (int b0 = 0; b0 < batch; b0 += per) {
+        const int nb = std::min(per, batch - b0);
+        const float *xb = x + (long)b0 * m.K;
+        float *yb = y + (long)b0 * m.N;
+        const int st = p.nt == 2 ? launch_mma_nt<QT, 2>(c, m, xb, yb, nb, p, o, s)
+                                 : launch_mma_nt<QT, 1>(c, m, xb, yb, nb, p, o, s);
+        if (st) return st;
+        o.pdl = true;
+    }
+    return X100_OK;
+}
+
+}  // namespace q
+
+bool qgemv_mma_ok(int qt, int K) {
+    return (qt == q::Q4_0 || qt == q::Q8_0) && q::mma_plan(qt, K, 8).stages > 0;
+}
+
+int launch_qgemv_mma(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
+                     cudaStream_t s) {
+    if (m.qtype == q::Q4_0) return q::launch_mma_qt<q::Q4_0>(c, m, x, y, batch, o, s);
+    if (m.qtype == q::Q8_0) return q::launch_mma_qt<q::Q8_0>(c, m, x, y, batch, o, s);
+    return X100_E_UNSUPPORTED;
+}
+
+}  // namespace x100
