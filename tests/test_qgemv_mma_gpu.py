@@ -31,7 +31,9 @@ def blocks(qt, N, K, seed):
     return po.quantize(qt, rng.normal(0, 0.02, size=(N, K)).astype(np.float32))
 
 
-SHAPES = [(37, 256), (1000, 2080), (8192, 2048), (2048, 4096), (300, 6144), (5120, 2048)]
+# (512, 7936): 31 slices per row (prime), so the rows are staged in ragged
+# K-chunks; (2048, 4096) and (300, 6144): whole chunks; the rest whole rows
+SHAPES = [(37, 256), (1000, 2080), (8192, 2048), (2048, 4096), (300, 6144), (5120, 2048), (512, 7936)]
 
 
 @pytest.mark.parametrize("qt", [po.Q4_0, po.Q8_0])

@@ -98,17 +98,24 @@ static MmaPlan mma_plan(int qt, int K, int batch) {
     for (int nt = batch > 8 ? 2 : 1; nt >= 1; --nt) {
         const size_t fixed = mma_fixed(K, nt);
         if (fixed >= kMmaSmemMax) continue;
+        // chunk sizes that divide the row first (no ragged last item, whose
+        // per-item overhead buys few bytes), if one keeps >= 48 KB in flight
         MmaPlan p;
         size_t inflight = 0;
-        for (int ck = ns; ck >= 1; --ck) {
-            const size_t stage = (size_t)kMmaRows * mma_row_stride(qt, ck);
-            const int st = (int)std::min<size_t>(kMmaMaxStages, (kMmaSmemMax - fixed) / stage);
-            if (st >= 2 && st * stage > inflight) {
-                inflight = st * stage;
-                p.nt = nt;
-                p.ck = ck;
-                p.stages = st;
-                p.smem = fixed + st * stage;
+        for (int pass = 0; pass < 2 && inflight < 48 * 1024; ++pass) {
+            p = MmaPlan();
+            inflight = 0;
+            for (int ck = ns; ck >= 1; --ck) {
+                if (pass == 0 && ns % ck) continue;
+                const size_t stage = (size_t)kMmaRows * mma_row_stride(qt, ck);
+                const int st = (int)std::min<size_t>(kMmaMaxStages, (kMmaSmemMax - fixed) / stage);
+                if (st >= 2 && st * stage > inflight) {
+                    inflight = st * stage;
+                    p.nt = nt;
+                    p.ck = ck;
+                    p.stages = st;
+                    p.smem = fixed + st * stage;
+                }
             }
         }
         if (p.stages && (nt == 1 || inflight >= 64 * 1024)) return p;
@@ -153,10 +160,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             const int c0 = chunk * ck, cb = min(ck, ns - c0) * SB / 16;
             uint8_t *dst = stage_base + (size_t)(it % stages) * kMmaRows * rsp;
             const uint8_t *src = W + (long)r0 * rb + (long)c0 * SB;
-            for (int k = threadIdx.x; k < rows * cb; k += blockDim.x) {
-                const int r = k / cb, c = k - r * cb;
-                cp_async16(dst + (size_t)r * rsp + 16 * c, src + (long)r * rb + 16 * c);
-            }
+            for (int r = warp; r < rows; r += nwarps)   // a warp per row, no index division
+                for (int c = lane; c < cb; c += 32) cp_async16(dst + (size_t)r * rsp + 16 * c, src + (long)r * rb + 16 * c);
         }
         cp_async_commit();
     };
