@@ -52,6 +52,18 @@ def test_mma_gemv_matches_oracle(qt, shape, batch):
         assert po.rel_l2(y[b], ref[b]) <= REL_Q
 
 
+@pytest.mark.parametrize("qt", [po.Q4_0, po.Q8_0])
+def test_single_token_tall_matrix(qt):
+    """One token on a matrix of 70000 rows (the lm_head shape class)."""
+    N, K = 70000, 2048
+    W = blocks(qt, N, K, 77 + qt)
+    x = np.random.default_rng(78).normal(0, 1, size=(1, K)).astype(np.float32)
+    ref = po.qgemv(qt, W, N, K, x, nthreads=8)
+    y = np.empty((1, N), np.float32)
+    x100b.Lin(qt, N, K, W).gemv(x, y, 1)
+    assert po.rel_l2(y, ref) <= REL_Q
+
+
 def test_mma_gemv_device_path_repeat_and_streams():
     """Device pointers, repeated calls on one stream (the persistent CTAs'
     barriers re-initialised per launch) and a second stream."""

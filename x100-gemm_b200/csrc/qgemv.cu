@@ -317,7 +317,11 @@ int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batc
     // CTAs let consecutive calls overlap, which the persistent tensor-core
     // kernel (one CTA per SM) cannot (Q4_0 6144 x 2048, 4 tokens: 1187 vs
     // 900 GB/s measured; from 8 tokens the tensor-core kernel is ahead).
-    if (batch > 1 && !dp4a_only && !(o.indep && batch <= 4) && qgemv_mma_ok(m.qtype, m.K)) {
+    // one token on a very tall matrix (an lm_head): the persistent
+    // tensor-core kernel streams it faster than the single-token dp4a kernel's
+    // many waves of small CTAs (151936 x 2048 Q8_0: 118 vs 145 us)
+    const bool tall = batch == 1 && m.N >= 65536;
+    if ((batch > 1 || tall) && !dp4a_only && !(o.indep && batch <= 4) && qgemv_mma_ok(m.qtype, m.K)) {
         const int st = launch_qgemv_mma(c, m, x, y, batch, o, s);
         if (st) set_error(st);
         return st;

@@ -40,9 +40,9 @@ int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batc
                     cudaStream_t s);
 // Several tokens of a Q4_0 / Q8_0 matrix on the tensor cores (qgemv_mma.cu):
 // the same integer block dots and summation order as the dp4a kernel.
-// launch_qgemv_ex uses it for batch > 1 when qgemv_mma_ok, except for
-// independent calls of up to 4 tokens (X100_GEMV_DP4A=1 keeps the dp4a
-// kernel everywhere).
+// launch_qgemv_ex uses it for batch > 1 and for one token on a matrix of
+// 65536 rows or more, when qgemv_mma_ok, except for independent calls of up
+// to 4 tokens (X100_GEMV_DP4A=1 keeps the dp4a kernel everywhere).
 bool qgemv_mma_ok(int qt, int K);
 int launch_qgemv_mma(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
                      cudaStream_t s);
