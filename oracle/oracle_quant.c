@@ -339,6 +339,108 @@ void orc_quantize_q8_0_ref(const float *x, size_t n, void *blocks)
     }
 }
 
+/* ---- the reference's activation packing ("A8") ---------------------------*/
+
+void orc_pack_a_i8(const float *x, int K, void *out)
+{
+    uint8_t *o = (uint8_t *)out;
+    for (int kg = 0; kg < K / 32; kg++) {
+        const float *a = x + 32 * kg;
+        uint8_t *r = o + 38 * kg;
+        float amax = 1e-6f;
+        for (int i = 0; i < 32; i++) {
+            float v = fabsf(a[i]);
+            if (v > amax) amax = v;
+        }
+        float scale = amax / 127.0f;
+        float inv = scale != 0.0f ? 1.0f / scale : 0.0f;
+        int32_t sum = 0;
+        for (int i = 0; i < 32; i++) {
+            long q = lrintf(a[i] * inv);
+            q = q > 127 ? 127 : (q < -128 ? -128 : q);
+            r[6 + i] = (uint8_t)(int8_t)q;
+            sum += (int32_t)q;
+        }
+        int16_t s16 = (int16_t)sum;
+        memcpy(r, &scale, 4);
+        memcpy(r + 4, &s16, 2);
+    }
+}
+
+void orc_pack_a_q3k(const float *x, int K, void *out)
+{
+    uint8_t *o = (uint8_t *)out;
+    for (int sb = 0; sb < K / 256; sb++) {
+        const float *a = x + 256 * sb;
+        uint8_t *r = o + 292 * sb;
+        float amax = 0.0f;
+        for (int i = 0; i < 256; i++) {
+            float v = fabsf(a[i]);
+            if (v > amax) amax = v;
+        }
+        float scale = amax / 127.0f;
+        float rep = scale != 0.0f ? 1.0f / scale : 0.0f;
+        memcpy(r, &scale, 4);
+        for (int b = 0; b < 16; b++) {
+            int32_t sum = 0;
+            for (int l = 0; l < 16; l++) {
+                int q = (int)roundf(a[16 * b + l] * rep);
+                q = q > 127 ? 127 : (q < -128 ? -128 : q);
+                r[36 + 16 * b + l] = (uint8_t)(int8_t)q;
+                sum += q;
+            }
+            int16_t s16 = (int16_t)(-sum);
+            memcpy(r + 4 + 2 * b, &s16, 2);
+        }
+    }
+}
+
+void orc_qgemv_a8(int qtype, int N, int K, const void *blocks, const float *x, float *y, int batch)
+{
+    const size_t rb = orc_row_bytes(qtype, K);
+    const int rec = qtype == ORC_Q8_0 ? 38 : 292, per = qtype == ORC_Q8_0 ? 32 : 256;
+    uint8_t *pa = (uint8_t *)malloc((size_t)(K / per) * rec);
+    for (int b = 0; b < batch; b++) {
+        if (qtype == ORC_Q8_0) orc_pack_a_i8(x + (size_t)b * K, K, pa);
+        else orc_pack_a_q3k(x + (size_t)b * K, K, pa);
+        for (int n = 0; n < N; n++) {
+            const uint8_t *w = (const uint8_t *)blocks + (size_t)n * rb;
+            double acc = 0.0;
+            if (qtype == ORC_Q8_0) {
+                for (int kg = 0; kg < K / 32; kg++) {
+                    const uint8_t *blk = w + 34 * kg, *r = pa + 38 * kg;
+                    float sa;
+                    memcpy(&sa, r, 4);
+                    int32_t dot = 0;
+                    for (int i = 0; i < 32; i++) dot += (int8_t)blk[2 + i] * (int8_t)r[6 + i];
+                    acc += (double)(rd_f16(blk) * (sa * (float)dot));
+                }
+            } else {
+                for (int sb = 0; sb < K / 256; sb++) {
+                    const uint8_t *blk = w + 110 * sb, *r = pa + 292 * sb, *hm = blk, *qs = blk + 32;
+                    float sa;
+                    memcpy(&sa, r, 4);
+                    const float d = rd_f16(blk + 108);
+                    int sc[16];
+                    q3k_scales(blk + 96, sc);
+                    for (int e = 0; e < 256; e += 16) {   /* sub-block e / 16 */
+                        int32_t dot = 0;
+                        for (int k = e; k < e + 16; k++) {
+                            const int h = k >> 7, t = (k >> 5) & 3, l = k & 31;
+                            const int q = (int)((qs[32 * h + l] >> (2 * t)) & 3) - ((hm[l] >> (4 * h + t)) & 1 ? 0 : 4);
+                            dot += q * (int8_t)r[36 + k];
+                        }
+                        const int i = 8 * (e >> 7) + 2 * ((e >> 5) & 3) + ((e >> 4) & 1);
+                        acc += (double)(d * (float)(sc[i] - 32) * (sa * (float)dot));
+                    }
+                }
+            }
+            y[(size_t)b * N + n] = (float)acc;
+        }
+    }
+    free(pa);
+}
+
 /* ---- encode (own encoders, written from the format definitions) ---------*/
 
 static int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }

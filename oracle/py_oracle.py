@@ -83,6 +83,12 @@ def lib():
         L.orc_gguf_bytes.restype = C.c_size_t
         L.orc_quantize_q8_0_ref.argtypes = [vp, C.c_size_t, vp]
         L.orc_quantize_q8_0_ref.restype = None
+        L.orc_pack_a_i8.argtypes = [vp, i, vp]
+        L.orc_pack_a_i8.restype = None
+        L.orc_pack_a_q3k.argtypes = [vp, i, vp]
+        L.orc_pack_a_q3k.restype = None
+        L.orc_qgemv_a8.argtypes = [i, i, i, vp, vp, vp, i]
+        L.orc_qgemv_a8.restype = None
         L.orc_silu.argtypes = [C.c_float]
         L.orc_silu.restype = C.c_float
         _lib = L
@@ -143,6 +149,27 @@ def quantize_q8_0_ref(x: np.ndarray) -> np.ndarray:
     out = np.empty(x.size // 32 * 34, np.uint8)
     lib().orc_quantize_q8_0_ref(_ptr(x), x.size, _ptr(out))
     return out
+
+
+# ---- the reference's activation packing ("A8") ----------------------------------
+def pack_a(mode: str, x: np.ndarray) -> np.ndarray:
+    """pack_A_i8 ('i8', 38 B per 32) or pack_A_q3k ('q3k', 292 B per 256) of
+    one fp32 row."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    if mode == "i8":
+        out = np.empty(x.size // 32 * 38, np.uint8)
+        lib().orc_pack_a_i8(_ptr(x), x.size, _ptr(out))
+    else:
+        out = np.empty(x.size // 256 * 292, np.uint8)
+        lib().orc_pack_a_q3k(_ptr(x), x.size, _ptr(out))
+    return out
+
+
+def qgemv_a8(qtype: int, blocks: np.ndarray, N: int, K: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, K)
+    y = np.empty((x.shape[0], N), np.float32)
+    lib().orc_qgemv_a8(qtype, N, K, _ptr(blocks), _ptr(x), _ptr(y), x.shape[0])
+    return y
 
 
 # ---- GEMM -------------------------------------------------------------------

@@ -53,6 +53,18 @@ size_t orc_gguf_bytes(int type, size_t n);
  * amax from 1e-6, d = amax/127, q = lrint(w/d) clamped to [-128, 127], d
  * stored as the truncating fp16 of qwen_moe_q3k.c:71-79.                    */
 void orc_quantize_q8_0_ref(const float *x, size_t n, void *blocks);
+
+/* The reference's activation packers for its IME kernels ("A8"):
+ * pack_A_i8 (qwen_moe_q3k.c:420-426), 38 B per 32 values: fp32 scale =
+ * max(|x|, 1e-6)/127, int16 sum of q, int8 q = lrint(x/scale) clamped;
+ * pack_A_q3k (:613-623), 292 B per 256: fp32 scale = max|x|/127, 16 int16
+ * negated sums of 16, int8 q = roundf(x/scale) clamped.  K % 32 / K % 256.  */
+void orc_pack_a_i8(const float *x, int K, void *out);
+void orc_pack_a_q3k(const float *x, int K, void *out);
+/* y[b][n] = W[n] . (x[b] packed as above): Q8_0 weights with pack_A_i8,
+ * Q3_K with pack_A_q3k; exact integer block dots, each block's (Q8_0) or
+ * sub-block's (Q3_K) term scaled in fp32 and summed in double in k order.  */
+void orc_qgemv_a8(int qtype, int N, int K, const void *blocks, const float *x, float *y, int batch);
 /* scale/min pair j of a K-quant 12-byte scale array (qwen_moe_q3k.c:534-538,
  * repack.cpp:222-233)                                                      */
 void orc_kq_scale_min(int j, const uint8_t *q, uint8_t *sc, uint8_t *m);

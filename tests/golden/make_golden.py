@@ -31,6 +31,11 @@ What it pins, and from which reference code:
                     qwen_moe_q3k.c:1098-1126) reads from a synthetic file made
                     by tests/gguf_writer.py (make_parse_file below): model
                     dimensions, defaults, tokens, tensor infos, data start.
+  a8_golden.npz     the reference's activation packers for its IME kernels,
+                    pack_A_i8 (qwen_moe_q3k.c:420-426) and pack_A_q3k
+                    (:613-623), compiled from the reference and run on fp32
+                    rows (normal values, rounding ties, zeros, tiny and large
+                    values).
   meta.json         struct-size known answers (block_q3_K 110 B,
                     block_q5_K 176 B, bench/q3k_probe.c:410-413) and the
                     x100_caps_t layout of the reference header.
@@ -359,7 +364,48 @@ def make_gguf_golden() -> None:
     print("wrote gguf_golden.npz, gguf_parse.json")
 
 
+def make_a8_golden() -> None:
+    q3k = open(os.path.join(REF_ROOT, "qwen_moe_q3k.c")).read()
+    parts = [
+        "#include <stdint.h>\n#include <string.h>\n#include <math.h>\n",
+        extract_line(q3k, r"^#define AREC_Q3K 292$"),
+        extract_function(q3k, r"static void pack_A_i8\(const float\*x, uint8_t\*out [^)]*\)\{"),
+        extract_function(q3k, r"static void pack_A_q3k\(const float\*a,uint8_t\*out\)\{"),
+        """
+void golden_pack_i8(const float*x,int K,uint8_t*out){ for(int kg=0;kg<K/32;kg++) pack_A_i8(x+32*kg,out+38*kg); }
+void golden_pack_q3k(const float*x,int K,uint8_t*out){ for(int sb=0;sb<K/256;sb++) pack_A_q3k(x+256*sb,out+AREC_Q3K*sb); }
+""",
+    ]
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "refa8.c")
+        with open(path, "w") as f:
+            f.write("\n".join(parts))
+        so = os.path.join(tmp, "librefa8.so")
+        subprocess.check_call(["gcc", "-std=gnu11", "-O2", "-ffp-contract=off", "-fPIC", "-shared", "-o", so, path,
+                               "-lm"])
+        L = C.CDLL(so)
+        L.golden_pack_i8.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        L.golden_pack_q3k.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        rng = np.random.default_rng(88)
+        rows = [rng.standard_normal(2048), rng.standard_normal(2048) * 1e-4, np.zeros(512),
+                np.tile([0.5, -0.5, 1.5, -2.5, 127.0, -127.0, 63.5, 0.25], 64) * (127.0 / 127.0),
+                np.full(256, 7e-7), rng.standard_normal(768) * 3e4,
+                np.r_[np.ones(255), 254.0].astype(np.float64)]   # ties at x / scale = k + 0.5
+        x = np.concatenate([np.asarray(r, np.float32) for r in rows])
+        assert x.size % 256 == 0
+        i8 = np.zeros(x.size // 32 * 38, np.uint8)
+        q3 = np.zeros(x.size // 256 * 292, np.uint8)
+        L.golden_pack_i8(x.ctypes.data, x.size, i8.ctypes.data)
+        L.golden_pack_q3k(x.ctypes.data, x.size, q3.ctypes.data)
+        np.savez_compressed(os.path.join(HERE, "a8_golden.npz"), x=x, pack_i8=i8, pack_q3k=q3)
+    print("wrote a8_golden.npz")
+
+
 def main():
+    if "--only-a8" in sys.argv:
+        po.build()
+        make_a8_golden()
+        return
     if "--only-gguf" in sys.argv:
         po.build()
         make_gguf_golden()
@@ -416,6 +462,7 @@ def main():
         json.dump(meta, f, indent=1, sort_keys=True)
     print("wrote gemm_golden.npz, quant_golden.npz, meta.json")
     make_gguf_golden()
+    make_a8_golden()
 
 
 if __name__ == "__main__":

@@ -161,3 +161,30 @@ def test_moe_oracle_partial_experts_sum_to_full():
              for lo in range(0, E, 4)]
     assert po.rel_l2(sum(parts), full) < 1e-6
     assert np.allclose(w.sum(1), 1.0, atol=1e-6)
+
+
+def test_oracle_a8_packers_equal_reference(golden_dir):
+    """pack_A_i8 / pack_A_q3k restated in the oracle give the reference's
+    packed bytes (a8_golden.npz, from the reference's own code)."""
+    g = np.load(os.path.join(golden_dir, "a8_golden.npz"))
+    np.testing.assert_array_equal(po.pack_a("i8", g["x"]), g["pack_i8"])
+    np.testing.assert_array_equal(po.pack_a("q3k", g["x"]), g["pack_q3k"])
+
+
+def test_oracle_a8_gemv_is_the_packed_product():
+    """orc_qgemv_a8 = sum over blocks of d * scale * (integer dot of the packed
+    values), checked against a numpy statement from the packed bytes."""
+    rng = np.random.default_rng(6)
+    N, K = 24, 512
+    W = po.quantize(po.Q8_0, rng.normal(0, 0.02, size=(N, K)).astype(np.float32))
+    x = rng.normal(0, 1, size=(2, K)).astype(np.float32)
+    y = po.qgemv_a8(po.Q8_0, W, N, K, x)
+    for b in range(2):
+        rec = po.pack_a("i8", x[b]).reshape(-1, 38)
+        sa = rec[:, 0:4].copy().view(np.float32)[:, 0].astype(np.float64)
+        qa = rec[:, 6:].view(np.int8).astype(np.int64)
+        blk = W.reshape(N, K // 32, 34)
+        d = blk[:, :, 0:2].copy().view(np.float16)[:, :, 0].astype(np.float64)
+        qw = blk[:, :, 2:].view(np.int8).astype(np.int64)
+        ref = (d * sa[None, :] * np.einsum("nbk,bk->nb", qw, qa)).sum(axis=1)
+        np.testing.assert_allclose(y[b], ref, rtol=1e-6, atol=1e-7)

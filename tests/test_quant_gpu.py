@@ -113,9 +113,9 @@ def test_qgemv_independent_calls(batch):
     x100b.sync()
     assert torch.equal(got[1:], ref[1:])
     assert torch.equal(got[0], ref[0])
-    with pytest.raises(x100b.X100Error):
+    with pytest.raises(x100b.X100Error):   # a flag bit the API does not define
         x100b.check(x100b.lib().x100q_lin_gemv_dev_flags(lins[0].h, xs[0].data_ptr(), got[0].data_ptr(), batch,
-                                                         2, torch.cuda.current_stream().cuda_stream))
+                                                         4, torch.cuda.current_stream().cuda_stream))
 
 
 def test_qgemv_edge_activations():

@@ -303,6 +303,81 @@ __device__ __forceinline__ void xprep_vals(const float4 v, XB *o, int t, bool ac
     if (t == 0) o->f = make_float4(s, s32, s16, other16);
 }
 
+// "A8" preparation: the activations quantised as the reference packs them
+// for its IME kernels, held in the same XB form (h = q, l = 0, s = scale /
+// 256, so 256 s h = scale q exactly and the dot products need no change;
+// the sums are scale * the integer sums of q).  xprep_vals_i8 is pack_A_i8
+// (qwen_moe_q3k.c:420-426) for one 32-element block held as in xprep_vals:
+// scale = max(|x|, 1e-6) / 127, q = round-to-nearest-even(x * (1 / scale))
+// clamped to int8, both divisions correctly rounded.
+__device__ __forceinline__ void xprep_vals_i8(const float4 v, XB *o, int t, bool active) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    amax = fmaxf(amax, 1e-6f);
+    const float scale = __fdiv_rn(amax, 127.0f);
+    const float inv = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+    const float e[4] = {v.x, v.y, v.z, v.w};
+    uint32_t hw = 0;
+    int s4 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int q = max(-128, min(127, __float2int_rn(__fmul_rn(e[k], inv))));
+        hw |= (uint32_t)(q & 0xFF) << (8 * k);
+        s4 += q;
+    }
+    int s16 = s4 + __shfl_xor_sync(0xffffffffu, s4, 1);
+    s16 += __shfl_xor_sync(0xffffffffu, s16, 2);
+    const int other16 = __shfl_xor_sync(0xffffffffu, s16, 4);
+    if (!active) return;
+    reinterpret_cast<uint32_t *>(&o->h0)[t] = hw;
+    reinterpret_cast<uint32_t *>(&o->l0)[t] = 0u;
+    if (t == 0) o->f = make_float4(scale * (1.0f / 256.0f), scale * (float)(s16 + other16), scale * (float)s16,
+                                   scale * (float)other16);
+}
+
+// pack_A_q3k (qwen_moe_q3k.c:613-623) into XB blocks: one warp per
+// 256-element superblock of a row, 8 elements per lane; scale = max|x| / 127
+// over the superblock, q = roundf(x * (1 / scale)) clamped to int8.  K must be
+// a multiple of 256.
+template <class RowPtr, class XBT>
+__device__ __forceinline__ void xprep_rows_q3k8(RowPtr row, int K, int nrows, const XBT &xb) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int nsb = K / 256, total = nrows * nsb, u4 = lane & 3;
+    for (int u = warp; u < total; u += nwarps) {   // warp-uniform
+        const int c = nrows == 1 ? 0 : u / nsb, sb = u - c * nsb;
+        const float4 *a = reinterpret_cast<const float4 *>(row(c) + sb * 256 + lane * 8);
+        const float4 p0 = __ldcg(a), p1 = __ldcg(a + 1);
+        const float e[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        float amax = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(e[k]));
+#pragma unroll
+        for (int m = 16; m; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        const float scale = __fdiv_rn(amax, 127.0f);
+        const float rep = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+        uint32_t w0 = 0, w1 = 0;
+        int s8 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int q = max(-128, min(127, (int)roundf(__fmul_rn(e[k], rep))));
+            (k < 4 ? w0 : w1) |= (uint32_t)(q & 0xFF) << (8 * (k & 3));
+            s8 += q;
+        }
+        const int s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);   // lanes 4j, 4j+1: elements 0-15 of block j
+        const int s16b = __shfl_xor_sync(0xffffffffu, s16, 2);       // lanes 4j+2, 4j+3: elements 16-31
+        XB *o = xb.block(c, sb * 8 + (lane >> 2));
+        uint32_t *h = reinterpret_cast<uint32_t *>(&o->h0), *l = reinterpret_cast<uint32_t *>(&o->l0);
+        h[2 * u4] = w0;
+        h[2 * u4 + 1] = w1;
+        l[2 * u4] = 0u;
+        l[2 * u4 + 1] = 0u;
+        if (u4 == 0) o->f = make_float4(scale * (1.0f / 256.0f), scale * (float)(s16 + s16b), scale * (float)s16,
+                                        scale * (float)s16b);
+    }
+}
+
 // The whole CTA prepares `nrows` activation rows row(c)[0 .. K) into xb as
 // tokens 0 .. nrows-1 (blocks past K, up to the slice boundary, are zero).
 // A warp converts 4 blocks at a time; each pass first issues up to PF (kXPF
@@ -319,7 +394,7 @@ __device__ __forceinline__ void xprep_vals(const float4 v, XB *o, int t, bool ac
 // W . rmsnorm(x) = s * (W . (x * nw)) without a second pass over x.
 constexpr int kXPF = 4;
 constexpr int kSsTok = 16;
-template <int PF = kXPF, class RowPtr, class XBT>
+template <int PF = kXPF, bool I8 = false, class RowPtr, class XBT>
 __device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const XBT &xb,
                                            const float *__restrict__ nw = nullptr, float *ss = nullptr) {
     const int nxb = xb.ns * 8, kb = K / 32;
@@ -358,10 +433,22 @@ __device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const X
                         x = make_float4(x.x * w4.x, x.y * w4.y, x.z * w4.z, x.w * w4.w);
                     }
                 }
-                xprep_vals(x, xb.block(c, j), t, active);
+                if constexpr (I8) xprep_vals_i8(x, xb.block(c, j), t, active);
+                else xprep_vals(x, xb.block(c, j), t, active);
             }
         }
     }
+}
+
+// Activation preparation of a GEMV: a8 = 0 the exact 16-bit split
+// (xprep_rows), 1 pack_A_i8 per 32 values, 2 pack_A_q3k per 256 values (no
+// RMS-norm folding in the A8 forms).
+template <class RowPtr, class XBT>
+__device__ __forceinline__ void xprep_gemv(int a8, RowPtr row, int K, int nrows, const XBT &xb, const float *nw,
+                                           float *ss) {
+    if (a8 == 2) xprep_rows_q3k8(row, K, nrows, xb);
+    else if (a8 == 1) xprep_rows<kXPF, true>(row, K, nrows, xb);
+    else xprep_rows(row, K, nrows, xb, nw, ss);
 }
 
 // 1 / sqrt(mean of squares + eps) of token c from the slots xprep_rows filled

@@ -50,7 +50,7 @@ template <int QT, int B>
 __global__ void __launch_bounds__(kGemvThreads, 1)
     qgemv_kernel(const uint8_t *__restrict__ W, int N, int K, int TR, const float *__restrict__ x,
                  float *__restrict__ y, int batch, const float *__restrict__ nw, float eps, int accum,
-                 int indep, int *status) {
+                 int indep, int a8, int *status) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ uint64_t bar;
     __shared__ int abort_flag;
@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     }
     pdl_launch_dependents();
     if (!indep) pdl_wait();                       // x may come from the previous kernel
-    xprep_rows([x, K](int c) { return x + (long)c * K; }, K, batch, xb, nw, ss);
+    xprep_gemv(a8, [x, K](int c) { return x + (long)c * K; }, K, batch, xb, nw, ss);
     __syncthreads();
     if (threadIdx.x < batch) scale[threadIdx.x] = nw ? rms_scale(ss, blockDim.x / 8, threadIdx.x, K, eps) : 1.0f;
     const bool ok = mbar_wait(&bar, 0, &abort_flag, status);
@@ -172,6 +172,64 @@ __global__ void repack_kernel(int qt, int N, int K, const uint8_t *__restrict__ 
     }
 }
 
+// ---- the reference's activation records (pack_act_i8 / pack_act_q3k) ----------
+__device__ __forceinline__ void st_bytes(uint8_t *p, const void *v, int n) {
+    for (int i = 0; i < n; ++i) p[i] = static_cast<const uint8_t *>(v)[i];
+}
+// One warp per 32-value record of 38 bytes (qwen_moe_q3k.c:420-426); the
+// arithmetic of xprep_vals_i8.
+__global__ void pack_i8_kernel(const float *__restrict__ x, long nrec, uint8_t *__restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    for (long r = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; r < nrec;
+         r += ((long)gridDim.x * blockDim.x) >> 5) {
+        const float v = x[32 * r + lane];
+        float amax = fabsf(v);
+        for (int m = 16; m; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        amax = fmaxf(amax, 1e-6f);
+        const float scale = __fdiv_rn(amax, 127.0f);
+        const float inv = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+        const int q = max(-128, min(127, __float2int_rn(__fmul_rn(v, inv))));
+        int sum = q;
+        for (int m = 16; m; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+        uint8_t *o = out + 38 * r;
+        o[6 + lane] = (uint8_t)(int8_t)q;
+        if (lane == 0) {
+            const int16_t s16 = (int16_t)sum;
+            st_bytes(o, &scale, 4);
+            st_bytes(o + 4, &s16, 2);
+        }
+    }
+}
+// One warp per 256-value record of 292 bytes (qwen_moe_q3k.c:613-623); the
+// arithmetic of xprep_rows_q3k8.
+__global__ void pack_q3k_kernel(const float *__restrict__ x, long nrec, uint8_t *__restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    for (long r = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; r < nrec;
+         r += ((long)gridDim.x * blockDim.x) >> 5) {
+        const float4 *a = reinterpret_cast<const float4 *>(x + 256 * r + 8 * lane);
+        const float4 p0 = a[0], p1 = a[1];
+        const float e[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        float amax = 0.f;
+        for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(e[k]));
+        for (int m = 16; m; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        const float scale = __fdiv_rn(amax, 127.0f);
+        const float rep = scale != 0.f ? __fdiv_rn(1.0f, scale) : 0.f;
+        uint8_t *o = out + 292 * r;
+        int s8 = 0;
+        for (int k = 0; k < 8; ++k) {
+            const int q = max(-128, min(127, (int)roundf(__fmul_rn(e[k], rep))));
+            o[36 + 8 * lane + k] = (uint8_t)(int8_t)q;
+            s8 += q;
+        }
+        const int s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);   // sub-block lane / 2
+        if (!(lane & 1)) {
+            const int16_t neg = (int16_t)(-s16);
+            st_bytes(o + 4 + 2 * (lane >> 1), &neg, 2);
+        }
+        if (lane == 0) st_bytes(o, &scale, 4);
+    }
+}
+
 constexpr size_t kGemvSmemMax = 220 * 1024;
 
 static size_t gemv_smem(int qt, int K, int TR, int B) {
@@ -211,7 +269,7 @@ static int launch_B(DevCtx *c, const QMat &m, const float *x, float *y, int batc
     const int threads = o.indep ? kGemvThreads / 2 : kGemvThreads;
     return launch_k(qgemv_kernel<QT, B>, dim3((m.N + TR - 1) / TR), dim3(threads), smem, s, o.pdl,
                     (const uint8_t *)m.w, m.N, m.K, TR, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0,
-                    o.indep ? 1 : 0, c->d_status);
+                    o.indep ? 1 : 0, o.a8, c->d_status);
 }
 
 template <int QT>
@@ -396,7 +454,7 @@ int x100q_lin_gemv_dev(const x100q_lin *l, const float *x, float *y, int batch, 
 
 int x100q_lin_gemv_dev_flags(const x100q_lin *l, const float *x, float *y, int batch, int flags, void *stream) {
     set_error(X100_OK);
-    if (flags & ~X100Q_GEMV_INDEPENDENT) {
+    if (flags & ~(X100Q_GEMV_INDEPENDENT | X100Q_GEMV_A8)) {
         set_error(X100_E_ARG);
         return X100_E_ARG;
     }
@@ -412,7 +470,35 @@ int x100q_lin_gemv_dev_flags(const x100q_lin *l, const float *x, float *y, int b
     if (!c) return get_error();
     GemvOpts o;
     o.indep = (flags & X100Q_GEMV_INDEPENDENT) != 0;
+    if (flags & X100Q_GEMV_A8) {   // the reference's activation packing for the weight type
+        if (l->m.qtype == Q8_0) o.a8 = 1;
+        else if (l->m.qtype == Q3_K) o.a8 = 2;
+        else {
+            set_error(X100_E_UNSUPPORTED);
+            return X100_E_UNSUPPORTED;
+        }
+    }
     int st = launch_qgemv_ex(c, l->m, x, y, batch, o, static_cast<cudaStream_t>(stream));
+    if (st) set_error(st);
+    return st;
+}
+
+int x100q_pack_act_dev(int mode, const float *x, int K, int batch, void *out, void *stream) {
+    set_error(X100_OK);
+    const int per = mode == X100Q_PACK_I8 ? 32 : 256;
+    if ((mode != X100Q_PACK_I8 && mode != X100Q_PACK_Q3K) || !x || !out || K <= 0 || K % per || batch < 1 ||
+        (reinterpret_cast<uintptr_t>(x) & 15)) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    DevCtx *c = ctx();
+    if (!c) return get_error();
+    const long nrec = (long)batch * (K / per);
+    const int grid = (int)std::min<long>((nrec + 7) / 8, (long)c->sm_count * 16);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (mode == X100Q_PACK_I8) pack_i8_kernel<<<grid, 256, 0, s>>>(x, nrec, static_cast<uint8_t *>(out));
+    else pack_q3k_kernel<<<grid, 256, 0, s>>>(x, nrec, static_cast<uint8_t *>(out));
+    const int st = check_cuda(cudaGetLastError(), X100_E_LAUNCH);
     if (st) set_error(st);
     return st;
 }

@@ -35,6 +35,7 @@ struct GemvOpts {
     bool accum = false;
     bool pdl = true;   // false: launch behind a full barrier (see launch_k)
     bool indep = false;   // x, y untouched by running kernels: prepare x before the dependency wait
+    int a8 = 0;           // activations packed as the reference's IME path: 1 pack_A_i8, 2 pack_A_q3k
 };
 int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
                     cudaStream_t s);

@@ -128,7 +128,7 @@ template <int QT, int NT>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     qgemv_mma_kernel(const uint8_t *__restrict__ W, int N, int K, int ck, int stages, const float *__restrict__ x,
                      float *__restrict__ y, int batch, const float *__restrict__ nw, float eps, int accum,
-                     int *status) {
+                     int a8, int *status) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float ssq[(kMmaThreads / 32) * 4][kSsTok];   // RMS-norm sums of squares per 8-lane group
     __shared__ float scale[16];
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     pdl_wait();   // x may come from the previous kernel; the previous call on this matrix is complete
 
     // ---- 2. activations ----
-    xprep_rows([x, K](int c) { return x + (long)c * K; }, K, batch, xb, nw, &ssq[0][0]);
+    xprep_gemv(a8, [x, K](int c) { return x + (long)c * K; }, K, batch, xb, nw, &ssq[0][0]);
     __syncthreads();
     if (threadIdx.x < batch) scale[threadIdx.x] = nw ? rms_scale(&ssq[0][0], blockDim.x / 8, threadIdx.x, K, eps) : 1.0f;
     __syncthreads();
@@ -274,7 +274,7 @@ static int launch_mma_nt(DevCtx *c, const QMat &m, const float *x, float *y, int
     const int ntiles = (m.N + kMmaRows - 1) / kMmaRows;
     const int grid = std::min(ntiles, c->sm_count);
     return launch_k(qgemv_mma_kernel<QT, NT>, dim3(grid), dim3(kMmaThreads), p.smem, s, o.pdl, (const uint8_t *)m.w,
-                    m.N, m.K, p.ck, p.stages, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0, c->d_status);
+                    m.N, m.K, p.ck, p.stages, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0, o.a8, c->d_status);
 }
 
 // Launches of 8 nt tokens each (nt from the plan).

@@ -111,6 +111,7 @@ _SIGS = {
     "x100q_model_load_gguf": ([vp, vp], vp),
     "x100q_gguf_dequant_dev": ([i32, vp, C.c_long, vp, vp], i32),
     "x100q_quantize_q8_0_dev": ([vp, C.c_long, vp, vp], i32),
+    "x100q_pack_act_dev": ([i32, vp, i32, i32, vp, vp], i32),
 }
 
 
@@ -231,9 +232,10 @@ class Lin:
     def gemv(self, x, y, batch: int) -> None:
         check(lib().x100q_lin_gemv(self.h, _p(x), _p(y), batch), "x100q_lin_gemv")
 
-    def gemv_dev(self, x, y, batch: int, stream=None, independent: bool = False) -> None:
-        check(lib().x100q_lin_gemv_dev_flags(self.h, _p(x), _p(y), batch, 1 if independent else 0,
-                                             _stream(stream)), "x100q_lin_gemv_dev_flags")
+    def gemv_dev(self, x, y, batch: int, stream=None, independent: bool = False, a8: bool = False) -> None:
+        flags = (1 if independent else 0) | (2 if a8 else 0)
+        check(lib().x100q_lin_gemv_dev_flags(self.h, _p(x), _p(y), batch, flags, _stream(stream)),
+              "x100q_lin_gemv_dev_flags")
 
     def device_bytes(self) -> int:
         b = C.c_size_t()
@@ -421,6 +423,15 @@ class Gguf:
 
 def gguf_dequant_dev(gtype: int, data, n: int, out, stream=None) -> None:
     check(lib().x100q_gguf_dequant_dev(gtype, _p(data), n, _p(out), _stream(stream)), "x100q_gguf_dequant_dev")
+
+
+PACK_I8, PACK_Q3K = 1, 2
+GEMV_INDEPENDENT, GEMV_A8 = 1, 2
+
+
+def pack_act_dev(mode: int, x, K: int, batch: int, out, stream=None) -> None:
+    """The reference's pack_act_i8 (mode PACK_I8) / pack_act_q3k (PACK_Q3K)."""
+    check(lib().x100q_pack_act_dev(mode, _p(x), K, batch, _p(out), _stream(stream)), "x100q_pack_act_dev")
 
 
 def quantize_q8_0_dev(x, n: int, blocks, stream=None) -> None:
