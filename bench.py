@@ -571,7 +571,9 @@ def bench_q4gemv(args, dist, peaks, peak_src):
         "metric": "Q4_0 dequant-GEMV HBM GB/s", "value": round(gbs * dist.world, 2), "unit": "GB/s",
         "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "q4_0 weights, fp32 activations (int32 dp4a on 16-bit split x)",
+        "vs_baseline": None,
+        "dtype": "q4_0 weights, fp32 activations (int32 dot products on 16-bit split x: " +
+                 ("dp4a)" if B <= 4 else "integer mma.sync)"),
         "data": "synthetic random well-formed Q4_0 blocks, x ~ N(0,1)",
         "config": {"workload": f"Q4_0 GEMV y=W.x W {N}x{K} batch {B}", "N": N, "K": K, "batch": B,
                    "l2": f"{COPIES} weight copies rotated per step ({COPIES * wbytes / 2**20:.0f} MiB > L2)",
@@ -581,7 +583,11 @@ def bench_q4gemv(args, dist, peaks, peak_src):
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": load_traffic(f"q4gemv_b{B}"),
                      "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
-                     "kernel": "x100::q::qgemv_kernel<Q4_0>", "algorithmic_bytes_per_launch": alg,
+                     # independent calls of up to 4 tokens run on the dp4a kernel, larger
+                     # batches on the tensor-core kernel (the dependent chain: 2+ tokens)
+                     "kernel": ("x100::q::qgemv_kernel<Q4_0> (dp4a)" if B <= 4 else
+                                "x100::q::qgemv_mma_kernel<Q4_0> (integer mma.sync)"),
+                     "algorithmic_bytes_per_launch": alg,
                      "kernel_us_mean": round(per_call_s * 1e6, 3), "parity_rel_l2": err,
                      "dependent_chain": {"achieved": round(chain_gbs, 1),
                                          "frac": round(chain_gbs / peaks["hbm_gbs"], 4),
@@ -715,7 +721,7 @@ def bench_moe(args, dist, peaks, peak_src):
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(f"moe_b{B}"),
                      "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
                      "kernel": ("router_logits + moe_fused (2 launches per call)" if B == 1 else
-                                "router_logits + route_group + gate_up_group + down_group + combine (5 launches per call)"),
+                                "router_logits + route_group + gate_up_pipe + down_pipe + combine (5 launches per call)"),
                      "algorithmic_bytes_per_token": alg_tok, "call_us_mean": round(per_call_us, 3),
                      "parity": err},
         "clocks": clocks,
