@@ -227,6 +227,22 @@ int x100q_model_forward_dev(x100q_model *m, const int *tokens, float *h,
  * (needs tok_embd and lm).                                                  */
 int x100q_model_forward(x100q_model *m, const int *tokens, const int *pos,
                         float *logits, int batch);
+/* Per-token sequence slots: as x100q_model_forward_dev, with token b using
+ * the cache of slot[b] (a device array of batch ints, each in
+ * [0, max_batch)) instead of slot b, so several tokens of one sequence, at
+ * different positions, can step together.  Every token's k and v are
+ * written to the cache before any token attends, and token b attends over
+ * positions 0 .. pos[b] of its slot, which takes in the step's own earlier
+ * positions (causal, as the reference's prefill).  Two tokens with the same
+ * slot and position are the caller's error; a slot out of range writes
+ * nothing and makes the next synchronising call report X100_E_ARG.          */
+int x100q_model_forward_slots_dev(x100q_model *m, const int *tokens, float *h, const int *pos,
+                                  const int *slot, float *logits, int batch, void *stream);
+/* Prefill: the reference's prefill_chunk4 (qwen_moe_hp.c:1748-1858) for n
+ * (1 <= n <= max_batch) tokens -- tokens[0 .. n) of the sequence in `slot`
+ * at positions pos0 .. pos0 + n - 1 in one step, their k and v left in the
+ * cache; logits [n][vocab] (host, or NULL for none).  Synchronous.          */
+int x100q_model_prefill(x100q_model *m, int slot, const int *tokens, int n, int pos0, float *logits);
 
 /* ---- expert-parallel combine over peer memory ------------------------------ */
 /* With experts split over `world` processes (one per GPU, x100q_moe_create

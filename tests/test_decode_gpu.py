@@ -218,6 +218,80 @@ def test_position_past_cache_is_reported(world):
     x100b.sync()
 
 
+def test_prefill_matches_token_by_token_oracle(world):
+    """x100q_model_prefill of 4 tokens of the sequence in slot 2 at positions
+    40..43 (the reference's prefill_chunk4) in one step: each token's logits
+    equal, within 1e-3, the oracle stepping the tokens one by one (each
+    attending over the cache the earlier ones extended); the chunk's k and v
+    land at positions 40..43 of slot 2 and nothing else in the cache moves."""
+    c, m = world["c"], world["model"]
+    load_kv(world)
+    toks, slot, pos0 = np.array([7, 100, 300, 5], np.int32), 2, 40
+    logits = m.prefill(slot, toks, pos0)
+    caches = [[x.copy() for x in world["kv"][li][slot]] for li in range(c["n_layers"])]
+    for i, t in enumerate(toks):
+        h = world["emb"][t].copy()
+        for li in range(c["n_layers"]):
+            po.decode_layer(c, world["layers"][li], caches[li][0], caches[li][1], h, pos0 + i, nthreads=8)
+        ref = po.decode_head(c, world["out_norm"], world["lm"], h, nthreads=8)
+        assert po.rel_l2(logits[i], ref) <= REL, (i, po.rel_l2(logits[i], ref))
+    kf = lambda a: a.view(np.float16).astype(np.float32)   # noqa: E731
+    for li in range(c["n_layers"]):
+        kg, vg = m.kv_read(li, slot, 0, c["ctx"])
+        rows = slice(pos0, pos0 + len(toks))
+        assert po.rel_l2(kf(kg[:, rows]), kf(caches[li][0][:, rows])) <= REL
+        assert po.rel_l2(kf(vg[:, rows]), kf(caches[li][1][:, rows])) <= REL
+        keep = np.ones(c["ctx"], bool)
+        keep[rows] = False
+        assert np.array_equal(kg[:, keep], world["kv"][li][slot][0][:, keep])
+        for other in (0, 1, 3):   # other sequences untouched
+            ko, _ = m.kv_read(li, other, 0, c["ctx"])
+            assert np.array_equal(ko, world["kv"][li][other][0])
+
+
+def test_forward_slots_identity_equals_forward_dev(world):
+    """With slot[b] = b the slot path (k and v written by their own kernel,
+    attention reading them back from the cache) gives the bits of the fused
+    path."""
+    import torch
+    c, m = world["c"], world["model"]
+    B = 3
+    toks = torch.tensor([11, 22, 33], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([15, 64, 159], dtype=torch.int32, device="cuda")
+    slot = torch.tensor([0, 1, 2], dtype=torch.int32, device="cuda")
+    h1, h2 = (torch.empty((B, c["d"]), device="cuda") for _ in range(2))
+    l1, l2 = (torch.empty((B, c["vocab"]), device="cuda") for _ in range(2))
+    load_kv(world)
+    m.forward_dev(toks, h1, pos, l1, B)
+    x100b.sync()
+    k1 = m.kv_read(1, 1, 0, c["ctx"])
+    load_kv(world)
+    m.forward_slots_dev(toks, h2, pos, slot, l2, B)
+    x100b.sync()
+    k2 = m.kv_read(1, 1, 0, c["ctx"])
+    assert torch.equal(h1, h2) and torch.equal(l1, l2)
+    assert np.array_equal(k1[0], k2[0]) and np.array_equal(k1[1], k2[1])
+
+
+def test_slot_out_of_range_is_reported(world):
+    import torch
+    c, m = world["c"], world["model"]
+    load_kv(world)
+    toks = torch.tensor([1], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([3], dtype=torch.int32, device="cuda")
+    slot = torch.tensor([c["max_batch"]], dtype=torch.int32, device="cuda")
+    h = torch.empty((1, c["d"]), device="cuda")
+    m.forward_slots_dev(toks, h, pos, slot, None, 1)
+    with pytest.raises(x100b.X100Error) as e:
+        x100b.sync()
+    assert e.value.code == x100b.X100_E_ARG
+    for s_ in range(c["max_batch"]):
+        kg, _ = m.kv_read(0, s_, 0, c["ctx"])
+        assert np.array_equal(kg, world["kv"][0][s_][0])
+    with pytest.raises(x100b.X100Error):
+        m.prefill(0, np.array([1, 2], np.int32), c["ctx"] - 1)   # runs past the cache
+
+
 def test_model_rejects_bad_config():
     with pytest.raises(x100b.X100Error):
         x100b.Model(**dict(CFG, head_dim=64))

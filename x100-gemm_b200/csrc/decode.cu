@@ -2,11 +2,15 @@
 // forward() (qwen_moe_q3k.c:1842-1983) as a chain of sm_100a kernels, and the
 // x100q_model_* entry points of include/x100q.h.
 //
-// Per layer and step (B tokens, one per sequence slot b < B):
+// Per layer and step (B tokens; token b uses sequence slot b, or slot[b]
+// when a slot array is given -- several tokens of one sequence, e.g. a
+// prefill chunk, then share a slot at different positions):
 //   1. qkv  = Wqkv . rmsnorm(h; attn_norm)        qgemv (norm folded in), Q8_0
 //   2. attention                                   attn_decode_kernel
 //        q/k per-head rmsnorm (q_norm / k_norm) + NEOX RoPE, k and v of the
-//        step written to the fp16 cache at pos, softmax(q.K^T / sqrt(hd)) . V
+//        step written to the fp16 cache at pos (with a slot array: by
+//        kv_write_kernel first, so every token of a shared slot sees the
+//        others' earlier positions), softmax(q.K^T / sqrt(hd)) . V
 //        over positions 0..pos (GQA: q head hh reads kv head hh / (nh/nkv))
 //   3. h   += Wo . att                             qgemv (accumulate)
 //   4. h   += MoE(rmsnorm(h; ffn_norm))            router (norm folded in) +
@@ -52,6 +56,9 @@ struct AttnArgs {
     long row_base;      // cache row (of the tensor maps) of this layer's first row
     float *part;        // [B][nh][nsplit][kPartStride]
     int kv_early;       // stage K/V before waiting on the previous kernel (see the kernel)
+    const int *slot;    // [B] sequence slot of each token, or null: token b uses slot b
+    int nslots;         // slots of the cache (max_batch); a slot outside [0, nslots) is an error
+    int prewritten;     // the step's k and v are already in the cache (kv_write_kernel)
     float *att;         // [B][nh * hd]
     int *status;
 };
@@ -114,6 +121,33 @@ __device__ __forceinline__ uint32_t kv_off(int row, int dim) {
     return (uint32_t)(sub * kChunk * 128 + row * 128 + ((chunk ^ (row & 7)) << 4) + (dim & 7) * 2);
 }
 
+// The step's k (normed, rotated) and v of every token into the cache at
+// its slot and position, rounded to fp16 exactly as attn_decode_kernel's own
+// write does.  Used when tokens may share a slot (a prefill chunk): the
+// attention kernel then reads every position, the step's included, through
+// the cache, so no token can miss another's earlier position.  grid (nkv, B),
+// one warp; a position or slot out of range writes nothing (the attention
+// kernel reports it).
+__global__ void __launch_bounds__(32) kv_write_kernel(const AttnArgs a) {
+    const int kvh = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
+    pdl_launch_dependents();
+    pdl_wait();   // qkv comes from the previous kernel
+    const int pos = a.pos[b], sb = a.slot ? a.slot[b] : b;
+    if (pos < 0 || pos >= a.ctx || sb < 0 || sb >= a.nslots) return;
+    const long head_row = ((long)sb * a.nkv + kvh) * a.ctx;
+    const float *qrow = a.qkv + (long)b * a.qkv_n;
+    float4 k = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + kvh) * kHD) + lane);
+    const float4 v = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + a.nkv + kvh) * kHD) + lane);
+    k = norm_rope_head(k, a.k_norm, a.eps, pos, a.rope_base);
+    uint2 kk, vv;
+    kk.x = h2u(__floats2half2_rn(k.x, k.y));
+    kk.y = h2u(__floats2half2_rn(k.z, k.w));
+    vv.x = h2u(__floats2half2_rn(v.x, v.y));
+    vv.y = h2u(__floats2half2_rn(v.z, v.w));
+    reinterpret_cast<uint2 *>(a.kc + (head_row + pos) * kHD)[lane] = kk;
+    reinterpret_cast<uint2 *>(a.vc + (head_row + pos) * kHD)[lane] = vv;
+}
+
 // Grid (nsplit, nkv, B).  CTA (sp, kvh, b) attends the query heads of kv head
 // kvh over positions [sp*64, min((sp+1)*64, pos+1)).  Its K and V rows
 // arrive by TMA (two 64-dim boxes each, 128-byte swizzle); the queries of the
@@ -148,7 +182,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     const int gpr = a.nh / a.nkv;
     const int hq = lane >> 2, q4 = lane & 3;   // fragment row (head) and column pair
     const int j0 = sp * C;
-    const long head_row = ((long)b * a.nkv + kvh) * a.ctx;   // cache row of position 0 in this layer
+    int sb = a.slot ? __ldg(a.slot + b) : b;                  // written before the step began
+    const bool bad_slot = sb < 0 || sb >= a.nslots;
+    if (bad_slot) sb = 0;                                     // nothing is staged or read for it
+    const long head_row = ((long)sb * a.nkv + kvh) * a.ctx;  // cache row of position 0 in this layer
     int pos = 0, n = 0;
     auto stage = [&]() {   // thread 0: barrier + the four TMA boxes of this CTA
         abort_flag = 0;
@@ -165,7 +202,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     };
     bool staged = false;
     if (a.kv_early) {
-        pos = a.pos[b];
+        pos = bad_slot ? -1 : a.pos[b];
         n = (pos < 0 || pos >= a.ctx) ? 0 : min(C, pos + 1 - j0);
         if (threadIdx.x == 0) {
             tma_prefetch_desc(&tmK);
@@ -177,7 +214,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     pdl_launch_dependents();
     pdl_wait();                                   // qkv comes from the previous kernel
     if (!staged) {
-        pos = a.pos[b];
+        pos = bad_slot ? -1 : a.pos[b];
         n = (pos < 0 || pos >= a.ctx) ? 0 : min(C, pos + 1 - j0);
         if (threadIdx.x == 0) stage();
     }
@@ -194,7 +231,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     }
     __syncthreads();                              // barrier initialised, queries ready
     if (n > 0) mbar_wait(&bar, 0, &abort_flag, a.status);   // raises abort_flag on timeout
-    if (n > 0 && pos < j0 + C && warp == 0) {
+    if (n > 0 && pos < j0 + C && warp == 0 && !a.prewritten) {
         // the step's own k (normed, rotated) and v, rounded to the cache's fp16
         float4 k = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + kvh) * kHD) + lane);
         const float4 v = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + a.nkv + kvh) * kHD) + lane);
@@ -669,9 +706,10 @@ int x100q_model_embed_dev(x100q_model *m, const int *tokens, float *h, int batch
 
 // One layer, steps 1-4 of the file comment.  kv_early: the step began behind
 // a full barrier (see attn_decode_kernel); barrier: launch the first kernel
-// behind one.
+// behind one.  slot: per-token cache slots (null: token b uses slot b); with
+// it the step's k and v go to the cache in a kernel of their own first.
 static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const int *pos, int batch, float *eout,
-                        cudaStream_t s, bool kv_early, bool barrier) {
+                        cudaStream_t s, bool kv_early, bool barrier, const int *slot = nullptr) {
     const x100q_model_cfg &g = m->cfg;
     ModelLayer &L = m->layers[layer];
     static bool attr[64];
@@ -706,9 +744,16 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     a.vc = m->vc + (size_t)layer * m->layer_kv;
     a.row_base = (long)layer * g.max_batch * g.n_kv_heads * g.ctx;
     a.part = m->part;
-    a.kv_early = kv_early ? 1 : 0;
+    a.kv_early = (kv_early && !slot) ? 1 : 0;
+    a.slot = slot;
+    a.nslots = g.max_batch;
+    a.prewritten = slot ? 1 : 0;
     a.att = m->att;
     a.status = c->d_status;
+    if (slot) {
+        st = launch_pdl(kv_write_kernel, dim3(g.n_kv_heads, batch), dim3(32), 0, s, a);
+        if (st) return st;
+    }
     st = launch_pdl(attn_decode_kernel, dim3(a.nsplit, g.n_kv_heads, batch), dim3(kAttnThreads), attn_smem(), s,
                     m->tmK, m->tmV, a);
     if (st) return st;
@@ -730,6 +775,9 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     o4.accum = eout == nullptr;
     return launch_moe_ex(c, L.moe, m->S, h, eout ? eout : h, batch, o4, s);
 }
+
+static int forward_impl(x100q_model *m, const int *tokens, float *h, const int *pos, const int *slot, float *logits,
+                        int batch, void *stream);
 
 extern "C" {
 
@@ -777,6 +825,22 @@ int x100q_model_head_dev(x100q_model *m, const float *h, float *logits, int batc
 
 int x100q_model_forward_dev(x100q_model *m, const int *tokens, float *h, const int *pos, float *logits, int batch,
                             void *stream) {
+    return forward_impl(m, tokens, h, pos, nullptr, logits, batch, stream);
+}
+
+int x100q_model_forward_slots_dev(x100q_model *m, const int *tokens, float *h, const int *pos, const int *slot,
+                                  float *logits, int batch, void *stream) {
+    if (!slot) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    return forward_impl(m, tokens, h, pos, slot, logits, batch, stream);
+}
+
+}  // extern "C"
+
+static int forward_impl(x100q_model *m, const int *tokens, float *h, const int *pos, const int *slot, float *logits,
+                        int batch, void *stream) {
     set_error(X100_OK);
     if (!m || !h || !pos) {
         set_error(X100_E_ARG);
@@ -799,11 +863,13 @@ int x100q_model_forward_dev(x100q_model *m, const int *tokens, float *h, const i
     int st = X100_OK;
     if (tokens) st = x100q_model_embed_dev(m, tokens, h, batch, stream);
     for (int l = 0; st == X100_OK && l < m->cfg.n_layers; ++l)
-        st = layer_launch(m, c, l, h, pos, batch, nullptr, s, true, l == 0 && !tokens);
+        st = layer_launch(m, c, l, h, pos, batch, nullptr, s, true, l == 0 && !tokens, slot);
     if (st == X100_OK && logits) st = x100q_model_head_dev(m, h, logits, batch, stream);
     if (st) set_error(st);
     return st;
 }
+
+extern "C" {
 
 int x100q_model_forward(x100q_model *m, const int *tokens, const int *pos, float *logits, int batch) {
     set_error(X100_OK);
@@ -829,6 +895,41 @@ int x100q_model_forward(x100q_model *m, const int *tokens, const int *pos, float
     if (!st) st = x100q_model_forward_dev(m, dtok, dh, dpos, dl, batch, c->stream);
     if (!st) st = check_cuda(cudaMemcpyAsync(logits, dl, lb, cudaMemcpyDefault, c->stream), X100_E_COPY);
     const int st2 = sync_and_status(c, c->stream);
+    if (st == X100_OK) st = st2;
+    if (st) set_error(st);
+    return st;
+}
+
+int x100q_model_prefill(x100q_model *m, int slot, const int *tokens, int n, int pos0, float *logits) {
+    set_error(X100_OK);
+    if (!m || !tokens || n < 1 || n > m->cfg.max_batch || slot < 0 || slot >= m->cfg.max_batch || pos0 < 0 ||
+        pos0 + n > m->cfg.ctx || !m->tok_embd || (logits && (!m->out_norm || !m->lm.w))) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    DeviceGuard dg(m->device);
+    DevCtx *c = ctx();
+    if (!c) return get_error();
+    std::lock_guard<std::mutex> lk(c->mu);
+    const x100q_model_cfg &g = m->cfg;
+    // staging: tokens, positions, slots, h, logits
+    const size_t tb = 256, hb = (size_t)n * g.d * 4, lb = (size_t)n * g.vocab * 4;
+    uint8_t *buf = static_cast<uint8_t *>(stage_buf(c, 0, 3 * tb + hb));
+    if (!buf) return get_error();
+    int *dtok = reinterpret_cast<int *>(buf), *dpos = reinterpret_cast<int *>(buf + tb),
+        *dslot = reinterpret_cast<int *>(buf + 2 * tb);
+    float *dh = reinterpret_cast<float *>(buf + 3 * tb);
+    float *dl = nullptr;
+    if (logits && !(dl = static_cast<float *>(stage_buf(c, 1, lb)))) return get_error();
+    std::vector<int> hp(n), hs(n, slot);
+    for (int i = 0; i < n; ++i) hp[i] = pos0 + i;
+    int st = check_cuda(cudaMemcpyAsync(dtok, tokens, n * 4, cudaMemcpyDefault, c->stream), X100_E_COPY);
+    if (!st) st = check_cuda(cudaMemcpyAsync(dpos, hp.data(), n * 4, cudaMemcpyHostToDevice, c->stream), X100_E_COPY);
+    if (!st) st = check_cuda(cudaMemcpyAsync(dslot, hs.data(), n * 4, cudaMemcpyHostToDevice, c->stream), X100_E_COPY);
+    if (!st) st = forward_impl(m, dtok, dh, dpos, dslot, dl, n, c->stream);
+    if (!st && logits)
+        st = check_cuda(cudaMemcpyAsync(logits, dl, lb, cudaMemcpyDefault, c->stream), X100_E_COPY);
+    const int st2 = sync_and_status(c, c->stream);   // the host vectors outlive the copies
     if (st == X100_OK) st = st2;
     if (st) set_error(st);
     return st;

@@ -89,6 +89,8 @@ _SIGS = {
     "x100q_model_head_dev": ([vp, vp, vp, i32, vp], i32),
     "x100q_model_forward_dev": ([vp, vp, vp, vp, vp, i32, vp], i32),
     "x100q_model_forward": ([vp, vp, vp, vp, i32], i32),
+    "x100q_model_forward_slots_dev": ([vp, vp, vp, vp, vp, vp, i32, vp], i32),
+    "x100q_model_prefill": ([vp, i32, vp, i32, i32, vp], i32),
     # expert-parallel combine
     "x100q_ep_create": ([i32, i32, i32], vp),
     "x100q_ep_handle": ([vp, vp], i32),
@@ -327,6 +329,19 @@ class Model:
     def forward_dev(self, tokens, h, pos, logits, batch, stream=None):
         check(lib().x100q_model_forward_dev(self.h, _p(tokens), _p(h), _p(pos), _p(logits), batch,
                                             _stream(stream)), "x100q_model_forward_dev")
+
+    def forward_slots_dev(self, tokens, h, pos, slot, logits, batch, stream=None):
+        check(lib().x100q_model_forward_slots_dev(self.h, _p(tokens), _p(h), _p(pos), _p(slot), _p(logits), batch,
+                                                  _stream(stream)), "x100q_model_forward_slots_dev")
+
+    def prefill(self, slot: int, tokens, pos0: int, logits: bool = True):
+        """n tokens of the sequence in `slot` at positions pos0 .. pos0+n-1 in
+        one step; returns their logits [n][vocab] (or None)."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        n = tokens.shape[0]
+        out = np.empty((n, self.cfg.vocab), np.float32) if logits else None
+        check(lib().x100q_model_prefill(self.h, slot, _p(tokens), n, pos0, _p(out)), "x100q_model_prefill")
+        return out
 
     def forward(self, tokens, pos):
         tokens = np.ascontiguousarray(tokens, np.int32)
