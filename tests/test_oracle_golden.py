@@ -188,3 +188,29 @@ def test_oracle_a8_gemv_is_the_packed_product():
         qw = blk[:, :, 2:].view(np.int8).astype(np.int64)
         ref = (d * sa[None, :] * np.einsum("nbk,bk->nb", qw, qa)).sum(axis=1)
         np.testing.assert_allclose(y[b], ref, rtol=1e-6, atol=1e-7)
+
+
+def test_oracle_a8_gemv_q3k_is_the_packed_product():
+    """orc_qgemv_a8 for Q3_K = sum over 16-element sub-blocks of
+    d * (scale - 32) * sa * (integer dot of the packed activations with the
+    3-bit weights), against a numpy statement: the 3-bit values are the
+    dequantised weights divided by their sub-block scale (exact small
+    integers), the packed values come from pack_A_q3k's bytes."""
+    rng = np.random.default_rng(8)
+    N, K = 12, 512
+    W = po.quantize(po.Q3_K, rng.normal(0, 0.02, size=(N, K)).astype(np.float32))
+    x = rng.normal(0, 1, size=(2, K)).astype(np.float32)
+    y = po.qgemv_a8(po.Q3_K, W, N, K, x)
+    deq = po.dequant(po.Q3_K, W, N, K).astype(np.float64)          # [N][K]
+    blk = W.reshape(N, K // 256, 110)
+    d = blk[:, :, 108:110].copy().view(np.float16)[:, :, 0].astype(np.float64)
+    for b in range(2):
+        rec = po.pack_a("q3k", x[b]).reshape(-1, 292)
+        sa = rec[:, 0:4].copy().view(np.float32)[:, 0].astype(np.float64)
+        qa = rec[:, 36:].view(np.int8).astype(np.float64)             # [K/256][256]
+        ref = np.zeros(N)
+        for n in range(N):
+            for sb in range(K // 256):
+                w = deq[n, 256 * sb:256 * (sb + 1)]
+                ref[n] += sa[sb] * np.dot(w, qa[sb])                 # = sum d*sc*q_w * sa*q_a
+        np.testing.assert_allclose(y[b], ref, rtol=1e-5, atol=1e-7)
