@@ -141,7 +141,10 @@ int x100q_moe_ffn_dev(const x100q_moe *moe, const float *hn, float *eout, int ba
  * thread's current CUDA device; the work is enqueued on `stream` and the call
  * returns without synchronising.  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before
- * any stream capture.  All calls share the one array: calls whose work
+ * any stream capture.  The address is cached per device together with the id
+ * of the CUDA context it was taken in; after a device reset (a new context)
+ * the next call looks it up again, so that call too should come before any
+ * capture.  All calls share the one array: calls whose work
  * overlaps on the GPU (other streams, other threads) race and must be
  * serialised by the caller.                                                 */
 int x100q_router_topk_noalloc(const float *router, const float *hn, int d, int n_exp,

@@ -736,23 +736,27 @@ void orc_fill_u8(uint64_t seed, uint8_t *dst, size_t n)
 
 /* ---- one decode step (qwen_moe_q3k.c:1842-1983) ----------------------------
  * Restates forward()'s per-layer body for one token of one sequence, with
- * the fp32 router (router mode 0), exact SiLU and a fp16 KV cache: the step's
- * k and v are rounded to fp16 (round-to-nearest-even) when stored, and the
+ * the fp32 router (router mode 0) and exact SiLU.  The cache is this layer's
+ * cache of this sequence, [nkv][ctx][hd]: fp16 bits (kv_f32 = 0; the step's
+ * k and v are rounded to fp16, round-to-nearest-even, when stored, as the
+ * BASELINE decode configuration asks) or fp32 (kv_f32 = 1; the reference's
+ * own cache precision, qwen_moe.c:282 / qwen_moe_q3k.c:1877-1880).  The
  * attention reads every position, the current one included, from the cache.
- * kc / vc: this layer's cache of this sequence, [nkv][ctx][hd] fp16 bits.
  * attn_w: the four projections as GGUF-native blocks of attn_qtype:
  * wq [nh*hd][d], wk / wv [nkv*hd][d], wo [d][nh*hd].  h (d floats) is
  * updated in place; sel_out / w_out (n_act each, may be NULL) get the
  * routing.                                                                   */
-void orc_decode_layer(int d, int nh, int nkv, int hd, int ctx, int pos, float rope_base, float eps,
-                      int attn_qtype, const float *attn_norm, const void *wq, const void *wk,
-                      const void *wv, const float *q_norm, const float *k_norm, const void *wo,
-                      const float *ffn_norm, int n_exp, int n_act, int ffn, int expert_qtype,
-                      const float *router, const void *gate_exps, const void *up_exps,
-                      const void *down_exps, uint16_t *kc, uint16_t *vc, float *h,
-                      int *sel_out, float *w_out, int nthreads)
+static void decode_layer_impl(int d, int nh, int nkv, int hd, int ctx, int pos, float rope_base, float eps,
+                              int attn_qtype, const float *attn_norm, const void *wq, const void *wk,
+                              const void *wv, const float *q_norm, const float *k_norm, const void *wo,
+                              const float *ffn_norm, int n_exp, int n_act, int ffn, int expert_qtype,
+                              const float *router, const void *gate_exps, const void *up_exps,
+                              const void *down_exps, void *kc_, void *vc_, int kv_f32, float *h,
+                              int *sel_out, float *w_out, int nthreads)
 {
     const int qd = nh * hd, kvd = nkv * hd, gpr = nh / nkv;
+    uint16_t *kc = (uint16_t *)kc_, *vc = (uint16_t *)vc_;
+    float *kcf = (float *)kc_, *vcf = (float *)vc_;
     float *hn = (float *)malloc((size_t)d * sizeof(float));
     float *q = (float *)malloc((size_t)qd * sizeof(float));
     float *k = (float *)malloc((size_t)kvd * sizeof(float));
@@ -778,17 +782,24 @@ void orc_decode_layer(int d, int nh, int nkv, int hd, int ctx, int pos, float ro
     /* :1877-1880 head-major cache write */
     for (int kvh = 0; kvh < nkv; kvh++)
         for (int t = 0; t < hd; t++) {
-            kc[((size_t)kvh * ctx + pos) * hd + t] = orc_f32_to_f16_rne(k[kvh * hd + t]);
-            vc[((size_t)kvh * ctx + pos) * hd + t] = orc_f32_to_f16_rne(v[kvh * hd + t]);
+            const size_t at = ((size_t)kvh * ctx + pos) * hd + t;
+            if (kv_f32) {
+                kcf[at] = k[kvh * hd + t];
+                vcf[at] = v[kvh * hd + t];
+            } else {
+                kc[at] = orc_f32_to_f16_rne(k[kvh * hd + t]);
+                vc[at] = orc_f32_to_f16_rne(v[kvh * hd + t]);
+            }
         }
     /* :1890-1899 serial attention */
     const float scale = 1.0f / sqrtf((float)hd);
     for (int hh = 0; hh < nh; hh++) {
         const int kvh = hh / gpr;
         const float *qh = q + hh * hd;
-        const uint16_t *Kh = kc + (size_t)kvh * ctx * hd, *Vh = vc + (size_t)kvh * ctx * hd;
+        const size_t base = (size_t)kvh * ctx * hd;
         for (int j = 0; j <= pos; j++) {
-            for (int t = 0; t < hd; t++) kf[t] = orc_f16_to_f32(Kh[(size_t)j * hd + t]);
+            for (int t = 0; t < hd; t++)
+                kf[t] = kv_f32 ? kcf[base + (size_t)j * hd + t] : orc_f16_to_f32(kc[base + (size_t)j * hd + t]);
             float s = 0.f;
             for (int t = 0; t < hd; t++) s += qh[t] * kf[t];
             sc[j] = s * scale;
@@ -797,7 +808,8 @@ void orc_decode_layer(int d, int nh, int nkv, int hd, int ctx, int pos, float ro
         float *oh = att + hh * hd;
         for (int t = 0; t < hd; t++) oh[t] = 0.f;
         for (int j = 0; j <= pos; j++)
-            for (int t = 0; t < hd; t++) oh[t] += sc[j] * orc_f16_to_f32(Vh[(size_t)j * hd + t]);
+            for (int t = 0; t < hd; t++)
+                oh[t] += sc[j] * (kv_f32 ? vcf[base + (size_t)j * hd + t] : orc_f16_to_f32(vc[base + (size_t)j * hd + t]));
     }
     /* :1912-1915 */
     orc_qgemv_mt(attn_qtype, d, qd, wo, att, tmp, 1, nthreads);
@@ -808,6 +820,32 @@ void orc_decode_layer(int d, int nh, int nkv, int hd, int ctx, int pos, float ro
                 hn, tmp, 1, sel_out, w_out, nthreads);
     for (int i = 0; i < d; i++) h[i] += tmp[i];
     free(hn); free(q); free(k); free(v); free(att); free(sc); free(tmp); free(kf);
+}
+
+void orc_decode_layer(int d, int nh, int nkv, int hd, int ctx, int pos, float rope_base, float eps,
+                      int attn_qtype, const float *attn_norm, const void *wq, const void *wk,
+                      const void *wv, const float *q_norm, const float *k_norm, const void *wo,
+                      const float *ffn_norm, int n_exp, int n_act, int ffn, int expert_qtype,
+                      const float *router, const void *gate_exps, const void *up_exps,
+                      const void *down_exps, uint16_t *kc, uint16_t *vc, float *h,
+                      int *sel_out, float *w_out, int nthreads)
+{
+    decode_layer_impl(d, nh, nkv, hd, ctx, pos, rope_base, eps, attn_qtype, attn_norm, wq, wk, wv, q_norm, k_norm,
+                      wo, ffn_norm, n_exp, n_act, ffn, expert_qtype, router, gate_exps, up_exps, down_exps, kc, vc,
+                      0, h, sel_out, w_out, nthreads);
+}
+
+void orc_decode_layer_f32kv(int d, int nh, int nkv, int hd, int ctx, int pos, float rope_base, float eps,
+                            int attn_qtype, const float *attn_norm, const void *wq, const void *wk,
+                            const void *wv, const float *q_norm, const float *k_norm, const void *wo,
+                            const float *ffn_norm, int n_exp, int n_act, int ffn, int expert_qtype,
+                            const float *router, const void *gate_exps, const void *up_exps,
+                            const void *down_exps, float *kc, float *vc, float *h,
+                            int *sel_out, float *w_out, int nthreads)
+{
+    decode_layer_impl(d, nh, nkv, hd, ctx, pos, rope_base, eps, attn_qtype, attn_norm, wq, wk, wv, q_norm, k_norm,
+                      wo, ffn_norm, n_exp, n_act, ffn, expert_qtype, router, gate_exps, up_exps, down_exps, kc, vc,
+                      1, h, sel_out, w_out, nthreads);
 }
 
 /* qwen_moe_q3k.c:1980-1981: logits = lm . rmsnorm(h, out_norm) */

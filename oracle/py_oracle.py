@@ -64,6 +64,8 @@ def lib():
             "orc_rope_neox": [vp, i, i, f],
             "orc_decode_layer": [i, i, i, i, i, i, f, f, i] + [vp] * 8 + [i, i, i, i] + [vp] * 4 +
                                 [vp, vp, vp, vp, vp, i],
+            "orc_decode_layer_f32kv": [i, i, i, i, i, i, f, f, i] + [vp] * 8 + [i, i, i, i] + [vp] * 4 +
+                                      [vp, vp, vp, vp, vp, i],
             "orc_decode_head": [i, i, f, i, vp, vp, vp, vp, i],
             "orc_fill_u8": [C.c_uint64, vp, C.c_size_t],
             "orc_kq_scale_min": [i, vp, vp, vp],
@@ -108,6 +110,28 @@ def ref_lib():
             getattr(L, n).restype = None
         _ref = L
     return _ref
+
+
+def ref_gemm_i8_mt(A, B, C, nthreads):
+    """C += A @ B by the reference's own gemm_ref_i8 (oracle/_ref/libx100ref.so,
+    src/gemm_ref.c compiled unchanged) on row slices, one host thread each
+    (ctypes releases the GIL for the call).  Raises if the library is absent."""
+    from concurrent.futures import ThreadPoolExecutor
+    ref = ref_lib()
+    if ref is None:
+        raise FileNotFoundError("oracle/_ref/libx100ref.so missing (build it where the reference tree exists)")
+    M, K = A.shape
+    N = B.shape[1]
+    assert A.flags.c_contiguous and B.flags.c_contiguous and C.flags.c_contiguous and C.shape == (M, N)
+    per = [(M * t) // nthreads for t in range(nthreads + 1)]
+
+    def work(t):
+        r0, r1 = per[t], per[t + 1]
+        if r1 > r0:
+            ref.gemm_ref_i8(r1 - r0, N, K, A[r0:].ctypes.data, B.ctypes.data, C[r0:].ctypes.data)
+    with ThreadPoolExecutor(nthreads) as ex:
+        list(ex.map(work, range(nthreads)))
+    return C
 
 
 # ---- generators ------------------------------------------------------------
@@ -244,6 +268,23 @@ def moe_ffn(d, n_exp, n_act, ffn, qtype, router, gate, up, down, hn,
     return eout, sel, w
 
 
+def route(router, hn, n_act):
+    """Routing only (qwen_moe.c:296-301): fp32 router logits in k order,
+    softmax, greedy top-n_act, renormalised weights.  router [n_exp][d],
+    hn [batch][d]; returns (sel, w), each [batch][n_act].  Runs orc_moe_ffn
+    with an empty expert range, so no expert weights are touched."""
+    router = np.ascontiguousarray(router, np.float32)
+    n_exp, d = router.shape
+    hn = np.ascontiguousarray(hn, np.float32).reshape(-1, d)
+    B = hn.shape[0]
+    eout = np.empty((B, d), np.float32)
+    sel = np.empty((B, n_act), np.int32)
+    w = np.empty((B, n_act), np.float32)
+    lib().orc_moe_ffn(d, n_exp, n_act, 32, Q4_0, _ptr(router), None, None, None, 0, 0,
+                      _ptr(hn), _ptr(eout), B, _ptr(sel), _ptr(w), 1)
+    return sel, w
+
+
 def f16_to_f32(h: int) -> float:
     return lib().orc_f16_to_f32(h)
 
@@ -275,6 +316,24 @@ def decode_layer(cfg, lw, kc, vc, h, pos, nthreads=1):
                            cfg["n_exp"], cfg["n_act"], cfg["moe_ffn"], cfg["expert_qtype"],
                            *(_ptr(ws[k]) for k in ("router", "gate", "up", "down")),
                            _ptr(kc), _ptr(vc), _ptr(h), _ptr(sel), _ptr(w), nthreads)
+    return sel, w
+
+
+def decode_layer_f32kv(cfg, lw, kc, vc, h, pos, nthreads=1):
+    """decode_layer with an fp32 cache (float32 [n_kv_heads][ctx][head_dim]),
+    the reference's own cache precision."""
+    assert h.dtype == np.float32 and h.flags.c_contiguous
+    assert kc.dtype == np.float32 and kc.flags.c_contiguous and vc.flags.c_contiguous
+    sel = np.empty(cfg["n_act"], np.int32)
+    w = np.empty(cfg["n_act"], np.float32)
+    ws = {k: np.ascontiguousarray(v) for k, v in lw.items()}
+    lib().orc_decode_layer_f32kv(cfg["d"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], cfg["ctx"], pos,
+                                 cfg["rope_base"], cfg["eps"], cfg["attn_qtype"],
+                                 *(_ptr(ws[k]) for k in ("attn_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo",
+                                                         "ffn_norm")),
+                                 cfg["n_exp"], cfg["n_act"], cfg["moe_ffn"], cfg["expert_qtype"],
+                                 *(_ptr(ws[k]) for k in ("router", "gate", "up", "down")),
+                                 _ptr(kc), _ptr(vc), _ptr(h), _ptr(sel), _ptr(w), nthreads)
     return sel, w
 
 

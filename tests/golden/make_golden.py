@@ -1,8 +1,8 @@
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container where the reference tree is mounted (REF_ROOT, default
-/root/reference); the fixtures it writes are committed so that the tests never
-need the reference at run time.
+Run where the reference tree is available (REF_ROOT, by default the directory
+`reference` beside this repository); the fixtures it writes are committed so
+that the tests never need the reference at run time.
 
 What it pins, and from which reference code:
   gemm_golden.npz   gemm_ref_i8 / gemm_ref_f32 of the reference's
@@ -39,8 +39,28 @@ What it pins, and from which reference code:
   meta.json         struct-size known answers (block_q3_K 110 B,
                     block_q5_K 176 B, bench/q3k_probe.c:410-413) and the
                     x100_caps_t layout of the reference header.
+  moe_golden.npz    the reference's routing and layer-body functions on
+                    edge-case inputs: softmax (qwen_moe.c:189, the scalar
+                    branch of qwen_moe_q3k.c:1221-1248 is the same text),
+                    the greedy top-k and renormalisation lines of forward()
+                    (qwen_moe.c:299-301) after that softmax (ties included),
+                    rmsnorm (qwen_moe.c:187 = qwen_moe_q3k.c:1166), rope
+                    (qwen_moe.c:188) and rope_table / rope_apply
+                    (qwen_moe_q3k.c:1170-1175) at positions 0 .. 4095, and
+                    swiglu_exact (qwen_moe_q3k.c:1678-1680).
+  forward_golden.npz  logits of the reference's whole forward()
+                    (qwen_moe.c:272-315: rmsnorm, q/k/v, per-head q/k norm and
+                    RoPE, fp32 KV cache, serial softmax attention, Wo,
+                    residual, router, softmax, top-k, renormalise, SwiGLU
+                    experts, weighted sum, residual, output norm, lm_head)
+                    compiled unchanged, with its linear layers (the RISC-V
+                    IME kernels lin_mm / lin_mm_packed / pack_act) replaced by
+                    the scalar fp32 dequant-GEMV -- the BASELINE's oracle
+                    definition -- over weights dequantised by the reference's
+                    own decoders.  Inputs: tests/golden/golden_inputs.py.
 The extracted reference functions are compiled under a temporary directory
-and never written into this repository.
+and never written into this repository.  REF_ROOT (environment) names the
+reference tree; by default the directory `reference` beside this repository.
 """
 from __future__ import annotations
 
@@ -60,7 +80,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "oracle"))
 import py_oracle as po  # noqa: E402
 
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("REF_ROOT") or os.path.normpath(os.path.join(REPO, "..", "reference"))
 
 GEMM_SHAPES = [(1, 1, 1), (3, 5, 7), (7, 9, 33), (16, 16, 16), (33, 17, 5),
                (64, 48, 40), (128, 64, 96), (129, 130, 131)]
@@ -401,7 +421,274 @@ void golden_pack_q3k(const float*x,int K,uint8_t*out){ for(int sb=0;sb<K/256;sb+
     print("wrote a8_golden.npz")
 
 
+# ---- routing and layer-body functions, and the whole forward() ------------------------
+FWD_STUBS = r"""
+/* ---- written here, not reference code: the linear layers as fp32 row-major
+ * matrices, y[n] = sum_k W[n][k] * x[k] in k order (the scalar dequant-GEMV),
+ * in place of the reference's IME kernels.  pack_act keeps the fp32 vector
+ * (in the caller's activation buffer) instead of quantising it. */
+typedef struct { int N, K; const float *W; } Lin;
+static void pack_act(const float *x, int K, int8_t *xt, float *xs_out) { memcpy(xt, x, (size_t)K * 4); *xs_out = 1.0f; }
+static void lin_mm_packed(const Lin *l, const int8_t *xt, float xs, float *y, int nt) {
+    const float *x = (const float *)xt; (void)xs; (void)nt;
+    for (int n = 0; n < l->N; n++) { const float *w = l->W + (size_t)n * l->K; float acc = 0;
+        for (int k = 0; k < l->K; k++) acc += w[k] * x[k]; y[n] = acc; }
+}
+static void lin_mm(const Lin *l, const float *x, float *y, int nt, int8_t *xt) {
+    float xs; pack_act(x, l->K, xt, &xs); lin_mm_packed(l, xt, xs, y, nt);
+}
+"""
+
+FWD_EXPORTS = r"""
+/* ---- written here: exported wrappers ---- */
+void golden_softmax(float *x, int n) { softmax(x, n); }
+void golden_rmsnorm(float *o, const float *x, const float *w, int n, float eps) { rmsnorm(o, x, w, n, eps); }
+void golden_rope(float *v, int hd, int pos, float base) { rope(v, hd, pos, base); }
+void golden_rope_table(float *c, float *s, int hd, int pos, float base) { rope_table(c, s, hd, pos, base); }
+void golden_rope_apply(float *v, int hd, const float *c, const float *s) { rope_apply(v, hd, c, s); }
+void golden_swiglu(float *g, const float *u, int n) { swiglu_exact(g, u, n); }
+void golden_topk(const float *logits, int ne, int na, int *sel, float *sw) {
+    float rl[256]; memcpy(rl, logits, (size_t)ne * 4); softmax(rl, ne);
+    TOPK_LINE
+    RENORM_LINE
+}
+static Model M;
+void golden_setup(int d, int nl, int nh, int nkv, int hd, int vocab, int n_exp, int n_act, int moe, float rope_base,
+                  float eps, float *tok_embd, float *out_norm, float *lm, float *attn_norm, float *ffn_norm,
+                  float *q_norm, float *k_norm, float *router, float *wq, float *wk, float *wv, float *wo,
+                  float *eg, float *eu, float *ed) {
+    const int qd = nh * hd, kvd = nkv * hd;
+    M.d = d; M.nl = nl; M.nh = nh; M.nkv = nkv; M.hd = hd; M.vocab = vocab; M.nt = 1; M.n_exp = n_exp;
+    M.n_act = n_act; M.moe = moe; M.rope_base = rope_base; M.eps = eps; M.tok_embd = tok_embd; M.out_norm = out_norm;
+    M.lm = (Lin){vocab, d, lm};
+    M.L = calloc((size_t)nl, sizeof(Layer));
+    for (int l = 0; l < nl; l++) { Layer *y = &M.L[l];
+        y->attn_norm = attn_norm + (size_t)l * d; y->ffn_norm = ffn_norm + (size_t)l * d;
+        y->q_norm = q_norm + (size_t)l * hd; y->k_norm = k_norm + (size_t)l * hd;
+        y->router = router + (size_t)l * n_exp * d;
+        y->q = (Lin){qd, d, wq + (size_t)l * qd * d}; y->k = (Lin){kvd, d, wk + (size_t)l * kvd * d};
+        y->v = (Lin){kvd, d, wv + (size_t)l * kvd * d}; y->o = (Lin){d, qd, wo + (size_t)l * d * qd};
+        y->eg = calloc((size_t)n_exp, sizeof(Lin)); y->eu = calloc((size_t)n_exp, sizeof(Lin));
+        y->ed = calloc((size_t)n_exp, sizeof(Lin));
+        for (int e = 0; e < n_exp; e++) { size_t i = (size_t)l * n_exp + e;
+            y->eg[e] = (Lin){moe, d, eg + i * moe * d}; y->eu[e] = (Lin){moe, d, eu + i * moe * d};
+            y->ed[e] = (Lin){d, moe, ed + i * d * moe}; } }
+}
+/* one forward() step; Kc / Vc in the reference's layout [layer][ctx][nkv*hd] */
+void golden_step(int tok, int pos, float *Kc, float *Vc, int ctx, float *logits) {
+    const int d = M.d, qd = M.nh * M.hd, kvd = M.nkv * M.hd;
+    size_t big = (size_t)(d > qd ? d : qd); if (big < (size_t)M.moe) big = M.moe; if (big < (size_t)ctx) big = ctx;
+    float *hn = malloc(d * 4), *q = malloc(qd * 4), *k = malloc(kvd * 4), *vv = malloc(kvd * 4), *att = malloc(qd * 4);
+    float *tmp = malloc(big * 4), *g = malloc(M.moe * 4), *u = malloc(M.moe * 4), *eout = malloc(d * 4);
+    int8_t *xt = malloc(big * 4), *xt2 = malloc(big * 4);
+    Kv kv = {Kc, Vc, kvd, ctx};
+    forward(&M, tok, pos, &kv, logits, hn, q, k, vv, att, tmp, g, u, eout, xt, xt2);
+    free(hn); free(q); free(k); free(vv); free(att); free(tmp); free(g); free(u); free(eout); free(xt); free(xt2);
+}
+"""
+
+
+def build_ref_forward(tmp: str, tag: str) -> C.CDLL:
+    """qwen_moe.c's forward() and its helpers, and qwen_moe_q3k.c's RoPE table
+    and exact SwiGLU, extracted unchanged and compiled under tmp with the fp32
+    linear-layer stubs above.  `tag` names the library file: forward() keeps
+    a static residual buffer sized by the first model's d, so every model
+    size gets its own copy of the library."""
+    moe = open(os.path.join(REF_ROOT, "qwen_moe.c")).read()
+    q3k = open(os.path.join(REF_ROOT, "qwen_moe_q3k.c")).read()
+    rms_moe = extract_line(moe, r"^static void rmsnorm\(float\*o,const float\*x,const float\*w,int n,float eps\).*$")
+    rms_q3k = extract_line(q3k, r"^static void rmsnorm\(float\*o,const float\*x,const float\*w,int n,float eps\).*$")
+    assert rms_moe == rms_q3k, "the engines' rmsnorm differ"
+    sm_moe = extract_line(moe, r"^static void softmax\(float\*x,int n\)\{ float m=-1e30f;.*$")
+    body = sm_moe[sm_moe.index("{") + 1:sm_moe.rindex("}")].strip()
+    q3k_soft = extract_function(q3k, r"static void softmax\(float\*x,int n\)\{")
+    assert body in q3k_soft, "qwen_moe_q3k.c softmax's scalar branch is not qwen_moe.c's softmax"
+    exports = FWD_EXPORTS.replace(
+        "TOPK_LINE", extract_line(moe, r"^\s*for\(int a=0;a<na;a\+\+\)\{ int bi=-1; float bv=-1;.*$").strip()).replace(
+        "RENORM_LINE", extract_line(moe, r"^\s*float ssum=0; for\(int a=0;a<na;a\+\+\)ssum\+=sw\[a\];.*$").strip())
+    parts = [
+        "#include <stdio.h>\n#include <stdlib.h>\n#include <stdint.h>\n#include <string.h>\n#include <math.h>\n"
+        "#include <time.h>\n",
+        FWD_STUBS,
+        extract_function(moe, r"static double now\(void\)\{"),
+        extract_line(moe, r"^static double gT_actpack=0, gT_lin=0, gT_attn=0, gT_rest=0;.*$"),
+        extract_line(moe, r"^typedef struct \{ float\*attn_norm,\*ffn_norm,\*q_norm,\*k_norm,\*router;.*\} Layer;$"),
+        extract_line(moe, r"^typedef struct \{ int d,nl,nh,nkv,hd,vocab,nt,n_exp,n_act,moe;.*\} Model;$"),
+        rms_moe,
+        extract_line(moe, r"^static void rope\(float\*v,int hd,int pos,float base\).*$"),
+        sm_moe,
+        extract_line(moe, r"^typedef struct \{ float\*Kc,\*Vc; int kvd,ctx; \} Kv;$"),
+        extract_function(moe, r"static void forward\(Model\*m,int tok,int pos,Kv\*kv,float\*logits,"),
+        extract_function(q3k, r"static void rope_table\(float\*cosb,float\*sinb,int hd,int pos,float base\)\{"),
+        extract_function(q3k, r"static void rope_apply\(float\*v,int hd,const float\*cosb,const float\*sinb\)\{"),
+        extract_function(q3k, r"static void swiglu_exact\(float\*g,const float\*u,int n\)\{"),
+        exports,
+    ]
+    path = os.path.join(tmp, f"reffwd_{tag}.c")
+    with open(path, "w") as f:
+        f.write("\n".join(parts))
+    so = os.path.join(tmp, f"libreffwd_{tag}.so")
+    subprocess.check_call(["gcc", "-std=gnu11", "-O2", "-ffp-contract=off", "-fPIC", "-shared", "-w",
+                           "-o", so, path, "-lm"])
+    L = C.CDLL(so)
+    vp, i, f = C.c_void_p, C.c_int, C.c_float
+    L.golden_softmax.argtypes = [vp, i]
+    L.golden_rmsnorm.argtypes = [vp, vp, vp, i, f]
+    L.golden_rope.argtypes = [vp, i, i, f]
+    L.golden_rope_table.argtypes = [vp, vp, i, i, f]
+    L.golden_rope_apply.argtypes = [vp, i, vp, vp]
+    L.golden_swiglu.argtypes = [vp, vp, i]
+    L.golden_topk.argtypes = [vp, i, i, vp, vp]
+    L.golden_setup.argtypes = [i] * 9 + [f, f] + [vp] * 15
+    L.golden_step.argtypes = [i, i, vp, vp, i, vp]
+    return L
+
+
+def _p(a):
+    return C.c_void_p(a.ctypes.data)
+
+
+def make_moe_golden() -> None:
+    rng = np.random.default_rng(4242)
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        L = build_ref_forward(tmp, "fn")
+        # softmax: router-sized, attention-sized, ties, huge and tiny logits, n = 1
+        vecs = [rng.standard_normal(128) * 3, np.full(8, 0.5), np.array([1e4, -1e4, 0.0, 1e4]), np.array([42.0]),
+                rng.standard_normal(4096) * 10, np.array([1.0, np.nextafter(np.float32(1), np.float32(2)), 1.0]),
+                np.array([-1e4, -1e4 + 1, -3e4]), rng.standard_normal(256) * 40]
+        vecs = [np.asarray(v, np.float32) for v in vecs]
+        x = np.concatenate(vecs)
+        off = np.cumsum([0] + [v.size for v in vecs]).astype(np.int64)
+        y = x.copy()
+        for a, b in zip(off[:-1], off[1:]):
+            seg = np.ascontiguousarray(y[a:b])
+            L.golden_softmax(_p(seg), int(b - a))
+            y[a:b] = seg
+        out.update(softmax_x=x, softmax_off=off, softmax_y=y)
+        # top-k after softmax: random routers, exact ties at the selection
+        # boundary, all-equal logits, duplicates above the boundary
+        cases = []
+        for t in range(6):
+            cases.append((128, 8, rng.standard_normal(128) * (0.2 + t)))
+        tie = rng.standard_normal(128) - 5.0
+        tie[[3, 5, 9, 100]] = 2.0                              # four equal maxima, two slots
+        cases.append((128, 2, tie))
+        bnd = rng.standard_normal(128) - 5.0
+        bnd[:6] = np.arange(6) + 3.0
+        bnd[[40, 7, 99, 64]] = 1.5                             # four tied for the last two of eight
+        cases.append((128, 8, bnd))
+        cases.append((16, 4, np.zeros(16)))                    # all equal
+        cases.append((128, 16, rng.standard_normal(128)))
+        dup = rng.standard_normal(64)
+        dup[10] = dup[20] = dup[30] = dup.max() + 1.0          # tied maxima
+        cases.append((64, 8, dup))
+        tl, tn, tk, ts, tw = [], [], [], [], []
+        for ne, na, lg in cases:
+            lg = np.ascontiguousarray(np.asarray(lg, np.float32))
+            sel = np.zeros(na, np.int32)
+            sw = np.zeros(na, np.float32)
+            L.golden_topk(_p(lg), ne, na, _p(sel), _p(sw))
+            tl.append(lg), tn.append(ne), tk.append(na), ts.append(sel), tw.append(sw)
+        out.update(topk_logits=np.concatenate(tl), topk_ne=np.array(tn, np.int32), topk_na=np.array(tk, np.int32),
+                   topk_sel=np.concatenate(ts), topk_w=np.concatenate(tw))
+        # rmsnorm: hidden-sized, head-sized, zero and large vectors
+        rx = [rng.standard_normal(2048), rng.standard_normal(128), np.zeros(128), rng.standard_normal(2048) * 1e3,
+              rng.standard_normal(256) * 1e-4]
+        rx = [np.asarray(v, np.float32) for v in rx]
+        rw = [np.asarray(1 + 0.1 * rng.standard_normal(v.size), np.float32) for v in rx]
+        ro = []
+        for v, w in zip(rx, rw):
+            o = np.zeros_like(v)
+            L.golden_rmsnorm(_p(o), _p(v), _p(w), v.size, C.c_float(1e-6))
+            ro.append(o)
+        out.update(rms_x=np.concatenate(rx), rms_w=np.concatenate(rw), rms_y=np.concatenate(ro),
+                   rms_off=np.cumsum([0] + [v.size for v in rx]).astype(np.int64))
+        # RoPE: head_dim 128, base 1e6 (the decode configuration) and 64 / 1e4
+        rp = [(128, 1e6, p) for p in (0, 1, 2, 63, 64, 1000, 2047, 4095)] + [(64, 1e4, p) for p in (0, 7, 511)]
+        cs, vin, vt, vr = [], [], [], []
+        for hd, base, pos in rp:
+            c = np.zeros(hd // 2, np.float32)
+            s_ = np.zeros(hd // 2, np.float32)
+            L.golden_rope_table(_p(c), _p(s_), hd, pos, C.c_float(base))
+            v = np.asarray(rng.standard_normal(hd), np.float32)
+            a1 = v.copy()
+            L.golden_rope_apply(_p(a1), hd, _p(c), _p(s_))
+            a2 = v.copy()
+            L.golden_rope(_p(a2), hd, pos, C.c_float(base))
+            cs.append(np.concatenate([c, s_])), vin.append(v), vt.append(a1), vr.append(a2)
+        out.update(rope_cfg=np.array(rp, np.float64), rope_cossin=np.concatenate(cs), rope_v=np.concatenate(vin),
+                   rope_table_apply=np.concatenate(vt), rope_inline=np.concatenate(vr))
+        # SwiGLU: a grid over the range where expf under/overflows, plus random
+        g = np.concatenate([np.linspace(-120, 120, 481), rng.standard_normal(1000) * 4, [0.0, -0.0, 88.7, -88.7, -104.0]])
+        g = np.asarray(g, np.float32)
+        u = np.asarray(rng.standard_normal(g.size), np.float32)
+        gy = g.copy()
+        L.golden_swiglu(_p(gy), _p(u), g.size)
+        out.update(swiglu_g=g, swiglu_u=u, swiglu_y=gy)
+    np.savez_compressed(os.path.join(HERE, "moe_golden.npz"), **out)
+    print("wrote moe_golden.npz")
+
+
+def make_forward_golden() -> None:
+    import golden_inputs as gi
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        dec = build_ref_decoders(tmp)
+
+        def deq(qt, blk, n):
+            y = np.zeros(n, np.float32)
+            if qt == po.Q3_K:
+                dec.golden_dq_q3k(blk.ctypes.data, n // 256, y.ctypes.data)
+            else:
+                dec.golden_dq_gguf(qt, blk.ctypes.data, n, y.ctypes.data)
+            return y
+
+        for case, c in gi.CASES.items():
+            m = gi.model(case)
+            d, hd, E, F, V = c["d"], c["head_dim"], c["n_exp"], c["moe_ffn"], c["vocab"]
+            qd, kvd, nl = c["n_heads"] * hd, c["n_kv_heads"] * hd, c["n_layers"]
+            at, et = c["attn_qtype"], c["expert_qtype"]
+            cat = lambda key: np.ascontiguousarray(np.concatenate([ly[key].reshape(-1) for ly in m["layers"]]))  # noqa: E731
+            dq = lambda key, qt, n: np.ascontiguousarray(np.concatenate(  # noqa: E731
+                [deq(qt, ly[key], n) for ly in m["layers"]]))
+            arrs = dict(tok_embd=np.ascontiguousarray(m["tok_embd"]), out_norm=m["out_norm"],
+                        lm=deq(c["lm_qtype"], m["lm"], V * d),
+                        attn_norm=cat("attn_norm"), ffn_norm=cat("ffn_norm"), q_norm=cat("q_norm"),
+                        k_norm=cat("k_norm"), router=cat("router"),
+                        wq=dq("wq", at, qd * d), wk=dq("wk", at, kvd * d), wv=dq("wv", at, kvd * d),
+                        wo=dq("wo", at, d * qd), eg=dq("gate", et, E * F * d), eu=dq("up", et, E * F * d),
+                        ed=dq("down", et, E * d * F))
+            L = build_ref_forward(tmp, case)
+            L.golden_setup(d, nl, c["n_heads"], c["n_kv_heads"], hd, V, E, c["n_act"], F,
+                           C.c_float(c["rope_base"]), C.c_float(c["eps"]),
+                           *(_p(arrs[k]) for k in ("tok_embd", "out_norm", "lm", "attn_norm", "ffn_norm", "q_norm",
+                                                   "k_norm", "router", "wq", "wk", "wv", "wo", "eg", "eu", "ed")))
+            ctx = c["ctx"]
+            Kc = np.zeros((nl, ctx, kvd), np.float32)
+            Vc = np.zeros((nl, ctx, kvd), np.float32)
+            logits = []
+            for st, (tok, pos) in enumerate(c["steps"]):
+                if c["prefill"]:
+                    for li in range(nl):   # oracle layout [nkv][ctx][hd] -> the reference's [ctx][nkv*hd]
+                        k, v = gi.prefill_cache(case, li, st)
+                        Kc[li] = k.transpose(1, 0, 2).reshape(ctx, kvd)
+                        Vc[li] = v.transpose(1, 0, 2).reshape(ctx, kvd)
+                lg = np.zeros(V, np.float32)
+                L.golden_step(tok, pos, _p(Kc), _p(Vc), ctx, _p(lg))
+                logits.append(lg)
+            out[f"{case}_logits"] = np.stack(logits)
+            print(f"forward case {case}: {len(logits)} steps")
+    np.savez_compressed(os.path.join(HERE, "forward_golden.npz"), **out)
+    print("wrote forward_golden.npz")
+
+
 def main():
+    if "--only-moe" in sys.argv:
+        po.build()
+        make_moe_golden()
+        make_forward_golden()
+        return
     if "--only-a8" in sys.argv:
         po.build()
         make_a8_golden()
@@ -414,7 +701,8 @@ def main():
     ref = po.ref_lib()
     if ref is None:
         raise SystemExit("oracle/_ref/libx100ref.so missing: the reference tree is needed")
-    meta = {"ref_root": REF_ROOT, "gemm_shapes": GEMM_SHAPES, "gemm_hash_shapes": GEMM_HASH_SHAPES}
+    meta = {"ref_root": os.path.relpath(REF_ROOT, REPO), "gemm_shapes": GEMM_SHAPES,
+            "gemm_hash_shapes": GEMM_HASH_SHAPES}
     gem = {}
     for (M, N, K) in GEMM_SHAPES + GEMM_HASH_SHAPES:
         seed = 1000003 * M + 1009 * N + K
@@ -463,6 +751,8 @@ def main():
     print("wrote gemm_golden.npz, quant_golden.npz, meta.json")
     make_gguf_golden()
     make_a8_golden()
+    make_moe_golden()
+    make_forward_golden()
 
 
 if __name__ == "__main__":

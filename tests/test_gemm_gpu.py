@@ -93,6 +93,26 @@ def test_i8_extreme_values_no_saturation():
     np.testing.assert_array_equal(C, np.broadcast_to(exp, (M, N)).astype(np.int32))
 
 
+def test_i8_8192_cubed_equals_reference_gemm_ref_i8():
+    """The benched configuration in full: M = N = K = 8192, operands uniform
+    in [-128, 127], C != 0 on entry, through the reference-signature host call
+    gemm_ime_i8, against the reference's own gemm_ref_i8 (src/gemm_ref.c
+    compiled unchanged) run row-sliced on every host thread.  Bit-exact."""
+    import os
+    M = N = K = 8192
+    A = po.rand_i8(81, M * K).reshape(M, K)
+    B = po.rand_i8(82, K * N).reshape(K, N)
+    C0 = (po.rand_i8(83, M * N).astype(np.int32) * 1000).reshape(M, N)
+    C = C0.copy()
+    x100b.gemm_host("gemm_ime_i8", A, B, C)
+    try:
+        nt = len(os.sched_getaffinity(0))
+    except AttributeError:
+        nt = os.cpu_count() or 1
+    ref = po.ref_gemm_i8_mt(A, B, C0, max(1, nt))
+    assert np.array_equal(C, ref), f"{int(np.count_nonzero(C != ref))} of {M * N} entries differ"
+
+
 def test_i8_device_path_large_properties():
     """4096^3 on the device: tensor-core result equals the CUDA-core exact
     kernel, and C accumulates (second call adds the same product again)."""

@@ -1,18 +1,23 @@
 """Pin the CPU oracle against fixtures produced by the reference's own code.
 
 The fixtures (tests/golden/*.npz, meta.json) were written by
-tests/golden/make_golden.py from the reference's src/gemm_ref.c and from its
-block decoders (qwen_moe.c:156-179, qwen_moe_q3k.c:541-577).  Every check
-here is bit-exact.
+tests/golden/make_golden.py from the reference's src/gemm_ref.c, its block
+decoders (qwen_moe.c:156-179, qwen_moe_q3k.c:541-577), its routing and
+layer-body functions (qwen_moe.c:187-189, 297-301; qwen_moe_q3k.c:1170-1175,
+1678) and its whole forward() (qwen_moe.c:272-315).  Every check here is
+bit-exact.
 """
 import hashlib
 import json
 import os
+import sys
 
 import numpy as np
 import pytest
 
 import py_oracle as po
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
 
 QT = {"Q4_0": po.Q4_0, "Q8_0": po.Q8_0, "Q3_K": po.Q3_K, "Q4_K": po.Q4_K}
 
@@ -214,3 +219,86 @@ def test_oracle_a8_gemv_q3k_is_the_packed_product():
                 w = deq[n, 256 * sb:256 * (sb + 1)]
                 ref[n] += sa[sb] * np.dot(w, qa[sb])                 # = sum d*sc*q_w * sa*q_a
         np.testing.assert_allclose(y[b], ref, rtol=1e-5, atol=1e-7)
+
+
+# ---- routing and decode-layer pins (moe_golden.npz, forward_golden.npz) ----------------
+# Outputs of the reference's own softmax, top-k lines, rmsnorm, rope /
+# rope_table / rope_apply, swiglu_exact and whole forward(), compiled from
+# its sources by tests/golden/make_golden.py.  The oracle must reproduce them
+# bit for bit (same fp32 operations in the same order, same libm).
+@pytest.fixture(scope="module")
+def moe_golden(golden_dir):
+    return np.load(os.path.join(golden_dir, "moe_golden.npz"))
+
+
+def test_softmax_equals_reference(moe_golden):
+    g = moe_golden
+    off = g["softmax_off"]
+    for a, b in zip(off[:-1], off[1:]):
+        x = np.ascontiguousarray(g["softmax_x"][a:b])
+        po.lib().orc_softmax(po._ptr(x), int(b - a))
+        np.testing.assert_array_equal(x, g["softmax_y"][a:b])
+
+
+def test_topk_equals_reference_lines(moe_golden):
+    """orc_softmax + orc_topk against qwen_moe.c:297-301 (softmax, greedy
+    top-k with strict > so the lowest index wins a tie, renormalisation),
+    including exact ties at the selection boundary and all-equal logits."""
+    g = moe_golden
+    lo = ko = 0
+    for ne, na in zip(g["topk_ne"], g["topk_na"]):
+        p = np.ascontiguousarray(g["topk_logits"][lo:lo + ne])
+        po.lib().orc_softmax(po._ptr(p), int(ne))
+        sel = np.zeros(na, np.int32)
+        w = np.zeros(na, np.float32)
+        po.lib().orc_topk(po._ptr(p), int(ne), int(na), po._ptr(sel), po._ptr(w))
+        np.testing.assert_array_equal(sel, g["topk_sel"][ko:ko + na])
+        np.testing.assert_array_equal(w, g["topk_w"][ko:ko + na])
+        lo += ne
+        ko += na
+    # the tie cases select the lowest indices among equals
+    assert list(g["topk_sel"][6 * 8:6 * 8 + 2]) == [3, 5]
+
+
+def test_rmsnorm_equals_reference(moe_golden):
+    g = moe_golden
+    off = g["rms_off"]
+    for a, b in zip(off[:-1], off[1:]):
+        o = np.zeros(b - a, np.float32)
+        x, w = np.ascontiguousarray(g["rms_x"][a:b]), np.ascontiguousarray(g["rms_w"][a:b])
+        po.lib().orc_rmsnorm(po._ptr(o), po._ptr(x), po._ptr(w), int(b - a), 1e-6)
+        np.testing.assert_array_equal(o, g["rms_y"][a:b])
+
+
+def test_rope_equals_reference_table_and_inline(moe_golden):
+    """orc_rope_neox = rope_table + rope_apply (qwen_moe_q3k.c:1170-1175) =
+    rope (qwen_moe.c:188), positions 0 .. 4095."""
+    g = moe_golden
+    o = 0
+    for hd, base, pos in g["rope_cfg"]:
+        hd, pos = int(hd), int(pos)
+        v = np.ascontiguousarray(g["rope_v"][o:o + hd])
+        po.lib().orc_rope_neox(po._ptr(v), hd, pos, float(base))
+        np.testing.assert_array_equal(v, g["rope_table_apply"][o:o + hd])
+        np.testing.assert_array_equal(v, g["rope_inline"][o:o + hd])
+        o += hd
+
+
+def test_swiglu_equals_reference(moe_golden):
+    g = moe_golden
+    y = np.array([po.lib().orc_silu(float(x)) for x in g["swiglu_g"]], np.float32) * g["swiglu_u"]
+    np.testing.assert_array_equal(y, g["swiglu_y"])
+
+
+@pytest.mark.parametrize("case", ["small", "c5"])
+def test_decode_chain_equals_reference_forward(golden_dir, case):
+    """The oracle's decode chain (orc_decode_layer with the reference's fp32
+    cache, then orc_decode_head) reproduces the logits of the reference's own
+    forward() (qwen_moe.c:272-315) step by step: "small" runs two layers for
+    eight steps from an empty cache, "c5" one layer of the decode
+    configuration's attention shape at positions 0, 1000 and 4095 of a
+    4096-position cache."""
+    import golden_inputs as gi
+    ref = np.load(os.path.join(golden_dir, "forward_golden.npz"))[f"{case}_logits"]
+    got = gi.oracle_logits(case)
+    np.testing.assert_array_equal(got, ref)

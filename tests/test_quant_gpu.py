@@ -179,6 +179,52 @@ def test_moe_c4_matches_oracle(c4_layer, batch):
         assert po.rel_l2(eout[b], ref[b]) <= REL_Q
 
 
+@pytest.fixture(scope="module")
+def c4_baseline_layer():
+    """BASELINE config 4 as stated: router N(0, 0.02) fp32, experts N(0, 0.02)
+    quantised by the Q4_K encoder, hn N(0, 1), batch 16.  Only the experts
+    some token selects can reach the output, so those are built by the rule
+    (quantising all 128 would take minutes of CPU); every other expert holds
+    random well-formed blocks, so reading a wrong expert shows up as
+    garbage."""
+    from concurrent.futures import ThreadPoolExecutor
+    d, E, k, ffn, B = 2048, 128, 8, 768, 16
+    rng = np.random.default_rng(4096)
+    router = rng.normal(0, 0.02, size=(E, d)).astype(np.float32)
+    hn = rng.normal(0, 1, size=(B, d)).astype(np.float32)
+    rsel, _ = po.route(router, hn, k)
+    used = sorted(set(rsel.reshape(-1).tolist()))
+    nb_d, nb_f = d // 256, ffn // 256
+    gate = wellformed_blocks(po.Q4_K, E * ffn * nb_d, 11).reshape(E, -1)
+    up = wellformed_blocks(po.Q4_K, E * ffn * nb_d, 12).reshape(E, -1)
+    down = wellformed_blocks(po.Q4_K, E * d * nb_f, 13).reshape(E, -1)
+
+    def build(e):
+        r = np.random.default_rng(1000 + e)
+        return (e, po.quantize(po.Q4_K, r.normal(0, 0.02, size=(ffn, d)).astype(np.float32)),
+                po.quantize(po.Q4_K, r.normal(0, 0.02, size=(ffn, d)).astype(np.float32)),
+                po.quantize(po.Q4_K, r.normal(0, 0.02, size=(d, ffn)).astype(np.float32)))
+    with ThreadPoolExecutor(8) as ex:
+        for e, g, u, dn in ex.map(build, used):
+            gate[e], up[e], down[e] = g, u, dn
+    return d, E, k, ffn, router, hn, [np.ascontiguousarray(x.reshape(-1)) for x in (gate, up, down)], used
+
+
+@pytest.mark.parametrize("batch", [1, 16])
+def test_moe_c4_baseline_weights(c4_baseline_layer, batch):
+    d, E, k, ffn, router, hn, (gate, up, down), used = c4_baseline_layer
+    assert len(used) > 50                       # a realistic expert union for 16 tokens
+    hb = hn[:batch]
+    ref, rsel, rw = po.moe_ffn(d, E, k, ffn, po.Q4_K, router, gate, up, down, hb, nthreads=8)
+    moe = x100b.Moe(d, E, k, ffn, x100b.Q4_K, router, gate, up, down)
+    eout, sel, w = moe.ffn_host(hb)
+    np.testing.assert_array_equal(sel, rsel)
+    np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-7)
+    for b in range(batch):
+        assert po.rel_l2(eout[b], ref[b]) <= REL_Q, (b, po.rel_l2(eout[b], ref[b]))
+    moe.close()
+
+
 @pytest.mark.parametrize("qt", [po.Q3_K, po.Q4_0, po.Q8_0])
 def test_moe_other_formats(qt):
     d, E, k, ffn = 1024, 32, 4, 512
@@ -189,6 +235,25 @@ def test_moe_other_formats(qt):
     eout, sel, _ = moe.ffn_host(hn)
     np.testing.assert_array_equal(sel, rsel)
     assert po.rel_l2(eout, ref) <= REL_Q
+
+
+@pytest.mark.parametrize("d", [160, 2080])
+@pytest.mark.parametrize("batch", [1, 3])
+def test_moe_ragged_hidden(d, batch):
+    """Hidden sizes that are not a multiple of 128 floats, with a 32-element
+    format: the router kernel streams each row's part past its registers'
+    share (d = 2080), or holds none of it in registers (d = 160).  Routing
+    and output against the oracle, batch 1 (fused kernel) and 3 (grouped)."""
+    qt, E, k, ffn = po.Q8_0, 32, 4, 96
+    router, gate, up, down = moe_weights(qt, d, E, ffn, 300 + d)
+    hn = np.random.default_rng(d + batch).normal(0, 1, size=(batch, d)).astype(np.float32)
+    ref, rsel, rw = po.moe_ffn(d, E, k, ffn, qt, router, gate, up, down, hn, nthreads=8)
+    moe = x100b.Moe(d, E, k, ffn, qt, router, gate, up, down)
+    eout, sel, w = moe.ffn_host(hn)
+    np.testing.assert_array_equal(sel, rsel)
+    np.testing.assert_allclose(w, rw, rtol=1e-5, atol=1e-7)
+    assert po.rel_l2(eout, ref) <= REL_Q
+    moe.close()
 
 
 def test_moe_expert_parallel_partials_sum(c4_layer):

@@ -54,10 +54,12 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float *__restric
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int e = blockIdx.x * nwarps + warp;
     // the router row (independent of the previous kernel) is loaded before
-    // waiting on it: up to 16 float4 per lane held in registers (d <= 2048),
-    // the rest of a longer row is streamed afterwards
+    // waiting on it: the first nv * 128 floats (at most 2048) held in
+    // registers, 16 bytes per lane per step; the rest of the row -- a longer
+    // row, or a d that is not a multiple of 128 -- is streamed afterwards,
+    // starting at float4 32 * nv
     constexpr int RV = 16;
-    const int nv = d / 128;
+    const int nv = min(d / 128, RV);
     const float4 *rw = reinterpret_cast<const float4 *>(router + (long)(e < n_exp ? e : 0) * d);
     float4 r[RV];
 #pragma unroll
@@ -81,7 +83,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float *__restric
                     s = fmaf(r[i].w, v.w, s);
                 }
             }
-            for (int i = lane + 32 * RV; i < d / 4; i += 32) {
+            for (int i = lane + 32 * nv; i < d / 4; i += 32) {
                 const float4 rr = __ldg(rw + i), v = __ldg(x + i);
                 s = fmaf(rr.x, v.x, s);
                 s = fmaf(rr.y, v.y, s);
@@ -213,7 +215,7 @@ __global__ void __launch_bounds__(64) router_logits_kernel(const float *__restri
 #pragma unroll
         for (int i = 0; i < RV; ++i)
             if (i < nv) q += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
-        for (int i = lane + 32 * RV; i < d / 4; i += 32) {   // hidden sizes above 2048
+        for (int i = lane + 32 * nv; i < d / 4; i += 32) {   // past the registers' share
             const float4 t = __ldcg(x + i);
             q += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
         }
@@ -237,7 +239,7 @@ __global__ void __launch_bounds__(64) router_logits_kernel(const float *__restri
         }
     }
     const bool write_hn = nw && hn_out && blockIdx.x == 0 && warp == 0;
-    for (int i = lane + 32 * RV; i < d / 4; i += 32) {
+    for (int i = lane + 32 * nv; i < d / 4; i += 32) {
         const float4 rr = __ldg(rw + i);
         float4 t = __ldcg(x + i);
         if (nw) {
@@ -1234,7 +1236,37 @@ namespace {
 constexpr int kNoAllocLogits = 2048;
 static __device__ __align__(256) unsigned char g_router_scratch[256 + kNoAllocLogits * 4];
 std::mutex g_noalloc_mu;
-void *g_noalloc_addr[64];   // device address of g_router_scratch, per device
+void *g_noalloc_addr[64];                  // device address of g_router_scratch, per device
+unsigned long long g_noalloc_ctx[64];      // unique id of the context that address belongs to
+
+// Unique id of the calling thread's current CUDA context (cuCtxGetId: ids are
+// never reused within a process), or 0 when there is none or the driver does
+// not offer the call.  A device reset destroys the primary context and the
+// module's static array moves with the new one, so the cached address is
+// trusted only while this id is unchanged.
+unsigned long long current_ctx_id() {
+    typedef CUresult (*PFN_getCurrent)(CUcontext *);
+    typedef CUresult (*PFN_getId)(CUcontext, unsigned long long *);
+    static PFN_getCurrent get_current = nullptr;
+    static PFN_getId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr, *q = nullptr;
+        cudaDriverEntryPointQueryResult r1, r2;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &r1) == cudaSuccess &&
+            cudaGetDriverEntryPoint("cuCtxGetId", &q, cudaEnableDefault, &r2) == cudaSuccess &&
+            r1 == cudaDriverEntryPointSuccess && r2 == cudaDriverEntryPointSuccess) {
+            get_current = reinterpret_cast<PFN_getCurrent>(p);
+            get_id = reinterpret_cast<PFN_getId>(q);
+        } else {
+            cudaGetLastError();
+        }
+    });
+    CUcontext cx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || get_current(&cx) != CUDA_SUCCESS || !cx || get_id(cx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
 }  // namespace
 
 extern "C" int x100q_router_topk_noalloc(const float *router, const float *hn, int d, int n_exp, int n_act,
@@ -1259,11 +1291,15 @@ extern "C" int x100q_router_topk_noalloc(const float *router, const float *hn, i
     void *base;
     {
         std::lock_guard<std::mutex> lk(g_noalloc_mu);
-        if (!g_noalloc_addr[dev]) {   // once per device, with that device current
+        // once per device, with that device current; again only if the device
+        // was reset since (a new context: the array lives at a new address)
+        const unsigned long long id = current_ctx_id();
+        if (!g_noalloc_addr[dev] || id != g_noalloc_ctx[dev]) {
             void *p = nullptr;
             const cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
             if (e != cudaSuccess || !p) return check_cuda(e != cudaSuccess ? e : cudaErrorUnknown, X100_E_LAUNCH);
             g_noalloc_addr[dev] = p;
+            g_noalloc_ctx[dev] = current_ctx_id();   // the lookup made the context current if it was not
         }
         base = g_noalloc_addr[dev];
     }
