@@ -618,7 +618,7 @@ def bench_moe(args, dist, peaks, peak_src):
     nb_d = ffn * d // 256
     layers = []
     host0 = None
-    LAYERS = 2
+    LAYERS = 8          # 8 copies x 340 MB of experts: no expert is re-read from L2 between its uses
     for li in range(LAYERS):
         # full-size tensors, only the local slice [lo, hi) is uploaded
         gate = np.zeros(E * nb_d * 144, np.uint8)
@@ -662,9 +662,22 @@ def bench_moe(args, dist, peaks, peak_src):
         ms, clocks = timed_graph(run, args.steps, args.warmup, dist, stream)
         calls = args.steps * PER
     tok_s = calls * B / (ms / 1e3)
-    alg_tok = 8 * 2654208 + 1048576 + 16384        # bytes per token (SURVEY config C4)
+    # Algorithmic bytes of one call: the experts its tokens select, each
+    # streamed once however many of the tokens share it (the measured union
+    # U, read back from the library's own routing of that call's tokens),
+    # plus the 1 MB fp32 router (read every call; with the expert stream in
+    # between it is not L2-resident) and the tokens' activations in and out.
+    EXPERT_BYTES, ROUTER_BYTES = 2654208, 4 * E * d
+    sel_t = torch.empty((B, k), dtype=torch.int32, device="cuda")
+    scratch_out = torch.empty((B, d), device="cuda")
+    unions = []
+    for j in range(PER):
+        layers[j % LAYERS].ffn_dev(hns[j % POOL], scratch_out, B, sel_t)
+        torch.cuda.synchronize()
+        unions.append(len(set(sel_t.cpu().numpy().reshape(-1).tolist())))
+    alg_call = [u * EXPERT_BYTES + ROUTER_BYTES + B * 2 * 4 * d for u in unions]
     per_call_us = ms * 1e3 / calls
-    achieved = alg_tok * B / (per_call_us / 1e6) / 1e9 / world   # per-GPU share
+    achieved = sum(alg_call) / PER / (per_call_us / 1e6) / 1e9 / world   # per-GPU share
     # parity of one step against the oracle on the same weights (1 GPU only)
     err = None
     if world == 1:
@@ -714,7 +727,8 @@ def bench_moe(args, dist, peaks, peak_src):
         "data": "synthetic: random well-formed Q4_K expert blocks, fp32 router N(0,0.02), hn ~ N(0,1)",
         "config": {"workload": f"MoE layer d={d} experts={E} top-{k} ffn={ffn} Q4_K, batch {B}",
                    "batch": B, "expert_parallel": f"{E // world} experts per GPU",
-                   "l2": f"{LAYERS} layer copies x {POOL} hn vectors rotated",
+                   "l2": f"{LAYERS} layer copies ({LAYERS * E * 2654208 / 2**30:.2f} GiB of experts) x "
+                         f"{PER} hn batches rotated",
                    "graph": f"{PER} MoE calls per CUDA graph" + ("" if world == 1 else
                                                                   f", each followed by the {args.combine} sum of eout")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -722,7 +736,11 @@ def bench_moe(args, dist, peaks, peak_src):
                      "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
                      "kernel": ("router_logits + moe_fused (2 launches per call)" if B == 1 else
                                 "router_logits + route_group + gate_up_pipe + down_pipe + combine (5 launches per call)"),
-                     "algorithmic_bytes_per_token": alg_tok, "call_us_mean": round(per_call_us, 3),
+                     "algorithmic_bytes_per_call": round(sum(alg_call) / PER),
+                     "expert_union_mean": round(sum(unions) / PER, 2),
+                     "bytes_rule": "U * 2654208 (distinct experts of the call's tokens) + 1048576 router + "
+                                   "B * 16384 activations",
+                     "call_us_mean": round(per_call_us, 3),
                      "parity": err},
         "clocks": clocks,
         "e2e": {"value": round(e2e_steps * B / dt, 1), "unit": "tokens/s",

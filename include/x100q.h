@@ -77,21 +77,29 @@ int x100q_lin_gemv_dev(const x100q_lin *lin, const float *x, float *y, int batch
 #define X100Q_GEMV_INDEPENDENT 1
 /* X100Q_GEMV_A8: the activations are first quantised as the reference packs
  * them for its IME kernels -- pack_A_i8 (qwen_moe_q3k.c:420-426, int8 per 32
- * values) for Q8_0 weights, pack_A_q3k (:613-623, int8 per 256) for Q3_K --
- * and the integer block dots are scaled by the packed scales, so the result
- * follows the reference's A8 numerics instead of the fp32-activation oracle
- * (a few 1e-3 relative apart).  Other weight types: X100_E_UNSUPPORTED.     */
+ * values) for Q8_0 weights, pack_A_q3k (:613-623, int8 per 256) for Q3_K,
+ * pack_A_hp (qwen_moe_hp.c:131-180, int8 per 32 under fp16 scales relative
+ * to a per-256 average) for Q4_0 (K % 256 == 0), the format of the int4
+ * "HP" engine -- and the integer block dots are scaled by the packed scales
+ * (HP: fp16 sub-scale x fp16 average), so the result follows the
+ * reference's A8 numerics instead of the fp32-activation oracle (a few 1e-3
+ * relative apart).  Other weight types: X100_E_UNSUPPORTED.                 */
 #define X100Q_GEMV_A8 2
 int x100q_lin_gemv_dev_flags(const x100q_lin *lin, const float *x, float *y, int batch,
                              int flags, void *stream);
-/* pack_act_i8 / pack_act_q3k (qwen_moe_q3k.c:887, :624) on the device: rows
- * x [batch][K] (fp32, device, 16-byte aligned) into the reference's packed
- * records, bit for bit: mode X100Q_PACK_I8 writes K/32 records of 38 bytes
- * (fp32 scale, int16 sum of q, int8 q[32]) per row, X100Q_PACK_Q3K K/256
- * records of 292 bytes (fp32 scale, int16 negated sums of 16, int8 q[256]);
- * rows follow each other in out.  Asynchronous on `stream`.                 */
+/* pack_act_i8 / pack_act_q3k / pack_act_hp (qwen_moe_q3k.c:887, :624;
+ * qwen_moe_hp.c:530) on the device: rows x [batch][K] (fp32, device, 16-byte
+ * aligned) into the reference's packed records, bit for bit: mode
+ * X100Q_PACK_I8 writes K/32 records of 38 bytes (fp32 scale, int16 sum of
+ * q, int8 q[32]) per row, X100Q_PACK_Q3K K/256 records of 292 bytes (fp32
+ * scale, int16 negated sums of 16, int8 q[256]), X100Q_PACK_HP K/256
+ * records of 290 bytes (8 x [fp16 sub-scale / average, int8 q[32]], 8 fp16
+ * -8 * sum(q), fp16 average scale; fp16 by the engine's truncating
+ * conversion, qwen_moe_hp.c:71-79); rows follow each other in out.
+ * Asynchronous on `stream`.                                                 */
 #define X100Q_PACK_I8  1
 #define X100Q_PACK_Q3K 2
+#define X100Q_PACK_HP  3
 int x100q_pack_act_dev(int mode, const float *x, int K, int batch, void *out, void *stream);
 
 /* ---- mixture-of-experts FFN ---------------------------------------------- */

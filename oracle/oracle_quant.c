@@ -395,18 +395,107 @@ void orc_pack_a_q3k(const float *x, int K, void *out)
     }
 }
 
+/* pack_A_hp (qwen_moe_hp.c:131-180), the activation packer of the engine's
+ * int4 "HP" kernels, in the scalar form the engine's RVV code was checked
+ * byte-identical against (bench/vendor_ime_actpack_probe.c:37-62), with the
+ * engine's own truncating f32_to_f16 (qwen_moe_hp.c:71-79).  290 bytes per
+ * 256 values: 8 x [fp16 sub-scale relative to the record's average scale,
+ * int8 q[32]], 8 fp16 values -8 * (sum of the sub-block's q), the fp16
+ * average scale.  Sub-block scale = max(|x|, 1e-6) / 127, average = their
+ * in-order sum / 8, q = lrint(x / sub-block scale) clamped to int8.         */
+void orc_pack_a_hp(const float *x, int K, void *out)
+{
+    uint8_t *o = (uint8_t *)out;
+    for (int sb = 0; sb < K / 256; sb++) {
+        const float *a = x + 256 * sb;
+        uint8_t *r = o + 290 * sb;
+        float st[8], avg = 0.0f;
+        for (int kk = 0; kk < 8; kk++) {
+            float amax = 1e-6f;
+            for (int i = 0; i < 32; i++) {
+                float v = fabsf(a[32 * kk + i]);
+                if (v > amax) amax = v;
+            }
+            st[kk] = amax / 127.0f;
+            avg += st[kk];
+        }
+        avg /= 8;
+        const float fac = avg != 0.0f ? 1.0f / avg : 0.0f;
+        for (int kk = 0; kk < 8; kk++) {
+            const float rep = st[kk] != 0.0f ? 1.0f / st[kk] : 0.0f;
+            int32_t sum = 0;
+            for (int i = 0; i < 32; i++) {
+                long q = lrintf(a[32 * kk + i] * rep);
+                q = q > 127 ? 127 : (q < -128 ? -128 : q);
+                r[34 * kk + 2 + i] = (uint8_t)(int8_t)q;
+                sum += (int32_t)q;
+            }
+            const uint16_t ss = orc_f32_to_f16_trunc(st[kk] * fac);
+            const uint16_t as = orc_f32_to_f16_trunc(-(float)(int16_t)sum * 8.0f);
+            memcpy(r + 34 * kk, &ss, 2);
+            memcpy(r + 272 + 2 * kk, &as, 2);
+        }
+        const uint16_t bs = orc_f32_to_f16_trunc(avg);
+        memcpy(r + 288, &bs, 2);
+    }
+}
+
+/* quantize_q4_0_native (qwen_moe_hp.c:102-109): the engine re-quantises its
+ * Q4_0 linears for the HP kernels with d = max(|w|, 1e-6) / 8 (stored by the
+ * truncating f32_to_f16), q = lrint(w / d) clamped to [-8, 7], nibble q + 8
+ * (element l < 16 low nibble of byte l, element l + 16 its high nibble): an
+ * ordinary GGUF Q4_0 block.  n % 32 == 0.                                   */
+void orc_quantize_q4_0_hp(const float *x, size_t n, void *blocks)
+{
+    uint8_t *o = (uint8_t *)blocks;
+    for (size_t b = 0; b < n / 32; b++) {
+        const float *w = x + 32 * b;
+        uint8_t *blk = o + 18 * b;
+        float amax = 1e-6f;
+        for (int i = 0; i < 32; i++) {
+            float v = fabsf(w[i]);
+            if (v > amax) amax = v;
+        }
+        const float d = amax / 8.0f, inv = d != 0.0f ? 1.0f / d : 0.0f;
+        int q[32];
+        for (int i = 0; i < 32; i++) {
+            long v = lrintf(w[i] * inv);
+            q[i] = (int)(v > 7 ? 7 : (v < -8 ? -8 : v));
+        }
+        const uint16_t dh = orc_f32_to_f16_trunc(d);
+        memcpy(blk, &dh, 2);
+        for (int l = 0; l < 16; l++) blk[2 + l] = (uint8_t)(((q[l] + 8) & 15) | (((q[l + 16] + 8) & 15) << 4));
+    }
+}
+
+/* Effective scale of sub-block kk of an HP record: fp16 sub-scale x fp16
+ * average scale, one fp32 product.                                          */
+static float hp_scale(const uint8_t *rec, int kk) { return rd_f16(rec + 34 * kk) * rd_f16(rec + 288); }
+
 void orc_qgemv_a8(int qtype, int N, int K, const void *blocks, const float *x, float *y, int batch)
 {
     const size_t rb = orc_row_bytes(qtype, K);
-    const int rec = qtype == ORC_Q8_0 ? 38 : 292, per = qtype == ORC_Q8_0 ? 32 : 256;
+    const int rec = qtype == ORC_Q8_0 ? 38 : (qtype == ORC_Q4_0 ? 290 : 292), per = qtype == ORC_Q8_0 ? 32 : 256;
     uint8_t *pa = (uint8_t *)malloc((size_t)(K / per) * rec);
     for (int b = 0; b < batch; b++) {
         if (qtype == ORC_Q8_0) orc_pack_a_i8(x + (size_t)b * K, K, pa);
+        else if (qtype == ORC_Q4_0) orc_pack_a_hp(x + (size_t)b * K, K, pa);
         else orc_pack_a_q3k(x + (size_t)b * K, K, pa);
         for (int n = 0; n < N; n++) {
             const uint8_t *w = (const uint8_t *)blocks + (size_t)n * rb;
             double acc = 0.0;
-            if (qtype == ORC_Q8_0) {
+            if (qtype == ORC_Q4_0) {
+                for (int kg = 0; kg < K / 32; kg++) {
+                    const uint8_t *blk = w + 18 * kg, *r = pa + 290 * (kg / 8);
+                    const int kk = kg % 8;
+                    int32_t dot = 0;
+                    for (int i = 0; i < 32; i++) {
+                        const int nib = i < 16 ? (blk[2 + i] & 15) : (blk[2 + i - 16] >> 4);
+                        dot += (nib - 8) * (int8_t)r[34 * kk + 2 + i];
+                    }
+                    acc += (double)(rd_f16(blk) * (hp_scale(r, kk) * (float)dot));
+                }
+            } else if (qtype == ORC_Q8_0) {
                 for (int kg = 0; kg < K / 32; kg++) {
                     const uint8_t *blk = w + 34 * kg, *r = pa + 38 * kg;
                     float sa;

@@ -89,6 +89,10 @@ def lib():
         L.orc_pack_a_i8.restype = None
         L.orc_pack_a_q3k.argtypes = [vp, i, vp]
         L.orc_pack_a_q3k.restype = None
+        L.orc_pack_a_hp.argtypes = [vp, i, vp]
+        L.orc_pack_a_hp.restype = None
+        L.orc_quantize_q4_0_hp.argtypes = [vp, C.c_size_t, vp]
+        L.orc_quantize_q4_0_hp.restype = None
         L.orc_qgemv_a8.argtypes = [i, i, i, vp, vp, vp, i]
         L.orc_qgemv_a8.restype = None
         L.orc_silu.argtypes = [C.c_float]
@@ -177,15 +181,27 @@ def quantize_q8_0_ref(x: np.ndarray) -> np.ndarray:
 
 # ---- the reference's activation packing ("A8") ----------------------------------
 def pack_a(mode: str, x: np.ndarray) -> np.ndarray:
-    """pack_A_i8 ('i8', 38 B per 32) or pack_A_q3k ('q3k', 292 B per 256) of
-    one fp32 row."""
+    """pack_A_i8 ('i8', 38 B per 32), pack_A_q3k ('q3k', 292 B per 256) or
+    pack_A_hp ('hp', 290 B per 256) of one fp32 row."""
     x = np.ascontiguousarray(x, np.float32).reshape(-1)
     if mode == "i8":
         out = np.empty(x.size // 32 * 38, np.uint8)
         lib().orc_pack_a_i8(_ptr(x), x.size, _ptr(out))
+    elif mode == "hp":
+        out = np.empty(x.size // 256 * 290, np.uint8)
+        lib().orc_pack_a_hp(_ptr(x), x.size, _ptr(out))
     else:
         out = np.empty(x.size // 256 * 292, np.uint8)
         lib().orc_pack_a_q3k(_ptr(x), x.size, _ptr(out))
+    return out
+
+
+def quantize_q4_0_hp(w: np.ndarray) -> np.ndarray:
+    """quantize_q4_0_native (qwen_moe_hp.c:102-109) of fp32 weights (rows of a
+    multiple of 32): GGUF Q4_0 blocks with d = max|w| / 8, q in [-8, 7]."""
+    w = np.ascontiguousarray(w, np.float32).reshape(-1)
+    out = np.empty(w.size // 32 * 18, np.uint8)
+    lib().orc_quantize_q4_0_hp(_ptr(w), w.size, _ptr(out))
     return out
 
 

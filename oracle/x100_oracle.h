@@ -61,9 +61,18 @@ void orc_quantize_q8_0_ref(const float *x, size_t n, void *blocks);
  * negated sums of 16, int8 q = roundf(x/scale) clamped.  K % 32 / K % 256.  */
 void orc_pack_a_i8(const float *x, int K, void *out);
 void orc_pack_a_q3k(const float *x, int K, void *out);
+/* pack_A_hp (qwen_moe_hp.c:131-180), 290 B per 256 values: 8 x [fp16
+ * sub-scale / average, int8 q[32]], 8 fp16 -8*sum(q), fp16 average scale;
+ * fp16 by the engine's truncating f32_to_f16 (qwen_moe_hp.c:71-79).  K%256. */
+void orc_pack_a_hp(const float *x, int K, void *out);
+/* quantize_q4_0_native (qwen_moe_hp.c:102-109): the HP kernels' Q4_0 weights
+ * (d = max(|w|,1e-6)/8 truncated to fp16, q in [-8, 7]); n % 32 == 0.       */
+void orc_quantize_q4_0_hp(const float *x, size_t n, void *blocks);
 /* y[b][n] = W[n] . (x[b] packed as above): Q8_0 weights with pack_A_i8,
- * Q3_K with pack_A_q3k; exact integer block dots, each block's (Q8_0) or
- * sub-block's (Q3_K) term scaled in fp32 and summed in double in k order.  */
+ * Q3_K with pack_A_q3k, Q4_0 with pack_A_hp; exact integer block dots, each
+ * block's (Q8_0, Q4_0) or sub-block's (Q3_K) term scaled in fp32 (Q4_0:
+ * d * ((fp16 sub-scale * fp16 average) * dot)) and summed in double in k
+ * order.                                                                     */
 void orc_qgemv_a8(int qtype, int N, int K, const void *blocks, const float *x, float *y, int batch);
 /* scale/min pair j of a K-quant 12-byte scale array (qwen_moe_q3k.c:534-538,
  * repack.cpp:222-233)                                                      */

@@ -32,10 +32,14 @@ What it pins, and from which reference code:
                     by tests/gguf_writer.py (make_parse_file below): model
                     dimensions, defaults, tokens, tensor infos, data start.
   a8_golden.npz     the reference's activation packers for its IME kernels,
-                    pack_A_i8 (qwen_moe_q3k.c:420-426) and pack_A_q3k
-                    (:613-623), compiled from the reference and run on fp32
-                    rows (normal values, rounding ties, zeros, tiny and large
-                    values).
+                    pack_A_i8 (qwen_moe_q3k.c:420-426), pack_A_q3k
+                    (:613-623) and pack_A_hp (qwen_moe_hp.c:131-180, in the
+                    scalar form of bench/vendor_ime_actpack_probe.c:37-62
+                    with the engine's truncating f32_to_f16,
+                    qwen_moe_hp.c:71-79), compiled from the reference and
+                    run on fp32 rows (normal values, rounding ties, zeros,
+                    tiny and large values); and the HP kernels' Q4_0 weight
+                    quantiser quantize_q4_0_native (qwen_moe_hp.c:102-109).
   meta.json         struct-size known answers (block_q3_K 110 B,
                     block_q5_K 176 B, bench/q3k_probe.c:410-413) and the
                     x100_caps_t layout of the reference header.
@@ -386,14 +390,28 @@ def make_gguf_golden() -> None:
 
 def make_a8_golden() -> None:
     q3k = open(os.path.join(REF_ROOT, "qwen_moe_q3k.c")).read()
+    hp = open(os.path.join(REF_ROOT, "qwen_moe_hp.c")).read()
+    probe = open(os.path.join(REF_ROOT, "bench", "vendor_ime_actpack_probe.c")).read()
     parts = [
         "#include <stdint.h>\n#include <string.h>\n#include <math.h>\n",
         extract_line(q3k, r"^#define AREC_Q3K 292$"),
         extract_function(q3k, r"static void pack_A_i8\(const float\*x, uint8_t\*out [^)]*\)\{"),
         extract_function(q3k, r"static void pack_A_q3k\(const float\*a,uint8_t\*out\)\{"),
+        # qwen_moe_hp.c: the engine's truncating f32_to_f16, the HP weight
+        # quantiser, and the scalar pack_A_hp its RVV packer was checked
+        # byte-identical against (kept in the probe); the engine pairs that
+        # packer with this f32_to_f16
+        extract_function(hp, r"static uint16_t f32_to_f16\(float f\)\{"),
+        extract_line(hp, r"^#define NSUB 8 .*$"),
+        extract_line(hp, r"^typedef struct \{ uint16_t d; uint8_t qs\[16\]; \} q4_0_native;$"),
+        extract_function(hp, r"static void quantize_q4_0_native\(const float\*w /\*32 elems\*/, q4_0_native\*out\)\{"),
+        extract_function(probe, r"static void pack_A_hp_scalar\(const float\*a, uint8_t\*out\)\{"),
         """
 void golden_pack_i8(const float*x,int K,uint8_t*out){ for(int kg=0;kg<K/32;kg++) pack_A_i8(x+32*kg,out+38*kg); }
 void golden_pack_q3k(const float*x,int K,uint8_t*out){ for(int sb=0;sb<K/256;sb++) pack_A_q3k(x+256*sb,out+AREC_Q3K*sb); }
+void golden_pack_hp(const float*x,int K,uint8_t*out){ for(int sb=0;sb<K/256;sb++) pack_A_hp_scalar(x+256*sb,out+290*sb); }
+void golden_q4_0_hp(const float*w,int n,uint8_t*out){ for(int b=0;b<n/32;b++) quantize_q4_0_native(w+32*b,(q4_0_native*)(out+18*b)); }
+int golden_sizeof_q4_0_native(void){ return (int)sizeof(q4_0_native); }
 """,
     ]
     with tempfile.TemporaryDirectory() as tmp:
@@ -406,6 +424,9 @@ void golden_pack_q3k(const float*x,int K,uint8_t*out){ for(int sb=0;sb<K/256;sb+
         L = C.CDLL(so)
         L.golden_pack_i8.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
         L.golden_pack_q3k.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        L.golden_pack_hp.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        L.golden_q4_0_hp.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        assert L.golden_sizeof_q4_0_native() == 18
         rng = np.random.default_rng(88)
         rows = [rng.standard_normal(2048), rng.standard_normal(2048) * 1e-4, np.zeros(512),
                 np.tile([0.5, -0.5, 1.5, -2.5, 127.0, -127.0, 63.5, 0.25], 64) * (127.0 / 127.0),
@@ -417,7 +438,17 @@ void golden_pack_q3k(const float*x,int K,uint8_t*out){ for(int sb=0;sb<K/256;sb+
         q3 = np.zeros(x.size // 256 * 292, np.uint8)
         L.golden_pack_i8(x.ctypes.data, x.size, i8.ctypes.data)
         L.golden_pack_q3k(x.ctypes.data, x.size, q3.ctypes.data)
-        np.savez_compressed(os.path.join(HERE, "a8_golden.npz"), x=x, pack_i8=i8, pack_q3k=q3)
+        hpk = np.zeros(x.size // 256 * 290, np.uint8)
+        L.golden_pack_hp(x.ctypes.data, x.size, hpk.ctypes.data)
+        # HP weight rows: N(0, 0.02) weights, zeros, values under the 1e-6
+        # floor, rounding ties at w / d = k + 0.5 and the clamp at -8 / +7
+        w_rows = [rng.normal(0, 0.02, 4096), np.zeros(64), np.full(32, 5e-7), rng.normal(0, 300.0, 256),
+                  np.r_[np.full(31, 0.25), 0.8] * np.tile([1, -1], 16), np.r_[np.full(31, -0.5), 1.0]]
+        w = np.concatenate([np.asarray(r, np.float32) for r in w_rows])
+        q4hp = np.zeros(w.size // 32 * 18, np.uint8)
+        L.golden_q4_0_hp(w.ctypes.data, w.size, q4hp.ctypes.data)
+        np.savez_compressed(os.path.join(HERE, "a8_golden.npz"), x=x, pack_i8=i8, pack_q3k=q3, pack_hp=hpk,
+                            w_hp=w, q4_0_hp=q4hp)
     print("wrote a8_golden.npz")
 
 

@@ -176,6 +176,39 @@ def test_oracle_a8_packers_equal_reference(golden_dir):
     np.testing.assert_array_equal(po.pack_a("q3k", g["x"]), g["pack_q3k"])
 
 
+def test_oracle_hp_packer_and_weight_quantiser_equal_reference(golden_dir):
+    """pack_A_hp and quantize_q4_0_native of the int4 HP engine
+    (qwen_moe_hp.c:102-109, 131-180, with its truncating f32_to_f16 :71-79)
+    restated in the oracle give the reference's bytes (a8_golden.npz)."""
+    g = np.load(os.path.join(golden_dir, "a8_golden.npz"))
+    np.testing.assert_array_equal(po.pack_a("hp", g["x"]), g["pack_hp"])
+    np.testing.assert_array_equal(po.quantize_q4_0_hp(g["w_hp"]), g["q4_0_hp"])
+
+
+def test_oracle_hp_gemv_is_the_packed_product():
+    """orc_qgemv_a8 for Q4_0 = sum over 32-blocks of d * (fp16 sub-scale *
+    fp16 average) * (integer dot of the packed activations with q = nibble -
+    8), against a numpy statement from the packed bytes."""
+    rng = np.random.default_rng(12)
+    N, K = 20, 768
+    W = po.quantize_q4_0_hp(rng.normal(0, 0.02, size=(N, K)).astype(np.float32))
+    x = rng.normal(0, 1, size=(2, K)).astype(np.float32)
+    y = po.qgemv_a8(po.Q4_0, W, N, K, x)
+    blk = W.reshape(N, K // 32, 18)
+    d = blk[:, :, 0:2].copy().view(np.float16)[:, :, 0].astype(np.float32)
+    qs = blk[:, :, 2:]
+    qw = np.concatenate([qs & 15, qs >> 4], axis=2).astype(np.int64) - 8        # [N][K/32][32]
+    for b in range(2):
+        rec = po.pack_a("hp", x[b]).reshape(-1, 290)
+        ss = np.stack([rec[:, 34 * k:34 * k + 2].copy().view(np.float16)[:, 0] for k in range(8)], 1)
+        avg = rec[:, 288:290].copy().view(np.float16)[:, 0]
+        eff = (ss.astype(np.float32) * avg.astype(np.float32)[:, None]).reshape(-1)   # per 32-block
+        qa = np.stack([rec[:, 34 * k + 2:34 * k + 34].view(np.int8) for k in range(8)], 1).reshape(-1, 32)
+        dots = np.einsum("nbk,bk->nb", qw, qa.astype(np.int64))
+        ref = (d * (eff[None, :] * dots.astype(np.float32))).astype(np.float64).sum(axis=1)
+        np.testing.assert_allclose(y[b], ref, rtol=1e-6, atol=1e-7)
+
+
 def test_oracle_a8_gemv_is_the_packed_product():
     """orc_qgemv_a8 = sum over blocks of d * scale * (integer dot of the packed
     values), checked against a numpy statement from the packed bytes."""

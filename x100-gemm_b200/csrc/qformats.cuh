@@ -22,6 +22,7 @@
 // from int32 dp4a sums (exact) and one fp32 scale per block or sub-block.
 #pragma once
 #include <cstdint>
+#include <cstring>
 #include <cuda_fp16.h>
 
 #include "ptx.cuh"
@@ -378,6 +379,96 @@ __device__ __forceinline__ void xprep_rows_q3k8(RowPtr row, int K, int nrows, co
     }
 }
 
+// fp32 -> fp16 bits by truncation, the conversion of the reference's int4
+// "HP" engine (qwen_moe_hp.c:71-79): mantissa bits below the fp16 precision
+// are dropped, subnormal results shifted out, overflow to infinity.
+__host__ __device__ __forceinline__ uint16_t f32_to_f16_trunc(float f) {
+#ifdef __CUDA_ARCH__
+    const uint32_t x = __float_as_uint(f);
+#else
+    uint32_t x;
+    memcpy(&x, &f, 4);
+#endif
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const int exp = (int)((x >> 23) & 0xffu) - 127 + 15;
+    uint32_t mant = x & 0x7fffffu;
+    if (exp <= 0) {
+        if (exp < -10) return (uint16_t)sign;
+        mant |= 0x800000u;
+        return (uint16_t)(sign | (mant >> (14 - exp)));
+    }
+    if (exp >= 31) return (uint16_t)(sign | 0x7c00u);
+    return (uint16_t)(sign | ((uint32_t)exp << 10) | (mant >> 13));
+}
+
+// The scales of one 256-element record of pack_A_hp (qwen_moe_hp.c:131-180)
+// for the calling lane, whose 8 elements e[] are elements 8 lane .. 8 lane+7
+// (sub-block lane / 4): every lane of the warp calls it together.
+// st = max(|x|, 1e-6) / 127 over the sub-block; avg = the in-order sum of the
+// 8 st / 8; ssub / blk = the truncated fp16 of st / avg and of avg; rep =
+// 1 / st; all divisions correctly rounded, as the reference's scalar C.
+struct HpScales { float st, rep; uint16_t ssub, blk; };
+__device__ __forceinline__ HpScales hp_scales(const float (&e)[8]) {
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(e[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, 1e-6f);
+    HpScales r;
+    r.st = __fdiv_rn(amax, 127.0f);
+    float avg = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) avg = __fadd_rn(avg, __shfl_sync(0xffffffffu, r.st, 4 * kk));
+    avg = __fdiv_rn(avg, 8.0f);
+    const float fac = avg != 0.f ? __fdiv_rn(1.0f, avg) : 0.f;
+    r.rep = r.st != 0.f ? __fdiv_rn(1.0f, r.st) : 0.f;
+    r.ssub = f32_to_f16_trunc(__fmul_rn(r.st, fac));
+    r.blk = f32_to_f16_trunc(avg);
+    return r;
+}
+// q = lrint(x * rep) clamped to int8 (round to nearest even)
+__device__ __forceinline__ int hp_quant(float x, float rep) {
+    return max(-128, min(127, __float2int_rn(__fmul_rn(x, rep))));
+}
+
+// pack_A_hp into XB blocks (the int4 "HP" engine's activations, used with
+// Q4_0 weights): one warp per 256-element record of a row, 8 elements per
+// lane.  Each 32-element block holds q and the effective scale the HP
+// numerics give it, fp16(sub-scale) * fp16(average) (one fp32 product).
+// K must be a multiple of 256.
+template <class RowPtr, class XBT>
+__device__ __forceinline__ void xprep_rows_hp8(RowPtr row, int K, int nrows, const XBT &xb) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int nsb = K / 256, total = nrows * nsb, u4 = lane & 3;
+    for (int u = warp; u < total; u += nwarps) {   // warp-uniform
+        const int c = nrows == 1 ? 0 : u / nsb, sb = u - c * nsb;
+        const float4 *a = reinterpret_cast<const float4 *>(row(c) + sb * 256 + lane * 8);
+        const float4 p0 = __ldcg(a), p1 = __ldcg(a + 1);
+        const float e[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const HpScales hs = hp_scales(e);
+        const float eff = __fmul_rn(__half2float(__ushort_as_half(hs.ssub)), __half2float(__ushort_as_half(hs.blk)));
+        uint32_t w0 = 0, w1 = 0;
+        int s8 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int q = hp_quant(e[k], hs.rep);
+            (k < 4 ? w0 : w1) |= (uint32_t)(q & 0xFF) << (8 * (k & 3));
+            s8 += q;
+        }
+        const int s16 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);   // lanes 4j, 4j+1: elements 0-15 of block j
+        const int s16b = __shfl_xor_sync(0xffffffffu, s16, 2);       // lanes 4j+2, 4j+3: elements 16-31
+        XB *o = xb.block(c, sb * 8 + (lane >> 2));
+        uint32_t *h = reinterpret_cast<uint32_t *>(&o->h0), *l = reinterpret_cast<uint32_t *>(&o->l0);
+        h[2 * u4] = w0;
+        h[2 * u4 + 1] = w1;
+        l[2 * u4] = 0u;
+        l[2 * u4 + 1] = 0u;
+        if (u4 == 0) o->f = make_float4(eff * (1.0f / 256.0f), eff * (float)(s16 + s16b), eff * (float)s16,
+                                        eff * (float)s16b);
+    }
+}
+
 // The whole CTA prepares `nrows` activation rows row(c)[0 .. K) into xb as
 // tokens 0 .. nrows-1 (blocks past K, up to the slice boundary, are zero).
 // A warp converts 4 blocks at a time; each pass first issues up to PF (kXPF
@@ -441,12 +532,13 @@ __device__ __forceinline__ void xprep_rows(RowPtr row, int K, int nrows, const X
 }
 
 // Activation preparation of a GEMV: a8 = 0 the exact 16-bit split
-// (xprep_rows), 1 pack_A_i8 per 32 values, 2 pack_A_q3k per 256 values (no
-// RMS-norm folding in the A8 forms).
+// (xprep_rows), 1 pack_A_i8 per 32 values, 2 pack_A_q3k per 256 values,
+// 3 pack_A_hp per 256 values (no RMS-norm folding in the A8 forms).
 template <class RowPtr, class XBT>
 __device__ __forceinline__ void xprep_gemv(int a8, RowPtr row, int K, int nrows, const XBT &xb, const float *nw,
                                            float *ss) {
-    if (a8 == 2) xprep_rows_q3k8(row, K, nrows, xb);
+    if (a8 == 3) xprep_rows_hp8(row, K, nrows, xb);
+    else if (a8 == 2) xprep_rows_q3k8(row, K, nrows, xb);
     else if (a8 == 1) xprep_rows<kXPF, true>(row, K, nrows, xb);
     else xprep_rows(row, K, nrows, xb, nw, ss);
 }

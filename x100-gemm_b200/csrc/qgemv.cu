@@ -230,6 +230,35 @@ __global__ void pack_q3k_kernel(const float *__restrict__ x, long nrec, uint8_t 
     }
 }
 
+// One warp per 256-value record of 290 bytes (pack_A_hp, qwen_moe_hp.c:131-180);
+// the arithmetic of xprep_rows_hp8.
+__global__ void pack_hp_kernel(const float *__restrict__ x, long nrec, uint8_t *__restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    for (long r = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; r < nrec;
+         r += ((long)gridDim.x * blockDim.x) >> 5) {
+        const float4 *a = reinterpret_cast<const float4 *>(x + 256 * r + 8 * lane);
+        const float4 p0 = a[0], p1 = a[1];
+        const float e[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const HpScales hs = hp_scales(e);
+        uint8_t *o = out + 290 * r;
+        const int kk = lane >> 2;
+        int s8 = 0;
+        for (int k = 0; k < 8; ++k) {
+            const int q = hp_quant(e[k], hs.rep);
+            o[34 * kk + 2 + 8 * (lane & 3) + k] = (uint8_t)(int8_t)q;
+            s8 += q;
+        }
+        int s32 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
+        s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
+        if ((lane & 3) == 0) {
+            const uint16_t as = f32_to_f16_trunc(__fmul_rn(-(float)(int16_t)s32, 8.0f));
+            st_bytes(o + 34 * kk, &hs.ssub, 2);
+            st_bytes(o + 272 + 2 * kk, &as, 2);
+        }
+        if (lane == 0) st_bytes(o + 288, &hs.blk, 2);
+    }
+}
+
 constexpr size_t kGemvSmemMax = 220 * 1024;
 
 static size_t gemv_smem(int qt, int K, int TR, int B) {
@@ -473,6 +502,7 @@ int x100q_lin_gemv_dev_flags(const x100q_lin *l, const float *x, float *y, int b
     if (flags & X100Q_GEMV_A8) {   // the reference's activation packing for the weight type
         if (l->m.qtype == Q8_0) o.a8 = 1;
         else if (l->m.qtype == Q3_K) o.a8 = 2;
+        else if (l->m.qtype == Q4_0 && l->m.K % 256 == 0) o.a8 = 3;
         else {
             set_error(X100_E_UNSUPPORTED);
             return X100_E_UNSUPPORTED;
@@ -486,7 +516,8 @@ int x100q_lin_gemv_dev_flags(const x100q_lin *l, const float *x, float *y, int b
 int x100q_pack_act_dev(int mode, const float *x, int K, int batch, void *out, void *stream) {
     set_error(X100_OK);
     const int per = mode == X100Q_PACK_I8 ? 32 : 256;
-    if ((mode != X100Q_PACK_I8 && mode != X100Q_PACK_Q3K) || !x || !out || K <= 0 || K % per || batch < 1 ||
+    if ((mode != X100Q_PACK_I8 && mode != X100Q_PACK_Q3K && mode != X100Q_PACK_HP) || !x || !out || K <= 0 ||
+        K % per || batch < 1 ||
         (reinterpret_cast<uintptr_t>(x) & 15)) {
         set_error(X100_E_ARG);
         return X100_E_ARG;
@@ -497,6 +528,7 @@ int x100q_pack_act_dev(int mode, const float *x, int K, int batch, void *out, vo
     const int grid = (int)std::min<long>((nrec + 7) / 8, (long)c->sm_count * 16);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (mode == X100Q_PACK_I8) pack_i8_kernel<<<grid, 256, 0, s>>>(x, nrec, static_cast<uint8_t *>(out));
+    else if (mode == X100Q_PACK_HP) pack_hp_kernel<<<grid, 256, 0, s>>>(x, nrec, static_cast<uint8_t *>(out));
     else pack_q3k_kernel<<<grid, 256, 0, s>>>(x, nrec, static_cast<uint8_t *>(out));
     const int st = check_cuda(cudaGetLastError(), X100_E_LAUNCH);
     if (st) set_error(st);

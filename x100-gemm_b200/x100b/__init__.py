@@ -440,12 +440,13 @@ def gguf_dequant_dev(gtype: int, data, n: int, out, stream=None) -> None:
     check(lib().x100q_gguf_dequant_dev(gtype, _p(data), n, _p(out), _stream(stream)), "x100q_gguf_dequant_dev")
 
 
-PACK_I8, PACK_Q3K = 1, 2
+PACK_I8, PACK_Q3K, PACK_HP = 1, 2, 3
 GEMV_INDEPENDENT, GEMV_A8 = 1, 2
 
 
 def pack_act_dev(mode: int, x, K: int, batch: int, out, stream=None) -> None:
-    """The reference's pack_act_i8 (mode PACK_I8) / pack_act_q3k (PACK_Q3K)."""
+    """The reference's pack_act_i8 (mode PACK_I8) / pack_act_q3k (PACK_Q3K) /
+    pack_act_hp (PACK_HP)."""
     check(lib().x100q_pack_act_dev(mode, _p(x), K, batch, _p(out), _stream(stream)), "x100q_pack_act_dev")
 
 
