@@ -741,11 +741,29 @@ float orc_silu(float x) { return x / (1.0f + expf(-x)); }
  * (swiglu mode 0) of qwen_moe_q3k.c:1925-1973.  Expert e's gate/up matrices
  * start at row e*ffn of gate_exps/up_exps, its down matrix at row e*d of
  * down_exps.  Only experts in [expert_lo, expert_hi) contribute to eout.    */
+static void moe_ffn_impl(int d, int n_exp, int n_act, int ffn, int qtype,
+                         const float *router, const void *gate_exps, const void *up_exps,
+                         const void *down_exps, int expert_lo, int expert_hi,
+                         const float *hn_all, float *eout_all, int batch, int *sel_out, float *w_out,
+                         float *probs_out, int nthreads);
+
 void orc_moe_ffn(int d, int n_exp, int n_act, int ffn, int qtype,
                  const float *router, const void *gate_exps, const void *up_exps,
                  const void *down_exps, int expert_lo, int expert_hi,
                  const float *hn_all, float *eout_all, int batch, int *sel_out, float *w_out,
                  int nthreads)
+{
+    moe_ffn_impl(d, n_exp, n_act, ffn, qtype, router, gate_exps, up_exps, down_exps, expert_lo, expert_hi,
+                 hn_all, eout_all, batch, sel_out, w_out, NULL, nthreads);
+}
+
+/* probs_out (may be NULL): the softmax probabilities [batch][n_exp] the
+ * top-k chose from (test diagnostics: how close a selection was to a tie). */
+static void moe_ffn_impl(int d, int n_exp, int n_act, int ffn, int qtype,
+                         const float *router, const void *gate_exps, const void *up_exps,
+                         const void *down_exps, int expert_lo, int expert_hi,
+                         const float *hn_all, float *eout_all, int batch, int *sel_out, float *w_out,
+                         float *probs_out, int nthreads)
 {
     size_t rb_d = orc_row_bytes(qtype, d), rb_f = orc_row_bytes(qtype, ffn);
     float *rl = (float *)malloc((size_t)n_exp * sizeof(float));
@@ -764,6 +782,7 @@ void orc_moe_ffn(int d, int n_exp, int n_act, int ffn, int qtype,
             rl[e] = s;
         }
         orc_softmax(rl, n_exp);
+        if (probs_out) memcpy(probs_out + (size_t)b * n_exp, rl, (size_t)n_exp * sizeof(float));
         orc_topk(rl, n_exp, n_act, sel, sw);
         if (sel_out) memcpy(sel_out + (size_t)b * n_act, sel, (size_t)n_act * sizeof(int));
         if (w_out) memcpy(w_out + (size_t)b * n_act, sw, (size_t)n_act * sizeof(float));
@@ -841,7 +860,7 @@ static void decode_layer_impl(int d, int nh, int nkv, int hd, int ctx, int pos, 
                               const float *ffn_norm, int n_exp, int n_act, int ffn, int expert_qtype,
                               const float *router, const void *gate_exps, const void *up_exps,
                               const void *down_exps, void *kc_, void *vc_, int kv_f32, float *h,
-                              int *sel_out, float *w_out, int nthreads)
+                              int *sel_out, float *w_out, float *probs_out, int nthreads)
 {
     const int qd = nh * hd, kvd = nkv * hd, gpr = nh / nkv;
     uint16_t *kc = (uint16_t *)kc_, *vc = (uint16_t *)vc_;
@@ -905,8 +924,8 @@ static void decode_layer_impl(int d, int nh, int nkv, int hd, int ctx, int pos, 
     for (int i = 0; i < d; i++) h[i] += tmp[i];
     /* :1916-1978 */
     orc_rmsnorm(hn, h, ffn_norm, d, eps);
-    orc_moe_ffn(d, n_exp, n_act, ffn, expert_qtype, router, gate_exps, up_exps, down_exps, 0, n_exp,
-                hn, tmp, 1, sel_out, w_out, nthreads);
+    moe_ffn_impl(d, n_exp, n_act, ffn, expert_qtype, router, gate_exps, up_exps, down_exps, 0, n_exp,
+                 hn, tmp, 1, sel_out, w_out, probs_out, nthreads);
     for (int i = 0; i < d; i++) h[i] += tmp[i];
     free(hn); free(q); free(k); free(v); free(att); free(sc); free(tmp); free(kf);
 }
@@ -921,7 +940,7 @@ void orc_decode_layer(int d, int nh, int nkv, int hd, int ctx, int pos, float ro
 {
     decode_layer_impl(d, nh, nkv, hd, ctx, pos, rope_base, eps, attn_qtype, attn_norm, wq, wk, wv, q_norm, k_norm,
                       wo, ffn_norm, n_exp, n_act, ffn, expert_qtype, router, gate_exps, up_exps, down_exps, kc, vc,
-                      0, h, sel_out, w_out, nthreads);
+                      0, h, sel_out, w_out, NULL, nthreads);
 }
 
 void orc_decode_layer_f32kv(int d, int nh, int nkv, int hd, int ctx, int pos, float rope_base, float eps,
@@ -934,7 +953,7 @@ void orc_decode_layer_f32kv(int d, int nh, int nkv, int hd, int ctx, int pos, fl
 {
     decode_layer_impl(d, nh, nkv, hd, ctx, pos, rope_base, eps, attn_qtype, attn_norm, wq, wk, wv, q_norm, k_norm,
                       wo, ffn_norm, n_exp, n_act, ffn, expert_qtype, router, gate_exps, up_exps, down_exps, kc, vc,
-                      1, h, sel_out, w_out, nthreads);
+                      1, h, sel_out, w_out, NULL, nthreads);
 }
 
 /* qwen_moe_q3k.c:1980-1981: logits = lm . rmsnorm(h, out_norm) */
@@ -945,4 +964,19 @@ void orc_decode_head(int d, int vocab, float eps, int lm_qtype, const float *out
     orc_rmsnorm(hn, h, out_norm, d, eps);
     orc_qgemv_mt(lm_qtype, vocab, d, lm, hn, logits, 1, nthreads);
     free(hn);
+}
+
+/* orc_decode_layer that also returns the router's softmax probabilities
+ * (n_exp floats): test diagnostics of how close the top-k came to a tie.    */
+void orc_decode_layer_probs(int d, int nh, int nkv, int hd, int ctx, int pos, float rope_base, float eps,
+                            int attn_qtype, const float *attn_norm, const void *wq, const void *wk,
+                            const void *wv, const float *q_norm, const float *k_norm, const void *wo,
+                            const float *ffn_norm, int n_exp, int n_act, int ffn, int expert_qtype,
+                            const float *router, const void *gate_exps, const void *up_exps,
+                            const void *down_exps, uint16_t *kc, uint16_t *vc, float *h,
+                            int *sel_out, float *w_out, float *probs_out, int nthreads)
+{
+    decode_layer_impl(d, nh, nkv, hd, ctx, pos, rope_base, eps, attn_qtype, attn_norm, wq, wk, wv, q_norm, k_norm,
+                      wo, ffn_norm, n_exp, n_act, ffn, expert_qtype, router, gate_exps, up_exps, down_exps, kc, vc,
+                      0, h, sel_out, w_out, probs_out, nthreads);
 }

@@ -66,6 +66,8 @@ def lib():
                                 [vp, vp, vp, vp, vp, i],
             "orc_decode_layer_f32kv": [i, i, i, i, i, i, f, f, i] + [vp] * 8 + [i, i, i, i] + [vp] * 4 +
                                       [vp, vp, vp, vp, vp, i],
+            "orc_decode_layer_probs": [i, i, i, i, i, i, f, f, i] + [vp] * 8 + [i, i, i, i] + [vp] * 4 +
+                                      [vp, vp, vp, vp, vp, vp, i],
             "orc_decode_head": [i, i, f, i, vp, vp, vp, vp, i],
             "orc_fill_u8": [C.c_uint64, vp, C.c_size_t],
             "orc_kq_scale_min": [i, vp, vp, vp],
@@ -312,7 +314,14 @@ def rel_l2(y, ref) -> float:
 
 
 # ---- decode step (qwen_moe_q3k.c:1842-1983) ------------------------------------------
-def decode_layer(cfg, lw, kc, vc, h, pos, nthreads=1):
+def top_margin(probs, k):
+    """Relative gap between the k-th and (k+1)-th largest routing
+    probabilities: how far the top-k was from a tie."""
+    srt = np.sort(np.asarray(probs, np.float64))[::-1]
+    return float((srt[k - 1] - srt[k]) / srt[k - 1])
+
+
+def decode_layer(cfg, lw, kc, vc, h, pos, nthreads=1, probs=None):
     """One layer of forward() for one token: cfg is a dict of the model shape
     (d, n_heads, n_kv_heads, head_dim, ctx, rope_base, eps, attn_qtype, n_exp,
     n_act, moe_ffn, expert_qtype); lw a dict of the layer's weights (numpy:
@@ -325,13 +334,17 @@ def decode_layer(cfg, lw, kc, vc, h, pos, nthreads=1):
     w = np.empty(cfg["n_act"], np.float32)
     c = lambda a: np.ascontiguousarray(a)
     ws = {k: c(v) for k, v in lw.items()}
-    lib().orc_decode_layer(cfg["d"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], cfg["ctx"], pos,
-                           cfg["rope_base"], cfg["eps"], cfg["attn_qtype"],
-                           *(_ptr(ws[k]) for k in ("attn_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo",
-                                                   "ffn_norm")),
-                           cfg["n_exp"], cfg["n_act"], cfg["moe_ffn"], cfg["expert_qtype"],
-                           *(_ptr(ws[k]) for k in ("router", "gate", "up", "down")),
-                           _ptr(kc), _ptr(vc), _ptr(h), _ptr(sel), _ptr(w), nthreads)
+    args = [cfg["d"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], cfg["ctx"], pos,
+            cfg["rope_base"], cfg["eps"], cfg["attn_qtype"],
+            *(_ptr(ws[k]) for k in ("attn_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo", "ffn_norm")),
+            cfg["n_exp"], cfg["n_act"], cfg["moe_ffn"], cfg["expert_qtype"],
+            *(_ptr(ws[k]) for k in ("router", "gate", "up", "down")),
+            _ptr(kc), _ptr(vc), _ptr(h), _ptr(sel), _ptr(w)]
+    if probs is None:
+        lib().orc_decode_layer(*args, nthreads)
+    else:
+        assert probs.dtype == np.float32 and probs.size >= cfg["n_exp"]
+        lib().orc_decode_layer_probs(*args, _ptr(probs), nthreads)
     return sel, w
 
 

@@ -121,6 +121,15 @@ void orc_decode_layer_f32kv(int d, int nh, int nkv, int hd, int ctx, int pos, fl
                             const float *router, const void *gate_exps, const void *up_exps,
                             const void *down_exps, float *kc, float *vc, float *h,
                             int *sel_out, float *w_out, int nthreads);
+/* orc_decode_layer that also writes the router's softmax probabilities
+ * (probs_out, n_exp floats): how close the top-k came to a tie.             */
+void orc_decode_layer_probs(int d, int nh, int nkv, int hd, int ctx, int pos, float rope_base, float eps,
+                            int attn_qtype, const float *attn_norm, const void *wq, const void *wk,
+                            const void *wv, const float *q_norm, const float *k_norm, const void *wo,
+                            const float *ffn_norm, int n_exp, int n_act, int ffn, int expert_qtype,
+                            const float *router, const void *gate_exps, const void *up_exps,
+                            const void *down_exps, uint16_t *kc, uint16_t *vc, float *h,
+                            int *sel_out, float *w_out, float *probs_out, int nthreads);
 /* logits = lm . rmsnorm(h, out_norm)  (qwen_moe_q3k.c:1980-1981)          */
 void orc_decode_head(int d, int vocab, float eps, int lm_qtype, const float *out_norm, const void *lm,
                      const float *h, float *logits, int nthreads);

@@ -33,6 +33,7 @@
 
 #include "../../include/x100q.h"
 #include "moe.h"
+#include "qgemm.h"
 #include "qgemv.h"
 #include "runtime.h"
 
@@ -456,6 +457,14 @@ struct x100q_model {
     void *moe_scratch = nullptr;
     MoeScratch S;
     int nsplit_max = 0;
+    // many-token prefill (chunks of up to pf_tmax tokens on the tensor-core
+    // GEMMs), allocated on first use
+    void *pf_base = nullptr;
+    int pf_tmax = 0;
+    float *pf_qkv = nullptr, *pf_att = nullptr;   // [tmax][qkv rows], [tmax][n_heads * hd]
+    __half *pf_xh = nullptr, *pf_xl = nullptr;    // [tmax][kp] fp16 planes of a linear's input
+    int pf_kp = 0;
+    MoeBigScratch pf_moe;
 };
 
 static bool cfg_ok(const x100q_model_cfg *c) {
@@ -549,6 +558,7 @@ void x100q_model_destroy(x100q_model *m) {
     cudaFree(m->vc);
     cudaFree(m->scratch);
     cudaFree(m->moe_scratch);
+    cudaFree(m->pf_base);
     delete m;
 }
 
@@ -778,6 +788,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
 
 static int forward_impl(x100q_model *m, const int *tokens, float *h, const int *pos, const int *slot, float *logits,
                         int batch, void *stream);
+static int prefill_tc(x100q_model *m, int slot, const int *tokens, int n, int pos0, float *logits);
 
 extern "C" {
 
@@ -869,6 +880,130 @@ static int forward_impl(x100q_model *m, const int *tokens, float *h, const int *
     return st;
 }
 
+// ---- many-token prefill on the tensor-core GEMMs -------------------------------------------
+constexpr int kPrefillChunk = 256;   // tokens per chunk of the tensor-core path
+
+static bool prefill_alloc(x100q_model *m) {
+    if (m->pf_base) return true;
+    const x100q_model_cfg &g = m->cfg;
+    const int T = kPrefillChunk;
+    const int kpd = slices_per_row(g.d) * 256, kpq = slices_per_row(g.n_heads * g.head_dim) * 256;
+    m->pf_kp = kpd > kpq ? kpd : kpq;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    const size_t qb = up((size_t)T * qkv_rows(g) * 4), ab = up((size_t)T * g.n_heads * g.head_dim * 4),
+                 xb = up((size_t)T * m->pf_kp * 2),
+                 mb = moe_big_scratch_bytes(g.d, g.n_exp, g.n_act, g.moe_ffn, T);
+    if (cudaMalloc(&m->pf_base, qb + ab + 2 * xb + mb + 256) != cudaSuccess) {
+        cudaGetLastError();
+        m->pf_base = nullptr;
+        set_error(X100_E_ALLOC);
+        return false;
+    }
+    uint8_t *p = static_cast<uint8_t *>(m->pf_base);
+    m->pf_qkv = reinterpret_cast<float *>(p);
+    m->pf_att = reinterpret_cast<float *>(p + qb);
+    m->pf_xh = reinterpret_cast<__half *>(p + qb + ab);
+    m->pf_xl = reinterpret_cast<__half *>(p + qb + ab + xb);
+    m->pf_moe = moe_big_scratch_carve(p + qb + ab + 2 * xb, g.d, g.n_exp, g.n_act, g.moe_ffn, T);
+    m->pf_tmax = T;
+    return true;
+}
+
+// One dense linear of a chunk: y (=, or += with add) W . x for T token rows
+// of x [T][K] (fp32, row pitch K), through the fp16 planes of x.
+static int prefill_linear(x100q_model *m, DevCtx *c, const QMat &W, const float *x, int K, int T,
+                          const float *norm_w, float *y, long ldy, bool add, cudaStream_t s) {
+    const int kp = W.ns * 256;
+    int st = launch_split_rows(x, K, K, kp, T, norm_w, m->cfg.eps, m->pf_xh, m->pf_xl, nullptr, s);
+    if (st) return st;
+    QgLaunch L;
+    L.mats[0] = &W;
+    L.n_rows = W.N;
+    L.T = T;
+    L.xh = m->pf_xh;
+    L.xl = m->pf_xl;
+    L.x_rows = T;
+    L.mode = add ? QG_ADD : QG_STORE;
+    L.out = y;
+    L.ldo = ldy;
+    return launch_qgemm(c, L, s);
+}
+
+// forward() over T consecutive tokens of one sequence (the reference's
+// prefill, qwen_moe_hp.c:1748-1858): per layer the q/k/v, Wo and expert
+// linears run as tensor-core GEMMs over all T tokens (each weight row
+// streamed once per 128 tokens), every token's k and v go to the cache
+// before any token attends, and the attention runs per token over its
+// positions 0 .. pos (causal) in groups of max_batch tokens.
+static int prefill_chunk_tc(x100q_model *m, DevCtx *c, const int *tok, float *h, const int *pos, const int *slot,
+                            float *logits, int T, cudaStream_t s) {
+    const x100q_model_cfg &g = m->cfg;
+    static bool attr[64];
+    if (!attr[c->device]) {
+        set_qkernel_attrs(embed_kernel);
+        set_qkernel_attrs(attn_decode_kernel);
+        set_qkernel_attrs(attn_merge_kernel);
+        attr[c->device] = true;
+    }
+    const int qd = g.n_heads * g.head_dim, qn = qkv_rows(g);
+    int st = launch_k(embed_kernel, dim3(2, T), dim3(256), 0, s, false, (const float *)m->tok_embd, g.vocab, g.d,
+                      tok, h, c->d_status);
+    for (int l = 0; st == X100_OK && l < g.n_layers; ++l) {
+        ModelLayer &L = m->layers[l];
+        // 1. qkv = Wqkv . rmsnorm(h, attn_norm)
+        st = prefill_linear(m, c, L.qkv, h, g.d, T, L.norms, m->pf_qkv, qn, false, s);
+        if (st) break;
+        // 2. every token's k, v into the cache, then attention per token
+        AttnArgs a;
+        a.qkv = m->pf_qkv;
+        a.qkv_n = qn;
+        a.q_norm = L.norms + 2 * g.d;
+        a.k_norm = L.norms + 2 * g.d + g.head_dim;
+        a.pos = pos;
+        a.nh = g.n_heads;
+        a.nkv = g.n_kv_heads;
+        a.ctx = g.ctx;
+        a.chunk = kChunk;
+        a.nsplit = (g.ctx + kChunk - 1) / kChunk;
+        a.eps = g.eps;
+        a.rope_base = g.rope_base;
+        a.scale = 1.0f / sqrtf((float)g.head_dim);
+        a.kc = m->kc + (size_t)l * m->layer_kv;
+        a.vc = m->vc + (size_t)l * m->layer_kv;
+        a.row_base = (long)l * g.max_batch * g.n_kv_heads * g.ctx;
+        a.part = m->part;
+        a.kv_early = 0;
+        a.slot = slot;
+        a.nslots = g.max_batch;
+        a.prewritten = 1;
+        a.att = m->pf_att;
+        a.status = c->d_status;
+        st = launch_pdl(kv_write_kernel, dim3(g.n_kv_heads, T), dim3(32), 0, s, a);
+        for (int g0 = 0; st == X100_OK && g0 < T; g0 += g.max_batch) {
+            const int gb = T - g0 < g.max_batch ? T - g0 : g.max_batch;
+            AttnArgs ag = a;
+            ag.qkv = m->pf_qkv + (size_t)g0 * qn;
+            ag.pos = pos + g0;
+            ag.slot = slot + g0;
+            ag.att = m->pf_att + (size_t)g0 * qd;
+            st = launch_pdl(attn_decode_kernel, dim3(ag.nsplit, g.n_kv_heads, gb), dim3(kAttnThreads), attn_smem(), s,
+                            m->tmK, m->tmV, ag);
+            if (!st && ag.nsplit > 1)
+                st = launch_pdl(attn_merge_kernel, dim3(g.n_heads, gb), dim3(128), merge_smem(ag.nsplit), s,
+                                (const float *)m->part, g.n_heads, ag.nsplit, ag.att);
+        }
+        if (st) break;
+        // 3. h += Wo . att
+        st = prefill_linear(m, c, L.o, m->pf_att, qd, T, nullptr, h, g.d, true, s);
+        if (st) break;
+        // 4. h += MoE(rmsnorm(h, ffn_norm))
+        st = launch_moe_prefill(c, L.moe, m->pf_moe, h, T, L.norms + g.d, g.eps, s);
+    }
+    // logits = Wlm . rmsnorm(h, out_norm)
+    if (st == X100_OK && logits) st = prefill_linear(m, c, m->lm, h, g.d, T, m->out_norm, logits, g.vocab, false, s);
+    return st;
+}
+
 extern "C" {
 
 int x100q_model_forward(x100q_model *m, const int *tokens, const int *pos, float *logits, int batch) {
@@ -902,11 +1037,12 @@ int x100q_model_forward(x100q_model *m, const int *tokens, const int *pos, float
 
 int x100q_model_prefill(x100q_model *m, int slot, const int *tokens, int n, int pos0, float *logits) {
     set_error(X100_OK);
-    if (!m || !tokens || n < 1 || n > m->cfg.max_batch || slot < 0 || slot >= m->cfg.max_batch || pos0 < 0 ||
-        pos0 + n > m->cfg.ctx || !m->tok_embd || (logits && (!m->out_norm || !m->lm.w))) {
+    if (!m || !tokens || n < 1 || slot < 0 || slot >= m->cfg.max_batch || pos0 < 0 || pos0 + n > m->cfg.ctx ||
+        !m->tok_embd || (logits && (!m->out_norm || !m->lm.w))) {
         set_error(X100_E_ARG);
         return X100_E_ARG;
     }
+    if (n > m->cfg.max_batch) return prefill_tc(m, slot, tokens, n, pos0, logits);
     DeviceGuard dg(m->device);
     DevCtx *c = ctx();
     if (!c) return get_error();
@@ -936,3 +1072,46 @@ int x100q_model_prefill(x100q_model *m, int slot, const int *tokens, int n, int 
 }
 
 }  // extern "C"
+
+// x100q_model_prefill for n > max_batch: chunks of up to kPrefillChunk tokens,
+// each through prefill_chunk_tc, in order (a chunk attends over the cache the
+// earlier chunks wrote).  Synchronous; host or device tokens / logits.
+static int prefill_tc(x100q_model *m, int slot, const int *tokens, int n, int pos0, float *logits) {
+    for (int l = 0; l < m->cfg.n_layers; ++l)
+        if (!m->layers[l].set || m->cfg.expert_lo != 0 || m->cfg.expert_hi != m->cfg.n_exp) {
+            set_error(X100_E_ARG);
+            return X100_E_ARG;
+        }
+    DeviceGuard dg(m->device);
+    DevCtx *c = ctx();
+    if (!c) return get_error();
+    std::lock_guard<std::mutex> lk(c->mu);
+    if (!prefill_alloc(m)) return get_error();
+    const x100q_model_cfg &g = m->cfg;
+    const int T = m->pf_tmax;
+    const size_t tb = 4 * (size_t)T, hb = (size_t)T * g.d * 4, lb = (size_t)T * g.vocab * 4;
+    uint8_t *buf = static_cast<uint8_t *>(stage_buf(c, 0, 3 * tb + hb + 1024));
+    if (!buf) return get_error();
+    int *dtok = reinterpret_cast<int *>(buf), *dpos = reinterpret_cast<int *>(buf + tb),
+        *dslot = reinterpret_cast<int *>(buf + 2 * tb);
+    float *dh = reinterpret_cast<float *>(buf + ((3 * tb + 255) & ~size_t(255)));
+    float *dl = nullptr;
+    if (logits && !(dl = static_cast<float *>(stage_buf(c, 1, lb)))) return get_error();
+    std::vector<int> hp(T), hs(T, slot);
+    int st = X100_OK;
+    for (int c0 = 0; st == X100_OK && c0 < n; c0 += T) {
+        const int cn = n - c0 < T ? n - c0 : T;
+        for (int i = 0; i < cn; ++i) hp[i] = pos0 + c0 + i;
+        st = check_cuda(cudaMemcpyAsync(dtok, tokens + c0, cn * 4, cudaMemcpyDefault, c->stream), X100_E_COPY);
+        if (!st) st = check_cuda(cudaMemcpyAsync(dpos, hp.data(), cn * 4, cudaMemcpyHostToDevice, c->stream), X100_E_COPY);
+        if (!st) st = check_cuda(cudaMemcpyAsync(dslot, hs.data(), cn * 4, cudaMemcpyHostToDevice, c->stream), X100_E_COPY);
+        if (!st) st = prefill_chunk_tc(m, c, dtok, dh, dpos, dslot, dl, cn, c->stream);
+        if (!st && logits)
+            st = check_cuda(cudaMemcpyAsync(logits + (size_t)c0 * g.vocab, dl, (size_t)cn * g.vocab * 4, cudaMemcpyDefault,
+                                            c->stream), X100_E_COPY);
+        const int st2 = sync_and_status(c, c->stream);   // the host vectors are reused by the next chunk
+        if (st == X100_OK) st = st2;
+    }
+    if (st) set_error(st);
+    return st;
+}

@@ -34,6 +34,7 @@
 #include "../../include/x100q.h"
 #include "moe.h"
 #include "qgemv.h"
+#include "qgemm.h"
 
 namespace x100 {
 namespace q {
@@ -697,6 +698,86 @@ __global__ void __launch_bounds__(256) combine_kernel(int d, int n_act, int lo, 
     *o = accum ? *o + tot : tot;
 }
 
+// ---- many-token (prefill) path: pairs sorted by expert ------------------------------------
+// route_count: one CTA per token routes it (route_fast: softmax, greedy top-k,
+// renormalise), writes sel / w, and counts its pairs per local expert.
+__global__ void __launch_bounds__(128) route_count_kernel(int n_exp, int n_act, int lo, int hi,
+                                                          const float *__restrict__ logits, int *__restrict__ sel,
+                                                          float *__restrict__ wsel, int *__restrict__ cnt) {
+    __shared__ __align__(16) float s_p[kMaxExp + 16];
+    __shared__ int s_rk[4 * kMaxExp];
+    __shared__ int s_sel[kMaxAct];
+    __shared__ float s_w[kMaxAct], s_wr[kMaxAct];
+    const int tok = blockIdx.x;
+    pdl_wait();                                   // logits and the cleared counters come from the router kernel
+    pdl_launch_dependents();
+    route_fast(logits + (long)tok * n_exp, n_exp, n_act, s_p, s_rk, s_sel, s_w, s_wr);
+    if (threadIdx.x < n_act) {
+        const int a = threadIdx.x, e = s_sel[a];
+        sel[tok * n_act + a] = e;
+        wsel[tok * n_act + a] = s_w[a];
+        if (e >= lo && e < hi) atomicAdd(&cnt[e - lo], 1);
+    }
+}
+
+// scatter: one CTA per token places each of its local pairs at the next free
+// position of its expert's run (runs in expert order: start = exclusive
+// prefix of the counts) and copies the token's activation planes there.  The
+// order of pairs inside a run does not change any result: every pair is its
+// own GEMM column.
+__global__ void __launch_bounds__(256) pair_scatter_kernel(int n_act, int lo, int hi, int kp,
+                                                           const int *__restrict__ sel, int *__restrict__ cnt,
+                                                           int *__restrict__ pair_at, const __half *__restrict__ xt_hi,
+                                                           const __half *__restrict__ xt_lo, __half *__restrict__ xg_hi,
+                                                           __half *__restrict__ xg_lo) {
+    __shared__ int s_start[kMaxExp + 1];
+    __shared__ int s_pos[kMaxAct];
+    const int tok = blockIdx.x, nl = hi - lo;
+    pdl_wait();                                   // counts complete: the routing kernel has finished
+    pdl_launch_dependents();
+    if (threadIdx.x < 32) {                       // exclusive prefix of the counts, one warp
+        const int per = (nl + 31) / 32, lane = threadIdx.x;
+        int sum = 0;
+        for (int k = 0; k < per; ++k) {
+            const int g = lane * per + k;
+            if (g < nl) sum += __ldcg(cnt + g);
+        }
+        int inc = sum;
+        for (int off = 1; off < 32; off <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, inc, off);
+            if (lane >= off) inc += v;
+        }
+        int run = inc - sum;
+        for (int k = 0; k < per; ++k) {
+            const int g = lane * per + k;
+            if (g < nl) {
+                s_start[g] = run;
+                run += __ldcg(cnt + g);
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < n_act) {
+        const int a = threadIdx.x, e = __ldcg(sel + tok * n_act + a);
+        int pos = -1;
+        if (e >= lo && e < hi) {
+            pos = s_start[e - lo] + atomicAdd(&cnt[nl + e - lo], 1);
+            pair_at[pos] = tok * n_act + a;
+        }
+        s_pos[a] = pos;
+    }
+    __syncthreads();
+    const int nv = kp / 8;                        // 16-byte vectors per plane row
+    for (int a = 0; a < n_act; ++a) {
+        const int pos = s_pos[a];
+        if (pos < 0) continue;
+        for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+            reinterpret_cast<uint4 *>(xg_hi + (long)pos * kp)[v] = __ldcg(reinterpret_cast<const uint4 *>(xt_hi + (long)tok * kp) + v);
+            reinterpret_cast<uint4 *>(xg_lo + (long)pos * kp)[v] = __ldcg(reinterpret_cast<const uint4 *>(xt_lo + (long)tok * kp) + v);
+        }
+    }
+}
+
 // ---- fused expert kernel (one token) ----------------------------------------------------
 // One CTA per SM.  After routing (route_fast on the router kernel's logits)
 // every CTA stages, at once, all the weight rows it owns: gate/up items (kFR
@@ -1036,6 +1117,114 @@ int launch_moe_ex(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float
 }
 
 void moe_fused_plan(MoeLayer &L, int sm_count) { fused_plan_impl(L, sm_count); }
+
+size_t moe_big_scratch_bytes(int d, int n_exp, int n_act, int ffn, int tmax) {
+    const size_t kpd = (size_t)slices_per_row(d) * 256, kpf = (size_t)slices_per_row(ffn) * 256;
+    const size_t P = (size_t)tmax * n_act;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    return up((size_t)tmax * d * 4) + 2 * up((size_t)tmax * kpd * 2) + up((size_t)tmax * n_exp * 4) +
+           2 * up(P * 4) + up((size_t)2 * n_exp * 4) + up(P * 4) + 2 * up(P * kpd * 2) + up(P * 2 * ffn * 4) +
+           2 * up(P * kpf * 2) + up(P * d * 4) + 256;
+}
+
+MoeBigScratch moe_big_scratch_carve(void *base, int d, int n_exp, int n_act, int ffn, int tmax) {
+    const size_t kpd = (size_t)slices_per_row(d) * 256, kpf = (size_t)slices_per_row(ffn) * 256;
+    const size_t P = (size_t)tmax * n_act;
+    uintptr_t p = (reinterpret_cast<uintptr_t>(base) + 255) & ~uintptr_t(255);
+    auto take = [&](size_t bytes) {
+        void *r = reinterpret_cast<void *>(p);
+        p = (p + bytes + 255) & ~uintptr_t(255);
+        return r;
+    };
+    MoeBigScratch S;
+    S.tmax = tmax;
+    S.hn = static_cast<float *>(take((size_t)tmax * d * 4));
+    S.xt_hi = static_cast<__half *>(take((size_t)tmax * kpd * 2));
+    S.xt_lo = static_cast<__half *>(take((size_t)tmax * kpd * 2));
+    S.logits = static_cast<float *>(take((size_t)tmax * n_exp * 4));
+    S.sel = static_cast<int *>(take(P * 4));
+    S.w = static_cast<float *>(take(P * 4));
+    S.cnt = static_cast<int *>(take((size_t)2 * n_exp * 4));
+    S.pair_at = static_cast<int *>(take(P * 4));
+    S.xg_hi = static_cast<__half *>(take(P * kpd * 2));
+    S.xg_lo = static_cast<__half *>(take(P * kpd * 2));
+    S.gu = static_cast<float *>(take(P * 2 * ffn * 4));
+    S.hh_hi = static_cast<__half *>(take(P * kpf * 2));
+    S.hh_lo = static_cast<__half *>(take(P * kpf * 2));
+    S.part = static_cast<float *>(take(P * d * 4));
+    return S;
+}
+
+int launch_moe_prefill(DevCtx *c, const MoeLayer &L, const MoeBigScratch &S, float *h, int T, const float *norm_w,
+                       float eps, cudaStream_t s) {
+    const int nl = L.hi - L.lo;
+    if (T < 1 || T > S.tmax || nl > kMaxExp || !norm_w) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    if (fault_injected("launch")) return X100_E_INJECTED;
+    static bool attr[64];
+    if (!attr[c->device]) {
+        set_qkernel_attrs(router_logits_kernel);
+        attr[c->device] = true;
+    }
+    const int kpd = slices_per_row(L.d) * 256, kpf = slices_per_row(L.ffn) * 256;
+    const int P = T * L.n_act;
+    // 1. router logits of the normed tokens (qwen_moe.c:296), hn written for
+    //    the experts, the counters cleared
+    int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2, T), dim3(64), 0, s, (const float *)L.router,
+                        (const float *)h, L.d, L.n_exp, T, S.logits, S.cnt, 2 * nl, norm_w, eps, S.hn);
+    if (st) return st;
+    // 2. the normed tokens as fp16 hi / lo planes
+    st = launch_split_rows(S.hn, L.d, L.d, kpd, T, nullptr, 0.f, S.xt_hi, S.xt_lo, nullptr, s);
+    if (st) return st;
+    // 3. softmax, top-k, renormalise (qwen_moe.c:297-301); pairs per expert
+    st = launch_pdl(route_count_kernel, dim3(T), dim3(128), 0, s, L.n_exp, L.n_act, L.lo, L.hi,
+                    (const float *)S.logits, S.sel, S.w, S.cnt);
+    if (st) return st;
+    // 4. pairs sorted by expert, each with its token's planes
+    st = launch_pdl(pair_scatter_kernel, dim3(T), dim3(256), 0, s, L.n_act, L.lo, L.hi, kpd, (const int *)S.sel,
+                    S.cnt, S.pair_at, (const __half *)S.xt_hi, (const __half *)S.xt_lo, S.xg_hi, S.xg_lo);
+    if (st) return st;
+    // 5. gate and up of every pair's expert: gu[pos] = [gate . hn, up . hn]
+    QgLaunch g;
+    g.mats[0] = &L.gate;
+    g.mats[1] = &L.up;
+    g.nmat = 2;
+    g.n_rows = L.ffn;
+    g.ngroups = nl;
+    g.cnt = S.cnt;
+    g.xh = S.xg_hi;
+    g.xl = S.xg_lo;
+    g.x_rows = P;
+    g.mode = QG_STORE;
+    g.out = S.gu;
+    g.ldo = 2L * L.ffn;
+    st = launch_qgemm(c, g, s);
+    if (st) return st;
+    // 6. h = silu(g) * u (qwen_moe.c:309)
+    st = launch_swiglu_split(S.gu, L.ffn, kpf, P, S.hh_hi, S.hh_lo, s);
+    if (st) return st;
+    // 7. down of every pair's expert, to the pair's row
+    QgLaunch dn;
+    dn.mats[0] = &L.down;
+    dn.nmat = 1;
+    dn.n_rows = L.d;
+    dn.ngroups = nl;
+    dn.cnt = S.cnt;
+    dn.xh = S.hh_hi;
+    dn.xl = S.hh_lo;
+    dn.x_rows = P;
+    dn.mode = QG_SCATTER;
+    dn.out = S.part;
+    dn.ldo = L.d;
+    dn.pair_at = S.pair_at;
+    st = launch_qgemm(c, dn, s);
+    if (st) return st;
+    // 8. h += sum over the token's local slots, in slot order, of w * part (qwen_moe.c:310)
+    return launch_pdl(combine_kernel, dim3((L.d + 255) / 256, T), dim3(256), 0, s, L.d, L.n_act, L.lo, L.hi,
+                      (const int *)S.sel, (const float *)S.w, (const float *)S.part, h, 1);
+}
 
 bool moe_layer_upload(DevCtx *c, MoeLayer &L, int d, int n_exp, int n_act, int ffn, int qtype, const float *router,
                       const void *gate_exps, const void *up_exps, const void *down_exps, int lo, int hi) {

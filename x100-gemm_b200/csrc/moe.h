@@ -1,5 +1,6 @@
 // moe.h -- resident mixture-of-experts layer and its launcher (moe.cu).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "qgemv.h"
@@ -59,6 +60,33 @@ struct MoeOpts {
     float *hn_out = nullptr;
     bool accum = false;
 };
+// Scratch of the many-token (prefill) MoE path for up to `tmax` tokens:
+// routing, the (token, slot) pairs sorted by expert, their activations as
+// fp16 hi / lo planes, the gate / up outputs, h planes and per-pair outputs.
+struct MoeBigScratch {
+    int tmax = 0;
+    float *hn = nullptr;          // [tmax][d] normed tokens (router input)
+    __half *xt_hi = nullptr, *xt_lo = nullptr;   // [tmax][kp_d] token planes
+    float *logits = nullptr;      // [tmax][n_exp]
+    int *sel = nullptr;           // [tmax][n_act]
+    float *w = nullptr;           // [tmax][n_act]
+    int *cnt = nullptr;           // [n_exp] tokens per local expert, then [n_exp] fill counters
+    int *pair_at = nullptr;       // [tmax * n_act] pair (token * n_act + slot) at each sorted position
+    __half *xg_hi = nullptr, *xg_lo = nullptr;   // [tmax * n_act][kp_d] planes of each pair's token
+    float *gu = nullptr;          // [tmax * n_act][2 ffn] gate then up outputs
+    __half *hh_hi = nullptr, *hh_lo = nullptr;   // [tmax * n_act][kp_f] silu(g) * u planes
+    float *part = nullptr;        // [tmax * n_act][d] unweighted expert outputs per pair
+};
+size_t moe_big_scratch_bytes(int d, int n_exp, int n_act, int ffn, int tmax);
+MoeBigScratch moe_big_scratch_carve(void *base, int d, int n_exp, int n_act, int ffn, int tmax);
+// h[t] += MoE(rmsnorm(h[t], norm_w)) for T <= S.tmax tokens (the experts this
+// layer holds; with a partial range, h receives this process's share): router
+// logits, top-k per token, the pairs sorted by expert, the experts' gate / up
+// and down layers as grouped tensor-core GEMMs (launch_qgemm), combine in
+// slot order.
+int launch_moe_prefill(DevCtx *c, const MoeLayer &L, const MoeBigScratch &S, float *h, int T, const float *norm_w,
+                       float eps, cudaStream_t s);
+
 int launch_moe_ex(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *x, float *eout, int batch,
                   const MoeOpts &o, cudaStream_t s);
 // Upload router [n_exp][d] and experts [lo, hi) of GGUF-native gate/up/down

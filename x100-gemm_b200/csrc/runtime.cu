@@ -160,6 +160,12 @@ static PFN_encodeTiled encoder() {
 
 bool make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+    return make_tmap_2d_sw(m, base, dt, inner, outer, row_stride_bytes, box_inner, box_outer,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+bool make_tmap_2d_sw(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+                     uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
     PFN_encodeTiled enc = encoder();
     if (!enc) return false;
     cuuint64_t dims[2] = {inner, outer};
@@ -167,8 +173,7 @@ bool make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 

@@ -85,6 +85,10 @@ bool is_device_ptr(const void *p);
 // `box_outer`, 128-byte swizzle, out-of-bounds elements read as zero.
 bool make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+// The same with the swizzle chosen by the caller (CU_TENSOR_MAP_SWIZZLE_NONE
+// for plain row-by-row boxes).
+bool make_tmap_2d_sw(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+                     uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw);
 
 // Map a CUDA error to an X100 status and record it.  Returns the status.
 int check_cuda(cudaError_t e, int code_if_error);
