@@ -44,11 +44,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="x100", choices=["x100", "reference"])
     ap.add_argument("--workload", default="gemm_i8",
-                    choices=["gemm_i8", "gemm_f16", "gemm_f32", "q4gemv", "moe", "decode"])
+                    choices=["gemm_i8", "gemm_f16", "gemm_f32", "q4gemv", "moe", "decode", "prefill"])
     ap.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workloads")
     ap.add_argument("--batch", type=int, default=1, help="tokens per step for q4gemv / moe")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--layers", type=int, default=48, help="layers of the decode workload")
+    ap.add_argument("--layers", type=int, default=48, help="layers of the decode / prefill workloads")
+    ap.add_argument("--tokens", type=int, default=512, help="prompt tokens of the prefill workload")
     ap.add_argument("--combine", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1 expert-parallel sum: the library's peer-memory kernel or an NCCL all-reduce")
     return ap.parse_args()
@@ -961,6 +962,81 @@ def bench_decode(args, dist, peaks, peak_src):
     }
 
 
+def bench_prefill(args, dist, peaks, peak_src):
+    """Prefill of a prompt into one sequence of the config-5 model (48 layers,
+    Q8_0 attention, 128 Q3_K experts, fp16 KV cache of 4096): x100q_model_prefill
+    with n tokens > max_batch, the chunked tensor-core path (chunks of 256
+    tokens: the q/k/v, Wo and expert linears as tcgen05 dequant GEMMs, the
+    experts grouped by the chunk's routing).  One step = one prefill of the
+    whole prompt at positions 0 .. n-1 of slot 0, without logits (a prompt's
+    logits are not needed).  1 GPU; the host call is synchronous, so the step
+    is timed on the host clock around it."""
+    import numpy as np
+    import torch
+    import x100b
+    if dist.world > 1:
+        raise SystemExit("prefill workload: 1 GPU (the prefill path does not shard)")
+    NL, n = args.layers, args.tokens
+    c = dict(DEC)
+    d, qd, kvd, E, F, V = c["d"], c["n_heads"] * 128, c["n_kv_heads"] * 128, c["n_exp"], c["moe_ffn"], c["vocab"]
+    m = x100b.Model(n_layers=NL, max_batch=16, expert_lo=0, expert_hi=E, **c)
+    gen = torch.Generator(device="cuda").manual_seed(56)
+    blk = lambda qt, k: wellformed_blocks_dev(qt, k, gen, on_device=True)   # noqa: E731
+    nrm = lambda k: (1 + 0.1 * torch.randn(k, device="cuda", generator=gen)).contiguous()   # noqa: E731
+    for li in range(NL):
+        lw = dict(attn_norm=nrm(d), wq=blk(8, qd * d // 32), wk=blk(8, kvd * d // 32), wv=blk(8, kvd * d // 32),
+                  q_norm=nrm(128), k_norm=nrm(128), wo=blk(8, d * qd // 32), ffn_norm=nrm(d),
+                  router=(0.02 * torch.randn((E, d), device="cuda", generator=gen)).contiguous(),
+                  gate=blk(11, E * F * d // 256), up=blk(11, E * F * d // 256), down=blk(11, E * d * F // 256))
+        m.set_layer(li, *(lw[k] for k in ("attn_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo", "ffn_norm",
+                                          "router", "gate", "up", "down")))
+        del lw
+    m.set_output(torch.randn((V, d), device="cuda", generator=gen), nrm(d), blk(8, V * d // 32))
+    torch.cuda.synchronize()
+    toks = np.random.default_rng(3).integers(0, V, size=n).astype(np.int32)
+    toks_p = torch.from_numpy(toks).pin_memory()
+    for _ in range(args.warmup):
+        m.prefill(0, toks_p.numpy(), 0, logits=False)
+    clk = ClockSampler(dist.physical_gpu())
+    clk.start()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.prefill(0, toks_p.numpy(), 0, logits=False)
+    dt = time.perf_counter() - t0
+    clocks = clk.stop()
+    step_ms = dt * 1e3 / args.steps
+    tok_s = n / (step_ms / 1e3)
+    # algorithmic work of one prompt: 2 flops per weight per token (q/k/v, Wo,
+    # the token's 8 experts), the single product (the kernel issues three to
+    # carry 22-bit operands); attention over the causal prefix
+    params_tok = (qd + 2 * kvd) * d + d * qd + c["n_act"] * 3 * F * d
+    flops = 2.0 * n * NL * params_tok + NL * 4.0 * c["n_heads"] * 128 * n * (n + 1) / 2
+    tflops = flops / (step_ms / 1e3) / 1e12
+    peak = peaks["bf16_tflops"]
+    return {
+        "metric": "prefill tokens/s (config-5 model)", "value": round(tok_s, 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+        "dtype": "q8_0 / q3_k weights, fp16 hi+lo operands on kind::f16, fp32 accumulate",
+        "data": "synthetic: random well-formed blocks, fp32 router N(0,0.02), random token ids",
+        "config": {"workload": f"prefill {n} tokens into one sequence, {NL} layers, Q8_0 attention, 128 Q3_K "
+                               f"experts top-8, chunks of 256 tokens", "tokens": n, "layers": NL,
+                   "timing": "host clock around the synchronous x100q_model_prefill call (syncs per chunk)",
+                   "l2": f"weights {NL * ((qd + 2 * kvd) * d + d * qd) * 34 / 32 / 2**30 + NL * E * 3 * F * d * 110 / 256 / 2**30:.1f} GiB per prompt (> L2)"},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / peak, 4), "traffic": None,
+                     "peak_source": f"bf16_tflops ({peak_src} MEASURED_PEAKS.json)",
+                     "kernel": "whole prefill (algorithmic flops: one product per weight and token; the dequant "
+                               "GEMM issues three kind::f16 products)",
+                     "algorithmic_flops_per_step": flops},
+        "clocks": clocks,
+        "e2e": {"value": round(tok_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 0,
+                "api": "x100q_model_prefill(model, slot, tokens, n, pos0, NULL) with pinned host tokens"},
+        "gpu_launches": None,
+        "cpu_baseline": None,
+    }
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -978,6 +1054,8 @@ def main():
             line = bench_q4gemv(args, dist, peaks, src)
         elif args.workload == "decode":
             line = bench_decode(args, dist, peaks, src)
+        elif args.workload == "prefill":
+            line = bench_prefill(args, dist, peaks, src)
         else:
             line = bench_moe(args, dist, peaks, src)
     finally:

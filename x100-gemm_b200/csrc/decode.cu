@@ -935,8 +935,12 @@ static int prefill_linear(x100q_model *m, DevCtx *c, const QMat &W, const float 
 // streamed once per 128 tokens), every token's k and v go to the cache
 // before any token attends, and the attention runs per token over its
 // positions 0 .. pos (causal) in groups of max_batch tokens.
+// position of token i of a chunk whose first token sits at pos0 (the
+// positions of a prefill chunk are consecutive)
+static inline int hpos_last(int pos0, int i) { return pos0 + i; }
+
 static int prefill_chunk_tc(x100q_model *m, DevCtx *c, const int *tok, float *h, const int *pos, const int *slot,
-                            float *logits, int T, cudaStream_t s) {
+                            int hpos0, float *logits, int T, cudaStream_t s) {
     const x100q_model_cfg &g = m->cfg;
     static bool attr[64];
     if (!attr[c->device]) {
@@ -979,18 +983,31 @@ static int prefill_chunk_tc(x100q_model *m, DevCtx *c, const int *tok, float *h,
         a.att = m->pf_att;
         a.status = c->d_status;
         st = launch_pdl(kv_write_kernel, dim3(g.n_kv_heads, T), dim3(32), 0, s, a);
-        for (int g0 = 0; st == X100_OK && g0 < T; g0 += g.max_batch) {
-            const int gb = T - g0 < g.max_batch ? T - g0 : g.max_batch;
+        // groups of tokens whose (token, split) partials fit the decode step's
+        // buffer (max_batch x nsplit_max of them); the group's splits cover
+        // its largest position only (the chunk's positions are consecutive:
+        // hpos[g0 + gb - 1] is the group's largest), so early chunks need few
+        const int cap = g.max_batch * m->nsplit_max;
+        for (int g0 = 0; st == X100_OK && g0 < T;) {
+            int gb = T - g0;
+            int nsp = (hpos_last(hpos0, g0 + gb - 1) + kChunk) / kChunk;
+            while (gb > 1 && gb * nsp > cap) {
+                gb = cap / nsp < gb ? cap / nsp : gb - 1;
+                if (gb < 1) gb = 1;
+                nsp = (hpos_last(hpos0, g0 + gb - 1) + kChunk) / kChunk;
+            }
             AttnArgs ag = a;
             ag.qkv = m->pf_qkv + (size_t)g0 * qn;
             ag.pos = pos + g0;
             ag.slot = slot + g0;
             ag.att = m->pf_att + (size_t)g0 * qd;
+            ag.nsplit = nsp;
             st = launch_pdl(attn_decode_kernel, dim3(ag.nsplit, g.n_kv_heads, gb), dim3(kAttnThreads), attn_smem(), s,
                             m->tmK, m->tmV, ag);
             if (!st && ag.nsplit > 1)
                 st = launch_pdl(attn_merge_kernel, dim3(g.n_heads, gb), dim3(128), merge_smem(ag.nsplit), s,
                                 (const float *)m->part, g.n_heads, ag.nsplit, ag.att);
+            g0 += gb;
         }
         if (st) break;
         // 3. h += Wo . att
@@ -1105,7 +1122,7 @@ static int prefill_tc(x100q_model *m, int slot, const int *tokens, int n, int po
         st = check_cuda(cudaMemcpyAsync(dtok, tokens + c0, cn * 4, cudaMemcpyDefault, c->stream), X100_E_COPY);
         if (!st) st = check_cuda(cudaMemcpyAsync(dpos, hp.data(), cn * 4, cudaMemcpyHostToDevice, c->stream), X100_E_COPY);
         if (!st) st = check_cuda(cudaMemcpyAsync(dslot, hs.data(), cn * 4, cudaMemcpyHostToDevice, c->stream), X100_E_COPY);
-        if (!st) st = prefill_chunk_tc(m, c, dtok, dh, dpos, dslot, dl, cn, c->stream);
+        if (!st) st = prefill_chunk_tc(m, c, dtok, dh, dpos, dslot, pos0 + c0, dl, cn, c->stream);
         if (!st && logits)
             st = check_cuda(cudaMemcpyAsync(logits + (size_t)c0 * g.vocab, dl, (size_t)cn * g.vocab * 4, cudaMemcpyDefault,
                                             c->stream), X100_E_COPY);

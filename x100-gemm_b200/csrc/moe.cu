@@ -699,6 +699,77 @@ __global__ void __launch_bounds__(256) combine_kernel(int d, int n_act, int lo, 
 }
 
 // ---- many-token (prefill) path: pairs sorted by expert ------------------------------------
+// router_many: logits[t][e] = router[e] . hn[t] (fp32, qwen_moe.c:296) for
+// many tokens: one warp per (expert, group of 32 tokens) holds the expert's
+// row in registers (d <= 2048: 16 float4 per lane; the rest streamed) and
+// walks its tokens two at a time, all of a token's 16-byte loads issued
+// before its arithmetic.  Grid (n_exp, ceil(T / 32)).  CTA (0, 0) also
+// clears zero[0, nzero) (the counters of the kernels that follow).
+constexpr int kRmTok = 32;
+__global__ void __launch_bounds__(32) router_many_kernel(const float *__restrict__ router,
+                                                         const float *__restrict__ hn, int d, int n_exp, int T,
+                                                         float *__restrict__ logits, int *__restrict__ zero,
+                                                         int nzero) {
+    constexpr int RV = 16;
+    const int lane = threadIdx.x, e = blockIdx.x, t0 = blockIdx.y * kRmTok;
+    const int nv = min(d / 128, RV);
+    const float4 *rw = reinterpret_cast<const float4 *>(router + (long)e * d);
+    float4 r[RV];
+#pragma unroll
+    for (int i = 0; i < RV; ++i)
+        if (i < nv) r[i] = __ldg(rw + lane + 32 * i);
+    pdl_wait();
+    pdl_launch_dependents();
+    if (zero && blockIdx.x == 0 && blockIdx.y == 0)
+        for (int i = lane; i < nzero; i += 32) zero[i] = 0;
+    const int tend = min(T, t0 + kRmTok);
+    for (int t = t0; t < tend; t += 2) {
+        const bool two = t + 1 < tend;
+        const float4 *x0 = reinterpret_cast<const float4 *>(hn + (long)t * d);
+        const float4 *x1 = reinterpret_cast<const float4 *>(hn + (long)(two ? t + 1 : t) * d);
+        float4 v0[RV], v1[RV];
+#pragma unroll
+        for (int i = 0; i < RV; ++i)
+            if (i < nv) {
+                v0[i] = __ldcg(x0 + lane + 32 * i);
+                v1[i] = __ldcg(x1 + lane + 32 * i);
+            }
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < RV; ++i)
+            if (i < nv) {
+                s0 = fmaf(r[i].x, v0[i].x, s0);
+                s0 = fmaf(r[i].y, v0[i].y, s0);
+                s0 = fmaf(r[i].z, v0[i].z, s0);
+                s0 = fmaf(r[i].w, v0[i].w, s0);
+                s1 = fmaf(r[i].x, v1[i].x, s1);
+                s1 = fmaf(r[i].y, v1[i].y, s1);
+                s1 = fmaf(r[i].z, v1[i].z, s1);
+                s1 = fmaf(r[i].w, v1[i].w, s1);
+            }
+        for (int i = lane + 32 * nv; i < d / 4; i += 32) {   // past the registers' share
+            const float4 rr = __ldg(rw + i), a0 = __ldcg(x0 + i), a1 = __ldcg(x1 + i);
+            s0 = fmaf(rr.x, a0.x, s0);
+            s0 = fmaf(rr.y, a0.y, s0);
+            s0 = fmaf(rr.z, a0.z, s0);
+            s0 = fmaf(rr.w, a0.w, s0);
+            s1 = fmaf(rr.x, a1.x, s1);
+            s1 = fmaf(rr.y, a1.y, s1);
+            s1 = fmaf(rr.z, a1.z, s1);
+            s1 = fmaf(rr.w, a1.w, s1);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+        }
+        if (lane == 0) {
+            logits[(long)t * n_exp + e] = s0;
+            if (two) logits[(long)(t + 1) * n_exp + e] = s1;
+        }
+    }
+}
+
 // route_count: one CTA per token routes it (route_fast: softmax, greedy top-k,
 // renormalise), writes sel / w, and counts its pairs per local expert.
 __global__ void __launch_bounds__(128) route_count_kernel(int n_exp, int n_act, int lo, int hi,
@@ -1163,20 +1234,15 @@ int launch_moe_prefill(DevCtx *c, const MoeLayer &L, const MoeBigScratch &S, flo
         return X100_E_ARG;
     }
     if (fault_injected("launch")) return X100_E_INJECTED;
-    static bool attr[64];
-    if (!attr[c->device]) {
-        set_qkernel_attrs(router_logits_kernel);
-        attr[c->device] = true;
-    }
     const int kpd = slices_per_row(L.d) * 256, kpf = slices_per_row(L.ffn) * 256;
     const int P = T * L.n_act;
-    // 1. router logits of the normed tokens (qwen_moe.c:296), hn written for
-    //    the experts, the counters cleared
-    int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2, T), dim3(64), 0, s, (const float *)L.router,
-                        (const float *)h, L.d, L.n_exp, T, S.logits, S.cnt, 2 * nl, norm_w, eps, S.hn);
+    // 1. hn = rmsnorm(h, norm_w) (qwen_moe_q3k.c:1166), fp32 for the router
+    //    and as fp16 hi / lo planes for the experts
+    int st = launch_split_rows(h, L.d, L.d, kpd, T, norm_w, eps, S.xt_hi, S.xt_lo, S.hn, s);
     if (st) return st;
-    // 2. the normed tokens as fp16 hi / lo planes
-    st = launch_split_rows(S.hn, L.d, L.d, kpd, T, nullptr, 0.f, S.xt_hi, S.xt_lo, nullptr, s);
+    // 2. router logits (qwen_moe.c:296); the counters cleared
+    st = launch_pdl(router_many_kernel, dim3(L.n_exp, (T + kRmTok - 1) / kRmTok), dim3(32), 0, s,
+                    (const float *)L.router, (const float *)S.hn, L.d, L.n_exp, T, S.logits, S.cnt, 2 * nl);
     if (st) return st;
     // 3. softmax, top-k, renormalise (qwen_moe.c:297-301); pairs per expert
     st = launch_pdl(route_count_kernel, dim3(T), dim3(128), 0, s, L.n_exp, L.n_act, L.lo, L.hi,

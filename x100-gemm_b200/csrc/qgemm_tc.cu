@@ -22,10 +22,13 @@
 //             (qwen_moe.c:162-165, qwen_moe_q3k.c:534-577, repack.cpp:222-283)
 //             and writes W_hi = fp16(w) and W_lo = fp16(w - W_hi) into the A
 //             planes in the 128-byte-swizzled K-major layout the MMA reads.
-//   warp 1    MMA issuer: per 16 elements of K, three tcgen05.mma kind::f16
-//             (fp32 accumulate in TMEM): W_hi.X_hi + W_hi.X_lo + W_lo.X_hi --
-//             weights and activations each carried to ~22 bits, so the
-//             products agree with the fp32 dequant-GEMV to ~1e-6 relative
+//   warp 1    MMA issuer: per 16 elements of K, two tcgen05.mma kind::f16
+//             (fp32 accumulate in TMEM): W_hi against [X_hi | X_lo] (the two
+//             planes sit one after the other, so one instruction with N =
+//             64 + n tokens forms both products in separate column ranges),
+//             then W_lo against X_hi into the first range; the epilogue adds
+//             the ranges.  Weights and activations each carried to ~22 bits,
+//             the products agree with the fp32 dequant-GEMV to ~1e-6 relative
 //             (the dropped W_lo.X_lo term is ~2^-22 of a product).
 //   warps 2-9 epilogue, once the item's MMAs are done: TMEM -> registers ->
 //             out (store, += residual, or scattered to the rows pair_at names).
@@ -43,27 +46,44 @@ namespace x100 {
 namespace q {
 
 constexpr int QG_ROWS = 128;                    // weight rows per item = TMEM lanes
-constexpr int QG_NT = 128;                      // tokens per item (MMA N, at most)
+constexpr int QG_NT = 64;                       // tokens per item (MMA N, at most)
 constexpr int QG_NT_SMALL = 32;                 // box of the small token tiles
-constexpr int QG_AB_STAGES = 2;
-constexpr int QG_RAW_STAGES = 2;
-constexpr int QG_DQ_WARPS = 8;
+constexpr int QG_A_STAGES = 2;                  // dequantised weight planes
+constexpr int QG_RAW_STAGES = 2;                // raw weight slices
+constexpr int QG_DQ_WARPS = 16;
 constexpr int QG_THREADS = 64 + 32 * QG_DQ_WARPS;
 constexpr int QG_PLANE_A = QG_ROWS * 128;       // 128 rows x 64 fp16
-constexpr int QG_PLANE_B = QG_NT * 128;         // 128 tokens x 64 fp16
-constexpr int QG_AB_BYTES = 2 * QG_PLANE_A + 2 * QG_PLANE_B;
-constexpr int QG_RAW_BYTES = QG_ROWS * 272;     // 128 rows of the largest slice (Q8_0)
+constexpr int QG_PLANE_B = QG_NT * 128;         // 64 tokens x 64 fp16
+constexpr int QG_A_BYTES = 2 * QG_PLANE_A;
+constexpr int QG_B_BYTES = 2 * QG_PLANE_B;
 constexpr int QG_MAX_GROUPS = 256;
-constexpr int QG_RAW_OFF = QG_AB_STAGES * QG_AB_BYTES;
-constexpr int QG_BAR_OFF = QG_RAW_OFF + QG_RAW_STAGES * QG_RAW_BYTES;
-constexpr int QG_NBARS = 4 * QG_AB_STAGES + 2 * QG_RAW_STAGES + 3;   // a_full b_full ab_empty x2 ... raw, t
-constexpr int QG_PFX_OFF = QG_BAR_OFF + QG_NBARS * 8 + 16;
-constexpr int QG_SMEM = QG_PFX_OFF + 2 * (QG_MAX_GROUPS + 1) * 4 + 1024;
-constexpr uint32_t QG_TMEM_COLS = QG_NT;
+constexpr uint32_t QG_TMEM_COLS = 2 * QG_NT;   // [W.X_hi | W_hi.X_lo]
 constexpr unsigned long long kQgDrainNs = 100000000ull;
+constexpr int QG_SMEM_CAP = 227 * 1024;
+
+// Shared-memory plan of one weight format: the activation ring is as deep as
+// the budget allows after the dequantised-weight and raw-slice rings.
+struct QgLayout {
+    int sb, raw_bytes, b_stages, a_off, b_off, raw_off, bar_off, pfx_off, smem;
+};
+__host__ __device__ constexpr QgLayout qg_layout(int qt) {
+    QgLayout L{};
+    L.sb = slice_bytes(qt);
+    L.raw_bytes = (QG_ROWS * L.sb + 1023) / 1024 * 1024;
+    const int fixed = QG_A_STAGES * QG_A_BYTES + QG_RAW_STAGES * L.raw_bytes + 4096 + 1024;
+    L.b_stages = (QG_SMEM_CAP - fixed) / QG_B_BYTES;
+    L.b_stages = L.b_stages > 8 ? 8 : L.b_stages;
+    L.a_off = 0;
+    L.b_off = QG_A_STAGES * QG_A_BYTES;
+    L.raw_off = L.b_off + L.b_stages * QG_B_BYTES;
+    L.bar_off = L.raw_off + QG_RAW_STAGES * L.raw_bytes;
+    L.pfx_off = L.bar_off + 64 * 8;
+    L.smem = L.pfx_off + 2 * (QG_MAX_GROUPS + 1) * 4 + 1024;
+    return L;
+}
 
 struct QgParams {
-    int nmat, n_rows, ns, ngroups, T, mode, sb;   // sb: slice bytes of the weight format
+    int nmat, n_rows, ns, ngroups, T, mode;
     const int *cnt;
     float *out;
     long ldo;
@@ -79,7 +99,7 @@ struct QgItem {
 // g, tok[g] token rows before it; within a group, token tiles vary fastest
 // (consecutive items share weight rows, so a second CTA reads them from L2).
 __device__ __forceinline__ QgItem qg_item(int i, const int *tiles, const int *tok, int ngroups, int rt_per_mat,
-                                          int nmat, const int *cnt, int T) {
+                                          const int *cnt, int T) {
     int lo = 0, hi = ngroups - 1;
     while (lo < hi) {   // last group whose first item is <= i
         const int mid = (lo + hi + 1) >> 1;
@@ -99,121 +119,198 @@ __device__ __forceinline__ QgItem qg_item(int i, const int *tiles, const int *to
     return it;
 }
 
-// ---- dequantisation of 32 weights (elements 32 b .. 32 b + 31 of a slice) -------------
+// ---- dequantisation: 16 weights (elements 16 q16 .. 16 q16 + 15 of 32-element
+// block b of a slice) as 8 fp16 pairs hi / lo, element order ---------------------------
 __device__ __forceinline__ float h2f_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFF))); }
 __device__ __forceinline__ float h2f_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
 __device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
     return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
-__device__ __forceinline__ int byte_of(const uint4 &v, int i) { return (word_of(v, i >> 2) >> (8 * (i & 3))) & 0xFF; }
+__device__ __forceinline__ __half2 u2h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+__device__ __forceinline__ uint32_t h22u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 bits_h2(unsigned short b) { return u2h2((uint32_t)b | ((uint32_t)b << 16)); }
 
-template <int QT> __device__ __forceinline__ void dq32(const uint8_t *sl, int b, float (&w)[32]);
+// Bytes 0-1 (sel 0) or 2-3 (sel 1) of a word of unsigned bytes v (< 256) as
+// the fp16 pair {1024 + v0, 1024 + v1}: the byte becomes the mantissa of a
+// half with exponent 10, exact.
+__device__ __forceinline__ __half2 bytes_h2(uint32_t w, int sel) {
+    return u2h2(__byte_perm(w, 0x64646464u, sel ? 0x4342u : 0x4140u));
+}
+// hi = fp16(s * q), lo = fp16(s * q - hi) for two weights q (small integers,
+// exact in fp16) under an fp16 scale s: the product has at most 19
+// significant bits, the fma returns its exact remainder, so hi + lo = s * q.
+__device__ __forceinline__ void split_h2(__half2 s, __half2 q, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __hmul2(s, q);
+    hi = h22u(h);
+    lo = h22u(__hfma2(s, q, __hneg2(h)));
+}
+
+// A thread's raw bytes of one slice, loaded once per slice (the bytes its 16
+// weights of each of the slice's four 64-element pieces come from).  Thread
+// quarter q4 owns elements 16 q4 .. 16 q4 + 15 of every piece, i.e. half
+// q4 & 1 of 32-element block 2 j + (q4 >> 1) of piece j.
+template <int QT> struct SliceRegs;
+template <> struct SliceRegs<Q8_0> { uint4 hd; };                 // the 8 block scales
+template <> struct SliceRegs<Q4_0> { uint4 hd; };
+template <> struct SliceRegs<Q4_K> { uint4 hdr; };                // d, dmin, scales / mins
+template <> struct SliceRegs<Q3_K> { uint4 qs[2], mm, hdr; };     // qs of both halves, hmask, scales + d
+
+template <int QT> __device__ __forceinline__ void load_slice(const uint8_t *sl, int q4, SliceRegs<QT> &R);
+template <> __device__ __forceinline__ void load_slice<Q8_0>(const uint8_t *sl, int, SliceRegs<Q8_0> &R) { R.hd = ld16(sl); }
+template <> __device__ __forceinline__ void load_slice<Q4_0>(const uint8_t *sl, int, SliceRegs<Q4_0> &R) { R.hd = ld16(sl); }
+template <> __device__ __forceinline__ void load_slice<Q4_K>(const uint8_t *sl, int, SliceRegs<Q4_K> &R) { R.hdr = ld16(sl); }
+template <> __device__ __forceinline__ void load_slice<Q3_K>(const uint8_t *sl, int q4, SliceRegs<Q3_K> &R) {
+    const int q16 = q4 & 1;
+    R.qs[0] = ld16(sl + 16 * q16);
+    R.qs[1] = ld16(sl + 32 + 16 * q16);
+    R.mm = ld16(sl + 64 + 16 * q16);
+    R.hdr = ld16(sl + 96);
+}
+
+// The thread's 16 weights of piece j as 8 fp16 pairs hi / lo, element order.
+template <int QT>
+__device__ __forceinline__ void dq16(const SliceRegs<QT> &R, const uint8_t *sl, int j, int q4, uint32_t (&hv)[8],
+                                     uint32_t (&lv)[8]);
 // Q8_0 slice: [8 fp16 d][8 x 32 int8]; w = d * q (qwen_moe.c:162-163)
-template <> __device__ __forceinline__ void dq32<Q8_0>(const uint8_t *sl, int b, float (&w)[32]) {
-    const uint4 hd = ld16(sl);
-    const uint32_t dw = word_of(hd, b >> 1);
-    const float d = (b & 1) ? h2f_hi(dw) : h2f_lo(dw);
-    const uint4 q0 = ld16(sl + 16 + 32 * b), q1 = ld16(sl + 32 + 32 * b);
+template <>
+__device__ __forceinline__ void dq16<Q8_0>(const SliceRegs<Q8_0> &R, const uint8_t *sl, int j, int q4, uint32_t (&hv)[8],
+                                           uint32_t (&lv)[8]) {
+    const int b = 2 * j + (q4 >> 1), q16 = q4 & 1;
+    const uint32_t dw = word_of(R.hd, b >> 1);
+    const __half2 d2 = bits_h2((unsigned short)((b & 1) ? dw >> 16 : dw & 0xFFFF));
+    const uint4 q = ld16(sl + 16 + 32 * b + 16 * q16);
+    const __half2 off = __float2half2_rn(1152.0f);   // 1024 + 128: the bytes carry q + 128
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        w[i] = d * (float)(int8_t)byte_of(q0, i);
-        w[16 + i] = d * (float)(int8_t)byte_of(q1, i);
+    for (int wi = 0; wi < 4; ++wi) {
+        const uint32_t u = word_of(q, wi) ^ 0x80808080u;
+#pragma unroll
+        for (int sel = 0; sel < 2; ++sel) split_h2(d2, __hsub2(bytes_h2(u, sel), off), hv[2 * wi + sel], lv[2 * wi + sel]);
     }
 }
 // Q4_0 slice: [8 fp16 d][8 x 16 B nibbles]; element i < 16 the low nibble of
 // byte i, i >= 16 the high nibble of byte i - 16; w = (nib - 8) * d
 // (qwen_moe.c:164-165)
-template <> __device__ __forceinline__ void dq32<Q4_0>(const uint8_t *sl, int b, float (&w)[32]) {
-    const uint4 hd = ld16(sl);
-    const uint32_t dw = word_of(hd, b >> 1);
-    const float d = (b & 1) ? h2f_hi(dw) : h2f_lo(dw);
+template <>
+__device__ __forceinline__ void dq16<Q4_0>(const SliceRegs<Q4_0> &R, const uint8_t *sl, int j, int q4, uint32_t (&hv)[8],
+                                           uint32_t (&lv)[8]) {
+    const int b = 2 * j + (q4 >> 1), q16 = q4 & 1;
+    const uint32_t dw = word_of(R.hd, b >> 1);
+    const __half2 d2 = bits_h2((unsigned short)((b & 1) ? dw >> 16 : dw & 0xFFFF));
     const uint4 q = ld16(sl + 16 + 16 * b);
+    const __half2 off = __float2half2_rn(1032.0f);   // 1024 + 8: nib - 8
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int v = byte_of(q, i);
-        w[i] = (float)((v & 15) - 8) * d;
-        w[16 + i] = (float)((v >> 4) - 8) * d;
+    for (int wi = 0; wi < 4; ++wi) {
+        const uint32_t w = word_of(q, wi);
+        const uint32_t nib = q16 ? (w >> 4) & 0x0F0F0F0Fu : w & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int sel = 0; sel < 2; ++sel) split_h2(d2, __hsub2(bytes_h2(nib, sel), off), hv[2 * wi + sel], lv[2 * wi + sel]);
+    }
+}
+// Q3_K slice: [qs 64][hmask 32][scales 12][d 2][pad 2]; element e = 32 b + l:
+// half hh = b / 4, shift 2t with t = b % 4, q = ((qs[32hh + l] >> 2t) & 3) -
+// (hmask bit 4hh + t of byte l ? 0 : 4), sub-block scale 8hh + 2t + l/16;
+// w = d * (sc - 32) * q (qwen_moe_q3k.c:557-577).  The scale (17 bits, exact
+// in fp32) is carried as an fp16 pair dh + dl: hi = fp16(dh q), lo =
+// fp16((dh q - hi) + dl q), so hi + lo = w to ~2^-22 relative.
+template <>
+__device__ __forceinline__ void dq16<Q3_K>(const SliceRegs<Q3_K> &R, const uint8_t *, int j, int q4, uint32_t (&hv)[8],
+                                           uint32_t (&lv)[8]) {
+    const int b = 2 * j + (q4 >> 1), q16 = q4 & 1;
+    const int hh = b >> 2, t = b & 3, hb = 4 * hh + t;
+    const uint4 qq = R.qs[hh];
+    const float dlf = h2f_lo(R.hdr.w) * (float)q3k_scale(8 * hh + 2 * t + q16, R.hdr.x, R.hdr.y, R.hdr.z);
+    const __half dh = __float2half_rn(dlf);
+    const __half dlo = __float2half_rn(dlf - __half2float(dh));
+    const __half2 dh2 = __halves2half2(dh, dh), dl2 = __halves2half2(dlo, dlo);
+    const __half2 off = __float2half2_rn(1028.0f);   // 1024 + 4: v - 4
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+        const uint32_t v = ((word_of(qq, wi) >> (2 * t)) & 0x03030303u) | (((word_of(R.mm, wi) >> hb) & 0x01010101u) << 2);
+#pragma unroll
+        for (int sel = 0; sel < 2; ++sel) {
+            const __half2 q2 = __hsub2(bytes_h2(v, sel), off);
+            const __half2 h = __hmul2(dh2, q2);
+            const __half2 r = __hfma2(dh2, q2, __hneg2(h));
+            hv[2 * wi + sel] = h22u(h);
+            lv[2 * wi + sel] = h22u(__hfma2(dl2, q2, r));
+        }
     }
 }
 // Q4_K superblock: fp16 d, fp16 dmin, 12 B scales/mins, qs[128]; elements
 // 64c .. 64c+31 are the low nibbles of qs[32c .. 32c+31] (sub-block 2c),
 // 64c+32 .. 64c+63 their high nibbles (sub-block 2c+1); w = d*sc*q - dmin*m
 // (repack.cpp:222-283, the Q5_K decoder of qwen_moe_q3k.c:541-552 without the
-// fifth bit)
-template <> __device__ __forceinline__ void dq32<Q4_K>(const uint8_t *sl, int b, float (&w)[32]) {
-    const uint4 hdr = ld16(sl);
-    const float d = h2f_lo(hdr.x), dmin = h2f_hi(hdr.x);
+// fifth bit), formed in fp32 and split by conversion.
+template <>
+__device__ __forceinline__ void dq16<Q4_K>(const SliceRegs<Q4_K> &R, const uint8_t *sl, int j, int q4, uint32_t (&hv)[8],
+                                           uint32_t (&lv)[8]) {
+    const int b = 2 * j + (q4 >> 1), q16 = q4 & 1;
     int sc, m;
-    kq_scale_min(b, hdr.y, hdr.z, hdr.w, sc, m);
-    const float d1 = d * (float)sc, m1 = dmin * (float)m;
-    const uint4 q0 = ld16(sl + 16 + 32 * (b >> 1)), q1 = ld16(sl + 32 + 32 * (b >> 1));
+    kq_scale_min(b, R.hdr.y, R.hdr.z, R.hdr.w, sc, m);
+    const float d1 = h2f_lo(R.hdr.x) * (float)sc, m1 = h2f_hi(R.hdr.x) * (float)m;
+    const uint4 q = ld16(sl + 16 + 32 * (b >> 1) + 16 * q16);
     const int sh = (b & 1) ? 4 : 0;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        w[i] = d1 * (float)((byte_of(q0, i) >> sh) & 15) - m1;
-        w[16 + i] = d1 * (float)((byte_of(q1, i) >> sh) & 15) - m1;
-    }
-}
-// Q3_K slice: [qs 64][hmask 32][scales 12][d 2][pad 2]; element e = 32 b + l:
-// half hh = b / 4, shift 2t with t = b % 4, q = ((qs[32hh + l] >> 2t) & 3) -
-// (hmask bit 4hh + t of byte l ? 0 : 4), sub-block scale 8hh + 2t + l/16;
-// w = d * (sc - 32) * q (qwen_moe_q3k.c:557-577)
-template <> __device__ __forceinline__ void dq32<Q3_K>(const uint8_t *sl, int b, float (&w)[32]) {
-    const int hh = b >> 2, t = b & 3;
-    const uint4 q0 = ld16(sl + 32 * hh), q1 = ld16(sl + 32 * hh + 16);
-    const uint4 m0 = ld16(sl + 64), m1 = ld16(sl + 80);
-    const uint4 hdr = ld16(sl + 96);
-    const float d = h2f_lo(hdr.w);
-    const float dl0 = d * (float)q3k_scale(8 * hh + 2 * t, hdr.x, hdr.y, hdr.z);
-    const float dl1 = d * (float)q3k_scale(8 * hh + 2 * t + 1, hdr.x, hdr.y, hdr.z);
-    const int hb = 4 * hh + t;
+    for (int wi = 0; wi < 4; ++wi) {
+        const uint32_t w = word_of(q, wi);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int a = ((byte_of(q0, i) >> (2 * t)) & 3) - (((byte_of(m0, i) >> hb) & 1) ? 0 : 4);
-        const int c = ((byte_of(q1, i) >> (2 * t)) & 3) - (((byte_of(m1, i) >> hb) & 1) ? 0 : 4);
-        w[i] = dl0 * (float)a;
-        w[16 + i] = dl1 * (float)c;
+        for (int sel = 0; sel < 2; ++sel) {
+            const float x0 = d1 * (float)((w >> (16 * sel + sh)) & 15) - m1;
+            const float x1 = d1 * (float)((w >> (16 * sel + 8 + sh)) & 15) - m1;
+            const __half2 h = __float22half2_rn(make_float2(x0, x1));
+            const float2 f = __half22float2(h);
+            hv[2 * wi + sel] = h22u(h);
+            lv[2 * wi + sel] = h22u(__float22half2_rn(make_float2(x0 - f.x, x1 - f.y)));
+        }
     }
 }
 
-__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
-    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
-}
-
+// Roles (one CTA per SM, QG_THREADS threads):
+//   warp 0 lane 0  raw weight slices (TMA, ring of QG_RAW_STAGES)
+//   warp 0 lane 1  activation tiles (TMA, ring of b_stages)
+//   warp 1 lane 0  MMA issuer; warp 1 allocates TMEM
+//   warps 2..17    dequantise (thread: weight row r, 16 weights of every
+//                  64-element piece), then the item's epilogue
 template <int QT>
 __global__ void __launch_bounds__(QG_THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constant__ CUtensorMap tmW1,
                  const __grid_constant__ CUtensorMap tmXh, const __grid_constant__ CUtensorMap tmXl,
                  const __grid_constant__ CUtensorMap tmXhs, const __grid_constant__ CUtensorMap tmXls,
                  const QgParams p) {
+    constexpr QgLayout LY = qg_layout(QT);
+    constexpr int SB = LY.sb, BST = LY.b_stages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + QG_BAR_OFF);
-    uint64_t *a_full = bars;                          // [AB]: 8 dequant warps arrive
-    uint64_t *b_full = bars + QG_AB_STAGES;           // [AB]: producer + TMA bytes
-    uint64_t *ab_empty = bars + 2 * QG_AB_STAGES;     // [AB]: MMA commit
-    uint64_t *raw_full = bars + 3 * QG_AB_STAGES;     // [RAW]: producer + TMA bytes
-    uint64_t *raw_empty = raw_full + QG_RAW_STAGES;   // [RAW]: 8 dequant warps arrive
-    uint64_t *tfull = raw_empty + QG_RAW_STAGES;      // MMA commit: accumulator complete
-    uint64_t *tempty = tfull + 1;                     // 8 epilogue warps: accumulator read
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + LY.bar_off);
+    uint64_t *a_full = bars;                          // [A]: dequant warps arrive
+    uint64_t *a_empty = a_full + QG_A_STAGES;         // [A]: MMA commit
+    uint64_t *raw_full = a_empty + QG_A_STAGES;       // [RAW]: TMA bytes
+    uint64_t *raw_empty = raw_full + QG_RAW_STAGES;   // [RAW]: dequant warps arrive
+    uint64_t *b_full = raw_empty + QG_RAW_STAGES;     // [B]: TMA bytes
+    uint64_t *b_empty = b_full + BST;                 // [B]: MMA commit
+    uint64_t *tfull = b_empty + BST;                  // MMA commit: accumulator complete
+    uint64_t *tempty = tfull + 1;                     // dequant warps: accumulator read
     uint64_t *drain = tempty + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + QG_NBARS);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    int *tiles = reinterpret_cast<int *>(smem + QG_PFX_OFF);   // [ngroups + 1]
+    int *tiles = reinterpret_cast<int *>(smem + LY.pfx_off);   // [ngroups + 1]
     int *tok = tiles + QG_MAX_GROUPS + 1;                        // [ngroups + 1]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rt_per_mat = (p.n_rows + QG_ROWS - 1) / QG_ROWS;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < QG_AB_STAGES; ++s) {
+        for (int s = 0; s < QG_A_STAGES; ++s) {
             mbar_init(&a_full[s], QG_DQ_WARPS);
-            mbar_init(&b_full[s], 1);
-            mbar_init(&ab_empty[s], 1);
+            mbar_init(&a_empty[s], 1);
         }
         for (int s = 0; s < QG_RAW_STAGES; ++s) {
             mbar_init(&raw_full[s], 1);
             mbar_init(&raw_empty[s], QG_DQ_WARPS);
+        }
+        for (int s = 0; s < BST; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
         }
         mbar_init(tfull, 1);
         mbar_init(tempty, QG_DQ_WARPS);
@@ -230,7 +327,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     }
     pdl_wait();                                   // X planes and counts come from earlier kernels
     pdl_launch_dependents();
-    // item list: per-group item and token prefixes (warp 0, the groups 8 per lane at most)
+    // item list: per-group item and token prefixes (warp 0, groups spread over the lanes)
     if (warp == 0) {
         const int per = (p.ngroups + 31) / 32;
         int ts = 0, ks = 0;
@@ -272,95 +369,106 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int total = tiles[p.ngroups];
-    const int SB = p.sb;
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---------------- TMA producer ----------------
-            uint32_t st = 0, ph = 0, rs = 0, rph = 0;
-            uint32_t ab_issued[QG_AB_STAGES] = {0, 0}, raw_issued[QG_RAW_STAGES] = {0, 0};
+            // ---------------- raw weight slices ----------------
+            uint32_t rs = 0, rph = 0, issued[QG_RAW_STAGES] = {0, 0};
             bool ok = true;
             for (int i = blockIdx.x; i < total && ok; i += gridDim.x) {
-                const QgItem it = qg_item(i, tiles, tok, p.ngroups, rt_per_mat, p.nmat, p.cnt, p.T);
+                const QgItem it = qg_item(i, tiles, tok, p.ngroups, rt_per_mat, p.cnt, p.T);
                 const CUtensorMap *tw = it.mat ? &tmW1 : &tmW0;
-                const bool small = it.nt <= QG_NT_SMALL;
-                const CUtensorMap *th = small ? &tmXhs : &tmXh, *tl = small ? &tmXls : &tmXl;
-                const uint32_t bbytes = 2u * (small ? QG_NT_SMALL : QG_NT) * 128u;
                 const int wrow = it.g * p.n_rows + it.rtile * QG_ROWS;
-                for (int s = 0; s < p.ns && ok; ++s) {
+                for (int s = 0; s < p.ns; ++s) {
                     if (!mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
-                    uint8_t *raw = smem + QG_RAW_OFF + rs * QG_RAW_BYTES;
                     mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)(QG_ROWS * SB));
-                    tma_load_2d(raw, tw, s * (SB / 2), wrow, &raw_full[rs]);
-                    raw_issued[rs]++;
+                    tma_load_2d(smem + LY.raw_off + rs * LY.raw_bytes, tw, s * (SB / 2), wrow, &raw_full[rs]);
+                    issued[rs]++;
                     if (++rs == QG_RAW_STAGES) {
                         rs = 0;
                         rph ^= 1u;
                     }
-                    for (int j = 0; j < 4; ++j) {
-                        if (!mbar_wait(&ab_empty[st], ph ^ 1u, abort_flag, p.status)) {
-                            ok = false;
-                            break;
-                        }
-                        uint8_t *stg = smem + st * QG_AB_BYTES;
-                        mbar_arrive_expect_tx(&b_full[st], bbytes);
-                        tma_load_2d(stg + 2 * QG_PLANE_A, th, s * 256 + 64 * j, it.tok0, &b_full[st]);
-                        tma_load_2d(stg + 2 * QG_PLANE_A + QG_PLANE_B, tl, s * 256 + 64 * j, it.tok0, &b_full[st]);
-                        ab_issued[st]++;
-                        if (++st == QG_AB_STAGES) {
-                            st = 0;
-                            ph ^= 1u;
-                        }
+                }
+            }
+            if (!ok)   // copies still in flight after a timeout
+                for (int k = 0; k < QG_RAW_STAGES; ++k)
+                    if (issued[k]) mbar_wait_drain(&raw_full[k], (issued[k] - 1u) & 1u, kQgDrainNs);
+        } else if (lane == 1) {
+            // ---------------- activation tiles ----------------
+            uint32_t sb = 0, bph = 0, issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            bool ok = true;
+            for (int i = blockIdx.x; i < total && ok; i += gridDim.x) {
+                const QgItem it = qg_item(i, tiles, tok, p.ngroups, rt_per_mat, p.cnt, p.T);
+                const bool small = it.nt <= QG_NT_SMALL;
+                const CUtensorMap *th = small ? &tmXhs : &tmXh, *tl = small ? &tmXls : &tmXl;
+                const uint32_t bbytes = 2u * (small ? QG_NT_SMALL : QG_NT) * 128u;
+                for (int kk = 0; kk < 4 * p.ns; ++kk) {
+                    if (!mbar_wait(&b_empty[sb], bph ^ 1u, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *dst = smem + LY.b_off + sb * QG_B_BYTES;
+                    mbar_arrive_expect_tx(&b_full[sb], bbytes);
+                    tma_load_2d(dst, th, 64 * kk, it.tok0, &b_full[sb]);
+                    tma_load_2d(dst + QG_PLANE_B, tl, 64 * kk, it.tok0, &b_full[sb]);
+                    issued[sb]++;
+                    if (++sb == (uint32_t)BST) {
+                        sb = 0;
+                        bph ^= 1u;
                     }
                 }
             }
-            if (!ok) {   // copies still in flight after a timeout
-                for (int k = 0; k < QG_RAW_STAGES; ++k)
-                    if (raw_issued[k]) mbar_wait_drain(&raw_full[k], (raw_issued[k] - 1u) & 1u, kQgDrainNs);
-                for (int k = 0; k < QG_AB_STAGES; ++k)
-                    if (ab_issued[k]) mbar_wait_drain(&b_full[k], (ab_issued[k] - 1u) & 1u, kQgDrainNs);
-            }
+            if (!ok)
+                for (int k = 0; k < BST; ++k)
+                    if (issued[k]) mbar_wait_drain(&b_full[k], (issued[k] - 1u) & 1u, kQgDrainNs);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            uint32_t st = 0, ph = 0, tph = 0;
+            uint32_t sa = 0, aph = 0, sb = 0, bph = 0, tph = 0;
             bool ok = true;
             for (int i = blockIdx.x; i < total && ok; i += gridDim.x) {
-                const QgItem it = qg_item(i, tiles, tok, p.ngroups, rt_per_mat, p.nmat, p.cnt, p.T);
+                const QgItem it = qg_item(i, tiles, tok, p.ngroups, rt_per_mat, p.cnt, p.T);
+                // MMA 1: A = W_hi against the X_hi plane (64 rows) and the X_lo
+                // plane right after it, N = 64 + n: columns [0, 64) get
+                // W_hi.X_hi, [64, 64 + n) W_hi.X_lo.  MMA 2: A = W_lo against
+                // X_hi, N = n, adds W_lo.X_hi into columns [0, n).
                 const uint32_t N = (uint32_t)max(16, (it.nt + 15) & ~15);
-                const uint32_t idesc = idesc_make(1, 0, 0, QG_ROWS, N);
+                const uint32_t idesc1 = idesc_make(1, 0, 0, QG_ROWS, QG_NT + N);
+                const uint32_t idesc2 = idesc_make(1, 0, 0, QG_ROWS, N);
                 if (!mbar_wait(tempty, tph ^ 1u, abort_flag, p.status)) break;   // previous item read out
                 tph ^= 1u;
                 tc_fence_after();
-                for (int s = 0; s < p.ns && ok; ++s) {
-                    for (int j = 0; j < 4; ++j) {
-                        if (!mbar_wait(&a_full[st], ph, abort_flag, p.status) ||
-                            !mbar_wait(&b_full[st], ph, abort_flag, p.status)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t a_hi = smem_u32(smem + st * QG_AB_BYTES), a_lo = a_hi + QG_PLANE_A;
-                        const uint32_t b_hi = a_hi + 2 * QG_PLANE_A, b_lo = b_hi + QG_PLANE_B;
+                for (int kk = 0; kk < 4 * p.ns; ++kk) {
+                    if (!mbar_wait(&a_full[sa], aph, abort_flag, p.status) ||
+                        !mbar_wait(&b_full[sb], bph, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_hi = smem_u32(smem + LY.a_off + sa * QG_A_BYTES), a_lo = a_hi + QG_PLANE_A;
+                    const uint32_t b_hi = smem_u32(smem + LY.b_off + sb * QG_B_BYTES), b_lo = b_hi + QG_PLANE_B;
+                    (void)b_lo;   // the X_lo plane follows X_hi: one B operand of 64 + n rows
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const uint64_t dah = smem_desc_sw128(a_hi + 32 * k, 16, 1024);
-                            const uint64_t dal = smem_desc_sw128(a_lo + 32 * k, 16, 1024);
-                            const uint64_t dbh = smem_desc_sw128(b_hi + 32 * k, 16, 1024);
-                            const uint64_t dbl = smem_desc_sw128(b_lo + 32 * k, 16, 1024);
-                            umma_f16(tmem_base, dah, dbh, idesc, (s | j | k) ? 1u : 0u);
-                            umma_f16(tmem_base, dah, dbl, idesc, 1u);
-                            umma_f16(tmem_base, dal, dbh, idesc, 1u);
-                        }
-                        umma_commit(&ab_empty[st]);
-                        if (++st == QG_AB_STAGES) {
-                            st = 0;
-                            ph ^= 1u;
-                        }
+                    for (int k = 0; k < 4; ++k) {
+                        const uint64_t dah = smem_desc_sw128(a_hi + 32 * k, 16, 1024);
+                        const uint64_t dal = smem_desc_sw128(a_lo + 32 * k, 16, 1024);
+                        const uint64_t dbh = smem_desc_sw128(b_hi + 32 * k, 16, 1024);
+                        umma_f16(tmem_base, dah, dbh, idesc1, (kk | k) ? 1u : 0u);
+                        umma_f16(tmem_base, dal, dbh, idesc2, 1u);
+                    }
+                    umma_commit(&a_empty[sa]);
+                    umma_commit(&b_empty[sb]);
+                    if (++sa == QG_A_STAGES) {
+                        sa = 0;
+                        aph ^= 1u;
+                    }
+                    if (++sb == (uint32_t)BST) {
+                        sb = 0;
+                        bph ^= 1u;
                     }
                 }
                 if (ok) umma_commit(tfull);
@@ -371,47 +479,43 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     } else {
         // ---------------- dequantise, then epilogue ----------------
         const int dq = threadIdx.x - 64;
-        const int r = dq & (QG_ROWS - 1), hf = dq >> 7;   // weight row of the tile, half of each piece
-        const int q = warp & 3;                           // TMEM lane quadrant this warp may read
-        const int cpart = (warp - 2) >> 2;                // which 64 of the 128 token columns
-        uint32_t st = 0, ph = 0, rs = 0, rph = 0, tph = 0;
+        const int r = dq & (QG_ROWS - 1), q4 = dq >> 7;   // weight row of the tile, 16-weight quarter of each piece
+        const int qd = warp & 3;                          // TMEM lane quadrant this warp may read
+        const int cpart = (warp - 2) >> 2;                // which 32 of the token columns (0..3; 0-1 used)
+        uint32_t sa = 0, aph = 0, rs = 0, rph = 0, tph = 0;
         bool ok = true;
         for (int i = blockIdx.x; i < total && ok; i += gridDim.x) {
-            const QgItem it = qg_item(i, tiles, tok, p.ngroups, rt_per_mat, p.nmat, p.cnt, p.T);
+            const QgItem it = qg_item(i, tiles, tok, p.ngroups, rt_per_mat, p.cnt, p.T);
             for (int s = 0; s < p.ns && ok; ++s) {
                 if (!mbar_wait(&raw_full[rs], rph, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
-                const uint8_t *sl = smem + QG_RAW_OFF + rs * QG_RAW_BYTES + r * SB;
+                const uint8_t *sl = smem + LY.raw_off + rs * LY.raw_bytes + r * SB;
+                SliceRegs<QT> R;
+                load_slice<QT>(sl, q4, R);
                 for (int j = 0; j < 4; ++j) {
-                    float w[32];
-                    dq32<QT>(sl, 2 * j + hf, w);
-                    if (!mbar_wait(&ab_empty[st], ph ^ 1u, abort_flag, p.status)) {
+                    uint32_t hv[8], lv[8];
+                    dq16<QT>(R, sl, j, q4, hv, lv);
+                    if (!mbar_wait(&a_empty[sa], aph ^ 1u, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
-                    uint8_t *ahi = smem + st * QG_AB_BYTES + r * 128, *alo = ahi + QG_PLANE_A;
+                    uint8_t *ahi = smem + LY.a_off + sa * QG_A_BYTES + r * 128, *alo = ahi + QG_PLANE_A;
 #pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {
-                        uint32_t hv[4], lv[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float x0 = w[8 * cc + 2 * e], x1 = w[8 * cc + 2 * e + 1];
-                            const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-                            hv[e] = pack_h2(h0, h1);
-                            lv[e] = pack_h2(__float2half_rn(x0 - __half2float(h0)), __float2half_rn(x1 - __half2float(h1)));
-                        }
-                        const int off = ((4 * hf + cc) ^ (r & 7)) << 4;
-                        *reinterpret_cast<uint4 *>(ahi + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-                        *reinterpret_cast<uint4 *>(alo + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+                    for (int cc = 0; cc < 2; ++cc) {
+                        const int off = ((2 * q4 + cc) ^ (r & 7)) << 4;
+                        *reinterpret_cast<uint4 *>(ahi + off) =
+                            make_uint4(hv[4 * cc], hv[4 * cc + 1], hv[4 * cc + 2], hv[4 * cc + 3]);
+                        *reinterpret_cast<uint4 *>(alo + off) =
+                            make_uint4(lv[4 * cc], lv[4 * cc + 1], lv[4 * cc + 2], lv[4 * cc + 3]);
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[st]);
-                    if (++st == QG_AB_STAGES) {
-                        st = 0;
-                        ph ^= 1u;
+                    if (lane == 0) mbar_arrive(&a_full[sa]);
+                    if (++sa == QG_A_STAGES) {
+                        sa = 0;
+                        aph ^= 1u;
                     }
                 }
                 __syncwarp();
@@ -426,19 +530,21 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
             if (!mbar_wait(tfull, tph, abort_flag, p.status)) break;
             tph ^= 1u;
             tc_fence_after();
-            const int row = it.rtile * QG_ROWS + q * 32 + lane;
+            const int row = it.rtile * QG_ROWS + qd * 32 + lane;
             const long col = (long)it.mat * p.n_rows + row;
-            for (int c0 = 64 * cpart; c0 < 64 * cpart + 64 && c0 < it.nt; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem_base + c0 + (static_cast<uint32_t>(q * 32) << 16), v);
+            const int c0 = 32 * cpart;
+            for (int c1 = c0; c1 < c0 + 32 && c1 < it.nt; c1 += 16) {   // warp-uniform
+                uint32_t v[16], w[16];
+                tmem_ld16(tmem_base + c1 + (static_cast<uint32_t>(qd * 32) << 16), v);
+                tmem_ld16(tmem_base + QG_NT + c1 + (static_cast<uint32_t>(qd * 32) << 16), w);
                 tmem_wait_ld();
                 if (row < p.n_rows) {
-#pragma unroll 4
-                    for (int k = 0; k < 32; ++k) {
-                        const int c = c0 + k;
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        const int c = c1 + k;
                         if (c < it.nt) {
                             const int t = it.tok0 + c;
-                            const float val = __uint_as_float(v[k]);
+                            const float val = __uint_as_float(v[k]) + __uint_as_float(w[k]);
                             if (p.mode == QG_SCATTER) {
                                 p.out[(long)__ldg(p.pair_at + t) * p.ldo + col] = val;
                             } else {
@@ -540,13 +646,15 @@ int launch_swiglu_split(const float *gu, int ffn, int kp, int rows, __half *hi, 
 template <int QT>
 static int launch_qgemm_qt(DevCtx *c, const QgLaunch &L, const CUtensorMap *tw, const CUtensorMap *tx,
                            const QgParams &p, cudaStream_t s) {
+    constexpr QgLayout LY = qg_layout(QT);
+    static_assert(LY.smem <= QG_SMEM_CAP && LY.b_stages >= 2, "shared-memory plan");
     static bool attr[64];
     if (!attr[c->device]) {
-        cudaFuncSetAttribute(qgemm_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, QG_SMEM);
+        cudaFuncSetAttribute(qgemm_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, LY.smem);
         attr[c->device] = true;
     }
     const int grid = c->sm_count;
-    return launch_pdl(qgemm_kernel<QT>, dim3(grid), dim3(QG_THREADS), (size_t)QG_SMEM, s, tw[0], tw[1], tx[0], tx[1],
+    return launch_pdl(qgemm_kernel<QT>, dim3(grid), dim3(QG_THREADS), (size_t)LY.smem, s, tw[0], tw[1], tx[0], tx[1],
                       tx[2], tx[3], p);
 }
 
@@ -587,7 +695,6 @@ int launch_qgemm(DevCtx *c, const QgLaunch &L, cudaStream_t s) {
     p.ngroups = L.ngroups;
     p.T = L.T;
     p.mode = L.mode;
-    p.sb = SB;
     p.cnt = L.cnt;
     p.out = L.out;
     p.ldo = L.ldo;
