@@ -39,6 +39,11 @@ CFG = dict(n_layers=2, d=2048, n_heads=32, n_kv_heads=4, head_dim=128, vocab=640
 
 @pytest.fixture(scope="module")
 def world():
+    # chunks of 96 tokens: the 256-token prefill runs as three chunks (each
+    # attending over the cache the earlier ones wrote), the 64-token one as one
+    import os
+    old = os.environ.get("X100_PREFILL_CHUNK")
+    os.environ["X100_PREFILL_CHUNK"] = "96"
     rng = np.random.default_rng(9090)
     c = CFG
     layers = [make_layer(rng, c) for _ in range(c["n_layers"])]
@@ -55,6 +60,10 @@ def world():
     m.set_output(emb, out_norm, lm)
     yield dict(c=c, layers=layers, emb=emb, out_norm=out_norm, lm=lm, kv=kv, model=m)
     m.close()
+    if old is None:
+        os.environ.pop("X100_PREFILL_CHUNK", None)
+    else:
+        os.environ["X100_PREFILL_CHUNK"] = old
 
 
 def load_kv(w):

@@ -881,12 +881,21 @@ static int forward_impl(x100q_model *m, const int *tokens, float *h, const int *
 }
 
 // ---- many-token prefill on the tensor-core GEMMs -------------------------------------------
-constexpr int kPrefillChunk = 256;   // tokens per chunk of the tensor-core path
+// Tokens per chunk of the tensor-core path: a chunk streams every weight once,
+// so longer chunks reuse each weight over more tokens (the experts see
+// ~chunk * top-k / n_exp tokens each) at the cost of scratch memory (about
+// 0.28 MB per token of chunk at the config-5 shape).  X100_PREFILL_CHUNK
+// overrides the default (32 .. 4096), read when a model first prefills.
+constexpr int kPrefillChunk = 1024;
 
 static bool prefill_alloc(x100q_model *m) {
     if (m->pf_base) return true;
     const x100q_model_cfg &g = m->cfg;
-    const int T = kPrefillChunk;
+    int T = kPrefillChunk;
+    if (const char *e = getenv("X100_PREFILL_CHUNK")) {
+        const int v = atoi(e);
+        if (v >= 32 && v <= 4096) T = v;
+    }
     const int kpd = slices_per_row(g.d) * 256, kpq = slices_per_row(g.n_heads * g.head_dim) * 256;
     m->pf_kp = kpd > kpq ? kpd : kpq;
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
@@ -1090,7 +1099,7 @@ int x100q_model_prefill(x100q_model *m, int slot, const int *tokens, int n, int 
 
 }  // extern "C"
 
-// x100q_model_prefill for n > max_batch: chunks of up to kPrefillChunk tokens,
+// x100q_model_prefill for n > max_batch: chunks of up to pf_tmax tokens,
 // each through prefill_chunk_tc, in order (a chunk attends over the cache the
 // earlier chunks wrote).  Synchronous; host or device tokens / logits.
 static int prefill_tc(x100q_model *m, int slot, const int *tokens, int n, int pos0, float *logits) {
