@@ -502,8 +502,12 @@ __device__ __forceinline__ void load_meta(const int *__restrict__ grp, int n_exp
 
 // gate_up_pipe: items (k, t) with t over ffn / TRg tiles; an item stages TRg
 // gate rows and TRg up rows of expert list[k], dots every half-slice with
-// each of the expert's tokens (prepared activations xq, read through L2) and
-// writes h[pair][rows] = silu(g) * u.
+// each of the expert's tokens and writes h[pair][rows] = silu(g) * u.  The
+// prepared activations of the expert's first kXsTok tokens are copied into
+// shared memory once per run of items of the same expert (the dot products
+// then read them at shared-memory latency); further tokens are read from xq
+// through L2.
+constexpr int kXsTok = 8;
 template <int QT>
 __global__ void __launch_bounds__(kMoeThreads, 1)
     gate_up_pipe_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
@@ -518,7 +522,8 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     const int ns = slices_per_row(d), xb1 = xbuf_bytes(ns, 1), S = red_stride(ns);
     const long rb = row_bytes_dev(QT, d);
     const int stage_bytes_ = (int)(2 * TRg * rb);
-    float *red = reinterpret_cast<float *>(smem + kStages * stage_bytes_);   // [pair][matrix][row][slice][half]
+    uint8_t *xs = smem + kStages * stage_bytes_;                               // [kXsTok] staged activations
+    float *red = reinterpret_cast<float *>(xs + kXsTok * xb1);                 // [pair][matrix][row][slice][half]
     if (threadIdx.x == 0) {
         for (int st = 0; st < kStages; ++st) mbar_init(&full[st], 1);
         abort_flag = 0;
@@ -549,7 +554,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     if (threadIdx.x == 0)
         for (int i = 0; i < kStages - 1; ++i) issue(i);
     __syncthreads();
-    int done = 0;
+    int done = 0, kprep = -1;
     for (int i = 0;; ++i) {
         const int it = s_item[i % kStages];      // claimed items form a prefix: -1 ends the loop
         if (it < 0) break;
@@ -557,6 +562,16 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
         if (threadIdx.x == 0) issue(i + kStages - 1);
         const int k = it / tiles, t = it - k * tiles;
         const int rows = min(TRg, ffn - t * TRg), np = M.cnt[k];
+        if (k != kprep) {                        // uniform: every thread sees the same item
+            const int nst = min(np, kXsTok), nv = xb1 / 16;
+            for (int v = threadIdx.x; v < nst * nv; v += blockDim.x) {
+                const int j = v / nv, o = v - j * nv;
+                reinterpret_cast<uint4 *>(xs + (size_t)j * xb1)[o] =
+                    __ldcg(reinterpret_cast<const uint4 *>(xq + (size_t)(M.pairs[k][j] / n_act) * xb1) + o);
+            }
+            __syncthreads();
+            kprep = k;
+        }
         const uint8_t *tg = smem + (i % kStages) * stage_bytes_, *tu = tg + TRg * rb;
         const bool ok = mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1), &abort_flag, status);
         done = i + 1;
@@ -568,7 +583,8 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
             WHalf<QT> w;
             if (ok) load_half<QT>((mat ? tu : tg) + (long)sp * SB, hf, w);
             for (int j = 0; j < np; ++j) {
-                const XBuf xj = xbuf_at(const_cast<uint8_t *>(xq) + (size_t)(M.pairs[k][j] / n_act) * xb1, ns);
+                const XBuf xj = j < kXsTok ? xbuf_at(xs + (size_t)j * xb1, ns)
+                                           : xbuf_at(const_cast<uint8_t *>(xq) + (size_t)(M.pairs[k][j] / n_act) * xb1, ns);
                 red[((j * 2 + mat) * TRg + r) * S + 2 * sl + hf] = ok ? dot_half<QT>(w, hf, xj.half(0, sl, hf)) : 0.f;
             }
         }
@@ -1042,10 +1058,11 @@ using namespace q;
 // thread (gate and up together for gate/up), with kStages stages, the
 // reduction buffer and (down) the prepared activations within kPipeSmem
 // bytes of dynamic shared memory.
-constexpr size_t kPipeSmem = 180 * 1024;
+constexpr size_t kPipeSmem = 200 * 1024;
 static size_t gate_up_smem(int qt, int d, int TR, int nb) {
     const int ns = slices_per_row(d);
-    return (size_t)kStages * 2 * TR * row_bytes_dev(qt, d) + (size_t)nb * 2 * TR * red_stride(ns) * 4;
+    return (size_t)kStages * 2 * TR * row_bytes_dev(qt, d) + (size_t)kXsTok * xbuf_bytes(ns, 1) +
+           (size_t)nb * 2 * TR * red_stride(ns) * 4;
 }
 static size_t down_smem(int qt, int ffn, int TR, int nb) {
     const int ns = slices_per_row(ffn);
