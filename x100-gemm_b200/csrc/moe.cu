@@ -480,10 +480,13 @@ struct PipeMeta {            // shared-memory copy of the groups
     int n_active;
     int list[kMaxExp];       // active local experts
     int cnt[kMaxExp];        // pairs per active expert (by list index)
-    int pairs[kMaxExp][kMaxBatch];
+    int start[kMaxExp];      // exclusive prefix of cnt: the expert's first slot
+    uint8_t pairs[kMaxExp][kMaxBatch];   // token * n_act + slot (< kMaxBatch * kMaxAct = 256)
+    uint8_t tok[kMaxExp][kMaxBatch];     // the pair's token
 };
+static_assert(kMaxBatch * kMaxAct <= 256, "pairs are stored as bytes");
 
-__device__ __forceinline__ void load_meta(const int *__restrict__ grp, int n_exp, PipeMeta &M) {
+__device__ __forceinline__ void load_meta(const int *__restrict__ grp, int n_exp, int n_act, PipeMeta &M) {
     if (threadIdx.x == 0) M.n_active = __ldcg(grp + grp_active(n_exp));
     __syncthreads();
     const int na = M.n_active;
@@ -493,9 +496,35 @@ __device__ __forceinline__ void load_meta(const int *__restrict__ grp, int n_exp
         M.cnt[k] = __ldcg(grp + le);
     }
     __syncthreads();
+    if (threadIdx.x < 32) {   // slot starts: warp 0 scans cnt, kMaxExp / 32 entries per lane
+        constexpr int E = kMaxExp / 32;
+        const int l = threadIdx.x;
+        int c[E], run = 0;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            c[i] = E * l + i < na ? M.cnt[E * l + i] : 0;
+            run += c[i];
+        }
+        int incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (l >= o) incl += v;
+        }
+        int base = incl - run;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            if (E * l + i < na) M.start[E * l + i] = base;
+            base += c[i];
+        }
+    }
     for (int t = threadIdx.x; t < na * kMaxBatch; t += blockDim.x) {
         const int k = t / kMaxBatch, j = t - k * kMaxBatch;
-        if (j < M.cnt[k]) M.pairs[k][j] = __ldcg(grp + grp_pairs(n_exp, M.list[k]) + j);
+        if (j < M.cnt[k]) {
+            const int pr = __ldcg(grp + grp_pairs(n_exp, M.list[k]) + j);
+            M.pairs[k][j] = (uint8_t)pr;
+            M.tok[k][j] = (uint8_t)(pr / n_act);
+        }
     }
     __syncthreads();
 }
@@ -531,7 +560,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     }
     pdl_wait();                                  // groups and activations come from the routing kernel
     pdl_launch_dependents();
-    load_meta(grp, n_exp, M);
+    load_meta(grp, n_exp, n_act, M);
     const int tiles = (ffn + TRg - 1) / TRg;
     const int W = M.n_active * tiles;
     int g_next = 0, g_end = 0;                   // thread 0: the claimed chunk not yet issued
@@ -632,7 +661,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
     // The routing kernel finished before the gate/up kernel let this grid
     // launch, so the groups may be read, and weights staged, before waiting
     // for h.
-    load_meta(grp, n_exp, M);
+    load_meta(grp, n_exp, 1, M);
     const int tiles = (d + TRd - 1) / TRd;
     const int W = M.n_active * tiles;
     int g_next = 0, g_end = 0;
@@ -664,7 +693,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
         const int k = it / tiles, t = it - k * tiles;
         const int rows = min(TRd, d - t * TRd), np = M.cnt[k];
         if (k != kprep) {                        // uniform: every thread sees the same item
-            const int *pr = M.pairs[k];
+            const uint8_t *pr = M.pairs[k];
             xprep_rows([h, pr, ffn](int j) { return h + (long)pr[j] * ffn; }, ffn, np, xb);
             __syncthreads();
             kprep = k;
@@ -694,6 +723,309 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
                 mbar_wait_drain(&full[i % kStages], (uint32_t)((i / kStages) & 1), 100000000ull);
         if (done > 0) mbar_wait_drain(&full[(done - 1) % kStages], (uint32_t)(((done - 1) / kStages) & 1), 100000000ull);
     }
+}
+
+// ---- warp-specialised expert kernels (batch > 1) ----------------------------------
+// A producer warp streams the items (active expert k, row tile) into a ring
+// of nst shared-memory stages with bulk copies (full[s] completes on the
+// copied bytes; empty[s] takes one arrival per consumer warp once it has read
+// the stage) and kWsWarps consumer warps compute them; warps wait for one
+// another only through the ring.  A consumer lane owns one half slice of a
+// row (or several, seg apart), unpacks it once (unpack_half) and dots it with
+// every token of the expert; the seg lanes of a row then sum their terms with
+// shuffles.  Expert k's tokens are its slots start[k] .. start[k] + cnt[k] - 1
+// of the grouped h / hq buffers.
+constexpr int kWsWarps = 15;                 // + the producer: 16 warps, 128 registers a thread
+constexpr int kWsThreads = 32 * (kWsWarps + 1);
+constexpr int kWsMaxSt = 4;
+constexpr int kWsTok = 4;                    // tokens dotted per pass over a lane's half slices
+constexpr size_t kWsSmem = 213 * 1024;       // dynamic shared memory (PipeMeta is static)
+
+// lanes per row: the row's 2 ns half slices, at most cap lanes (then a lane
+// takes half slices ls, ls + cap, ...)
+__host__ __device__ inline int ws_seg(int hsr, int cap) { return hsr < cap ? hsr : cap; }
+// top = the largest power of two below seg (0 for seg = 1)
+__host__ __device__ inline int ws_top(int seg) {
+    int top = 1;
+    while (2 * top < seg) top <<= 1;
+    return seg > 1 ? top : 0;
+}
+// sum over the seg lanes of each segment (lanes rr * seg .. rr * seg + seg - 1
+// of the warp); the first lane of a segment receives it.  top = ws_top(seg).
+__device__ __forceinline__ float seg_sum(float v, int ls, int seg, int top) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+        if (off <= top) {
+            const float o = __shfl_down_sync(0xffffffffu, v, off);
+            if (ls + off < seg) v += o;
+        }
+    return v;
+}
+
+// The producer lane's loop, shared by both kernels: claim items in chunks of
+// kGrab from *work, and for each stage wait until the consumers released it,
+// record the item (-1 ends the consumers' loop) and start its copies
+// (fill(stage, item) announces and issues them).  On a timeout it waits for
+// its copies still in flight before returning.
+template <typename Fill>
+__device__ __forceinline__ void ws_produce(int nst, int W, int *work, uint64_t *full, uint64_t *empty, int *s_item,
+                                           volatile int *abort_flag, int *status, Fill fill) {
+    int g_next = 0, g_end = 0, i = 0;
+    for (;; ++i) {
+        const int st = i % nst;
+        if (i >= nst && !mbar_wait(&empty[st], (uint32_t)(((i / nst) - 1) & 1), abort_flag, status)) break;
+        if (g_next == g_end) {
+            g_next = atomicAdd(work, kGrab);
+            g_end = min(g_next + kGrab, W);
+        }
+        const int it = g_next < W ? g_next++ : -1;
+        s_item[st] = it;
+        if (it < 0) {
+            mbar_arrive(&full[st]);
+            return;
+        }
+        fill(st, it);
+    }
+    for (int u = max(0, i - nst); u < i; ++u)   // copies issued but perhaps not landed
+        mbar_wait_drain(&full[u % nst], (uint32_t)((u / nst) & 1), 100000000ull);
+}
+
+// gate / up: an item is (k, TR = kWsWarps * rpw rows of gate and the same
+// rows of up); lanes 0-15 of a warp hold gate, 16-31 up, each half holding
+// rpw rows of seg lanes.  The prepared activations of the batch's nb tokens
+// (xq, token after token) are copied into shared memory once per CTA.
+// Writes h[slot][row] = silu(gate . x) * (up . x) (qwen_moe.c:304-309).
+template <int QT>
+__global__ void __launch_bounds__(kWsThreads, 1)
+    gate_up_ws_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
+                      int n_act, int nb, int nst, const int *__restrict__ grp, const uint8_t *__restrict__ xq,
+                      float *__restrict__ h, int *__restrict__ work, int *status) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ uint64_t full[kWsMaxSt], empty[kWsMaxSt], xbar;
+    __shared__ int s_item[kWsMaxSt];
+    __shared__ int abort_flag;
+    __shared__ PipeMeta M;
+    constexpr int SB = slice_bytes(QT);
+    const int ns = slices_per_row(d), xb1 = xbuf_bytes(ns, 1), hsr = 2 * ns;
+    const long rb = row_bytes_dev(QT, d);
+    const int seg = ws_seg(hsr, 16), rpw = 16 / seg, TR = kWsWarps * rpw;
+    const int stage_b = (int)(2 * TR * rb);
+    uint8_t *xa = smem + (size_t)nst * stage_b;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < nst; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], kWsWarps);
+        }
+        mbar_init(&xbar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    pdl_wait();                                  // groups and activations come from the routing kernel
+    pdl_launch_dependents();
+    load_meta(grp, n_exp, n_act, M);
+    const int tiles = (ffn + TR - 1) / TR, W = M.n_active * tiles;
+    if (warp == kWsWarps) {                      // producer
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&xbar, (uint32_t)(nb * xb1));
+            stage_bytes(xa, xq, (uint32_t)(nb * xb1), &xbar);
+            ws_produce(nst, W, work, full, empty, s_item, &abort_flag, status, [&](int st, int it) {
+                const int k = it / tiles, t = it - k * tiles;
+                const int rows = min(TR, ffn - t * TR);
+                const long r0 = (long)M.list[k] * ffn + (long)t * TR;
+                uint8_t *dst = smem + (size_t)st * stage_b;
+                mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * rows * rb));
+                stage_bytes(dst, gw + r0 * rb, (uint32_t)(rows * rb), &full[st]);
+                stage_bytes(dst + TR * rb, uw + r0 * rb, (uint32_t)(rows * rb), &full[st]);
+            });
+            mbar_wait_drain(&xbar, 0, 100000000ull);
+        }
+        return;
+    }
+    if (!mbar_wait(&xbar, 0, &abort_flag, status)) return;
+    const int mat = lane >> 4, l16 = lane & 15, rr = l16 / seg, ls = l16 - rr * seg, top = ws_top(seg);
+    const int rin = warp * rpw + rr;             // row within the item
+    for (int i = 0;; ++i) {
+        const int st = i % nst;
+        if (!mbar_wait(&full[st], (uint32_t)((i / nst) & 1), &abort_flag, status)) break;
+        const int it = *(volatile int *)&s_item[st];
+        if (it < 0) break;
+        const int k = it / tiles, t = it - k * tiles;
+        const int rows = min(TR, ffn - t * TR), np = M.cnt[k];
+        const bool live = rr < rpw && rin < rows;
+        const uint8_t *wr = smem + (size_t)st * stage_b + (mat ? TR * rb : 0) + (long)rin * rb;
+        for (int j0 = 0; j0 < np; j0 += kWsTok) {   // passes of kWsTok tokens (one for most experts)
+            float a[kWsTok] = {};
+            const uint8_t *xt[kWsTok];
+#pragma unroll
+            for (int jj = 0; jj < kWsTok; ++jj) xt[jj] = xa + (size_t)M.tok[k][min(j0 + jj, np - 1)] * xb1;
+            for (int hq = ls; live && hq < hsr; hq += seg) {
+                UHalf<QT> u;
+                {
+                    WHalf<QT> w;
+                    load_half<QT>(wr + (long)(hq >> 1) * SB, hq & 1, w);
+                    unpack_half<QT>(w, hq & 1, u);
+                }
+                const int xo = (hq >> 1) * kXSlice + (hq & 1) * kXHalf;
+#pragma unroll
+                for (int jj = 0; jj < kWsTok; ++jj)
+                    if (j0 + jj < np) a[jj] += dot_uhalf<QT>(u, reinterpret_cast<const XB *>(xt[jj] + xo));
+            }
+            if (j0 + kWsTok >= np) {             // the last read of this stage
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);
+            }
+#pragma unroll
+            for (int jj = 0; jj < kWsTok; ++jj)
+                if (j0 + jj < np) {
+                    const float g = seg_sum(a[jj], ls, seg, top);
+                    const float u = __shfl_down_sync(0xffffffffu, g, 16);   // the up row's sum
+                    if (mat == 0 && ls == 0 && live)
+                        h[(long)(M.start[k] + j0 + jj) * ffn + t * TR + rin] = swiglu(g, u);
+                }
+        }
+    }
+}
+
+// h of every slot -> the prepared form (xprep_rows) the down kernel dots.
+__global__ void __launch_bounds__(256) prep_slots_kernel(const float *__restrict__ h, int ffn, uint8_t *__restrict__ hq) {
+    pdl_wait();                                  // h comes from the gate / up kernel
+    pdl_launch_dependents();
+    const int p = blockIdx.x, ns = slices_per_row(ffn);
+    xprep_rows([h, p, ffn](int) { return h + (long)p * ffn; }, ffn, 1, xbuf_at(hq + (size_t)p * xbuf_bytes(ns, 1), ns));
+}
+
+// down: an item is (k, TR = kWsWarps * rpw rows of down); a stage holds the
+// rows and the expert's prepared h (its slots, contiguous in hq).  Writes
+// the unweighted part[pair][row] for the combine.  The weights of the first
+// stages are requested before the dependency wait (the groups are final once
+// this kernel runs: the gate / up kernel read them behind its own wait).
+template <int QT>
+__global__ void __launch_bounds__(kWsThreads, 1)
+    down_ws_kernel(const uint8_t *__restrict__ dw, int ffn, int d, int n_exp, int nb, int nst,
+                   const int *__restrict__ grp, const uint8_t *__restrict__ hq, float *__restrict__ part,
+                   int *__restrict__ work, int *status) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ uint64_t full[kWsMaxSt], empty[kWsMaxSt];
+    __shared__ int s_item[kWsMaxSt];
+    __shared__ int abort_flag;
+    __shared__ PipeMeta M;
+    constexpr int SB = slice_bytes(QT);
+    const int ns = slices_per_row(ffn), xb1 = xbuf_bytes(ns, 1), hsr = 2 * ns;
+    const long rb = row_bytes_dev(QT, ffn);
+    const int seg = ws_seg(hsr, 32), rpw = 32 / seg, TR = kWsWarps * rpw;
+    const int wbytes = (int)(TR * rb), stage_b = wbytes + nb * xb1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < nst; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], kWsWarps);
+        }
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    load_meta(grp, n_exp, 1, M);
+    const int tiles = (d + TR - 1) / TR, W = M.n_active * tiles;
+    if (warp == kWsWarps) {                      // producer
+        if (lane == 0) {
+            int nfill = 0;                       // stages whose h copies wait for the dependency
+            int pend_st[kWsMaxSt], pend_k[kWsMaxSt];
+            ws_produce(nst, W, work, full, empty, s_item, &abort_flag, status, [&](int st, int it) {
+                const int k = it / tiles, t = it - k * tiles;
+                const int rows = min(TR, d - t * TR);
+                uint8_t *dst = smem + (size_t)st * stage_b;
+                mbar_arrive_expect_tx(&full[st], (uint32_t)(rows * rb + M.cnt[k] * xb1));
+                stage_bytes(dst, dw + ((long)M.list[k] * d + (long)t * TR) * rb, (uint32_t)(rows * rb), &full[st]);
+                if (nfill >= 0 && nfill < nst) {  // still before the dependency wait
+                    pend_st[nfill] = st;
+                    pend_k[nfill] = k;
+                    if (++nfill == nst) {
+                        pdl_wait();              // hq comes from the preparation kernel
+                        for (int f = 0; f < nst; ++f)
+                            stage_bytes(smem + (size_t)pend_st[f] * stage_b + wbytes,
+                                        hq + (size_t)M.start[pend_k[f]] * xb1, (uint32_t)(M.cnt[pend_k[f]] * xb1),
+                                        &full[pend_st[f]]);
+                        nfill = -1;
+                    }
+                    return;
+                }
+                stage_bytes(dst + wbytes, hq + (size_t)M.start[k] * xb1, (uint32_t)(M.cnt[k] * xb1), &full[st]);
+            });
+            if (nfill > 0) {                     // fewer items than stages
+                pdl_wait();
+                for (int f = 0; f < nfill; ++f)
+                    stage_bytes(smem + (size_t)pend_st[f] * stage_b + wbytes, hq + (size_t)M.start[pend_k[f]] * xb1,
+                                (uint32_t)(M.cnt[pend_k[f]] * xb1), &full[pend_st[f]]);
+            }
+            if (nfill != -1) pdl_wait();
+        }
+        pdl_launch_dependents();
+        return;
+    }
+    pdl_launch_dependents();
+    const int rr = lane / seg, ls = lane - rr * seg, top = ws_top(seg);
+    const int rin = warp * rpw + rr;
+    for (int i = 0;; ++i) {
+        const int st = i % nst;
+        if (!mbar_wait(&full[st], (uint32_t)((i / nst) & 1), &abort_flag, status)) break;
+        const int it = *(volatile int *)&s_item[st];
+        if (it < 0) break;
+        const int k = it / tiles, t = it - k * tiles;
+        const int rows = min(TR, d - t * TR), np = M.cnt[k];
+        const bool live = rr < rpw && rin < rows;
+        const uint8_t *wr = smem + (size_t)st * stage_b + (long)rin * rb;
+        const uint8_t *xh = smem + (size_t)st * stage_b + wbytes;   // the expert's slots, xb1 apart
+        for (int j0 = 0; j0 < np; j0 += kWsTok) {
+            float a[kWsTok] = {};
+            for (int hq2 = ls; live && hq2 < hsr; hq2 += seg) {
+                UHalf<QT> u;
+                {
+                    WHalf<QT> w;
+                    load_half<QT>(wr + (long)(hq2 >> 1) * SB, hq2 & 1, w);
+                    unpack_half<QT>(w, hq2 & 1, u);
+                }
+                const uint8_t *xo = xh + (size_t)j0 * xb1 + (hq2 >> 1) * kXSlice + (hq2 & 1) * kXHalf;
+#pragma unroll
+                for (int jj = 0; jj < kWsTok; ++jj)
+                    if (j0 + jj < np) a[jj] += dot_uhalf<QT>(u, reinterpret_cast<const XB *>(xo + (size_t)jj * xb1));
+            }
+            if (j0 + kWsTok >= np) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);
+            }
+#pragma unroll
+            for (int jj = 0; jj < kWsTok; ++jj)
+                if (j0 + jj < np) {
+                    const float v = seg_sum(a[jj], ls, seg, top);
+                    if (ls == 0 && live) part[(long)M.pairs[k][j0 + jj] * d + t * TR + rin] = v;
+                }
+        }
+    }
+}
+
+// Launch shape of the warp-specialised kernels: stages and staged tokens.
+struct WsPlan {
+    int nst = 0;
+    size_t smem = 0;
+};
+static WsPlan ws_plan_gate_up(int qt, int d, int batch) {
+    const int ns = slices_per_row(d), seg = ws_seg(2 * ns, 16), TR = kWsWarps * (16 / seg);
+    const size_t stage = 2 * (size_t)TR * row_bytes_dev(qt, d), xb1 = xbuf_bytes(ns, 1);
+    WsPlan p;   // the deepest ring that leaves room for every token (none: the pipelined kernels)
+    const size_t xs = (size_t)batch * xb1;
+    if (xs < kWsSmem) p.nst = (int)std::min<size_t>(kWsMaxSt, (kWsSmem - xs) / stage);
+    if (p.nst < 2) p.nst = 0;
+    if (p.nst) p.smem = p.nst * stage + xs;
+    return p;
+}
+static WsPlan ws_plan_down(int qt, int ffn, int batch) {
+    const int ns = slices_per_row(ffn), seg = ws_seg(2 * ns, 32), TR = kWsWarps * (32 / seg);
+    const size_t stage = (size_t)TR * row_bytes_dev(qt, ffn) + (size_t)batch * xbuf_bytes(ns, 1);
+    WsPlan p;
+    p.nst = (int)std::min<size_t>(kWsMaxSt, kWsSmem / stage);
+    if (p.nst < 2) p.nst = 0;
+    if (p.nst) p.smem = p.nst * stage;
+    return p;
 }
 
 // combine: eout[token][n] = sum over the token's local slots, in slot order,
@@ -1130,6 +1462,9 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
         set_qkernel_attrs(route_group_kernel);
         set_qkernel_attrs(gate_up_pipe_kernel<QT>, (int)kPipeSmem);
         set_qkernel_attrs(down_pipe_kernel<QT>, (int)kPipeSmem);
+        set_qkernel_attrs(gate_up_ws_kernel<QT>, (int)kWsSmem);
+        set_qkernel_attrs(down_ws_kernel<QT>, (int)kWsSmem);
+        set_qkernel_attrs(prep_slots_kernel);
         set_qkernel_attrs(combine_kernel);
         set_qkernel_attrs(moe_fused_kernel<QT>, 220 * 1024);
         attr[c->device] = true;
@@ -1169,16 +1504,31 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
     st = launch_pdl(route_group_kernel, dim3(batch), dim3(kMoeThreads), 0, s, L.d, L.n_exp, L.n_act, L.lo, L.hi, hn,
                     (const float *)S.logits, S.sel, S.w, S.grp, S.xq, S.cnt + 1);
     if (st) return st;
-    const int TRg = gate_up_rows_per_cta(QT, L.d), TRd = down_rows_per_cta(QT, L.ffn);
     const int G = c->sm_count;   // persistent: one CTA per SM
-    st = launch_pdl(gate_up_pipe_kernel<QT>, dim3(G), dim3(kMoeThreads), gate_up_smem(QT, L.d, TRg, batch), s,
-                    (const uint8_t *)L.gate.w, (const uint8_t *)L.up.w, L.ffn, L.d, L.n_exp, L.n_act, TRg,
-                    (const int *)S.grp, (const uint8_t *)S.xq, S.h, S.cnt + 1, c->d_status);
-    if (st) return st;
-    st = launch_pdl(down_pipe_kernel<QT>, dim3(G), dim3(kMoeThreads), down_smem(QT, L.ffn, TRd, batch), s,
-                    (const uint8_t *)L.down.w, L.ffn, L.d, L.n_exp, TRd, batch, (const int *)S.grp,
-                    (const float *)S.h, S.part, S.cnt + 2, c->d_status);
-    if (st) return st;
+    static const bool no_ws = getenv("X100_MOE_NO_WS") != nullptr;
+    const WsPlan pg = ws_plan_gate_up(QT, L.d, batch), pd = ws_plan_down(QT, L.ffn, batch);
+    if (pg.nst && pd.nst && !no_ws) {
+        st = launch_pdl(gate_up_ws_kernel<QT>, dim3(G), dim3(kWsThreads), pg.smem, s, (const uint8_t *)L.gate.w,
+                        (const uint8_t *)L.up.w, L.ffn, L.d, L.n_exp, L.n_act, batch, pg.nst, (const int *)S.grp,
+                        (const uint8_t *)S.xq, S.h, S.cnt + 1, c->d_status);
+        if (st) return st;
+        st = launch_pdl(prep_slots_kernel, dim3(batch * L.n_act), dim3(256), 0, s, (const float *)S.h, L.ffn, S.hq);
+        if (st) return st;
+        st = launch_pdl(down_ws_kernel<QT>, dim3(G), dim3(kWsThreads), pd.smem, s, (const uint8_t *)L.down.w, L.ffn,
+                        L.d, L.n_exp, batch, pd.nst, (const int *)S.grp, (const uint8_t *)S.hq, S.part, S.cnt + 2,
+                        c->d_status);
+        if (st) return st;
+    } else {
+        const int TRg = gate_up_rows_per_cta(QT, L.d), TRd = down_rows_per_cta(QT, L.ffn);
+        st = launch_pdl(gate_up_pipe_kernel<QT>, dim3(G), dim3(kMoeThreads), gate_up_smem(QT, L.d, TRg, batch), s,
+                        (const uint8_t *)L.gate.w, (const uint8_t *)L.up.w, L.ffn, L.d, L.n_exp, L.n_act, TRg,
+                        (const int *)S.grp, (const uint8_t *)S.xq, S.h, S.cnt + 1, c->d_status);
+        if (st) return st;
+        st = launch_pdl(down_pipe_kernel<QT>, dim3(G), dim3(kMoeThreads), down_smem(QT, L.ffn, TRd, batch), s,
+                        (const uint8_t *)L.down.w, L.ffn, L.d, L.n_exp, TRd, batch, (const int *)S.grp,
+                        (const float *)S.h, S.part, S.cnt + 2, c->d_status);
+        if (st) return st;
+    }
     return launch_pdl(combine_kernel, dim3((L.d + 255) / 256, batch), dim3(256), 0, s, L.d, L.n_act, L.lo, L.hi,
                       (const int *)S.sel, (const float *)S.w, (const float *)S.part, eout, accum);
 }
@@ -1358,7 +1708,8 @@ size_t moe_scratch_bytes(int d, int n_exp, int n_act, int ffn) {
     b += (size_t)(2 * n_exp + 1 + n_exp * kMaxBatch) * 4;             // groups
     b += (size_t)kMaxBatch * xbuf_bytes(slices_per_row(d), 1);        // prepared activations
     b += (size_t)kMaxBatch * n_act * d * 4;                           // partial outputs
-    b += 256 * 10;                                                    // alignment, ticket, counter
+    b += (size_t)kMaxBatch * n_act * xbuf_bytes(slices_per_row(ffn), 1);   // prepared h per slot
+    b += 256 * 11;                                                    // alignment, ticket, counter
     return b;
 }
 
@@ -1380,6 +1731,7 @@ MoeScratch moe_scratch_carve(void *base, int d, int n_exp, int n_act, int ffn) {
     S.grp = static_cast<int *>(take((size_t)(2 * n_exp + 1 + n_exp * kMaxBatch) * 4));
     S.xq = static_cast<uint8_t *>(take((size_t)kMaxBatch * xbuf_bytes(slices_per_row(d), 1)));
     S.part = static_cast<float *>(take((size_t)kMaxBatch * n_act * d * 4));
+    S.hq = static_cast<uint8_t *>(take((size_t)kMaxBatch * n_act * xbuf_bytes(slices_per_row(ffn), 1)));
     return S;
 }
 

@@ -41,6 +41,7 @@ struct MoeScratch {
     int *grp = nullptr;
     uint8_t *xq = nullptr;   // prepared activations, one token after the other
     float *part = nullptr;
+    uint8_t *hq = nullptr;   // prepared h of the (expert, token) slots, slot after slot
 };
 
 bool moe_shapes_ok(int d, int n_exp, int n_act, int ffn, int qtype);

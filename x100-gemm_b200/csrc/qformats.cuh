@@ -267,6 +267,118 @@ template <> __device__ __forceinline__ float dot_half<Q3_K>(const WHalf<Q3_K> &w
     return acc;
 }
 
+// ---- half a slice unpacked once for many tokens ----------------------------------------------
+// UHalf holds a half slice with its weight bytes already in dp4a form and
+// its scales decoded, so a kernel that dots the same weights with several
+// tokens pays the unpacking once; dot_uhalf(u, x) evaluates exactly the
+// expression of dot_half(w, h, x) (same operations, same order).
+template <int QT> struct UHalf;
+template <> struct UHalf<Q4_0> { uint4 lo[4], hi[4]; float d[4]; };
+template <> struct UHalf<Q8_0> { uint4 q[8]; float d[4]; };
+template <> struct UHalf<Q4_K> { uint4 lo[4], hi[4]; float ds[4], dm[4]; };   // sub-blocks 4h .. 4h+3
+template <> struct UHalf<Q3_K> { uint4 v[4][2]; float s[4][2]; };             // [j][lh]
+
+template <int QT> __device__ __forceinline__ void unpack_half(const WHalf<QT> &w, int h, UHalf<QT> &u);
+template <> __device__ __forceinline__ void unpack_half<Q4_0>(const WHalf<Q4_0> &w, int h, UHalf<Q4_0> &u) {
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        u.lo[b] = nib_lo(w.q[b]);
+        u.hi[b] = nib_hi(w.q[b]);
+        const uint32_t dw = u4_word(w.dh, 2 * h + (b >> 1));
+        u.d[b] = (b & 1) ? half_hi(dw) : half_lo(dw);
+    }
+}
+template <> __device__ __forceinline__ void unpack_half<Q8_0>(const WHalf<Q8_0> &w, int h, UHalf<Q8_0> &u) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) u.q[i] = w.q[i];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const uint32_t dw = u4_word(w.dh, 2 * h + (b >> 1));
+        u.d[b] = (b & 1) ? half_hi(dw) : half_lo(dw);
+    }
+}
+template <> __device__ __forceinline__ void unpack_half<Q4_K>(const WHalf<Q4_K> &w, int h, UHalf<Q4_K> &u) {
+    const float d = half_lo(w.hdr.x), dmin = half_hi(w.hdr.x);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        u.lo[i] = nib_lo(w.q[i]);
+        u.hi[i] = nib_hi(w.q[i]);
+    }
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * h + cc;
+        int sc0, m0, sc1, m1;
+        kq_scale_min(2 * c, w.hdr.y, w.hdr.z, w.hdr.w, sc0, m0);
+        kq_scale_min(2 * c + 1, w.hdr.y, w.hdr.z, w.hdr.w, sc1, m1);
+        u.ds[2 * cc] = d * (float)sc0;
+        u.dm[2 * cc] = dmin * (float)m0;
+        u.ds[2 * cc + 1] = d * (float)sc1;
+        u.dm[2 * cc + 1] = dmin * (float)m1;
+    }
+}
+template <> __device__ __forceinline__ void unpack_half<Q3_K>(const WHalf<Q3_K> &w, int h, UHalf<Q3_K> &u) {
+    const float d = half_lo(w.hdr.w);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int hs = 4 * h + j;
+#pragma unroll
+        for (int lh = 0; lh < 2; ++lh) {
+            const uint4 q = w.q[lh], hm = w.hm[lh];
+            uint4 vv;
+            vv.x = ((q.x >> (2 * j)) & 0x03030303u) | (((hm.x >> hs) & 0x01010101u) << 2);
+            vv.y = ((q.y >> (2 * j)) & 0x03030303u) | (((hm.y >> hs) & 0x01010101u) << 2);
+            vv.z = ((q.z >> (2 * j)) & 0x03030303u) | (((hm.z >> hs) & 0x01010101u) << 2);
+            vv.w = ((q.w >> (2 * j)) & 0x03030303u) | (((hm.w >> hs) & 0x01010101u) << 2);
+            u.v[j][lh] = vv;
+            u.s[j][lh] = d * (float)q3k_scale(8 * h + 2 * j + lh, w.hdr.x, w.hdr.y, w.hdr.z);
+        }
+    }
+}
+
+template <int QT> __device__ __forceinline__ float dot_uhalf(const UHalf<QT> &u, const XB *x);
+template <> __device__ __forceinline__ float dot_uhalf<Q4_0>(const UHalf<Q4_0> &u, const XB *x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const XB &xb = x[b];
+        const int dot = dot16_u(u.lo[b], xb.h0, xb.l0) + dot16_u(u.hi[b], xb.h1, xb.l1);
+        acc += u.d[b] * (xb.f.x * (float)dot - 8.0f * xb.f.y);
+    }
+    return acc;
+}
+template <> __device__ __forceinline__ float dot_uhalf<Q8_0>(const UHalf<Q8_0> &u, const XB *x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const XB &xb = x[b];
+        const int dot = dot16_s(u.q[2 * b], xb.h0, xb.l0) + dot16_s(u.q[2 * b + 1], xb.h1, xb.l1);
+        acc += u.d[b] * (xb.f.x * (float)dot);
+    }
+    return acc;
+}
+template <> __device__ __forceinline__ float dot_uhalf<Q4_K>(const UHalf<Q4_K> &u, const XB *x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+        const XB &xa = x[2 * cc], &xb = x[2 * cc + 1];
+        const int da = dot16_u(u.lo[2 * cc], xa.h0, xa.l0) + dot16_u(u.lo[2 * cc + 1], xa.h1, xa.l1);
+        const int db = dot16_u(u.hi[2 * cc], xb.h0, xb.l0) + dot16_u(u.hi[2 * cc + 1], xb.h1, xb.l1);
+        acc += u.ds[2 * cc] * (xa.f.x * (float)da) - u.dm[2 * cc] * xa.f.y;
+        acc += u.ds[2 * cc + 1] * (xb.f.x * (float)db) - u.dm[2 * cc + 1] * xb.f.y;
+    }
+    return acc;
+}
+template <> __device__ __forceinline__ float dot_uhalf<Q3_K>(const UHalf<Q3_K> &u, const XB *x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const XB &xb = x[j];
+        const int d0 = dot16_u(u.v[j][0], xb.h0, xb.l0), d1 = dot16_u(u.v[j][1], xb.h1, xb.l1);
+        acc += u.s[j][0] * (xb.f.x * (float)d0 - 4.0f * xb.f.z) + u.s[j][1] * (xb.f.x * (float)d1 - 4.0f * xb.f.w);
+    }
+    return acc;
+}
+
 // ---- activation preparation -----------------------------------------------------------
 // Eight consecutive threads (t = lane % 8) convert one 32-element block, held
 // as one float4 per thread, into *o.  Every lane of the warp calls it
