@@ -736,7 +736,8 @@ def bench_moe(args, dist, peaks, peak_src):
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(f"moe_b{B}"),
                      "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)",
                      "kernel": ("router_logits + moe_fused (2 launches per call)" if B == 1 else
-                                "router_logits + route_group + gate_up_pipe + down_pipe + combine (5 launches per call)"),
+                                "router_logits + route_group + gate_up_ws + prep_slots + down_ws + combine "
+                                "(6 launches per call)"),
                      "algorithmic_bytes_per_call": round(sum(alg_call) / PER),
                      "expert_union_mean": round(sum(unions) / PER, 2),
                      "bytes_rule": "U * 2654208 (distinct experts of the call's tokens) + 1048576 router + "
@@ -747,7 +748,7 @@ def bench_moe(args, dist, peaks, peak_src):
         "e2e": {"value": round(e2e_steps * B / dt, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": 4 * B * d, "d2h_bytes_per_step": 4 * B * d,
                 "api": "x100q_moe_ffn(moe, hn, eout, batch) with pinned host hn, eout (synchronous)"},
-        "gpu_launches": calls * ((2 if B == 1 else 5) + (1 if ep is not None else 0)),
+        "gpu_launches": calls * ((2 if B == 1 else 6) + (1 if ep is not None else 0)),
         "cpu_baseline": cpu,
     }
 
@@ -835,8 +836,8 @@ def bench_decode(args, dist, peaks, peak_src):
     ep = dist.ep_group(B * d) if world > 1 and args.combine == "p2p" else None
     # launches per step: embed, head, and per layer qkv GEMV, attention, Wo GEMV
     # (two launches above 8 tokens: its 4096-wide activations of 16 tokens
-    # exceed one CTA's shared memory) and the MoE kernels (2 fused, 5 grouped)
-    launches = 2 + NL * (3 + (1 if B <= 8 else 2) + (2 if B == 1 else 5) + (1 if ep is not None else 0))
+    # exceed one CTA's shared memory) and the MoE kernels (2 fused, 6 grouped)
+    launches = 2 + NL * (3 + (1 if B <= 8 else 2) + (2 if B == 1 else 6) + (1 if ep is not None else 0))
 
     def step():
         if world == 1:
@@ -935,6 +936,19 @@ def bench_decode(args, dist, peaks, peak_src):
         e2e = {"value": round(n_e2e * B / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8 * B,
                "d2h_bytes_per_step": 4 * B * V,
                "api": "x100q_model_forward(model, tokens, pos, logits, batch) with host tokens/pos/logits"}
+    # per-bucket step times (x100q_model_timing: the reference's decode buckets,
+    # qwen_moe_q3k.c:910-941), from a few eager steps after the timed ones
+    buckets = None
+    if world == 1:
+        m.timing(True)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+        tms, tsteps = m.timing_read()
+        m.timing(False)
+        buckets = {k: round(v / tsteps, 4) for k, v in tms.items()}
+        buckets["sum"] = round(sum(tms.values()) / tsteps, 4)
     return {
         "metric": "decode tokens/s (48-layer Qwen3-30B-A3B-shaped step)", "value": round(tok_s, 2),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -955,6 +969,9 @@ def bench_decode(args, dist, peaks, peak_src):
                      "kernel": "whole step (qgemv, attn_decode, router, moe kernels)",
                      "algorithmic_bytes_per_step": step_bytes,
                      "expert_union_mean": round(float(np.mean(union)), 2), "parity_rel_l2_layer0": err},
+        "buckets_ms_per_step": buckets,
+        "buckets_note": "x100q_model_timing over 3 eager steps (events at bucket boundaries serialise the "
+                        "kernels around them, so the sum exceeds ms_per_step slightly)",
         "clocks": clocks,
         "e2e": e2e,
         "gpu_launches": launches * args.steps,
@@ -962,10 +979,34 @@ def bench_decode(args, dist, peaks, peak_src):
     }
 
 
+def prefill_launches(n, NL, chunk=1024, max_batch=16, ctx=4096, kc=64):
+    """Kernel launches of one x100q_model_prefill of n tokens at positions 0 ..
+    n-1 without logits (decode.cu prefill_chunk_tc): per chunk the embedding,
+    and per layer the q/k/v linear (split + GEMM), the k/v cache write, the
+    attention groups (attention + split merge each; groups sized as the
+    library sizes them), the Wo linear (split + GEMM) and the MoE (split,
+    router, count, scatter, gate/up GEMM, swiglu split, down GEMM, combine)."""
+    cap = max_batch * ((ctx + kc - 1) // kc)
+    total = 0
+    for c0 in range(0, n, chunk):
+        T = min(chunk, n - c0)
+        attn, g0 = 0, 0
+        while g0 < T:
+            gb = T - g0
+            nsp = (c0 + g0 + gb - 1 + kc) // kc
+            while gb > 1 and gb * nsp > cap:
+                gb = max(1, cap // nsp if cap // nsp < gb else gb - 1)
+                nsp = (c0 + g0 + gb - 1 + kc) // kc
+            attn += 1 + (1 if nsp > 1 else 0)
+            g0 += gb
+        total += 1 + NL * (2 + 1 + attn + 2 + 8)
+    return total
+
+
 def bench_prefill(args, dist, peaks, peak_src):
     """Prefill of a prompt into one sequence of the config-5 model (48 layers,
     Q8_0 attention, 128 Q3_K experts, fp16 KV cache of 4096): x100q_model_prefill
-    with n tokens > max_batch, the chunked tensor-core path (chunks of 256
+    with n tokens > max_batch, the chunked tensor-core path (chunks of 1024
     tokens: the q/k/v, Wo and expert linears as tcgen05 dequant GEMMs, the
     experts grouped by the chunk's routing).  One step = one prefill of the
     whole prompt at positions 0 .. n-1 of slot 0, without logits (a prompt's
@@ -1032,7 +1073,7 @@ def bench_prefill(args, dist, peaks, peak_src):
         "clocks": clocks,
         "e2e": {"value": round(tok_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 0,
                 "api": "x100q_model_prefill(model, slot, tokens, n, pos0, NULL) with pinned host tokens"},
-        "gpu_launches": None,
+        "gpu_launches": prefill_launches(n, NL) * args.steps,
         "cpu_baseline": None,
     }
 

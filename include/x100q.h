@@ -249,11 +249,48 @@ int x100q_model_forward(x100q_model *m, const int *tokens, const int *pos,
  * nothing and makes the next synchronising call report X100_E_ARG.          */
 int x100q_model_forward_slots_dev(x100q_model *m, const int *tokens, float *h, const int *pos,
                                   const int *slot, float *logits, int batch, void *stream);
-/* Prefill: the reference's prefill_chunk4 (qwen_moe_hp.c:1748-1858) for n
- * (1 <= n <= max_batch) tokens -- tokens[0 .. n) of the sequence in `slot`
- * at positions pos0 .. pos0 + n - 1 in one step, their k and v left in the
- * cache; logits [n][vocab] (host, or NULL for none).  Synchronous.          */
+/* Prefill: the reference's prefill_chunk4 (qwen_moe_hp.c:1748-1858) for
+ * n >= 1 tokens -- tokens[0 .. n) of the sequence in `slot` at positions
+ * pos0 .. pos0 + n - 1 (pos0 + n <= ctx), their k and v left in the cache;
+ * logits [n][vocab] (host, or NULL for none).  Up to max_batch tokens run as
+ * one decode step; more run in chunks (1024 tokens, X100_PREFILL_CHUNK
+ * overrides, 32 .. 4096) whose linear layers are tensor-core GEMMs over all
+ * the chunk's tokens.  Synchronous.                                         */
 int x100q_model_prefill(x100q_model *m, int slot, const int *tokens, int n, int pos0, float *logits);
+
+/* ---- per-bucket step timing ------------------------------------------------ */
+/* The reference's decode-step buckets (qwen_moe_q3k.c:910-941, printed per
+ * token at :2295-2327: act-pack, linear {qkv, o, expert, lm_head},
+ * attention, rope+qknorm, router, swiglu, rest) at this library's kernel
+ * boundaries.  Activation packing is fused into each linear's kernel,
+ * rope + q/k norm into the attention kernel and swiglu into the expert
+ * kernels, so those time under their hosts:
+ *   EMBED    token embedding
+ *   QKV      rmsnorm + packing + the q/k/v linear
+ *   ATTN     k/v cache write, q/k norm, rope, attention, split merge
+ *   O        the output linear (+ residual)
+ *   ROUTER   rmsnorm + router logits + top-k (+ grouping at batch > 1)
+ *   EXPERT   gate / up / swiglu / down of the routed experts
+ *   COMBINE  weighted sum of the experts' outputs into the residual
+ *   LM       final rmsnorm + lm_head
+ * x100q_model_timing(m, 1) clears the totals and starts timing; every
+ * forward call (x100q_model_forward, _forward_dev, _forward_slots_dev and
+ * _layer_dev) then records a CUDA event at each bucket boundary (which
+ * serialises the kernels on either side, so the sum runs a little above an
+ * untimed step), and x100q_model_timing(m, 0) stops.  Calls made while the
+ * stream is being captured into a graph record nothing.
+ * x100q_model_timing_read waits for the recorded events and writes the
+ * totals since the start, in milliseconds, to ms[X100Q_NBUCKETS] and the
+ * number of timed calls to *steps (either may be NULL).                    */
+enum {
+    X100Q_T_EMBED = 0, X100Q_T_QKV, X100Q_T_ATTN, X100Q_T_O, X100Q_T_ROUTER,
+    X100Q_T_EXPERT, X100Q_T_COMBINE, X100Q_T_LM, X100Q_NBUCKETS
+};
+int x100q_model_timing(x100q_model *m, int on);
+int x100q_model_timing_read(x100q_model *m, double *ms, long *steps);
+/* "embed", "qkv", "attention", "o", "router", "expert", "combine", "lm";
+ * NULL out of range.                                                        */
+const char *x100q_timing_bucket_name(int bucket);
 
 /* ---- expert-parallel combine over peer memory ------------------------------ */
 /* With experts split over `world` processes (one per GPU, x100q_moe_create

@@ -95,3 +95,17 @@ def test_quant_create_without_device_fails_cleanly():
         {"CUDA_VISIBLE_DEVICES": ""})
     null, code = map(int, out.split())
     assert null == 1 and code == x100b.X100_E_NODEV
+
+
+def test_step_timing_buckets_named_and_checked():
+    """The timing buckets follow the header's enum order; a null model is an
+    argument error (no device touched)."""
+    src = open(os.path.join(os.path.dirname(x100b.LIB_PATH), "..", "include", "x100q.h")).read()
+    a = src.index("X100Q_T_EMBED = 0")
+    enum = src[a:src.index("X100Q_NBUCKETS", a)]
+    assert enum.count("X100Q_T_") == x100b.TIMING_BUCKETS
+    names = [x100b.timing_bucket_name(i) for i in range(x100b.TIMING_BUCKETS)]
+    assert names == ["embed", "qkv", "attention", "o", "router", "expert", "combine", "lm"]
+    assert x100b.timing_bucket_name(-1) is None and x100b.timing_bucket_name(x100b.TIMING_BUCKETS) is None
+    L = x100b.lib()
+    assert L.x100q_model_timing(None, 1) == 1 and L.x100q_model_timing_read(None, None, None) == 1

@@ -160,6 +160,42 @@ def test_forward_dev_equals_layer_by_layer(world):
     assert torch.equal(h1, h2) and torch.equal(l1, l2)
 
 
+@pytest.mark.parametrize("B", [1, 4])
+def test_step_timing_buckets(world, B):
+    """Per-bucket timing (the reference's decode buckets, qwen_moe_q3k.c:
+    910-941): timing leaves the results bit-identical, counts the calls,
+    charges every layer bucket, and its buckets sum to about the wall time of
+    the timed calls (the events serialise the kernels around each boundary,
+    so the sum may exceed an untimed step, never the timed wall time)."""
+    import time
+    c, m = world["c"], world["model"]
+    toks = np.arange(B, dtype=np.int32) + 5
+    pos = np.arange(B, dtype=np.int32) * 7 + 30
+    load_kv(world)
+    ref = m.forward(toks, pos)
+    m.timing(True)
+    t0 = time.perf_counter()
+    for _ in range(3):
+        load_kv(world)
+        got = m.forward(toks, pos)
+        assert np.array_equal(got, ref)
+    wall = (time.perf_counter() - t0) * 1e3
+    ms, steps = m.timing_read()
+    m.timing(False)
+    assert steps == 3
+    assert list(ms) == ["embed", "qkv", "attention", "o", "router", "expert", "combine", "lm"]
+    for b in ("embed", "qkv", "attention", "o", "router", "expert", "lm"):
+        assert ms[b] > 0, (b, ms)
+    if B > 1:   # batch 1 fuses routing's top-k, the experts and the combine into one kernel
+        assert ms["combine"] > 0, ms
+    assert 0 < sum(ms.values()) <= wall, (ms, wall)
+    # stopped: further calls add nothing
+    load_kv(world)
+    m.forward(toks, pos)
+    ms2, steps2 = m.timing_read()
+    assert steps2 == 3 and ms2 == ms
+
+
 def test_expert_parallel_split_sums_to_full(world):
     """Two handles holding experts [0, 16) and [16, 32): h + eout_a + eout_b
     equals the full layer (the sum an NCCL all-reduce of eout forms)."""

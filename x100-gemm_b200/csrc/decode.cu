@@ -442,8 +442,60 @@ struct ModelLayer {
     bool set = false;
 };
 
+// Per-bucket step timing (x100q_model_timing): a CUDA event at each bucket
+// boundary of a forward call; the interval from event i to event i + 1 is
+// charged to bucket[i] (-1: not charged, the gap between calls).
+struct StepTimer {
+    bool on = false;
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> bucket;
+    int used = 0;
+    double ms[X100Q_NBUCKETS] = {};
+    long steps = 0;
+};
+static void timer_flush(StepTimer &t) {
+    if (t.used >= 2 && cudaEventSynchronize(t.ev[t.used - 1]) == cudaSuccess)
+        for (int i = 0; i + 1 < t.used; ++i) {
+            float ms = 0.f;
+            if (t.bucket[i] >= 0 && cudaEventElapsedTime(&ms, t.ev[i], t.ev[i + 1]) == cudaSuccess)
+                t.ms[t.bucket[i]] += ms;
+        }
+    cudaGetLastError();
+    t.used = 0;
+}
+// Start bucket b (-1: end of a call) on stream s.
+static void timer_mark(StepTimer &t, int b, cudaStream_t s) {
+    if (!t.on) return;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return;
+    }
+    if (t.used >= 4096) {   // keep the pool bounded: settle what is recorded, keep the open interval
+        const int last = t.bucket[t.used - 1];
+        timer_flush(t);
+        if (last >= 0) timer_mark(t, last, s);
+    }
+    if (t.used == (int)t.ev.size()) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) {
+            cudaGetLastError();
+            return;
+        }
+        t.ev.push_back(e);
+        t.bucket.push_back(-1);
+    }
+    if (cudaEventRecord(t.ev[t.used], s) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    t.bucket[t.used++] = b;
+}
+static void timer_mark_cb(void *ctx, int b, cudaStream_t s) { timer_mark(*static_cast<StepTimer *>(ctx), b, s); }
+
 struct x100q_model {
     int device = 0;
+    StepTimer timer;
     x100q_model_cfg cfg;
     std::vector<ModelLayer> layers;
     float *tok_embd = nullptr, *out_norm = nullptr;
@@ -559,6 +611,7 @@ void x100q_model_destroy(x100q_model *m) {
     cudaFree(m->scratch);
     cudaFree(m->moe_scratch);
     cudaFree(m->pf_base);
+    for (cudaEvent_t e : m->timer.ev) cudaEventDestroy(e);
     delete m;
 }
 
@@ -729,6 +782,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
         attr[c->device] = true;
     }
     // 1. qkv = Wqkv . rmsnorm(h)
+    timer_mark(m->timer, X100Q_T_QKV, s);
     GemvOpts o1;
     o1.norm_w = L.norms;
     o1.eps = g.eps;
@@ -760,6 +814,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     a.prewritten = slot ? 1 : 0;
     a.att = m->att;
     a.status = c->d_status;
+    timer_mark(m->timer, X100Q_T_ATTN, s);
     if (slot) {
         st = launch_pdl(kv_write_kernel, dim3(g.n_kv_heads, batch), dim3(32), 0, s, a);
         if (st) return st;
@@ -773,6 +828,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
         if (st) return st;
     }
     // 3. h += Wo . att
+    timer_mark(m->timer, X100Q_T_O, s);
     GemvOpts o3;
     o3.accum = true;
     st = launch_qgemv_ex(c, L.o, m->att, h, batch, o3, s);
@@ -783,6 +839,8 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     o4.eps = g.eps;
     o4.hn_out = m->hn;
     o4.accum = eout == nullptr;
+    o4.mark = timer_mark_cb;
+    o4.mark_ctx = &m->timer;
     return launch_moe_ex(c, L.moe, m->S, h, eout ? eout : h, batch, o4, s);
 }
 
@@ -809,6 +867,10 @@ int x100q_model_layer_dev(x100q_model *m, int layer, float *h, const int *pos, i
     if (!c) return get_error();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int st = layer_launch(m, c, layer, h, pos, batch, eout, s, false, false);
+    if (m->timer.on) {
+        timer_mark(m->timer, -1, s);
+        ++m->timer.steps;
+    }
     if (st) return st;
     if (sel_out || w_out) {
         const size_t nb = (size_t)batch * m->cfg.n_act * 4;
@@ -872,10 +934,20 @@ static int forward_impl(x100q_model *m, const int *tokens, float *h, const int *
     // the step starts behind a full barrier (embed, or layer 0's first
     // kernel), so every attention kernel of the step may stage early
     int st = X100_OK;
-    if (tokens) st = x100q_model_embed_dev(m, tokens, h, batch, stream);
+    if (tokens) {
+        timer_mark(m->timer, X100Q_T_EMBED, s);
+        st = x100q_model_embed_dev(m, tokens, h, batch, stream);
+    }
     for (int l = 0; st == X100_OK && l < m->cfg.n_layers; ++l)
         st = layer_launch(m, c, l, h, pos, batch, nullptr, s, true, l == 0 && !tokens, slot);
-    if (st == X100_OK && logits) st = x100q_model_head_dev(m, h, logits, batch, stream);
+    if (st == X100_OK && logits) {
+        timer_mark(m->timer, X100Q_T_LM, s);
+        st = x100q_model_head_dev(m, h, logits, batch, stream);
+    }
+    if (m->timer.on) {
+        timer_mark(m->timer, -1, s);
+        ++m->timer.steps;
+    }
     if (st) set_error(st);
     return st;
 }
@@ -1031,6 +1103,43 @@ static int prefill_chunk_tc(x100q_model *m, DevCtx *c, const int *tok, float *h,
 }
 
 extern "C" {
+
+int x100q_model_timing(x100q_model *m, int on) {
+    set_error(X100_OK);
+    if (!m) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    DeviceGuard dg(m->device);
+    StepTimer &t = m->timer;
+    if (on) {
+        timer_flush(t);
+        for (double &v : t.ms) v = 0.0;
+        t.steps = 0;
+    }
+    t.on = on != 0;
+    return X100_OK;
+}
+
+int x100q_model_timing_read(x100q_model *m, double *ms, long *steps) {
+    set_error(X100_OK);
+    if (!m) {
+        set_error(X100_E_ARG);
+        return X100_E_ARG;
+    }
+    DeviceGuard dg(m->device);
+    StepTimer &t = m->timer;
+    timer_flush(t);   // every call ends with its closing mark, so nothing is left open
+    if (ms)
+        for (int i = 0; i < X100Q_NBUCKETS; ++i) ms[i] = t.ms[i];
+    if (steps) *steps = t.steps;
+    return X100_OK;
+}
+
+const char *x100q_timing_bucket_name(int bucket) {
+    static const char *names[X100Q_NBUCKETS] = {"embed", "qkv", "attention", "o", "router", "expert", "combine", "lm"};
+    return bucket >= 0 && bucket < X100Q_NBUCKETS ? names[bucket] : nullptr;
+}
 
 int x100q_model_forward(x100q_model *m, const int *tokens, const int *pos, float *logits, int batch) {
     set_error(X100_OK);

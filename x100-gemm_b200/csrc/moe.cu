@@ -735,11 +735,11 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
 // every token of the expert; the seg lanes of a row then sum their terms with
 // shuffles.  Expert k's tokens are its slots start[k] .. start[k] + cnt[k] - 1
 // of the grouped h / hq buffers.
-constexpr int kWsWarps = 15;                 // + the producer: 16 warps, 128 registers a thread
+constexpr int kWsWarps = 8;                  // + the producer: 9 warps, up to 168 registers a thread
 constexpr int kWsThreads = 32 * (kWsWarps + 1);
 constexpr int kWsMaxSt = 4;
 constexpr int kWsTok = 4;                    // tokens dotted per pass over a lane's half slices
-constexpr size_t kWsSmem = 213 * 1024;       // dynamic shared memory (PipeMeta is static)
+constexpr size_t kWsSmem = 215 * 1024;       // dynamic shared memory (PipeMeta and the barriers are static)
 
 // lanes per row: the row's 2 ns half slices, at most cap lanes (then a lane
 // takes half slices ls, ls + cap, ...)
@@ -791,10 +791,11 @@ __device__ __forceinline__ void ws_produce(int nst, int W, int *work, uint64_t *
 }
 
 // gate / up: an item is (k, TR = kWsWarps * rpw rows of gate and the same
-// rows of up); lanes 0-15 of a warp hold gate, 16-31 up, each half holding
-// rpw rows of seg lanes.  The prepared activations of the batch's nb tokens
-// (xq, token after token) are copied into shared memory once per CTA.
-// Writes h[slot][row] = silu(gate . x) * (up . x) (qwen_moe.c:304-309).
+// rows of up); a warp holds rpw rows of seg lanes, and a lane the same half
+// slice of the row in both matrices, so each activation load serves both
+// dots.  The prepared activations of the batch's nb tokens (xq, token after
+// token) are copied into shared memory once per CTA.  Writes h[slot][row] =
+// silu(gate . x) * (up . x) (qwen_moe.c:304-309).
 template <int QT>
 __global__ void __launch_bounds__(kWsThreads, 1)
     gate_up_ws_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
@@ -808,7 +809,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     constexpr int SB = slice_bytes(QT);
     const int ns = slices_per_row(d), xb1 = xbuf_bytes(ns, 1), hsr = 2 * ns;
     const long rb = row_bytes_dev(QT, d);
-    const int seg = ws_seg(hsr, 16), rpw = 16 / seg, TR = kWsWarps * rpw;
+    const int seg = ws_seg(hsr, 32), rpw = 32 / seg, TR = kWsWarps * rpw;
     const int stage_b = (int)(2 * TR * rb);
     uint8_t *xa = smem + (size_t)nst * stage_b;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -843,7 +844,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         return;
     }
     if (!mbar_wait(&xbar, 0, &abort_flag, status)) return;
-    const int mat = lane >> 4, l16 = lane & 15, rr = l16 / seg, ls = l16 - rr * seg, top = ws_top(seg);
+    const int rr = lane / seg, ls = lane - rr * seg, top = ws_top(seg);
     const int rin = warp * rpw + rr;             // row within the item
     for (int i = 0;; ++i) {
         const int st = i % nst;
@@ -853,23 +854,29 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         const int k = it / tiles, t = it - k * tiles;
         const int rows = min(TR, ffn - t * TR), np = M.cnt[k];
         const bool live = rr < rpw && rin < rows;
-        const uint8_t *wr = smem + (size_t)st * stage_b + (mat ? TR * rb : 0) + (long)rin * rb;
+        const uint8_t *wg = smem + (size_t)st * stage_b + (long)rin * rb, *wu = wg + TR * rb;
         for (int j0 = 0; j0 < np; j0 += kWsTok) {   // passes of kWsTok tokens (one for most experts)
-            float a[kWsTok] = {};
+            float ag[kWsTok] = {}, au[kWsTok] = {};
             const uint8_t *xt[kWsTok];
 #pragma unroll
             for (int jj = 0; jj < kWsTok; ++jj) xt[jj] = xa + (size_t)M.tok[k][min(j0 + jj, np - 1)] * xb1;
             for (int hq = ls; live && hq < hsr; hq += seg) {
-                UHalf<QT> u;
+                UHalf<QT> ug, uu;
                 {
                     WHalf<QT> w;
-                    load_half<QT>(wr + (long)(hq >> 1) * SB, hq & 1, w);
-                    unpack_half<QT>(w, hq & 1, u);
+                    load_half<QT>(wg + (long)(hq >> 1) * SB, hq & 1, w);
+                    unpack_half<QT>(w, hq & 1, ug);
+                    load_half<QT>(wu + (long)(hq >> 1) * SB, hq & 1, w);
+                    unpack_half<QT>(w, hq & 1, uu);
                 }
                 const int xo = (hq >> 1) * kXSlice + (hq & 1) * kXHalf;
 #pragma unroll
                 for (int jj = 0; jj < kWsTok; ++jj)
-                    if (j0 + jj < np) a[jj] += dot_uhalf<QT>(u, reinterpret_cast<const XB *>(xt[jj] + xo));
+                    if (j0 + jj < np) {
+                        const XB *x = reinterpret_cast<const XB *>(xt[jj] + xo);
+                        ag[jj] += dot_uhalf<QT>(ug, x);
+                        au[jj] += dot_uhalf<QT>(uu, x);
+                    }
             }
             if (j0 + kWsTok >= np) {             // the last read of this stage
                 __syncwarp();
@@ -878,10 +885,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
             for (int jj = 0; jj < kWsTok; ++jj)
                 if (j0 + jj < np) {
-                    const float g = seg_sum(a[jj], ls, seg, top);
-                    const float u = __shfl_down_sync(0xffffffffu, g, 16);   // the up row's sum
-                    if (mat == 0 && ls == 0 && live)
-                        h[(long)(M.start[k] + j0 + jj) * ffn + t * TR + rin] = swiglu(g, u);
+                    const float g = seg_sum(ag[jj], ls, seg, top), u = seg_sum(au[jj], ls, seg, top);
+                    if (ls == 0 && live) h[(long)(M.start[k] + j0 + jj) * ffn + t * TR + rin] = swiglu(g, u);
                 }
         }
     }
@@ -895,8 +900,10 @@ __global__ void __launch_bounds__(256) prep_slots_kernel(const float *__restrict
     xprep_rows([h, p, ffn](int) { return h + (long)p * ffn; }, ffn, 1, xbuf_at(hq + (size_t)p * xbuf_bytes(ns, 1), ns));
 }
 
-// down: an item is (k, TR = kWsWarps * rpw rows of down); a stage holds the
-// rows and the expert's prepared h (its slots, contiguous in hq).  Writes
+// down: an item is (k, TR = 2 kWsWarps rpw rows of down); a warp holds rpw
+// pairs of rows of seg lanes, a lane the same half slice of row r and row r
+// + TR / 2 (one activation load, two dots); a stage holds the rows and the
+// expert's prepared h (its slots, contiguous in hq).  Writes
 // the unweighted part[pair][row] for the combine.  The weights of the first
 // stages are requested before the dependency wait (the groups are final once
 // this kernel runs: the gate / up kernel read them behind its own wait).
@@ -913,7 +920,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     constexpr int SB = slice_bytes(QT);
     const int ns = slices_per_row(ffn), xb1 = xbuf_bytes(ns, 1), hsr = 2 * ns;
     const long rb = row_bytes_dev(QT, ffn);
-    const int seg = ws_seg(hsr, 32), rpw = 32 / seg, TR = kWsWarps * rpw;
+    const int seg = ws_seg(hsr, 32), rpw = 32 / seg, TRh = kWsWarps * rpw, TR = 2 * TRh;
     const int wbytes = (int)(TR * rb), stage_b = wbytes + nb * xb1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -964,7 +971,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     }
     pdl_launch_dependents();
     const int rr = lane / seg, ls = lane - rr * seg, top = ws_top(seg);
-    const int rin = warp * rpw + rr;
+    const int rin = warp * rpw + rr;             // rows rin and rin + TRh of the item
     for (int i = 0;; ++i) {
         const int st = i % nst;
         if (!mbar_wait(&full[st], (uint32_t)((i / nst) & 1), &abort_flag, status)) break;
@@ -972,22 +979,28 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         if (it < 0) break;
         const int k = it / tiles, t = it - k * tiles;
         const int rows = min(TR, d - t * TR), np = M.cnt[k];
-        const bool live = rr < rpw && rin < rows;
-        const uint8_t *wr = smem + (size_t)st * stage_b + (long)rin * rb;
+        const bool live0 = rr < rpw && rin < rows, live1 = rr < rpw && rin + TRh < rows;
+        const uint8_t *w0 = smem + (size_t)st * stage_b + (long)rin * rb, *w1 = w0 + (long)TRh * rb;
         const uint8_t *xh = smem + (size_t)st * stage_b + wbytes;   // the expert's slots, xb1 apart
         for (int j0 = 0; j0 < np; j0 += kWsTok) {
-            float a[kWsTok] = {};
-            for (int hq2 = ls; live && hq2 < hsr; hq2 += seg) {
-                UHalf<QT> u;
+            float a0[kWsTok] = {}, a1[kWsTok] = {};
+            for (int hq2 = ls; live0 && hq2 < hsr; hq2 += seg) {
+                UHalf<QT> u0, u1;
                 {
                     WHalf<QT> w;
-                    load_half<QT>(wr + (long)(hq2 >> 1) * SB, hq2 & 1, w);
-                    unpack_half<QT>(w, hq2 & 1, u);
+                    load_half<QT>(w0 + (long)(hq2 >> 1) * SB, hq2 & 1, w);
+                    unpack_half<QT>(w, hq2 & 1, u0);
+                    if (live1) load_half<QT>(w1 + (long)(hq2 >> 1) * SB, hq2 & 1, w);
+                    unpack_half<QT>(w, hq2 & 1, u1);   // a copy of row 0 when row 1 is past the matrix
                 }
                 const uint8_t *xo = xh + (size_t)j0 * xb1 + (hq2 >> 1) * kXSlice + (hq2 & 1) * kXHalf;
 #pragma unroll
                 for (int jj = 0; jj < kWsTok; ++jj)
-                    if (j0 + jj < np) a[jj] += dot_uhalf<QT>(u, reinterpret_cast<const XB *>(xo + (size_t)jj * xb1));
+                    if (j0 + jj < np) {
+                        const XB *x = reinterpret_cast<const XB *>(xo + (size_t)jj * xb1);
+                        a0[jj] += dot_uhalf<QT>(u0, x);
+                        a1[jj] += dot_uhalf<QT>(u1, x);
+                    }
             }
             if (j0 + kWsTok >= np) {
                 __syncwarp();
@@ -996,8 +1009,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
             for (int jj = 0; jj < kWsTok; ++jj)
                 if (j0 + jj < np) {
-                    const float v = seg_sum(a[jj], ls, seg, top);
-                    if (ls == 0 && live) part[(long)M.pairs[k][j0 + jj] * d + t * TR + rin] = v;
+                    const float v0 = seg_sum(a0[jj], ls, seg, top), v1 = seg_sum(a1[jj], ls, seg, top);
+                    float *o = part + (long)M.pairs[k][j0 + jj] * d + t * TR + rin;
+                    if (ls == 0 && live0) o[0] = v0;
+                    if (ls == 0 && live1) o[TRh] = v1;
                 }
         }
     }
@@ -1009,7 +1024,7 @@ struct WsPlan {
     size_t smem = 0;
 };
 static WsPlan ws_plan_gate_up(int qt, int d, int batch) {
-    const int ns = slices_per_row(d), seg = ws_seg(2 * ns, 16), TR = kWsWarps * (16 / seg);
+    const int ns = slices_per_row(d), seg = ws_seg(2 * ns, 32), TR = kWsWarps * (32 / seg);
     const size_t stage = 2 * (size_t)TR * row_bytes_dev(qt, d), xb1 = xbuf_bytes(ns, 1);
     WsPlan p;   // the deepest ring that leaves room for every token (none: the pipelined kernels)
     const size_t xs = (size_t)batch * xb1;
@@ -1019,7 +1034,7 @@ static WsPlan ws_plan_gate_up(int qt, int d, int batch) {
     return p;
 }
 static WsPlan ws_plan_down(int qt, int ffn, int batch) {
-    const int ns = slices_per_row(ffn), seg = ws_seg(2 * ns, 32), TR = kWsWarps * (32 / seg);
+    const int ns = slices_per_row(ffn), seg = ws_seg(2 * ns, 32), TR = 2 * kWsWarps * (32 / seg);
     const size_t stage = (size_t)TR * row_bytes_dev(qt, ffn) + (size_t)batch * xbuf_bytes(ns, 1);
     WsPlan p;
     p.nst = (int)std::min<size_t>(kWsMaxSt, kWsSmem / stage);
@@ -1470,6 +1485,7 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
         attr[c->device] = true;
     }
     if (batch == 1 && L.fused_ok && !no_fused) {
+        if (o.mark) o.mark(o.mark_ctx, X100Q_T_ROUTER, s);
         int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2, 1), dim3(64), 0, s,
                             (const float *)L.router, x, L.d, L.n_exp, 1, S.logits, S.cnt, 1, o.norm_w, o.eps,
                             o.hn_out);
@@ -1494,9 +1510,11 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
         fa.eout = eout;
         fa.accum = accum;
         fa.status = c->d_status;
+        if (o.mark) o.mark(o.mark_ctx, X100Q_T_EXPERT, s);   // routing, experts and combine in one kernel
         return launch_pdl(moe_fused_kernel<QT>, dim3(L.fused_grid), dim3(kMoeThreads), L.fused_smem, s, fa);
     }
     // batch > 1: tokens grouped by expert
+    if (o.mark) o.mark(o.mark_ctx, X100Q_T_ROUTER, s);
     int st = launch_pdl(router_logits_kernel, dim3((L.n_exp + 1) / 2, batch), dim3(64), 0, s,
                         (const float *)L.router, x, L.d, L.n_exp, batch, S.logits, S.grp, L.n_exp + 1, o.norm_w,
                         o.eps, o.hn_out);
@@ -1504,6 +1522,7 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
     st = launch_pdl(route_group_kernel, dim3(batch), dim3(kMoeThreads), 0, s, L.d, L.n_exp, L.n_act, L.lo, L.hi, hn,
                     (const float *)S.logits, S.sel, S.w, S.grp, S.xq, S.cnt + 1);
     if (st) return st;
+    if (o.mark) o.mark(o.mark_ctx, X100Q_T_EXPERT, s);
     const int G = c->sm_count;   // persistent: one CTA per SM
     static const bool no_ws = getenv("X100_MOE_NO_WS") != nullptr;
     const WsPlan pg = ws_plan_gate_up(QT, L.d, batch), pd = ws_plan_down(QT, L.ffn, batch);
@@ -1529,6 +1548,7 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
                         (const float *)S.h, S.part, S.cnt + 2, c->d_status);
         if (st) return st;
     }
+    if (o.mark) o.mark(o.mark_ctx, X100Q_T_COMBINE, s);
     return launch_pdl(combine_kernel, dim3((L.d + 255) / 256, batch), dim3(256), 0, s, L.d, L.n_act, L.lo, L.hi,
                       (const int *)S.sel, (const float *)S.w, (const float *)S.part, eout, accum);
 }

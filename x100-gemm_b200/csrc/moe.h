@@ -60,6 +60,10 @@ struct MoeOpts {
     float eps = 1e-6f;
     float *hn_out = nullptr;
     bool accum = false;
+    // step timing: mark(mark_ctx, bucket, s) before the router, expert and
+    // combine launches (buckets of x100q_model_timing)
+    void (*mark)(void *ctx, int bucket, cudaStream_t s) = nullptr;
+    void *mark_ctx = nullptr;
 };
 // Scratch of the many-token (prefill) MoE path for up to `tmax` tokens:
 // routing, the (token, slot) pairs sorted by expert, their activations as

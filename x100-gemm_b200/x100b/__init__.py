@@ -91,6 +91,9 @@ _SIGS = {
     "x100q_model_forward": ([vp, vp, vp, vp, i32], i32),
     "x100q_model_forward_slots_dev": ([vp, vp, vp, vp, vp, vp, i32, vp], i32),
     "x100q_model_prefill": ([vp, i32, vp, i32, i32, vp], i32),
+    "x100q_model_timing": ([vp, i32], i32),
+    "x100q_model_timing_read": ([vp, vp, vp], i32),
+    "x100q_timing_bucket_name": ([i32], C.c_char_p),
     # expert-parallel combine
     "x100q_ep_create": ([i32, i32, i32], vp),
     "x100q_ep_handle": ([vp, vp], i32),
@@ -146,6 +149,15 @@ def lib():
             fn.restype = res
         _lib = L
     return _lib
+
+
+TIMING_BUCKETS = 8   # X100Q_NBUCKETS
+
+
+def timing_bucket_name(i: int) -> str | None:
+    """Name of step-timing bucket i (x100q_timing_bucket_name)."""
+    n = lib().x100q_timing_bucket_name(i)
+    return n.decode() if n else None
 
 
 def header_functions() -> list[str]:
@@ -350,6 +362,17 @@ class Model:
         logits = np.empty((B, self.cfg.vocab), np.float32)
         check(lib().x100q_model_forward(self.h, _p(tokens), _p(pos), _p(logits), B), "x100q_model_forward")
         return logits
+
+    def timing(self, on: bool):
+        """Start (clearing the totals) or stop per-bucket step timing."""
+        check(lib().x100q_model_timing(self.h, 1 if on else 0), "x100q_model_timing")
+
+    def timing_read(self) -> tuple[dict, int]:
+        """({bucket name: total ms}, timed calls) since timing started."""
+        ms = np.zeros(TIMING_BUCKETS, np.float64)
+        steps = C.c_long(0)
+        check(lib().x100q_model_timing_read(self.h, _p(ms), C.byref(steps)), "x100q_model_timing_read")
+        return {timing_bucket_name(i): float(ms[i]) for i in range(TIMING_BUCKETS)}, steps.value
 
     def close(self):
         if getattr(self, "h", None) and _lib is not None:
