@@ -10,7 +10,8 @@
 //   Q4_0  [8 fp16 block scales][8 x 16 B nibbles]          144 B =  9 chunks
 //   Q8_0  [8 fp16 block scales][8 x 32 B int8]             272 B = 17 chunks
 //   Q4_K  the native 144-byte superblock                    144 B =  9 chunks
-//   Q3_K  [qs 64][hmask 32][scales 12][d 2][pad 2]          112 B =  7 chunks
+//   Q3_K  [8 x 12 B values][scales 12][d 2][pad 2]          112 B =  7 chunks
+//         (values v = q + 4 in 3 bits, packed for cheap unpacking: q3k_groups)
 // A row of K weights holds ceil(K/256) slices; for Q4_0 / Q8_0 the blocks
 // past K are zero (scale 0), so rows stay whole slices.  Rows are contiguous,
 // so a run of rows is one contiguous byte range (one bulk copy).
@@ -141,15 +142,31 @@ __device__ __forceinline__ void kq_scale_min(int j, uint32_t s0, uint32_t s1, ui
         m = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
     }
 }
-// Q3_K scale i (0..15), biased by 32 (restates qwen_moe_q3k.c:560-564).
-__device__ __forceinline__ int q3k_scale(int i, uint32_t s0, uint32_t s1, uint32_t s2) {
-    auto byte = [&](int k) -> int {
-        uint32_t w = k < 4 ? s0 : (k < 8 ? s1 : s2);
-        return (w >> (8 * (k & 3))) & 0xFF;
-    };
-    int lo = i < 8 ? (byte(i) & 0xF) : (byte(i - 8) >> 4);
-    int hi = (byte(8 + (i & 3)) >> (2 * (i >> 2))) & 3;
-    return (lo | (hi << 4)) - 32;
+// Q3_K values of one 32-element block, v = q + 4 in [0, 7] (qwen_moe_q3k.c:
+// 568-577), in three words W0, W1, W2 whose byte i holds element 4g + i of
+// the block's 4-element groups g: bits 0-2 of W0 / W1 / W2 groups 0 / 2 / 4,
+// bits 3-5 groups 1 / 3 / 5, bits 6-7 of W0 / W1 the low two bits of groups
+// 6 / 7 and bits 6 / 7 of W2 their high bits.  a (groups 0-3) and b (4-7)
+// come out as dp4a-ready bytes, four elements a word.
+__device__ __forceinline__ void q3k_groups(uint32_t W0, uint32_t W1, uint32_t W2, uint4 &a, uint4 &b) {
+    a.x = W0 & 0x07070707u;
+    a.y = (W0 >> 3) & 0x07070707u;
+    a.z = W1 & 0x07070707u;
+    a.w = (W1 >> 3) & 0x07070707u;
+    b.x = W2 & 0x07070707u;
+    b.y = (W2 >> 3) & 0x07070707u;
+    b.z = ((W0 >> 6) & 0x03030303u) | ((W2 >> 4) & 0x04040404u);
+    b.w = ((W1 >> 6) & 0x03030303u) | ((W2 >> 5) & 0x04040404u);
+}
+// The unbiased 6-bit scales of sub-blocks 8h .. 8h+3 (c = 0) or 8h+4 ..
+// 8h+7 (c = 1) as the four bytes of a word (0 .. 63; the scale is byte - 32)
+// from the 12 scale bytes s0, s1, s2 (the packing of qwen_moe_q3k.c:560-564:
+// low nibbles in bytes 0-7, high nibbles for scales 8-15, top two bits in
+// bytes 8-11).
+__device__ __forceinline__ uint32_t q3k_scale_word(int h, int c, uint32_t s0, uint32_t s1, uint32_t s2) {
+    const uint32_t lo = ((c ? s1 : s0) >> (4 * h)) & 0x0F0F0F0Fu;
+    const uint32_t hi = h ? (c ? s2 >> 2 : s2) : (c ? s2 << 2 : s2 << 4);
+    return lo | (hi & 0x30303030u);
 }
 
 // ---- half a slice in registers ------------------------------------------------------
@@ -158,7 +175,7 @@ template <int QT> struct WHalf;
 template <> struct WHalf<Q4_0> { uint4 dh; uint4 q[4]; };          // scales + blocks 4h..4h+3
 template <> struct WHalf<Q8_0> { uint4 dh; uint4 q[8]; };
 template <> struct WHalf<Q4_K> { uint4 hdr; uint4 q[4]; };         // header + qs chunks of pairs 2h, 2h+1
-template <> struct WHalf<Q3_K> { uint4 q[2]; uint4 hm[2]; uint4 hdr; };
+template <> struct WHalf<Q3_K> { uint4 v[3]; uint4 hdr; };        // blocks 4h..4h+3: 12 words; scales + d
 
 __device__ __forceinline__ uint4 ld16(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
 
@@ -180,10 +197,8 @@ template <> __device__ __forceinline__ void load_half<Q4_K>(const uint8_t *p, in
     for (int i = 0; i < 4; ++i) w.q[i] = ld16(p + 16 * (1 + 4 * h + i));
 }
 template <> __device__ __forceinline__ void load_half<Q3_K>(const uint8_t *p, int h, WHalf<Q3_K> &w) {
-    w.q[0] = ld16(p + 32 * h);
-    w.q[1] = ld16(p + 32 * h + 16);
-    w.hm[0] = ld16(p + 64);
-    w.hm[1] = ld16(p + 80);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) w.v[i] = ld16(p + 48 * h + 16 * i);
     w.hdr = ld16(p + 96);
 }
 
@@ -240,29 +255,27 @@ template <> __device__ __forceinline__ float dot_half<Q4_K>(const WHalf<Q4_K> &w
     }
     return acc;
 }
-// Q3_K: qs chunk 2hh + lh and hmask chunk lh hold elements 128hh + 32j + 16lh
-// + i (j < 4), two bits at shift 2j and the bit 4hh + j; half hh = h.
+// Q3_K: block j of the half in words 3j .. 3j+2 of w.v (q3k_groups); its
+// sub-blocks 8h + 2j + lh take scale byte 2j + lh of the half's two scale
+// words.
+__device__ __forceinline__ uint32_t q3k_w(const uint4 (&v)[3], int k) { return u4_word(v[k >> 2], k & 3); }
+__device__ __forceinline__ float q3k_s(uint32_t scw, int byte, float d) {
+    return d * (float)((int)((scw >> (8 * byte)) & 0xFFu) - 32);
+}
 template <> __device__ __forceinline__ float dot_half<Q3_K>(const WHalf<Q3_K> &w, int h, const XB *x) {
     const float d = half_lo(w.hdr.w);
+    const uint32_t sc0 = q3k_scale_word(h, 0, w.hdr.x, w.hdr.y, w.hdr.z),
+                   sc1 = q3k_scale_word(h, 1, w.hdr.x, w.hdr.y, w.hdr.z);
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const XB &xb = x[j];
-        const int hs = 4 * h + j;
-        int dots[2];
-#pragma unroll
-        for (int lh = 0; lh < 2; ++lh) {
-            const uint4 q = w.q[lh], hm = w.hm[lh];
-            uint4 vv;
-            vv.x = ((q.x >> (2 * j)) & 0x03030303u) | (((hm.x >> hs) & 0x01010101u) << 2);
-            vv.y = ((q.y >> (2 * j)) & 0x03030303u) | (((hm.y >> hs) & 0x01010101u) << 2);
-            vv.z = ((q.z >> (2 * j)) & 0x03030303u) | (((hm.z >> hs) & 0x01010101u) << 2);
-            vv.w = ((q.w >> (2 * j)) & 0x03030303u) | (((hm.w >> hs) & 0x01010101u) << 2);
-            dots[lh] = dot16_u(vv, lh ? xb.h1 : xb.h0, lh ? xb.l1 : xb.l0);   // v in [0,7]; q = v - 4
-        }
-        const float s0 = d * (float)q3k_scale(8 * h + 2 * j, w.hdr.x, w.hdr.y, w.hdr.z);
-        const float s1 = d * (float)q3k_scale(8 * h + 2 * j + 1, w.hdr.x, w.hdr.y, w.hdr.z);
-        acc += s0 * (xb.f.x * (float)dots[0] - 4.0f * xb.f.z) + s1 * (xb.f.x * (float)dots[1] - 4.0f * xb.f.w);
+        uint4 a, b;
+        q3k_groups(q3k_w(w.v, 3 * j), q3k_w(w.v, 3 * j + 1), q3k_w(w.v, 3 * j + 2), a, b);
+        const int d0 = dot16_u(a, xb.h0, xb.l0), d1 = dot16_u(b, xb.h1, xb.l1);   // v in [0,7]; q = v - 4
+        const uint32_t scw = j < 2 ? sc0 : sc1;
+        const float s0 = q3k_s(scw, (2 * j) & 3, d), s1 = q3k_s(scw, (2 * j + 1) & 3, d);
+        acc += s0 * (xb.f.x * (float)d0 - 4.0f * xb.f.z) + s1 * (xb.f.x * (float)d1 - 4.0f * xb.f.w);
     }
     return acc;
 }
@@ -318,20 +331,14 @@ template <> __device__ __forceinline__ void unpack_half<Q4_K>(const WHalf<Q4_K> 
 }
 template <> __device__ __forceinline__ void unpack_half<Q3_K>(const WHalf<Q3_K> &w, int h, UHalf<Q3_K> &u) {
     const float d = half_lo(w.hdr.w);
+    const uint32_t sc0 = q3k_scale_word(h, 0, w.hdr.x, w.hdr.y, w.hdr.z),
+                   sc1 = q3k_scale_word(h, 1, w.hdr.x, w.hdr.y, w.hdr.z);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const int hs = 4 * h + j;
-#pragma unroll
-        for (int lh = 0; lh < 2; ++lh) {
-            const uint4 q = w.q[lh], hm = w.hm[lh];
-            uint4 vv;
-            vv.x = ((q.x >> (2 * j)) & 0x03030303u) | (((hm.x >> hs) & 0x01010101u) << 2);
-            vv.y = ((q.y >> (2 * j)) & 0x03030303u) | (((hm.y >> hs) & 0x01010101u) << 2);
-            vv.z = ((q.z >> (2 * j)) & 0x03030303u) | (((hm.z >> hs) & 0x01010101u) << 2);
-            vv.w = ((q.w >> (2 * j)) & 0x03030303u) | (((hm.w >> hs) & 0x01010101u) << 2);
-            u.v[j][lh] = vv;
-            u.s[j][lh] = d * (float)q3k_scale(8 * h + 2 * j + lh, w.hdr.x, w.hdr.y, w.hdr.z);
-        }
+        q3k_groups(q3k_w(w.v, 3 * j), q3k_w(w.v, 3 * j + 1), q3k_w(w.v, 3 * j + 2), u.v[j][0], u.v[j][1]);
+        const uint32_t scw = j < 2 ? sc0 : sc1;
+        u.s[j][0] = q3k_s(scw, (2 * j) & 3, d);
+        u.s[j][1] = q3k_s(scw, (2 * j + 1) & 3, d);
     }
 }
 

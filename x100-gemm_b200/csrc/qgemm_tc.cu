@@ -153,18 +153,20 @@ template <int QT> struct SliceRegs;
 template <> struct SliceRegs<Q8_0> { uint4 hd; };                 // the 8 block scales
 template <> struct SliceRegs<Q4_0> { uint4 hd; };
 template <> struct SliceRegs<Q4_K> { uint4 hdr; };                // d, dmin, scales / mins
-template <> struct SliceRegs<Q3_K> { uint4 qs[2], mm, hdr; };     // qs of both halves, hmask, scales + d
+template <> struct SliceRegs<Q3_K> { uint32_t sc; float d; };   // the thread's scale byte of each piece, d
 
 template <int QT> __device__ __forceinline__ void load_slice(const uint8_t *sl, int q4, SliceRegs<QT> &R);
 template <> __device__ __forceinline__ void load_slice<Q8_0>(const uint8_t *sl, int, SliceRegs<Q8_0> &R) { R.hd = ld16(sl); }
 template <> __device__ __forceinline__ void load_slice<Q4_0>(const uint8_t *sl, int, SliceRegs<Q4_0> &R) { R.hd = ld16(sl); }
 template <> __device__ __forceinline__ void load_slice<Q4_K>(const uint8_t *sl, int, SliceRegs<Q4_K> &R) { R.hdr = ld16(sl); }
 template <> __device__ __forceinline__ void load_slice<Q3_K>(const uint8_t *sl, int q4, SliceRegs<Q3_K> &R) {
-    const int q16 = q4 & 1;
-    R.qs[0] = ld16(sl + 16 * q16);
-    R.qs[1] = ld16(sl + 32 + 16 * q16);
-    R.mm = ld16(sl + 64 + 16 * q16);
-    R.hdr = ld16(sl + 96);
+    const uint4 hdr = ld16(sl + 96);
+    // piece j's sub-block for quarter q4 is 4 j + q4: byte q4 of scale word j
+    R.sc = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        R.sc |= ((q3k_scale_word(j >> 1, j & 1, hdr.x, hdr.y, hdr.z) >> (8 * q4)) & 0xFFu) << (8 * j);
+    R.d = h2f_lo(hdr.w);
 }
 
 // The thread's 16 weights of piece j as 8 fp16 pairs hi / lo, element order.
@@ -206,26 +208,27 @@ __device__ __forceinline__ void dq16<Q4_0>(const SliceRegs<Q4_0> &R, const uint8
         for (int sel = 0; sel < 2; ++sel) split_h2(d2, __hsub2(bytes_h2(nib, sel), off), hv[2 * wi + sel], lv[2 * wi + sel]);
     }
 }
-// Q3_K slice: [qs 64][hmask 32][scales 12][d 2][pad 2]; element e = 32 b + l:
-// half hh = b / 4, shift 2t with t = b % 4, q = ((qs[32hh + l] >> 2t) & 3) -
-// (hmask bit 4hh + t of byte l ? 0 : 4), sub-block scale 8hh + 2t + l/16;
-// w = d * (sc - 32) * q (qwen_moe_q3k.c:557-577).  The scale (17 bits, exact
-// in fp32) is carried as an fp16 pair dh + dl: hi = fp16(dh q), lo =
-// fp16((dh q - hi) + dl q), so hi + lo = w to ~2^-22 relative.
+// Q3_K slice: [8 x 12 B values][scales 12][d 2][pad 2]; block b's values v =
+// q + 4 in the three words at 12 b (q3k_groups), sub-block 2 b + q16 with
+// scale sc - 32; w = d * (sc - 32) * q (qwen_moe_q3k.c:557-577).  The scale
+// (17 bits, exact in fp32) is carried as an fp16 pair dh + dl: hi = fp16(dh
+// q), lo = fp16((dh q - hi) + dl q), so hi + lo = w to ~2^-22 relative.
 template <>
-__device__ __forceinline__ void dq16<Q3_K>(const SliceRegs<Q3_K> &R, const uint8_t *, int j, int q4, uint32_t (&hv)[8],
+__device__ __forceinline__ void dq16<Q3_K>(const SliceRegs<Q3_K> &R, const uint8_t *sl, int j, int q4, uint32_t (&hv)[8],
                                            uint32_t (&lv)[8]) {
     const int b = 2 * j + (q4 >> 1), q16 = q4 & 1;
-    const int hh = b >> 2, t = b & 3, hb = 4 * hh + t;
-    const uint4 qq = R.qs[hh];
-    const float dlf = h2f_lo(R.hdr.w) * (float)q3k_scale(8 * hh + 2 * t + q16, R.hdr.x, R.hdr.y, R.hdr.z);
+    const uint32_t *wp = reinterpret_cast<const uint32_t *>(sl + 12 * b);
+    uint4 ga, gb;
+    q3k_groups(wp[0], wp[1], wp[2], ga, gb);
+    const uint4 g = q16 ? gb : ga;
+    const float dlf = R.d * (float)((int)((R.sc >> (8 * j)) & 0xFFu) - 32);
     const __half dh = __float2half_rn(dlf);
     const __half dlo = __float2half_rn(dlf - __half2float(dh));
     const __half2 dh2 = __halves2half2(dh, dh), dl2 = __halves2half2(dlo, dlo);
     const __half2 off = __float2half2_rn(1028.0f);   // 1024 + 4: v - 4
 #pragma unroll
     for (int wi = 0; wi < 4; ++wi) {
-        const uint32_t v = ((word_of(qq, wi) >> (2 * t)) & 0x03030303u) | (((word_of(R.mm, wi) >> hb) & 0x01010101u) << 2);
+        const uint32_t v = word_of(g, wi);
 #pragma unroll
         for (int sel = 0; sel < 2; ++sel) {
             const __half2 q2 = __hsub2(bytes_h2(v, sel), off);

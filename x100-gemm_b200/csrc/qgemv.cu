@@ -161,10 +161,28 @@ __global__ void repack_kernel(int qt, int N, int K, const uint8_t *__restrict__ 
             for (int k = 0; k < 144; ++k) o[k] = b[k];
         } else if (qt == Q3_K) {
             // block_q3_K (qwen_moe_q3k.c:531): hmask[32] @0, qs[64] @32,
-            // scales[12] @96, d @108  ->  qs @0, hmask @64, scales @96, d @108
+            // scales[12] @96, d @108.  Element e's value v = q + 4 is the two
+            // bits of qs[32 (e / 128) + e % 32] at shift 2 ((e % 128) / 32)
+            // plus 4 x bit e / 32 of hmask[e % 32] (qwen_moe_q3k.c:568-577);
+            // the values go to the 3-word blocks of q3k_groups, scales and d
+            // to @96 / @108.
             const uint8_t *b = src + i * 110;
-            for (int k = 0; k < 64; ++k) o[k] = b[32 + k];
-            for (int k = 0; k < 32; ++k) o[64 + k] = b[k];
+            for (int blk = 0; blk < 8; ++blk) {
+                uint8_t wb[12] = {};
+                for (int g = 0; g < 8; ++g)
+                    for (int ii = 0; ii < 4; ++ii) {
+                        const int e = 32 * blk + 4 * g + ii;
+                        const int q2 = (b[32 + 32 * (e / 128) + e % 32] >> (2 * ((e % 128) / 32))) & 3;
+                        const int v = q2 | (((b[e % 32] >> (e / 32)) & 1) << 2);
+                        if (g < 6) {
+                            wb[4 * (g / 2) + ii] |= (uint8_t)(v << (3 * (g % 2)));
+                        } else {
+                            wb[4 * (g - 6) + ii] |= (uint8_t)((v & 3) << 6);
+                            wb[8 + ii] |= (uint8_t)((v >> 2) << (g == 6 ? 6 : 7));
+                        }
+                    }
+                for (int k = 0; k < 12; ++k) o[12 * blk + k] = wb[k];
+            }
             for (int k = 0; k < 14; ++k) o[96 + k] = b[96 + k];
             o[110] = 0;
             o[111] = 0;
