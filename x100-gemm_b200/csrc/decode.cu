@@ -53,6 +53,7 @@ struct AttnArgs {
     const int *pos;     // [B]: position of the step's token, < ctx
     int nh, nkv, ctx, nsplit, chunk;
     float eps, rope_base, scale;
+    const float2 *rope; // [ctx][hd / 2]: (cos, sin) of pos * base^(-2i / hd) (rope_table_kernel)
     __half *kc, *vc;    // this layer's cache, [B][nkv][ctx][hd]
     long row_base;      // cache row (of the tensor maps) of this layer's first row
     float *part;        // [B][nh][nsplit][kPartStride]
@@ -64,12 +65,26 @@ struct AttnArgs {
     int *status;
 };
 
-// RMS norm (qwen_moe_q3k.c:1166) and NEOX RoPE (qwen_moe_q3k.c:1170-1175) of
-// one 128-wide head held by a warp as 4 consecutive elements per lane (lane
-// l: elements 4l..4l+3).  The rotation pairs element i with i + 64, held by
-// lane l ^ 16.
-__device__ __forceinline__ float4 norm_rope_head(float4 v, const float *__restrict__ nw, float eps, int pos,
-                                                float base) {
+// The RoPE table: rope[pos][i] = (cos a, sin a), a = pos * base^(-2i/hd),
+// i < hd / 2, with the reference's float expressions (rope_table,
+// qwen_moe_q3k.c:1170-1172).  Built once per model: the angles depend only on
+// the position, so every head, layer and attention split reads the same row.
+__global__ void rope_table_kernel(float2 *__restrict__ rope, int ctx, float base) {
+    for (long t = blockIdx.x * (long)blockDim.x + threadIdx.x; t < (long)ctx * (kHD / 2);
+         t += (long)gridDim.x * blockDim.x) {
+        const int pos = (int)(t / (kHD / 2)), i = (int)(t % (kHD / 2));
+        const float fr = powf(base, -2.0f * (float)i / (float)kHD), a = (float)pos * fr;
+        rope[t] = make_float2(cosf(a), sinf(a));
+    }
+}
+
+// RMS norm (qwen_moe_q3k.c:1166) and NEOX RoPE (rope_apply,
+// qwen_moe_q3k.c:1173-1175) of one 128-wide head held by a warp as 4
+// consecutive elements per lane (lane l: elements 4l..4l+3).  The rotation
+// pairs element i with i + 64, held by lane l ^ 16; rope_row = the table's
+// row of the position.
+__device__ __forceinline__ float4 norm_rope_head(float4 v, const float *__restrict__ nw, float eps,
+                                                const float2 *__restrict__ rope_row) {
     const int lane = threadIdx.x & 31;
     float q = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
 #pragma unroll
@@ -77,16 +92,16 @@ __device__ __forceinline__ float4 norm_rope_head(float4 v, const float *__restri
     const float s = 1.0f / sqrtf(q / (float)kHD + eps);
     const float4 w = __ldg(reinterpret_cast<const float4 *>(nw) + lane);
     v = make_float4(v.x * s * w.x, v.y * s * w.y, v.z * s * w.z, v.w * s * w.w);
+    const float4 *rp = reinterpret_cast<const float4 *>(rope_row + ((4 * lane) & (kHD / 2 - 1)));
+    const float4 r0 = __ldg(rp), r1 = __ldg(rp + 1);   // (cos, sin) of elements 4l .. 4l+3 mod 64
+    const float cs[4] = {r0.x, r0.z, r1.x, r1.z}, sn[4] = {r0.y, r0.w, r1.y, r1.w};
     float e[4] = {v.x, v.y, v.z, v.w};
     float o[4];
     const bool first = lane < 16;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int i = (4 * lane + k) & (kHD / 2 - 1);
-        const float fr = powf(base, -2.0f * (float)i / (float)kHD), a = (float)pos * fr;
-        const float c = cosf(a), sn = sinf(a);
         const float other = __shfl_xor_sync(0xffffffffu, e[k], 16);
-        o[k] = first ? e[k] * c - other * sn : other * sn + e[k] * c;
+        o[k] = first ? e[k] * cs[k] - other * sn[k] : other * sn[k] + e[k] * cs[k];
     }
     return make_float4(o[0], o[1], o[2], o[3]);
 }
@@ -139,7 +154,7 @@ __global__ void __launch_bounds__(32) kv_write_kernel(const AttnArgs a) {
     const float *qrow = a.qkv + (long)b * a.qkv_n;
     float4 k = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + kvh) * kHD) + lane);
     const float4 v = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + a.nkv + kvh) * kHD) + lane);
-    k = norm_rope_head(k, a.k_norm, a.eps, pos, a.rope_base);
+    k = norm_rope_head(k, a.k_norm, a.eps, a.rope + (long)pos * (kHD / 2));
     uint2 kk, vv;
     kk.x = h2u(__floats2half2_rn(k.x, k.y));
     kk.y = h2u(__floats2half2_rn(k.z, k.w));
@@ -227,7 +242,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     if (warp < gpr && n > 0) {
         const int hh = kvh * gpr + warp;
         float4 v = __ldcg(reinterpret_cast<const float4 *>(qrow + hh * kHD) + lane);
-        v = norm_rope_head(v, a.q_norm, a.eps, pos, a.rope_base);
+        v = norm_rope_head(v, a.q_norm, a.eps, a.rope + (long)pos * (kHD / 2));
         reinterpret_cast<float4 *>(sQ + warp * kHD)[lane] = v;
     }
     __syncthreads();                              // barrier initialised, queries ready
@@ -236,7 +251,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         // the step's own k (normed, rotated) and v, rounded to the cache's fp16
         float4 k = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + kvh) * kHD) + lane);
         const float4 v = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + a.nkv + kvh) * kHD) + lane);
-        k = norm_rope_head(k, a.k_norm, a.eps, pos, a.rope_base);
+        k = norm_rope_head(k, a.k_norm, a.eps, a.rope + (long)pos * (kHD / 2));
         uint2 kk, vv;
         kk.x = h2u(__floats2half2_rn(k.x, k.y));
         kk.y = h2u(__floats2half2_rn(k.z, k.w));
@@ -506,6 +521,7 @@ struct x100q_model {
     // scratch
     void *scratch = nullptr;
     float *qkv = nullptr, *att = nullptr, *hn = nullptr, *part = nullptr;
+    float2 *rope = nullptr;   // [ctx][64] RoPE table
     void *moe_scratch = nullptr;
     MoeScratch S;
     int nsplit_max = 0;
@@ -555,9 +571,10 @@ x100q_model *x100q_model_create(const x100q_model_cfg *cfg) {
     m->nsplit_max = (g.ctx + kChunk - 1) / kChunk;
     const size_t qkvb = (size_t)g.max_batch * qkv_rows(g) * 4, attb = (size_t)g.max_batch * g.n_heads * kHD * 4,
                  hnb = (size_t)g.max_batch * g.d * 4,
-                 partb = (size_t)g.max_batch * g.n_heads * m->nsplit_max * kPartStride * 4;
+                 partb = (size_t)g.max_batch * g.n_heads * m->nsplit_max * kPartStride * 4,
+                 ropeb = (size_t)g.ctx * (kHD / 2) * sizeof(float2);
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-    const size_t sb = up(qkvb) + up(attb) + up(hnb) + up(partb);
+    const size_t sb = up(qkvb) + up(attb) + up(hnb) + up(partb) + up(ropeb);
     const size_t msb = moe_scratch_bytes(g.d, g.n_exp, g.n_act, g.moe_ffn);
     bool ok = cudaMalloc(&m->kc, kvb) == cudaSuccess && cudaMalloc(&m->vc, kvb) == cudaSuccess &&
               cudaMalloc(&m->scratch, sb) == cudaSuccess && cudaMalloc(&m->moe_scratch, msb) == cudaSuccess;
@@ -586,6 +603,9 @@ x100q_model *x100q_model_create(const x100q_model_cfg *cfg) {
     m->hn = reinterpret_cast<float *>(p);
     p += up(hnb);
     m->part = reinterpret_cast<float *>(p);
+    p += up(partb);
+    m->rope = reinterpret_cast<float2 *>(p);
+    rope_table_kernel<<<256, 256>>>(m->rope, g.ctx, g.rope_base);
     m->S = moe_scratch_carve(m->moe_scratch, g.d, g.n_exp, g.n_act, g.moe_ffn);
     if (check_cuda(cudaDeviceSynchronize(), X100_E_ALLOC)) {
         x100q_model_destroy(m);
@@ -803,6 +823,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     a.nsplit = (g.ctx + kChunk - 1) / kChunk;
     a.eps = g.eps;
     a.rope_base = g.rope_base;
+    a.rope = m->rope;
     a.scale = 1.0f / sqrtf((float)g.head_dim);
     a.kc = m->kc + (size_t)layer * m->layer_kv;
     a.vc = m->vc + (size_t)layer * m->layer_kv;
@@ -1052,6 +1073,7 @@ static int prefill_chunk_tc(x100q_model *m, DevCtx *c, const int *tok, float *h,
         a.nsplit = (g.ctx + kChunk - 1) / kChunk;
         a.eps = g.eps;
         a.rope_base = g.rope_base;
+        a.rope = m->rope;
         a.scale = 1.0f / sqrtf((float)g.head_dim);
         a.kc = m->kc + (size_t)l * m->layer_kv;
         a.vc = m->vc + (size_t)l * m->layer_kv;
