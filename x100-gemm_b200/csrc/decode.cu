@@ -522,6 +522,7 @@ struct x100q_model {
     void *scratch = nullptr;
     float *qkv = nullptr, *att = nullptr, *hn = nullptr, *part = nullptr;
     float2 *rope = nullptr;   // [ctx][64] RoPE table
+    uint8_t *prep = nullptr;  // prepared activations of the batched GEMVs (GemvOpts::prep)
     void *moe_scratch = nullptr;
     MoeScratch S;
     int nsplit_max = 0;
@@ -572,9 +573,10 @@ x100q_model *x100q_model_create(const x100q_model_cfg *cfg) {
     const size_t qkvb = (size_t)g.max_batch * qkv_rows(g) * 4, attb = (size_t)g.max_batch * g.n_heads * kHD * 4,
                  hnb = (size_t)g.max_batch * g.d * 4,
                  partb = (size_t)g.max_batch * g.n_heads * m->nsplit_max * kPartStride * 4,
-                 ropeb = (size_t)g.ctx * (kHD / 2) * sizeof(float2);
+                 ropeb = (size_t)g.ctx * (kHD / 2) * sizeof(float2),
+                 prepb = qgemv_prep_bytes(16, std::max(g.d, g.n_heads * kHD));
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-    const size_t sb = up(qkvb) + up(attb) + up(hnb) + up(partb) + up(ropeb);
+    const size_t sb = up(qkvb) + up(attb) + up(hnb) + up(partb) + up(ropeb) + up(prepb);
     const size_t msb = moe_scratch_bytes(g.d, g.n_exp, g.n_act, g.moe_ffn);
     bool ok = cudaMalloc(&m->kc, kvb) == cudaSuccess && cudaMalloc(&m->vc, kvb) == cudaSuccess &&
               cudaMalloc(&m->scratch, sb) == cudaSuccess && cudaMalloc(&m->moe_scratch, msb) == cudaSuccess;
@@ -605,6 +607,8 @@ x100q_model *x100q_model_create(const x100q_model_cfg *cfg) {
     m->part = reinterpret_cast<float *>(p);
     p += up(partb);
     m->rope = reinterpret_cast<float2 *>(p);
+    p += up(ropeb);
+    m->prep = p;
     rope_table_kernel<<<256, 256>>>(m->rope, g.ctx, g.rope_base);
     m->S = moe_scratch_carve(m->moe_scratch, g.d, g.n_exp, g.n_act, g.moe_ffn);
     if (check_cuda(cudaDeviceSynchronize(), X100_E_ALLOC)) {
@@ -807,6 +811,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     o1.norm_w = L.norms;
     o1.eps = g.eps;
     o1.pdl = !barrier;
+    o1.prep = m->prep;
     int st = launch_qgemv_ex(c, L.qkv, h, m->qkv, batch, o1, s);
     if (st) return st;
     // 2. attention (+ merge of the splits)
@@ -852,6 +857,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     timer_mark(m->timer, X100Q_T_O, s);
     GemvOpts o3;
     o3.accum = true;
+    o3.prep = m->prep;
     st = launch_qgemv_ex(c, L.o, m->att, h, batch, o3, s);
     if (st) return st;
     // 4. h += MoE(rmsnorm(h))  (or eout = this process's experts' share)
@@ -914,6 +920,7 @@ int x100q_model_head_dev(x100q_model *m, const float *h, float *logits, int batc
     GemvOpts o;
     o.norm_w = m->out_norm;
     o.eps = m->cfg.eps;
+    o.prep = m->prep;
     return launch_qgemv_ex(c, m->lm, h, logits, batch, o, static_cast<cudaStream_t>(stream));
 }
 

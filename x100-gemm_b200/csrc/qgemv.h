@@ -36,7 +36,13 @@ struct GemvOpts {
     bool pdl = true;   // false: launch behind a full barrier (see launch_k)
     bool indep = false;   // x, y untouched by running kernels: prepare x before the dependency wait
     int a8 = 0;           // activations packed as the reference's IME path: 1 pack_A_i8, 2 pack_A_q3k
+    // Scratch of qgemv_prep_bytes(16, K) bytes (or null): with it, a call of
+    // 2..16 tokens on the tensor-core kernel prepares the tokens' activations
+    // once, in a kernel of its own, instead of in every CTA.  One buffer per
+    // stream of calls (the model's own).
+    uint8_t *prep = nullptr;
 };
+size_t qgemv_prep_bytes(int batch, int K);
 int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
                     cudaStream_t s);
 // Several tokens of a Q4_0 / Q8_0 matrix on the tensor cores (qgemv_mma.cu):

@@ -124,14 +124,48 @@ static MmaPlan mma_plan(int qt, int K, int batch) {
     return best;
 }
 
+// ---- activations prepared once per call (GemvOpts::prep) ----------------------------
+// Layout of the scratch for `batch` tokens of a K-long row (nxb = 8 ns
+// blocks): the prepared blocks, block-major in groups of ntok tokens (group
+// g's block j of token t at ((g nxb + j) ntok + t % ntok) 80 bytes -- the
+// XBufBM image of the CTA's shared memory for tokens g ntok .. g ntok + ntok
+// - 1), then the blocks' sums of squares qs[token][nxb] (fp32).
+static size_t prep_xbm_bytes(int K) { return (size_t)16 * slices_per_row(K) * 8 * 80; }
+// Grid (ceil(nxb / 8), batch), 64 threads: each 8 threads convert one
+// 32-element block of token blockIdx.y (x, times nw when given) with
+// xprep_vals and record the block's sum of squares of x.
+__global__ void __launch_bounds__(64) prep_bm_kernel(const float *__restrict__ x, int K, const float *__restrict__ nw,
+                                                     int ntok, uint8_t *__restrict__ xbm, float *__restrict__ qs) {
+    pdl_wait();                                   // x comes from the previous kernel
+    pdl_launch_dependents();
+    const int nxb = slices_per_row(K) * 8, kb = K / 32;
+    const int t = threadIdx.x & 7, j = blockIdx.x * 8 + (threadIdx.x >> 3), c = blockIdx.y;
+    const bool active = j < nxb;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j < kb) v = __ldcg(reinterpret_cast<const float4 *>(x + (long)c * K + j * 32) + t);
+    float q = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    q += __shfl_xor_sync(0xffffffffu, q, 1);
+    q += __shfl_xor_sync(0xffffffffu, q, 2);
+    q += __shfl_xor_sync(0xffffffffu, q, 4);
+    if (active && t == 0) qs[(long)c * nxb + j] = q;
+    if (nw && j < kb) {
+        const float4 w4 = __ldg(reinterpret_cast<const float4 *>(nw + j * 32) + t);
+        v = make_float4(v.x * w4.x, v.y * w4.y, v.z * w4.z, v.w * w4.w);
+    }
+    XB *o = reinterpret_cast<XB *>(xbm + (((long)(c / ntok) * nxb + (active ? j : 0)) * ntok + c % ntok) * 80);
+    xprep_vals(v, o, t, active);
+}
+
 template <int QT, int NT>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     qgemv_mma_kernel(const uint8_t *__restrict__ W, int N, int K, int ck, int stages, const float *__restrict__ x,
                      float *__restrict__ y, int batch, const float *__restrict__ nw, float eps, int accum,
-                     int a8, int *status) {
+                     int a8, const uint8_t *__restrict__ xbm, const float *__restrict__ qs, int *status) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float ssq[(kMmaThreads / 32) * 4][kSsTok];   // RMS-norm sums of squares per 8-lane group
     __shared__ float scale[16];
+    __shared__ uint64_t xbar;
+    __shared__ int abort_flag;
     constexpr int SB = slice_bytes(QT);
     constexpr int NTOK = 8 * NT;
     const int ns = slices_per_row(K), nb = ns * 8;
@@ -170,10 +204,30 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     pdl_wait();   // x may come from the previous kernel; the previous call on this matrix is complete
 
     // ---- 2. activations ----
-    xprep_gemv(a8, [x, K](int c) { return x + (long)c * K; }, K, batch, xb, nw, &ssq[0][0]);
-    __syncthreads();
-    if (threadIdx.x < batch) scale[threadIdx.x] = nw ? rms_scale(&ssq[0][0], blockDim.x / 8, threadIdx.x, K, eps) : 1.0f;
-    __syncthreads();
+    if (xbm) {   // prepared by prep_bm_kernel: one bulk copy of this launch's group
+        if (threadIdx.x == 0) {
+            abort_flag = 0;
+            mbar_init(&xbar, 1);
+            fence_barrier_init();
+            const uint32_t bytes = (uint32_t)nb * NTOK * 80;
+            mbar_arrive_expect_tx(&xbar, bytes);
+            stage_bytes(xbase, xbm, bytes, &xbar);
+        }
+        if (threadIdx.x < batch) {
+            float q = 0.f;
+            if (nw)
+                for (int j = 0; j < nb; ++j) q += __ldcg(qs + (long)threadIdx.x * nb + j);
+            scale[threadIdx.x] = nw ? 1.0f / sqrtf(q / (float)K + eps) : 1.0f;
+        }
+        __syncthreads();   // the barrier is initialised
+        mbar_wait(&xbar, 0, &abort_flag, status);   // bounded; on a timeout the status records it
+        __syncthreads();
+    } else {
+        xprep_gemv(a8, [x, K](int c) { return x + (long)c * K; }, K, batch, xb, nw, &ssq[0][0]);
+        __syncthreads();
+        if (threadIdx.x < batch) scale[threadIdx.x] = nw ? rms_scale(&ssq[0][0], blockDim.x / 8, threadIdx.x, K, eps) : 1.0f;
+        __syncthreads();
+    }
     const uint32_t xs_addr = smem_u32(xbase);
 
     // ---- 3. the items ----
@@ -265,7 +319,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 
 template <int QT, int NT>
 static int launch_mma_nt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const MmaPlan &p,
-                         const GemvOpts &o, cudaStream_t s) {
+                         const GemvOpts &o, cudaStream_t s, const uint8_t *xbm, const float *qs) {
     static bool attr[64];
     if (!attr[c->device]) {
         set_qkernel_attrs(qgemv_mma_kernel<QT, NT>, (int)kMmaSmemMax);
@@ -274,7 +328,8 @@ static int launch_mma_nt(DevCtx *c, const QMat &m, const float *x, float *y, int
     const int ntiles = (m.N + kMmaRows - 1) / kMmaRows;
     const int grid = std::min(ntiles, c->sm_count);
     return launch_k(qgemv_mma_kernel<QT, NT>, dim3(grid), dim3(kMmaThreads), p.smem, s, o.pdl, (const uint8_t *)m.w,
-                    m.N, m.K, p.ck, p.stages, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0, o.a8, c->d_status);
+                    m.N, m.K, p.ck, p.stages, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0, o.a8, xbm, qs,
+                    c->d_status);
 }
 
 // Launches of 8 nt tokens each (nt from the plan).
@@ -284,12 +339,32 @@ static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int
     const MmaPlan p = mma_plan(QT, m.K, batch);
     if (!p.stages) return X100_E_UNSUPPORTED;
     const int per = 8 * p.nt;
+    const int nxb = slices_per_row(m.K) * 8;
+    // activations prepared once for all the call's launches (not for the
+    // reference's A8 packings, and not for independent calls, whose point is
+    // to prepare before the dependency wait)
+    const bool prep = o.prep && batch > 1 && o.a8 == 0 && !o.indep && m.K % 32 == 0;
+    uint8_t *xbm = o.prep;
+    float *qs = reinterpret_cast<float *>(o.prep + prep_xbm_bytes(m.K));
+    if (prep) {
+        static bool attr[64];
+        if (!attr[c->device]) {
+            set_qkernel_attrs(prep_bm_kernel);
+            attr[c->device] = true;
+        }
+        const int st = launch_k(prep_bm_kernel, dim3((nxb + 7) / 8, batch), dim3(64), 0, s, o.pdl, x, m.K, o.norm_w,
+                                per, xbm, qs);
+        if (st) return st;
+        o.pdl = true;
+    }
     for (int b0 = 0; b0 < batch; b0 += per) {
         const int nb = std::min(per, batch - b0);
         const float *xb = x + (long)b0 * m.K;
         float *yb = y + (long)b0 * m.N;
-        const int st = p.nt == 2 ? launch_mma_nt<QT, 2>(c, m, xb, yb, nb, p, o, s)
-                                 : launch_mma_nt<QT, 1>(c, m, xb, yb, nb, p, o, s);
+        const uint8_t *gx = prep ? xbm + (size_t)(b0 / per) * nxb * per * 80 : nullptr;
+        const float *gq = prep ? qs + (size_t)b0 * nxb : nullptr;
+        const int st = p.nt == 2 ? launch_mma_nt<QT, 2>(c, m, xb, yb, nb, p, o, s, gx, gq)
+                                 : launch_mma_nt<QT, 1>(c, m, xb, yb, nb, p, o, s, gx, gq);
         if (st) return st;
         o.pdl = true;
     }
@@ -297,6 +372,10 @@ static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int
 }
 
 }  // namespace q
+
+size_t qgemv_prep_bytes(int batch, int K) {
+    return q::prep_xbm_bytes(K) + (size_t)batch * q::slices_per_row(K) * 8 * 4;
+}
 
 bool qgemv_mma_ok(int qt, int K) {
     return (qt == q::Q4_0 || qt == q::Q8_0) && q::mma_plan(qt, K, 8).stages > 0;
