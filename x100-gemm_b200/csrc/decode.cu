@@ -52,6 +52,7 @@ struct AttnArgs {
     const float *q_norm, *k_norm;   // [hd]
     const int *pos;     // [B]: position of the step's token, < ctx
     int nh, nkv, ctx, nsplit, chunk;
+    int cps;            // chunks of kChunk positions per split (1..8; above 1 a two-stage ring)
     float eps, rope_base, scale;
     const float2 *rope; // [ctx][hd / 2]: (cos, sin) of pos * base^(-2i / hd) (rope_table_kernel)
     __half *kc, *vc;    // this layer's cache, [B][nkv][ctx][hd]
@@ -183,164 +184,191 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
                                                                    const __grid_constant__ CUtensorMap tmV,
                                                                    const AttnArgs a) {
     constexpr int C = kChunk, PS = C + 8;   // P row stride (halfs): conflict-free fragment loads
+    constexpr uint32_t kStageBytes = 4u * C * 128;   // K and V of one chunk
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sK = base;
-    uint8_t *sV = base + 2 * C * 128;
-    float *sQ = reinterpret_cast<float *>(base + 4 * C * 128);   // [8][hd]
+    const int cps = a.cps, nst = cps > 1 ? 2 : 1;            // chunks of this split, ring stages
+    float *sQ = reinterpret_cast<float *>(base + nst * kStageBytes);   // [8][hd]
     __half *sP = reinterpret_cast<__half *>(sQ + 8 * kHD);        // [8][PS]
     float *sMax = reinterpret_cast<float *>(sP + 8 * PS);         // [8 warps][8 heads]
     float *sSum = sMax + 64;
-    __shared__ uint64_t bar;
+    __shared__ uint64_t bar[2];
     __shared__ int abort_flag;
     const int sp = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gpr = a.nh / a.nkv;
     const int hq = lane >> 2, q4 = lane & 3;   // fragment row (head) and column pair
-    const int j0 = sp * C;
+    const int j0s = sp * cps * C;               // first position of this split
     int sb = a.slot ? __ldg(a.slot + b) : b;                  // written before the step began
     const bool bad_slot = sb < 0 || sb >= a.nslots;
     if (bad_slot) sb = 0;                                     // nothing is staged or read for it
     const long head_row = ((long)sb * a.nkv + kvh) * a.ctx;  // cache row of position 0 in this layer
-    int pos = 0, n = 0;
-    auto stage = [&]() {   // thread 0: barrier + the four TMA boxes of this CTA
-        abort_flag = 0;
-        if (n > 0) {
-            mbar_init(&bar, 1);
-            fence_barrier_init();
-            mbar_arrive_expect_tx(&bar, 4u * C * 128);
-            const int row = (int)(a.row_base + head_row + j0);
-            tma_load_2d(sK, &tmK, 0, row, &bar);
-            tma_load_2d(sK + C * 128, &tmK, 64, row, &bar);
-            tma_load_2d(sV, &tmV, 0, row, &bar);
-            tma_load_2d(sV + C * 128, &tmV, 64, row, &bar);
-        }
+    int pos = 0, nch = 0;                                     // chunks holding positions <= pos
+    auto chunks = [&]() {
+        pos = bad_slot ? -1 : a.pos[b];
+        nch = (pos < 0 || pos >= a.ctx) ? 0 : min(cps, (pos - j0s) / C + 1);
+        if (pos < j0s) nch = 0;
     };
+    auto stage = [&](int c) {   // thread 0: the four TMA boxes of chunk c into stage c % nst
+        const int st = c % nst;
+        uint8_t *sK = base + st * kStageBytes, *sV = sK + 2 * C * 128;
+        mbar_arrive_expect_tx(&bar[st], kStageBytes);
+        const int row = (int)(a.row_base + head_row + j0s + c * C);
+        tma_load_2d(sK, &tmK, 0, row, &bar[st]);
+        tma_load_2d(sK + C * 128, &tmK, 64, row, &bar[st]);
+        tma_load_2d(sV, &tmV, 0, row, &bar[st]);
+        tma_load_2d(sV + C * 128, &tmV, 64, row, &bar[st]);
+    };
+    int issued = 0;                              // thread 0: chunks whose copies were started
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int st = 0; st < nst; ++st) mbar_init(&bar[st], 1);
+        fence_barrier_init();
+    }
     bool staged = false;
     if (a.kv_early) {
-        pos = bad_slot ? -1 : a.pos[b];
-        n = (pos < 0 || pos >= a.ctx) ? 0 : min(C, pos + 1 - j0);
+        chunks();
         if (threadIdx.x == 0) {
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            stage();
+            for (; issued < min(nst, nch); ++issued) stage(issued);
         }
         staged = true;
     }
     pdl_launch_dependents();
     pdl_wait();                                   // qkv comes from the previous kernel
     if (!staged) {
-        pos = bad_slot ? -1 : a.pos[b];
-        n = (pos < 0 || pos >= a.ctx) ? 0 : min(C, pos + 1 - j0);
-        if (threadIdx.x == 0) stage();
+        chunks();
+        if (threadIdx.x == 0)
+            for (; issued < min(nst, nch); ++issued) stage(issued);
     }
     if (pos < 0 || pos >= a.ctx) {   // KV overflow (the reference aborts, qwen_moe_q3k.c:1865-1868)
         if (threadIdx.x == 0 && sp == 0 && kvh == 0) atomicCAS(a.status, 0, X100_E_ARG);
         return;
     }
     const float *qrow = a.qkv + (long)b * a.qkv_n;
-    if (warp < gpr && n > 0) {
+    if (warp < gpr && nch > 0) {
         const int hh = kvh * gpr + warp;
         float4 v = __ldcg(reinterpret_cast<const float4 *>(qrow + hh * kHD) + lane);
         v = norm_rope_head(v, a.q_norm, a.eps, a.rope + (long)pos * (kHD / 2));
         reinterpret_cast<float4 *>(sQ + warp * kHD)[lane] = v;
     }
-    __syncthreads();                              // barrier initialised, queries ready
-    if (n > 0) mbar_wait(&bar, 0, &abort_flag, a.status);   // raises abort_flag on timeout
-    if (n > 0 && pos < j0 + C && warp == 0 && !a.prewritten) {
-        // the step's own k (normed, rotated) and v, rounded to the cache's fp16
-        float4 k = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + kvh) * kHD) + lane);
-        const float4 v = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + a.nkv + kvh) * kHD) + lane);
-        k = norm_rope_head(k, a.k_norm, a.eps, a.rope + (long)pos * (kHD / 2));
-        uint2 kk, vv;
-        kk.x = h2u(__floats2half2_rn(k.x, k.y));
-        kk.y = h2u(__floats2half2_rn(k.z, k.w));
-        vv.x = h2u(__floats2half2_rn(v.x, v.y));
-        vv.y = h2u(__floats2half2_rn(v.z, v.w));
-        reinterpret_cast<uint2 *>(a.kc + (head_row + pos) * kHD)[lane] = kk;
-        reinterpret_cast<uint2 *>(a.vc + (head_row + pos) * kHD)[lane] = vv;
-        *reinterpret_cast<uint2 *>(sK + kv_off(pos - j0, 4 * lane)) = kk;
-        *reinterpret_cast<uint2 *>(sV + kv_off(pos - j0, 4 * lane)) = vv;
-    }
-    __syncthreads();
-    const bool ok = abort_flag == 0 && n > 0;     // uniform over the CTA
-    // ---- S = Q . K^T for positions [16 warp, 16 warp + 16) ----
-    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    const int pw = 16 * warp;
-    const bool sw = pw < C;                       // warps holding score columns
-    if (ok && sw && pw < n) {
-        const uint32_t kbase = smem_u32(sK);
-        const int m = lane >> 3, r = lane & 7;
-        const int prow = pw + (m >> 1) * 8 + r;
-#pragma unroll
-        for (int kk = 0; kk < kHD / 16; ++kk) {
-            const float *qr = sQ + hq * kHD + 16 * kk + 2 * q4;
-            const bool live = hq < gpr;
-            const uint32_t a0 = live ? h2u(__floats2half2_rn(qr[0], qr[1])) : 0u;
-            const uint32_t a2 = live ? h2u(__floats2half2_rn(qr[8], qr[9])) : 0u;
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(kbase + kv_off(prow, 16 * kk + (m & 1) * 8), b0, b1, b2, b3);
-            mma16816(acc[0], a0, a2, b0, b1);
-            mma16816(acc[1], a0, a2, b2, b3);
-        }
-    }
-    // scores of head hq at positions pw + 8 nt + 2 q4 + {0, 1}; masked past n
-    float sc[4];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        const int jj = pw + 8 * (t >> 1) + 2 * q4 + (t & 1);
-        sc[t] = (ok && jj < n) ? acc[t >> 1][t & 1] * a.scale : -INFINITY;
-        mx = fmaxf(mx, sc[t]);
-    }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    if (q4 == 0) sMax[warp * 8 + hq] = mx;
-    __syncthreads();
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) M = fmaxf(M, sMax[w * 8 + hq]);
-    float ps[4], lsum = 0.f;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        ps[t] = sc[t] == -INFINITY ? 0.f : expf(sc[t] - M);
-        lsum += ps[t];
-    }
-    if (sw) {
-        *reinterpret_cast<__half2 *>(sP + hq * PS + pw + 2 * q4) = __floats2half2_rn(ps[0], ps[1]);
-        *reinterpret_cast<__half2 *>(sP + hq * PS + pw + 8 + 2 * q4) = __floats2half2_rn(ps[2], ps[3]);
-    }
-    lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
-    lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
-    if (q4 == 0) sSum[warp * 8 + hq] = lsum;
-    __syncthreads();
-    float L = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) L += sSum[w * 8 + hq];
-    // ---- O[:, 16 warp .. +16) = P . V ----
+    __syncthreads();                              // barriers initialised, queries ready
+    // running softmax state of head hq (the same in every warp) and this
+    // warp's 16 output dims of it
+    float m_run = -INFINITY, l_run = 0.f;
     float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    const int d0 = 16 * warp;
-    if (ok) {
-        const uint32_t vbase = smem_u32(sV);
-        const int m = lane >> 3, r = lane & 7;
+    bool ok = nch > 0;
+    int done = 0;
+    for (int c = 0; c < nch; ++c) {
+        const int st = c % nst, j0 = j0s + c * C, n = min(C, pos + 1 - j0);
+        uint8_t *sK = base + st * kStageBytes, *sV = sK + 2 * C * 128;
+        mbar_wait(&bar[st], (uint32_t)((c / nst) & 1), &abort_flag, a.status);   // raises abort_flag on timeout
+        done = c + 1;
+        if (pos < j0 + C && warp == 0 && !a.prewritten && abort_flag == 0) {
+            // the step's own k (normed, rotated) and v, rounded to the cache's fp16
+            float4 k = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + kvh) * kHD) + lane);
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(qrow + (a.nh + a.nkv + kvh) * kHD) + lane);
+            k = norm_rope_head(k, a.k_norm, a.eps, a.rope + (long)pos * (kHD / 2));
+            uint2 kk, vv;
+            kk.x = h2u(__floats2half2_rn(k.x, k.y));
+            kk.y = h2u(__floats2half2_rn(k.z, k.w));
+            vv.x = h2u(__floats2half2_rn(v.x, v.y));
+            vv.y = h2u(__floats2half2_rn(v.z, v.w));
+            reinterpret_cast<uint2 *>(a.kc + (head_row + pos) * kHD)[lane] = kk;
+            reinterpret_cast<uint2 *>(a.vc + (head_row + pos) * kHD)[lane] = vv;
+            *reinterpret_cast<uint2 *>(sK + kv_off(pos - j0, 4 * lane)) = kk;
+            *reinterpret_cast<uint2 *>(sV + kv_off(pos - j0, 4 * lane)) = vv;
+        }
+        __syncthreads();
+        ok = abort_flag == 0;                     // uniform over the CTA
+        if (!ok) break;
+        // ---- S = Q . K^T for positions [16 warp, 16 warp + 16) of the chunk ----
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const int pw = 16 * warp;
+        const bool sw = pw < C;                   // warps holding score columns
+        if (sw && pw < n) {
+            const uint32_t kbase = smem_u32(sK);
+            const int m = lane >> 3, r = lane & 7;
+            const int prow = pw + (m >> 1) * 8 + r;
 #pragma unroll
-        for (int kk = 0; kk < C / 16; ++kk) {
-            if (16 * kk < n) {
-                const uint32_t a0 = *reinterpret_cast<const uint32_t *>(sP + hq * PS + 16 * kk + 2 * q4);
-                const uint32_t a2 = *reinterpret_cast<const uint32_t *>(sP + hq * PS + 16 * kk + 8 + 2 * q4);
+            for (int kk = 0; kk < kHD / 16; ++kk) {
+                const float *qr = sQ + hq * kHD + 16 * kk + 2 * q4;
+                const bool live = hq < gpr;
+                const uint32_t a0 = live ? h2u(__floats2half2_rn(qr[0], qr[1])) : 0u;
+                const uint32_t a2 = live ? h2u(__floats2half2_rn(qr[8], qr[9])) : 0u;
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(vbase + kv_off(16 * kk + (m & 1) * 8 + r, d0 + (m >> 1) * 8), b0, b1, b2, b3);
-                mma16816(o[0], a0, a2, b0, b1);
-                mma16816(o[1], a0, a2, b2, b3);
+                ldsm_x4(kbase + kv_off(prow, 16 * kk + (m & 1) * 8), b0, b1, b2, b3);
+                mma16816(acc[0], a0, a2, b0, b1);
+                mma16816(acc[1], a0, a2, b2, b3);
             }
         }
+        // scores of head hq at positions pw + 8 nt + 2 q4 + {0, 1}; masked past n
+        float sc[4];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int jj = pw + 8 * (t >> 1) + 2 * q4 + (t & 1);
+            sc[t] = jj < n ? acc[t >> 1][t & 1] * a.scale : -INFINITY;
+            mx = fmaxf(mx, sc[t]);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        if (q4 == 0) sMax[warp * 8 + hq] = mx;
+        __syncthreads();
+        float M = m_run;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) M = fmaxf(M, sMax[w * 8 + hq]);
+        const float alpha = expf(m_run - M);      // 0 for the first chunk (m_run = -inf)
+        float ps[4], lsum = 0.f;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            ps[t] = sc[t] == -INFINITY ? 0.f : expf(sc[t] - M);
+            lsum += ps[t];
+        }
+        if (sw) {
+            *reinterpret_cast<__half2 *>(sP + hq * PS + pw + 2 * q4) = __floats2half2_rn(ps[0], ps[1]);
+            *reinterpret_cast<__half2 *>(sP + hq * PS + pw + 8 + 2 * q4) = __floats2half2_rn(ps[2], ps[3]);
+        }
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+        if (q4 == 0) sSum[warp * 8 + hq] = lsum;
+        __syncthreads();
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) L += sSum[w * 8 + hq];
+        l_run = l_run * alpha + L;
+        m_run = M;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[nt][i] *= alpha;
+        // ---- O[:, 16 warp .. +16) += P . V ----
+        const int d0 = 16 * warp;
+        {
+            const uint32_t vbase = smem_u32(sV);
+            const int m = lane >> 3, r = lane & 7;
+#pragma unroll
+            for (int kk = 0; kk < C / 16; ++kk) {
+                if (16 * kk < n) {
+                    const uint32_t a0 = *reinterpret_cast<const uint32_t *>(sP + hq * PS + 16 * kk + 2 * q4);
+                    const uint32_t a2 = *reinterpret_cast<const uint32_t *>(sP + hq * PS + 16 * kk + 8 + 2 * q4);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(vbase + kv_off(16 * kk + (m & 1) * 8 + r, d0 + (m >> 1) * 8), b0, b1, b2, b3);
+                    mma16816(o[0], a0, a2, b0, b1);
+                    mma16816(o[1], a0, a2, b2, b3);
+                }
+            }
+        }
+        __syncthreads();                          // stage st and sP are free again
+        if (threadIdx.x == 0 && issued < nch) stage(issued++);
     }
-    // o[nt][0..1]: head hq, dims d0 + 8 nt + 2 q4 + {0, 1}
+    // o[nt][0..1]: head hq, dims 16 warp + 8 nt + 2 q4 + {0, 1}
     const bool live = hq < gpr;
-    const int hh = kvh * gpr + hq;
-    if (live) {
+    const int hh = kvh * gpr + hq, d0 = 16 * warp;
+    if (live && nch > 0) {
         if (a.nsplit == 1) {
-            const float inv = L > 0.f ? 1.0f / L : 0.f;
+            const float inv = ok && l_run > 0.f ? 1.0f / l_run : 0.f;
             float *out = a.att + (long)b * a.nh * kHD + hh * kHD + d0 + 2 * q4;
             *reinterpret_cast<float2 *>(out) = make_float2(o[0][0] * inv, o[0][1] * inv);
             *reinterpret_cast<float2 *>(out + 8) = make_float2(o[1][0] * inv, o[1][1] * inv);
@@ -349,12 +377,21 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
             *reinterpret_cast<float2 *>(pr + d0 + 2 * q4) = make_float2(o[0][0], o[0][1]);
             *reinterpret_cast<float2 *>(pr + d0 + 8 + 2 * q4) = make_float2(o[1][0], o[1][1]);
             if (warp == 0 && q4 == 0) {
-                pr[kHD] = ok ? M : -INFINITY;
-                pr[kHD + 1] = ok ? L : 0.f;
+                pr[kHD] = ok ? m_run : -INFINITY;
+                pr[kHD + 1] = ok ? l_run : 0.f;
             }
         }
+    } else if (live && a.nsplit > 1) {            // a split past pos: an empty partial
+        float *pr = a.part + (((long)b * a.nh + hh) * a.nsplit + sp) * kPartStride;
+        *reinterpret_cast<float2 *>(pr + d0 + 2 * q4) = make_float2(0.f, 0.f);
+        *reinterpret_cast<float2 *>(pr + d0 + 8 + 2 * q4) = make_float2(0.f, 0.f);
+        if (warp == 0 && q4 == 0) {
+            pr[kHD] = -INFINITY;
+            pr[kHD + 1] = 0.f;
+        }
     }
-    if (threadIdx.x == 0 && n > 0 && abort_flag) mbar_wait_drain(&bar, 0, 100000000ull);
+    if (threadIdx.x == 0 && !ok)                  // copies still in flight after a timeout
+        for (int c = done; c < issued; ++c) mbar_wait_drain(&bar[c % nst], (uint32_t)((c / nst) & 1), 100000000ull);
 }
 
 // Grid (nh, B), 128 threads: att[b][head] = sum_s e^(m_s-M) o_s / sum_s
@@ -441,7 +478,25 @@ __global__ void __launch_bounds__(256) embed_kernel(const float *__restrict__ em
         reinterpret_cast<float4 *>(h + (long)b * d)[i] = __ldg(reinterpret_cast<const float4 *>(emb + (long)t * d) + i);
 }
 
-static size_t attn_smem() { return 1024 + (size_t)4 * kChunk * 128 + 8 * kHD * 4 + 8 * (kChunk + 8) * 2 + 128 * 4; }
+static size_t attn_smem(int cps = 1) {
+    return 1024 + (size_t)(cps > 1 ? 2 : 1) * 4 * kChunk * 128 + 8 * kHD * 4 + 8 * (kChunk + 8) * 2 + 128 * 4;
+}
+// Chunks per attention split for a decode step of `batch` tokens: one at
+// small batches (the splits are the grid's parallelism), more when the grid
+// has CTAs to spare, so each CTA streams several chunks through its ring and
+// the merge has fewer splits.
+// X100_ATTN_CPS (1..8) overrides the choice.
+static int attn_cps(int batch) {
+    static const int forced = [] {
+        const char *e = getenv("X100_ATTN_CPS");
+        const int v = e ? atoi(e) : 0;
+        return v >= 1 && v <= 8 ? v : 0;
+    }();
+    if (forced) return forced;
+    // measured, decode step at context 4096: batch 1 best with 1, batch 2 with
+    // 2, batch 4 and 16 with 4 (8 was slower at 16)
+    return batch >= 4 ? 4 : (batch >= 2 ? 2 : 1);
+}
 static size_t merge_smem(int nsplit) { return (size_t)(((2 * nsplit + 3) & ~3) + 4 * kHD) * 4; }
 
 }  // namespace dec
@@ -825,7 +880,8 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     a.nkv = g.n_kv_heads;
     a.ctx = g.ctx;
     a.chunk = kChunk;
-    a.nsplit = (g.ctx + kChunk - 1) / kChunk;
+    a.cps = attn_cps(batch);
+    a.nsplit = (g.ctx + kChunk * a.cps - 1) / (kChunk * a.cps);
     a.eps = g.eps;
     a.rope_base = g.rope_base;
     a.rope = m->rope;
@@ -845,7 +901,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
         st = launch_pdl(kv_write_kernel, dim3(g.n_kv_heads, batch), dim3(32), 0, s, a);
         if (st) return st;
     }
-    st = launch_pdl(attn_decode_kernel, dim3(a.nsplit, g.n_kv_heads, batch), dim3(kAttnThreads), attn_smem(), s,
+    st = launch_pdl(attn_decode_kernel, dim3(a.nsplit, g.n_kv_heads, batch), dim3(kAttnThreads), attn_smem(a.cps), s,
                     m->tmK, m->tmV, a);
     if (st) return st;
     if (a.nsplit > 1) {
@@ -1077,6 +1133,7 @@ static int prefill_chunk_tc(x100q_model *m, DevCtx *c, const int *tok, float *h,
         a.nkv = g.n_kv_heads;
         a.ctx = g.ctx;
         a.chunk = kChunk;
+        a.cps = 1;
         a.nsplit = (g.ctx + kChunk - 1) / kChunk;
         a.eps = g.eps;
         a.rope_base = g.rope_base;
