@@ -28,6 +28,10 @@
 #include "ptx.cuh"
 
 namespace x100 {
+bool pdl_enabled();   // qgemv.cu: false when X100_NO_PDL is set
+}
+
+namespace x100 {
 namespace tc {
 
 constexpr int BM = 128;
@@ -522,6 +526,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     cluster_sync_all();                  // barriers of both CTAs initialised, TMEM allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched with programmatic dependent launch, the CTA may start while the
+    // previous kernel of the stream runs: the setup above overlaps its tail,
+    // and nothing touches A, B or C before it has completed.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const int num_m = (M + TM - 1) / TM;
     const int num_n = (N + TN - 1) / TN;
@@ -739,9 +748,19 @@ static int launch_te(DevCtx *c, int M, int N, int K, const CUtensorMap &ta, cons
         // K = 4096 and 9.7e-6 at K = 8192 in one piece); int8 is exact and
         // fp16 C is rounded to fp16 anyway: one piece
         const int kp = KIND == 3 ? kpiece / (128 / Traits<KIND>::ES) : KIND == 1 ? 4096 / 64 : (1 << 30);
-        gemm_tc2_kernel<KIND, TE><<<2 * pairs, THREADS, P_SMEM_BYTES, s>>>(
-            ta, tb, tc_, ta2, tb2, reinterpret_cast<CT *>(C), M, N, K, ldc, sk, kp, c->d_status);
-        return check_cuda(cudaGetLastError(), X100_E_LAUNCH);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * pairs);
+        cfg.blockDim = dim3(THREADS);
+        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl_enabled() ? 1 : 0;
+        return check_cuda(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<KIND, TE>, ta, tb, tc_, ta2, tb2,
+                                             reinterpret_cast<CT *>(C), M, N, K, ldc, sk, kp, c->d_status),
+                          X100_E_LAUNCH);
     }
     if constexpr (KIND == 3) {   // the 3-product form exists only as a 2-SM kernel
         set_error(X100_E_UNSUPPORTED);
