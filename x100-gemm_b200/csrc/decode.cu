@@ -166,17 +166,19 @@ __global__ void __launch_bounds__(32) kv_write_kernel(const AttnArgs a) {
 }
 
 // Grid (nsplit, nkv, B).  CTA (sp, kvh, b) attends the query heads of kv head
-// kvh over positions [sp*64, min((sp+1)*64, pos+1)).  Its K and V rows
-// arrive by TMA (two 64-dim boxes each, 128-byte swizzle); the queries of the
-// group (warp h: head kvh*gpr + h) are normed, rotated and held as the rows
-// of an m16n8k16 A operand (rows gpr..15 zero).  Warp w < 4 computes the
-// scores S = Q.K^T of positions [16w, 16w+16) on the tensor cores; the
-// CTA-wide row max and sum go through shared memory; P = e^(S-M) is stored as
-// fp16 and warp w computes O[:, 16w..16w+16) = P.V over all positions.  The
-// CTA whose range holds pos first computes the step's k and v (norm + RoPE on
-// k), stores them to the cache in fp16 and into the staged tile.  Output: a
-// partial (o, m, l) per head, merged by attn_merge_kernel (or att itself when
-// there is one split).
+// kvh over positions [sp*64*cps, min((sp+1)*64*cps, pos+1)), cps chunks of 64
+// positions (a.cps; above one they stream through a two-stage ring).  A
+// chunk's K and V rows arrive by TMA (two 64-dim boxes each, 128-byte
+// swizzle); the queries of the group (warp h: head kvh*gpr + h) are normed,
+// rotated and held as the rows of an m16n8k16 A operand (rows gpr..15 zero).
+// Warp w < 4 computes the scores S = Q.K^T of positions [16w, 16w+16) of the
+// chunk on the tensor cores; the CTA-wide row max and sum go through shared
+// memory and update the running max, sum and output of each head (online
+// softmax); P = e^(S-M) is stored as fp16 and warp w accumulates
+// O[:, 16w..16w+16) += P.V.  The chunk holding pos first gets the step's k
+// and v (norm + RoPE on k), stored to the cache in fp16 and into the staged
+// tile.  Output: a partial (o, m, l) per head, merged by attn_merge_kernel (or
+// att itself when there is one split).
 // With kv_early the step began behind a full barrier (every earlier step is
 // complete), so positions < pos of the cache are final and the CTA reads pos
 // and stages its K/V rows before waiting on the previous kernel.
