@@ -740,6 +740,7 @@ constexpr int kWsThreads = 32 * (kWsWarps + 1);
 constexpr int kWsMaxSt = 4;
 constexpr int kWsTok = 4;                    // tokens dotted per pass over a lane's half slices
 constexpr size_t kWsSmem = 215 * 1024;       // dynamic shared memory (PipeMeta and the barriers are static)
+template <int N> struct IntC { static constexpr int value = N; };   // a token count as a type
 
 // lanes per row: the row's 2 ns half slices, at most cap lanes (then a lane
 // takes half slices ls, ls + cap, ...)
@@ -855,11 +856,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         const int rows = min(TR, ffn - t * TR), np = M.cnt[k];
         const bool live = rr < rpw && rin < rows;
         const uint8_t *wg = smem + (size_t)st * stage_b + (long)rin * rb, *wu = wg + TR * rb;
-        for (int j0 = 0; j0 < np; j0 += kWsTok) {   // passes of kWsTok tokens (one for most experts)
-            float ag[kWsTok] = {}, au[kWsTok] = {};
-            const uint8_t *xt[kWsTok];
+        // one pass over the lane's half slices for NT tokens j0 .. j0 + NT - 1;
+        // NT is a compile-time constant, so no dot is issued for an empty token slot
+        auto pass = [&](int j0, auto ntc) {
+            constexpr int NT = decltype(ntc)::value;
+            float ag[NT] = {}, au[NT] = {};
+            const uint8_t *xt[NT];
 #pragma unroll
-            for (int jj = 0; jj < kWsTok; ++jj) xt[jj] = xa + (size_t)M.tok[k][min(j0 + jj, np - 1)] * xb1;
+            for (int jj = 0; jj < NT; ++jj) xt[jj] = xa + (size_t)M.tok[k][j0 + jj] * xb1;
             for (int hq = ls; live && hq < hsr; hq += seg) {
                 UHalf<QT> ug, uu;
                 {
@@ -871,23 +875,29 @@ __global__ void __launch_bounds__(kWsThreads, 1)
                 }
                 const int xo = (hq >> 1) * kXSlice + (hq & 1) * kXHalf;
 #pragma unroll
-                for (int jj = 0; jj < kWsTok; ++jj)
-                    if (j0 + jj < np) {
-                        const XB *x = reinterpret_cast<const XB *>(xt[jj] + xo);
-                        ag[jj] += dot_uhalf<QT>(ug, x);
-                        au[jj] += dot_uhalf<QT>(uu, x);
-                    }
+                for (int jj = 0; jj < NT; ++jj) {
+                    const XB *x = reinterpret_cast<const XB *>(xt[jj] + xo);
+                    ag[jj] += dot_uhalf<QT>(ug, x);
+                    au[jj] += dot_uhalf<QT>(uu, x);
+                }
             }
-            if (j0 + kWsTok >= np) {             // the last read of this stage
+            if (j0 + NT >= np) {                 // the last read of this stage
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[st]);
             }
 #pragma unroll
-            for (int jj = 0; jj < kWsTok; ++jj)
-                if (j0 + jj < np) {
-                    const float g = seg_sum(ag[jj], ls, seg, top), u = seg_sum(au[jj], ls, seg, top);
-                    if (ls == 0 && live) h[(long)(M.start[k] + j0 + jj) * ffn + t * TR + rin] = swiglu(g, u);
-                }
+            for (int jj = 0; jj < NT; ++jj) {
+                const float g = seg_sum(ag[jj], ls, seg, top), u = seg_sum(au[jj], ls, seg, top);
+                if (ls == 0 && live) h[(long)(M.start[k] + j0 + jj) * ffn + t * TR + rin] = swiglu(g, u);
+            }
+        };
+        for (int j0 = 0; j0 < np; j0 += kWsTok) {   // passes of up to kWsTok tokens (one for most experts)
+            switch (min(np - j0, kWsTok)) {
+            case 1: pass(j0, IntC<1>{}); break;
+            case 2: pass(j0, IntC<2>{}); break;
+            case 3: pass(j0, IntC<3>{}); break;
+            default: pass(j0, IntC<kWsTok>{}); break;
+            }
         }
     }
 }
@@ -982,8 +992,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         const bool live0 = rr < rpw && rin < rows, live1 = rr < rpw && rin + TRh < rows;
         const uint8_t *w0 = smem + (size_t)st * stage_b + (long)rin * rb, *w1 = w0 + (long)TRh * rb;
         const uint8_t *xh = smem + (size_t)st * stage_b + wbytes;   // the expert's slots, xb1 apart
-        for (int j0 = 0; j0 < np; j0 += kWsTok) {
-            float a0[kWsTok] = {}, a1[kWsTok] = {};
+        auto pass = [&](int j0, auto ntc) {      // NT tokens from j0, NT known at compile time
+            constexpr int NT = decltype(ntc)::value;
+            float a0[NT] = {}, a1[NT] = {};
             for (int hq2 = ls; live0 && hq2 < hsr; hq2 += seg) {
                 UHalf<QT> u0, u1;
                 {
@@ -995,25 +1006,31 @@ __global__ void __launch_bounds__(kWsThreads, 1)
                 }
                 const uint8_t *xo = xh + (size_t)j0 * xb1 + (hq2 >> 1) * kXSlice + (hq2 & 1) * kXHalf;
 #pragma unroll
-                for (int jj = 0; jj < kWsTok; ++jj)
-                    if (j0 + jj < np) {
-                        const XB *x = reinterpret_cast<const XB *>(xo + (size_t)jj * xb1);
-                        a0[jj] += dot_uhalf<QT>(u0, x);
-                        a1[jj] += dot_uhalf<QT>(u1, x);
-                    }
+                for (int jj = 0; jj < NT; ++jj) {
+                    const XB *x = reinterpret_cast<const XB *>(xo + (size_t)jj * xb1);
+                    a0[jj] += dot_uhalf<QT>(u0, x);
+                    a1[jj] += dot_uhalf<QT>(u1, x);
+                }
             }
-            if (j0 + kWsTok >= np) {
+            if (j0 + NT >= np) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[st]);
             }
 #pragma unroll
-            for (int jj = 0; jj < kWsTok; ++jj)
-                if (j0 + jj < np) {
-                    const float v0 = seg_sum(a0[jj], ls, seg, top), v1 = seg_sum(a1[jj], ls, seg, top);
-                    float *o = part + (long)M.pairs[k][j0 + jj] * d + t * TR + rin;
-                    if (ls == 0 && live0) o[0] = v0;
-                    if (ls == 0 && live1) o[TRh] = v1;
-                }
+            for (int jj = 0; jj < NT; ++jj) {
+                const float v0 = seg_sum(a0[jj], ls, seg, top), v1 = seg_sum(a1[jj], ls, seg, top);
+                float *o = part + (long)M.pairs[k][j0 + jj] * d + t * TR + rin;
+                if (ls == 0 && live0) o[0] = v0;
+                if (ls == 0 && live1) o[TRh] = v1;
+            }
+        };
+        for (int j0 = 0; j0 < np; j0 += kWsTok) {
+            switch (min(np - j0, kWsTok)) {
+            case 1: pass(j0, IntC<1>{}); break;
+            case 2: pass(j0, IntC<2>{}); break;
+            case 3: pass(j0, IntC<3>{}); break;
+            default: pass(j0, IntC<kWsTok>{}); break;
+            }
         }
     }
 }
