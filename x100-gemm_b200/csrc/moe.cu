@@ -729,14 +729,19 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
 // A producer warp streams the items (active expert k, row tile) into a ring
 // of nst shared-memory stages with bulk copies (full[s] completes on the
 // copied bytes; empty[s] takes one arrival per consumer warp once it has read
-// the stage) and kWsWarps consumer warps compute them; warps wait for one
+// the stage) and NW consumer warps compute them; warps wait for one
 // another only through the ring.  A consumer lane owns one half slice of a
 // row (or several, seg apart), unpacks it once (unpack_half) and dots it with
 // every token of the expert; the seg lanes of a row then sum their terms with
 // shuffles.  Expert k's tokens are its slots start[k] .. start[k] + cnt[k] - 1
 // of the grouped h / hq buffers.
-constexpr int kWsWarps = 8;                  // + the producer: 9 warps, up to 168 registers a thread
-constexpr int kWsThreads = 32 * (kWsWarps + 1);
+// Consumer warps per kernel: with the producer, 12 warps = 3 on each of the
+// SM's four schedulers, whose register files cap a thread at 168 registers
+// (the unpacked half slices need ~150).  A 17th warp puts 5 warps on one
+// scheduler and caps every thread at 96 registers; 8 consumers left three
+// schedulers with 2 warps each.
+constexpr int kWsGateWarps = 11;
+constexpr int kWsDownWarps = 11;
 constexpr int kWsMaxSt = 4;
 constexpr int kWsTok = 4;                    // tokens dotted per pass over a lane's half slices
 constexpr size_t kWsSmem = 215 * 1024;       // dynamic shared memory (PipeMeta and the barriers are static)
@@ -791,14 +796,14 @@ __device__ __forceinline__ void ws_produce(int nst, int W, int *work, uint64_t *
         mbar_wait_drain(&full[u % nst], (uint32_t)((u / nst) & 1), 100000000ull);
 }
 
-// gate / up: an item is (k, TR = kWsWarps * rpw rows of gate and the same
+// gate / up: an item is (k, TR = NW * rpw rows of gate and the same
 // rows of up); a warp holds rpw rows of seg lanes, and a lane the same half
 // slice of the row in both matrices, so each activation load serves both
 // dots.  The prepared activations of the batch's nb tokens (xq, token after
 // token) are copied into shared memory once per CTA.  Writes h[slot][row] =
 // silu(gate . x) * (up . x) (qwen_moe.c:304-309).
-template <int QT>
-__global__ void __launch_bounds__(kWsThreads, 1)
+template <int QT, int NW>
+__global__ void __launch_bounds__(32 * (NW + 1), 1)
     gate_up_ws_kernel(const uint8_t *__restrict__ gw, const uint8_t *__restrict__ uw, int ffn, int d, int n_exp,
                       int n_act, int nb, int nst, const int *__restrict__ grp, const uint8_t *__restrict__ xq,
                       float *__restrict__ h, int *__restrict__ work, int *status) {
@@ -810,14 +815,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     constexpr int SB = slice_bytes(QT);
     const int ns = slices_per_row(d), xb1 = xbuf_bytes(ns, 1), hsr = 2 * ns;
     const long rb = row_bytes_dev(QT, d);
-    const int seg = ws_seg(hsr, 32), rpw = 32 / seg, TR = kWsWarps * rpw;
+    const int seg = ws_seg(hsr, 32), rpw = 32 / seg, TR = NW * rpw;
     const int stage_b = (int)(2 * TR * rb);
     uint8_t *xa = smem + (size_t)nst * stage_b;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int st = 0; st < nst; ++st) {
             mbar_init(&full[st], 1);
-            mbar_init(&empty[st], kWsWarps);
+            mbar_init(&empty[st], NW);
         }
         mbar_init(&xbar, 1);
         abort_flag = 0;
@@ -827,7 +832,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     pdl_launch_dependents();
     load_meta(grp, n_exp, n_act, M);
     const int tiles = (ffn + TR - 1) / TR, W = M.n_active * tiles;
-    if (warp == kWsWarps) {                      // producer
+    if (warp == NW) {                      // producer
         if (lane == 0) {
             mbar_arrive_expect_tx(&xbar, (uint32_t)(nb * xb1));
             stage_bytes(xa, xq, (uint32_t)(nb * xb1), &xbar);
@@ -910,15 +915,15 @@ __global__ void __launch_bounds__(256) prep_slots_kernel(const float *__restrict
     xprep_rows([h, p, ffn](int) { return h + (long)p * ffn; }, ffn, 1, xbuf_at(hq + (size_t)p * xbuf_bytes(ns, 1), ns));
 }
 
-// down: an item is (k, TR = 2 kWsWarps rpw rows of down); a warp holds rpw
+// down: an item is (k, TR = 2 NW rpw rows of down); a warp holds rpw
 // pairs of rows of seg lanes, a lane the same half slice of row r and row r
 // + TR / 2 (one activation load, two dots); a stage holds the rows and the
 // expert's prepared h (its slots, contiguous in hq).  Writes
 // the unweighted part[pair][row] for the combine.  The weights of the first
 // stages are requested before the dependency wait (the groups are final once
 // this kernel runs: the gate / up kernel read them behind its own wait).
-template <int QT>
-__global__ void __launch_bounds__(kWsThreads, 1)
+template <int QT, int NW>
+__global__ void __launch_bounds__(32 * (NW + 1), 1)
     down_ws_kernel(const uint8_t *__restrict__ dw, int ffn, int d, int n_exp, int nb, int nst,
                    const int *__restrict__ grp, const uint8_t *__restrict__ hq, float *__restrict__ part,
                    int *__restrict__ work, int *status) {
@@ -930,20 +935,20 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     constexpr int SB = slice_bytes(QT);
     const int ns = slices_per_row(ffn), xb1 = xbuf_bytes(ns, 1), hsr = 2 * ns;
     const long rb = row_bytes_dev(QT, ffn);
-    const int seg = ws_seg(hsr, 32), rpw = 32 / seg, TRh = kWsWarps * rpw, TR = 2 * TRh;
+    const int seg = ws_seg(hsr, 32), rpw = 32 / seg, TRh = NW * rpw, TR = 2 * TRh;
     const int wbytes = (int)(TR * rb), stage_b = wbytes + nb * xb1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int st = 0; st < nst; ++st) {
             mbar_init(&full[st], 1);
-            mbar_init(&empty[st], kWsWarps);
+            mbar_init(&empty[st], NW);
         }
         abort_flag = 0;
         fence_barrier_init();
     }
     load_meta(grp, n_exp, 1, M);
     const int tiles = (d + TR - 1) / TR, W = M.n_active * tiles;
-    if (warp == kWsWarps) {                      // producer
+    if (warp == NW) {                      // producer
         if (lane == 0) {
             int nfill = 0;                       // stages whose h copies wait for the dependency
             int pend_st[kWsMaxSt], pend_k[kWsMaxSt];
@@ -1041,7 +1046,7 @@ struct WsPlan {
     size_t smem = 0;
 };
 static WsPlan ws_plan_gate_up(int qt, int d, int batch) {
-    const int ns = slices_per_row(d), seg = ws_seg(2 * ns, 32), TR = kWsWarps * (32 / seg);
+    const int ns = slices_per_row(d), seg = ws_seg(2 * ns, 32), TR = kWsGateWarps * (32 / seg);
     const size_t stage = 2 * (size_t)TR * row_bytes_dev(qt, d), xb1 = xbuf_bytes(ns, 1);
     WsPlan p;   // the deepest ring that leaves room for every token (none: the pipelined kernels)
     const size_t xs = (size_t)batch * xb1;
@@ -1051,7 +1056,7 @@ static WsPlan ws_plan_gate_up(int qt, int d, int batch) {
     return p;
 }
 static WsPlan ws_plan_down(int qt, int ffn, int batch) {
-    const int ns = slices_per_row(ffn), seg = ws_seg(2 * ns, 32), TR = 2 * kWsWarps * (32 / seg);
+    const int ns = slices_per_row(ffn), seg = ws_seg(2 * ns, 32), TR = 2 * kWsDownWarps * (32 / seg);
     const size_t stage = (size_t)TR * row_bytes_dev(qt, ffn) + (size_t)batch * xbuf_bytes(ns, 1);
     WsPlan p;
     p.nst = (int)std::min<size_t>(kWsMaxSt, kWsSmem / stage);
@@ -1494,8 +1499,8 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
         set_qkernel_attrs(route_group_kernel);
         set_qkernel_attrs(gate_up_pipe_kernel<QT>, (int)kPipeSmem);
         set_qkernel_attrs(down_pipe_kernel<QT>, (int)kPipeSmem);
-        set_qkernel_attrs(gate_up_ws_kernel<QT>, (int)kWsSmem);
-        set_qkernel_attrs(down_ws_kernel<QT>, (int)kWsSmem);
+        set_qkernel_attrs(gate_up_ws_kernel<QT, kWsGateWarps>, (int)kWsSmem);
+        set_qkernel_attrs(down_ws_kernel<QT, kWsDownWarps>, (int)kWsSmem);
         set_qkernel_attrs(prep_slots_kernel);
         set_qkernel_attrs(combine_kernel);
         set_qkernel_attrs(moe_fused_kernel<QT>, 220 * 1024);
@@ -1544,13 +1549,13 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
     static const bool no_ws = getenv("X100_MOE_NO_WS") != nullptr;
     const WsPlan pg = ws_plan_gate_up(QT, L.d, batch), pd = ws_plan_down(QT, L.ffn, batch);
     if (pg.nst && pd.nst && !no_ws) {
-        st = launch_pdl(gate_up_ws_kernel<QT>, dim3(G), dim3(kWsThreads), pg.smem, s, (const uint8_t *)L.gate.w,
+        st = launch_pdl(gate_up_ws_kernel<QT, kWsGateWarps>, dim3(G), dim3(32 * (kWsGateWarps + 1)), pg.smem, s, (const uint8_t *)L.gate.w,
                         (const uint8_t *)L.up.w, L.ffn, L.d, L.n_exp, L.n_act, batch, pg.nst, (const int *)S.grp,
                         (const uint8_t *)S.xq, S.h, S.cnt + 1, c->d_status);
         if (st) return st;
         st = launch_pdl(prep_slots_kernel, dim3(batch * L.n_act), dim3(256), 0, s, (const float *)S.h, L.ffn, S.hq);
         if (st) return st;
-        st = launch_pdl(down_ws_kernel<QT>, dim3(G), dim3(kWsThreads), pd.smem, s, (const uint8_t *)L.down.w, L.ffn,
+        st = launch_pdl(down_ws_kernel<QT, kWsDownWarps>, dim3(G), dim3(32 * (kWsDownWarps + 1)), pd.smem, s, (const uint8_t *)L.down.w, L.ffn,
                         L.d, L.n_exp, batch, pd.nst, (const int *)S.grp, (const uint8_t *)S.hq, S.part, S.cnt + 2,
                         c->d_status);
         if (st) return st;
