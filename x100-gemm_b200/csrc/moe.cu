@@ -735,17 +735,29 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
 // every token of the expert; the seg lanes of a row then sum their terms with
 // shuffles.  Expert k's tokens are its slots start[k] .. start[k] + cnt[k] - 1
 // of the grouped h / hq buffers.
-// Consumer warps per kernel: with the producer, 12 warps = 3 on each of the
-// SM's four schedulers, whose register files cap a thread at 168 registers
-// (the unpacked half slices need ~150).  A 17th warp puts 5 warps on one
-// scheduler and caps every thread at 96 registers; 8 consumers left three
-// schedulers with 2 warps each.
-constexpr int kWsGateWarps = 11;
-constexpr int kWsDownWarps = 11;
+// Consumer warps per kernel, with the producer 16 (4 on each of the SM's
+// four schedulers, whose register files then cap a thread at 128 registers)
+// when the ring of the wider item still has two stages in the shared memory
+// left by the batch's activations, else 12 (3 per scheduler, 168 registers).
+// A 17th warp would put 5 warps on one scheduler and cap every thread at 96.
+constexpr int kWsWide = 15;
+constexpr int kWsNarrow = 11;
+// Q4_K's two unpacked half slices do not fit 128 registers (ptxas spills)
+constexpr bool ws_wide_fits(int qt) { return qt != Q4_K; }
 constexpr int kWsMaxSt = 4;
-constexpr int kWsTok = 4;                    // tokens dotted per pass over a lane's half slices
+constexpr int kWsTok = 2;                    // tokens dotted per pass over a lane's half slices (more need more registers)
 constexpr size_t kWsSmem = 215 * 1024;       // dynamic shared memory (PipeMeta and the barriers are static)
 template <int N> struct IntC { static constexpr int value = N; };   // a token count as a type
+// f(IntC<n>{}) for a run-time n in 1 .. N
+template <int N, typename F> __device__ __forceinline__ void with_count(int n, F &&f) {
+    if constexpr (N > 1) {
+        if (n < N) {
+            with_count<N - 1>(n, f);
+            return;
+        }
+    }
+    f(IntC<N>{});
+}
 
 // lanes per row: the row's 2 ns half slices, at most cap lanes (then a lane
 // takes half slices ls, ls + cap, ...)
@@ -897,12 +909,7 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
             }
         };
         for (int j0 = 0; j0 < np; j0 += kWsTok) {   // passes of up to kWsTok tokens (one for most experts)
-            switch (min(np - j0, kWsTok)) {
-            case 1: pass(j0, IntC<1>{}); break;
-            case 2: pass(j0, IntC<2>{}); break;
-            case 3: pass(j0, IntC<3>{}); break;
-            default: pass(j0, IntC<kWsTok>{}); break;
-            }
+            with_count<kWsTok>(min(np - j0, kWsTok), [&](auto c) { pass(j0, c); });
         }
     }
 }
@@ -1030,39 +1037,41 @@ __global__ void __launch_bounds__(32 * (NW + 1), 1)
             }
         };
         for (int j0 = 0; j0 < np; j0 += kWsTok) {
-            switch (min(np - j0, kWsTok)) {
-            case 1: pass(j0, IntC<1>{}); break;
-            case 2: pass(j0, IntC<2>{}); break;
-            case 3: pass(j0, IntC<3>{}); break;
-            default: pass(j0, IntC<kWsTok>{}); break;
-            }
+            with_count<kWsTok>(min(np - j0, kWsTok), [&](auto c) { pass(j0, c); });
         }
     }
 }
 
 // Launch shape of the warp-specialised kernels: stages and staged tokens.
 struct WsPlan {
-    int nst = 0;
+    int nst = 0, nw = 0;
     size_t smem = 0;
 };
-static WsPlan ws_plan_gate_up(int qt, int d, int batch) {
-    const int ns = slices_per_row(d), seg = ws_seg(2 * ns, 32), TR = kWsGateWarps * (32 / seg);
+static WsPlan ws_plan_gate_up(int qt, int d, int batch, int nw) {
+    const int ns = slices_per_row(d), seg = ws_seg(2 * ns, 32), TR = nw * (32 / seg);
     const size_t stage = 2 * (size_t)TR * row_bytes_dev(qt, d), xb1 = xbuf_bytes(ns, 1);
     WsPlan p;   // the deepest ring that leaves room for every token (none: the pipelined kernels)
     const size_t xs = (size_t)batch * xb1;
     if (xs < kWsSmem) p.nst = (int)std::min<size_t>(kWsMaxSt, (kWsSmem - xs) / stage);
     if (p.nst < 2) p.nst = 0;
     if (p.nst) p.smem = p.nst * stage + xs;
+    p.nw = nw;
     return p;
 }
-static WsPlan ws_plan_down(int qt, int ffn, int batch) {
-    const int ns = slices_per_row(ffn), seg = ws_seg(2 * ns, 32), TR = 2 * kWsDownWarps * (32 / seg);
+static WsPlan ws_plan_down(int qt, int ffn, int batch, int nw) {
+    const int ns = slices_per_row(ffn), seg = ws_seg(2 * ns, 32), TR = 2 * nw * (32 / seg);
     const size_t stage = (size_t)TR * row_bytes_dev(qt, ffn) + (size_t)batch * xbuf_bytes(ns, 1);
     WsPlan p;
     p.nst = (int)std::min<size_t>(kWsMaxSt, kWsSmem / stage);
     if (p.nst < 2) p.nst = 0;
     if (p.nst) p.smem = p.nst * stage;
+    p.nw = nw;
     return p;
+}
+// the wide kernel when its ring fits, else the narrow one (nst = 0: neither)
+static WsPlan ws_plan(WsPlan (*plan)(int, int, int, int), int qt, int n, int batch) {
+    const WsPlan w = ws_wide_fits(qt) ? plan(qt, n, batch, kWsWide) : WsPlan{};
+    return w.nst ? w : plan(qt, n, batch, kWsNarrow);
 }
 
 // combine: eout[token][n] = sum over the token's local slots, in slot order,
@@ -1499,8 +1508,12 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
         set_qkernel_attrs(route_group_kernel);
         set_qkernel_attrs(gate_up_pipe_kernel<QT>, (int)kPipeSmem);
         set_qkernel_attrs(down_pipe_kernel<QT>, (int)kPipeSmem);
-        set_qkernel_attrs(gate_up_ws_kernel<QT, kWsGateWarps>, (int)kWsSmem);
-        set_qkernel_attrs(down_ws_kernel<QT, kWsDownWarps>, (int)kWsSmem);
+        if constexpr (ws_wide_fits(QT)) {
+            set_qkernel_attrs(gate_up_ws_kernel<QT, kWsWide>, (int)kWsSmem);
+            set_qkernel_attrs(down_ws_kernel<QT, kWsWide>, (int)kWsSmem);
+        }
+        set_qkernel_attrs(gate_up_ws_kernel<QT, kWsNarrow>, (int)kWsSmem);
+        set_qkernel_attrs(down_ws_kernel<QT, kWsNarrow>, (int)kWsSmem);
         set_qkernel_attrs(prep_slots_kernel);
         set_qkernel_attrs(combine_kernel);
         set_qkernel_attrs(moe_fused_kernel<QT>, 220 * 1024);
@@ -1547,17 +1560,31 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
     if (o.mark) o.mark(o.mark_ctx, X100Q_T_EXPERT, s);
     const int G = c->sm_count;   // persistent: one CTA per SM
     static const bool no_ws = getenv("X100_MOE_NO_WS") != nullptr;
-    const WsPlan pg = ws_plan_gate_up(QT, L.d, batch), pd = ws_plan_down(QT, L.ffn, batch);
+    const WsPlan pg = ws_plan(ws_plan_gate_up, QT, L.d, batch), pd = ws_plan(ws_plan_down, QT, L.ffn, batch);
     if (pg.nst && pd.nst && !no_ws) {
-        st = launch_pdl(gate_up_ws_kernel<QT, kWsGateWarps>, dim3(G), dim3(32 * (kWsGateWarps + 1)), pg.smem, s, (const uint8_t *)L.gate.w,
-                        (const uint8_t *)L.up.w, L.ffn, L.d, L.n_exp, L.n_act, batch, pg.nst, (const int *)S.grp,
-                        (const uint8_t *)S.xq, S.h, S.cnt + 1, c->d_status);
+        auto gate_up = [&](auto nwc) {
+            constexpr int NW = decltype(nwc)::value;
+            return launch_pdl(gate_up_ws_kernel<QT, NW>, dim3(G), dim3(32 * (NW + 1)), pg.smem, s,
+                              (const uint8_t *)L.gate.w, (const uint8_t *)L.up.w, L.ffn, L.d, L.n_exp, L.n_act, batch,
+                              pg.nst, (const int *)S.grp, (const uint8_t *)S.xq, S.h, S.cnt + 1, c->d_status);
+        };
+        auto down = [&](auto nwc) {
+            constexpr int NW = decltype(nwc)::value;
+            return launch_pdl(down_ws_kernel<QT, NW>, dim3(G), dim3(32 * (NW + 1)), pd.smem, s,
+                              (const uint8_t *)L.down.w, L.ffn, L.d, L.n_exp, batch, pd.nst, (const int *)S.grp,
+                              (const uint8_t *)S.hq, S.part, S.cnt + 2, c->d_status);
+        };
+        if constexpr (ws_wide_fits(QT))
+            st = pg.nw == kWsWide ? gate_up(IntC<kWsWide>{}) : gate_up(IntC<kWsNarrow>{});
+        else
+            st = gate_up(IntC<kWsNarrow>{});
         if (st) return st;
         st = launch_pdl(prep_slots_kernel, dim3(batch * L.n_act), dim3(256), 0, s, (const float *)S.h, L.ffn, S.hq);
         if (st) return st;
-        st = launch_pdl(down_ws_kernel<QT, kWsDownWarps>, dim3(G), dim3(32 * (kWsDownWarps + 1)), pd.smem, s, (const uint8_t *)L.down.w, L.ffn,
-                        L.d, L.n_exp, batch, pd.nst, (const int *)S.grp, (const uint8_t *)S.hq, S.part, S.cnt + 2,
-                        c->d_status);
+        if constexpr (ws_wide_fits(QT))
+            st = pd.nw == kWsWide ? down(IntC<kWsWide>{}) : down(IntC<kWsNarrow>{});
+        else
+            st = down(IntC<kWsNarrow>{});
         if (st) return st;
     } else {
         const int TRg = gate_up_rows_per_cta(QT, L.d), TRd = down_rows_per_cta(QT, L.ffn);
