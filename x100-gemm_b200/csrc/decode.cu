@@ -483,21 +483,40 @@ __global__ void __launch_bounds__(256) embed_kernel(const float *__restrict__ em
 static size_t attn_smem(int cps = 1) {
     return 1024 + (size_t)(cps > 1 ? 2 : 1) * 4 * kChunk * 128 + 8 * kHD * 4 + 8 * (kChunk + 8) * 2 + 128 * 4;
 }
-// Chunks per attention split for a decode step of `batch` tokens: one at
-// small batches (the splits are the grid's parallelism), more when the grid
-// has CTAs to spare, so each CTA streams several chunks through its ring and
-// the merge has fewer splits.
+// Chunks per attention split (cps) for a decode step of `batch` tokens over
+// ctx positions.  A CTA streams its cps chunks through the TMA ring, so a wave
+// of the grid lasts about cps chunk times: the choice minimises waves x cps,
+// a wave being the SM count x the CTAs resident on an SM, and on a tie takes
+// more chunks per CTA (fewer splits to merge, less setup per chunk).  At
+// context 4096 this picks 1 at batch 1, 2 at batch 2, 3 at batch 4 and 5 at
+// batch 16, the best of the measured settings (batch 16: 1948 tokens/s with
+// 5, 1916 with 4, 1926 with 6; batch 4: 901 with 3, 892 with 4, 864 with 1).
 // X100_ATTN_CPS (1..8) overrides the choice.
-static int attn_cps(int batch) {
+static int attn_cps(int batch, int nkv, int ctx, int device, int sm_count) {
     static const int forced = [] {
         const char *e = getenv("X100_ATTN_CPS");
         const int v = e ? atoi(e) : 0;
         return v >= 1 && v <= 8 ? v : 0;
     }();
     if (forced) return forced;
-    // measured, decode step at context 4096: batch 1 best with 1, batch 2 with
-    // 2, batch 4 and 16 with 4 (8 was slower at 16)
-    return batch >= 4 ? 4 : (batch >= 2 ? 2 : 1);
+    static int occ[64][9];   // resident CTAs per SM for each cps (its shared memory)
+    int best = 1;
+    long best_cost = -1;
+    for (int cps = 1; cps <= 8; ++cps) {
+        int &r = occ[device & 63][cps];
+        if (!r) {
+            int n = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_decode_kernel, kAttnThreads, attn_smem(cps));
+            r = n > 0 ? n : 1;
+        }
+        const long ctas = (long)((ctx + kChunk * cps - 1) / (kChunk * cps)) * nkv * batch;
+        const long slots = (long)sm_count * r, cost = (ctas + slots - 1) / slots * cps;
+        if (best_cost < 0 || cost <= best_cost) {
+            best_cost = cost;
+            best = cps;
+        }
+    }
+    return best;
 }
 static size_t merge_smem(int nsplit) { return (size_t)(((2 * nsplit + 3) & ~3) + 4 * kHD) * 4; }
 
@@ -882,7 +901,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     a.nkv = g.n_kv_heads;
     a.ctx = g.ctx;
     a.chunk = kChunk;
-    a.cps = attn_cps(batch);
+    a.cps = attn_cps(batch, g.n_kv_heads, g.ctx, c->device, c->sm_count);
     a.nsplit = (g.ctx + kChunk * a.cps - 1) / (kChunk * a.cps);
     a.eps = g.eps;
     a.rope_base = g.rope_base;

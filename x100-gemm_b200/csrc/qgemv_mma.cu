@@ -160,7 +160,7 @@ template <int QT, int NT>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     qgemv_mma_kernel(const uint8_t *__restrict__ W, int N, int K, int ck, int stages, const float *__restrict__ x,
                      float *__restrict__ y, int batch, const float *__restrict__ nw, float eps, int accum,
-                     int a8, const uint8_t *__restrict__ xbm, const float *__restrict__ qs, int *status) {
+                     int a8, const uint8_t *__restrict__ xbm, const float *__restrict__ qs, long rbw, int *status) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float ssq[(kMmaThreads / 32) * 4][kSsTok];   // RMS-norm sums of squares per 8-lane group
     __shared__ float scale[16];
@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     constexpr int SB = slice_bytes(QT);
     constexpr int NTOK = 8 * NT;
     const int ns = slices_per_row(K), nb = ns * 8;
-    const long rb = (long)ns * SB;
+    const long rb = rbw ? rbw : (long)ns * SB;   // bytes per weight row (rbw: a piece of a longer row)
     const int rsp = mma_row_stride(QT, ck);
     // partials [tok][row][half-slice]: row stride RS odd and token stride TS =
     // 8 mod 32 words per two tokens, so the 32 lanes' writes hit distinct banks
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 
 template <int QT, int NT>
 static int launch_mma_nt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const MmaPlan &p,
-                         const GemvOpts &o, cudaStream_t s, const uint8_t *xbm, const float *qs) {
+                         const GemvOpts &o, cudaStream_t s, const uint8_t *xbm, const float *qs, long rbw = 0) {
     static bool attr[64];
     if (!attr[c->device]) {
         set_qkernel_attrs(qgemv_mma_kernel<QT, NT>, (int)kMmaSmemMax);
@@ -328,7 +328,7 @@ static int launch_mma_nt(DevCtx *c, const QMat &m, const float *x, float *y, int
     const int ntiles = (m.N + kMmaRows - 1) / kMmaRows;
     const int grid = std::min(ntiles, c->sm_count);
     return launch_k(qgemv_mma_kernel<QT, NT>, dim3(grid), dim3(kMmaThreads), p.smem, s, o.pdl, (const uint8_t *)m.w,
-                    m.N, m.K, p.ck, p.stages, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0, o.a8, xbm, qs,
+                    m.N, m.K, p.ck, p.stages, x, y, batch, o.norm_w, o.eps, o.accum ? 1 : 0, o.a8, xbm, qs, rbw,
                     c->d_status);
 }
 
@@ -336,14 +336,30 @@ static int launch_mma_nt(DevCtx *c, const QMat &m, const float *x, float *y, int
 template <int QT>
 static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, GemvOpts o,
                          cudaStream_t s) {
-    const MmaPlan p = mma_plan(QT, m.K, batch);
+    MmaPlan p = mma_plan(QT, m.K, batch);
     if (!p.stages) return X100_E_UNSUPPORTED;
-    const int per = 8 * p.nt;
-    const int nxb = slices_per_row(m.K) * 8;
     // activations prepared once for all the call's launches (not for the
     // reference's A8 packings, and not for independent calls, whose point is
     // to prepare before the dependency wait)
     const bool prep = o.prep && batch > 1 && o.a8 == 0 && !o.indep && m.K % 32 == 0;
+    // K in pieces: when the tokens' activations over the whole row leave no
+    // room for a 16-token launch but do over a piece of the row, the call is
+    // one 16-token launch per piece, each adding its piece's dots into y, so
+    // the weights stream once instead of once per 8-token group (Wo at 16
+    // tokens).  Not with a folded RMS norm, whose scale needs the whole row.
+    const int ns = slices_per_row(m.K);
+    int kpieces = 1;
+    if (prep && batch > 8 && p.nt == 1 && !o.norm_w && m.K % 256 == 0)
+        for (int k = 2; k <= 4 && kpieces == 1; ++k)
+            if (ns % k == 0) {
+                const MmaPlan q = mma_plan(QT, m.K / k, batch);
+                if (q.stages && q.nt == 2) {
+                    kpieces = k;
+                    p = q;
+                }
+            }
+    const int per = 8 * p.nt;
+    const int nxb = ns * 8;
     uint8_t *xbm = o.prep;
     float *qs = reinterpret_cast<float *>(o.prep + prep_xbm_bytes(m.K));
     if (prep) {
@@ -356,6 +372,21 @@ static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int
                                 per, xbm, qs);
         if (st) return st;
         o.pdl = true;
+    }
+    if (kpieces > 1) {   // one group of `per` tokens, block-major: a piece's blocks are contiguous
+        const int nsp = ns / kpieces;
+        for (int i = 0; i < kpieces; ++i) {
+            QMat mp = m;
+            mp.w = m.w + (size_t)i * nsp * slice_bytes(QT);
+            mp.K = nsp * 256;
+            GemvOpts oi = o;
+            oi.accum = i ? true : o.accum;
+            const int st = launch_mma_nt<QT, 2>(c, mp, x, y, batch, p, oi, s, xbm + (size_t)i * nsp * 8 * per * 80,
+                                                nullptr, m.row_bytes);
+            if (st) return st;
+            o.pdl = true;
+        }
+        return X100_OK;
     }
     for (int b0 = 0; b0 < batch; b0 += per) {
         const int nb = std::min(per, batch - b0);
