@@ -213,11 +213,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             mbar_arrive_expect_tx(&xbar, bytes);
             stage_bytes(xbase, xbm, bytes, &xbar);
         }
-        if (threadIdx.x < batch) {
+        if (warp < batch) {   // a warp per token: its block sums of squares, lane-strided, then a fixed shuffle tree
             float q = 0.f;
             if (nw)
-                for (int j = 0; j < nb; ++j) q += __ldcg(qs + (long)threadIdx.x * nb + j);
-            scale[threadIdx.x] = nw ? 1.0f / sqrtf(q / (float)K + eps) : 1.0f;
+                for (int j = lane; j < nb; j += 32) q += __ldcg(qs + (long)warp * nb + j);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+            if (lane == 0) scale[warp] = nw ? 1.0f / sqrtf(q / (float)K + eps) : 1.0f;
         }
         __syncthreads();   // the barrier is initialised
         mbar_wait(&xbar, 0, &abort_flag, status);   // bounded; on a timeout the status records it
