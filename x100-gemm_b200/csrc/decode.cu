@@ -399,9 +399,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 // Grid (nh, B), 128 threads: att[b][head] = sum_s e^(m_s-M) o_s / sum_s
 // e^(m_s-M) l_s over the splits of attn_decode_kernel.  Warp w sums the
 // splits of its quarter (16 loads in flight per lane), the quarters are added
-// in order, so the result does not depend on timing.
+// in order, so the result does not depend on timing.  With xbm set it also
+// writes the head's four 32-element blocks prepared for the Wo GEMV
+// (xprep_vals, the preparation kernel's layout: groups of ntok tokens, nxb
+// blocks a token), so that call launches no preparation of its own.
 __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict__ part, int nh, int nsplit,
-                                                         float *__restrict__ att) {
+                                                         float *__restrict__ att, uint8_t *__restrict__ xbm,
+                                                         int ntok, int nxb) {
     extern __shared__ float msm[];
     // sO [4][hd] starts on a 16-byte boundary (float4 accesses)
     float *sW = msm, *sL = msm + nsplit, *sO = msm + ((2 * nsplit + 3) & ~3);
@@ -457,8 +461,13 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
             T = make_float4(T.x + u.x, T.y + u.y, T.z + u.z, T.w + u.w);
         }
         const float inv = Ls > 0.f ? 1.0f / Ls : 0.f;
-        reinterpret_cast<float4 *>(att + (long)b * nh * kHD + hh * kHD)[lane] =
-            make_float4(T.x * inv, T.y * inv, T.z * inv, T.w * inv);
+        const float4 v = make_float4(T.x * inv, T.y * inv, T.z * inv, T.w * inv);
+        reinterpret_cast<float4 *>(att + (long)b * nh * kHD + hh * kHD)[lane] = v;
+        if (xbm) {   // lanes 8i .. 8i+7 hold block i of the head: the preparation's own grouping
+            const int j = hh * (kHD / 32) + (lane >> 3);
+            xprep_vals(v, reinterpret_cast<XB *>(xbm + (((long)(b / ntok) * nxb + j) * ntok + b % ntok) * 80),
+                       lane & 7, true);
+        }
     }
 }
 
@@ -925,16 +934,19 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     st = launch_pdl(attn_decode_kernel, dim3(a.nsplit, g.n_kv_heads, batch), dim3(kAttnThreads), attn_smem(a.cps), s,
                     m->tmK, m->tmV, a);
     if (st) return st;
+    GemvOpts o3;   // the Wo call: its activations prepared by the merge when it prepares them once
+    o3.accum = true;
+    o3.prep = m->prep;
     if (a.nsplit > 1) {
+        const int grp = qgemv_prep_group(L.o, batch, o3);
         st = launch_pdl(attn_merge_kernel, dim3(g.n_heads, batch), dim3(128), merge_smem(a.nsplit), s,
-                        (const float *)m->part, g.n_heads, a.nsplit, m->att);
+                        (const float *)m->part, g.n_heads, a.nsplit, m->att, grp ? m->prep : nullptr, grp,
+                        slices_per_row(g.n_heads * kHD) * 8);
         if (st) return st;
+        o3.prepared = grp > 0;
     }
     // 3. h += Wo . att
     timer_mark(m->timer, X100Q_T_O, s);
-    GemvOpts o3;
-    o3.accum = true;
-    o3.prep = m->prep;
     st = launch_qgemv_ex(c, L.o, m->att, h, batch, o3, s);
     if (st) return st;
     // 4. h += MoE(rmsnorm(h))  (or eout = this process's experts' share)
@@ -1194,7 +1206,7 @@ static int prefill_chunk_tc(x100q_model *m, DevCtx *c, const int *tok, float *h,
                             m->tmK, m->tmV, ag);
             if (!st && ag.nsplit > 1)
                 st = launch_pdl(attn_merge_kernel, dim3(g.n_heads, gb), dim3(128), merge_smem(ag.nsplit), s,
-                                (const float *)m->part, g.n_heads, ag.nsplit, ag.att);
+                                (const float *)m->part, g.n_heads, ag.nsplit, ag.att, (uint8_t *)nullptr, 0, 0);
             g0 += gb;
         }
         if (st) break;

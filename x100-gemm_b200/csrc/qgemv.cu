@@ -407,6 +407,28 @@ int launch_qgemv(DevCtx *c, const QMat &m, const float *x, float *y, int batch, 
     return launch_qgemv_ex(c, m, x, y, batch, GemvOpts(), s);
 }
 
+// Whether the tensor-core kernel takes a call.  Independent calls of up to 4
+// tokens stay on the dp4a kernel: its small CTAs let consecutive calls
+// overlap, which the persistent tensor-core kernel (one CTA per SM) cannot
+// (Q4_0 6144 x 2048, 4 tokens: 1187 vs 900 GB/s measured; from 8 tokens the
+// tensor-core kernel is ahead).  One token on a very tall matrix (an
+// lm_head): the persistent tensor-core kernel streams it faster than the
+// single-token dp4a kernel's many waves of small CTAs (151936 x 2048 Q8_0:
+// 118 vs 145 us).  X100_GEMV_DP4A=1 keeps every call on the dp4a kernel.
+static bool takes_mma(const QMat &m, int batch, const GemvOpts &o) {
+    static const bool dp4a_only = [] {
+        const char *e = getenv("X100_GEMV_DP4A");
+        return e && *e && *e != '0';
+    }();
+    const bool tall = batch == 1 && m.N >= 65536;
+    return (batch > 1 || tall) && !dp4a_only && !(o.indep && batch <= 4) && qgemv_mma_ok(m.qtype, m.K);
+}
+
+int qgemv_prep_group(const QMat &m, int batch, const GemvOpts &o) {
+    if (batch < 2 || batch > 16 || o.norm_w || !takes_mma(m, batch, o)) return 0;
+    return qgemv_mma_prep_group(m, batch, o);
+}
+
 int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
                     cudaStream_t s) {
     if (batch < 1 || batch > 16) {
@@ -414,19 +436,7 @@ int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batc
         return X100_E_ARG;
     }
     if (fault_injected("launch")) return X100_E_INJECTED;
-    static const bool dp4a_only = [] {
-        const char *e = getenv("X100_GEMV_DP4A");
-        return e && *e && *e != '0';
-    }();
-    // Independent calls of up to 4 tokens stay on the dp4a kernel: its small
-    // CTAs let consecutive calls overlap, which the persistent tensor-core
-    // kernel (one CTA per SM) cannot (Q4_0 6144 x 2048, 4 tokens: 1187 vs
-    // 900 GB/s measured; from 8 tokens the tensor-core kernel is ahead).
-    // one token on a very tall matrix (an lm_head): the persistent
-    // tensor-core kernel streams it faster than the single-token dp4a kernel's
-    // many waves of small CTAs (151936 x 2048 Q8_0: 118 vs 145 us)
-    const bool tall = batch == 1 && m.N >= 65536;
-    if ((batch > 1 || tall) && !dp4a_only && !(o.indep && batch <= 4) && qgemv_mma_ok(m.qtype, m.K)) {
+    if (takes_mma(m, batch, o)) {
         const int st = launch_qgemv_mma(c, m, x, y, batch, o, s);
         if (st) set_error(st);
         return st;

@@ -41,8 +41,20 @@ struct GemvOpts {
     // once, in a kernel of its own, instead of in every CTA.  One buffer per
     // stream of calls (the model's own).
     uint8_t *prep = nullptr;
+    // prep already holds the call's prepared activations, written by the
+    // kernel that produced x in the layout the preparation kernel writes
+    // (groups of qgemv_prep_group tokens): the call launches no preparation.
+    bool prepared = false;
 };
 size_t qgemv_prep_bytes(int batch, int K);
+// Tokens per block-major group of the prepared activations when the call
+// prepares them once in o.prep (the tensor-core kernel with o.prep, no A8
+// packing, not independent), else 0.  A producer that writes x may write the
+// prepared blocks too (xprep_vals of each 32-element block): block j of token
+// t at ((t / g) * nxb + j) * g + t % g, 80 bytes each, g = the group, nxb = 8
+// ceil(K / 256); and set o.prepared.  Not with a folded RMS norm.
+int qgemv_prep_group(const QMat &m, int batch, const GemvOpts &o);
+int qgemv_mma_prep_group(const QMat &m, int batch, const GemvOpts &o);   // qgemv_mma.cu
 int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
                     cudaStream_t s);
 // Several tokens of a Q4_0 / Q8_0 matrix on the tensor cores (qgemv_mma.cu):

@@ -335,36 +335,53 @@ static int launch_mma_nt(DevCtx *c, const QMat &m, const float *x, float *y, int
 }
 
 // Launches of 8 nt tokens each (nt from the plan).
-template <int QT>
-static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, GemvOpts o,
-                         cudaStream_t s) {
-    MmaPlan p = mma_plan(QT, m.K, batch);
-    if (!p.stages) return X100_E_UNSUPPORTED;
+// The launch plan of a call: the per-launch plan, K pieces, and whether the
+// activations are prepared once in o.prep.
+struct CallPlan {
+    MmaPlan p;
+    int kpieces = 1;
+    bool prep = false;
+};
+static CallPlan call_plan(int qt, const QMat &m, int batch, const GemvOpts &o) {
+    CallPlan cp;
+    cp.p = mma_plan(qt, m.K, batch);
+    if (!cp.p.stages) return cp;
     // activations prepared once for all the call's launches (not for the
     // reference's A8 packings, and not for independent calls, whose point is
     // to prepare before the dependency wait)
-    const bool prep = o.prep && batch > 1 && o.a8 == 0 && !o.indep && m.K % 32 == 0;
+    cp.prep = o.prep && batch > 1 && o.a8 == 0 && !o.indep && m.K % 32 == 0;
     // K in pieces: when the tokens' activations over the whole row leave no
     // room for a 16-token launch but do over a piece of the row, the call is
     // one 16-token launch per piece, each adding its piece's dots into y, so
     // the weights stream once instead of once per 8-token group (Wo at 16
     // tokens).  Not with a folded RMS norm, whose scale needs the whole row.
     const int ns = slices_per_row(m.K);
-    int kpieces = 1;
-    if (prep && batch > 8 && p.nt == 1 && !o.norm_w && m.K % 256 == 0)
-        for (int k = 2; k <= 4 && kpieces == 1; ++k)
+    if (cp.prep && batch > 8 && cp.p.nt == 1 && !o.norm_w && m.K % 256 == 0)
+        for (int k = 2; k <= 4 && cp.kpieces == 1; ++k)
             if (ns % k == 0) {
-                const MmaPlan q = mma_plan(QT, m.K / k, batch);
+                const MmaPlan q = mma_plan(qt, m.K / k, batch);
                 if (q.stages && q.nt == 2) {
-                    kpieces = k;
-                    p = q;
+                    cp.kpieces = k;
+                    cp.p = q;
                 }
             }
+    return cp;
+}
+
+template <int QT>
+static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int batch, GemvOpts o,
+                         cudaStream_t s) {
+    const CallPlan cp = call_plan(QT, m, batch, o);
+    const MmaPlan &p = cp.p;
+    if (!p.stages) return X100_E_UNSUPPORTED;
+    const bool prep = cp.prep;
+    const int kpieces = cp.kpieces;
+    const int ns = slices_per_row(m.K);
     const int per = 8 * p.nt;
     const int nxb = ns * 8;
     uint8_t *xbm = o.prep;
     float *qs = reinterpret_cast<float *>(o.prep + prep_xbm_bytes(m.K));
-    if (prep) {
+    if (prep && !(o.prepared && !o.norm_w)) {   // prepared by the producer of x: nothing to launch
         static bool attr[64];
         if (!attr[c->device]) {
             set_qkernel_attrs(prep_bm_kernel);
@@ -408,6 +425,11 @@ static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int
 
 size_t qgemv_prep_bytes(int batch, int K) {
     return q::prep_xbm_bytes(K) + (size_t)batch * q::slices_per_row(K) * 8 * 4;
+}
+
+int qgemv_mma_prep_group(const QMat &m, int batch, const GemvOpts &o) {
+    const q::CallPlan cp = q::call_plan(m.qtype, m, batch, o);
+    return cp.p.stages && cp.prep ? 8 * cp.p.nt : 0;
 }
 
 bool qgemv_mma_ok(int qt, int K) {
