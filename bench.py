@@ -836,13 +836,14 @@ def bench_decode(args, dist, peaks, peak_src):
     ep = dist.ep_group(B * d) if world > 1 and args.combine == "p2p" else None
     # launches per step: embed; per layer the q/k/v GEMV, attention and the
     # merge of its splits, the Wo GEMV (two launches above 8 tokens: the
-    # 4096-wide activations of 16 tokens exceed one CTA's shared memory), the
-    # MoE kernels (2 fused at batch 1; 6 grouped: router, grouping, gate/up,
-    # h preparation, down, combine); above one token every tensor-core GEMV
-    # call adds its activation-preparation kernel; the lm_head (+ its
-    # preparation above one token)
+    # 4096-wide activations of 16 tokens exceed one CTA's shared memory, so
+    # the row is taken in two K pieces; its activations are prepared by the
+    # attention merge), the MoE kernels (2 fused at batch 1; 6 grouped: router,
+    # grouping, gate/up, h preparation, down, combine); above one token the
+    # q/k/v and lm_head tensor-core GEMV calls add their activation-preparation
+    # kernel; the lm_head (+ its preparation above one token)
     prep = 0 if B == 1 else 1
-    launches = 1 + NL * ((1 + prep) + 2 + (prep + (1 if B <= 8 else 2)) + (2 if B == 1 else 6) +
+    launches = 1 + NL * ((1 + prep) + 2 + (1 if B <= 8 else 2) + (2 if B == 1 else 6) +
                          (1 if ep is not None else 0)) + (1 + prep)
 
     def step():
