@@ -841,10 +841,13 @@ def bench_decode(args, dist, peaks, peak_src):
     # attention merge), the MoE kernels (2 fused at batch 1; 6 grouped: router,
     # grouping, gate/up, h preparation, down, combine); above one token the
     # q/k/v and lm_head tensor-core GEMV calls add their activation-preparation
-    # kernel; the lm_head (+ its preparation above one token)
+    # kernel -- in the one-process step (forward_dev) only layer 0's q/k/v, the
+    # others and the lm_head's being prepared by the MoE combine before them;
+    # the lm_head
     prep = 0 if B == 1 else 1
-    launches = 1 + NL * ((1 + prep) + 2 + (1 if B <= 8 else 2) + (2 if B == 1 else 6) +
-                         (1 if ep is not None else 0)) + (1 + prep)
+    chained = world == 1
+    launches = (1 + NL * (1 + 2 + (1 if B <= 8 else 2) + (2 if B == 1 else 6) + (1 if ep is not None else 0))
+                + prep * (1 if chained else NL) + 1 + (0 if chained else prep))
 
     def step():
         if world == 1:

@@ -880,8 +880,15 @@ int x100q_model_embed_dev(x100q_model *m, const int *tokens, float *h, int batch
 // a full barrier (see attn_decode_kernel); barrier: launch the first kernel
 // behind one.  slot: per-token cache slots (null: token b uses slot b); with
 // it the step's k and v go to the cache in a kernel of their own first.
+// next_m / next_nw: the GEMV that reads h after this layer (the next layer's
+// q/k/v, or the lm_head) and its RMS norm, for the MoE combine to prepare its
+// activations (*next_prepared says whether it does); qkv_prepared: this
+// layer's q/k/v activations were prepared that way by the previous layer.
 static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const int *pos, int batch, float *eout,
-                        cudaStream_t s, bool kv_early, bool barrier, const int *slot = nullptr) {
+                        cudaStream_t s, bool kv_early, bool barrier, const int *slot = nullptr,
+                        const QMat *next_m = nullptr, const float *next_nw = nullptr, bool qkv_prepared = false,
+                        bool *next_prepared = nullptr) {
+    if (next_prepared) *next_prepared = false;
     const x100q_model_cfg &g = m->cfg;
     ModelLayer &L = m->layers[layer];
     static bool attr[64];
@@ -897,6 +904,7 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     o1.eps = g.eps;
     o1.pdl = !barrier;
     o1.prep = m->prep;
+    o1.prepared = qkv_prepared;
     int st = launch_qgemv_ex(c, L.qkv, h, m->qkv, batch, o1, s);
     if (st) return st;
     // 2. attention (+ merge of the splits)
@@ -957,6 +965,21 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     o4.accum = eout == nullptr;
     o4.mark = timer_mark_cb;
     o4.mark_ctx = &m->timer;
+    if (next_m && !eout) {   // h is complete after the combine: it prepares the next GEMV's activations
+        GemvOpts on;
+        on.norm_w = next_nw;
+        on.eps = g.eps;
+        on.prep = m->prep;
+        const int grp = qgemv_prep_group(*next_m, batch, on);
+        if (grp) {
+            o4.next_xbm = m->prep;
+            o4.next_qs = qgemv_prep_qs(m->prep, next_m->K);
+            o4.next_nw = next_nw;
+            o4.next_ntok = grp;
+            o4.next_nxb = slices_per_row(next_m->K) * 8;
+            if (next_prepared) *next_prepared = true;
+        }
+    }
     return launch_moe_ex(c, L.moe, m->S, h, eout ? eout : h, batch, o4, s);
 }
 
@@ -998,6 +1021,18 @@ int x100q_model_layer_dev(x100q_model *m, int layer, float *h, const int *pos, i
     return X100_OK;
 }
 
+// logits = lm_head . rmsnorm(h, out_norm); prepared: the last layer's combine
+// prepared the activations
+static int head_launch(x100q_model *m, DevCtx *c, const float *h, float *logits, int batch, cudaStream_t s,
+                       bool prepared) {
+    GemvOpts o;
+    o.norm_w = m->out_norm;
+    o.eps = m->cfg.eps;
+    o.prep = m->prep;
+    o.prepared = prepared;
+    return launch_qgemv_ex(c, m->lm, h, logits, batch, o, s);
+}
+
 int x100q_model_head_dev(x100q_model *m, const float *h, float *logits, int batch, void *stream) {
     set_error(X100_OK);
     if (!m || !h || !logits || batch < 1 || batch > m->cfg.max_batch || !m->out_norm || !m->lm.w) {
@@ -1006,11 +1041,7 @@ int x100q_model_head_dev(x100q_model *m, const float *h, float *logits, int batc
     }
     DevCtx *c = ctx();
     if (!c) return get_error();
-    GemvOpts o;
-    o.norm_w = m->out_norm;
-    o.eps = m->cfg.eps;
-    o.prep = m->prep;
-    return launch_qgemv_ex(c, m->lm, h, logits, batch, o, static_cast<cudaStream_t>(stream));
+    return head_launch(m, c, h, logits, batch, static_cast<cudaStream_t>(stream), false);
 }
 
 int x100q_model_forward_dev(x100q_model *m, const int *tokens, float *h, const int *pos, float *logits, int batch,
@@ -1055,11 +1086,21 @@ static int forward_impl(x100q_model *m, const int *tokens, float *h, const int *
         timer_mark(m->timer, X100Q_T_EMBED, s);
         st = x100q_model_embed_dev(m, tokens, h, batch, stream);
     }
-    for (int l = 0; st == X100_OK && l < m->cfg.n_layers; ++l)
-        st = layer_launch(m, c, l, h, pos, batch, nullptr, s, true, l == 0 && !tokens, slot);
+    // each layer's combine prepares the activations of the GEMV after it (the
+    // next layer's q/k/v, the lm_head) when that call prepares them once
+    const bool head_ok = logits && m->out_norm && m->lm.w;
+    bool prepared = false;
+    for (int l = 0; st == X100_OK && l < m->cfg.n_layers; ++l) {
+        const bool last = l + 1 == m->cfg.n_layers;
+        const QMat *nm = !last ? &m->layers[l + 1].qkv : (head_ok ? &m->lm : nullptr);
+        const float *nnw = !last ? m->layers[l + 1].norms : m->out_norm;
+        bool np = false;
+        st = layer_launch(m, c, l, h, pos, batch, nullptr, s, true, l == 0 && !tokens, slot, nm, nnw, prepared, &np);
+        prepared = np;
+    }
     if (st == X100_OK && logits) {
         timer_mark(m->timer, X100Q_T_LM, s);
-        st = x100q_model_head_dev(m, h, logits, batch, stream);
+        st = head_ok ? head_launch(m, c, h, logits, batch, s, prepared) : x100q_model_head_dev(m, h, logits, batch, stream);
     }
     if (m->timer.on) {
         timer_mark(m->timer, -1, s);

@@ -1075,10 +1075,17 @@ static WsPlan ws_plan(WsPlan (*plan)(int, int, int, int), int qt, int n, int bat
 }
 
 // combine: eout[token][n] = sum over the token's local slots, in slot order,
-// of w * part[token][slot][n] (qwen_moe.c:310); zero if none is local.
+// of w * part[token][slot][n] (qwen_moe.c:310); zero if none is local.  With
+// xbm set (d a multiple of 32: a warp holds one 32-element block of the row)
+// each warp also writes its block prepared for the next GEMV: lanes 0-7
+// gather four consecutive values each and form the block's sum of squares
+// and its xprep_vals form of row * nw, the operations of the preparation
+// kernel on the same values.
 __global__ void __launch_bounds__(256) combine_kernel(int d, int n_act, int lo, int hi, const int *__restrict__ sel,
                                                       const float *__restrict__ w, const float *__restrict__ part,
-                                                      float *__restrict__ eout, int accum) {
+                                                      float *__restrict__ eout, int accum, uint8_t *__restrict__ xbm,
+                                                      float *__restrict__ qs, const float *__restrict__ nw, int ntok,
+                                                      int nxb) {
     const int tok = blockIdx.y, n = blockIdx.x * blockDim.x + threadIdx.x;
     pdl_wait();                                  // part comes from the down kernel
     pdl_launch_dependents();
@@ -1089,7 +1096,27 @@ __global__ void __launch_bounds__(256) combine_kernel(int d, int n_act, int lo, 
         if (e >= lo && e < hi) tot += __ldcg(w + tok * n_act + a) * __ldcg(part + ((long)tok * n_act + a) * d + n);
     }
     float *o = eout + (long)tok * d + n;
-    *o = accum ? *o + tot : tot;
+    const float val = accum ? *o + tot : tot;
+    *o = val;
+    if (xbm) {
+        const int lane = threadIdx.x & 31, t = lane & 7, j = n >> 5;
+        float4 v;
+        v.x = __shfl_sync(0xffffffffu, val, 4 * t);
+        v.y = __shfl_sync(0xffffffffu, val, 4 * t + 1);
+        v.z = __shfl_sync(0xffffffffu, val, 4 * t + 2);
+        v.w = __shfl_sync(0xffffffffu, val, 4 * t + 3);
+        float q = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        q += __shfl_xor_sync(0xffffffffu, q, 1);
+        q += __shfl_xor_sync(0xffffffffu, q, 2);
+        q += __shfl_xor_sync(0xffffffffu, q, 4);
+        if (lane == 0) qs[(long)tok * nxb + j] = q;
+        if (nw) {
+            const float4 w4 = __ldg(reinterpret_cast<const float4 *>(nw + j * 32) + t);
+            v = make_float4(v.x * w4.x, v.y * w4.y, v.z * w4.z, v.w * w4.w);
+        }
+        xprep_vals(v, reinterpret_cast<XB *>(xbm + (((long)(tok / ntok) * nxb + j) * ntok + tok % ntok) * 80), t,
+                   lane < 8);
+    }
 }
 
 // ---- many-token (prefill) path: pairs sorted by expert ------------------------------------
@@ -1599,7 +1626,8 @@ static int launch_moe_qt(DevCtx *c, const MoeLayer &L, const MoeScratch &S, cons
     }
     if (o.mark) o.mark(o.mark_ctx, X100Q_T_COMBINE, s);
     return launch_pdl(combine_kernel, dim3((L.d + 255) / 256, batch), dim3(256), 0, s, L.d, L.n_act, L.lo, L.hi,
-                      (const int *)S.sel, (const float *)S.w, (const float *)S.part, eout, accum);
+                      (const int *)S.sel, (const float *)S.w, (const float *)S.part, eout, accum,
+                      L.d % 32 == 0 ? o.next_xbm : nullptr, o.next_qs, o.next_nw, o.next_ntok, o.next_nxb);
 }
 
 int launch_moe(DevCtx *c, const MoeLayer &L, const MoeScratch &S, const float *hn, float *eout, int batch,
@@ -1725,7 +1753,8 @@ int launch_moe_prefill(DevCtx *c, const MoeLayer &L, const MoeBigScratch &S, flo
     if (st) return st;
     // 8. h += sum over the token's local slots, in slot order, of w * part (qwen_moe.c:310)
     return launch_pdl(combine_kernel, dim3((L.d + 255) / 256, T), dim3(256), 0, s, L.d, L.n_act, L.lo, L.hi,
-                      (const int *)S.sel, (const float *)S.w, (const float *)S.part, h, 1);
+                      (const int *)S.sel, (const float *)S.w, (const float *)S.part, h, 1, (uint8_t *)nullptr,
+                      (float *)nullptr, (const float *)nullptr, 0, 0);
 }
 
 bool moe_layer_upload(DevCtx *c, MoeLayer &L, int d, int n_exp, int n_act, int ffn, int qtype, const float *router,

@@ -64,6 +64,15 @@ struct MoeOpts {
     // combine launches (buckets of x100q_model_timing)
     void (*mark)(void *ctx, int bucket, cudaStream_t s) = nullptr;
     void *mark_ctx = nullptr;
+    // batch > 1, eout summed in one process: the combine also prepares the
+    // next GEMV's activations from the rows it writes (qgemv_prep_group's
+    // layout: groups of next_ntok tokens, next_nxb blocks a token, blocks of
+    // row * next_nw and each block's sum of squares of the row in next_qs);
+    // next_xbm null: not
+    uint8_t *next_xbm = nullptr;
+    float *next_qs = nullptr;
+    const float *next_nw = nullptr;
+    int next_ntok = 0, next_nxb = 0;
 };
 // Scratch of the many-token (prefill) MoE path for up to `tmax` tokens:
 // routing, the (token, slot) pairs sorted by expert, their activations as

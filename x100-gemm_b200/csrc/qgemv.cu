@@ -425,7 +425,7 @@ static bool takes_mma(const QMat &m, int batch, const GemvOpts &o) {
 }
 
 int qgemv_prep_group(const QMat &m, int batch, const GemvOpts &o) {
-    if (batch < 2 || batch > 16 || o.norm_w || !takes_mma(m, batch, o)) return 0;
+    if (batch < 2 || batch > 16 || !takes_mma(m, batch, o)) return 0;
     return qgemv_mma_prep_group(m, batch, o);
 }
 

@@ -50,10 +50,14 @@ size_t qgemv_prep_bytes(int batch, int K);
 // Tokens per block-major group of the prepared activations when the call
 // prepares them once in o.prep (the tensor-core kernel with o.prep, no A8
 // packing, not independent), else 0.  A producer that writes x may write the
-// prepared blocks too (xprep_vals of each 32-element block): block j of token
-// t at ((t / g) * nxb + j) * g + t % g, 80 bytes each, g = the group, nxb = 8
-// ceil(K / 256); and set o.prepared.  Not with a folded RMS norm.
+// prepared blocks too (xprep_vals of each 32-element block of x, times
+// o.norm_w when the call folds an RMS norm): block j of token t at ((t / g) *
+// nxb + j) * g + t % g, 80 bytes each, g = the group, nxb = 8 ceil(K / 256);
+// with a norm also each block's sum of squares of x at qgemv_prep_qs(o.prep,
+// K)[t * nxb + j] (four squares per lane of eight, summed as the preparation
+// kernel does); and set o.prepared.
 int qgemv_prep_group(const QMat &m, int batch, const GemvOpts &o);
+float *qgemv_prep_qs(uint8_t *prep, int K);
 int qgemv_mma_prep_group(const QMat &m, int batch, const GemvOpts &o);   // qgemv_mma.cu
 int launch_qgemv_ex(DevCtx *c, const QMat &m, const float *x, float *y, int batch, const GemvOpts &o,
                     cudaStream_t s);

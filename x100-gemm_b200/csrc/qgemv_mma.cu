@@ -381,7 +381,7 @@ static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int
     const int nxb = ns * 8;
     uint8_t *xbm = o.prep;
     float *qs = reinterpret_cast<float *>(o.prep + prep_xbm_bytes(m.K));
-    if (prep && !(o.prepared && !o.norm_w)) {   // prepared by the producer of x: nothing to launch
+    if (prep && !o.prepared) {   // o.prepared: the producer of x prepared it, nothing to launch
         static bool attr[64];
         if (!attr[c->device]) {
             set_qkernel_attrs(prep_bm_kernel);
@@ -426,6 +426,8 @@ static int launch_mma_qt(DevCtx *c, const QMat &m, const float *x, float *y, int
 size_t qgemv_prep_bytes(int batch, int K) {
     return q::prep_xbm_bytes(K) + (size_t)batch * q::slices_per_row(K) * 8 * 4;
 }
+
+float *qgemv_prep_qs(uint8_t *prep, int K) { return reinterpret_cast<float *>(prep + q::prep_xbm_bytes(K)); }
 
 int qgemv_mma_prep_group(const QMat &m, int batch, const GemvOpts &o) {
     const q::CallPlan cp = q::call_plan(m.qtype, m, batch, o);
