@@ -348,26 +348,28 @@ def bench_gemm(args, dist, peaks, peak_src):
     torch.cuda.synchronize()
     clk = ClockSampler(dist.physical_gpu())
     clk.start()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    # two events around the K launches: an event between two launches would
+    # serialise them (no programmatic-dependent-launch overlap) and add its own
+    # gap, ~3 us per launch at the 8-GPU shard (measured)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     dist.barrier()
     torch.cuda.synchronize()
     ev[0].record(stream)
     for i in range(args.steps):
         step(i)
-        ev[i + 1].record(stream)
+    ev[1].record(stream)
     torch.cuda.synchronize()
     dist.barrier()
     clocks = clk.stop()
     st = x100b.lib().x100_sync(sptr)
     if st:
         raise x100b.X100Error(st, "device status after timing")
-    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
-    total_ms = ev[0].elapsed_time(ev[-1])
-    total_ms = dist.max(total_ms)
+    rank_ms = ev[0].elapsed_time(ev[1])
+    total_ms = dist.max(rank_ms)
     ops_rank = 2.0 * M * N * K
     ops_total = 2.0 * S * S * S
     value = ops_total * args.steps / (total_ms / 1e3) / 1e12
-    kernel_ms = statistics.mean(per)
+    kernel_ms = rank_ms / args.steps           # this rank's average launch, back to back
     achieved = ops_rank / (kernel_ms / 1e3) / 1e12
     if kind == "gemm_i8":
         peak = 2.0 * peaks["bf16_tflops"]
