@@ -399,10 +399,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 // Grid (nh, B), 128 threads: att[b][head] = sum_s e^(m_s-M) o_s / sum_s
 // e^(m_s-M) l_s over the splits of attn_decode_kernel.  Warp w sums the
 // splits of its quarter (16 loads in flight per lane), the quarters are added
-// in order, so the result does not depend on timing.  With xbm set it also
-// writes the head's four 32-element blocks prepared for the Wo GEMV
+// in order, so the result does not depend on timing.  PREP: it also writes
+// the head's four 32-element blocks prepared for the Wo GEMV into xbm
 // (xprep_vals, the preparation kernel's layout: groups of ntok tokens, nxb
-// blocks a token), so that call launches no preparation of its own.
+// blocks a token), so that call launches no preparation of its own (a
+// separate instantiation: the code changes the main loop's register use,
+// which cost the one-token step 4 us a layer).
+template <bool PREP>
 __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict__ part, int nh, int nsplit,
                                                          float *__restrict__ att, uint8_t *__restrict__ xbm,
                                                          int ntok, int nxb) {
@@ -463,7 +466,7 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(const float *__restrict
         const float inv = Ls > 0.f ? 1.0f / Ls : 0.f;
         const float4 v = make_float4(T.x * inv, T.y * inv, T.z * inv, T.w * inv);
         reinterpret_cast<float4 *>(att + (long)b * nh * kHD + hh * kHD)[lane] = v;
-        if (xbm) {   // lanes 8i .. 8i+7 hold block i of the head: the preparation's own grouping
+        if constexpr (PREP) {   // lanes 8i .. 8i+7 hold block i of the head: the preparation's own grouping
             const int j = hh * (kHD / 32) + (lane >> 3);
             xprep_vals(v, reinterpret_cast<XB *>(xbm + (((long)(b / ntok) * nxb + j) * ntok + b % ntok) * 80),
                        lane & 7, true);
@@ -894,7 +897,8 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     static bool attr[64];
     if (!attr[c->device]) {
         set_qkernel_attrs(attn_decode_kernel);
-        set_qkernel_attrs(attn_merge_kernel);
+        set_qkernel_attrs(attn_merge_kernel<false>);
+        set_qkernel_attrs(attn_merge_kernel<true>);
         attr[c->device] = true;
     }
     // 1. qkv = Wqkv . rmsnorm(h)
@@ -947,9 +951,9 @@ static int layer_launch(x100q_model *m, DevCtx *c, int layer, float *h, const in
     o3.prep = m->prep;
     if (a.nsplit > 1) {
         const int grp = qgemv_prep_group(L.o, batch, o3);
-        st = launch_pdl(attn_merge_kernel, dim3(g.n_heads, batch), dim3(128), merge_smem(a.nsplit), s,
-                        (const float *)m->part, g.n_heads, a.nsplit, m->att, grp ? m->prep : nullptr, grp,
-                        slices_per_row(g.n_heads * kHD) * 8);
+        st = launch_pdl(grp ? attn_merge_kernel<true> : attn_merge_kernel<false>, dim3(g.n_heads, batch), dim3(128),
+                        merge_smem(a.nsplit), s, (const float *)m->part, g.n_heads, a.nsplit, m->att,
+                        grp ? m->prep : nullptr, grp, slices_per_row(g.n_heads * kHD) * 8);
         if (st) return st;
         o3.prepared = grp > 0;
     }
@@ -1185,7 +1189,8 @@ static int prefill_chunk_tc(x100q_model *m, DevCtx *c, const int *tok, float *h,
     if (!attr[c->device]) {
         set_qkernel_attrs(embed_kernel);
         set_qkernel_attrs(attn_decode_kernel);
-        set_qkernel_attrs(attn_merge_kernel);
+        set_qkernel_attrs(attn_merge_kernel<false>);
+        set_qkernel_attrs(attn_merge_kernel<true>);
         attr[c->device] = true;
     }
     const int qd = g.n_heads * g.head_dim, qn = qkv_rows(g);
@@ -1246,7 +1251,7 @@ static int prefill_chunk_tc(x100q_model *m, DevCtx *c, const int *tok, float *h,
             st = launch_pdl(attn_decode_kernel, dim3(ag.nsplit, g.n_kv_heads, gb), dim3(kAttnThreads), attn_smem(), s,
                             m->tmK, m->tmV, ag);
             if (!st && ag.nsplit > 1)
-                st = launch_pdl(attn_merge_kernel, dim3(g.n_heads, gb), dim3(128), merge_smem(ag.nsplit), s,
+                st = launch_pdl(attn_merge_kernel<false>, dim3(g.n_heads, gb), dim3(128), merge_smem(ag.nsplit), s,
                                 (const float *)m->part, g.n_heads, ag.nsplit, ag.att, (uint8_t *)nullptr, 0, 0);
             g0 += gb;
         }
