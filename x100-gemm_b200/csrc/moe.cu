@@ -466,15 +466,19 @@ __global__ void __launch_bounds__(kMoeThreads, 1)
 // ---- persistent pipelined expert kernels (batch > 1) ------------------------------
 // The work is a list of items (active expert k, row tile t), expert-major.
 // Thread 0 of each CTA claims chunks of kGrab consecutive items from a
-// per-call counter (so CTAs stay balanced whatever the tokens per expert,
-// and an item's neighbours mostly share its expert), and keeps kStages
+// per-call counter (so CTAs stay balanced whatever the tokens per expert),
+// and keeps kStages
 // claimed items in flight as bulk copies (one mbarrier per stage, use u of a
 // stage waits parity u & 1) while the CTA computes the oldest.  A stage is
 // refilled only after the barrier that ends the item last held in it.  The
 // routing metadata (active list, counts, pairs) is read into shared memory
 // once per CTA.
 constexpr int kStages = 4;
-constexpr int kGrab = 4;
+// Items per claim: one.  With ~13 items per CTA at batch 16, claims of 4
+// left CTAs finishing up to a claim (~5 us) apart; one item per claim:
+// decode batch 16 2057 -> 2277 tokens/s, MoE batch 16 150.8 K -> 165.6 K
+// (2: 2199 / 160.3 K).
+constexpr int kGrab = 1;
 
 struct PipeMeta {            // shared-memory copy of the groups
     int n_active;
